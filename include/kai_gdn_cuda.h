@@ -1,0 +1,213 @@
+/*
+ * kai_gdn_cuda.h -- C ABI of libkai_gdn_cuda.so, the B200 (sm_100a) Gated
+ * DeltaNet hot path that drops in for OrionsBelt's kai GDN operators.
+ *
+ * Three groups of entry points:
+ *
+ *  1. Drop-in symbols, with the exact names, signatures and semantics of the
+ *     reference's C kernels (caller-owned buffers, [seq][channels] row-major,
+ *     `state` / `hist` updated in place, seq == 0 or channels == 0 is a no-op,
+ *     the call returns when the result is in place).  They accept host
+ *     pointers (staged through device memory) or device / managed pointers
+ *     (used in place).  They return void like the originals; a failure is
+ *     recorded for kai_gdn_cuda_last_error() and never aborts the process.
+ *
+ *  2. Stream-ordered device entry points (suffix _sm100a): device pointers
+ *     only, launched on `stream` (a cudaStream_t; NULL = the legacy default
+ *     stream), asynchronous, returning a KAI_GDN_* status.  They add a batch
+ *     dimension, narrow storage types, and the two matrix-state operators the
+ *     reference has only in OpenCL / third-party form: the single-token
+ *     delta-rule decode step and the chunkwise WY gated delta-rule scan.
+ *
+ *  3. Library control: device selection, errors, version.
+ *
+ * Thread safety: every entry point may be called from several host threads;
+ * each thread gets its own staging stream and buffers per device.  Calls that
+ * share output buffers must be ordered by the caller, as with the reference.
+ */
+#ifndef KAI_GDN_CUDA_H
+#define KAI_GDN_CUDA_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define KAI_GDN_API __attribute__((visibility("default")))
+#else
+#define KAI_GDN_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---------------------------------------------------------------- status */
+#define KAI_GDN_OK 0
+#define KAI_GDN_ERR_INVALID 1     /* bad argument (null pointer, size, shape) */
+#define KAI_GDN_ERR_CUDA 2        /* a CUDA runtime call or a launch failed   */
+#define KAI_GDN_ERR_UNSUPPORTED 3 /* valid but not implemented (e.g. dk>256)  */
+#define KAI_GDN_ERR_NOMEM 4       /* device or pinned allocation failed       */
+
+/* --------------------------------------------------------- storage types */
+#define KAI_GDN_F32 0
+#define KAI_GDN_BF16 1 /* bfloat16, round-to-nearest-even on store */
+#define KAI_GDN_F16 2  /* IEEE binary16, round-to-nearest-even on store */
+
+/* ======================================================================
+ * 1. Drop-in replacements (host or device pointers, synchronous)
+ * ==================================================================== */
+
+/* decay[t][c] = prod_{i<=t} a[i][c].
+ * Replaces kleidiai_submission/kai/ukernels/gdn/kai_gdn_cumdecay_f32_sve.h:33 */
+KAI_GDN_API void kai_run_gdn_cumdecay_f32_sve(const float *a, float *decay, size_t seq,
+                                  size_t channels);
+
+/* s[t][c] = g[t][c] * s[t-1][c] + x[t][c]; state[] is s[-1] on entry and
+ * s[seq-1] on exit.
+ * Replaces kleidiai_submission/kai/ukernels/gdn/kai_gdn_gated_scan_f32_sve.h:35 */
+KAI_GDN_API void kai_run_gdn_gated_scan_f32_sve(const float *g, const float *x, float *s,
+                                    float *state, size_t seq, size_t channels);
+
+/* out[t][c] = w[0][c]*in[t-3][c] + w[1][c]*in[t-2][c] + w[2][c]*in[t-1][c]
+ *           + w[3][c]*in[t][c], with in[-3..-1] = hist[0..2] (oldest first);
+ * hist[] holds the last three inputs on exit.
+ * Replaces kleidiai_submission/kai/ukernels/gdn/kai_gdn_causal_dwconv1d_f32_k4_sve.h:39 */
+KAI_GDN_API void kai_run_gdn_causal_dwconv1d_f32_k4_sve(const float *in, const float *w,
+                                            float *out, float *hist, size_t seq,
+                                            size_t channels);
+
+/* c[j] = sum_k a[k] * b[k][j]  (k == 0 writes zeros; n == 0 is a no-op).
+ * Replaces kleidiai_submission/kai/ukernels/gdn/kai_gdn_gemv_f32_f32_f32_1x4_neon.h:40 */
+KAI_GDN_API void kai_run_gdn_gemv_f32_f32_f32_1x4_neon(const float *a, const float *b, float *c,
+                                           size_t k, size_t n);
+
+/* Project-form twins, src/orionsbelt/engines/cpu/kernels/gdn_sve.h:30-86.
+ * `__fp16 *` there is ABI-identical to `uint16_t *` here (IEEE binary16 bits);
+ * bf16 is the upper half of an fp32, rounded to nearest even. */
+KAI_GDN_API void gdn_cumdecay_f32(const float *a, float *decay, size_t seq, size_t channels);
+KAI_GDN_API void gdn_gated_scan_f32(const float *g, const float *x, float *s, float *state,
+                        size_t seq, size_t channels);
+KAI_GDN_API void gdn_causal_dwconv1d_f32(const float *in, const float *w, float *out, float *hist,
+                             size_t seq, size_t channels);
+KAI_GDN_API void gdn_cumdecay_f16(const float *a, uint16_t *decay, size_t seq, size_t channels);
+KAI_GDN_API void gdn_gated_scan_f16(const float *g, const float *x, float *s, uint16_t *state,
+                        size_t seq, size_t channels);
+KAI_GDN_API void gdn_cumdecay_bf16(const float *a, uint16_t *decay, size_t seq, size_t channels);
+KAI_GDN_API void gdn_gated_scan_bf16(const float *g, const float *x, float *s, uint16_t *state,
+                         size_t seq, size_t channels);
+/* GDN-2 channel scan s[t] = w[t]*x[t] + s[t-1]*(g[t]*b[t]).  gdn_sve.h:79 */
+KAI_GDN_API void gdn2_gated_scan_f32(const float *g, const float *b_gate, const float *w_gate,
+                         const float *x, float *s, float *state, size_t seq,
+                         size_t channels);
+
+/* C[M][N] = A[M][K] . B[K][N], row-major, no bias.
+ * Replaces src/orionsbelt/engines/cpu/kernels/gdn_delta_matmul.h:15 */
+KAI_GDN_API void gdn_delta_rule_matmul(const float *A, const float *B, float *C, size_t M,
+                           size_t K, size_t N);
+
+/* ======================================================================
+ * 2. Stream-ordered device entry points (device pointers, asynchronous)
+ *    Layouts are row-major; `batch` independent problems lie back to back.
+ * ==================================================================== */
+
+/* Prefix product over seq of a[batch][seq][channels]; decay is stored as
+ * decay_dtype (F32, F16 or BF16) with an fp32 running product.
+ * Batched form of kai_gdn_cumdecay_f32_sve.h:33 / gdn_sve.h:30,57,65. */
+KAI_GDN_API int kai_run_gdn_cumdecay_sm100a(const float *a, void *decay, int decay_dtype,
+                                size_t batch, size_t seq, size_t channels,
+                                void *stream);
+
+/* Log-space decay cumsum gcum[b][t][c] = sum_{i<=t} g[b][i][c] (the form the
+ * chunkwise scan consumes; docs/GDN_ARCHITECTURE_AUDIT.md:142-153). */
+KAI_GDN_API int kai_run_gdn_cumsum_f32_sm100a(const float *g, float *gcum, size_t batch,
+                                  size_t seq, size_t channels, void *stream);
+
+/* Gated scan over [batch][seq][channels]; state[batch][channels] stored as
+ * state_dtype (F32, F16 or BF16), widened on entry and narrowed once on exit.
+ * Batched form of kai_gdn_gated_scan_f32_sve.h:35 / gdn_sve.h:36,61,69. */
+KAI_GDN_API int kai_run_gdn_gated_scan_sm100a(const float *g, const float *x, float *s,
+                                  void *state, int state_dtype, size_t batch,
+                                  size_t seq, size_t channels, void *stream);
+
+/* GDN-2 gated scan (gdn_sve.h:79), fp32 state. */
+KAI_GDN_API int kai_run_gdn2_gated_scan_f32_sm100a(const float *g, const float *b_gate,
+                                       const float *w_gate, const float *x, float *s,
+                                       float *state, size_t batch, size_t seq,
+                                       size_t channels, void *stream);
+
+/* Causal depthwise Conv1D k=4 over in[batch][seq][channels]; in, out and
+ * hist[batch][3][channels] stored as io_dtype, w[4][channels] fp32, sums in
+ * fp32.  Batched form of kai_gdn_causal_dwconv1d_f32_k4_sve.h:39. */
+KAI_GDN_API int kai_run_gdn_causal_dwconv1d_k4_sm100a(const void *in, const float *w, void *out,
+                                          void *hist, int io_dtype, size_t batch,
+                                          size_t seq, size_t channels, void *stream);
+
+/* C = A . B (fp32; M == 1 is the GEMV of kai_gdn_gemv_f32_f32_f32_1x4_neon.h:40,
+ * any M is gdn_delta_matmul.h:15). */
+KAI_GDN_API int kai_run_gdn_matmul_f32_sm100a(const float *A, const float *B, float *C, size_t M,
+                                  size_t K, size_t N, void *stream);
+
+/* Single-token matrix-state delta-rule step for every (batch, value head).
+ * Per (b, h), with key head hk = h / (heads_v / heads_k), a = exp(g[b][h]):
+ *   S *= a;  kv = S^T k;  delta = (v - kv) * beta;  S += k delta^T;
+ *   o = scale * S^T q
+ * The math of gpu/gdn_gpu_kernels.cl:158-206 and its C twin
+ * gpu/gdn_gpu_validate.c:100-118 (which use one beta and decay for all heads
+ * and scale 1), with per-(b,h) gates and grouped value heads. */
+typedef struct kai_gdn_decode_args {
+    void *state;       /* [batch][heads_v][dk][dv], state_dtype, in/out   */
+    const void *q;     /* [batch][heads_k][dk], in_dtype                  */
+    const void *k;     /* [batch][heads_k][dk], in_dtype                  */
+    const void *v;     /* [batch][heads_v][dv], in_dtype                  */
+    const float *g;    /* [batch][heads_v] log-decay (decay = exp(g))     */
+    const float *beta; /* [batch][heads_v]                                */
+    void *o;           /* [batch][heads_v][dv], out_dtype                 */
+    size_t batch, heads_k, heads_v, dk, dv;
+    float scale;       /* query scale; 1 = the reference C, 1/sqrt(dk) = HF */
+    int in_dtype, state_dtype, out_dtype;
+} kai_gdn_decode_args;
+KAI_GDN_API int kai_run_gdn_delta_rule_decode_sm100a(const kai_gdn_decode_args *args, void *stream);
+
+/* Chunkwise (WY / UT-transform) gated delta-rule scan over a whole sequence,
+ * for every (batch, value head), chunk length `chunk` (64).  Equal, up to
+ * rounding, to applying the decode step above for t = 0 .. seq-1 with
+ * g, beta taken per token.  The reference names this form
+ * (docs/GDN_ARCHITECTURE_AUDIT.md:142-153) and reaches it only through HF
+ * transformers' torch_chunk_gated_delta_rule. */
+typedef struct kai_gdn_chunk_args {
+    const void *q;     /* [batch][seq][heads_k][dk], in_dtype             */
+    const void *k;     /* [batch][seq][heads_k][dk], in_dtype             */
+    const void *v;     /* [batch][seq][heads_v][dv], in_dtype             */
+    const float *g;    /* [batch][seq][heads_v] log-decay                 */
+    const float *beta; /* [batch][seq][heads_v]                           */
+    void *state;       /* [batch][heads_v][dk][dv], state_dtype: initial
+                          state on entry, final state on exit             */
+    void *o;           /* [batch][seq][heads_v][dv], out_dtype            */
+    size_t batch, seq, heads_k, heads_v, dk, dv, chunk;
+    float scale;
+    int in_dtype, state_dtype, out_dtype;
+} kai_gdn_chunk_args;
+KAI_GDN_API int kai_run_gdn_chunk_delta_rule_sm100a(const kai_gdn_chunk_args *args, void *stream);
+
+/* ======================================================================
+ * 3. Library control
+ * ==================================================================== */
+
+/* Make `device` current for this host thread (one thread per GPU in the
+ * multi-GPU driver).  Returns a status. */
+KAI_GDN_API int kai_gdn_cuda_set_device(int device);
+/* Number of visible CUDA devices, or -1 on error. */
+KAI_GDN_API int kai_gdn_cuda_device_count(void);
+/* Status and message of the last failure on this host thread ("" if none);
+ * kai_gdn_cuda_clear_error() resets both. */
+KAI_GDN_API int kai_gdn_cuda_last_status(void);
+KAI_GDN_API const char *kai_gdn_cuda_last_error(void);
+KAI_GDN_API void kai_gdn_cuda_clear_error(void);
+/* Library version string. */
+KAI_GDN_API const char *kai_gdn_cuda_version(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* KAI_GDN_CUDA_H */

@@ -1,0 +1,272 @@
+"""Parity oracle for the GDN hot path -- TEST INFRASTRUCTURE ONLY.
+
+Only tests/, __graft_entry__.smoke() and bench.py's cpu_baseline /
+``--impl reference`` legs may import this package.  The product library
+(orionsbelt_b200/libkai_gdn_cuda.so) never calls into it and has no CPU
+fallback.
+
+Two CPU implementations are exposed through ctypes:
+
+* ``orc``: liboracle.so, built from gdn_oracle.c -- a restatement of the
+  reference's arithmetic (file:line citations in that file), bit-identical to
+  the reference's scalar path where the reference has code, plus the token-loop
+  and chunked-WY forms of the matrix-state delta rule.
+* ``ref``: _ref/libgdnref.so, the reference's OWN C kernels compiled from
+  source by oracle/Makefile (absent when the reference tree was not available
+  at build time; then ``ref`` is None).
+
+Arrays are numpy, C-contiguous; the wrappers allocate outputs and copy in/out
+buffers so callers keep their inputs.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import subprocess
+from pathlib import Path
+
+import numpy as np
+
+HERE = Path(__file__).resolve().parent
+ORACLE_SO = HERE / "liboracle.so"
+REF_SO = HERE / "_ref" / "libgdnref.so"
+
+_f = C.POINTER(C.c_float)
+_u16 = C.POINTER(C.c_uint16)
+_sz = C.c_size_t
+
+
+def build(ref: bool = True) -> None:
+    """Compile liboracle.so (and, when the reference tree exists, _ref/)."""
+    subprocess.run(["make", "-s", "-C", str(HERE), "oracle"], check=True)
+    if ref and Path("/root/reference").is_dir():
+        subprocess.run(["make", "-s", "-C", str(HERE), "ref", "ref-tests"], check=True)
+
+
+def _load(path: Path):
+    if not path.exists():
+        return None
+    return C.CDLL(str(path))
+
+
+def _p(a: np.ndarray, dtype) -> C.POINTER:
+    assert a.flags["C_CONTIGUOUS"] and a.dtype == dtype, (a.dtype, dtype)
+    return a.ctypes.data_as(_f if dtype == np.float32 else _u16)
+
+
+def _f32(a) -> np.ndarray:
+    return np.ascontiguousarray(a, dtype=np.float32)
+
+
+class _Kernels:
+    """The four kai ops and the gdn_sve.h twins, on one of the two libraries."""
+
+    def __init__(self, lib, prefix: str):
+        self.lib = lib
+        self.prefix = prefix
+
+    def _fn(self, name):
+        return getattr(self.lib, self.prefix + name)
+
+    def cumdecay(self, a):
+        a = _f32(a)
+        out = np.empty_like(a)
+        self._fn("cumdecay_f32")(_p(a, np.float32), _p(out, np.float32), _sz(a.shape[0]), _sz(a.shape[1]))
+        return out
+
+    def cumdecay_narrow(self, a, kind: str):
+        a = _f32(a)
+        out = np.empty(a.shape, np.uint16)
+        self._fn("cumdecay_" + kind)(_p(a, np.float32), _p(out, np.uint16), _sz(a.shape[0]), _sz(a.shape[1]))
+        return out
+
+    def gated_scan(self, g, x, state):
+        g, x = _f32(g), _f32(x)
+        st = _f32(state).copy()
+        s = np.empty_like(x)
+        self._fn("gated_scan_f32")(_p(g, np.float32), _p(x, np.float32), _p(s, np.float32),
+                                   _p(st, np.float32), _sz(x.shape[0]), _sz(x.shape[1]))
+        return s, st
+
+    def gated_scan_narrow(self, g, x, state_u16, kind: str):
+        g, x = _f32(g), _f32(x)
+        st = np.ascontiguousarray(state_u16, dtype=np.uint16).copy()
+        s = np.empty_like(x)
+        self._fn("gated_scan_" + kind)(_p(g, np.float32), _p(x, np.float32), _p(s, np.float32),
+                                       _p(st, np.uint16), _sz(x.shape[0]), _sz(x.shape[1]))
+        return s, st
+
+    def conv(self, x, w, hist):
+        x, w = _f32(x), _f32(w)
+        h = _f32(hist).copy()
+        out = np.empty_like(x)
+        self._fn("causal_dwconv1d_f32")(_p(x, np.float32), _p(w, np.float32), _p(out, np.float32),
+                                        _p(h, np.float32), _sz(x.shape[0]), _sz(x.shape[1]))
+        return out, h
+
+
+class _Ref(_Kernels):
+    """The reference's own build: kai_run_* and gdn_* symbols."""
+
+    def __init__(self, lib):
+        super().__init__(lib, "gdn_")
+
+    def kai_cumdecay(self, a):
+        a = _f32(a)
+        out = np.empty_like(a)
+        self.lib.kai_run_gdn_cumdecay_f32_sve(_p(a, np.float32), _p(out, np.float32), _sz(a.shape[0]),
+                                              _sz(a.shape[1]))
+        return out
+
+    def matmul(self, A, B):
+        A, B = _f32(A), _f32(B)
+        Cm = np.empty((A.shape[0], B.shape[1]), np.float32)
+        self.lib.gdn_delta_rule_matmul(_p(A, np.float32), _p(B, np.float32), _p(Cm, np.float32),
+                                       _sz(A.shape[0]), _sz(A.shape[1]), _sz(B.shape[1]))
+        return Cm
+
+    def gemv(self, a, b):
+        a, b = _f32(a), _f32(b)
+        c = np.empty((b.shape[1],), np.float32)
+        self.lib.kai_run_gdn_gemv_f32_f32_f32_1x4_neon(_p(a, np.float32), _p(b, np.float32), _p(c, np.float32),
+                                                       _sz(b.shape[0]), _sz(b.shape[1]))
+        return c
+
+    def gdn2_scan(self, g, bg, wg, x, state):
+        g, bg, wg, x = map(_f32, (g, bg, wg, x))
+        st = _f32(state).copy()
+        s = np.empty_like(x)
+        self.lib.gdn2_gated_scan_f32(_p(g, np.float32), _p(bg, np.float32), _p(wg, np.float32),
+                                     _p(x, np.float32), _p(s, np.float32), _p(st, np.float32),
+                                     _sz(x.shape[0]), _sz(x.shape[1]))
+        return s, st
+
+
+class _Oracle(_Kernels):
+    """The restatement in gdn_oracle.c."""
+
+    def __init__(self, lib):
+        super().__init__(lib, "orc_")
+        lib.orc_num_threads.restype = C.c_int
+
+    def cumsum(self, g):
+        g = _f32(g)
+        out = np.empty_like(g)
+        self.lib.orc_cumsum_f32(_p(g, np.float32), _p(out, np.float32), _sz(g.shape[0]), _sz(g.shape[1]))
+        return out
+
+    def matmul(self, A, B):
+        A, B = _f32(A), _f32(B)
+        Cm = np.empty((A.shape[0], B.shape[1]), np.float32)
+        self.lib.orc_matmul_f32(_p(A, np.float32), _p(B, np.float32), _p(Cm, np.float32),
+                                _sz(A.shape[0]), _sz(A.shape[1]), _sz(B.shape[1]))
+        return Cm
+
+    def gemv(self, a, b):
+        return self.matmul(np.asarray(a, np.float32)[None, :], b)[0]
+
+    def gdn2_scan(self, g, bg, wg, x, state):
+        g, bg, wg, x = map(_f32, (g, bg, wg, x))
+        st = _f32(state).copy()
+        s = np.empty_like(x)
+        self.lib.orc_gdn2_gated_scan_f32(_p(g, np.float32), _p(bg, np.float32), _p(wg, np.float32),
+                                         _p(x, np.float32), _p(s, np.float32), _p(st, np.float32),
+                                         _sz(x.shape[0]), _sz(x.shape[1]))
+        return s, st
+
+    def conv_narrow(self, x_u16, w, hist_u16, kind: str):
+        x = np.ascontiguousarray(x_u16, dtype=np.uint16)
+        w = _f32(w)
+        h = np.ascontiguousarray(hist_u16, dtype=np.uint16).copy()
+        out = np.empty_like(x)
+        self.lib.orc_causal_dwconv1d_narrow(_p(x, np.uint16), _p(w, np.float32), _p(out, np.uint16),
+                                            _p(h, np.uint16), _sz(x.shape[0]), _sz(x.shape[1]),
+                                            C.c_int(1 if kind == "bf16" else 0))
+        return out, h
+
+    def delta_rule_step(self, S, k, v, q, beta, decay):
+        """One head, one token: gpu/gdn_gpu_validate.c:100-118 (scale 1)."""
+        S = _f32(S).copy()
+        k, v, q = map(_f32, (k, v, q))
+        out = np.empty((S.shape[1],), np.float32)
+        self.lib.orc_delta_rule_step(_p(S, np.float32), _p(k, np.float32), _p(v, np.float32),
+                                     _p(q, np.float32), C.c_float(beta), C.c_float(decay),
+                                     _p(out, np.float32), _sz(S.shape[0]), _sz(S.shape[1]))
+        return S, out
+
+    def delta_rule_decode(self, S, q, k, v, g, beta, scale=1.0, nthreads=0):
+        """S [B][Hv][dk][dv], q,k [B][Hk][dk], v [B][Hv][dv], g,beta [B][Hv]."""
+        S = _f32(S).copy()
+        q, k, v, g, beta = map(_f32, (q, k, v, g, beta))
+        B, Hv, dk, dv = S.shape
+        Hk = q.shape[1]
+        o = np.empty((B, Hv, dv), np.float32)
+        self.lib.orc_delta_rule_decode(_p(S, np.float32), _p(q, np.float32), _p(k, np.float32),
+                                       _p(v, np.float32), _p(g, np.float32), _p(beta, np.float32),
+                                       _p(o, np.float32), _sz(B), _sz(Hk), _sz(Hv), _sz(dk), _sz(dv),
+                                       C.c_float(scale), C.c_int(nthreads))
+        return S, o
+
+    def delta_rule_seq(self, S, q, k, v, g, beta, scale=1.0, nthreads=0):
+        """Token loop.  q,k [B][T][Hk][dk], v [B][T][Hv][dv], g,beta [B][T][Hv]."""
+        S = _f32(S).copy()
+        q, k, v, g, beta = map(_f32, (q, k, v, g, beta))
+        B, T, Hk, dk = q.shape
+        Hv, dv = v.shape[2], v.shape[3]
+        o = np.empty((B, T, Hv, dv), np.float32)
+        self.lib.orc_delta_rule_seq(_p(S, np.float32), _p(q, np.float32), _p(k, np.float32),
+                                    _p(v, np.float32), _p(g, np.float32), _p(beta, np.float32),
+                                    _p(o, np.float32), _sz(B), _sz(T), _sz(Hk), _sz(Hv), _sz(dk), _sz(dv),
+                                    C.c_float(scale), C.c_int(nthreads))
+        return S, o
+
+    def chunk_wy(self, S, q, k, v, g, beta, scale=1.0, chunk=64, nthreads=0):
+        """Chunked WY form in float64 (same layouts as delta_rule_seq)."""
+        S = _f32(S).copy()
+        q, k, v, g, beta = map(_f32, (q, k, v, g, beta))
+        B, T, Hk, dk = q.shape
+        Hv, dv = v.shape[2], v.shape[3]
+        o = np.empty((B, T, Hv, dv), np.float32)
+        self.lib.orc_chunk_wy_f64(_p(S, np.float32), _p(q, np.float32), _p(k, np.float32),
+                                  _p(v, np.float32), _p(g, np.float32), _p(beta, np.float32),
+                                  _p(o, np.float32), _sz(B), _sz(T), _sz(Hk), _sz(Hv), _sz(dk), _sz(dv),
+                                  _sz(chunk), C.c_float(scale), C.c_int(nthreads))
+        return S, o
+
+    def num_threads(self) -> int:
+        return int(self.lib.orc_num_threads())
+
+
+def _f16_to_u16(a) -> np.ndarray:
+    return np.ascontiguousarray(np.asarray(a, np.float32).astype(np.float16)).view(np.uint16)
+
+
+def _u16_to_f32(a, kind: str) -> np.ndarray:
+    a = np.ascontiguousarray(a, dtype=np.uint16)
+    if kind == "f16":
+        return a.view(np.float16).astype(np.float32)
+    return (a.astype(np.uint32) << 16).view(np.float32)
+
+
+def f32_to_u16(a, kind: str) -> np.ndarray:
+    """fp32 -> fp16 / bf16 bits, round to nearest even (bf16 rule of gdn_sve.c:81-88)."""
+    a = np.ascontiguousarray(a, dtype=np.float32)
+    if kind == "f16":
+        return _f16_to_u16(a)
+    u = a.view(np.uint32).astype(np.uint64)
+    return ((u + 0x7FFF + ((u >> 16) & 1)) >> 16).astype(np.uint16)
+
+
+u16_to_f32 = _u16_to_f32
+
+orc = _Oracle(_load(ORACLE_SO)) if ORACLE_SO.exists() else None
+_ref_lib = _load(REF_SO)
+ref = _Ref(_ref_lib) if _ref_lib is not None else None
+
+
+def require():
+    """Return (orc, ref), building liboracle.so if it is missing."""
+    global orc
+    if orc is None:
+        build(ref=False)
+        orc = _Oracle(_load(ORACLE_SO))
+    return orc, ref

@@ -1,0 +1,446 @@
+/*
+ * gdn_oracle.c -- CPU restatement of OrionsBelt's Gated DeltaNet hot path.
+ *
+ * TEST INFRASTRUCTURE ONLY.  This file is the parity checker for the CUDA
+ * library in orionsbelt_b200/.  Only tests/, __graft_entry__.smoke() and the
+ * cpu_baseline / --impl reference legs of bench.py may load it.  The product
+ * path never calls into it and has no CPU fallback.
+ *
+ * Every function restates the arithmetic of a reference function, in the same
+ * evaluation order and with float accumulators, so that on x86-64 (where the
+ * reference's SVE/NEON branches compile out and its scalar `#else` branch
+ * runs, with no FMA contraction) the results are bit-identical to the
+ * reference build in oracle/_ref/.  Citations are path:line inside the
+ * OrionsBelt repository.
+ *
+ * Pinning: tests/test_oracle_pin.py checks every function here against
+ *   - the reference's own C compiled from source into oracle/_ref/ (bit-exact),
+ *   - the NumPy float64 recurrence bench/gdn2_reference.py::gdn1_recurrent
+ *     and HF transformers' torch_chunk_gated_delta_rule, through the fixtures
+ *     in tests/golden/ (made by tests/golden/make_golden.py),
+ *   - the known-answer case of bench/gdn2_reference.py:251-290.
+ *
+ * Build: oracle/Makefile (gcc -O2 -fopenmp, no -march flags, so no FMA).
+ */
+#include <math.h>
+#include <stddef.h>
+#include <stdint.h>
+#include <string.h>
+#include <stdlib.h>
+#ifdef _OPENMP
+#include <omp.h>
+#endif
+
+/* ------------------------------------------------------------------------
+ * Narrow formats.  fp16 uses the compiler's IEEE binary16 type (conversion
+ * rounds to nearest even), which is what the reference's `__fp16` casts do
+ * (gdn_sve.c:434-441).  bf16 is round-to-nearest-even on the top 16 bits, the
+ * rule of gdn_sve.c:81-88.
+ * ---------------------------------------------------------------------- */
+static inline uint16_t orc_f32_to_f16(float f) {
+    _Float16 h = (_Float16)f;
+    uint16_t u;
+    memcpy(&u, &h, 2);
+    return u;
+}
+static inline float orc_f16_to_f32(uint16_t u) {
+    _Float16 h;
+    memcpy(&h, &u, 2);
+    return (float)h;
+}
+static inline uint16_t orc_f32_to_bf16(float f) {
+    uint32_t u;
+    memcpy(&u, &f, 4);
+    uint32_t bias = 0x7FFFu + ((u >> 16) & 1u);
+    return (uint16_t)((u + bias) >> 16);
+}
+static inline float orc_bf16_to_f32(uint16_t b) {
+    uint32_t u = (uint32_t)b << 16;
+    float f;
+    memcpy(&f, &u, 4);
+    return f;
+}
+
+void orc_f32_to_f16_array(const float *x, uint16_t *y, size_t n) {
+    for (size_t i = 0; i < n; ++i) y[i] = orc_f32_to_f16(x[i]);
+}
+void orc_f16_to_f32_array(const uint16_t *x, float *y, size_t n) {
+    for (size_t i = 0; i < n; ++i) y[i] = orc_f16_to_f32(x[i]);
+}
+void orc_f32_to_bf16_array(const float *x, uint16_t *y, size_t n) {
+    for (size_t i = 0; i < n; ++i) y[i] = orc_f32_to_bf16(x[i]);
+}
+void orc_bf16_to_f32_array(const uint16_t *x, float *y, size_t n) {
+    for (size_t i = 0; i < n; ++i) y[i] = orc_bf16_to_f32(x[i]);
+}
+
+/* ------------------------------------------------------------------------
+ * a1: gated cumulative decay, inclusive prefix product per channel.
+ * kleidiai_submission/kai/ukernels/gdn/kai_gdn_cumdecay_f32_sve.c:82-89
+ * ---------------------------------------------------------------------- */
+void orc_cumdecay_f32(const float *a, float *decay, size_t seq, size_t ch) {
+    for (size_t c = 0; c < ch; ++c) {
+        float run = 1.0f;
+        for (size_t t = 0; t < seq; ++t) {
+            run *= a[t * ch + c];
+            decay[t * ch + c] = run;
+        }
+    }
+}
+
+/* fp16 / bf16 output: fp32 running product, each stored value narrowed.
+ * src/orionsbelt/engines/cpu/kernels/gdn_sve.c:535 (f16), :700 (bf16). */
+void orc_cumdecay_f16(const float *a, uint16_t *decay, size_t seq, size_t ch) {
+    for (size_t c = 0; c < ch; ++c) {
+        float run = 1.0f;
+        for (size_t t = 0; t < seq; ++t) {
+            run *= a[t * ch + c];
+            decay[t * ch + c] = orc_f32_to_f16(run);
+        }
+    }
+}
+void orc_cumdecay_bf16(const float *a, uint16_t *decay, size_t seq, size_t ch) {
+    for (size_t c = 0; c < ch; ++c) {
+        float run = 1.0f;
+        for (size_t t = 0; t < seq; ++t) {
+            run *= a[t * ch + c];
+            decay[t * ch + c] = orc_f32_to_bf16(run);
+        }
+    }
+}
+
+/* Log-space decay cumsum: gcum[t][c] = sum_{i<=t} g[i][c].  The reference
+ * reaches this form only through HF transformers (`g.cumsum(dim=-1)` in
+ * torch_chunk_gated_delta_rule, reached via bench/hf_backend.py:156-193, and
+ * docs/GDN_ARCHITECTURE_AUDIT.md:142-153); the sequential float sum is the
+ * additive twin of orc_cumdecay_f32. */
+void orc_cumsum_f32(const float *g, float *out, size_t seq, size_t ch) {
+    for (size_t c = 0; c < ch; ++c) {
+        float run = 0.0f;
+        for (size_t t = 0; t < seq; ++t) {
+            run += g[t * ch + c];
+            out[t * ch + c] = run;
+        }
+    }
+}
+
+/* ------------------------------------------------------------------------
+ * a3: gated scan s[t] = g[t]*s[t-1] + x[t], state carried across calls.
+ * kleidiai_submission/kai/ukernels/gdn/kai_gdn_gated_scan_f32_sve.c:86-95
+ * ---------------------------------------------------------------------- */
+void orc_gated_scan_f32(const float *g, const float *x, float *s, float *state,
+                        size_t seq, size_t ch) {
+    for (size_t c = 0; c < ch; ++c) {
+        float acc = state[c];
+        for (size_t t = 0; t < seq; ++t) {
+            acc = x[t * ch + c] + acc * g[t * ch + c];
+            s[t * ch + c] = acc;
+        }
+        state[c] = acc;
+    }
+}
+
+/* Narrow-state variants: the state is widened on entry and narrowed once on
+ * exit (gdn_sve.c:434-441 for fp16, :616 for bf16). */
+void orc_gated_scan_f16(const float *g, const float *x, float *s, uint16_t *state,
+                        size_t seq, size_t ch) {
+    for (size_t c = 0; c < ch; ++c) {
+        float acc = orc_f16_to_f32(state[c]);
+        for (size_t t = 0; t < seq; ++t) {
+            acc = x[t * ch + c] + acc * g[t * ch + c];
+            s[t * ch + c] = acc;
+        }
+        state[c] = orc_f32_to_f16(acc);
+    }
+}
+void orc_gated_scan_bf16(const float *g, const float *x, float *s, uint16_t *state,
+                         size_t seq, size_t ch) {
+    for (size_t c = 0; c < ch; ++c) {
+        float acc = orc_bf16_to_f32(state[c]);
+        for (size_t t = 0; t < seq; ++t) {
+            acc = x[t * ch + c] + acc * g[t * ch + c];
+            s[t * ch + c] = acc;
+        }
+        state[c] = orc_f32_to_bf16(acc);
+    }
+}
+
+/* ------------------------------------------------------------------------
+ * a2: causal depthwise Conv1D, width 4, hist[3][ch] carried (oldest first).
+ * kleidiai_submission/kai/ukernels/gdn/kai_gdn_causal_dwconv1d_f32_k4_sve.c:149-165
+ * ---------------------------------------------------------------------- */
+void orc_causal_dwconv1d_f32(const float *in, const float *w, float *out,
+                             float *hist, size_t seq, size_t ch) {
+    for (size_t c = 0; c < ch; ++c) {
+        float h[3];
+        for (int j = 0; j < 3; ++j) h[j] = hist[(size_t)j * ch + c];
+        for (size_t t = 0; t < seq; ++t) {
+            float cur = in[t * ch + c];
+            float acc = h[0] * w[0 * ch + c] + h[1] * w[1 * ch + c] +
+                        h[2] * w[2 * ch + c] + cur * w[3 * ch + c];
+            out[t * ch + c] = acc;
+            h[0] = h[1];
+            h[1] = h[2];
+            h[2] = cur;
+        }
+        for (int j = 0; j < 3; ++j) hist[(size_t)j * ch + c] = h[j];
+    }
+}
+
+/* Narrow-I/O twin (in, out and hist in fp16 or bf16; weights fp32; the sum is
+ * formed in fp32 exactly as above and narrowed once per output).  The
+ * reference has no narrow conv; this is the arithmetic of the fp32 kernel
+ * with the storage rule of gdn_sve.c:535 (narrow on store). */
+void orc_causal_dwconv1d_narrow(const uint16_t *in, const float *w, uint16_t *out,
+                                uint16_t *hist, size_t seq, size_t ch, int is_bf16) {
+    for (size_t c = 0; c < ch; ++c) {
+        float h[3];
+        for (int j = 0; j < 3; ++j) {
+            uint16_t u = hist[(size_t)j * ch + c];
+            h[j] = is_bf16 ? orc_bf16_to_f32(u) : orc_f16_to_f32(u);
+        }
+        for (size_t t = 0; t < seq; ++t) {
+            uint16_t u = in[t * ch + c];
+            float cur = is_bf16 ? orc_bf16_to_f32(u) : orc_f16_to_f32(u);
+            float acc = h[0] * w[0 * ch + c] + h[1] * w[1 * ch + c] +
+                        h[2] * w[2 * ch + c] + cur * w[3 * ch + c];
+            out[t * ch + c] = is_bf16 ? orc_f32_to_bf16(acc) : orc_f32_to_f16(acc);
+            h[0] = h[1];
+            h[1] = h[2];
+            h[2] = cur;
+        }
+        for (int j = 0; j < 3; ++j)
+            hist[(size_t)j * ch + c] = is_bf16 ? orc_f32_to_bf16(h[j]) : orc_f32_to_f16(h[j]);
+    }
+}
+
+/* ------------------------------------------------------------------------
+ * a4: delta-rule matmul C[M][N] = A[M][K] . B[K][N], k-sequential float sums.
+ * src/orionsbelt/engines/cpu/kernels/gdn_delta_matmul.c:109-117 (the scalar
+ * path, used at every M on x86); GEMV (M=1) is
+ * kleidiai_submission/kai/ukernels/gdn/kai_gdn_gemv_f32_f32_f32_1x4_neon.c:77-85.
+ * ---------------------------------------------------------------------- */
+void orc_matmul_f32(const float *A, const float *B, float *C, size_t M, size_t K,
+                    size_t N) {
+    for (size_t i = 0; i < M; ++i)
+        for (size_t j = 0; j < N; ++j) {
+            float acc = 0.0f;
+            for (size_t k = 0; k < K; ++k) acc += A[i * K + k] * B[k * N + j];
+            C[i * N + j] = acc;
+        }
+}
+void orc_gemv_f32(const float *a, const float *b, float *c, size_t k, size_t n) {
+    orc_matmul_f32(a, b, c, 1, k, n);
+}
+
+/* ------------------------------------------------------------------------
+ * a5: one matrix-state delta-rule step for one head, S[dk][dv] row-major.
+ * gpu/gdn_gpu_validate.c:100-118 (the C twin of gpu/gdn_gpu_kernels.cl:158-206):
+ *   S *= decay;  kv_i = sum_j S[j,i] k_j;  delta_i = (v_i - kv_i) * beta;
+ *   S[j,i] += k_j * delta_i;  o_i = sum_j S[j,i] q_j.
+ * `q` is used as given; callers that want a query scale pre-multiply it (the
+ * HF convention, `query = query * scale`).
+ * ---------------------------------------------------------------------- */
+void orc_delta_rule_step(float *S, const float *k, const float *v, const float *q,
+                         float beta, float decay, float *out, size_t dk, size_t dv) {
+    for (size_t j = 0; j < dk; j++)
+        for (size_t i = 0; i < dv; i++) S[j * dv + i] *= decay;
+    for (size_t i = 0; i < dv; i++) {
+        float kv = 0.0f;
+        for (size_t j = 0; j < dk; j++) kv += S[j * dv + i] * k[j];
+        float delta = (v[i] - kv) * beta;
+        for (size_t j = 0; j < dk; j++) S[j * dv + i] += k[j] * delta;
+        float o = 0.0f;
+        for (size_t j = 0; j < dk; j++) o += S[j * dv + i] * q[j];
+        out[i] = o;
+    }
+}
+
+/* Batched decode step with grouped value heads (value head h reads key head
+ * h / (Hv/Hk), docs/GDN_ARCHITECTURE_AUDIT.md:43-47 and
+ * bench/gdn2_reference.py:182-187) and per-(b,h) log-decay g and beta.
+ *   S: [B][Hv][dk][dv], q,k: [B][Hk][dk], v: [B][Hv][dv], g,beta: [B][Hv],
+ *   o: [B][Hv][dv].   decay = expf(g).   nthreads <= 0: all OpenMP threads. */
+void orc_delta_rule_decode(float *S, const float *q, const float *k, const float *v,
+                           const float *g, const float *beta, float *o, size_t B,
+                           size_t Hk, size_t Hv, size_t dk, size_t dv, float scale,
+                           int nthreads) {
+    size_t group = Hv / Hk;
+    long units = (long)(B * Hv);
+#ifdef _OPENMP
+    int nt = nthreads > 0 ? nthreads : omp_get_max_threads();
+#pragma omp parallel for schedule(static) num_threads(nt)
+#endif
+    for (long u = 0; u < units; ++u) {
+        size_t b = (size_t)u / Hv, h = (size_t)u % Hv, hk = h / group;
+        float qs[512];
+        const float *qh = q + (b * Hk + hk) * dk;
+        for (size_t j = 0; j < dk; ++j) qs[j] = qh[j] * scale;
+        orc_delta_rule_step(S + (b * Hv + h) * dk * dv, k + (b * Hk + hk) * dk,
+                            v + (b * Hv + h) * dv, qs, beta[b * Hv + h],
+                            expf(g[b * Hv + h]), o + (b * Hv + h) * dv, dk, dv);
+    }
+}
+
+/* Token loop over a whole sequence: the recurrent form of the gated delta rule
+ * (the per-token math of gpu/gdn_gpu_validate.c:100-118 applied for t=0..T-1,
+ * as in bench/gdn2_reference.py:149-218 and HF torch_recurrent_gated_delta_rule).
+ *   q,k: [B][T][Hk][dk], v: [B][T][Hv][dv], g,beta: [B][T][Hv],
+ *   S: [B][Hv][dk][dv] (in: initial state, out: final state),
+ *   o: [B][T][Hv][dv].  nthreads <= 0: all OpenMP threads. */
+void orc_delta_rule_seq(float *S, const float *q, const float *k, const float *v,
+                        const float *g, const float *beta, float *o, size_t B,
+                        size_t T, size_t Hk, size_t Hv, size_t dk, size_t dv,
+                        float scale, int nthreads) {
+    size_t group = Hv / Hk;
+    long units = (long)(B * Hv);
+#ifdef _OPENMP
+    int nt = nthreads > 0 ? nthreads : omp_get_max_threads();
+#pragma omp parallel for schedule(dynamic, 1) num_threads(nt)
+#endif
+    for (long u = 0; u < units; ++u) {
+        size_t b = (size_t)u / Hv, h = (size_t)u % Hv, hk = h / group;
+        float qs[512];
+        float *Sh = S + (b * Hv + h) * dk * dv;
+        for (size_t t = 0; t < T; ++t) {
+            const float *qt = q + ((b * T + t) * Hk + hk) * dk;
+            for (size_t j = 0; j < dk; ++j) qs[j] = qt[j] * scale;
+            size_t gi = (b * T + t) * Hv + h;
+            orc_delta_rule_step(Sh, k + ((b * T + t) * Hk + hk) * dk,
+                                v + ((b * T + t) * Hv + h) * dv, qs, beta[gi], expf(g[gi]),
+                                o + ((b * T + t) * Hv + h) * dv, dk, dv);
+        }
+    }
+}
+
+/* ------------------------------------------------------------------------
+ * a6: chunkwise WY form, in double, written from the math of
+ * docs/GDN_ARCHITECTURE_AUDIT.md:142-153 (the reference has no code for it; it
+ * reaches it through HF transformers' torch_chunk_gated_delta_rule).  Per
+ * (b, h) and chunk of C rows with in-chunk cumulative log-decay G_r:
+ *   A[r][s] = beta_r (k_r . k_s) exp(G_r - G_s)             (s < r)
+ *   Tm      = (I + A)^-1                                     (unit lower)
+ *   W       = Tm (beta * K * exp(G)),   U = Tm (beta * V)
+ *   V'      = U - W S
+ *   O       = (Q * exp(G)) S + (Q K^T * exp(G_r - G_s))_{s<=r} V'
+ *   S      <- exp(G_last) S + (K * exp(G_last - G))^T V'
+ * W and U are found by forward substitution on (I + A).  Rows past T are
+ * treated as padding (k = v = 0, beta = 0, g = 0), as HF pads.
+ * Used to check that the chunk decomposition equals the token loop; the token
+ * loop (orc_delta_rule_seq) is the parity oracle for the CUDA chunk kernel.
+ * ---------------------------------------------------------------------- */
+void orc_chunk_wy_f64(float *S_io, const float *q, const float *k, const float *v,
+                      const float *g, const float *beta, float *o, size_t B, size_t T,
+                      size_t Hk, size_t Hv, size_t dk, size_t dv, size_t C, float scale,
+                      int nthreads) {
+    size_t group = Hv / Hk;
+    long units = (long)(B * Hv);
+#ifdef _OPENMP
+    int nt = nthreads > 0 ? nthreads : omp_get_max_threads();
+#pragma omp parallel for schedule(dynamic, 1) num_threads(nt)
+#endif
+    for (long u = 0; u < units; ++u) {
+        size_t b = (size_t)u / Hv, h = (size_t)u % Hv, hk = h / group;
+        double *S = malloc(sizeof(double) * dk * dv);
+        double *Kc = malloc(sizeof(double) * C * dk), *Qc = malloc(sizeof(double) * C * dk);
+        double *Vc = malloc(sizeof(double) * C * dv), *W = malloc(sizeof(double) * C * dk);
+        double *U = malloc(sizeof(double) * C * dv), *A = malloc(sizeof(double) * C * C);
+        double *G = malloc(sizeof(double) * C), *bt = malloc(sizeof(double) * C);
+        double *Vp = malloc(sizeof(double) * C * dv);
+        float *Sf = S_io + (b * Hv + h) * dk * dv;
+        for (size_t i = 0; i < dk * dv; ++i) S[i] = Sf[i];
+        for (size_t c0 = 0; c0 < T; c0 += C) {
+            double run = 0.0;
+            for (size_t r = 0; r < C; ++r) {
+                size_t t = c0 + r;
+                int live = t < T;
+                size_t gi = (b * T + t) * Hv + h;
+                run += live ? (double)g[gi] : 0.0;
+                G[r] = run;
+                bt[r] = live ? (double)beta[gi] : 0.0;
+                for (size_t j = 0; j < dk; ++j) {
+                    Kc[r * dk + j] = live ? (double)k[((b * T + t) * Hk + hk) * dk + j] : 0.0;
+                    Qc[r * dk + j] =
+                        live ? (double)q[((b * T + t) * Hk + hk) * dk + j] * (double)scale : 0.0;
+                }
+                for (size_t i = 0; i < dv; ++i)
+                    Vc[r * dv + i] = live ? (double)v[((b * T + t) * Hv + h) * dv + i] : 0.0;
+            }
+            for (size_t r = 0; r < C; ++r)
+                for (size_t s = 0; s < r; ++s) {
+                    double d = 0.0;
+                    for (size_t j = 0; j < dk; ++j) d += Kc[r * dk + j] * Kc[s * dk + j];
+                    A[r * C + s] = bt[r] * d * exp(G[r] - G[s]);
+                }
+            for (size_t r = 0; r < C; ++r) {
+                double eg = exp(G[r]);
+                for (size_t j = 0; j < dk; ++j) {
+                    double acc = bt[r] * Kc[r * dk + j] * eg;
+                    for (size_t s = 0; s < r; ++s) acc -= A[r * C + s] * W[s * dk + j];
+                    W[r * dk + j] = acc;
+                }
+                for (size_t i = 0; i < dv; ++i) {
+                    double acc = bt[r] * Vc[r * dv + i];
+                    for (size_t s = 0; s < r; ++s) acc -= A[r * C + s] * U[s * dv + i];
+                    U[r * dv + i] = acc;
+                }
+            }
+            for (size_t r = 0; r < C; ++r)
+                for (size_t i = 0; i < dv; ++i) {
+                    double acc = U[r * dv + i];
+                    for (size_t j = 0; j < dk; ++j) acc -= W[r * dk + j] * S[j * dv + i];
+                    Vp[r * dv + i] = acc;
+                }
+            for (size_t r = 0; r < C && c0 + r < T; ++r) {
+                double eg = exp(G[r]);
+                for (size_t i = 0; i < dv; ++i) {
+                    double acc = 0.0;
+                    for (size_t j = 0; j < dk; ++j) acc += Qc[r * dk + j] * eg * S[j * dv + i];
+                    for (size_t s = 0; s <= r; ++s) {
+                        double qk = 0.0;
+                        for (size_t j = 0; j < dk; ++j) qk += Qc[r * dk + j] * Kc[s * dk + j];
+                        acc += qk * exp(G[r] - G[s]) * Vp[s * dv + i];
+                    }
+                    o[((b * T + c0 + r) * Hv + h) * dv + i] = (float)acc;
+                }
+            }
+            double gl = G[C - 1], egl = exp(gl);
+            for (size_t j = 0; j < dk; ++j)
+                for (size_t i = 0; i < dv; ++i) {
+                    double acc = egl * S[j * dv + i];
+                    for (size_t r = 0; r < C; ++r)
+                        acc += Kc[r * dk + j] * exp(gl - G[r]) * Vp[r * dv + i];
+                    S[j * dv + i] = acc;
+                }
+        }
+        for (size_t i = 0; i < dk * dv; ++i) Sf[i] = (float)S[i];
+        free(S); free(Kc); free(Qc); free(Vc); free(W); free(U); free(A); free(G);
+        free(bt); free(Vp);
+    }
+}
+
+/* ------------------------------------------------------------------------
+ * f4: GDN-2 decoupled-gating channel scan s = w*x + s*(g*b).
+ * src/orionsbelt/engines/cpu/kernels/gdn_sve.c:865-872 (scalar branch).
+ * ---------------------------------------------------------------------- */
+void orc_gdn2_gated_scan_f32(const float *g, const float *bg, const float *wg,
+                             const float *x, float *s, float *state, size_t seq,
+                             size_t ch) {
+    for (size_t c = 0; c < ch; ++c) {
+        float acc = state[c];
+        for (size_t t = 0; t < seq; ++t) {
+            size_t i = t * ch + c;
+            acc = wg[i] * x[i] + acc * (g[i] * bg[i]);
+            s[i] = acc;
+        }
+        state[c] = acc;
+    }
+}
+
+int orc_num_threads(void) {
+#ifdef _OPENMP
+    return omp_get_max_threads();
+#else
+    return 1;
+#endif
+}

@@ -1,0 +1,113 @@
+"""ctypes binding of libkai_gdn_cuda.so (the C ABI in include/kai_gdn_cuda.h).
+
+The library is loaded from this package directory (built in-tree by
+orionsbelt_b200/build.py).  There is no fallback: if the library is missing
+or a symbol is absent, loading raises.
+"""
+from __future__ import annotations
+
+import ctypes as C
+from pathlib import Path
+
+LIB_PATH = Path(__file__).resolve().parent / "libkai_gdn_cuda.so"
+
+OK, ERR_INVALID, ERR_CUDA, ERR_UNSUPPORTED, ERR_NOMEM = 0, 1, 2, 3, 4
+F32, BF16, F16 = 0, 1, 2
+
+_sz = C.c_size_t
+_vp = C.c_void_p
+_i = C.c_int
+_f = C.c_float
+
+
+class DecodeArgs(C.Structure):
+    """struct kai_gdn_decode_args."""
+    _fields_ = [("state", _vp), ("q", _vp), ("k", _vp), ("v", _vp), ("g", _vp), ("beta", _vp), ("o", _vp),
+                ("batch", _sz), ("heads_k", _sz), ("heads_v", _sz), ("dk", _sz), ("dv", _sz),
+                ("scale", _f), ("in_dtype", _i), ("state_dtype", _i), ("out_dtype", _i)]
+
+
+class ChunkArgs(C.Structure):
+    """struct kai_gdn_chunk_args."""
+    _fields_ = [("q", _vp), ("k", _vp), ("v", _vp), ("g", _vp), ("beta", _vp), ("state", _vp), ("o", _vp),
+                ("batch", _sz), ("seq", _sz), ("heads_k", _sz), ("heads_v", _sz), ("dk", _sz), ("dv", _sz),
+                ("chunk", _sz), ("scale", _f), ("in_dtype", _i), ("state_dtype", _i), ("out_dtype", _i)]
+
+
+# name -> (restype, argtypes); every symbol declared in include/kai_gdn_cuda.h.
+SIGNATURES = {
+    # drop-in (void)
+    "kai_run_gdn_cumdecay_f32_sve": (None, [_vp, _vp, _sz, _sz]),
+    "kai_run_gdn_gated_scan_f32_sve": (None, [_vp, _vp, _vp, _vp, _sz, _sz]),
+    "kai_run_gdn_causal_dwconv1d_f32_k4_sve": (None, [_vp, _vp, _vp, _vp, _sz, _sz]),
+    "kai_run_gdn_gemv_f32_f32_f32_1x4_neon": (None, [_vp, _vp, _vp, _sz, _sz]),
+    "gdn_cumdecay_f32": (None, [_vp, _vp, _sz, _sz]),
+    "gdn_gated_scan_f32": (None, [_vp, _vp, _vp, _vp, _sz, _sz]),
+    "gdn_causal_dwconv1d_f32": (None, [_vp, _vp, _vp, _vp, _sz, _sz]),
+    "gdn_cumdecay_f16": (None, [_vp, _vp, _sz, _sz]),
+    "gdn_gated_scan_f16": (None, [_vp, _vp, _vp, _vp, _sz, _sz]),
+    "gdn_cumdecay_bf16": (None, [_vp, _vp, _sz, _sz]),
+    "gdn_gated_scan_bf16": (None, [_vp, _vp, _vp, _vp, _sz, _sz]),
+    "gdn2_gated_scan_f32": (None, [_vp, _vp, _vp, _vp, _vp, _vp, _sz, _sz]),
+    "gdn_delta_rule_matmul": (None, [_vp, _vp, _vp, _sz, _sz, _sz]),
+    # device, stream-ordered (int status)
+    "kai_run_gdn_cumdecay_sm100a": (_i, [_vp, _vp, _i, _sz, _sz, _sz, _vp]),
+    "kai_run_gdn_cumsum_f32_sm100a": (_i, [_vp, _vp, _sz, _sz, _sz, _vp]),
+    "kai_run_gdn_gated_scan_sm100a": (_i, [_vp, _vp, _vp, _vp, _i, _sz, _sz, _sz, _vp]),
+    "kai_run_gdn2_gated_scan_f32_sm100a": (_i, [_vp, _vp, _vp, _vp, _vp, _vp, _sz, _sz, _sz, _vp]),
+    "kai_run_gdn_causal_dwconv1d_k4_sm100a": (_i, [_vp, _vp, _vp, _vp, _i, _sz, _sz, _sz, _vp]),
+    "kai_run_gdn_matmul_f32_sm100a": (_i, [_vp, _vp, _vp, _sz, _sz, _sz, _vp]),
+    "kai_run_gdn_delta_rule_decode_sm100a": (_i, [C.POINTER(DecodeArgs), _vp]),
+    "kai_run_gdn_chunk_delta_rule_sm100a": (_i, [C.POINTER(ChunkArgs), _vp]),
+    # control
+    "kai_gdn_cuda_set_device": (_i, [_i]),
+    "kai_gdn_cuda_device_count": (_i, []),
+    "kai_gdn_cuda_last_status": (_i, []),
+    "kai_gdn_cuda_last_error": (C.c_char_p, []),
+    "kai_gdn_cuda_clear_error": (None, []),
+    "kai_gdn_cuda_version": (C.c_char_p, []),
+}
+
+
+class GdnError(RuntimeError):
+    def __init__(self, status: int, msg: str):
+        super().__init__(f"kai_gdn_cuda status {status}: {msg}")
+        self.status = status
+
+
+_lib = None
+
+
+def lib():
+    """Load (once) and return the CDLL with every declared signature bound."""
+    global _lib
+    if _lib is None:
+        if not LIB_PATH.exists():
+            raise ImportError(f"{LIB_PATH} is missing: build it with `python -m orionsbelt_b200.build`")
+        h = C.CDLL(str(LIB_PATH))
+        for name, (res, args) in SIGNATURES.items():
+            fn = getattr(h, name)  # AttributeError if the library lacks a declared symbol
+            fn.restype = res
+            fn.argtypes = args
+        _lib = h
+    return _lib
+
+
+def last_error() -> str:
+    return (lib().kai_gdn_cuda_last_error() or b"").decode()
+
+
+def check(status: int) -> None:
+    """Raise GdnError for a non-zero status from a device entry point."""
+    if status != OK:
+        raise GdnError(status, last_error())
+
+
+def check_dropin() -> None:
+    """Raise if the last drop-in (void) call on this thread recorded a failure."""
+    L = lib()
+    st = L.kai_gdn_cuda_last_status()
+    if st != OK:
+        msg = last_error()
+        L.kai_gdn_cuda_clear_error()
+        raise GdnError(st, msg)

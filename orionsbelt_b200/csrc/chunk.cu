@@ -1,0 +1,329 @@
+// chunk.cu -- chunkwise (WY / UT-transform) gated delta-rule scan, fp32 on
+// CUDA cores (sm_100a).
+//
+// The form named in docs/GDN_ARCHITECTURE_AUDIT.md:142-153 (the reference
+// reaches it only through HF transformers' torch_chunk_gated_delta_rule).
+// Per (batch b, value head h) and chunk of C = 64 tokens, with G_r the
+// in-chunk cumulative log-decay, Q already multiplied by `scale`:
+//   A[r][s] = beta_r (k_r . k_s) exp(G_r - G_s)              s <  r
+//   P[r][s] = (q_r . k_s) exp(G_r - G_s)                     s <= r
+//   W = (I + A)^-1 (beta * K * exp(G)),   U = (I + A)^-1 (beta * V)
+//   V' = U - W S
+//   O  = (Q * exp(G)) S + P V'
+//   S <- exp(G_last) S + (K * exp(G_last - G))^T V'
+// (I + A)^-1 is applied by forward substitution, one thread per column.
+//
+// Work split: one CTA per (b, h, block of DVB value columns).  Every quantity
+// above except S, U, V', O depends on the key side only, and the state's value
+// columns evolve independently, so value-column blocks are exact splits (the
+// key-side work is recomputed per block).  The state block lives in shared
+// memory for the whole sequence; the sequence is walked chunk by chunk.
+//
+// All products use 16x16 thread tiles with fp32 FMA; this is the fp32-exact
+// path (1e-4 relative L2 against the token loop) and the reference point for
+// the tensor-core kernel.
+#include "gdn_internal.cuh"
+
+namespace gdn {
+namespace {
+
+constexpr int CH = 64;        // chunk length
+constexpr int THREADS = 256;  // 16 x 16
+
+__device__ __forceinline__ float ld_any(const void *p, size_t i, int dt) {
+    switch (dt) {
+        case KAI_GDN_BF16: return __bfloat162float(static_cast<const __nv_bfloat16 *>(p)[i]);
+        case KAI_GDN_F16: return __half2float(static_cast<const __half *>(p)[i]);
+        default: return static_cast<const float *>(p)[i];
+    }
+}
+__device__ __forceinline__ void st_any(void *p, size_t i, int dt, float v) {
+    switch (dt) {
+        case KAI_GDN_BF16: static_cast<__nv_bfloat16 *>(p)[i] = __float2bfloat16_rn(v); break;
+        case KAI_GDN_F16: static_cast<__half *>(p)[i] = __float2half_rn(v); break;
+        default: static_cast<float *>(p)[i] = v;
+    }
+}
+
+// acc[i][j] += sum_k a(ty + 16 i, k) * b(k, tx + 16 j)
+//   a(m, k) = TA ? A[k*lda + m] : A[m*lda + k];  b(k, n) = TB ? B[n*ldb + k] : B[k*ldb + n]
+template <int MI, int NJ, bool TA, bool TB>
+__device__ __forceinline__ void mm(float (&acc)[MI][NJ], const float *A, int lda,
+                                   const float *B, int ldb, int kd) {
+    const int tx = threadIdx.x % 16, ty = threadIdx.x / 16;
+#pragma unroll 4
+    for (int k = 0; k < kd; ++k) {
+        float a[MI], b[NJ];
+#pragma unroll
+        for (int i = 0; i < MI; ++i) a[i] = TA ? A[k * lda + ty + 16 * i] : A[(ty + 16 * i) * lda + k];
+#pragma unroll
+        for (int j = 0; j < NJ; ++j) b[j] = TB ? B[(tx + 16 * j) * ldb + k] : B[k * ldb + tx + 16 * j];
+#pragma unroll
+        for (int i = 0; i < MI; ++i)
+#pragma unroll
+            for (int j = 0; j < NJ; ++j) acc[i][j] = fmaf(a[i], b[j], acc[i][j]);
+    }
+}
+
+template <int MI, int NJ>
+__device__ __forceinline__ void zero(float (&acc)[MI][NJ]) {
+#pragma unroll
+    for (int i = 0; i < MI; ++i)
+#pragma unroll
+        for (int j = 0; j < NJ; ++j) acc[i][j] = 0.f;
+}
+
+template <int DK, int DVB>
+struct Smem {
+    static constexpr int LDK = DK + 1;   // odd strides: conflict-free column reads
+    static constexpr int LDV = DVB + 1;
+    static constexpr int LDP = CH + 1;
+    float K[CH * LDK];     // K, later K * exp(G_last - G)
+    float Q[CH * LDK];     // scale * Q, later * exp(G)
+    float W[CH * LDK];     // beta * K * exp(G), then W
+    float V[CH * LDV];     // V, beta * V, U, then V'
+    float A[CH * LDP];     // strictly lower A
+    float P[CH * LDP];     // lower-with-diagonal P
+    float S[DK * LDV];     // state block [DK][DVB]
+    float G[CH], eG[CH], eGl[CH], beta[CH];
+};
+
+template <int DK, int DVB, int SDT>
+__global__ void __launch_bounds__(THREADS, 1) chunk_scan_fp32_kernel(kai_gdn_chunk_args p) {
+    using SM = Smem<DK, DVB>;
+    constexpr int LDK = SM::LDK, LDV = SM::LDV, LDP = SM::LDP;
+    extern __shared__ __align__(16) unsigned char smem_raw[];
+    SM &sm = *reinterpret_cast<SM *>(smem_raw);
+
+    const int t = threadIdx.x, tx = t % 16, ty = t / 16;
+    const long long Hv = (long long)p.heads_v, Hk = (long long)p.heads_k;
+    const long long T = (long long)p.seq, DV = (long long)p.dv;
+    const int nvb = (int)(DV / DVB);
+    const long long unit = blockIdx.x / nvb;  // b * Hv + h
+    const int vb = blockIdx.x % nvb;
+    const long long b = unit / Hv, h = unit % Hv, hk = h / (Hv / Hk);
+    const long long v0 = (long long)vb * DVB;
+
+    // State block in.
+    using S = Store<SDT>;
+    const typename S::T *st_in = static_cast<const typename S::T *>(p.state) + (size_t)unit * DK * DV;
+    for (int e = t; e < DK * DVB; e += THREADS) {
+        int d = e / DVB, n = e % DVB;
+        sm.S[d * LDV + n] = S::load(st_in + (size_t)d * DV + v0 + n);
+    }
+
+    for (long long c0 = 0; c0 < T; c0 += CH) {
+        // ---- loads (rows past T are zero padding with g = beta = 0)
+        for (int e = t; e < CH * DK; e += THREADS) {
+            int r = e / DK, d = e % DK;
+            long long tok = c0 + r;
+            float kv = 0.f, qv = 0.f;
+            if (tok < T) {
+                size_t i = ((size_t)(b * T + tok) * Hk + hk) * DK + d;
+                kv = ld_any(p.k, i, p.in_dtype);
+                qv = ld_any(p.q, i, p.in_dtype) * p.scale;
+            }
+            sm.K[r * LDK + d] = kv;
+            sm.Q[r * LDK + d] = qv;
+        }
+        for (int e = t; e < CH * DVB; e += THREADS) {
+            int r = e / DVB, n = e % DVB;
+            long long tok = c0 + r;
+            sm.V[r * LDV + n] =
+                tok < T ? ld_any(p.v, ((size_t)(b * T + tok) * Hv + h) * DV + v0 + n, p.in_dtype) : 0.f;
+        }
+        if (t < 32) {
+            // In-chunk inclusive cumsum of g (2 rows per lane), beta.
+            float g0 = 0.f, g1 = 0.f, b0 = 0.f, b1 = 0.f;
+            long long r0 = c0 + 2 * t, r1 = r0 + 1;
+            if (r0 < T) { g0 = p.g[(size_t)(b * T + r0) * Hv + h]; b0 = p.beta[(size_t)(b * T + r0) * Hv + h]; }
+            if (r1 < T) { g1 = p.g[(size_t)(b * T + r1) * Hv + h]; b1 = p.beta[(size_t)(b * T + r1) * Hv + h]; }
+            float pair = g0 + g1, incl = pair;
+#pragma unroll
+            for (int o = 1; o < 32; o <<= 1) {
+                float u = __shfl_up_sync(0xffffffffu, incl, o);
+                if (t >= o) incl += u;
+            }
+            float excl = incl - pair;
+            sm.G[2 * t] = excl + g0;
+            sm.G[2 * t + 1] = incl;
+            sm.beta[2 * t] = b0;
+            sm.beta[2 * t + 1] = b1;
+        }
+        __syncthreads();
+        if (t < CH) {
+            sm.eG[t] = expf(sm.G[t]);
+            sm.eGl[t] = expf(sm.G[CH - 1] - sm.G[t]);
+        }
+        // ---- A = beta K K^T decay (s < r), P = Q K^T decay (s <= r)
+        {
+            float kk[4][4], qk[4][4];
+            zero(kk);
+            zero(qk);
+            const int tx_ = tx, ty_ = ty;
+#pragma unroll 2
+            for (int d = 0; d < DK; ++d) {
+                float kr[4], qr[4], ks[4];
+#pragma unroll
+                for (int i = 0; i < 4; ++i) {
+                    kr[i] = sm.K[(ty_ + 16 * i) * LDK + d];
+                    qr[i] = sm.Q[(ty_ + 16 * i) * LDK + d];
+                    ks[i] = sm.K[(tx_ + 16 * i) * LDK + d];
+                }
+#pragma unroll
+                for (int i = 0; i < 4; ++i)
+#pragma unroll
+                    for (int j = 0; j < 4; ++j) {
+                        kk[i][j] = fmaf(kr[i], ks[j], kk[i][j]);
+                        qk[i][j] = fmaf(qr[i], ks[j], qk[i][j]);
+                    }
+            }
+#pragma unroll
+            for (int i = 0; i < 4; ++i)
+#pragma unroll
+                for (int j = 0; j < 4; ++j) {
+                    int r = ty + 16 * i, s = tx + 16 * j;
+                    float dec = r >= s ? expf(sm.G[r] - sm.G[s]) : 0.f;
+                    sm.A[r * LDP + s] = r > s ? sm.beta[r] * kk[i][j] * dec : 0.f;
+                    sm.P[r * LDP + s] = qk[i][j] * dec;
+                }
+        }
+        __syncthreads();
+        // ---- right-hand sides: beta K exp(G) into W, beta V in place
+        for (int e = t; e < CH * DK; e += THREADS) {
+            int r = e / DK, d = e % DK;
+            sm.W[r * LDK + d] = sm.beta[r] * sm.K[r * LDK + d] * sm.eG[r];
+        }
+        for (int e = t; e < CH * DVB; e += THREADS) {
+            int r = e / DVB, n = e % DVB;
+            sm.V[r * LDV + n] *= sm.beta[r];
+        }
+        __syncthreads();
+        // ---- forward substitution X_r = R_r - sum_{s<r} A[r][s] X_s, per column
+        for (int col = t; col < DK + DVB; col += THREADS) {
+            float *X = col < DK ? sm.W + col : sm.V + (col - DK);
+            const int ld = col < DK ? LDK : LDV;
+            for (int r = 1; r < CH; ++r) {
+                float acc = X[r * ld];
+                for (int s = 0; s < r; ++s) acc = fmaf(-sm.A[r * LDP + s], X[s * ld], acc);
+                X[r * ld] = acc;
+            }
+        }
+        __syncthreads();
+        // ---- V' = U - W S (in place over U);  Q *= exp(G);  K *= exp(G_last - G)
+        {
+            float ws[4][DVB / 16];
+            zero(ws);
+            mm<4, DVB / 16, false, false>(ws, sm.W, LDK, sm.S, LDV, DK);
+#pragma unroll
+            for (int i = 0; i < 4; ++i)
+#pragma unroll
+                for (int j = 0; j < DVB / 16; ++j) sm.V[(ty + 16 * i) * LDV + tx + 16 * j] -= ws[i][j];
+        }
+        for (int e = t; e < CH * DK; e += THREADS) {
+            int r = e / DK, d = e % DK;
+            sm.Q[r * LDK + d] *= sm.eG[r];
+            sm.K[r * LDK + d] *= sm.eGl[r];
+        }
+        __syncthreads();
+        // ---- O = (Q exp(G)) S + P V'
+        {
+            float o[4][DVB / 16];
+            zero(o);
+            mm<4, DVB / 16, false, false>(o, sm.Q, LDK, sm.S, LDV, DK);
+            mm<4, DVB / 16, false, false>(o, sm.P, LDP, sm.V, LDV, CH);
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                long long tok = c0 + ty + 16 * i;
+                if (tok < T) {
+#pragma unroll
+                    for (int j = 0; j < DVB / 16; ++j)
+                        st_any(p.o, ((size_t)(b * T + tok) * Hv + h) * DV + v0 + tx + 16 * j, p.out_dtype,
+                               o[i][j]);
+                }
+            }
+        }
+        __syncthreads();
+        // ---- S = exp(G_last) S + (K exp(G_last - G))^T V'
+        {
+            constexpr int MI = DK / 16, NJ = DVB / 16;
+            float acc[MI][NJ];
+            const float egl = sm.eG[CH - 1];
+#pragma unroll
+            for (int i = 0; i < MI; ++i)
+#pragma unroll
+                for (int j = 0; j < NJ; ++j) acc[i][j] = egl * sm.S[(ty + 16 * i) * LDV + tx + 16 * j];
+            mm<MI, NJ, true, false>(acc, sm.K, LDK, sm.V, LDV, CH);
+#pragma unroll
+            for (int i = 0; i < MI; ++i)
+#pragma unroll
+                for (int j = 0; j < NJ; ++j) sm.S[(ty + 16 * i) * LDV + tx + 16 * j] = acc[i][j];
+        }
+        __syncthreads();
+    }
+
+    typename S::T *st_out = static_cast<typename S::T *>(p.state) + (size_t)unit * DK * DV;
+    for (int e = t; e < DK * DVB; e += THREADS) {
+        int d = e / DVB, n = e % DVB;
+        S::store(st_out + (size_t)d * DV + v0 + n, sm.S[d * LDV + n]);
+    }
+}
+
+template <int DK, int DVB>
+int run_chunk(const kai_gdn_chunk_args *a, cudaStream_t st) {
+    const size_t smem = sizeof(Smem<DK, DVB>);
+    const long long blocks = (long long)(a->batch * a->heads_v) * (long long)(a->dv / DVB);
+    if (blocks > 0x7fffffffll) return set_error(KAI_GDN_ERR_UNSUPPORTED, "chunk: too many heads");
+    int rc = 0;
+    switch (a->state_dtype) {
+        case KAI_GDN_F32:
+            rc = check_cuda(cudaFuncSetAttribute(chunk_scan_fp32_kernel<DK, DVB, KAI_GDN_F32>,
+                                                 cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem),
+                            "chunk: smem attribute");
+            if (!rc) chunk_scan_fp32_kernel<DK, DVB, KAI_GDN_F32><<<(unsigned)blocks, THREADS, smem, st>>>(*a);
+            break;
+        case KAI_GDN_F16:
+            rc = check_cuda(cudaFuncSetAttribute(chunk_scan_fp32_kernel<DK, DVB, KAI_GDN_F16>,
+                                                 cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem),
+                            "chunk: smem attribute");
+            if (!rc) chunk_scan_fp32_kernel<DK, DVB, KAI_GDN_F16><<<(unsigned)blocks, THREADS, smem, st>>>(*a);
+            break;
+        case KAI_GDN_BF16:
+            rc = check_cuda(cudaFuncSetAttribute(chunk_scan_fp32_kernel<DK, DVB, KAI_GDN_BF16>,
+                                                 cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem),
+                            "chunk: smem attribute");
+            if (!rc) chunk_scan_fp32_kernel<DK, DVB, KAI_GDN_BF16><<<(unsigned)blocks, THREADS, smem, st>>>(*a);
+            break;
+    }
+    if (rc) return rc;
+    return check_launch("chunk_delta_rule_fp32");
+}
+
+}  // namespace
+
+int launch_chunk_fp32(const kai_gdn_chunk_args *a, cudaStream_t st) {
+    if (a->dk == 128 && a->dv % 64 == 0) return run_chunk<128, 64>(a, st);
+    if (a->dk == 64 && a->dv % 64 == 0) return run_chunk<64, 64>(a, st);
+    if (a->dk == 32 && a->dv % 32 == 0) return run_chunk<32, 32>(a, st);
+    if (a->dk == 64 && a->dv % 32 == 0) return run_chunk<64, 32>(a, st);
+    if (a->dk == 128 && a->dv % 32 == 0) return run_chunk<128, 32>(a, st);
+    return set_error(KAI_GDN_ERR_UNSUPPORTED, "chunk: dk %zu / dv %zu (supported: dk in {32,64,128}, "
+                     "dv a multiple of 32)", a->dk, a->dv);
+}
+
+int launch_chunk(const kai_gdn_chunk_args *a, cudaStream_t st) {
+    if (!a) return set_error(KAI_GDN_ERR_INVALID, "chunk: null args");
+    if (a->batch == 0 || a->heads_v == 0 || a->seq == 0) return KAI_GDN_OK;
+    if (!a->q || !a->k || !a->v || !a->g || !a->beta || !a->state || !a->o)
+        return set_error(KAI_GDN_ERR_INVALID, "chunk: null pointer");
+    if (a->heads_k == 0 || a->heads_v % a->heads_k)
+        return set_error(KAI_GDN_ERR_INVALID, "chunk: heads_v %zu not a multiple of heads_k %zu",
+                         a->heads_v, a->heads_k);
+    if (!valid_dtype(a->in_dtype) || !valid_dtype(a->state_dtype) || !valid_dtype(a->out_dtype))
+        return set_error(KAI_GDN_ERR_INVALID, "chunk: bad dtype");
+    if (a->chunk != (size_t)CH)
+        return set_error(KAI_GDN_ERR_UNSUPPORTED, "chunk: chunk length %zu (supported: 64)", a->chunk);
+    return launch_chunk_fp32(a, st);
+}
+
+}  // namespace gdn

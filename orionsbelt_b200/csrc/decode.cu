@@ -1,0 +1,183 @@
+// decode.cu -- single-token matrix-state gated delta-rule step on sm_100a.
+//
+// Per (batch b, value head h), key head hk = h / (Hv/Hk), a = exp(g[b][h]):
+//   S *= a;  kv_i = sum_j S[j][i] k_j;  delta_i = (v_i - kv_i) * beta;
+//   S[j][i] += k_j delta_i;  o_i = sum_j S[j][i] (scale q_j)
+// gpu/gdn_gpu_kernels.cl:158-206 and its C twin gpu/gdn_gpu_validate.c:100-118.
+// The OpenCL kernel makes four passes over S (decay, retrieve, write, read);
+// here S is read from HBM once and written once: the CTA holds its head's
+// whole dk x dv state in registers (64 floats per thread at 128x128), so the
+// kernel is bound by 2 * dk * dv * sizeof(state) bytes per head.
+//
+// Thread layout: DV/4 threads cover one row of S with 16-byte accesses (a warp
+// reads 512 contiguous bytes at dv = 128), and the 256 threads take rows
+// j = rg, rg + RPP, ...  Column sums over j are per-thread partials reduced
+// across row groups through shared memory.
+#include "gdn_internal.cuh"
+
+namespace gdn {
+namespace {
+
+constexpr int THREADS = 256;
+
+__device__ __forceinline__ float load_any(const void *p, size_t i, int dt) {
+    switch (dt) {
+        case KAI_GDN_BF16: return __bfloat162float(static_cast<const __nv_bfloat16 *>(p)[i]);
+        case KAI_GDN_F16: return __half2float(static_cast<const __half *>(p)[i]);
+        default: return static_cast<const float *>(p)[i];
+    }
+}
+__device__ __forceinline__ void store_any(void *p, size_t i, int dt, float v) {
+    switch (dt) {
+        case KAI_GDN_BF16: static_cast<__nv_bfloat16 *>(p)[i] = __float2bfloat16_rn(v); break;
+        case KAI_GDN_F16: static_cast<__half *>(p)[i] = __float2half_rn(v); break;
+        default: static_cast<float *>(p)[i] = v;
+    }
+}
+
+// 4 consecutive state elements.
+template <int SDT>
+__device__ __forceinline__ float4 ld4(const void *base, size_t idx) {
+    if (SDT == KAI_GDN_F32) return *reinterpret_cast<const float4 *>(static_cast<const float *>(base) + idx);
+    uint2 u = *reinterpret_cast<const uint2 *>(static_cast<const uint16_t *>(base) + idx);
+    using S = Store<SDT>;
+    const typename S::T *h = reinterpret_cast<const typename S::T *>(&u);
+    return make_float4(S::load(h), S::load(h + 1), S::load(h + 2), S::load(h + 3));
+}
+template <int SDT>
+__device__ __forceinline__ void st4(void *base, size_t idx, float4 v) {
+    if (SDT == KAI_GDN_F32) {
+        *reinterpret_cast<float4 *>(static_cast<float *>(base) + idx) = v;
+        return;
+    }
+    using S = Store<SDT>;
+    uint2 u;
+    typename S::T *h = reinterpret_cast<typename S::T *>(&u);
+    S::store(h, v.x);
+    S::store(h + 1, v.y);
+    S::store(h + 2, v.z);
+    S::store(h + 3, v.w);
+    *reinterpret_cast<uint2 *>(static_cast<uint16_t *>(base) + idx) = u;
+}
+
+template <int D, int SDT>
+__global__ void __launch_bounds__(THREADS, 2) decode_step_kernel(kai_gdn_decode_args p) {
+    constexpr int DK = D, DV = D;
+    constexpr int CPR = DV / 4;          // threads per row
+    constexpr int RPP = THREADS / CPR;   // rows per pass
+    constexpr int RPT = DK / RPP;        // rows per thread
+    static_assert(RPT >= 1 && DK % RPP == 0, "shape");
+
+    __shared__ float ks[DK], qs[DK], vs[DV], dl[DV];
+    __shared__ float red[RPP][DV + 4];
+
+    const long long unit = blockIdx.x;   // b * Hv + h
+    const long long Hv = (long long)p.heads_v, Hk = (long long)p.heads_k;
+    const long long b = unit / Hv, h = unit % Hv, hk = h / (Hv / Hk);
+    const int t = threadIdx.x, cq = t % CPR, rg = t / CPR;
+    const size_t sbase = (size_t)unit * DK * DV;
+
+    // Issue the state loads first: they are the bytes that matter.
+    float4 s[RPT];
+#pragma unroll
+    for (int r = 0; r < RPT; ++r) s[r] = ld4<SDT>(p.state, sbase + (size_t)(rg + RPP * r) * DV + 4 * cq);
+
+    const size_t kq = (size_t)(b * Hk + hk) * DK;
+    for (int j = t; j < DK; j += THREADS) {
+        ks[j] = load_any(p.k, kq + j, p.in_dtype);
+        qs[j] = __fmul_rn(load_any(p.q, kq + j, p.in_dtype), p.scale);
+    }
+    for (int i = t; i < DV; i += THREADS) vs[i] = load_any(p.v, (size_t)unit * DV + i, p.in_dtype);
+    const float a = expf(p.g[unit]);
+    const float beta = p.beta[unit];
+    __syncthreads();
+
+    // Decay and retrieve: kv partial over this thread's rows.
+    float4 kv = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+    for (int r = 0; r < RPT; ++r) {
+        const float kj = ks[rg + RPP * r];
+        s[r].x = __fmul_rn(s[r].x, a);
+        s[r].y = __fmul_rn(s[r].y, a);
+        s[r].z = __fmul_rn(s[r].z, a);
+        s[r].w = __fmul_rn(s[r].w, a);
+        kv.x = fmaf(s[r].x, kj, kv.x);
+        kv.y = fmaf(s[r].y, kj, kv.y);
+        kv.z = fmaf(s[r].z, kj, kv.z);
+        kv.w = fmaf(s[r].w, kj, kv.w);
+    }
+    *reinterpret_cast<float4 *>(&red[rg][4 * cq]) = kv;
+    __syncthreads();
+    for (int i = t; i < DV; i += THREADS) {
+        float acc = 0.f;
+#pragma unroll
+        for (int g2 = 0; g2 < RPP; ++g2) acc += red[g2][i];
+        dl[i] = (vs[i] - acc) * beta;
+    }
+    __syncthreads();
+
+    // Rank-1 write, read-out partial, and the store of the new state.
+    const float4 d = *reinterpret_cast<const float4 *>(&dl[4 * cq]);
+    float4 o = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+    for (int r = 0; r < RPT; ++r) {
+        const int j = rg + RPP * r;
+        const float kj = ks[j], qj = qs[j];
+        s[r].x = fmaf(kj, d.x, s[r].x);
+        s[r].y = fmaf(kj, d.y, s[r].y);
+        s[r].z = fmaf(kj, d.z, s[r].z);
+        s[r].w = fmaf(kj, d.w, s[r].w);
+        st4<SDT>(p.state, sbase + (size_t)j * DV + 4 * cq, s[r]);
+        o.x = fmaf(s[r].x, qj, o.x);
+        o.y = fmaf(s[r].y, qj, o.y);
+        o.z = fmaf(s[r].z, qj, o.z);
+        o.w = fmaf(s[r].w, qj, o.w);
+    }
+    *reinterpret_cast<float4 *>(&red[rg][4 * cq]) = o;
+    __syncthreads();
+    for (int i = t; i < DV; i += THREADS) {
+        float acc = 0.f;
+#pragma unroll
+        for (int g2 = 0; g2 < RPP; ++g2) acc += red[g2][i];
+        store_any(p.o, (size_t)unit * DV + i, p.out_dtype, acc);
+    }
+}
+
+template <int D>
+int run_decode(const kai_gdn_decode_args *a, cudaStream_t st) {
+    const long long units = (long long)(a->batch * a->heads_v);
+    if (units > 0x7fffffffll) return set_error(KAI_GDN_ERR_UNSUPPORTED, "decode: too many heads");
+    switch (a->state_dtype) {
+        case KAI_GDN_F32: decode_step_kernel<D, KAI_GDN_F32><<<(unsigned)units, THREADS, 0, st>>>(*a); break;
+        case KAI_GDN_F16: decode_step_kernel<D, KAI_GDN_F16><<<(unsigned)units, THREADS, 0, st>>>(*a); break;
+        case KAI_GDN_BF16: decode_step_kernel<D, KAI_GDN_BF16><<<(unsigned)units, THREADS, 0, st>>>(*a); break;
+    }
+    return check_launch("delta_rule_decode");
+}
+
+}  // namespace
+
+int launch_decode(const kai_gdn_decode_args *a, cudaStream_t st) {
+    if (!a) return set_error(KAI_GDN_ERR_INVALID, "decode: null args");
+    if (a->batch == 0 || a->heads_v == 0) return KAI_GDN_OK;
+    if (!a->state || !a->q || !a->k || !a->v || !a->g || !a->beta || !a->o)
+        return set_error(KAI_GDN_ERR_INVALID, "decode: null pointer");
+    if (a->heads_k == 0 || a->heads_v % a->heads_k)
+        return set_error(KAI_GDN_ERR_INVALID, "decode: heads_v %zu not a multiple of heads_k %zu",
+                         a->heads_v, a->heads_k);
+    if (!valid_dtype(a->in_dtype) || !valid_dtype(a->state_dtype) || !valid_dtype(a->out_dtype))
+        return set_error(KAI_GDN_ERR_INVALID, "decode: bad dtype");
+    size_t es = dtype_size(a->state_dtype);
+    if ((uintptr_t)a->state % (4 * es))
+        return set_error(KAI_GDN_ERR_INVALID, "decode: state must be %zu-byte aligned", 4 * es);
+    if (a->dk != a->dv)
+        return set_error(KAI_GDN_ERR_UNSUPPORTED, "decode: dk %zu != dv %zu", a->dk, a->dv);
+    switch (a->dk) {
+        case 32: return run_decode<32>(a, st);
+        case 64: return run_decode<64>(a, st);
+        case 128: return run_decode<128>(a, st);
+    }
+    return set_error(KAI_GDN_ERR_UNSUPPORTED, "decode: head dim %zu (supported: 32, 64, 128)", a->dk);
+}
+
+}  // namespace gdn

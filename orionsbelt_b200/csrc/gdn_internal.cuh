@@ -1,0 +1,74 @@
+// gdn_internal.cuh -- shared declarations of libkai_gdn_cuda.so (sm_100a).
+#pragma once
+
+#include <cuda_runtime.h>
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <stddef.h>
+#include <stdint.h>
+
+#include "../../include/kai_gdn_cuda.h"
+
+namespace gdn {
+
+// ------------------------------------------------------------- errors
+// Thread-local status + message (runtime.cu).  set_error returns `status`
+// so call sites can `return set_error(...)`.
+int set_error(int status, const char *fmt, ...);
+int check_cuda(cudaError_t err, const char *what);
+// Check the launch that was just issued.
+int check_launch(const char *kernel);
+
+// Number of SMs of the current device (cached per device).
+int sm_count();
+
+// Scratch memory owned by the library for kernels that need it (the segment
+// aggregates of the scan kernels).  One buffer per (device, stream), grown on
+// demand with cudaMalloc (which synchronises the device), never shrunk.  The
+// returned pointer is valid until the next call for the same stream.
+int scratch_for_stream(cudaStream_t stream, size_t bytes, void **out);
+
+// Launchers shared between the drop-in and the device entry points.  All take
+// device pointers and return a KAI_GDN_* status.
+int launch_cumdecay(const float *a, void *decay, int decay_dtype, size_t batch,
+                    size_t seq, size_t ch, cudaStream_t st);
+int launch_cumsum(const float *g, float *gcum, size_t batch, size_t seq, size_t ch,
+                  cudaStream_t st);
+int launch_gated_scan(const float *g, const float *x, float *s, void *state,
+                      int state_dtype, size_t batch, size_t seq, size_t ch,
+                      cudaStream_t st);
+int launch_gdn2_scan(const float *g, const float *bg, const float *wg, const float *x,
+                     float *s, float *state, size_t batch, size_t seq, size_t ch,
+                     cudaStream_t st);
+int launch_conv(const void *in, const float *w, void *out, void *hist, int io_dtype,
+                size_t batch, size_t seq, size_t ch, cudaStream_t st);
+int launch_matmul(const float *A, const float *B, float *C, size_t M, size_t K,
+                  size_t N, cudaStream_t st);
+int launch_decode(const kai_gdn_decode_args *a, cudaStream_t st);
+int launch_chunk(const kai_gdn_chunk_args *a, cudaStream_t st);
+
+// --------------------------------------------------- storage conversions
+// Loads widen to fp32 exactly; stores round to nearest even.
+template <int DT> struct Store;
+template <> struct Store<KAI_GDN_F32> {
+    using T = float;
+    static __device__ __forceinline__ float load(const T *p) { return *p; }
+    static __device__ __forceinline__ void store(T *p, float v) { *p = v; }
+};
+template <> struct Store<KAI_GDN_BF16> {
+    using T = __nv_bfloat16;
+    static __device__ __forceinline__ float load(const T *p) { return __bfloat162float(*p); }
+    static __device__ __forceinline__ void store(T *p, float v) { *p = __float2bfloat16_rn(v); }
+};
+template <> struct Store<KAI_GDN_F16> {
+    using T = __half;
+    static __device__ __forceinline__ float load(const T *p) { return __half2float(*p); }
+    static __device__ __forceinline__ void store(T *p, float v) { *p = __float2half_rn(v); }
+};
+
+static inline bool valid_dtype(int dt) {
+    return dt == KAI_GDN_F32 || dt == KAI_GDN_BF16 || dt == KAI_GDN_F16;
+}
+static inline size_t dtype_size(int dt) { return dt == KAI_GDN_F32 ? 4 : 2; }
+
+}  // namespace gdn

@@ -1,0 +1,198 @@
+"""Python mirror of the kai GDN operator interface over libkai_gdn_cuda.so.
+
+Two layers, both calling the C ABI (include/kai_gdn_cuda.h) through ctypes:
+
+* The drop-in names take numpy arrays (host memory) exactly like the reference
+  C functions take host pointers: ``kai_run_gdn_cumdecay_f32_sve(a, decay)``
+  fills ``decay`` in place, ``state`` / ``hist`` are updated in place, and the
+  call returns when the result is there (kleidiai_submission/kai/ukernels/gdn/
+  *.h, src/orionsbelt/engines/cpu/kernels/gdn_sve.h, gdn_delta_matmul.h).
+* The device layer takes CUDA tensors (torch is used only to own device memory
+  and streams) and launches on the current torch stream: ``cumdecay``,
+  ``cumsum``, ``gated_scan``, ``gdn2_gated_scan``, ``causal_dwconv1d``,
+  ``matmul``, ``delta_rule_decode`` and ``chunk_delta_rule``.
+
+There is no CPU fallback anywhere: a missing library raises at import of the
+first call, and every failed call raises GdnError with the library's message.
+"""
+from __future__ import annotations
+
+import numpy as np
+
+from . import _lib
+from ._lib import BF16, F16, F32, check, check_dropin, lib
+
+# ----------------------------------------------------------------- drop-in
+
+
+def _host(a: np.ndarray, dtype=np.float32) -> int:
+    if not isinstance(a, np.ndarray) or a.dtype != dtype or not a.flags["C_CONTIGUOUS"]:
+        raise TypeError(f"expected a C-contiguous numpy {np.dtype(dtype).name} array")
+    return a.ctypes.data
+
+
+def kai_run_gdn_cumdecay_f32_sve(a: np.ndarray, decay: np.ndarray) -> None:
+    seq, ch = a.shape
+    lib().kai_run_gdn_cumdecay_f32_sve(_host(a), _host(decay), seq, ch)
+    check_dropin()
+
+
+def kai_run_gdn_gated_scan_f32_sve(g, x, s, state) -> None:
+    seq, ch = x.shape
+    lib().kai_run_gdn_gated_scan_f32_sve(_host(g), _host(x), _host(s), _host(state), seq, ch)
+    check_dropin()
+
+
+def kai_run_gdn_causal_dwconv1d_f32_k4_sve(x, w, out, hist) -> None:
+    seq, ch = x.shape
+    lib().kai_run_gdn_causal_dwconv1d_f32_k4_sve(_host(x), _host(w), _host(out), _host(hist), seq, ch)
+    check_dropin()
+
+
+def kai_run_gdn_gemv_f32_f32_f32_1x4_neon(a, b, c) -> None:
+    k, n = b.shape
+    lib().kai_run_gdn_gemv_f32_f32_f32_1x4_neon(_host(a), _host(b), _host(c), k, n)
+    check_dropin()
+
+
+def gdn_delta_rule_matmul(A, B, Cm) -> None:
+    M, K = A.shape
+    N = B.shape[1]
+    lib().gdn_delta_rule_matmul(_host(A), _host(B), _host(Cm), M, K, N)
+    check_dropin()
+
+
+def gdn_cumdecay_narrow(a, decay_u16, kind: str) -> None:
+    seq, ch = a.shape
+    getattr(lib(), "gdn_cumdecay_" + kind)(_host(a), _host(decay_u16, np.uint16), seq, ch)
+    check_dropin()
+
+
+def gdn_gated_scan_narrow(g, x, s, state_u16, kind: str) -> None:
+    seq, ch = x.shape
+    getattr(lib(), "gdn_gated_scan_" + kind)(_host(g), _host(x), _host(s), _host(state_u16, np.uint16), seq, ch)
+    check_dropin()
+
+
+def gdn2_gated_scan_f32(g, b_gate, w_gate, x, s, state) -> None:
+    seq, ch = x.shape
+    lib().gdn2_gated_scan_f32(_host(g), _host(b_gate), _host(w_gate), _host(x), _host(s), _host(state), seq, ch)
+    check_dropin()
+
+
+# ------------------------------------------------------------ device layer
+
+def _torch():
+    import torch
+    return torch
+
+
+def _dt(t) -> int:
+    torch = _torch()
+    return {torch.float32: F32, torch.bfloat16: BF16, torch.float16: F16}[t.dtype]
+
+
+def _dev(t, *, dtype=None) -> int:
+    torch = _torch()
+    if not isinstance(t, torch.Tensor) or not t.is_cuda:
+        raise TypeError("expected a CUDA tensor")
+    if not t.is_contiguous():
+        raise ValueError("expected a contiguous tensor")
+    if dtype is not None and t.dtype != dtype:
+        raise TypeError(f"expected {dtype}, got {t.dtype}")
+    return t.data_ptr()
+
+
+def _stream(stream=None) -> int:
+    torch = _torch()
+    s = stream if stream is not None else torch.cuda.current_stream()
+    return s.cuda_stream
+
+
+def cumdecay(a, decay, stream=None) -> None:
+    """a [batch][seq][ch] fp32 -> decay (fp32 / fp16 / bf16) prefix product."""
+    torch = _torch()
+    b, s, c = a.shape if a.dim() == 3 else (1, *a.shape)
+    check(lib().kai_run_gdn_cumdecay_sm100a(_dev(a, dtype=torch.float32), _dev(decay), _dt(decay), b, s, c,
+                                            _stream(stream)))
+
+
+def cumsum(g, gcum, stream=None) -> None:
+    torch = _torch()
+    b, s, c = g.shape if g.dim() == 3 else (1, *g.shape)
+    check(lib().kai_run_gdn_cumsum_f32_sm100a(_dev(g, dtype=torch.float32), _dev(gcum, dtype=torch.float32),
+                                              b, s, c, _stream(stream)))
+
+
+def gated_scan(g, x, s, state, stream=None) -> None:
+    torch = _torch()
+    b, t, c = x.shape if x.dim() == 3 else (1, *x.shape)
+    f = torch.float32
+    check(lib().kai_run_gdn_gated_scan_sm100a(_dev(g, dtype=f), _dev(x, dtype=f), _dev(s, dtype=f), _dev(state),
+                                              _dt(state), b, t, c, _stream(stream)))
+
+
+def gdn2_gated_scan(g, b_gate, w_gate, x, s, state, stream=None) -> None:
+    torch = _torch()
+    b, t, c = x.shape if x.dim() == 3 else (1, *x.shape)
+    f = torch.float32
+    check(lib().kai_run_gdn2_gated_scan_f32_sm100a(_dev(g, dtype=f), _dev(b_gate, dtype=f), _dev(w_gate, dtype=f),
+                                                   _dev(x, dtype=f), _dev(s, dtype=f), _dev(state, dtype=f),
+                                                   b, t, c, _stream(stream)))
+
+
+def causal_dwconv1d(x, w, out, hist, stream=None) -> None:
+    """x, out [batch][seq][ch], hist [batch][3][ch] (same dtype), w [4][ch] fp32."""
+    torch = _torch()
+    b, t, c = x.shape if x.dim() == 3 else (1, *x.shape)
+    if out.dtype != x.dtype or hist.dtype != x.dtype:
+        raise TypeError("x, out and hist must share a dtype")
+    check(lib().kai_run_gdn_causal_dwconv1d_k4_sm100a(_dev(x), _dev(w, dtype=torch.float32), _dev(out), _dev(hist),
+                                                      _dt(x), b, t, c, _stream(stream)))
+
+
+def matmul(A, B, Cm, stream=None) -> None:
+    torch = _torch()
+    f = torch.float32
+    M, K = A.shape
+    N = B.shape[1]
+    check(lib().kai_run_gdn_matmul_f32_sm100a(_dev(A, dtype=f), _dev(B, dtype=f), _dev(Cm, dtype=f), M, K, N,
+                                              _stream(stream)))
+
+
+def decode_args(state, q, k, v, g, beta, o, scale: float) -> _lib.DecodeArgs:
+    """Pack struct kai_gdn_decode_args from tensors:
+    state [B][Hv][dk][dv], q,k [B][Hk][dk], v [B][Hv][dv], g,beta [B][Hv], o [B][Hv][dv]."""
+    torch = _torch()
+    B, Hv, dk, dv = state.shape
+    Hk = q.shape[1]
+    if q.dtype != k.dtype or v.dtype != q.dtype:
+        raise TypeError("q, k, v must share a dtype")
+    return _lib.DecodeArgs(_dev(state), _dev(q), _dev(k), _dev(v), _dev(g, dtype=torch.float32),
+                           _dev(beta, dtype=torch.float32), _dev(o), B, Hk, Hv, dk, dv, float(scale),
+                           _dt(q), _dt(state), _dt(o))
+
+
+def delta_rule_decode(state, q, k, v, g, beta, o, scale: float = 1.0, stream=None) -> None:
+    """One token of the matrix-state gated delta rule for every (batch, value head)."""
+    args = decode_args(state, q, k, v, g, beta, o, scale)
+    check(lib().kai_run_gdn_delta_rule_decode_sm100a(args, _stream(stream)))
+
+
+def chunk_args(q, k, v, g, beta, state, o, scale: float, chunk: int = 64) -> _lib.ChunkArgs:
+    """Pack struct kai_gdn_chunk_args: q,k [B][T][Hk][dk], v [B][T][Hv][dv],
+    g,beta [B][T][Hv], state [B][Hv][dk][dv], o [B][T][Hv][dv]."""
+    torch = _torch()
+    B, T, Hk, dk = q.shape
+    Hv, dv = v.shape[2], v.shape[3]
+    if q.dtype != k.dtype or v.dtype != q.dtype:
+        raise TypeError("q, k, v must share a dtype")
+    return _lib.ChunkArgs(_dev(q), _dev(k), _dev(v), _dev(g, dtype=torch.float32), _dev(beta, dtype=torch.float32),
+                          _dev(state), _dev(o), B, T, Hk, Hv, dk, dv, chunk, float(scale),
+                          _dt(q), _dt(state), _dt(o))
+
+
+def chunk_delta_rule(q, k, v, g, beta, state, o, scale: float = 1.0, chunk: int = 64, stream=None) -> None:
+    """Chunkwise WY gated delta-rule scan over the whole sequence (state in/out)."""
+    args = chunk_args(q, k, v, g, beta, state, o, scale, chunk)
+    check(lib().kai_run_gdn_chunk_delta_rule_sm100a(args, _stream(stream)))

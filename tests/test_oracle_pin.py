@@ -1,0 +1,145 @@
+"""Pin the CPU oracle (oracle/gdn_oracle.c) before trusting it (CPU only).
+
+* Against the reference's own C kernels, compiled from the reference sources
+  into oracle/_ref/libgdnref.so: bit-identical on every kernel the reference
+  has C code for.
+* Against the committed golden fixtures: the reference's NumPy recurrence
+  (bench/gdn2_reference.py), its GDN-2 path with uniform gates, HF's chunkwise
+  form, and the reference C on the kai test's LCG inputs.
+* The chunked-WY restatement against the token loop, and the hand-checkable
+  known answer.
+"""
+from __future__ import annotations
+
+import numpy as np
+import pytest
+
+from conftest import rel_l2
+
+import oracle
+
+
+def _need_ref(ref):
+    if ref is None:
+        pytest.skip("oracle/_ref/libgdnref.so not built (no reference tree at build time)")
+
+
+SHAPES = [(1, 1), (4, 3), (16, 7), (64, 17), (64, 33), (130, 128), (257, 2051)]
+
+
+@pytest.mark.parametrize("seq,ch", SHAPES)
+def test_channel_kernels_bit_identical_to_reference(orc, ref, seq, ch):
+    _need_ref(ref)
+    r = np.random.default_rng(seq * 1000 + ch)
+    a = r.uniform(0.5, 1.5, (seq, ch)).astype(np.float32)
+    assert np.array_equal(orc.cumdecay(a), ref.cumdecay(a))
+    assert np.array_equal(orc.cumdecay(a), ref.kai_cumdecay(a))
+    for kind in ("f16", "bf16"):
+        assert np.array_equal(orc.cumdecay_narrow(a, kind), ref.cumdecay_narrow(a, kind))
+    g = r.uniform(-0.99, 0.99, (seq, ch)).astype(np.float32)
+    x = r.uniform(-2, 2, (seq, ch)).astype(np.float32)
+    st = r.uniform(-1, 1, ch).astype(np.float32)
+    s1, st1 = orc.gated_scan(g, x, st)
+    s2, st2 = ref.gated_scan(g, x, st)
+    assert np.array_equal(s1, s2) and np.array_equal(st1, st2)
+    for kind in ("f16", "bf16"):
+        stn = oracle.f32_to_u16(st, kind)
+        s1, st1 = orc.gated_scan_narrow(g, x, stn, kind)
+        s2, st2 = ref.gated_scan_narrow(g, x, stn, kind)
+        assert np.array_equal(s1, s2) and np.array_equal(st1, st2)
+    w = r.uniform(-1, 1, (4, ch)).astype(np.float32)
+    h = r.uniform(-1, 1, (3, ch)).astype(np.float32)
+    o1, h1 = orc.conv(x, w, h)
+    o2, h2 = ref.conv(x, w, h)
+    assert np.array_equal(o1, o2) and np.array_equal(h1, h2)
+    bg = r.uniform(0, 1, (seq, ch)).astype(np.float32)
+    wg = r.uniform(0, 1, (seq, ch)).astype(np.float32)
+    s1, st1 = orc.gdn2_scan(g, bg, wg, x, st)
+    s2, st2 = ref.gdn2_scan(g, bg, wg, x, st)
+    assert np.array_equal(s1, s2) and np.array_equal(st1, st2)
+
+
+@pytest.mark.parametrize("M,K,N", [(1, 128, 128), (64, 128, 128), (1, 128, 2048), (64, 128, 130), (5, 7, 3)])
+def test_matmul_bit_identical_to_reference(orc, ref, M, K, N):
+    _need_ref(ref)
+    r = np.random.default_rng(M * 7 + N)
+    A = r.uniform(-1, 1, (M, K)).astype(np.float32)
+    B = r.uniform(-1, 1, (K, N)).astype(np.float32)
+    assert np.array_equal(orc.matmul(A, B), ref.matmul(A, B))
+    if M == 1:
+        assert np.array_equal(orc.gemv(A[0], B), ref.gemv(A[0], B))
+
+
+def test_kai_lcg_golden(orc, golden):
+    """The reference C on the kai test's own LCG inputs (kai_lcg.npz)."""
+    d = golden("kai_lcg.npz")
+    assert np.array_equal(orc.cumdecay(d["a"]), d["decay"])
+    s, st = orc.gated_scan(d["g"], d["x"], d["s0"])
+    assert np.array_equal(s, d["s"]) and np.array_equal(st, d["s_state"])
+    o, h = orc.conv(d["cin"], d["w"], d["h0"])
+    assert np.array_equal(o, d["conv_out"]) and np.array_equal(h, d["conv_hist"])
+    assert np.array_equal(orc.gemv(d["ga"], d["gb"]), d["gemv"])
+
+
+def test_gdn1_recurrent_golden(orc, golden):
+    """bench/gdn2_reference.py::gdn1_recurrent (float64) on grouped heads."""
+    d = golden("gdn1_recurrent.npz")
+    S, o = orc.delta_rule_seq(d["S0"], d["q"], d["k"], d["v"], d["g"], d["beta"], scale=float(d["scale"]))
+    assert rel_l2(o[0], d["o"]) < 1e-5
+    assert rel_l2(S[0], d["S"]) < 1e-5
+
+
+def test_gdn2_uniform_golden(orc, golden):
+    """The reference's GDN-2 recurrence with uniform gates equals GDN-1 with beta."""
+    d = golden("gdn2_uniform.npz")
+    S, o = orc.delta_rule_seq(d["S0"], d["q"], d["k"], d["v"], d["g"], d["beta"], scale=1.0)
+    assert rel_l2(o[0], d["o"]) < 1e-5
+    assert rel_l2(S[0], d["S"]) < 1e-5
+
+
+def test_hf_chunk_golden(orc, golden):
+    """HF torch_chunk_gated_delta_rule (chunked WY, fp32) vs both oracle forms."""
+    d = golden("hf_chunk.npz")
+    sc = float(d["scale"])
+    S, o = orc.delta_rule_seq(d["S0"], d["q"], d["k"], d["v"], d["g"], d["beta"], scale=sc)
+    assert rel_l2(o, d["o"]) < 1e-5 and rel_l2(S, d["S"]) < 1e-5
+    S2, o2 = orc.chunk_wy(d["S0"], d["q"], d["k"], d["v"], d["g"], d["beta"], scale=sc)
+    assert rel_l2(o2, d["o"]) < 1e-5 and rel_l2(S2, d["S"]) < 1e-5
+
+
+@pytest.mark.parametrize("T", [1, 63, 64, 65, 130])
+def test_chunk_wy_equals_token_loop(orc, T):
+    from orionsbelt_b200 import synth
+    d = synth.host_gdn(1, T, 2, 4, 16, 16, g_scale=1.0, seed=T, state_std=0.2)
+    S1, o1 = orc.delta_rule_seq(d["S0"], d["q"], d["k"], d["v"], d["g"], d["beta"], scale=0.25)
+    S2, o2 = orc.chunk_wy(d["S0"], d["q"], d["k"], d["v"], d["g"], d["beta"], scale=0.25)
+    assert rel_l2(o2, o1) < 1e-5 and rel_l2(S2, S1) < 1e-5
+
+
+def test_known_answer(orc):
+    """T=1, dk=dv=2, S0=0, beta=1: S = k v^T, o = S^T q (hand-computed, in the
+    spirit of bench/gdn2_reference.py:251-290)."""
+    k = np.array([0.8, 0.6], np.float32)
+    v = np.array([1.0, 2.0], np.float32)
+    q = np.array([0.6, 0.8], np.float32)
+    S, o = orc.delta_rule_step(np.zeros((2, 2), np.float32), k, v, q, 1.0, 0.5)
+    assert np.allclose(S, [[0.8, 1.6], [0.6, 1.2]], atol=1e-7)
+    assert np.allclose(o, [0.96, 1.92], atol=1e-6)
+    # beta = 0: no write, only decay (tests/test_gdn2_reference.py:212 analogue)
+    S0 = np.array([[1.0, 2.0], [3.0, 4.0]], np.float32)
+    S, o = orc.delta_rule_step(S0, k, v, q, 0.0, 0.5)
+    assert np.array_equal(S, S0 * np.float32(0.5))
+
+
+def test_integer_inputs_exact(orc):
+    """Conv and cumsum are exact on integer-valued inputs."""
+    r = np.random.default_rng(5)
+    x = r.integers(-3, 4, (100, 9)).astype(np.float32)
+    w = r.integers(-3, 4, (4, 9)).astype(np.float32)
+    h = r.integers(-3, 4, (3, 9)).astype(np.float32)
+    o, _ = orc.conv(x, w, h)
+    full = np.concatenate([h, x]).astype(np.int64)
+    want = sum(w[j].astype(np.int64) * full[j:j + 100] for j in range(4))
+    assert np.array_equal(o.astype(np.int64), want)
+    g = r.integers(-3, 1, (100, 9)).astype(np.float32)
+    assert np.array_equal(orc.cumsum(g).astype(np.int64), np.cumsum(g.astype(np.int64), axis=0))
