@@ -60,7 +60,8 @@ def test_cumsum(cuda, orc, seq, ch):
     if seq <= 128:
         assert np.array_equal(got, want)
     else:
-        assert rel_l2(got, want) < 1e-6
+        # float sums of up to 32768 terms in two association orders
+        assert rel_l2(got, want) < 1e-5
 
 
 def test_cumsum_integer_exact_batched(cuda):
