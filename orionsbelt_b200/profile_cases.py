@@ -1,0 +1,69 @@
+"""Small, self-terminating workloads for ncu captures of one kernel at a time.
+
+    python -m orionsbelt_b200.profile_cases decode [--launches 3]
+    python -m orionsbelt_b200.profile_cases chunk  [--launches 1]
+    python -m orionsbelt_b200.profile_cases conv | cumsum | scan
+
+Each case holds a few hundred MB to a few GB on the device (inputs larger
+than the 126 MB L2, so DRAM counters mean something), runs a few launches of
+its kernel through the C ABI, and exits.  Cases:
+  decode  one config-1 layer: B=64, 32 value / 16 key heads, 128x128 fp32
+          state (268 MB), bf16 q/k/v/o
+  chunk   config-2 numerics on a reduced shard: B=1, T=8192, bf16 in / fp32 state
+  conv    config-0 Conv1D: T=2048, 8192 channels, fp32 (134 MB)
+  cumsum  config-2 decay cumsum: 8 x 32768 x 32 log-decays, fp32
+  scan    gated scan, 4096 tokens x 8192 channels, fp32
+"""
+from __future__ import annotations
+
+import argparse
+
+import torch
+
+from . import _lib, ops, synth
+
+
+def main() -> None:
+    ap = argparse.ArgumentParser()
+    ap.add_argument("case", choices=["decode", "chunk", "conv", "cumsum", "scan"])
+    ap.add_argument("--launches", type=int, default=3)
+    a = ap.parse_args()
+    torch.cuda.set_device(0)
+    _lib.lib()
+    if a.case == "decode":
+        d = synth.device_gdn(64, 1, 16, 32, 128, 128, seed=1, in_dtype=torch.bfloat16, state_std=0.02)
+        o = torch.empty((64, 32, 128), dtype=torch.bfloat16, device="cuda")
+        args = ops.decode_args(d["S0"], d["q"][:, 0].contiguous(), d["k"][:, 0].contiguous(),
+                               d["v"][:, 0].contiguous(), d["g"][:, 0].contiguous(), d["beta"][:, 0].contiguous(),
+                               o, scale=1.0)
+        fn = lambda: _lib.check(_lib.lib().kai_run_gdn_delta_rule_decode_sm100a(  # noqa: E731
+            args, torch.cuda.current_stream().cuda_stream))
+    elif a.case == "chunk":
+        d = synth.device_gdn(1, 8192, 16, 32, 128, 128, seed=2, in_dtype=torch.bfloat16)
+        o = torch.empty_like(d["v"])
+        fn = lambda: ops.chunk_delta_rule(d["q"], d["k"], d["v"], d["g"], d["beta"], d["S0"], o)  # noqa: E731
+    elif a.case == "conv":
+        x = synth.device_normal((2048, 8192), 3, 1)
+        w = synth.device_normal((4, 8192), 3, 2, std=0.5)
+        out = torch.empty_like(x)
+        hist = torch.zeros((3, 8192), device="cuda")
+        fn = lambda: ops.causal_dwconv1d(x, w, out, hist)  # noqa: E731
+    elif a.case == "cumsum":
+        g = -torch.nn.functional.softplus(synth.device_normal((8, 32768, 32), 4, 1)) * 0.1
+        out = torch.empty_like(g)
+        fn = lambda: ops.cumsum(g, out)  # noqa: E731
+    else:
+        g = torch.sigmoid(synth.device_normal((4096, 8192), 5, 1))
+        x = synth.device_normal((4096, 8192), 5, 2)
+        s = torch.empty_like(x)
+        st = torch.zeros(8192, device="cuda")
+        fn = lambda: ops.gated_scan(g, x, s, st)  # noqa: E731
+    torch.cuda.synchronize()
+    for _ in range(a.launches):
+        fn()
+    torch.cuda.synchronize()
+    print(f"{a.case}: {a.launches} launches ok")
+
+
+if __name__ == "__main__":
+    main()
