@@ -129,6 +129,25 @@ KAI_GDN_API int kai_run_gdn_gated_scan_sm100a(const float *g, const float *x, fl
                                   void *state, int state_dtype, size_t batch,
                                   size_t seq, size_t channels, void *stream);
 
+/* The gated scan above with no allocation at call time.  This entry point
+ * has no counterpart in the reference.  It is for callers that cannot
+ * allocate device memory when they call (an engine that gives all of HBM to
+ * its own pools at start-up, or a host whose other streams cannot wait for
+ * the device-wide synchronisation cudaMalloc / cudaFree may cause).  A long
+ * scan's segment carries use a fixed array inside the library image instead
+ * of library-allocated scratch: every GPU that loads the library holds
+ * KAI_GDN_NOALLOC_SCRATCH_BYTES of device memory until the process exits.
+ * Limit: 2 * batch * ceil(seq / 128) * channels * 4 bytes <= that size
+ * (scans with seq <= 128 need none); larger calls return
+ * KAI_GDN_ERR_INVALID with a message.  The first call on a device looks up
+ * the array's address (cudaGetSymbolAddress) and should come before any
+ * stream capture.  All calls share the array: calls that overlap on the GPU
+ * (several streams or host threads) race and must be serialised. */
+#define KAI_GDN_NOALLOC_SCRATCH_BYTES (4u << 20)
+KAI_GDN_API int kai_run_gdn_gated_scan_noalloc_sm100a(const float *g, const float *x, float *s,
+                                                      void *state, int state_dtype, size_t batch,
+                                                      size_t seq, size_t channels, void *stream);
+
 /* GDN-2 gated scan (gdn_sve.h:79), fp32 state. */
 KAI_GDN_API int kai_run_gdn2_gated_scan_f32_sm100a(const float *g, const float *b_gate,
                                        const float *w_gate, const float *x, float *s,

@@ -54,6 +54,7 @@ SIGNATURES = {
     "kai_run_gdn_cumdecay_sm100a": (_i, [_vp, _vp, _i, _sz, _sz, _sz, _vp]),
     "kai_run_gdn_cumsum_f32_sm100a": (_i, [_vp, _vp, _sz, _sz, _sz, _vp]),
     "kai_run_gdn_gated_scan_sm100a": (_i, [_vp, _vp, _vp, _vp, _i, _sz, _sz, _sz, _vp]),
+    "kai_run_gdn_gated_scan_noalloc_sm100a": (_i, [_vp, _vp, _vp, _vp, _i, _sz, _sz, _sz, _vp]),
     "kai_run_gdn2_gated_scan_f32_sm100a": (_i, [_vp, _vp, _vp, _vp, _vp, _vp, _sz, _sz, _sz, _vp]),
     "kai_run_gdn_causal_dwconv1d_k4_sm100a": (_i, [_vp, _vp, _vp, _vp, _i, _sz, _sz, _sz, _vp]),
     "kai_run_gdn_matmul_f32_sm100a": (_i, [_vp, _vp, _vp, _sz, _sz, _sz, _vp]),

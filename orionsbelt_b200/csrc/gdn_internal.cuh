@@ -37,6 +37,9 @@ int launch_cumsum(const float *g, float *gcum, size_t batch, size_t seq, size_t 
 int launch_gated_scan(const float *g, const float *x, float *s, void *state,
                       int state_dtype, size_t batch, size_t seq, size_t ch,
                       cudaStream_t st);
+int launch_gated_scan_noalloc(const float *g, const float *x, float *s, void *state,
+                              int state_dtype, size_t batch, size_t seq, size_t ch,
+                              cudaStream_t st);
 int launch_gdn2_scan(const float *g, const float *bg, const float *wg, const float *x,
                      float *s, float *state, size_t batch, size_t seq, size_t ch,
                      cudaStream_t st);

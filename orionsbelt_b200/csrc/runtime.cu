@@ -320,6 +320,12 @@ int kai_run_gdn_gated_scan_sm100a(const float *g, const float *x, float *s, void
     return launch_gated_scan(g, x, s, state, state_dtype, batch, seq, channels, (cudaStream_t)stream);
 }
 
+int kai_run_gdn_gated_scan_noalloc_sm100a(const float *g, const float *x, float *s, void *state,
+                                          int state_dtype, size_t batch, size_t seq, size_t channels,
+                                          void *stream) {
+    return launch_gated_scan_noalloc(g, x, s, state, state_dtype, batch, seq, channels, (cudaStream_t)stream);
+}
+
 int kai_run_gdn2_gated_scan_f32_sm100a(const float *g, const float *b_gate, const float *w_gate, const float *x,
                                        float *s, float *state, size_t batch, size_t seq, size_t channels,
                                        void *stream) {

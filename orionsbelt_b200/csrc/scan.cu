@@ -18,6 +18,8 @@
 // each segment's carry-in, in order; (3) every segment re-walks its rows from
 // its carry.  Pass 3's re-read of the input is served from L2 for inputs that
 // fit in it (126 MB).
+#include <mutex>
+
 #include "gdn_internal.cuh"
 
 namespace gdn {
@@ -291,6 +293,110 @@ int launch_gdn2_scan(const float *g, const float *bg, const float *wg, const flo
     p.seq = (long long)seq;
     p.ch = (long long)ch;
     return run_scan<GDN2, KAI_GDN_F32, KAI_GDN_F32>(p, batch, st, "gdn2_gated_scan");
+}
+
+// ---------------------------------------------------------------------------
+// Allocation-free gated scan.
+//
+// Some callers cannot allocate device memory when they call us: a serving
+// engine that hands all of HBM to its own state / KV pool at start-up and
+// budgets nothing for a library, or a host that keeps other streams busy and
+// cannot afford cudaMalloc / cudaFree, which may synchronise the whole
+// device.  kai_run_gdn_gated_scan_noalloc_sm100a serves them: the segment
+// carries of a long scan live in the fixed array below instead of the
+// library's cudaMalloc'd per-stream scratch.
+//
+// The array is part of the library's device image, so every GPU that loads
+// the library holds KAI_GDN_NOALLOC_SCRATCH_BYTES of it until the process
+// exits.  Host code cannot use the name `g_noalloc_scratch` as a device
+// address (on the host it is only a stand-in), so the address is looked up
+// once per device with cudaGetSymbolAddress, with that device current, on the
+// first call there; that first call should come before any stream capture.
+// Every call shares the array and overwrites what it uses (each element a
+// call reads was written earlier in the same call, so nothing needs zeroing);
+// calls that overlap on the GPU -- two streams, or two host threads -- race
+// on it and must be serialised by the caller.
+// ---------------------------------------------------------------------------
+namespace {
+
+constexpr size_t kNoallocFloats = KAI_GDN_NOALLOC_SCRATCH_BYTES / sizeof(float);
+static __device__ __align__(256) float g_noalloc_scratch[kNoallocFloats];
+
+std::mutex g_noalloc_mu;
+float *g_noalloc_ptr[64] = {nullptr};
+
+int noalloc_scratch(float **out) {
+    int dev = 0;
+    int rc = check_cuda(cudaGetDevice(&dev), "gated_scan_noalloc: cudaGetDevice");
+    if (rc) return rc;
+    if (dev < 0 || dev >= 64) return set_error(KAI_GDN_ERR_UNSUPPORTED, "gated_scan_noalloc: device %d", dev);
+    std::lock_guard<std::mutex> lock(g_noalloc_mu);
+    if (!g_noalloc_ptr[dev]) {
+        void *p = nullptr;
+        rc = check_cuda(cudaGetSymbolAddress(&p, g_noalloc_scratch), "gated_scan_noalloc: cudaGetSymbolAddress");
+        if (rc) return rc;
+        g_noalloc_ptr[dev] = static_cast<float *>(p);
+    }
+    *out = g_noalloc_ptr[dev];
+    return KAI_GDN_OK;
+}
+
+template <int SDT>
+int run_scan_noalloc(ScanParams p, size_t batch, cudaStream_t st) {
+    const char *name = "gated_scan_noalloc";
+    if (batch > 65535) return set_error(KAI_GDN_ERR_UNSUPPORTED, "%s: batch %zu > 65535", name, batch);
+    long long nseg = (p.seq + SEG_LEN - 1) / SEG_LEN;
+    if (nseg > (1ll << 24)) return set_error(KAI_GDN_ERR_UNSUPPORTED, "%s: seq too long", name);
+    p.nseg = (int)nseg;
+    int sw = nseg >= 8 ? 8 : nseg >= 4 ? 4 : nseg >= 2 ? 2 : 1;
+    p.cw = 8 / sw;
+    dim3 block(32, 8);
+    long long gx = (p.ch + 32 * p.cw - 1) / (32 * p.cw);
+    long long gy = (nseg + sw - 1) / sw;
+    if (gx > 0x7fffffffll || gy > 65535)
+        return set_error(KAI_GDN_ERR_UNSUPPORTED, "%s: shape too large for the grid", name);
+    dim3 grid((unsigned)gx, (unsigned)gy, (unsigned)batch);
+    int rc;
+    if (nseg > 1) {
+        size_t n = batch * (size_t)nseg * (size_t)p.ch;
+        if (n > kNoallocFloats / 2)
+            return set_error(KAI_GDN_ERR_INVALID,
+                             "%s: batch*ceil(seq/%d)*channels = %zu needs %zu bytes of scratch; the static "
+                             "maximum is %zu bytes (use kai_run_gdn_gated_scan_sm100a for larger calls)",
+                             name, SEG_LEN, n, 2 * n * sizeof(float), (size_t)KAI_GDN_NOALLOC_SCRATCH_BYTES);
+        float *scr = nullptr;
+        if ((rc = noalloc_scratch(&scr))) return rc;
+        p.aggA = scr;
+        p.aggB = scr + n;
+        scan_aggregate_kernel<AFFINE><<<grid, block, 0, st>>>(p);
+        if ((rc = check_launch(name))) return rc;
+        dim3 cgrid((unsigned)((p.ch + 127) / 128), (unsigned)batch);
+        scan_carry_kernel<AFFINE, SDT><<<cgrid, 128, 0, st>>>(p);
+        if ((rc = check_launch(name))) return rc;
+    }
+    scan_final_kernel<AFFINE, KAI_GDN_F32, SDT><<<grid, block, 0, st>>>(p);
+    return check_launch(name);
+}
+
+}  // namespace
+
+int launch_gated_scan_noalloc(const float *g, const float *x, float *s, void *state, int sdt, size_t batch,
+                              size_t seq, size_t ch, cudaStream_t st) {
+    if (batch == 0 || seq == 0 || ch == 0) return KAI_GDN_OK;
+    if (!g || !x || !s || !state) return set_error(KAI_GDN_ERR_INVALID, "gated_scan_noalloc: null pointer");
+    ScanParams p{};
+    p.x = x;
+    p.g = g;
+    p.out = s;
+    p.state = state;
+    p.seq = (long long)seq;
+    p.ch = (long long)ch;
+    switch (sdt) {
+        case KAI_GDN_F32: return run_scan_noalloc<KAI_GDN_F32>(p, batch, st);
+        case KAI_GDN_F16: return run_scan_noalloc<KAI_GDN_F16>(p, batch, st);
+        case KAI_GDN_BF16: return run_scan_noalloc<KAI_GDN_BF16>(p, batch, st);
+    }
+    return set_error(KAI_GDN_ERR_INVALID, "gated_scan_noalloc: bad state dtype %d", sdt);
 }
 
 }  // namespace gdn
