@@ -21,6 +21,8 @@ ROOT = PKG.parent
 CSRC = PKG / "csrc"
 BUILD = PKG / "_build"
 LIB = PKG / "libkai_gdn_cuda.so"
+SELFTEST_SRC = ROOT / "tests" / "c" / "umma_selftest.cu"
+SELFTEST_LIB = ROOT / "tests" / "c" / "bin" / "libumma_selftest.so"
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 NVCC_FLAGS = ARCH + [
     "-O3", "-lineinfo", "-std=c++17", "-Xcompiler", "-fPIC", "-Xcompiler", "-fvisibility=hidden",
@@ -74,6 +76,22 @@ def build(verbose: bool = False, force: bool = False) -> Path:
     return LIB
 
 
+def build_selftest(verbose: bool = False) -> Path:
+    """Test-only library checking the tcgen05 building blocks (tests/c/umma_selftest.cu)."""
+    SELFTEST_LIB.parent.mkdir(parents=True, exist_ok=True)
+    deps = [SELFTEST_SRC, CSRC / "umma.cuh"]
+    if SELFTEST_LIB.exists() and SELFTEST_LIB.stat().st_mtime >= max(d.stat().st_mtime for d in deps):
+        return SELFTEST_LIB
+    cmd = [nvcc(), *NVCC_FLAGS, "-shared", "-cudart", "static", str(SELFTEST_SRC), "-o", str(SELFTEST_LIB)]
+    if verbose:
+        print(" ".join(cmd), flush=True)
+    r = subprocess.run(cmd, capture_output=True, text=True)
+    if r.returncode != 0:
+        raise RuntimeError(f"nvcc failed on {SELFTEST_SRC.name}:\n{r.stdout}\n{r.stderr}")
+    return SELFTEST_LIB
+
+
 if __name__ == "__main__":
     build(verbose="-v" in sys.argv, force="--force" in sys.argv)
+    build_selftest(verbose="-v" in sys.argv)
     print(LIB)

@@ -1,0 +1,175 @@
+// umma.cuh -- sm_100a tensor-core (tcgen05) building blocks used by the
+// chunked delta-rule kernel: shared-memory operand layouts and descriptors,
+// instruction descriptors, TMEM allocation, MMA issue/commit, TMEM <-> register
+// moves, and bounded mbarrier waits.
+//
+// Operand layouts (no swizzle).  An MMA operand tile is stored as 8 x 16-byte
+// "core matrices" (128 contiguous bytes each):
+//   K-major  (rows = M or N, K contiguous): element (r, k) of a tile with KK
+//            columns of K sits at  (r/8)*SBO + (k/8)*128 + (r%8)*16 + (k%8)*2
+//            [16-bit types; for 32-bit types replace 8 by 4 along k and *2 by *4]
+//            LBO = 128 (next 8 k's), SBO = (KK/8)*128 (next 8 rows).
+//   MN-major (M or N contiguous): element (k, c) of a tile with CC columns of
+//            M/N sits at  (k/8)*LBO + (c/8)*128 + (k%8)*16 + (c%8)*2
+//            SBO = 128 (next 8 columns), LBO = (CC/8)*128 (next 8 k's).
+// One kind::f16 MMA consumes K = 16 (two 8-k groups); the next K step starts
+// 2 groups further on: +256 bytes (K-major) or +2*LBO (MN-major).
+//
+// Accumulators (fp32, cta_group::1): M = 128 puts row i in TMEM lane i;
+// M = 64 puts rows 16q..16q+15 in lanes 32q..32q+15 (q = 0..3).  A warp
+// w reads lanes 32*(w%4) .. 32*(w%4)+31 with tcgen05.ld.32x32b.
+//
+// Waits are bounded: a wait that runs out sets *err (when given) and returns
+// false, so a kernel can stop cleanly instead of hanging the GPU.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace gdn {
+namespace umma {
+
+__device__ __forceinline__ uint32_t smem_addr(const void *p) {
+    return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+// ------------------------------------------------------------ descriptors
+__host__ __device__ constexpr uint64_t smem_desc(uint32_t saddr, uint32_t lbo, uint32_t sbo) {
+    return (uint64_t)((saddr & 0x3FFFFu) >> 4) | ((uint64_t)((lbo >> 4) & 0x3FFFu) << 16) |
+           ((uint64_t)((sbo >> 4) & 0x3FFFu) << 32) | (1ull << 46);  // version 1, no swizzle
+}
+
+enum Fmt : uint32_t { F16 = 0, BF16 = 1, TF32 = 2 };
+
+// kind::f16 / kind::tf32 instruction descriptor, fp32 accumulate.
+__host__ __device__ constexpr uint32_t idesc(int M, int N, uint32_t ab_fmt, bool a_mn_major, bool b_mn_major,
+                                             bool a_neg = false) {
+    return (1u << 4)                               // D format: F32
+           | (ab_fmt << 7) | (ab_fmt << 10)        // A, B formats
+           | ((a_neg ? 1u : 0u) << 13)
+           | ((a_mn_major ? 1u : 0u) << 15) | ((b_mn_major ? 1u : 0u) << 16)
+           | ((uint32_t)(N >> 3) << 17) | ((uint32_t)(M >> 4) << 24);
+}
+
+// ------------------------------------------------------------------ TMEM
+// Warp-collective: the calling warp allocates `cols` columns (power of 2,
+// >= 32) and the base address is written to *dst (shared memory).
+__device__ __forceinline__ void tmem_alloc(uint32_t *dst, uint32_t cols) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_addr(dst)),
+                 "r"(cols));
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+}
+__device__ __forceinline__ void tmem_dealloc(uint32_t taddr, uint32_t cols) {
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(cols));
+}
+__device__ __forceinline__ void fence_before_sync() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void fence_after_sync() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+// Make generic-proxy shared-memory writes visible to the tensor core.
+__device__ __forceinline__ void fence_smem_to_async() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+
+// ------------------------------------------------------------------- MMA
+__device__ __forceinline__ void mma_f16(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t id,
+                                        bool accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}\n" ::"r"(d_tmem),
+        "l"(adesc), "l"(bdesc), "r"(id), "r"(accumulate ? 1u : 0u));
+}
+__device__ __forceinline__ void mma_tf32(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t id,
+                                         bool accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::tf32 [%0], %1, %2, %3, p;\n\t}\n" ::"r"(d_tmem),
+        "l"(adesc), "l"(bdesc), "r"(id), "r"(accumulate ? 1u : 0u));
+}
+// Arrive on `bar` once every MMA this thread issued so far has completed.
+__device__ __forceinline__ void commit(uint64_t *bar) {
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+                     smem_addr(bar))
+                 : "memory");
+}
+
+// -------------------------------------------------------------- mbarrier
+__device__ __forceinline__ void mbar_init(uint64_t *bar, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_addr(bar)), "r"(count) : "memory");
+}
+__device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, uint32_t phase) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}\n"
+        : "=r"(ok)
+        : "r"(smem_addr(bar)), "r"(phase)
+        : "memory");
+    return ok != 0;
+}
+// Wait for the phase with parity `phase` to complete, at most `limit` polls.
+__device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t phase, int *err, uint32_t limit = 1u << 26) {
+    for (uint32_t i = 0; i < limit; ++i)
+        if (mbar_try_wait(bar, phase)) return true;
+    if (err) atomicExch(err, 1);
+    return false;
+}
+
+// ------------------------------------------------------- TMEM <-> regs
+// 32 lanes x 16 consecutive 32-bit columns: thread t gets lane (base lane + t).
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, float (&v)[16]) {
+    uint32_t r[16];
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x16.b32 "
+        "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+        : "r"(taddr));
+#pragma unroll
+    for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
+}
+__device__ __forceinline__ void tmem_st16(uint32_t taddr, const float (&v)[16]) {
+    asm volatile(
+        "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], "
+        "{%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};" ::"r"(taddr),
+        "r"(__float_as_uint(v[0])), "r"(__float_as_uint(v[1])), "r"(__float_as_uint(v[2])),
+        "r"(__float_as_uint(v[3])), "r"(__float_as_uint(v[4])), "r"(__float_as_uint(v[5])),
+        "r"(__float_as_uint(v[6])), "r"(__float_as_uint(v[7])), "r"(__float_as_uint(v[8])),
+        "r"(__float_as_uint(v[9])), "r"(__float_as_uint(v[10])), "r"(__float_as_uint(v[11])),
+        "r"(__float_as_uint(v[12])), "r"(__float_as_uint(v[13])), "r"(__float_as_uint(v[14])),
+        "r"(__float_as_uint(v[15])));
+}
+__device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+__device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
+
+// TMEM address of (lane, column).
+__device__ __forceinline__ uint32_t taddr(uint32_t base, uint32_t lane, uint32_t col) {
+    return base + (lane << 16) + col;
+}
+
+// ------------------------------------------------------ layout offsets
+// Byte offset of element (r, k) in a K-major 16-bit tile with KK k-columns.
+__host__ __device__ constexpr uint32_t kmaj16(uint32_t r, uint32_t k, uint32_t KK) {
+    return (r >> 3) * (KK / 8) * 128 + (k >> 3) * 128 + (r & 7) * 16 + (k & 7) * 2;
+}
+// Byte offset of element (k, c) in an MN-major 16-bit tile with CC mn-columns.
+__host__ __device__ constexpr uint32_t mnmaj16(uint32_t k, uint32_t c, uint32_t CC) {
+    return (k >> 3) * (CC / 8) * 128 + (c >> 3) * 128 + (k & 7) * 16 + (c & 7) * 2;
+}
+// Descriptor of K-step `ks` (16 k's) of a K-major 16-bit tile with KK columns.
+__device__ __forceinline__ uint64_t desc_kmaj16(const void *tile, uint32_t KK, uint32_t ks) {
+    return smem_desc(smem_addr(tile) + ks * 256, 128, (KK / 8) * 128);
+}
+// Descriptor of K-step `ks` of an MN-major 16-bit tile with CC mn-columns.
+__device__ __forceinline__ uint64_t desc_mnmaj16(const void *tile, uint32_t CC, uint32_t ks) {
+    return smem_desc(smem_addr(tile) + ks * 2 * (CC / 8) * 128, (CC / 8) * 128, 128);
+}
+// 32-bit (tf32) K-major: 4 k's per 16 bytes; one kind::tf32 MMA consumes K = 8.
+__host__ __device__ constexpr uint32_t kmaj32(uint32_t r, uint32_t k, uint32_t KK) {
+    return (r >> 3) * (KK / 4) * 128 + (k >> 2) * 128 + (r & 7) * 16 + (k & 3) * 4;
+}
+__device__ __forceinline__ uint64_t desc_kmaj32(const void *tile, uint32_t KK, uint32_t ks) {
+    return smem_desc(smem_addr(tile) + ks * 256, 128, (KK / 4) * 128);
+}
+
+}  // namespace umma
+}  // namespace gdn
