@@ -393,7 +393,7 @@ def run_chunk_bench(args, world, barrier, peaks):
     nbytes = metrics.chunk_bytes(c["B"], c["T"], c["Hk"], c["Hv"], c["dk"], c["dv"], e_in=2, e_out=2, e_state=4)
     tok = c["B"] * c["T"] * world / (ms / 1e3)
     return {"workload": "config 2 shard per GPU: B=8, T=32768, 16/32 heads, 128x128, bf16 q/k/v/o, fp32 state",
-            "kernel": "chunk_scan_fp32_kernel (CUDA-core fp32)",
+            "kernel": "chunk_tc_kernel<bf16> (tcgen05 MMAs, fp32 state in TMEM)",
             "tokens_per_s": round(tok, 1), "ms": round(ms, 3),
             "tflops": round(flops / (ms / 1e3) / 1e12, 2), "gbs": round(nbytes / (ms / 1e3) / 1e9, 1),
             "tensor_frac_of_bf16_peak": round(flops / (ms / 1e3) / 1e12 / peaks["bf16_tflops"], 4),

@@ -1,0 +1,101 @@
+"""The tensor-core chunked scan (csrc/chunk_tc.cu, bf16/fp16 q/k/v, fp32 state
+in TMEM) against the oracle token loop and against the fp32 CUDA-core kernel.
+
+Tolerance: 2e-2 relative L2 on outputs and final state (the build's bar for
+bf16 / fp16 paths); both kernels see the same rounded inputs.
+"""
+from __future__ import annotations
+
+import numpy as np
+import pytest
+
+import oracle
+from conftest import rel_l2
+from orionsbelt_b200 import ops, synth
+
+pytestmark = pytest.mark.gpu
+
+TOL = 2e-2
+
+
+def _round(a, kind):
+    return oracle.u16_to_f32(oracle.f32_to_u16(a, kind), kind)
+
+
+def _dev(cuda, a, dt):
+    return cuda.from_numpy(np.ascontiguousarray(a)).cuda().to(dt)
+
+
+@pytest.mark.parametrize("T", [1, 63, 64, 65, 200, 640])
+@pytest.mark.parametrize("kind", ["bf16", "f16"])
+def test_tc_vs_token_loop(cuda, orc, T, kind):
+    dt = cuda.bfloat16 if kind == "bf16" else cuda.float16
+    d = synth.host_gdn(2, T, 2, 4, 128, 128, g_scale=0.3, seed=T, state_std=0.05)
+    for key in ("q", "k", "v"):
+        d[key] = _round(d[key], kind)
+    S_want, o_want = orc.delta_rule_seq(d["S0"], d["q"], d["k"], d["v"], d["g"], d["beta"], scale=0.088)
+    S = cuda.from_numpy(d["S0"]).cuda()
+    o = cuda.empty(d["v"].shape, dtype=cuda.float32, device="cuda")
+    ops.chunk_delta_rule(_dev(cuda, d["q"], dt), _dev(cuda, d["k"], dt), _dev(cuda, d["v"], dt),
+                         cuda.from_numpy(d["g"]).cuda(), cuda.from_numpy(d["beta"]).cuda(), S, o, scale=0.088)
+    cuda.cuda.synchronize()
+    assert rel_l2(o.cpu().numpy(), o_want) < TOL
+    assert rel_l2(S.cpu().numpy(), S_want) < TOL
+
+
+def test_tc_strong_decay_fp16_state(cuda, orc):
+    """Config-3 numerics: g = -softplus(N(0,1)), fp16 state storage, fp16 inputs."""
+    d = synth.host_gdn(2, 500, 2, 4, 128, 128, g_scale=1.0, seed=7, state_std=0.05)
+    for key in ("q", "k", "v"):
+        d[key] = _round(d[key], "f16")
+    d["S0"] = _round(d["S0"], "f16")
+    S_want, o_want = orc.delta_rule_seq(d["S0"], d["q"], d["k"], d["v"], d["g"], d["beta"], scale=1.0)
+    S = _dev(cuda, d["S0"], cuda.float16)
+    o = cuda.empty(d["v"].shape, dtype=cuda.float16, device="cuda")
+    h = cuda.float16
+    ops.chunk_delta_rule(_dev(cuda, d["q"], h), _dev(cuda, d["k"], h), _dev(cuda, d["v"], h),
+                         cuda.from_numpy(d["g"]).cuda(), cuda.from_numpy(d["beta"]).cuda(), S, o, scale=1.0)
+    assert rel_l2(o.float().cpu().numpy(), o_want) < TOL
+    assert rel_l2(S.float().cpu().numpy(), S_want) < TOL
+
+
+def _fp32_reference_run(cuda, d, scale):
+    """The fp32 CUDA-core kernel on the same (rounded) values."""
+    f = {k: v.float().contiguous() for k, v in d.items() if k in ("q", "k", "v")}
+    S = d["S0"].float().clone()
+    o = cuda.empty(f["v"].shape, dtype=cuda.float32, device="cuda")
+    ops.chunk_delta_rule(f["q"], f["k"], f["v"], d["g"], d["beta"], S, o, scale=scale)
+    return S, o
+
+
+def test_tc_config2_shard_against_fp32_kernel(cuda):
+    """Full config-2 shard (B=8, T=32768, 16/32 heads, bf16 q/k/v, fp32 state)
+    against the fp32 CUDA-core kernel on the same values."""
+    torch = cuda
+    d = synth.device_gdn(8, 32768, 16, 32, 128, 128, g_scale=0.1, seed=77, in_dtype=torch.bfloat16)
+    S = d["S0"].clone()
+    o = torch.empty_like(d["v"])
+    ops.chunk_delta_rule(d["q"], d["k"], d["v"], d["g"], d["beta"], S, o, scale=1.0)
+    S_ref, o_ref = _fp32_reference_run(cuda, d, 1.0)
+    rl = lambda a, b: (torch.linalg.norm(a.float() - b) / torch.linalg.norm(b)).item()  # noqa: E731
+    assert rl(o, o_ref) < TOL
+    assert rl(S, S_ref) < TOL
+
+
+def test_tc_continuity(cuda):
+    """Two tensor-core calls with the state carried == one call."""
+    torch = cuda
+    d = synth.device_gdn(1, 512, 2, 4, 128, 128, g_scale=0.2, seed=9, in_dtype=torch.bfloat16, state_std=0.05)
+    S_full = d["S0"].clone()
+    o_full = torch.empty_like(d["v"])
+    ops.chunk_delta_rule(d["q"], d["k"], d["v"], d["g"], d["beta"], S_full, o_full, scale=0.1)
+    S = d["S0"].clone()
+    o_a = torch.empty_like(d["v"][:, :256])
+    o_b = torch.empty_like(d["v"][:, 256:])
+    part = lambda x, a, b: x[:, a:b].contiguous()  # noqa: E731
+    ops.chunk_delta_rule(part(d["q"], 0, 256), part(d["k"], 0, 256), part(d["v"], 0, 256), part(d["g"], 0, 256),
+                         part(d["beta"], 0, 256), S, o_a, scale=0.1)
+    ops.chunk_delta_rule(part(d["q"], 256, 512), part(d["k"], 256, 512), part(d["v"], 256, 512),
+                         part(d["g"], 256, 512), part(d["beta"], 256, 512), S, o_b, scale=0.1)
+    rl = lambda a, b: (torch.linalg.norm(a.float() - b.float()) / torch.linalg.norm(b.float())).item()  # noqa: E731
+    assert rl(torch.cat([o_a, o_b], 1), o_full) < 1e-3 and rl(S, S_full) < 1e-3
