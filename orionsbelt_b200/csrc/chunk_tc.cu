@@ -102,6 +102,70 @@ __device__ __forceinline__ void st_any(void *p, size_t i, int dt, float v) {
     }
 }
 
+// Loads of one chunk held in registers until they are stored to shared
+// memory.  Thread t owns row r = 8*(t/32) + t%8 of the chunk and the four
+// 8-element column groups cc = 8*(4*i + (t%32)/8), i = 0..3: a warp covers 8
+// consecutive rows x 4 column groups, so its 16-byte global loads use whole
+// 32-byte sectors and its 16-byte shared stores into the core-matrix layouts
+// (8 rows x 16 bytes contiguous) are free of bank conflicts.
+struct ChunkRegs {
+    uint4 k[4], q[4], v[4];
+    float g0, g1, b0, b1;  // gates of rows 2*lane, 2*lane+1 (warp 0 only)
+};
+
+template <typename IT>
+__device__ __forceinline__ void prefetch_chunk(ChunkRegs &cr, const kai_gdn_chunk_args &p, long long b,
+                                               long long h, long long hk, long long c0, int t) {
+    const long long Hv = (long long)p.heads_v, Hk = (long long)p.heads_k, T = (long long)p.seq;
+    const IT *kp = static_cast<const IT *>(p.k), *qp = static_cast<const IT *>(p.q);
+    const IT *vp = static_cast<const IT *>(p.v);
+    const int r = 8 * (t / 32) + (t % 8), a = (t % 32) / 8;
+    const long long tok = c0 + r;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        const int cc = 8 * (4 * i + a);
+        if (tok < T) {
+            const size_t ki = ((size_t)(b * T + tok) * Hk + hk) * D + cc;
+            const size_t vi = ((size_t)(b * T + tok) * Hv + h) * D + cc;
+            cr.k[i] = __ldg(reinterpret_cast<const uint4 *>(kp + ki));
+            cr.q[i] = __ldg(reinterpret_cast<const uint4 *>(qp + ki));
+            cr.v[i] = __ldg(reinterpret_cast<const uint4 *>(vp + vi));
+        } else {
+            cr.k[i] = cr.q[i] = cr.v[i] = make_uint4(0, 0, 0, 0);
+        }
+    }
+    if (t < 32) {
+        const long long r0 = c0 + 2 * t, r1 = r0 + 1;
+        cr.g0 = r0 < T ? __ldg(p.g + (size_t)(b * T + r0) * Hv + h) : 0.f;
+        cr.b0 = r0 < T ? __ldg(p.beta + (size_t)(b * T + r0) * Hv + h) : 0.f;
+        cr.g1 = r1 < T ? __ldg(p.g + (size_t)(b * T + r1) * Hv + h) : 0.f;
+        cr.b1 = r1 < T ? __ldg(p.beta + (size_t)(b * T + r1) * Hv + h) : 0.f;
+    }
+}
+
+// 16 consecutive output values of one row, as 16-byte vector stores.
+__device__ __forceinline__ void st16_out(void *o, size_t idx, int dt, const float (&v)[16]) {
+    if (dt == KAI_GDN_F32) {
+        float4 *f = reinterpret_cast<float4 *>(static_cast<float *>(o) + idx);
+#pragma unroll
+        for (int i = 0; i < 4; ++i) f[i] = make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
+        return;
+    }
+    uint4 u[2];
+    if (dt == KAI_GDN_BF16) {
+        __nv_bfloat16 *hh = reinterpret_cast<__nv_bfloat16 *>(u);
+#pragma unroll
+        for (int i = 0; i < 16; ++i) hh[i] = __float2bfloat16_rn(v[i]);
+    } else {
+        __half *hh = reinterpret_cast<__half *>(u);
+#pragma unroll
+        for (int i = 0; i < 16; ++i) hh[i] = __float2half_rn(v[i]);
+    }
+    uint4 *dst = reinterpret_cast<uint4 *>(static_cast<uint16_t *>(o) + idx);
+    dst[0] = u[0];
+    dst[1] = u[1];
+}
+
 // out(i, j) of the 16x16 block product X[xr.., xc..] . Y[yr.., yc..] (fp32, stride LDF)
 __device__ __forceinline__ float bprod(const float *X, int xr, int xc, const float *Y, int yr, int yc, int i,
                                        int j) {
@@ -130,9 +194,10 @@ __device__ void invert_unit_lower(TcSmem &sm, int t) {
     } else {
         // zero the blocks above the diagonal
         for (int e = t - 64; e < 6 * 256; e += NT - 64) {
+            // block pairs (0,1) (0,2) (0,3) (1,2) (1,3) (2,3)
             int b = e / 256, w = e % 256, i = w / 16, j = w % 16;
-            const int bi[6] = {0, 0, 0, 1, 1, 2}, bj[6] = {1, 2, 3, 2, 3, 3};
-            T[(16 * bi[b] + i) * LDF + 16 * bj[b] + j] = 0.f;
+            int bi = b < 3 ? 0 : (b < 5 ? 1 : 2), bj = b < 3 ? b + 1 : (b < 5 ? b - 1 : 3);
+            T[(16 * bi + i) * LDF + 16 * bj + j] = 0.f;
         }
     }
     __syncthreads();
@@ -198,8 +263,6 @@ __global__ void __launch_bounds__(NT, 1) chunk_tc_kernel(kai_gdn_chunk_args p, i
     const int t = threadIdx.x, warp = t / 32, lane = t % 32, q = warp % 4, hf = warp / 4;
     const long long Hv = (long long)p.heads_v, Hk = (long long)p.heads_k, T = (long long)p.seq;
     const long long unit = blockIdx.x, b = unit / Hv, h = unit % Hv, hk = h / (Hv / Hk);
-    const IT *kp = static_cast<const IT *>(p.k), *qp = static_cast<const IT *>(p.q);
-    const IT *vp = static_cast<const IT *>(p.v);
     const float scale = p.scale;
 
     if (t == 0) {
@@ -236,13 +299,12 @@ __global__ void __launch_bounds__(NT, 1) chunk_tc_kernel(kai_gdn_chunk_args p, i
         tmem_wait_st();
     }
 
+    ChunkRegs cr;
+    prefetch_chunk<IT>(cr, p, b, h, hk, 0, t);
     for (long long c0 = 0; c0 < T; c0 += C) {
         // ---------------------------------------------------- L: gates
         if (t < 32) {
-            float g0 = 0.f, g1 = 0.f, b0 = 0.f, b1 = 0.f;
-            long long r0 = c0 + 2 * t, r1 = r0 + 1;
-            if (r0 < T) { g0 = p.g[(size_t)(b * T + r0) * Hv + h]; b0 = p.beta[(size_t)(b * T + r0) * Hv + h]; }
-            if (r1 < T) { g1 = p.g[(size_t)(b * T + r1) * Hv + h]; b1 = p.beta[(size_t)(b * T + r1) * Hv + h]; }
+            const float g0 = cr.g0, g1 = cr.g1;
             float pair = g0 + g1, incl = pair;
 #pragma unroll
             for (int o = 1; o < 32; o <<= 1) {
@@ -252,8 +314,8 @@ __global__ void __launch_bounds__(NT, 1) chunk_tc_kernel(kai_gdn_chunk_args p, i
             float excl = incl - pair;
             sm.G[2 * t] = excl + g0;
             sm.G[2 * t + 1] = incl;
-            sm.beta[2 * t] = b0;
-            sm.beta[2 * t + 1] = b1;
+            sm.beta[2 * t] = cr.b0;
+            sm.beta[2 * t + 1] = cr.b1;
         }
         __syncthreads();
         if (t < C) {
@@ -262,39 +324,24 @@ __global__ void __launch_bounds__(NT, 1) chunk_tc_kernel(kai_gdn_chunk_args p, i
         }
         __syncthreads();
         // ------------------------------------------ L: K, Q, V -> tiles
-        for (int e = t; e < C * 16; e += NT) {
-            const int r = e / 16, cc = (e % 16) * 8;
-            const long long tok = c0 + r;
-            float kv[8], qv[8], vv[8];
-            if (tok < T) {
-                const size_t ki = ((size_t)(b * T + tok) * Hk + hk) * D + cc;
-                const size_t vi = ((size_t)(b * T + tok) * Hv + h) * D + cc;
-                uint4 ku = *reinterpret_cast<const uint4 *>(kp + ki);
-                uint4 qu = *reinterpret_cast<const uint4 *>(qp + ki);
-                uint4 vu = *reinterpret_cast<const uint4 *>(vp + vi);
-                *reinterpret_cast<uint4 *>(sm.KQ + kmaj16(r, cc, D)) = ku;
-                *reinterpret_cast<uint4 *>(sm.KQ + kmaj16(C + r, cc, D)) = qu;
-                const IT *kh = reinterpret_cast<const IT *>(&ku), *vh = reinterpret_cast<const IT *>(&vu);
-#pragma unroll
-                for (int i = 0; i < 8; ++i) {
-                    kv[i] = TR::to_f(kh[i]);
-                    vv[i] = TR::to_f(vh[i]);
-                }
-            } else {
-#pragma unroll
-                for (int i = 0; i < 8; ++i) kv[i] = qv[i] = vv[i] = 0.f;
-                *reinterpret_cast<uint4 *>(sm.KQ + kmaj16(r, cc, D)) = make_uint4(0, 0, 0, 0);
-                *reinterpret_cast<uint4 *>(sm.KQ + kmaj16(C + r, cc, D)) = make_uint4(0, 0, 0, 0);
-            }
+        {
+            const int r = 8 * warp + (lane % 8), a = lane / 8;
             const float bk = sm.beta[r] * sm.eG[r], bv = sm.beta[r];
 #pragma unroll
-            for (int i = 0; i < 8; ++i) {
-                kv[i] *= bk;
-                vv[i] *= bv;
+            for (int i = 0; i < 4; ++i) {
+                const int cc = 8 * (4 * i + a);
+                *reinterpret_cast<uint4 *>(sm.KQ + kmaj16(r, cc, D)) = cr.k[i];
+                *reinterpret_cast<uint4 *>(sm.KQ + kmaj16(C + r, cc, D)) = cr.q[i];
+                const IT *kh = reinterpret_cast<const IT *>(&cr.k[i]), *vh = reinterpret_cast<const IT *>(&cr.v[i]);
+                float kv[8], vv[8];
+#pragma unroll
+                for (int j = 0; j < 8; ++j) {
+                    kv[j] = TR::to_f(kh[j]) * bk;
+                    vv[j] = TR::to_f(vh[j]) * bv;
+                }
+                st_vec8<IT>(sm.R, mnmaj16(r, cc, 2 * D), kv);
+                st_vec8<IT>(sm.R, mnmaj16(r, D + cc, 2 * D), vv);
             }
-            st_vec8<IT>(sm.R, mnmaj16(r, cc, 2 * D), kv);
-            st_vec8<IT>(sm.R, mnmaj16(r, D + cc, 2 * D), vv);
-            (void)qv;
         }
         // ------------------------------------------ M1: [K;Q] K^T
         issue_sync();
@@ -320,7 +367,7 @@ __global__ void __launch_bounds__(NT, 1) chunk_tc_kernel(kai_gdn_chunk_args p, i
 #pragma unroll
                     for (int jj = 0; jj < 16; ++jj) {
                         const int s = cb + jj;
-                        sm.Af[r * LDF + s] = s < r ? br * v[jj] * expf(gr - sm.G[s]) : 0.f;
+                        sm.Af[r * LDF + s] = s < r ? br * v[jj] * __expf(gr - sm.G[s]) : 0.f;
                     }
                 } else {
                     const int r = i - C;
@@ -329,23 +376,33 @@ __global__ void __launch_bounds__(NT, 1) chunk_tc_kernel(kai_gdn_chunk_args p, i
 #pragma unroll
                     for (int jj = 0; jj < 8; ++jj) {
                         const int s0 = cb + jj, s1 = cb + 8 + jj;
-                        a[jj] = s0 <= r ? scale * v[jj] * expf(gr - sm.G[s0]) : 0.f;
-                        c[jj] = s1 <= r ? scale * v[8 + jj] * expf(gr - sm.G[s1]) : 0.f;
+                        a[jj] = s0 <= r ? scale * v[jj] * __expf(gr - sm.G[s0]) : 0.f;
+                        c[jj] = s1 <= r ? scale * v[8 + jj] * __expf(gr - sm.G[s1]) : 0.f;
                     }
                     st_vec8<IT>(sm.P, kmaj16(r, cb, C), a);
                     st_vec8<IT>(sm.P, kmaj16(r, cb + 8, C), c);
                 }
             }
         }
-        // K' = K e^(G_63 - G) over K rows, Qg = scale Q e^G over Q rows (in place)
-        for (int e = t; e < 2 * C * 16; e += NT) {
-            const int row = e / 16, cc = (e % 16) * 8;
-            const float f = row < C ? sm.eGl[row] : scale * sm.eG[row - C];
-            float v[8];
-            ld_vec8<IT>(sm.KQ, kmaj16(row, cc, D), v);
+        // K' = K e^(G_63 - G) over the K rows, Qg = scale Q e^G over the Q rows,
+        // from the raw values still in registers; then fetch the next chunk.
+        {
+            const int r = 8 * warp + (lane % 8), a = lane / 8;
+            const float fk = sm.eGl[r], fq = scale * sm.eG[r];
 #pragma unroll
-            for (int i = 0; i < 8; ++i) v[i] *= f;
-            st_vec8<IT>(sm.KQ, kmaj16(row, cc, D), v);
+            for (int i = 0; i < 4; ++i) {
+                const int cc = 8 * (4 * i + a);
+                const IT *kh = reinterpret_cast<const IT *>(&cr.k[i]), *qh = reinterpret_cast<const IT *>(&cr.q[i]);
+                float kv[8], qv[8];
+#pragma unroll
+                for (int j = 0; j < 8; ++j) {
+                    kv[j] = TR::to_f(kh[j]) * fk;
+                    qv[j] = TR::to_f(qh[j]) * fq;
+                }
+                st_vec8<IT>(sm.KQ, kmaj16(r, cc, D), kv);
+                st_vec8<IT>(sm.KQ, kmaj16(C + r, cc, D), qv);
+            }
+            if (c0 + C < T) prefetch_chunk<IT>(cr, p, b, h, hk, c0 + C, t);
         }
         __syncthreads();
         // ------------------------------------------ INV: T = (I + A)^-1
@@ -458,11 +515,7 @@ __global__ void __launch_bounds__(NT, 1) chunk_tc_kernel(kai_gdn_chunk_args p, i
                 float o[16];
                 tmem_ld16(taddr(TO, 32 * q, cb), o);
                 tmem_wait_ld();
-                if (lane < 16 && tok < T) {
-                    const size_t oi = ((size_t)(b * T + tok) * Hv + h) * D + cb;
-#pragma unroll
-                    for (int i = 0; i < 16; ++i) st_any(p.o, oi + i, p.out_dtype, o[i]);
-                }
+                if (lane < 16 && tok < T) st16_out(p.o, ((size_t)(b * T + tok) * Hv + h) * D + cb, p.out_dtype, o);
             }
             const int d = 32 * q + lane;
             for (int cb = hf * 64; cb < hf * 64 + 64; cb += 16) {
@@ -507,7 +560,7 @@ __global__ void __launch_bounds__(NT, 1) chunk_tc_kernel(kai_gdn_chunk_args p, i
 bool chunk_tc_supported(const kai_gdn_chunk_args *a) {
     if (a->dk != 128 || a->dv != 128 || a->chunk != 64) return false;
     if (a->in_dtype != KAI_GDN_BF16 && a->in_dtype != KAI_GDN_F16) return false;
-    if (((uintptr_t)a->q | (uintptr_t)a->k | (uintptr_t)a->v) % 16) return false;
+    if (((uintptr_t)a->q | (uintptr_t)a->k | (uintptr_t)a->v | (uintptr_t)a->o) % 16) return false;
     return true;
 }
 
