@@ -26,9 +26,14 @@
 //   [256,384) W, later O (after W has been copied out), M=64
 //   [384,512) U        M=64
 // Operand tiles are bf16/fp16 in the no-swizzle core-matrix layouts of
-// umma.cuh.  The K-major [K;Q] tile doubles as the MN-major A operand of
-// K'^T V' (a K-major tile with 128 columns is the MN-major tile of its
-// transpose), so K' is written over K in place.
+// umma.cuh.  Once [W | U] is computed the R tile is free and holds K' and Qg
+// (K-major 64 x 128 each); a K-major tile with 128 columns is also the
+// MN-major tile of its transpose, so K' serves directly as the A operand of
+// K'^T V'.
+//
+// Overlap: the S *= gamma pass runs while W S / Qg S execute, and the next
+// chunk's gates are scanned while P V' / K'^T V' execute; the next chunk's
+// q, k, v, g, beta are loaded into registers during the current chunk.
 #include "gdn_internal.cuh"
 #include "umma.cuh"
 
@@ -38,7 +43,7 @@ namespace {
 using namespace umma;
 
 constexpr int C = 64, D = 128, NT = 256;
-constexpr int LDF = 65;  // padded fp32 row stride (conflict-free column walks)
+constexpr int LDF = 68;  // fp32 row stride: 16-byte aligned rows, 8 rows span all banks
 
 template <typename IT> struct InTraits;
 template <> struct InTraits<__nv_bfloat16> {
@@ -166,82 +171,107 @@ __device__ __forceinline__ void st16_out(void *o, size_t idx, int dt, const floa
     dst[1] = u[1];
 }
 
-// out(i, j) of the 16x16 block product X[xr.., xc..] . Y[yr.., yc..] (fp32, stride LDF)
-__device__ __forceinline__ float bprod(const float *X, int xr, int xc, const float *Y, int yr, int yc, int i,
-                                       int j) {
-    float acc = 0.f;
-#pragma unroll
-    for (int k = 0; k < 16; ++k) acc = fmaf(X[(xr + i) * LDF + xc + k], Y[(yr + k) * LDF + yc + j], acc);
-    return acc;
-}
-
-// T = (I + A)^-1 for strictly lower A (64 x 64, fp32), by 16 x 16 blocks:
-// diagonal blocks by forward substitution, then T_ij = -T_ii sum_k A_ik T_kj.
+// T = (I + A)^-1 for strictly lower A (64 x 64, fp32, row stride LDF), by
+// 16 x 16 blocks: the four diagonal blocks by right-looking substitution (a
+// dependency chain of 16 steps per column), then T_ij = -T_ii sum_k A_ik T_kj
+// for the block diagonals i - j = 1, 2, 3.  Every thread computes its outputs
+// with interleaved accumulators so the FMA chains overlap.
 __device__ void invert_unit_lower(TcSmem &sm, int t) {
     float *A = sm.Af, *T = sm.Tf, *M = sm.Mscr;
     if (t < 64) {
-        const int blk = t / 16, j = t % 16, o = 16 * blk;
-        float x[16];
+        const int o = 16 * (t / 16), j = t % 16;
+        float acc[16];
 #pragma unroll
-        for (int r = 0; r < 16; ++r) {
-            float acc = 0.f;
+        for (int r = 0; r < 16; ++r) acc[r] = 0.f;
 #pragma unroll
-            for (int s = 0; s < r; ++s) acc = fmaf(A[(o + r) * LDF + o + s], x[s], acc);
-            x[r] = r < j ? 0.f : (r == j ? 1.f : -acc);
+        for (int s = 0; s < 16; ++s) {
+            const float xs = s < j ? 0.f : (s == j ? 1.f : -acc[s]);
+            T[(o + s) * LDF + o + j] = xs;
+#pragma unroll
+            for (int r = s + 1; r < 16; ++r) acc[r] = fmaf(A[(o + r) * LDF + o + s], xs, acc[r]);
         }
-#pragma unroll
-        for (int r = 0; r < 16; ++r) T[(o + r) * LDF + o + j] = x[r];
     } else {
-        // zero the blocks above the diagonal
-        for (int e = t - 64; e < 6 * 256; e += NT - 64) {
-            // block pairs (0,1) (0,2) (0,3) (1,2) (1,3) (2,3)
-            int b = e / 256, w = e % 256, i = w / 16, j = w % 16;
-            int bi = b < 3 ? 0 : (b < 5 ? 1 : 2), bj = b < 3 ? b + 1 : (b < 5 ? b - 1 : 3);
-            T[(16 * bi + i) * LDF + 16 * bj + j] = 0.f;
+        // zero the six blocks above the diagonal: (0,1) (0,2) (0,3) (1,2) (1,3) (2,3)
+        for (int e = t - 64; e < 6 * 64; e += NT - 64) {
+            const int bb = e / 64, w = e % 64, i = w / 4, j4 = (w % 4) * 4;
+            const int bi = bb < 3 ? 0 : (bb < 5 ? 1 : 2), bj = bb < 3 ? bb + 1 : (bb < 5 ? bb - 1 : 3);
+            *reinterpret_cast<float4 *>(&T[(16 * bi + i) * LDF + 16 * bj + j4]) = make_float4(0.f, 0.f, 0.f, 0.f);
         }
     }
     __syncthreads();
-    // level 1: (1,0), (2,1), (3,2)
-    for (int e = t; e < 3 * 256; e += NT) {
-        int b = e / 256, i = (e % 256) / 16, j = e % 16;
-        M[b * 272 + i * 17 + j] = bprod(A, 16 * (b + 1), 16 * b, T, 16 * b, 16 * b, i, j);
-    }
-    __syncthreads();
-    for (int e = t; e < 3 * 256; e += NT) {
-        int b = e / 256, i = (e % 256) / 16, j = e % 16, r0 = 16 * (b + 1);
-        float acc = 0.f;
-#pragma unroll
-        for (int k = 0; k < 16; ++k) acc = fmaf(T[(r0 + i) * LDF + r0 + k], M[b * 272 + k * 17 + j], acc);
-        T[(r0 + i) * LDF + 16 * b + j] = -acc;
-    }
-    __syncthreads();
-    // level 2: (2,0), (3,1)
-    for (int e = t; e < 2 * 256; e += NT) {
-        int b = e / 256, i = (e % 256) / 16, j = e % 16, ri = 16 * (b + 2), cj = 16 * b;
-        M[b * 272 + i * 17 + j] = bprod(A, ri, cj, T, cj, cj, i, j) + bprod(A, ri, cj + 16, T, cj + 16, cj, i, j);
-    }
-    __syncthreads();
-    for (int e = t; e < 2 * 256; e += NT) {
-        int b = e / 256, i = (e % 256) / 16, j = e % 16, ri = 16 * (b + 2);
-        float acc = 0.f;
-#pragma unroll
-        for (int k = 0; k < 16; ++k) acc = fmaf(T[(ri + i) * LDF + ri + k], M[b * 272 + k * 17 + j], acc);
-        T[(ri + i) * LDF + 16 * b + j] = -acc;
-    }
-    __syncthreads();
-    // level 3: (3,0)
+    const int i = t / 16, j = t % 16;
+    // level 1: M_b = A_{b+1,b} T_bb, then T_{b+1,b} = -T_{b+1,b+1} M_b  (b = 0, 1, 2)
     {
-        int i = t / 16, j = t % 16;
-        M[i * 17 + j] = bprod(A, 48, 0, T, 0, 0, i, j) + bprod(A, 48, 16, T, 16, 0, i, j) +
-                        bprod(A, 48, 32, T, 32, 0, i, j);
+        float m0 = 0.f, m1 = 0.f, m2 = 0.f;
+#pragma unroll
+        for (int k = 0; k < 16; ++k) {
+            m0 = fmaf(A[(16 + i) * LDF + k], T[k * LDF + j], m0);
+            m1 = fmaf(A[(32 + i) * LDF + 16 + k], T[(16 + k) * LDF + 16 + j], m1);
+            m2 = fmaf(A[(48 + i) * LDF + 32 + k], T[(32 + k) * LDF + 32 + j], m2);
+        }
+        M[0 * 272 + i * 17 + j] = m0;
+        M[1 * 272 + i * 17 + j] = m1;
+        M[2 * 272 + i * 17 + j] = m2;
     }
     __syncthreads();
     {
-        int i = t / 16, j = t % 16;
-        float acc = 0.f;
+        float t0 = 0.f, t1 = 0.f, t2 = 0.f;
 #pragma unroll
-        for (int k = 0; k < 16; ++k) acc = fmaf(T[(48 + i) * LDF + 48 + k], M[k * 17 + j], acc);
-        T[(48 + i) * LDF + j] = -acc;
+        for (int k = 0; k < 16; ++k) {
+            t0 = fmaf(T[(16 + i) * LDF + 16 + k], M[0 * 272 + k * 17 + j], t0);
+            t1 = fmaf(T[(32 + i) * LDF + 32 + k], M[1 * 272 + k * 17 + j], t1);
+            t2 = fmaf(T[(48 + i) * LDF + 48 + k], M[2 * 272 + k * 17 + j], t2);
+        }
+        T[(16 + i) * LDF + j] = -t0;
+        T[(32 + i) * LDF + 16 + j] = -t1;
+        T[(48 + i) * LDF + 32 + j] = -t2;
+    }
+    __syncthreads();
+    // level 2: M_b = A_{b+2,b} T_bb + A_{b+2,b+1} T_{b+1,b}, T_{b+2,b} = -T_{b+2,b+2} M_b  (b = 0, 1)
+    {
+        float a0 = 0.f, a1 = 0.f, c0 = 0.f, c1 = 0.f;
+#pragma unroll
+        for (int k = 0; k < 16; ++k) {
+            a0 = fmaf(A[(32 + i) * LDF + k], T[k * LDF + j], a0);
+            a1 = fmaf(A[(32 + i) * LDF + 16 + k], T[(16 + k) * LDF + j], a1);
+            c0 = fmaf(A[(48 + i) * LDF + 16 + k], T[(16 + k) * LDF + 16 + j], c0);
+            c1 = fmaf(A[(48 + i) * LDF + 32 + k], T[(32 + k) * LDF + 16 + j], c1);
+        }
+        M[0 * 272 + i * 17 + j] = a0 + a1;
+        M[1 * 272 + i * 17 + j] = c0 + c1;
+    }
+    __syncthreads();
+    {
+        float t0 = 0.f, t1 = 0.f;
+#pragma unroll
+        for (int k = 0; k < 16; ++k) {
+            t0 = fmaf(T[(32 + i) * LDF + 32 + k], M[0 * 272 + k * 17 + j], t0);
+            t1 = fmaf(T[(48 + i) * LDF + 48 + k], M[1 * 272 + k * 17 + j], t1);
+        }
+        T[(32 + i) * LDF + j] = -t0;
+        T[(48 + i) * LDF + 16 + j] = -t1;
+    }
+    __syncthreads();
+    // level 3: M = A_30 T_00 + A_31 T_10 + A_32 T_20, T_30 = -T_33 M
+    {
+        float a0 = 0.f, a1 = 0.f, a2 = 0.f;
+#pragma unroll
+        for (int k = 0; k < 16; ++k) {
+            a0 = fmaf(A[(48 + i) * LDF + k], T[k * LDF + j], a0);
+            a1 = fmaf(A[(48 + i) * LDF + 16 + k], T[(16 + k) * LDF + j], a1);
+            a2 = fmaf(A[(48 + i) * LDF + 32 + k], T[(32 + k) * LDF + j], a2);
+        }
+        M[i * 17 + j] = a0 + a1 + a2;
+    }
+    __syncthreads();
+    {
+        float t0 = 0.f, t1 = 0.f;
+#pragma unroll
+        for (int k = 0; k < 16; k += 2) {
+            t0 = fmaf(T[(48 + i) * LDF + 48 + k], M[k * 17 + j], t0);
+            t1 = fmaf(T[(48 + i) * LDF + 48 + k + 1], M[(k + 1) * 17 + j], t1);
+        }
+        T[(48 + i) * LDF + j] = -(t0 + t1);
     }
     __syncthreads();
 }
@@ -254,6 +284,30 @@ __device__ __forceinline__ void issue_sync() {
     fence_after_sync();
 }
 
+// In-chunk cumulative log decay and its exponentials, from the gate values
+// the prefetch left in warp 0's registers.
+__device__ __forceinline__ void chunk_gates(TcSmem &sm, const ChunkRegs &cr, int t) {
+    if (t < 32) {
+        const float g0 = cr.g0, g1 = cr.g1;
+        float pair = g0 + g1, incl = pair;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            float u = __shfl_up_sync(0xffffffffu, incl, o);
+            if (t >= o) incl += u;
+        }
+        const float excl = incl - pair, gl = __shfl_sync(0xffffffffu, incl, 31);
+        const float G0 = excl + g0, G1 = incl;
+        sm.G[2 * t] = G0;
+        sm.G[2 * t + 1] = G1;
+        sm.beta[2 * t] = cr.b0;
+        sm.beta[2 * t + 1] = cr.b1;
+        sm.eG[2 * t] = expf(G0);
+        sm.eG[2 * t + 1] = expf(G1);
+        sm.eGl[2 * t] = expf(gl - G0);
+        sm.eGl[2 * t + 1] = expf(gl - G1);
+    }
+}
+
 template <typename IT>
 __global__ void __launch_bounds__(NT, 1) chunk_tc_kernel(kai_gdn_chunk_args p, int *err) {
     extern __shared__ __align__(1024) unsigned char smem_raw[];
@@ -264,6 +318,8 @@ __global__ void __launch_bounds__(NT, 1) chunk_tc_kernel(kai_gdn_chunk_args p, i
     const long long Hv = (long long)p.heads_v, Hk = (long long)p.heads_k, T = (long long)p.seq;
     const long long unit = blockIdx.x, b = unit / Hv, h = unit % Hv, hk = h / (Hv / Hk);
     const float scale = p.scale;
+    // this thread's row and column groups in the chunk loads (see ChunkRegs)
+    const int lr = 8 * warp + (lane % 8), la = lane / 8;
 
     if (t == 0) {
         mbar_init(&sm.bar, 1);
@@ -278,7 +334,7 @@ __global__ void __launch_bounds__(NT, 1) chunk_tc_kernel(kai_gdn_chunk_args p, i
     const uint32_t TS = tm, TD1 = tm + 128, TD3 = tm + 128, TW = tm + 256, TO = tm + 256, TU = tm + 384;
     uint32_t phase = 0;
 
-    // ---- initial state: fp32 into TMEM columns 0..127, bf16 copy into sm.S
+    // ---- initial state: fp32 into TMEM columns 0..127, a copy into sm.S
     {
         const int d = 32 * q + lane;
         const size_t sb = (size_t)unit * D * D + (size_t)d * D;
@@ -301,50 +357,32 @@ __global__ void __launch_bounds__(NT, 1) chunk_tc_kernel(kai_gdn_chunk_args p, i
 
     ChunkRegs cr;
     prefetch_chunk<IT>(cr, p, b, h, hk, 0, t);
+    chunk_gates(sm, cr, t);
+    __syncthreads();
+
     for (long long c0 = 0; c0 < T; c0 += C) {
-        // ---------------------------------------------------- L: gates
-        if (t < 32) {
-            const float g0 = cr.g0, g1 = cr.g1;
-            float pair = g0 + g1, incl = pair;
-#pragma unroll
-            for (int o = 1; o < 32; o <<= 1) {
-                float u = __shfl_up_sync(0xffffffffu, incl, o);
-                if (t >= o) incl += u;
-            }
-            float excl = incl - pair;
-            sm.G[2 * t] = excl + g0;
-            sm.G[2 * t + 1] = incl;
-            sm.beta[2 * t] = cr.b0;
-            sm.beta[2 * t + 1] = cr.b1;
-        }
-        __syncthreads();
-        if (t < C) {
-            sm.eG[t] = expf(sm.G[t]);
-            sm.eGl[t] = expf(sm.G[C - 1] - sm.G[t]);
-        }
-        __syncthreads();
-        // ------------------------------------------ L: K, Q, V -> tiles
+        // -------------------------------- L: raw K, Q -> [K;Q]; beta K e^G | beta V -> R
         {
-            const int r = 8 * warp + (lane % 8), a = lane / 8;
-            const float bk = sm.beta[r] * sm.eG[r], bv = sm.beta[r];
+            const float bk = sm.beta[lr] * sm.eG[lr], bv = sm.beta[lr];
 #pragma unroll
             for (int i = 0; i < 4; ++i) {
-                const int cc = 8 * (4 * i + a);
-                *reinterpret_cast<uint4 *>(sm.KQ + kmaj16(r, cc, D)) = cr.k[i];
-                *reinterpret_cast<uint4 *>(sm.KQ + kmaj16(C + r, cc, D)) = cr.q[i];
+                const int cc = 8 * (4 * i + la);
+                *reinterpret_cast<uint4 *>(sm.KQ + kmaj16(lr, cc, D)) = cr.k[i];
+                *reinterpret_cast<uint4 *>(sm.KQ + kmaj16(C + lr, cc, D)) = cr.q[i];
                 const IT *kh = reinterpret_cast<const IT *>(&cr.k[i]), *vh = reinterpret_cast<const IT *>(&cr.v[i]);
                 float kv[8], vv[8];
 #pragma unroll
-                for (int j = 0; j < 8; ++j) {
-                    kv[j] = TR::to_f(kh[j]) * bk;
-                    vv[j] = TR::to_f(vh[j]) * bv;
+                for (int jj = 0; jj < 8; ++jj) {
+                    kv[jj] = TR::to_f(kh[jj]) * bk;
+                    vv[jj] = TR::to_f(vh[jj]) * bv;
                 }
-                st_vec8<IT>(sm.R, mnmaj16(r, cc, 2 * D), kv);
-                st_vec8<IT>(sm.R, mnmaj16(r, D + cc, 2 * D), vv);
+                st_vec8<IT>(sm.R, mnmaj16(lr, cc, 2 * D), kv);
+                st_vec8<IT>(sm.R, mnmaj16(lr, D + cc, 2 * D), vv);
             }
         }
-        // ------------------------------------------ M1: [K;Q] K^T
+        // -------------------------------- M1: [K;Q] K^T
         issue_sync();
+        if (sm.stop) break;
         if (t == 0) {
             const uint32_t id = idesc(128, 64, TR::fmt, false, false);
             for (int ks = 0; ks < D / 16; ++ks)
@@ -354,67 +392,54 @@ __global__ void __launch_bounds__(NT, 1) chunk_tc_kernel(kai_gdn_chunk_args p, i
         if (!mbar_wait(&sm.bar, phase, err)) sm.stop = 1;
         phase ^= 1;
         fence_after_sync();
-        // ------------------------------------------ E1: A, P; K', Qg
+        // -------------------------------- E1: A (fp32) and P (operand tile)
         {
-            const int i = 32 * q + lane;  // D1 row
-            float v[16];
-            for (int cb = hf * 32; cb < hf * 32 + 32; cb += 16) {
-                tmem_ld16(taddr(TD1, 32 * q, cb), v);
-                tmem_wait_ld();
-                if (i < C) {
-                    const int r = i;
-                    const float gr = sm.G[r], br = sm.beta[r];
+            const int i = 32 * q + lane;  // row of [K;Q]K^T
+            float v[32];
+            tmem_ld16(taddr(TD1, 32 * q, hf * 32), *reinterpret_cast<float(*)[16]>(&v[0]));
+            tmem_ld16(taddr(TD1, 32 * q, hf * 32 + 16), *reinterpret_cast<float(*)[16]>(&v[16]));
+            tmem_wait_ld();
+            const int cb = hf * 32;
+            if (i < C) {
+                const int r = i;
+                const float gr = sm.G[r], br = sm.beta[r];
 #pragma unroll
-                    for (int jj = 0; jj < 16; ++jj) {
-                        const int s = cb + jj;
-                        sm.Af[r * LDF + s] = s < r ? br * v[jj] * __expf(gr - sm.G[s]) : 0.f;
-                    }
-                } else {
-                    const int r = i - C;
-                    const float gr = sm.G[r];
-                    float a[8], c[8];
+                for (int jj = 0; jj < 32; jj += 4) {
+                    float4 f;
+                    f.x = cb + jj + 0 < r ? br * v[jj + 0] * __expf(gr - sm.G[cb + jj + 0]) : 0.f;
+                    f.y = cb + jj + 1 < r ? br * v[jj + 1] * __expf(gr - sm.G[cb + jj + 1]) : 0.f;
+                    f.z = cb + jj + 2 < r ? br * v[jj + 2] * __expf(gr - sm.G[cb + jj + 2]) : 0.f;
+                    f.w = cb + jj + 3 < r ? br * v[jj + 3] * __expf(gr - sm.G[cb + jj + 3]) : 0.f;
+                    *reinterpret_cast<float4 *>(&sm.Af[r * LDF + cb + jj]) = f;
+                }
+            } else {
+                const int r = i - C;
+                const float gr = sm.G[r];
 #pragma unroll
-                    for (int jj = 0; jj < 8; ++jj) {
-                        const int s0 = cb + jj, s1 = cb + 8 + jj;
-                        a[jj] = s0 <= r ? scale * v[jj] * __expf(gr - sm.G[s0]) : 0.f;
-                        c[jj] = s1 <= r ? scale * v[8 + jj] * __expf(gr - sm.G[s1]) : 0.f;
+                for (int jj = 0; jj < 32; jj += 8) {
+                    float a[8];
+#pragma unroll
+                    for (int u = 0; u < 8; ++u) {
+                        const int s = cb + jj + u;
+                        a[u] = s <= r ? scale * v[jj + u] * __expf(gr - sm.G[s]) : 0.f;
                     }
-                    st_vec8<IT>(sm.P, kmaj16(r, cb, C), a);
-                    st_vec8<IT>(sm.P, kmaj16(r, cb + 8, C), c);
+                    st_vec8<IT>(sm.P, kmaj16(r, cb + jj, C), a);
                 }
             }
-        }
-        // K' = K e^(G_63 - G) over the K rows, Qg = scale Q e^G over the Q rows,
-        // from the raw values still in registers; then fetch the next chunk.
-        {
-            const int r = 8 * warp + (lane % 8), a = lane / 8;
-            const float fk = sm.eGl[r], fq = scale * sm.eG[r];
-#pragma unroll
-            for (int i = 0; i < 4; ++i) {
-                const int cc = 8 * (4 * i + a);
-                const IT *kh = reinterpret_cast<const IT *>(&cr.k[i]), *qh = reinterpret_cast<const IT *>(&cr.q[i]);
-                float kv[8], qv[8];
-#pragma unroll
-                for (int j = 0; j < 8; ++j) {
-                    kv[j] = TR::to_f(kh[j]) * fk;
-                    qv[j] = TR::to_f(qh[j]) * fq;
-                }
-                st_vec8<IT>(sm.KQ, kmaj16(r, cc, D), kv);
-                st_vec8<IT>(sm.KQ, kmaj16(C + r, cc, D), qv);
-            }
-            if (c0 + C < T) prefetch_chunk<IT>(cr, p, b, h, hk, c0 + C, t);
         }
         __syncthreads();
-        // ------------------------------------------ INV: T = (I + A)^-1
+        // -------------------------------- INV: T = (I + A)^-1 -> operand tile
         invert_unit_lower(sm, t);
         for (int e = t; e < C * C / 8; e += NT) {
-            const int r = e / 8, s0 = (e % 8) * 8;
+            const int r = e % C, s0 = (e / C) * 8;
             float v[8];
-#pragma unroll
-            for (int i = 0; i < 8; ++i) v[i] = sm.Tf[r * LDF + s0 + i];
+            const float4 x0 = *reinterpret_cast<const float4 *>(&sm.Tf[r * LDF + s0]);
+            const float4 x1 = *reinterpret_cast<const float4 *>(&sm.Tf[r * LDF + s0 + 4]);
+            v[0] = x0.x; v[1] = x0.y; v[2] = x0.z; v[3] = x0.w;
+            v[4] = x1.x; v[5] = x1.y; v[6] = x1.z; v[7] = x1.w;
             st_vec8<IT>(sm.T, kmaj16(r, s0, C), v);
         }
-        // ------------------------------------------ M2: [W | U] = T R
+        // -------------------------------- M2: [W | U] = T R
         issue_sync();
         if (sm.stop) break;
         if (t == 0) {
@@ -426,31 +451,47 @@ __global__ void __launch_bounds__(NT, 1) chunk_tc_kernel(kai_gdn_chunk_args p, i
         if (!mbar_wait(&sm.bar, phase, err)) sm.stop = 1;
         phase ^= 1;
         fence_after_sync();
-        // ------------------------------------------ E2: W -> smem
+        // -------------------------------- E2: W -> tile; K', Qg -> R (free now); prefetch next
         {
             const int r = 16 * q + lane;
-            for (int cb = hf * 64; cb < hf * 64 + 64; cb += 16) {
-                float v[16];
-                tmem_ld16(taddr(TW, 32 * q, cb), v);
-                tmem_wait_ld();
-                if (lane < 16) {
-                    float a[8], c[8];
+            float w[64];
 #pragma unroll
-                    for (int i = 0; i < 8; ++i) {
-                        a[i] = v[i];
-                        c[i] = v[8 + i];
-                    }
-                    st_vec8<IT>(sm.W, kmaj16(r, cb, D), a);
-                    st_vec8<IT>(sm.W, kmaj16(r, cb + 8, D), c);
+            for (int u = 0; u < 4; ++u)
+                tmem_ld16(taddr(TW, 32 * q, hf * 64 + 16 * u), *reinterpret_cast<float(*)[16]>(&w[16 * u]));
+            tmem_wait_ld();
+            if (lane < 16) {
+#pragma unroll
+                for (int u = 0; u < 8; ++u) {
+                    float a[8];
+#pragma unroll
+                    for (int x = 0; x < 8; ++x) a[x] = w[8 * u + x];
+                    st_vec8<IT>(sm.W, kmaj16(r, hf * 64 + 8 * u, D), a);
                 }
             }
+            // K' = K e^(G_63 - G) and Qg = scale Q e^G, K-major 64 x 128 each, in R
+            unsigned char *Kp = sm.R, *Qg = sm.R + C * D * 2;
+            const float fk = sm.eGl[lr], fq = scale * sm.eG[lr];
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                const int cc = 8 * (4 * i + la);
+                const IT *kh = reinterpret_cast<const IT *>(&cr.k[i]), *qh = reinterpret_cast<const IT *>(&cr.q[i]);
+                float kv[8], qv[8];
+#pragma unroll
+                for (int jj = 0; jj < 8; ++jj) {
+                    kv[jj] = TR::to_f(kh[jj]) * fk;
+                    qv[jj] = TR::to_f(qh[jj]) * fq;
+                }
+                st_vec8<IT>(Kp, kmaj16(lr, cc, D), kv);
+                st_vec8<IT>(Qg, kmaj16(lr, cc, D), qv);
+            }
+            if (c0 + C < T) prefetch_chunk<IT>(cr, p, b, h, hk, c0 + C, t);
         }
-        // ------------------------------------------ M3: W S, Qg S
+        // -------------------------------- M3: W S, Qg S   (overlap: S *= gamma)
         issue_sync();
         if (sm.stop) break;
         if (t == 0) {
             const uint32_t id = idesc(64, 128, TR::fmt, false, true);
-            const unsigned char *Qg = sm.KQ + C * D * 2;  // rows 64..127 of the K-major tile
+            const unsigned char *Qg = sm.R + C * D * 2;
             for (int ks = 0; ks < D / 16; ++ks) {
                 const uint64_t bd = desc_mnmaj16(sm.S, D, ks);
                 mma_f16(TD3, desc_kmaj16(sm.W, D, ks), bd, id, ks > 0);
@@ -458,40 +499,48 @@ __global__ void __launch_bounds__(NT, 1) chunk_tc_kernel(kai_gdn_chunk_args p, i
             }
             commit(&sm.bar);
         }
+        {
+            // S columns are not touched by M3 (it reads the copy in sm.S).
+            const float gamma = sm.eG[C - 1];
+            float s[64];
+#pragma unroll
+            for (int u = 0; u < 4; ++u)
+                tmem_ld16(taddr(TS, 32 * q, hf * 64 + 16 * u), *reinterpret_cast<float(*)[16]>(&s[16 * u]));
+            tmem_wait_ld();
+#pragma unroll
+            for (int x = 0; x < 64; ++x) s[x] *= gamma;
+#pragma unroll
+            for (int u = 0; u < 4; ++u)
+                tmem_st16(taddr(TS, 32 * q, hf * 64 + 16 * u), *reinterpret_cast<float(*)[16]>(&s[16 * u]));
+            tmem_wait_st();
+        }
         if (!mbar_wait(&sm.bar, phase, err)) sm.stop = 1;
         phase ^= 1;
         fence_after_sync();
-        // ------------------------------------------ E3: V' = U - W S; S *= gamma
+        // -------------------------------- E3: V' = U - W S -> tile
         {
             const int r = 16 * q + lane;
-            for (int cb = hf * 64; cb < hf * 64 + 64; cb += 16) {
-                float ws[16], u[16];
-                tmem_ld16(taddr(TD3, 32 * q, cb), ws);
-                tmem_ld16(taddr(TU, 32 * q, cb), u);
+#pragma unroll
+            for (int half = 0; half < 2; ++half) {
+                const int cb = hf * 64 + 32 * half;
+                float ws[32], u[32];
+                tmem_ld16(taddr(TD3, 32 * q, cb), *reinterpret_cast<float(*)[16]>(&ws[0]));
+                tmem_ld16(taddr(TD3, 32 * q, cb + 16), *reinterpret_cast<float(*)[16]>(&ws[16]));
+                tmem_ld16(taddr(TU, 32 * q, cb), *reinterpret_cast<float(*)[16]>(&u[0]));
+                tmem_ld16(taddr(TU, 32 * q, cb + 16), *reinterpret_cast<float(*)[16]>(&u[16]));
                 tmem_wait_ld();
                 if (lane < 16) {
-                    float a[8], c[8];
 #pragma unroll
-                    for (int i = 0; i < 8; ++i) {
-                        a[i] = u[i] - ws[i];
-                        c[i] = u[8 + i] - ws[8 + i];
+                    for (int x = 0; x < 4; ++x) {
+                        float a[8];
+#pragma unroll
+                        for (int y = 0; y < 8; ++y) a[y] = u[8 * x + y] - ws[8 * x + y];
+                        st_vec8<IT>(sm.Vp, mnmaj16(r, cb + 8 * x, D), a);
                     }
-                    st_vec8<IT>(sm.Vp, mnmaj16(r, cb, D), a);
-                    st_vec8<IT>(sm.Vp, mnmaj16(r, cb + 8, D), c);
                 }
             }
-            const float gamma = sm.eG[C - 1];
-            for (int cb = hf * 64; cb < hf * 64 + 64; cb += 16) {
-                float s[16];
-                tmem_ld16(taddr(TS, 32 * q, cb), s);
-                tmem_wait_ld();
-#pragma unroll
-                for (int i = 0; i < 16; ++i) s[i] *= gamma;
-                tmem_st16(taddr(TS, 32 * q, cb), s);
-            }
-            tmem_wait_st();
         }
-        // ------------------------------------------ M4: O += P V'; S += K'^T V'
+        // -------------------------------- M4: O += P V'; S += K'^T V'  (overlap: next gates)
         issue_sync();
         if (sm.stop) break;
         if (t == 0) {
@@ -500,41 +549,46 @@ __global__ void __launch_bounds__(NT, 1) chunk_tc_kernel(kai_gdn_chunk_args p, i
             for (int ks = 0; ks < C / 16; ++ks) {
                 const uint64_t vd = desc_mnmaj16(sm.Vp, D, ks);
                 mma_f16(TO, desc_kmaj16(sm.P, C, ks), vd, id_o, true);
-                mma_f16(TS, desc_mnmaj16(sm.KQ, D, ks), vd, id_s, true);
+                mma_f16(TS, desc_mnmaj16(sm.R, D, ks), vd, id_s, true);
             }
             commit(&sm.bar);
         }
+        const bool more = c0 + C < T;
+        if (more) chunk_gates(sm, cr, t);  // G, beta, e^G of the next chunk (M4 does not read them)
         if (!mbar_wait(&sm.bar, phase, err)) sm.stop = 1;
         phase ^= 1;
         fence_after_sync();
-        // ------------------------------------------ E4: O out; S -> smem copy
+        // -------------------------------- E4: O out; S -> operand copy
         {
             const int r = 16 * q + lane;
             const long long tok = c0 + r;
-            for (int cb = hf * 64; cb < hf * 64 + 64; cb += 16) {
-                float o[16];
-                tmem_ld16(taddr(TO, 32 * q, cb), o);
-                tmem_wait_ld();
-                if (lane < 16 && tok < T) st16_out(p.o, ((size_t)(b * T + tok) * Hv + h) * D + cb, p.out_dtype, o);
+            float o[64];
+#pragma unroll
+            for (int u = 0; u < 4; ++u)
+                tmem_ld16(taddr(TO, 32 * q, hf * 64 + 16 * u), *reinterpret_cast<float(*)[16]>(&o[16 * u]));
+            tmem_wait_ld();
+            if (lane < 16 && tok < T) {
+#pragma unroll
+                for (int u = 0; u < 4; ++u)
+                    st16_out(p.o, ((size_t)(b * T + tok) * Hv + h) * D + hf * 64 + 16 * u, p.out_dtype,
+                             *reinterpret_cast<float(*)[16]>(&o[16 * u]));
             }
             const int d = 32 * q + lane;
-            for (int cb = hf * 64; cb < hf * 64 + 64; cb += 16) {
-                float s[16];
-                tmem_ld16(taddr(TS, 32 * q, cb), s);
-                tmem_wait_ld();
-                float a[8], c[8];
+            float s[64];
 #pragma unroll
-                for (int i = 0; i < 8; ++i) {
-                    a[i] = s[i];
-                    c[i] = s[8 + i];
-                }
-                st_vec8<IT>(sm.S, mnmaj16(d, cb, D), a);
-                st_vec8<IT>(sm.S, mnmaj16(d, cb + 8, D), c);
+            for (int u = 0; u < 4; ++u)
+                tmem_ld16(taddr(TS, 32 * q, hf * 64 + 16 * u), *reinterpret_cast<float(*)[16]>(&s[16 * u]));
+            tmem_wait_ld();
+#pragma unroll
+            for (int u = 0; u < 8; ++u) {
+                float a[8];
+#pragma unroll
+                for (int x = 0; x < 8; ++x) a[x] = s[8 * u + x];
+                st_vec8<IT>(sm.S, mnmaj16(d, hf * 64 + 8 * u, D), a);
             }
         }
         fence_before_sync();
         __syncthreads();
-        if (sm.stop) break;
     }
 
     // ---- final state out (fp32 from TMEM)

@@ -18,7 +18,7 @@ namespace {
 
 __global__ void __launch_bounds__(128, 1)
     gemm_kernel(const float *A, const float *B, float *D, int M, int N, int K, int a_mn, int b_mn, int tf32,
-                int *err) {
+                int lane16, int *err) {
     extern __shared__ __align__(1024) unsigned char smem[];
     unsigned char *As = smem;                  // up to 128 x 128 x 4 bytes
     unsigned char *Bs = smem + 64 * 1024;      // up to 256 x 128 x 4 bytes (128 KB)
@@ -54,7 +54,9 @@ __global__ void __launch_bounds__(128, 1)
     fence_before_sync();
     __syncthreads();
     fence_after_sync();
-    const uint32_t tbase = tmem_slot;
+    // lane16: an M=64 accumulator placed in the upper half of each 32-lane
+    // quadrant (TMEM lane offset 16), the second of two interleaved tiles.
+    const uint32_t tbase = tmem_slot + (lane16 ? (16u << 16) : 0u);
 
     if (t == 0) {
         if (!tf32) {
@@ -75,11 +77,11 @@ __global__ void __launch_bounds__(128, 1)
     fence_after_sync();
     if (ok) {
         // M=128: row = 32*warp + lane.  M=64: rows 16*warp + lane for lane < 16.
-        const int row = M == 128 ? 32 * warp + lane : 16 * warp + lane;
-        const bool live = M == 128 || lane < 16;
+        const int row = M == 128 ? 32 * warp + lane : 16 * warp + (lane16 ? lane - 16 : lane);
+        const bool live = M == 128 || (lane16 ? lane >= 16 : lane < 16);
         for (int c = 0; c < N; c += 16) {
             float v[16];
-            tmem_ld16(taddr(tbase, 32 * warp, c), v);
+            tmem_ld16(taddr(tmem_slot, 32 * warp, c), v);
             tmem_wait_ld();
             if (live)
                 for (int i = 0; i < 16; ++i) D[row * N + c + i] = v[i];
@@ -87,18 +89,19 @@ __global__ void __launch_bounds__(128, 1)
     }
     fence_before_sync();
     __syncthreads();
-    if (warp == 0) tmem_dealloc(tbase, 256);
+    if (warp == 0) tmem_dealloc(tmem_slot, 256);
 }
 
 }  // namespace
 
 extern "C" __attribute__((visibility("default"))) int umma_selftest_gemm(const float *A, const float *B, float *D,
                                                                           int M, int N, int K, int a_mn, int b_mn,
-                                                                          int tf32, int *err) {
+                                                                          int tf32, int lane16, int *err) {
     if ((M != 64 && M != 128) || N % 16 || N < 16 || N > 256 || K % 16 || K > 128) return 1;
+    if (lane16 && M != 64) return 1;
     const int smem = 64 * 1024 + 128 * 1024;
     cudaFuncSetAttribute(gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-    gemm_kernel<<<1, 128, smem>>>(A, B, D, M, N, K, a_mn, b_mn, tf32, err);
+    gemm_kernel<<<1, 128, smem>>>(A, B, D, M, N, K, a_mn, b_mn, tf32, lane16, err);
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return 2;
     e = cudaDeviceSynchronize();

@@ -24,7 +24,7 @@ pytestmark = pytest.mark.gpu
 def selftest():
     lib = C.CDLL(str(build.SELFTEST_LIB))
     lib.umma_selftest_gemm.restype = C.c_int
-    lib.umma_selftest_gemm.argtypes = [C.c_void_p] * 3 + [C.c_int] * 6 + [C.c_void_p]
+    lib.umma_selftest_gemm.argtypes = [C.c_void_p] * 3 + [C.c_int] * 7 + [C.c_void_p]
     return lib
 
 
@@ -44,7 +44,7 @@ def test_bf16_layouts(cuda, selftest, M, N, K, a_mn, b_mn):
     Ad, Bd = cuda.from_numpy(A).cuda(), cuda.from_numpy(B).cuda()
     D = cuda.full((M, N), float("nan"), device="cuda")
     err = cuda.zeros(1, dtype=cuda.int32, device="cuda")
-    rc = selftest.umma_selftest_gemm(Ad.data_ptr(), Bd.data_ptr(), D.data_ptr(), M, N, K, a_mn, b_mn, 0,
+    rc = selftest.umma_selftest_gemm(Ad.data_ptr(), Bd.data_ptr(), D.data_ptr(), M, N, K, a_mn, b_mn, 0, 0,
                                      err.data_ptr())
     assert rc == 0 and err.item() == 0
     want = _bf16(A).astype(np.float64) @ _bf16(B).astype(np.float64)
@@ -59,7 +59,25 @@ def test_tf32_kmajor(cuda, selftest, M, N, K):
     Ad, Bd = cuda.from_numpy(A).cuda(), cuda.from_numpy(B).cuda()
     D = cuda.full((M, N), float("nan"), device="cuda")
     err = cuda.zeros(1, dtype=cuda.int32, device="cuda")
-    assert selftest.umma_selftest_gemm(Ad.data_ptr(), Bd.data_ptr(), D.data_ptr(), M, N, K, 0, 0, 1,
+    assert selftest.umma_selftest_gemm(Ad.data_ptr(), Bd.data_ptr(), D.data_ptr(), M, N, K, 0, 0, 1, 0,
                                        err.data_ptr()) == 0
     assert err.item() == 0
     assert rel_l2(D.cpu().numpy(), A.astype(np.float64) @ B.astype(np.float64)) < 3e-3
+
+
+@pytest.mark.parametrize("N,b_mn", [(128, 1), (64, 0)])
+def test_m64_upper_lane_half(cuda, selftest, N, b_mn):
+    """An M=64 accumulator at TMEM lane offset 16 (the second of two
+    interleaved half-quadrant tiles): rows 16w..16w+15 land in lanes
+    32w+16..32w+31."""
+    r = np.random.default_rng(N)
+    A = r.standard_normal((64, 64)).astype(np.float32)
+    B = r.standard_normal((64, N)).astype(np.float32)
+    Ad, Bd = cuda.from_numpy(A).cuda(), cuda.from_numpy(B).cuda()
+    D = cuda.full((64, N), float("nan"), device="cuda")
+    err = cuda.zeros(1, dtype=cuda.int32, device="cuda")
+    assert selftest.umma_selftest_gemm(Ad.data_ptr(), Bd.data_ptr(), D.data_ptr(), 64, N, 64, 0, b_mn, 0, 1,
+                                       err.data_ptr()) == 0
+    assert err.item() == 0
+    want = _bf16(A).astype(np.float64) @ _bf16(B).astype(np.float64)
+    assert rel_l2(D.cpu().numpy(), want) < 1e-5
