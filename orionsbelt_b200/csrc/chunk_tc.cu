@@ -8,32 +8,40 @@
 //   A  = beta_r (k_r.k_s) exp(G_r - G_s), s <  r        (from  [K;Q] K^T)
 //   P  = scale (q_r.k_s) exp(G_r - G_s), s <= r        (same MMA, rows 64..127)
 //   T  = (I + A)^-1                                     (CUDA cores, fp32)
-//   [W | U] = T [beta K exp(G) | beta V]                (one MMA, N = 256)
+//   W = T (beta K exp(G)),  U = T (beta V)              (two MMAs)
 //   V' = U - W S                                        (MMA W.S)
-//   O  = (scale Q exp(G)) S + P V'                      (MMA Qg.S, then P.V')
+//   O  = (scale Q exp(G)) S + P V'                      (MMAs Qg.S and P.V')
 //   S <- gamma S + (K exp(G_63 - G))^T V'               (MMA, M = 128)
 //
 // One CTA (256 threads) owns one (b, h) for the whole sequence; its fp32
-// state S [128 x 128] stays in TMEM columns 0..127 and a bf16 copy in shared
-// memory feeds the next chunk's MMAs.  Thread 0 issues every MMA; completion
-// is signalled with tcgen05.commit on one mbarrier, and every wait is bounded
-// (a timeout sets *err and the CTA leaves after freeing its TMEM).
+// state S [128 x 128] stays in TMEM and a 16-bit copy in shared memory feeds
+// the next chunk's MMAs.  The kernel is latency-bound (a chain of dependent
+// phases per chunk), so it is sized for TWO resident CTAs per SM, whose
+// phases interleave: 256 TMEM columns, ~105 KB of shared memory and at most
+// 128 registers per thread.  Thread 0 issues every MMA; completion is
+// signalled by tcgen05.commit on one mbarrier, and every wait is bounded (a
+// timeout sets *err and the CTA leaves after freeing its TMEM).
 //
-// TMEM columns (512, one CTA per SM):
-//   [  0,128) S        M=128 (lane = key index d)
-//   [128,192) [K;Q]K^T M=128 (lanes 0-63: K K^T rows, 64-127: Q K^T rows)
-//   [128,256) W S      M=64  (after [K;Q]K^T has been read)
-//   [256,384) W, later O (after W has been copied out), M=64
-//   [384,512) U        M=64
-// Operand tiles are bf16/fp16 in the no-swizzle core-matrix layouts of
-// umma.cuh.  Once [W | U] is computed the R tile is free and holds K' and Qg
-// (K-major 64 x 128 each); a K-major tile with 128 columns is also the
-// MN-major tile of its transpose, so K' serves directly as the A operand of
-// K'^T V'.
+// TMEM (256 columns).  M=64 accumulators put rows 16q..16q+15 in lanes
+// 32q..32q+15 ("lower half") or, at lane offset 16, in lanes 32q+16..32q+31
+// ("upper half"), so two of them share columns:
+//   [  0,128) S             M=128, lane = key index d
+//   [128,192) [K;Q] K^T     M=128 (lanes 0-63: K K^T, 64-127: Q K^T)
+//   [128,256) W | U         M=64, lower | upper half       (after [K;Q]K^T is read)
+//   [128,256) W S | O       M=64, lower | upper half       (after W, U are read)
+// A warp's 32x32b TMEM load then returns W S in lanes 0-15 and U (or O) in
+// lanes 16-31 of the same columns.
 //
-// Overlap: the S *= gamma pass runs while W S / Qg S execute, and the next
-// chunk's gates are scanned while P V' / K'^T V' execute; the next chunk's
-// q, k, v, g, beta are loaded into registers during the current chunk.
+// Shared memory, regions reused by lifetime within a chunk:
+//   S     16-bit state copy, MN-major                        always
+//   A     raw [K;Q] (K-major 128 x 128)       L  .. M1
+//         A, T = (I+A)^-1 fp32 (block-packed), then T tile   E1 .. M2
+//         K' and Qg (K-major 64 x 128 each)   E2 .. M4
+//   B     [beta K e^G | beta V] (MN-major 64 x 256)          L  .. M2
+//         W (K-major 64 x 128) | V' (MN-major 64 x 128)      E2 .. M4
+//   P     P tile (K-major 64 x 64)                           E1 .. M4
+// A K-major tile with 128 columns is also the MN-major tile of its transpose,
+// so K' serves directly as the A operand of K'^T V'.
 #include "gdn_internal.cuh"
 #include "umma.cuh"
 
@@ -43,7 +51,6 @@ namespace {
 using namespace umma;
 
 constexpr int C = 64, D = 128, NT = 256;
-constexpr int LDF = 68;  // fp32 row stride: 16-byte aligned rows, 8 rows span all banks
 
 template <typename IT> struct InTraits;
 template <> struct InTraits<__nv_bfloat16> {
@@ -57,17 +64,37 @@ template <> struct InTraits<__half> {
     static __device__ __forceinline__ __half from_f(float x) { return __float2half_rn(x); }
 };
 
+// Block-packed lower triangle of a 64 x 64 fp32 matrix: the ten 16 x 16
+// blocks (bi >= bj) at id = bi(bi+1)/2 + bj, rows padded to 20 floats (16-byte
+// aligned rows; eight consecutive rows cover all 32 banks).
+constexpr int BLD = 20, BSZ = 16 * BLD;
+__host__ __device__ constexpr int blk(int bi, int bj) { return (bi * (bi + 1) / 2 + bj) * BSZ; }
+
 struct __align__(128) TcSmem {
-    unsigned char KQ[2 * C * D * 2];   // [K;Q] K-major 128 x 128; later [K';Qg]
-    unsigned char R[C * 2 * D * 2];    // [beta K e^G | beta V] MN-major 64 x 256
-    unsigned char S[D * D * 2];        // state copy, MN-major (k = d, n = value col)
-    unsigned char W[C * D * 2];        // W, K-major 64 x 128
-    unsigned char Vp[C * D * 2];       // V', MN-major (k = row, n = value col)
-    unsigned char P[C * C * 2];        // P, K-major 64 x 64
-    unsigned char T[C * C * 2];        // T, K-major 64 x 64
-    float Af[C * LDF];                 // A (strictly lower), fp32
-    float Tf[C * LDF];                 // T = (I + A)^-1, fp32
-    float Mscr[3 * 16 * 17];           // block products of the inverse
+    unsigned char S[D * D * 2];
+    union {
+        unsigned char KQ[2 * C * D * 2];
+        struct {
+            union {
+                float Af[10 * BSZ];
+                unsigned char T[C * C * 2];
+            };
+            float Tf[10 * BSZ];
+            float Mscr[3 * 16 * 17];
+        } inv;
+        struct {
+            unsigned char Kp[C * D * 2];
+            unsigned char Qg[C * D * 2];
+        } kq;
+    } a;
+    union {
+        unsigned char R[C * 2 * D * 2];
+        struct {
+            unsigned char W[C * D * 2];
+            unsigned char Vp[C * D * 2];
+        } wv;
+    } b;
+    unsigned char P[C * C * 2];
     float G[C], eG[C], eGl[C], beta[C];
     uint64_t bar;
     uint32_t tmem;
@@ -171,31 +198,24 @@ __device__ __forceinline__ void st16_out(void *o, size_t idx, int dt, const floa
     dst[1] = u[1];
 }
 
-// T = (I + A)^-1 for strictly lower A (64 x 64, fp32, row stride LDF), by
+// T = (I + A)^-1 for strictly lower A (64 x 64, fp32, block-packed), by
 // 16 x 16 blocks: the four diagonal blocks by right-looking substitution (a
 // dependency chain of 16 steps per column), then T_ij = -T_ii sum_k A_ik T_kj
-// for the block diagonals i - j = 1, 2, 3.  Every thread computes its outputs
-// with interleaved accumulators so the FMA chains overlap.
+// for the block diagonals i - j = 1, 2, 3 with interleaved accumulators.
 __device__ void invert_unit_lower(TcSmem &sm, int t) {
-    float *A = sm.Af, *T = sm.Tf, *M = sm.Mscr;
+    const float *A = sm.a.inv.Af;
+    float *T = sm.a.inv.Tf, *M = sm.a.inv.Mscr;
     if (t < 64) {
-        const int o = 16 * (t / 16), j = t % 16;
+        const int bb = t / 16, j = t % 16, o = blk(bb, bb);
         float acc[16];
 #pragma unroll
         for (int r = 0; r < 16; ++r) acc[r] = 0.f;
 #pragma unroll
         for (int s = 0; s < 16; ++s) {
             const float xs = s < j ? 0.f : (s == j ? 1.f : -acc[s]);
-            T[(o + s) * LDF + o + j] = xs;
+            T[o + s * BLD + j] = xs;
 #pragma unroll
-            for (int r = s + 1; r < 16; ++r) acc[r] = fmaf(A[(o + r) * LDF + o + s], xs, acc[r]);
-        }
-    } else {
-        // zero the six blocks above the diagonal: (0,1) (0,2) (0,3) (1,2) (1,3) (2,3)
-        for (int e = t - 64; e < 6 * 64; e += NT - 64) {
-            const int bb = e / 64, w = e % 64, i = w / 4, j4 = (w % 4) * 4;
-            const int bi = bb < 3 ? 0 : (bb < 5 ? 1 : 2), bj = bb < 3 ? bb + 1 : (bb < 5 ? bb - 1 : 3);
-            *reinterpret_cast<float4 *>(&T[(16 * bi + i) * LDF + 16 * bj + j4]) = make_float4(0.f, 0.f, 0.f, 0.f);
+            for (int r = s + 1; r < 16; ++r) acc[r] = fmaf(A[o + r * BLD + s], xs, acc[r]);
         }
     }
     __syncthreads();
@@ -205,9 +225,9 @@ __device__ void invert_unit_lower(TcSmem &sm, int t) {
         float m0 = 0.f, m1 = 0.f, m2 = 0.f;
 #pragma unroll
         for (int k = 0; k < 16; ++k) {
-            m0 = fmaf(A[(16 + i) * LDF + k], T[k * LDF + j], m0);
-            m1 = fmaf(A[(32 + i) * LDF + 16 + k], T[(16 + k) * LDF + 16 + j], m1);
-            m2 = fmaf(A[(48 + i) * LDF + 32 + k], T[(32 + k) * LDF + 32 + j], m2);
+            m0 = fmaf(A[blk(1, 0) + i * BLD + k], T[blk(0, 0) + k * BLD + j], m0);
+            m1 = fmaf(A[blk(2, 1) + i * BLD + k], T[blk(1, 1) + k * BLD + j], m1);
+            m2 = fmaf(A[blk(3, 2) + i * BLD + k], T[blk(2, 2) + k * BLD + j], m2);
         }
         M[0 * 272 + i * 17 + j] = m0;
         M[1 * 272 + i * 17 + j] = m1;
@@ -218,13 +238,13 @@ __device__ void invert_unit_lower(TcSmem &sm, int t) {
         float t0 = 0.f, t1 = 0.f, t2 = 0.f;
 #pragma unroll
         for (int k = 0; k < 16; ++k) {
-            t0 = fmaf(T[(16 + i) * LDF + 16 + k], M[0 * 272 + k * 17 + j], t0);
-            t1 = fmaf(T[(32 + i) * LDF + 32 + k], M[1 * 272 + k * 17 + j], t1);
-            t2 = fmaf(T[(48 + i) * LDF + 48 + k], M[2 * 272 + k * 17 + j], t2);
+            t0 = fmaf(T[blk(1, 1) + i * BLD + k], M[0 * 272 + k * 17 + j], t0);
+            t1 = fmaf(T[blk(2, 2) + i * BLD + k], M[1 * 272 + k * 17 + j], t1);
+            t2 = fmaf(T[blk(3, 3) + i * BLD + k], M[2 * 272 + k * 17 + j], t2);
         }
-        T[(16 + i) * LDF + j] = -t0;
-        T[(32 + i) * LDF + 16 + j] = -t1;
-        T[(48 + i) * LDF + 32 + j] = -t2;
+        T[blk(1, 0) + i * BLD + j] = -t0;
+        T[blk(2, 1) + i * BLD + j] = -t1;
+        T[blk(3, 2) + i * BLD + j] = -t2;
     }
     __syncthreads();
     // level 2: M_b = A_{b+2,b} T_bb + A_{b+2,b+1} T_{b+1,b}, T_{b+2,b} = -T_{b+2,b+2} M_b  (b = 0, 1)
@@ -232,10 +252,10 @@ __device__ void invert_unit_lower(TcSmem &sm, int t) {
         float a0 = 0.f, a1 = 0.f, c0 = 0.f, c1 = 0.f;
 #pragma unroll
         for (int k = 0; k < 16; ++k) {
-            a0 = fmaf(A[(32 + i) * LDF + k], T[k * LDF + j], a0);
-            a1 = fmaf(A[(32 + i) * LDF + 16 + k], T[(16 + k) * LDF + j], a1);
-            c0 = fmaf(A[(48 + i) * LDF + 16 + k], T[(16 + k) * LDF + 16 + j], c0);
-            c1 = fmaf(A[(48 + i) * LDF + 32 + k], T[(32 + k) * LDF + 16 + j], c1);
+            a0 = fmaf(A[blk(2, 0) + i * BLD + k], T[blk(0, 0) + k * BLD + j], a0);
+            a1 = fmaf(A[blk(2, 1) + i * BLD + k], T[blk(1, 0) + k * BLD + j], a1);
+            c0 = fmaf(A[blk(3, 1) + i * BLD + k], T[blk(1, 1) + k * BLD + j], c0);
+            c1 = fmaf(A[blk(3, 2) + i * BLD + k], T[blk(2, 1) + k * BLD + j], c1);
         }
         M[0 * 272 + i * 17 + j] = a0 + a1;
         M[1 * 272 + i * 17 + j] = c0 + c1;
@@ -245,11 +265,11 @@ __device__ void invert_unit_lower(TcSmem &sm, int t) {
         float t0 = 0.f, t1 = 0.f;
 #pragma unroll
         for (int k = 0; k < 16; ++k) {
-            t0 = fmaf(T[(32 + i) * LDF + 32 + k], M[0 * 272 + k * 17 + j], t0);
-            t1 = fmaf(T[(48 + i) * LDF + 48 + k], M[1 * 272 + k * 17 + j], t1);
+            t0 = fmaf(T[blk(2, 2) + i * BLD + k], M[0 * 272 + k * 17 + j], t0);
+            t1 = fmaf(T[blk(3, 3) + i * BLD + k], M[1 * 272 + k * 17 + j], t1);
         }
-        T[(32 + i) * LDF + j] = -t0;
-        T[(48 + i) * LDF + 16 + j] = -t1;
+        T[blk(2, 0) + i * BLD + j] = -t0;
+        T[blk(3, 1) + i * BLD + j] = -t1;
     }
     __syncthreads();
     // level 3: M = A_30 T_00 + A_31 T_10 + A_32 T_20, T_30 = -T_33 M
@@ -257,9 +277,9 @@ __device__ void invert_unit_lower(TcSmem &sm, int t) {
         float a0 = 0.f, a1 = 0.f, a2 = 0.f;
 #pragma unroll
         for (int k = 0; k < 16; ++k) {
-            a0 = fmaf(A[(48 + i) * LDF + k], T[k * LDF + j], a0);
-            a1 = fmaf(A[(48 + i) * LDF + 16 + k], T[(16 + k) * LDF + j], a1);
-            a2 = fmaf(A[(48 + i) * LDF + 32 + k], T[(32 + k) * LDF + j], a2);
+            a0 = fmaf(A[blk(3, 0) + i * BLD + k], T[blk(0, 0) + k * BLD + j], a0);
+            a1 = fmaf(A[blk(3, 1) + i * BLD + k], T[blk(1, 0) + k * BLD + j], a1);
+            a2 = fmaf(A[blk(3, 2) + i * BLD + k], T[blk(2, 0) + k * BLD + j], a2);
         }
         M[i * 17 + j] = a0 + a1 + a2;
     }
@@ -268,10 +288,10 @@ __device__ void invert_unit_lower(TcSmem &sm, int t) {
         float t0 = 0.f, t1 = 0.f;
 #pragma unroll
         for (int k = 0; k < 16; k += 2) {
-            t0 = fmaf(T[(48 + i) * LDF + 48 + k], M[k * 17 + j], t0);
-            t1 = fmaf(T[(48 + i) * LDF + 48 + k + 1], M[(k + 1) * 17 + j], t1);
+            t0 = fmaf(T[blk(3, 3) + i * BLD + k], M[k * 17 + j], t0);
+            t1 = fmaf(T[blk(3, 3) + i * BLD + k + 1], M[(k + 1) * 17 + j], t1);
         }
-        T[(48 + i) * LDF + j] = -(t0 + t1);
+        T[blk(3, 0) + i * BLD + j] = -(t0 + t1);
     }
     __syncthreads();
 }
@@ -309,8 +329,8 @@ __device__ __forceinline__ void chunk_gates(TcSmem &sm, const ChunkRegs &cr, int
 }
 
 template <typename IT>
-__global__ void __launch_bounds__(NT, 1) chunk_tc_kernel(kai_gdn_chunk_args p, int *err) {
-    extern __shared__ __align__(1024) unsigned char smem_raw[];
+__global__ void __launch_bounds__(NT, 2) chunk_tc_kernel(kai_gdn_chunk_args p, int *err) {
+    extern __shared__ __align__(128) unsigned char smem_raw[];
     TcSmem &sm = *reinterpret_cast<TcSmem *>(smem_raw);
     using TR = InTraits<IT>;
 
@@ -325,16 +345,16 @@ __global__ void __launch_bounds__(NT, 1) chunk_tc_kernel(kai_gdn_chunk_args p, i
         mbar_init(&sm.bar, 1);
         sm.stop = 0;
     }
-    if (warp == 0) tmem_alloc(&sm.tmem, 512);
+    if (warp == 0) tmem_alloc(&sm.tmem, 256);
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     fence_before_sync();
     __syncthreads();
     fence_after_sync();
     const uint32_t tm = sm.tmem;
-    const uint32_t TS = tm, TD1 = tm + 128, TD3 = tm + 128, TW = tm + 256, TO = tm + 256, TU = tm + 384;
+    const uint32_t TS = tm, TD1 = tm + 128, TLO = tm + 128, THI = tm + 128 + (16u << 16);
     uint32_t phase = 0;
 
-    // ---- initial state: fp32 into TMEM columns 0..127, a copy into sm.S
+    // ---- initial state: fp32 into TMEM columns 0..127, a 16-bit copy into sm.S
     {
         const int d = 32 * q + lane;
         const size_t sb = (size_t)unit * D * D + (size_t)d * D;
@@ -367,8 +387,8 @@ __global__ void __launch_bounds__(NT, 1) chunk_tc_kernel(kai_gdn_chunk_args p, i
 #pragma unroll
             for (int i = 0; i < 4; ++i) {
                 const int cc = 8 * (4 * i + la);
-                *reinterpret_cast<uint4 *>(sm.KQ + kmaj16(lr, cc, D)) = cr.k[i];
-                *reinterpret_cast<uint4 *>(sm.KQ + kmaj16(C + lr, cc, D)) = cr.q[i];
+                *reinterpret_cast<uint4 *>(sm.a.KQ + kmaj16(lr, cc, D)) = cr.k[i];
+                *reinterpret_cast<uint4 *>(sm.a.KQ + kmaj16(C + lr, cc, D)) = cr.q[i];
                 const IT *kh = reinterpret_cast<const IT *>(&cr.k[i]), *vh = reinterpret_cast<const IT *>(&cr.v[i]);
                 float kv[8], vv[8];
 #pragma unroll
@@ -376,8 +396,8 @@ __global__ void __launch_bounds__(NT, 1) chunk_tc_kernel(kai_gdn_chunk_args p, i
                     kv[jj] = TR::to_f(kh[jj]) * bk;
                     vv[jj] = TR::to_f(vh[jj]) * bv;
                 }
-                st_vec8<IT>(sm.R, mnmaj16(lr, cc, 2 * D), kv);
-                st_vec8<IT>(sm.R, mnmaj16(lr, D + cc, 2 * D), vv);
+                st_vec8<IT>(sm.b.R, mnmaj16(lr, cc, 2 * D), kv);
+                st_vec8<IT>(sm.b.R, mnmaj16(lr, D + cc, 2 * D), vv);
             }
         }
         // -------------------------------- M1: [K;Q] K^T
@@ -386,31 +406,39 @@ __global__ void __launch_bounds__(NT, 1) chunk_tc_kernel(kai_gdn_chunk_args p, i
         if (t == 0) {
             const uint32_t id = idesc(128, 64, TR::fmt, false, false);
             for (int ks = 0; ks < D / 16; ++ks)
-                mma_f16(TD1, desc_kmaj16(sm.KQ, D, ks), desc_kmaj16(sm.KQ, D, ks), id, ks > 0);
+                mma_f16(TD1, desc_kmaj16(sm.a.KQ, D, ks), desc_kmaj16(sm.a.KQ, D, ks), id, ks > 0);
             commit(&sm.bar);
         }
         if (!mbar_wait(&sm.bar, phase, err)) sm.stop = 1;
         phase ^= 1;
         fence_after_sync();
-        // -------------------------------- E1: A (fp32) and P (operand tile)
+        // -------------------------------- E1: A (fp32, packed) and P (operand tile)
         {
             const int i = 32 * q + lane;  // row of [K;Q]K^T
-            float v[32];
-            tmem_ld16(taddr(TD1, 32 * q, hf * 32), *reinterpret_cast<float(*)[16]>(&v[0]));
-            tmem_ld16(taddr(TD1, 32 * q, hf * 32 + 16), *reinterpret_cast<float(*)[16]>(&v[16]));
-            tmem_wait_ld();
             const int cb = hf * 32;
+            float v[32];
+            tmem_ld16(taddr(TD1, 32 * q, cb), *reinterpret_cast<float(*)[16]>(&v[0]));
+            tmem_ld16(taddr(TD1, 32 * q, cb + 16), *reinterpret_cast<float(*)[16]>(&v[16]));
+            tmem_wait_ld();
             if (i < C) {
                 const int r = i;
                 const float gr = sm.G[r], br = sm.beta[r];
 #pragma unroll
-                for (int jj = 0; jj < 32; jj += 4) {
-                    float4 f;
-                    f.x = cb + jj + 0 < r ? br * v[jj + 0] * __expf(gr - sm.G[cb + jj + 0]) : 0.f;
-                    f.y = cb + jj + 1 < r ? br * v[jj + 1] * __expf(gr - sm.G[cb + jj + 1]) : 0.f;
-                    f.z = cb + jj + 2 < r ? br * v[jj + 2] * __expf(gr - sm.G[cb + jj + 2]) : 0.f;
-                    f.w = cb + jj + 3 < r ? br * v[jj + 3] * __expf(gr - sm.G[cb + jj + 3]) : 0.f;
-                    *reinterpret_cast<float4 *>(&sm.Af[r * LDF + cb + jj]) = f;
+                for (int half = 0; half < 2; ++half) {
+                    const int s0 = cb + 16 * half;
+                    if (s0 / 16 <= r / 16) {
+                        float *dst = sm.a.inv.Af + blk(r / 16, s0 / 16) + (r % 16) * BLD;
+#pragma unroll
+                        for (int jj = 0; jj < 16; jj += 4) {
+                            float4 f;
+                            const int s = s0 + jj;
+                            f.x = s + 0 < r ? br * v[16 * half + jj + 0] * __expf(gr - sm.G[s + 0]) : 0.f;
+                            f.y = s + 1 < r ? br * v[16 * half + jj + 1] * __expf(gr - sm.G[s + 1]) : 0.f;
+                            f.z = s + 2 < r ? br * v[16 * half + jj + 2] * __expf(gr - sm.G[s + 2]) : 0.f;
+                            f.w = s + 3 < r ? br * v[16 * half + jj + 3] * __expf(gr - sm.G[s + 3]) : 0.f;
+                            *reinterpret_cast<float4 *>(dst + jj) = f;
+                        }
+                    }
                 }
             } else {
                 const int r = i - C;
@@ -428,48 +456,62 @@ __global__ void __launch_bounds__(NT, 1) chunk_tc_kernel(kai_gdn_chunk_args p, i
             }
         }
         __syncthreads();
-        // -------------------------------- INV: T = (I + A)^-1 -> operand tile
+        // -------------------------------- INV: T = (I + A)^-1 -> operand tile (over A)
         invert_unit_lower(sm, t);
         for (int e = t; e < C * C / 8; e += NT) {
             const int r = e % C, s0 = (e / C) * 8;
             float v[8];
-            const float4 x0 = *reinterpret_cast<const float4 *>(&sm.Tf[r * LDF + s0]);
-            const float4 x1 = *reinterpret_cast<const float4 *>(&sm.Tf[r * LDF + s0 + 4]);
-            v[0] = x0.x; v[1] = x0.y; v[2] = x0.z; v[3] = x0.w;
-            v[4] = x1.x; v[5] = x1.y; v[6] = x1.z; v[7] = x1.w;
-            st_vec8<IT>(sm.T, kmaj16(r, s0, C), v);
+            if (s0 / 16 <= r / 16) {
+                const float *src = sm.a.inv.Tf + blk(r / 16, s0 / 16) + (r % 16) * BLD + (s0 % 16);
+                const float4 x0 = *reinterpret_cast<const float4 *>(src);
+                const float4 x1 = *reinterpret_cast<const float4 *>(src + 4);
+                v[0] = x0.x; v[1] = x0.y; v[2] = x0.z; v[3] = x0.w;
+                v[4] = x1.x; v[5] = x1.y; v[6] = x1.z; v[7] = x1.w;
+            } else {
+#pragma unroll
+                for (int u = 0; u < 8; ++u) v[u] = 0.f;
+            }
+            st_vec8<IT>(sm.a.inv.T, kmaj16(r, s0, C), v);
         }
-        // -------------------------------- M2: [W | U] = T R
+        // -------------------------------- M2: W = T (beta K e^G) -> lower, U = T (beta V) -> upper
         issue_sync();
         if (sm.stop) break;
         if (t == 0) {
-            const uint32_t id = idesc(64, 256, TR::fmt, false, true);
-            for (int ks = 0; ks < C / 16; ++ks)
-                mma_f16(TW, desc_kmaj16(sm.T, C, ks), desc_mnmaj16(sm.R, 2 * D, ks), id, ks > 0);
+            const uint32_t id = idesc(64, 128, TR::fmt, false, true);
+            const uint32_t rb = smem_addr(sm.b.R), lbo = (2 * D / 8) * 128;
+            for (int ks = 0; ks < C / 16; ++ks) {
+                const uint64_t ad = desc_kmaj16(sm.a.inv.T, C, ks);
+                mma_f16(TLO, ad, smem_desc(rb + ks * 2 * lbo, lbo, 128), id, ks > 0);
+                mma_f16(THI, ad, smem_desc(rb + (D / 8) * 128 + ks * 2 * lbo, lbo, 128), id, ks > 0);
+            }
             commit(&sm.bar);
         }
         if (!mbar_wait(&sm.bar, phase, err)) sm.stop = 1;
         phase ^= 1;
         fence_after_sync();
-        // -------------------------------- E2: W -> tile; K', Qg -> R (free now); prefetch next
+        // -------------------------------- E2: W -> tile; K', Qg -> region A; prefetch next
         {
             const int r = 16 * q + lane;
-            float w[64];
 #pragma unroll
-            for (int u = 0; u < 4; ++u)
-                tmem_ld16(taddr(TW, 32 * q, hf * 64 + 16 * u), *reinterpret_cast<float(*)[16]>(&w[16 * u]));
-            tmem_wait_ld();
-            if (lane < 16) {
+            for (int half = 0; half < 2; ++half) {
+                const int cb = hf * 64 + 32 * half;
+                float w[32];
+                tmem_ld16(taddr(TLO, 32 * q, cb), *reinterpret_cast<float(*)[16]>(&w[0]));
+                tmem_ld16(taddr(TLO, 32 * q, cb + 16), *reinterpret_cast<float(*)[16]>(&w[16]));
+                tmem_wait_ld();
+                if (lane < 16) {
 #pragma unroll
-                for (int u = 0; u < 8; ++u) {
-                    float a[8];
+                    for (int u = 0; u < 4; ++u) {
+                        float a[8];
 #pragma unroll
-                    for (int x = 0; x < 8; ++x) a[x] = w[8 * u + x];
-                    st_vec8<IT>(sm.W, kmaj16(r, hf * 64 + 8 * u, D), a);
+                        for (int x = 0; x < 8; ++x) a[x] = w[8 * u + x];
+                        st_vec8<IT>(sm.b.wv.W, kmaj16(r, cb + 8 * u, D), a);
+                    }
                 }
             }
-            // K' = K e^(G_63 - G) and Qg = scale Q e^G, K-major 64 x 128 each, in R
-            unsigned char *Kp = sm.R, *Qg = sm.R + C * D * 2;
+        }
+        __syncthreads();  // the T tile (region A) is dead once every thread is past M2's wait
+        {
             const float fk = sm.eGl[lr], fq = scale * sm.eG[lr];
 #pragma unroll
             for (int i = 0; i < 4; ++i) {
@@ -481,75 +523,74 @@ __global__ void __launch_bounds__(NT, 1) chunk_tc_kernel(kai_gdn_chunk_args p, i
                     kv[jj] = TR::to_f(kh[jj]) * fk;
                     qv[jj] = TR::to_f(qh[jj]) * fq;
                 }
-                st_vec8<IT>(Kp, kmaj16(lr, cc, D), kv);
-                st_vec8<IT>(Qg, kmaj16(lr, cc, D), qv);
+                st_vec8<IT>(sm.a.kq.Kp, kmaj16(lr, cc, D), kv);
+                st_vec8<IT>(sm.a.kq.Qg, kmaj16(lr, cc, D), qv);
             }
             if (c0 + C < T) prefetch_chunk<IT>(cr, p, b, h, hk, c0 + C, t);
         }
-        // -------------------------------- M3: W S, Qg S   (overlap: S *= gamma)
+        // -------------------------------- M3: W S -> lower   (overlap: S *= gamma)
         issue_sync();
         if (sm.stop) break;
         if (t == 0) {
             const uint32_t id = idesc(64, 128, TR::fmt, false, true);
-            const unsigned char *Qg = sm.R + C * D * 2;
-            for (int ks = 0; ks < D / 16; ++ks) {
-                const uint64_t bd = desc_mnmaj16(sm.S, D, ks);
-                mma_f16(TD3, desc_kmaj16(sm.W, D, ks), bd, id, ks > 0);
-                mma_f16(TO, desc_kmaj16(Qg, D, ks), bd, id, ks > 0);
-            }
+            for (int ks = 0; ks < D / 16; ++ks)
+                mma_f16(TLO, desc_kmaj16(sm.b.wv.W, D, ks), desc_mnmaj16(sm.S, D, ks), id, ks > 0);
             commit(&sm.bar);
         }
         {
-            // S columns are not touched by M3 (it reads the copy in sm.S).
+            // TMEM columns 0..127 are not touched by M3 (it reads the copy in sm.S).
             const float gamma = sm.eG[C - 1];
-            float s[64];
 #pragma unroll
-            for (int u = 0; u < 4; ++u)
-                tmem_ld16(taddr(TS, 32 * q, hf * 64 + 16 * u), *reinterpret_cast<float(*)[16]>(&s[16 * u]));
-            tmem_wait_ld();
+            for (int half = 0; half < 2; ++half) {
+                const int cb = hf * 64 + 32 * half;
+                float s[32];
+                tmem_ld16(taddr(TS, 32 * q, cb), *reinterpret_cast<float(*)[16]>(&s[0]));
+                tmem_ld16(taddr(TS, 32 * q, cb + 16), *reinterpret_cast<float(*)[16]>(&s[16]));
+                tmem_wait_ld();
 #pragma unroll
-            for (int x = 0; x < 64; ++x) s[x] *= gamma;
-#pragma unroll
-            for (int u = 0; u < 4; ++u)
-                tmem_st16(taddr(TS, 32 * q, hf * 64 + 16 * u), *reinterpret_cast<float(*)[16]>(&s[16 * u]));
+                for (int x = 0; x < 32; ++x) s[x] *= gamma;
+                tmem_st16(taddr(TS, 32 * q, cb), *reinterpret_cast<float(*)[16]>(&s[0]));
+                tmem_st16(taddr(TS, 32 * q, cb + 16), *reinterpret_cast<float(*)[16]>(&s[16]));
+            }
             tmem_wait_st();
         }
         if (!mbar_wait(&sm.bar, phase, err)) sm.stop = 1;
         phase ^= 1;
         fence_after_sync();
-        // -------------------------------- E3: V' = U - W S -> tile
+        // -------------------------------- E3: V' = U - W S -> tile (lanes 0-15 W S, 16-31 U)
         {
             const int r = 16 * q + lane;
 #pragma unroll
             for (int half = 0; half < 2; ++half) {
                 const int cb = hf * 64 + 32 * half;
-                float ws[32], u[32];
-                tmem_ld16(taddr(TD3, 32 * q, cb), *reinterpret_cast<float(*)[16]>(&ws[0]));
-                tmem_ld16(taddr(TD3, 32 * q, cb + 16), *reinterpret_cast<float(*)[16]>(&ws[16]));
-                tmem_ld16(taddr(TU, 32 * q, cb), *reinterpret_cast<float(*)[16]>(&u[0]));
-                tmem_ld16(taddr(TU, 32 * q, cb + 16), *reinterpret_cast<float(*)[16]>(&u[16]));
+                float x[32];
+                tmem_ld16(taddr(TLO, 32 * q, cb), *reinterpret_cast<float(*)[16]>(&x[0]));
+                tmem_ld16(taddr(TLO, 32 * q, cb + 16), *reinterpret_cast<float(*)[16]>(&x[16]));
                 tmem_wait_ld();
-                if (lane < 16) {
 #pragma unroll
-                    for (int x = 0; x < 4; ++x) {
-                        float a[8];
+                for (int u = 0; u < 4; ++u) {
+                    float a[8];
 #pragma unroll
-                        for (int y = 0; y < 8; ++y) a[y] = u[8 * x + y] - ws[8 * x + y];
-                        st_vec8<IT>(sm.Vp, mnmaj16(r, cb + 8 * x, D), a);
+                    for (int y = 0; y < 8; ++y) {
+                        const float uu = __shfl_down_sync(0xffffffffu, x[8 * u + y], 16);
+                        a[y] = uu - x[8 * u + y];
                     }
+                    if (lane < 16) st_vec8<IT>(sm.b.wv.Vp, mnmaj16(r, cb + 8 * u, D), a);
                 }
             }
         }
-        // -------------------------------- M4: O += P V'; S += K'^T V'  (overlap: next gates)
+        // -------------------------------- M4: O = Qg S + P V' -> upper; S += K'^T V'  (overlap: next gates)
         issue_sync();
         if (sm.stop) break;
         if (t == 0) {
             const uint32_t id_o = idesc(64, 128, TR::fmt, false, true);
             const uint32_t id_s = idesc(128, 128, TR::fmt, true, true);
+            for (int ks = 0; ks < D / 16; ++ks)
+                mma_f16(THI, desc_kmaj16(sm.a.kq.Qg, D, ks), desc_mnmaj16(sm.S, D, ks), id_o, ks > 0);
             for (int ks = 0; ks < C / 16; ++ks) {
-                const uint64_t vd = desc_mnmaj16(sm.Vp, D, ks);
-                mma_f16(TO, desc_kmaj16(sm.P, C, ks), vd, id_o, true);
-                mma_f16(TS, desc_mnmaj16(sm.R, D, ks), vd, id_s, true);
+                const uint64_t vd = desc_mnmaj16(sm.b.wv.Vp, D, ks);
+                mma_f16(THI, desc_kmaj16(sm.P, C, ks), vd, id_o, true);
+                mma_f16(TS, desc_mnmaj16(sm.a.kq.Kp, D, ks), vd, id_s, true);
             }
             commit(&sm.bar);
         }
@@ -558,33 +599,38 @@ __global__ void __launch_bounds__(NT, 1) chunk_tc_kernel(kai_gdn_chunk_args p, i
         if (!mbar_wait(&sm.bar, phase, err)) sm.stop = 1;
         phase ^= 1;
         fence_after_sync();
-        // -------------------------------- E4: O out; S -> operand copy
+        // -------------------------------- E4: O out (lanes 16-31); S -> operand copy
         {
-            const int r = 16 * q + lane;
+            const int r = 16 * q + lane - 16;
             const long long tok = c0 + r;
-            float o[64];
 #pragma unroll
-            for (int u = 0; u < 4; ++u)
-                tmem_ld16(taddr(TO, 32 * q, hf * 64 + 16 * u), *reinterpret_cast<float(*)[16]>(&o[16 * u]));
-            tmem_wait_ld();
-            if (lane < 16 && tok < T) {
-#pragma unroll
-                for (int u = 0; u < 4; ++u)
-                    st16_out(p.o, ((size_t)(b * T + tok) * Hv + h) * D + hf * 64 + 16 * u, p.out_dtype,
-                             *reinterpret_cast<float(*)[16]>(&o[16 * u]));
+            for (int half = 0; half < 2; ++half) {
+                const int cb = hf * 64 + 32 * half;
+                float o[32];
+                tmem_ld16(taddr(THI - (16u << 16), 32 * q, cb), *reinterpret_cast<float(*)[16]>(&o[0]));
+                tmem_ld16(taddr(THI - (16u << 16), 32 * q, cb + 16), *reinterpret_cast<float(*)[16]>(&o[16]));
+                tmem_wait_ld();
+                if (lane >= 16 && tok < T) {
+                    const size_t oi = ((size_t)(b * T + tok) * Hv + h) * D + cb;
+                    st16_out(p.o, oi, p.out_dtype, *reinterpret_cast<float(*)[16]>(&o[0]));
+                    st16_out(p.o, oi + 16, p.out_dtype, *reinterpret_cast<float(*)[16]>(&o[16]));
+                }
             }
             const int d = 32 * q + lane;
-            float s[64];
 #pragma unroll
-            for (int u = 0; u < 4; ++u)
-                tmem_ld16(taddr(TS, 32 * q, hf * 64 + 16 * u), *reinterpret_cast<float(*)[16]>(&s[16 * u]));
-            tmem_wait_ld();
+            for (int half = 0; half < 2; ++half) {
+                const int cb = hf * 64 + 32 * half;
+                float s[32];
+                tmem_ld16(taddr(TS, 32 * q, cb), *reinterpret_cast<float(*)[16]>(&s[0]));
+                tmem_ld16(taddr(TS, 32 * q, cb + 16), *reinterpret_cast<float(*)[16]>(&s[16]));
+                tmem_wait_ld();
 #pragma unroll
-            for (int u = 0; u < 8; ++u) {
-                float a[8];
+                for (int u = 0; u < 4; ++u) {
+                    float a[8];
 #pragma unroll
-                for (int x = 0; x < 8; ++x) a[x] = s[8 * u + x];
-                st_vec8<IT>(sm.S, mnmaj16(d, hf * 64 + 8 * u, D), a);
+                    for (int x = 0; x < 8; ++x) a[x] = s[8 * u + x];
+                    st_vec8<IT>(sm.S, mnmaj16(d, cb + 8 * u, D), a);
+                }
             }
         }
         fence_before_sync();
@@ -606,7 +652,7 @@ __global__ void __launch_bounds__(NT, 1) chunk_tc_kernel(kai_gdn_chunk_args p, i
     }
     fence_before_sync();
     __syncthreads();
-    if (warp == 0) tmem_dealloc(tm, 512);
+    if (warp == 0) tmem_dealloc(tm, 256);
 }
 
 }  // namespace
@@ -625,17 +671,27 @@ int launch_chunk_tc(const kai_gdn_chunk_args *a, cudaStream_t st) {
     int rc = scratch_for_stream(st, 256, &flag);
     if (rc) return rc;
     if ((rc = check_cuda(cudaMemsetAsync(flag, 0, sizeof(int), st), "chunk_tc: clear flag"))) return rc;
-    const size_t smem = sizeof(TcSmem) + 1024;
+    const size_t smem = sizeof(TcSmem);
     if (a->in_dtype == KAI_GDN_BF16) {
         rc = check_cuda(cudaFuncSetAttribute(chunk_tc_kernel<__nv_bfloat16>,
                                              cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem),
                         "chunk_tc: smem attribute");
+        if (rc) return rc;
+        // two CTAs per SM need the largest shared-memory carveout
+        rc = check_cuda(cudaFuncSetAttribute(chunk_tc_kernel<__nv_bfloat16>, cudaFuncAttributePreferredSharedMemoryCarveout,
+                                             (int)cudaSharedmemCarveoutMaxShared),
+                        "chunk_tc: carveout attribute");
         if (rc) return rc;
         chunk_tc_kernel<__nv_bfloat16><<<(unsigned)units, NT, smem, st>>>(*a, static_cast<int *>(flag));
     } else {
         rc = check_cuda(cudaFuncSetAttribute(chunk_tc_kernel<__half>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                              (int)smem),
                         "chunk_tc: smem attribute");
+        if (rc) return rc;
+        // two CTAs per SM need the largest shared-memory carveout
+        rc = check_cuda(cudaFuncSetAttribute(chunk_tc_kernel<__half>, cudaFuncAttributePreferredSharedMemoryCarveout,
+                                             (int)cudaSharedmemCarveoutMaxShared),
+                        "chunk_tc: carveout attribute");
         if (rc) return rc;
         chunk_tc_kernel<__half><<<(unsigned)units, NT, smem, st>>>(*a, static_cast<int *>(flag));
     }
