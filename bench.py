@@ -51,6 +51,7 @@ def parse():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-chunk", action="store_true", help="skip the chunk-scan measurement")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline sample")
+    ap.add_argument("--no-rows", action="store_true", help="skip the per-row measurements")
     return ap.parse_args()
 
 
@@ -210,6 +211,9 @@ def run_ours(args):
     # ---- chunk scan (config-2 shard) on this GPU
     chunk = None if args.no_chunk else run_chunk_bench(args, world, barrier, peaks)
 
+    # ---- every other hot-path row on its own configuration (this GPU)
+    rows = None if args.no_rows else run_rows(args, peaks)
+
     # ---- CPU baseline on a bounded sample (rank 0, N = 1 only)
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu:
@@ -249,6 +253,7 @@ def run_ours(args):
             "gpu_launches": K * c["layers"],
             "clocks": clk.summary(),
             "chunk_scan": chunk,
+            "rows": rows,
             "cpu_baseline": cpu,
         }
         print(json.dumps(line), flush=True)
@@ -399,6 +404,120 @@ def run_chunk_bench(args, world, barrier, peaks):
             "tensor_frac_of_bf16_peak": round(flops / (ms / 1e3) / 1e12 / peaks["bf16_tflops"], 4),
             "hbm_frac": round(nbytes / (ms / 1e3) / 1e9 / peaks["hbm_gbs"], 4),
             "l2": "256 MB buffer written before each timed call"}
+
+
+def _time(fn, reps: int, flush=None) -> float:
+    """Average milliseconds of fn() over `reps` launches, CUDA events on the
+    current stream, optionally writing a buffer larger than L2 before each."""
+    import torch
+
+    stream = torch.cuda.current_stream()
+    fn()
+    torch.cuda.synchronize()
+    tot = 0.0
+    for _ in range(reps):
+        if flush is not None:
+            flush.zero_()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        fn()
+        e1.record(stream)
+        torch.cuda.synchronize()
+        tot += e0.elapsed_time(e1)
+    return tot / reps
+
+
+def run_rows(args, peaks) -> dict:
+    """One measurement per hot-path row of the scope table, each on its
+    configuration's shape, with the HBM (or tensor) roofline fraction."""
+    import torch
+
+    from orionsbelt_b200 import ops, synth
+
+    hbm = peaks["hbm_gbs"]
+    flush = torch.empty(256 * 1024 * 1024, dtype=torch.uint8, device="cuda")
+    reps = 5
+    out = {}
+
+    def bw_row(name, workload, nbytes, ms, kernel):
+        out[name] = {"workload": workload, "kernel": kernel, "ms": round(ms, 4),
+                     "gbs": round(nbytes / (ms / 1e3) / 1e9, 1),
+                     "hbm_frac": round(nbytes / (ms / 1e3) / 1e9 / hbm, 4), "bytes": nbytes}
+
+    # a1: decay cumsum at config 2 (B=8 x T=32768 x 32 log-decays) and the
+    # prefix product at config 0 ([2048][32]) and at the e2e's key channels
+    g = -torch.nn.functional.softplus(synth.device_normal((8, 32768, 32), 11, 1)) * 0.1
+    gc = torch.empty_like(g)
+    ms = _time(lambda: ops.cumsum(g, gc), reps, flush)
+    bw_row("a1_cumsum_cfg2", "log-decay cumsum, 8 x 32768 x 32 fp32", 2 * g.numel() * 4, ms, "scan_*_kernel<CUMSUM>")
+    a = torch.exp(g[0, :2048].contiguous())
+    dcy = torch.empty_like(a)
+    ms = _time(lambda: ops.cumdecay(a, dcy), reps, flush)
+    bw_row("a1_cumdecay_cfg0", "prefix product, 2048 x 32 fp32 (launch-bound size)", 2 * a.numel() * 4, ms,
+           "scan_final_kernel<CUMPROD>")
+    a2 = torch.rand((4096, 4096), device="cuda") * 0.2 + 0.9
+    d2 = torch.empty_like(a2)
+    ms = _time(lambda: ops.cumdecay(a2, d2), reps, flush)
+    bw_row("a1_cumdecay_4096x4096", "prefix product, 4096 x 4096 fp32", 2 * a2.numel() * 4, ms,
+           "scan_*_kernel<CUMPROD>")
+    del g, gc, a, dcy, a2, d2
+    # a2: conv at config 0 (fp32, T=2048, 8192 channels) and a config-3 shard (fp16 I/O)
+    x, w = synth.device_normal((2048, 8192), 12, 1), synth.device_normal((4, 8192), 12, 2, std=0.5)
+    o, hist = torch.empty_like(x), torch.zeros((3, 8192), device="cuda")
+    ms = _time(lambda: ops.causal_dwconv1d(x, w, o, hist), reps, flush)
+    bw_row("a2_conv_cfg0", "causal dwconv k4, T=2048 x 8192 ch fp32", metrics.conv_bytes(1, 2048, 8192, 4), ms,
+           "conv_k4_kernel<f32,4>")
+    xh = synth.device_normal((8, 8192, 8192), 12, 3, dtype=torch.float16)
+    oh, hh = torch.empty_like(xh), torch.zeros((8, 3, 8192), device="cuda", dtype=torch.float16)
+    ms = _time(lambda: ops.causal_dwconv1d(xh, w, oh, hh), reps, flush)
+    bw_row("a2_conv_cfg3_shard", "causal dwconv k4, 8 x 8192 x 8192 ch fp16 I/O (config-3 shard)",
+           metrics.conv_bytes(8, 8192, 8192, 2), ms, "conv_k4_kernel<f16,8>")
+    del x, w, o, hist, xh, oh, hh
+    # a3: gated scan over the e2e's value channels (4096) for a 32768-token prefill
+    gs = torch.sigmoid(synth.device_normal((32768, 4096), 13, 1))
+    xs = synth.device_normal((32768, 4096), 13, 2)
+    ss, st = torch.empty_like(xs), torch.zeros(4096, device="cuda")
+    ms = _time(lambda: ops.gated_scan(gs, xs, ss, st), reps, flush)
+    bw_row("a3_gated_scan", "gated scan, 32768 x 4096 fp32", metrics.gated_scan_bytes(1, 32768, 4096), ms,
+           "scan_*_kernel<AFFINE>")
+    del gs, xs, ss, st
+    # a4: delta-rule GEMV (decode k.S over 32 heads) and matmul (one chunk, 16 heads)
+    av, B1 = torch.randn(128, device="cuda"), torch.randn((128, 4096), device="cuda")
+    cv = torch.empty(4096, device="cuda")
+    ms = _time(lambda: ops.matmul(av[None], B1, cv[None]), reps, flush)
+    bw_row("a4_gemv", "GEMV K=128 N=4096 fp32", metrics.matmul_bytes(1, 128, 4096), ms, "gemv_rows_kernel")
+    Am, Bm = torch.randn((64, 128), device="cuda"), torch.randn((128, 2048), device="cuda")
+    Cm = torch.empty((64, 2048), device="cuda")
+    ms = _time(lambda: ops.matmul(Am, Bm, Cm), reps, flush)
+    bw_row("a4_matmul", "matmul M=64 K=128 N=2048 fp32 (reference op order)", metrics.matmul_bytes(64, 128, 2048),
+           ms, "sgemm_tile_kernel")
+    out["a4_matmul"]["tflops"] = round(2 * 64 * 128 * 2048 / (ms / 1e3) / 1e12, 3)
+    del av, B1, cv, Am, Bm, Cm
+    # a6: chunk scan at config 0 (fp32 throughout) and config 3 (fp16 in, fp16 state, strong decay)
+    for name, c, dt, sdt, kern in [
+            ("a6_chunk_cfg0", dict(B=1, T=2048, g=0.1), torch.float32, torch.float32,
+             "chunk_scan_fp32_kernel (fp32 CUDA cores)"),
+            ("a6_chunk_cfg3", dict(B=32, T=8192, g=1.0), torch.float16, torch.float16,
+             "chunk_tc_kernel<f16> (tcgen05)")]:
+        d = synth.device_gdn(c["B"], c["T"], 16, 32, 128, 128, g_scale=c["g"], seed=14, in_dtype=dt,
+                             state_dtype=sdt)
+        oo = torch.empty_like(d["v"])
+        S0 = d["S0"]
+
+        def run(d=d, oo=oo, S0=S0):
+            ops.chunk_delta_rule(d["q"], d["k"], d["v"], d["g"], d["beta"], S0, oo, scale=1.0)
+
+        ms = _time(run, 2 if c["B"] > 1 else reps, flush)
+        fl = metrics.chunk_flops(c["B"], c["T"], 32, 128, 64)
+        nb = metrics.chunk_bytes(c["B"], c["T"], 16, 32, 128, 128, e_in=dt.itemsize, e_out=dt.itemsize,
+                                 e_state=sdt.itemsize)
+        out[name] = {"workload": f"B={c['B']}, T={c['T']}, 16/32 heads, 128x128, in {dt}, state {sdt}",
+                     "kernel": kern, "ms": round(ms, 3), "tokens_per_s": round(c["B"] * c["T"] / (ms / 1e3), 1),
+                     "tflops": round(fl / (ms / 1e3) / 1e12, 2),
+                     "gbs": round(nb / (ms / 1e3) / 1e9, 1)}
+        del d, oo, S0
+    torch.cuda.empty_cache()
+    return out
 
 
 def cpu_decode_sample(seconds: float = 10.0, nthreads: int = 0) -> dict:
