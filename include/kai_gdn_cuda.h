@@ -134,11 +134,11 @@ KAI_GDN_API int kai_run_gdn_gated_scan_sm100a(const float *g, const float *x, fl
  * allocate device memory when they call (an engine that gives all of HBM to
  * its own pools at start-up, or a host whose other streams cannot wait for
  * the device-wide synchronisation cudaMalloc / cudaFree may cause).  A long
- * scan's segment carries use a fixed array inside the library image instead
+ * scan's tile records use a fixed array inside the library image instead
  * of library-allocated scratch: every GPU that loads the library holds
  * KAI_GDN_NOALLOC_SCRATCH_BYTES of device memory until the process exits.
- * Limit: 2 * batch * ceil(seq / 128) * channels * 4 bytes <= that size
- * (scans with seq <= 128 need none); larger calls return
+ * Limit: 256 + 512 * batch * ceil(seq / 256) * ceil(channels / 32) bytes
+ * <= that size (scans with seq <= 128 need none); larger calls return
  * KAI_GDN_ERR_INVALID with a message.  The first call on a device looks up
  * the array's address (cudaGetSymbolAddress) and should come before any
  * stream capture.  All calls share the array: calls that overlap on the GPU

@@ -68,11 +68,40 @@ struct ConvParams {
     int nseg;
 };
 
+// One raw 16-byte vector (or one element for the scalar fallback) of a row.
+template <int DT, int VEC> struct Raw;
+template <int DT> struct Raw<DT, 1> {
+    using S = Store<DT>;
+    typename S::T v;
+    __device__ __forceinline__ void load(const void *base, size_t idx) {
+        v = static_cast<const typename S::T *>(base)[idx];
+    }
+    __device__ __forceinline__ float get(int) const { return S::load(&v); }
+};
+template <> struct Raw<KAI_GDN_F32, 4> {
+    float4 v;
+    __device__ __forceinline__ void load(const void *base, size_t idx) {
+        v = __ldg(reinterpret_cast<const float4 *>(static_cast<const float *>(base) + idx));
+    }
+    __device__ __forceinline__ float get(int i) const { return i == 0 ? v.x : i == 1 ? v.y : i == 2 ? v.z : v.w; }
+};
+template <int DT> struct Raw<DT, 8> {
+    using S = Store<DT>;
+    uint4 v;
+    __device__ __forceinline__ void load(const void *base, size_t idx) {
+        v = __ldg(reinterpret_cast<const uint4 *>(static_cast<const uint16_t *>(base) + idx));
+    }
+    __device__ __forceinline__ float get(int i) const {
+        return S::load(reinterpret_cast<const typename S::T *>(&v) + i);
+    }
+};
+
 template <int DT, int VEC>
-__global__ void __launch_bounds__(THREADS) conv_k4_kernel(ConvParams p) {
-    long long c = ((long long)blockIdx.x * THREADS + threadIdx.x) * VEC;
-    int seg = blockIdx.y;
-    long long b = blockIdx.z;
+__global__ void __launch_bounds__(THREADS, 2) conv_k4_kernel(ConvParams p) {
+    constexpr int R = VEC == 8 ? 4 : 8;  // rows loaded ahead
+    const long long c = ((long long)blockIdx.x * THREADS + threadIdx.x) * VEC;
+    const int seg = blockIdx.y;
+    const long long b = blockIdx.z;
     if (c >= p.ch) return;
     const long long T = p.seq, C = p.ch;
     const size_t xb = (size_t)b * T * C + (size_t)c;   // in/out base
@@ -91,46 +120,65 @@ __global__ void __launch_bounds__(THREADS) conv_k4_kernel(ConvParams p) {
     const long long t1 = min(t0 + (long long)SEG, T);
     // Window h0 (oldest) .. h2 (newest) = inputs t0-3 .. t0-1.
     float h0[VEC], h1[VEC], h2[VEC];
-    if (seg == 0) {
-        ld<DT, VEC>(p.hist, hb + 0 * C, h0);
-        ld<DT, VEC>(p.hist, hb + 1 * C, h1);
-        ld<DT, VEC>(p.hist, hb + 2 * C, h2);
-    } else {
-        ld<DT, VEC>(p.in, xb + (size_t)(t0 - 3) * C, h0);
-        ld<DT, VEC>(p.in, xb + (size_t)(t0 - 2) * C, h1);
-        ld<DT, VEC>(p.in, xb + (size_t)(t0 - 1) * C, h2);
-    }
-    constexpr int R = 8;  // rows loaded ahead
-    long long t = t0;
-    for (; t < t1; t += R) {
-        float cur[R][VEC];
-#pragma unroll
-        for (int r = 0; r < R; ++r)
-            if (t + r < t1) ld<DT, VEC>(p.in, xb + (size_t)(t + r) * C, cur[r]);
-#pragma unroll
-        for (int r = 0; r < R; ++r) {
-            if (t + r < t1) {
-                float o[VEC];
-#pragma unroll
-                for (int i = 0; i < VEC; ++i) {
-                    float acc = __fadd_rn(__fmul_rn(h0[i], w0[i]), __fmul_rn(h1[i], w1[i]));
-                    acc = __fadd_rn(acc, __fmul_rn(h2[i], w2[i]));
-                    o[i] = __fadd_rn(acc, __fmul_rn(cur[r][i], w3[i]));
-                    h0[i] = h1[i];
-                    h1[i] = h2[i];
-                    h2[i] = cur[r][i];
-                }
-                st<DT, VEC>(p.out, xb + (size_t)(t + r) * C, o);
-            }
+    {
+        Raw<DT, VEC> r0, r1, r2;
+        if (seg == 0) {
+            r0.load(p.hist, hb + 0 * C);
+            r1.load(p.hist, hb + 1 * C);
+            r2.load(p.hist, hb + 2 * C);
+        } else {
+            r0.load(p.in, xb + (size_t)(t0 - 3) * C);
+            r1.load(p.in, xb + (size_t)(t0 - 2) * C);
+            r2.load(p.in, xb + (size_t)(t0 - 1) * C);
         }
+#pragma unroll
+        for (int i = 0; i < VEC; ++i) {
+            h0[i] = r0.get(i);
+            h1[i] = r1.get(i);
+            h2[i] = r2.get(i);
+        }
+    }
+    auto emit = [&](const Raw<DT, VEC> &cur, long long t) {
+        float o[VEC];
+#pragma unroll
+        for (int i = 0; i < VEC; ++i) {
+            const float x = cur.get(i);
+            float acc = __fadd_rn(__fmul_rn(h0[i], w0[i]), __fmul_rn(h1[i], w1[i]));
+            acc = __fadd_rn(acc, __fmul_rn(h2[i], w2[i]));
+            o[i] = __fadd_rn(acc, __fmul_rn(x, w3[i]));
+            h0[i] = h1[i];
+            h1[i] = h2[i];
+            h2[i] = x;
+        }
+        st<DT, VEC>(p.out, xb + (size_t)t * C, o);
+    };
+    long long t = t0;
+    for (; t + R <= t1; t += R) {
+        Raw<DT, VEC> cur[R];
+#pragma unroll
+        for (int r = 0; r < R; ++r) cur[r].load(p.in, xb + (size_t)(t + r) * C);
+#pragma unroll
+        for (int r = 0; r < R; ++r) emit(cur[r], t + r);
+    }
+    for (; t < t1; ++t) {
+        Raw<DT, VEC> cur;
+        cur.load(p.in, xb + (size_t)t * C);
+        emit(cur, t);
     }
     if (seg == 0) {
         // New history = the last three inputs of the whole call.  With one
         // segment the window already holds them; otherwise read them.
         if (p.nseg > 1) {
-            ld<DT, VEC>(p.in, xb + (size_t)(T - 3) * C, h0);
-            ld<DT, VEC>(p.in, xb + (size_t)(T - 2) * C, h1);
-            ld<DT, VEC>(p.in, xb + (size_t)(T - 1) * C, h2);
+            Raw<DT, VEC> r0, r1, r2;
+            r0.load(p.in, xb + (size_t)(T - 3) * C);
+            r1.load(p.in, xb + (size_t)(T - 2) * C);
+            r2.load(p.in, xb + (size_t)(T - 1) * C);
+#pragma unroll
+            for (int i = 0; i < VEC; ++i) {
+                h0[i] = r0.get(i);
+                h1[i] = r1.get(i);
+                h2[i] = r2.get(i);
+            }
         }
         st<DT, VEC>(p.hist, hb + 0 * C, h0);
         st<DT, VEC>(p.hist, hb + 1 * C, h1);

@@ -6,18 +6,25 @@
 //
 // All are HBM-bound: one read of each input stream, one write of the output.
 // Layout [batch][seq][channels]; a warp covers 32 consecutive channels of one
-// row, so every access is a full 128-byte line.
+// row, so every access is a full 128-byte line.  Every step uses the
+// reference's operation order with one rounding per operation
+// (__fmul_rn / __fadd_rn, no FMA contraction).
 //
-// Time parallelism: each thread walks one SEGMENT of SEG_LEN rows of one
-// channel sequentially, with the reference's operation order and one rounding
-// per operation (__fmul_rn / __fadd_rn, no FMA contraction), so a sequence of
-// at most SEG_LEN rows is bit-identical to the reference's scalar path.
-// Longer sequences use three launches: (1) each segment's aggregate (the
-// product, the sum, or the affine pair (A, B) with s_end = B + s_in*A) goes
-// to scratch; (2) one thread per (batch, channel) turns the aggregates into
-// each segment's carry-in, in order; (3) every segment re-walks its rows from
-// its carry.  Pass 3's re-read of the input is served from L2 for inputs that
-// fit in it (126 MB).
+// seq <= SEG_LEN (128): one thread walks each channel's whole sequence, so
+// the result is bit-identical to the reference's scalar path (the reference's
+// own tests require this at T = 64).
+//
+// Longer sequences: a single pass with decoupled look-back.  A tile is
+// 8*RPW rows x 32 channels; each of its 256 threads holds RPW rows of one
+// channel in registers.  The tile's aggregate (the product, the sum, or the
+// affine map s -> A*s + B) is published per channel; the tile then walks back
+// over its predecessors' records, eight at a time (one per warp), composing
+// their aggregates until it finds one that already holds its inclusive prefix,
+// publishes its own inclusive prefix and writes its outputs from registers.  Tiles are numbered by an
+// atomic counter in the order blocks start, so a tile only ever waits for
+// tiles that are already running; every wait is bounded and a timeout sets an
+// error word instead of hanging.  HBM traffic is the algorithmic one (read
+// once, write once) plus a 16-byte record per tile and channel.
 #include <mutex>
 
 #include "gdn_internal.cuh"
@@ -25,7 +32,7 @@
 namespace gdn {
 namespace {
 
-constexpr int SEG_LEN = 128;  // rows per thread
+constexpr int SEG_LEN = 128;  // rows per thread in the exact single-walk path
 constexpr int BATCH_LD = 8;   // loads issued ahead of the dependent chain
 
 enum Op { CUMPROD = 0, CUMSUM = 1, AFFINE = 2, GDN2 = 3 };
@@ -37,34 +44,19 @@ struct ScanParams {
     const float *w;  // gdn2 write gate
     void *out;       // [batch][seq][ch]
     void *state;     // affine/gdn2: [batch][ch]
-    float *aggA;     // scratch [batch][nseg][ch]
-    float *aggB;     // scratch [batch][nseg][ch] (affine/gdn2)
     long long seq, ch;
-    int nseg;
-    int cw;          // warps per block along channels (block = 32*cw channels)
+    int cw;          // single-walk path: warps per block along channels
 };
 
-template <int OP> struct Step;
-template <> struct Step<CUMPROD> {
-    static constexpr int NIN = 1;
-    __device__ static float apply(float run, const float *v) { return __fmul_rn(run, v[0]); }
-};
-template <> struct Step<CUMSUM> {
-    static constexpr int NIN = 1;
-    __device__ static float apply(float run, const float *v) { return __fadd_rn(run, v[0]); }
-};
-template <> struct Step<AFFINE> {
-    static constexpr int NIN = 2;  // v[0] = x, v[1] = g
-    __device__ static float apply(float run, const float *v) {
-        return __fadd_rn(v[0], __fmul_rn(run, v[1]));
-    }
-};
-template <> struct Step<GDN2> {
-    static constexpr int NIN = 4;  // x, g, b, w
-    __device__ static float apply(float run, const float *v) {
-        return __fadd_rn(__fmul_rn(v[3], v[0]), __fmul_rn(run, __fmul_rn(v[1], v[2])));
-    }
-};
+template <int OP> struct Nin { static constexpr int n = OP == GDN2 ? 4 : (OP == AFFINE ? 2 : 1); };
+
+template <int OP>
+__device__ __forceinline__ float step(float run, const float *v) {
+    if (OP == CUMPROD) return __fmul_rn(run, v[0]);
+    if (OP == CUMSUM) return __fadd_rn(run, v[0]);
+    if (OP == AFFINE) return __fadd_rn(v[0], __fmul_rn(run, v[1]));
+    return __fadd_rn(__fmul_rn(v[3], v[0]), __fmul_rn(run, __fmul_rn(v[1], v[2])));
+}
 
 template <int OP>
 __device__ __forceinline__ void load_row(const ScanParams &p, size_t idx, float *v) {
@@ -76,155 +68,272 @@ __device__ __forceinline__ void load_row(const ScanParams &p, size_t idx, float 
     }
 }
 
-// Thread coordinates: blockDim = (32, 8).  Warps split into cw channel groups
-// and 8/cw segment groups.
-struct Coord {
-    long long c;
-    int seg;
-    long long b;
-    bool live;
+// Aggregates compose as maps s -> A*s + B (A = product of multipliers, B = the
+// scan from 0); for cumprod only A is used, for cumsum only B.
+struct Agg {
+    float A, B;
 };
-__device__ __forceinline__ Coord coord(const ScanParams &p) {
-    int ty = threadIdx.y;
-    int cg = ty % p.cw, sg = ty / p.cw, sw = 8 / p.cw;
-    Coord k;
-    k.c = (long long)blockIdx.x * (32 * p.cw) + cg * 32 + threadIdx.x;
-    k.seg = blockIdx.y * sw + sg;
-    k.b = blockIdx.z;
-    k.live = k.c < p.ch && k.seg < p.nseg;
-    return k;
-}
-
-// Pass 1: aggregate of every segment except the last.
+template <int OP> __device__ __forceinline__ Agg agg_identity() { return {1.0f, 0.0f}; }
+// Fold one element into a running aggregate (the element comes after it).
 template <int OP>
-__global__ void __launch_bounds__(256) scan_aggregate_kernel(ScanParams p) {
-    Coord k = coord(p);
-    if (!k.live || k.seg == p.nseg - 1) return;
-    long long t0 = (long long)k.seg * SEG_LEN;
-    size_t base = (size_t)k.b * p.seq * p.ch + (size_t)k.c;
-    float A = (OP == CUMSUM) ? 0.0f : 1.0f, B = 0.0f;
-    for (int r0 = 0; r0 < SEG_LEN; r0 += BATCH_LD) {
-        float v[BATCH_LD][4];
-#pragma unroll
-        for (int r = 0; r < BATCH_LD; ++r) load_row<OP>(p, base + (size_t)(t0 + r0 + r) * p.ch, v[r]);
-#pragma unroll
-        for (int r = 0; r < BATCH_LD; ++r) {
-            if (OP == CUMPROD) A = __fmul_rn(A, v[r][0]);
-            else if (OP == CUMSUM) A = __fadd_rn(A, v[r][0]);
-            else {
-                float m = (OP == AFFINE) ? v[r][1] : __fmul_rn(v[r][1], v[r][2]);
-                B = Step<OP>::apply(B, v[r]);
-                A = __fmul_rn(A, m);
-            }
-        }
-    }
-    size_t ai = ((size_t)k.b * p.nseg + k.seg) * p.ch + k.c;
-    p.aggA[ai] = A;
-    if (OP == AFFINE || OP == GDN2) p.aggB[ai] = B;
+__device__ __forceinline__ Agg agg_push(Agg a, const float *v) {
+    if (OP == CUMPROD) return {__fmul_rn(a.A, v[0]), 0.0f};
+    if (OP == CUMSUM) return {1.0f, __fadd_rn(a.B, v[0])};
+    const float m = OP == AFFINE ? v[1] : __fmul_rn(v[1], v[2]);
+    return {__fmul_rn(a.A, m), step<OP>(a.B, v)};
+}
+// first, then second
+template <int OP>
+__device__ __forceinline__ Agg agg_then(Agg first, Agg second) {
+    if (OP == CUMPROD) return {__fmul_rn(first.A, second.A), 0.0f};
+    if (OP == CUMSUM) return {1.0f, __fadd_rn(first.B, second.B)};
+    return {__fmul_rn(first.A, second.A), __fadd_rn(__fmul_rn(first.B, second.A), second.B)};
+}
+// Apply an aggregate to a carried value.
+template <int OP>
+__device__ __forceinline__ float agg_apply(Agg a, float s) {
+    if (OP == CUMPROD) return __fmul_rn(s, a.A);
+    if (OP == CUMSUM) return __fadd_rn(s, a.B);
+    return __fadd_rn(a.B, __fmul_rn(s, a.A));
 }
 
-// Pass 2: carry-in of every segment, in order, one thread per (batch, channel).
-// Overwrites aggA[seg] with the carry into seg.
 template <int OP, int SDT>
-__global__ void scan_carry_kernel(ScanParams p) {
-    long long c = (long long)blockIdx.x * blockDim.x + threadIdx.x;
-    long long b = blockIdx.y;
-    if (c >= p.ch) return;
-    float carry;
-    if (OP == CUMPROD) carry = 1.0f;
-    else if (OP == CUMSUM) carry = 0.0f;
-    else {
-        using S = Store<SDT>;
-        carry = S::load(reinterpret_cast<const typename S::T *>(p.state) + b * p.ch + c);
-    }
-    for (int s = 0; s < p.nseg; ++s) {
-        size_t ai = ((size_t)b * p.nseg + s) * p.ch + c;
-        float A = p.aggA[ai];
-        float B = (OP == AFFINE || OP == GDN2) ? p.aggB[ai] : 0.0f;
-        p.aggA[ai] = carry;
-        if (s == p.nseg - 1) break;
-        if (OP == CUMPROD) carry = __fmul_rn(carry, A);
-        else if (OP == CUMSUM) carry = __fadd_rn(carry, A);
-        else carry = __fadd_rn(B, __fmul_rn(carry, A));
-    }
+__device__ __forceinline__ float initial_carry(const ScanParams &p, long long b, long long c) {
+    if (OP == CUMPROD) return 1.0f;
+    if (OP == CUMSUM) return 0.0f;
+    using S = Store<SDT>;
+    return S::load(reinterpret_cast<const typename S::T *>(p.state) + b * p.ch + c);
 }
 
-// Pass 3 (or the only pass when nseg == 1): walk the segment from its carry.
-// ODT: storage type of the output (cumprod only; others write fp32).
-// SDT: storage type of the carried state (affine only).
+// ------------------------------------------------------ exact single walk
+// One thread per channel walks the whole (<= SEG_LEN rows) sequence.
+// blockDim = (32, 8): warps are channel groups.
 template <int OP, int ODT, int SDT>
-__global__ void __launch_bounds__(256) scan_final_kernel(ScanParams p) {
-    Coord k = coord(p);
-    if (!k.live) return;
-    long long t0 = (long long)k.seg * SEG_LEN;
-    long long t1 = min(t0 + (long long)SEG_LEN, p.seq);
-    size_t base = (size_t)k.b * p.seq * p.ch + (size_t)k.c;
-    float run;
-    if (p.nseg > 1) {
-        run = p.aggA[((size_t)k.b * p.nseg + k.seg) * p.ch + k.c];
-    } else if (OP == CUMPROD) {
-        run = 1.0f;
-    } else if (OP == CUMSUM) {
-        run = 0.0f;
-    } else {
-        using S = Store<SDT>;
-        run = S::load(reinterpret_cast<const typename S::T *>(p.state) + k.b * p.ch + k.c);
-    }
+__global__ void __launch_bounds__(256) scan_walk_kernel(ScanParams p) {
+    const long long c = (long long)blockIdx.x * 256 + threadIdx.y * 32 + threadIdx.x;
+    const long long b = blockIdx.z;
+    if (c >= p.ch) return;
+    const size_t base = (size_t)b * p.seq * p.ch + (size_t)c;
+    float run = initial_carry<OP, SDT>(p, b, c);
     using O = Store<ODT>;
     typename O::T *out = reinterpret_cast<typename O::T *>(p.out);
-    long long t = t0;
-    for (; t + BATCH_LD <= t1; t += BATCH_LD) {
+    long long t = 0;
+    for (; t + BATCH_LD <= p.seq; t += BATCH_LD) {
         float v[BATCH_LD][4];
 #pragma unroll
         for (int r = 0; r < BATCH_LD; ++r) load_row<OP>(p, base + (size_t)(t + r) * p.ch, v[r]);
 #pragma unroll
         for (int r = 0; r < BATCH_LD; ++r) {
-            run = Step<OP>::apply(run, v[r]);
+            run = step<OP>(run, v[r]);
             O::store(out + base + (size_t)(t + r) * p.ch, run);
         }
     }
-    for (; t < t1; ++t) {
+    for (; t < p.seq; ++t) {
         float v[4];
         load_row<OP>(p, base + (size_t)t * p.ch, v);
-        run = Step<OP>::apply(run, v);
+        run = step<OP>(run, v);
         O::store(out + base + (size_t)t * p.ch, run);
     }
-    if ((OP == AFFINE || OP == GDN2) && k.seg == p.nseg - 1) {
+    if (OP == AFFINE || OP == GDN2) {
         using S = Store<SDT>;
-        S::store(reinterpret_cast<typename S::T *>(p.state) + k.b * p.ch + k.c, run);
+        S::store(reinterpret_cast<typename S::T *>(p.state) + b * p.ch + c, run);
     }
+}
+
+// ------------------------------------------------ single pass, look-back
+struct __align__(16) TileRecord {
+    unsigned int flag;  // 0 empty, 1 aggregate (A, B) ready, 2 inclusive prefix P ready too
+    float A, B;         // the tile's aggregate map (never rewritten once flag is set)
+    float P;            // the carried value after the tile
+};
+
+struct Lookback {
+    unsigned int *counter;  // tile ticket, zeroed before the launch
+    int *err;               // set when a wait runs out
+    TileRecord *rec;        // [ntiles][32], zeroed before the launch
+    long long nct, ntr, batch;
+};
+
+constexpr uint32_t SPIN_LIMIT = 1u << 22;
+
+__device__ __forceinline__ unsigned int ld_flag(const TileRecord *r) {
+    return *reinterpret_cast<const volatile unsigned int *>(&r->flag);
+}
+
+__device__ __forceinline__ void publish_aggregate(TileRecord *r, float A, float B) {
+    *reinterpret_cast<volatile float *>(&r->A) = A;
+    *reinterpret_cast<volatile float *>(&r->B) = B;
+    __threadfence();
+    *reinterpret_cast<volatile unsigned int *>(&r->flag) = 1u;
+}
+__device__ __forceinline__ void publish_prefix(TileRecord *r, float P) {
+    *reinterpret_cast<volatile float *>(&r->P) = P;
+    __threadfence();
+    *reinterpret_cast<volatile unsigned int *>(&r->flag) = 2u;
+}
+
+template <int OP, int ODT, int SDT, int RPW>
+__global__ void __launch_bounds__(256) scan_lookback_kernel(ScanParams p, Lookback lb) {
+    constexpr int NIN = Nin<OP>::n, TROWS = 8 * RPW;
+    __shared__ long long s_tile;
+    __shared__ float s_A[8][32], s_B[8][32], s_carry[32], s_tile_agg[2][32], s_acc[2][32];
+    __shared__ float s_rA[8][32], s_rB[8][32], s_rP[8][32];
+    __shared__ unsigned int s_rf[8][32];
+    __shared__ int s_done[32];
+    const int lane = threadIdx.x % 32, w = threadIdx.x / 32;
+    if (threadIdx.x == 0) s_tile = (long long)atomicAdd(lb.counter, 1u);
+    __syncthreads();
+    const long long id = s_tile;
+    const long long chains = lb.batch * lb.nct;
+    const long long tr = id / chains, chain = id % chains, b = chain / lb.nct, ct = chain % lb.nct;
+    const long long c = ct * 32 + lane;
+    const bool live_c = c < p.ch;
+    const long long row0 = tr * TROWS + (long long)w * RPW;
+    const size_t base = (size_t)b * p.seq * p.ch + (size_t)c;
+
+    // rows of this thread that exist (the last tile of a sequence is ragged)
+    const int nrow = live_c ? (int)max(0ll, min((long long)RPW, p.seq - row0)) : 0;
+    const size_t first = base + (size_t)row0 * p.ch;
+    const size_t stride = (size_t)p.ch;
+    float v[RPW][NIN];
+#pragma unroll
+    for (int r = 0; r < RPW; ++r) {
+        if (r < nrow) {
+            float t4[4];
+            load_row<OP>(p, first + (size_t)r * stride, t4);
+#pragma unroll
+            for (int k = 0; k < NIN; ++k) v[r][k] = t4[k];
+        }
+    }
+    Agg a = agg_identity<OP>();
+#pragma unroll
+    for (int r = 0; r < RPW; ++r)
+        if (r < nrow) a = agg_push<OP>(a, v[r]);
+    s_A[w][lane] = a.A;
+    s_B[w][lane] = a.B;
+    __syncthreads();
+
+    // Tile aggregate per channel, published at once so that successors can
+    // look past this tile while it looks back itself.
+    if (w == 0) {
+        Agg tile = agg_identity<OP>();
+#pragma unroll
+        for (int ww = 0; ww < 8; ++ww) tile = agg_then<OP>(tile, {s_A[ww][lane], s_B[ww][lane]});
+        s_tile_agg[0][lane] = tile.A;
+        s_tile_agg[1][lane] = tile.B;
+        if (tr == 0) s_carry[lane] = live_c ? initial_carry<OP, SDT>(p, b, c) : 0.0f;
+        else publish_aggregate(lb.rec + (size_t)id * 32 + lane, tile.A, tile.B);
+        s_acc[0][lane] = 1.0f;  // composed maps of the predecessors walked so far
+        s_acc[1][lane] = 0.0f;
+        s_done[lane] = tr == 0;
+    }
+    __syncthreads();
+    // Look back 8 predecessors per round, one per warp, nearest first.
+    for (long long base = tr - 1; base >= 0; base -= 8) {
+        if (__syncthreads_and(s_done[lane] != 0) ) break;
+        const long long k = base - w;
+        unsigned int f = 2u;
+        float pA = 1.0f, pB = 0.0f, pP = 0.0f;
+        if (k >= 0 && !s_done[lane]) {
+            const TileRecord *pr = lb.rec + (size_t)(k * chains + chain) * 32 + lane;
+            f = 0;
+            for (uint32_t it = 0; it < SPIN_LIMIT; ++it) {
+                f = ld_flag(pr);
+                if (f) break;
+                __nanosleep(32);
+            }
+            if (!f) {
+                atomicExch(lb.err, 1);
+                f = 2u;  // give up on this chain: treat as a prefix of 0
+            }
+            __threadfence();
+            pA = *reinterpret_cast<const volatile float *>(&pr->A);
+            pB = *reinterpret_cast<const volatile float *>(&pr->B);
+            pP = *reinterpret_cast<const volatile float *>(&pr->P);
+        }
+        s_rf[w][lane] = f;
+        s_rA[w][lane] = pA;
+        s_rB[w][lane] = pB;
+        s_rP[w][lane] = pP;
+        __syncthreads();
+        if (w == 0 && !s_done[lane]) {
+            Agg acc = {s_acc[0][lane], s_acc[1][lane]};
+            for (int ww = 0; ww < 8; ++ww) {
+                if (base - ww < 0) break;
+                if (s_rf[ww][lane] == 2u) {
+                    s_carry[lane] = agg_apply<OP>(acc, s_rP[ww][lane]);
+                    s_done[lane] = 1;
+                    break;
+                }
+                acc = agg_then<OP>({s_rA[ww][lane], s_rB[ww][lane]}, acc);
+            }
+            s_acc[0][lane] = acc.A;
+            s_acc[1][lane] = acc.B;
+        }
+    }
+    __syncthreads();
+    if (w == 0)
+        publish_prefix(lb.rec + (size_t)id * 32 + lane,
+                       agg_apply<OP>({s_tile_agg[0][lane], s_tile_agg[1][lane]}, s_carry[lane]));
+    float run = s_carry[lane];
+    for (int ww = 0; ww < w; ++ww) run = agg_apply<OP>({s_A[ww][lane], s_B[ww][lane]}, run);
+    using O = Store<ODT>;
+    typename O::T *out = reinterpret_cast<typename O::T *>(p.out);
+#pragma unroll
+    for (int r = 0; r < RPW; ++r) {
+        if (r < nrow) {
+            run = step<OP>(run, v[r]);
+            O::store(out + first + (size_t)r * stride, run);
+            if ((OP == AFFINE || OP == GDN2) && row0 + r == p.seq - 1) {
+                using S = Store<SDT>;
+                S::store(reinterpret_cast<typename S::T *>(p.state) + b * p.ch + c, run);
+            }
+        }
+    }
+}
+
+template <int OP> constexpr int rows_per_warp() { return OP == GDN2 ? 16 : 32; }
+
+// Scratch bytes of a look-back launch: ticket + error word, then the records.
+size_t lookback_bytes(size_t batch, long long seq, long long ch, int rpw) {
+    const long long ntr = (seq + 8 * rpw - 1) / (8 * rpw), nct = (ch + 31) / 32;
+    return 256 + (size_t)ntr * (size_t)nct * batch * 32 * sizeof(TileRecord);
+}
+
+template <int OP, int ODT, int SDT>
+int run_scan_with(ScanParams p, size_t batch, cudaStream_t st, const char *name, void *scratch) {
+    constexpr int RPW = rows_per_warp<OP>();
+    if (p.seq <= SEG_LEN) {
+        if (batch > 65535) return set_error(KAI_GDN_ERR_UNSUPPORTED, "%s: batch %zu > 65535", name, batch);
+        long long gx = (p.ch + 255) / 256;
+        if (gx > 0x7fffffffll) return set_error(KAI_GDN_ERR_UNSUPPORTED, "%s: too many channels", name);
+        scan_walk_kernel<OP, ODT, SDT><<<dim3((unsigned)gx, 1, (unsigned)batch), dim3(32, 8), 0, st>>>(p);
+        return check_launch(name);
+    }
+    Lookback lb;
+    lb.ntr = (p.seq + 8 * RPW - 1) / (8 * RPW);
+    lb.nct = (p.ch + 31) / 32;
+    lb.batch = (long long)batch;
+    const long long tiles = lb.ntr * lb.nct * lb.batch;
+    if (tiles > 0x7fffffffll) return set_error(KAI_GDN_ERR_UNSUPPORTED, "%s: shape too large", name);
+    const size_t bytes = lookback_bytes(batch, p.seq, p.ch, RPW);
+    int rc = check_cuda(cudaMemsetAsync(scratch, 0, bytes, st), name);
+    if (rc) return rc;
+    lb.counter = static_cast<unsigned int *>(scratch);
+    lb.err = reinterpret_cast<int *>(static_cast<char *>(scratch) + 16);
+    lb.rec = reinterpret_cast<TileRecord *>(static_cast<char *>(scratch) + 256);
+    scan_lookback_kernel<OP, ODT, SDT, RPW><<<(unsigned)tiles, 256, 0, st>>>(p, lb);
+    return check_launch(name);
 }
 
 template <int OP, int ODT, int SDT>
 int run_scan(ScanParams p, size_t batch, cudaStream_t st, const char *name) {
-    if (batch > 65535) return set_error(KAI_GDN_ERR_UNSUPPORTED, "%s: batch %zu > 65535", name, batch);
-    long long nseg = (p.seq + SEG_LEN - 1) / SEG_LEN;
-    if (nseg > (1ll << 24)) return set_error(KAI_GDN_ERR_UNSUPPORTED, "%s: seq too long", name);
-    p.nseg = (int)nseg;
-    int sw = nseg >= 8 ? 8 : nseg >= 4 ? 4 : nseg >= 2 ? 2 : 1;
-    p.cw = 8 / sw;
-    dim3 block(32, 8);
-    long long gx = (p.ch + 32 * p.cw - 1) / (32 * p.cw);
-    long long gy = (nseg + sw - 1) / sw;
-    if (gx > 0x7fffffffll || gy > 65535)
-        return set_error(KAI_GDN_ERR_UNSUPPORTED, "%s: shape too large for the grid", name);
-    dim3 grid((unsigned)gx, (unsigned)gy, (unsigned)batch);
-    if (nseg > 1) {
-        size_t n = batch * (size_t)nseg * (size_t)p.ch;
-        int naggs = (OP == AFFINE || OP == GDN2) ? 2 : 1;
-        void *scr = nullptr;
-        int rc = scratch_for_stream(st, n * naggs * sizeof(float), &scr);
+    void *scr = nullptr;
+    if (p.seq > SEG_LEN) {
+        int rc = scratch_for_stream(st, lookback_bytes(batch, p.seq, p.ch, rows_per_warp<OP>()), &scr);
         if (rc) return rc;
-        p.aggA = static_cast<float *>(scr);
-        p.aggB = p.aggA + n;
-        scan_aggregate_kernel<OP><<<grid, block, 0, st>>>(p);
-        if ((rc = check_launch(name))) return rc;
-        dim3 cgrid((unsigned)((p.ch + 127) / 128), (unsigned)batch);
-        scan_carry_kernel<OP, SDT><<<cgrid, 128, 0, st>>>(p);
-        if ((rc = check_launch(name))) return rc;
     }
-    scan_final_kernel<OP, ODT, SDT><<<grid, block, 0, st>>>(p);
-    return check_launch(name);
+    return run_scan_with<OP, ODT, SDT>(p, batch, st, name, scr);
 }
 
 }  // namespace
@@ -302,8 +411,8 @@ int launch_gdn2_scan(const float *g, const float *bg, const float *wg, const flo
 // engine that hands all of HBM to its own state / KV pool at start-up and
 // budgets nothing for a library, or a host that keeps other streams busy and
 // cannot afford cudaMalloc / cudaFree, which may synchronise the whole
-// device.  kai_run_gdn_gated_scan_noalloc_sm100a serves them: the segment
-// carries of a long scan live in the fixed array below instead of the
+// device.  kai_run_gdn_gated_scan_noalloc_sm100a serves them: the look-back
+// records of a long scan live in the fixed array below instead of the
 // library's cudaMalloc'd per-stream scratch.
 //
 // The array is part of the library's device image, so every GPU that loads
@@ -312,10 +421,10 @@ int launch_gdn2_scan(const float *g, const float *bg, const float *wg, const flo
 // address (on the host it is only a stand-in), so the address is looked up
 // once per device with cudaGetSymbolAddress, with that device current, on the
 // first call there; that first call should come before any stream capture.
-// Every call shares the array and overwrites what it uses (each element a
-// call reads was written earlier in the same call, so nothing needs zeroing);
-// calls that overlap on the GPU -- two streams, or two host threads -- race
-// on it and must be serialised by the caller.
+// Every call shares the array; each call clears (cudaMemsetAsync, which
+// allocates nothing) the part it uses before its kernel runs.  Calls that
+// overlap on the GPU -- two streams, or two host threads -- race on it and
+// must be serialised by the caller.
 // ---------------------------------------------------------------------------
 namespace {
 
@@ -344,38 +453,18 @@ int noalloc_scratch(float **out) {
 template <int SDT>
 int run_scan_noalloc(ScanParams p, size_t batch, cudaStream_t st) {
     const char *name = "gated_scan_noalloc";
-    if (batch > 65535) return set_error(KAI_GDN_ERR_UNSUPPORTED, "%s: batch %zu > 65535", name, batch);
-    long long nseg = (p.seq + SEG_LEN - 1) / SEG_LEN;
-    if (nseg > (1ll << 24)) return set_error(KAI_GDN_ERR_UNSUPPORTED, "%s: seq too long", name);
-    p.nseg = (int)nseg;
-    int sw = nseg >= 8 ? 8 : nseg >= 4 ? 4 : nseg >= 2 ? 2 : 1;
-    p.cw = 8 / sw;
-    dim3 block(32, 8);
-    long long gx = (p.ch + 32 * p.cw - 1) / (32 * p.cw);
-    long long gy = (nseg + sw - 1) / sw;
-    if (gx > 0x7fffffffll || gy > 65535)
-        return set_error(KAI_GDN_ERR_UNSUPPORTED, "%s: shape too large for the grid", name);
-    dim3 grid((unsigned)gx, (unsigned)gy, (unsigned)batch);
-    int rc;
-    if (nseg > 1) {
-        size_t n = batch * (size_t)nseg * (size_t)p.ch;
-        if (n > kNoallocFloats / 2)
+    float *scr = nullptr;
+    if (p.seq > SEG_LEN) {
+        const size_t need = lookback_bytes(batch, p.seq, p.ch, rows_per_warp<AFFINE>());
+        if (need > (size_t)KAI_GDN_NOALLOC_SCRATCH_BYTES)
             return set_error(KAI_GDN_ERR_INVALID,
-                             "%s: batch*ceil(seq/%d)*channels = %zu needs %zu bytes of scratch; the static "
+                             "%s: batch %zu x seq %lld x channels %lld needs %zu bytes of scratch; the static "
                              "maximum is %zu bytes (use kai_run_gdn_gated_scan_sm100a for larger calls)",
-                             name, SEG_LEN, n, 2 * n * sizeof(float), (size_t)KAI_GDN_NOALLOC_SCRATCH_BYTES);
-        float *scr = nullptr;
-        if ((rc = noalloc_scratch(&scr))) return rc;
-        p.aggA = scr;
-        p.aggB = scr + n;
-        scan_aggregate_kernel<AFFINE><<<grid, block, 0, st>>>(p);
-        if ((rc = check_launch(name))) return rc;
-        dim3 cgrid((unsigned)((p.ch + 127) / 128), (unsigned)batch);
-        scan_carry_kernel<AFFINE, SDT><<<cgrid, 128, 0, st>>>(p);
-        if ((rc = check_launch(name))) return rc;
+                             name, batch, p.seq, p.ch, need, (size_t)KAI_GDN_NOALLOC_SCRATCH_BYTES);
+        int rc = noalloc_scratch(&scr);
+        if (rc) return rc;
     }
-    scan_final_kernel<AFFINE, KAI_GDN_F32, SDT><<<grid, block, 0, st>>>(p);
-    return check_launch(name);
+    return run_scan_with<AFFINE, KAI_GDN_F32, SDT>(p, batch, st, name, scr);
 }
 
 }  // namespace
