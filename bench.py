@@ -141,7 +141,8 @@ def run_ours(args):
     peaks = load_peaks()
     c = CFG1
     bf16 = torch.bfloat16
-    seed = 1000 + rank  # each rank owns different sequences
+    from orionsbelt_b200 import shard
+    seed = shard.rank_seed(1, rank)  # each rank owns its own 64 sequences (weak scaling)
 
     # ---- per-layer inputs and states, resident in HBM
     layers = []
@@ -209,10 +210,10 @@ def run_ours(args):
     e2e = run_e2e_decode(args, layers, launch_layers, world, barrier, step_bytes)
 
     # ---- chunk scan (config-2 shard) on this GPU
-    chunk = None if args.no_chunk else run_chunk_bench(args, world, barrier, peaks)
+    chunk = None if args.no_chunk else run_chunk_bench(args, world, barrier, peaks, seed)
 
     # ---- every other hot-path row on its own configuration (this GPU)
-    rows = None if args.no_rows else run_rows(args, peaks)
+    rows = None if (args.no_rows or world > 1) else run_rows(args, peaks)
 
     # ---- CPU baseline on a bounded sample (rank 0, N = 1 only)
     cpu = None
@@ -365,14 +366,15 @@ def run_e2e_decode(args, layers, launch_layers, world, barrier, step_bytes):
                     "uploads/downloads of neighbouring steps overlap compute on two copy streams"}
 
 
-def run_chunk_bench(args, world, barrier, peaks):
-    """Config-2 shard on this GPU: B=8, T=32768, bf16 q/k/v, fp32 state."""
+def run_chunk_bench(args, world, barrier, peaks, seed):
+    """Config-2 shard on each GPU: B=8, T=32768, bf16 q/k/v, fp32 state; the
+    time is the max over ranks."""
     import torch
 
     from orionsbelt_b200 import _lib, ops, synth
 
     c = CFG2_SHARD
-    d = synth.device_gdn(c["B"], c["T"], c["Hk"], c["Hv"], c["dk"], c["dv"], g_scale=0.1, seed=77,
+    d = synth.device_gdn(c["B"], c["T"], c["Hk"], c["Hv"], c["dk"], c["dv"], g_scale=0.1, seed=seed + 77,
                          in_dtype=torch.bfloat16)
     o = torch.empty_like(d["v"])
     S = d["S0"].clone()
@@ -394,15 +396,21 @@ def run_chunk_bench(args, world, barrier, peaks):
         torch.cuda.synchronize()
         tot += e0.elapsed_time(e1)
     ms = tot / reps
-    flops = metrics.chunk_flops(c["B"], c["T"], c["Hv"], c["dk"], 64)
-    nbytes = metrics.chunk_bytes(c["B"], c["T"], c["Hk"], c["Hv"], c["dk"], c["dv"], e_in=2, e_out=2, e_state=4)
+    if world > 1:
+        import torch.distributed as dist
+        t = torch.tensor([ms], device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = t.item()
+    flops = metrics.chunk_flops(c["B"], c["T"], c["Hv"], c["dk"], 64) * world
+    nbytes = metrics.chunk_bytes(c["B"], c["T"], c["Hk"], c["Hv"], c["dk"], c["dv"], e_in=2, e_out=2, e_state=4) * world
     tok = c["B"] * c["T"] * world / (ms / 1e3)
-    return {"workload": "config 2 shard per GPU: B=8, T=32768, 16/32 heads, 128x128, bf16 q/k/v/o, fp32 state",
+    return {"workload": "config 2 shard per GPU: B=8, T=32768, 16/32 heads, 128x128, bf16 q/k/v/o, fp32 state "
+                        "(aggregate tokens/s and TF/s over all GPUs; fractions per GPU)",
             "kernel": "chunk_tc_kernel<bf16> (tcgen05 MMAs, fp32 state in TMEM)",
             "tokens_per_s": round(tok, 1), "ms": round(ms, 3),
             "tflops": round(flops / (ms / 1e3) / 1e12, 2), "gbs": round(nbytes / (ms / 1e3) / 1e9, 1),
-            "tensor_frac_of_bf16_peak": round(flops / (ms / 1e3) / 1e12 / peaks["bf16_tflops"], 4),
-            "hbm_frac": round(nbytes / (ms / 1e3) / 1e9 / peaks["hbm_gbs"], 4),
+            "tensor_frac_of_bf16_peak": round(flops / world / (ms / 1e3) / 1e12 / peaks["bf16_tflops"], 4),
+            "hbm_frac": round(nbytes / world / (ms / 1e3) / 1e9 / peaks["hbm_gbs"], 4),
             "l2": "256 MB buffer written before each timed call"}
 
 
