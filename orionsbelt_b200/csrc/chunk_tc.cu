@@ -667,10 +667,9 @@ bool chunk_tc_supported(const kai_gdn_chunk_args *a) {
 int launch_chunk_tc(const kai_gdn_chunk_args *a, cudaStream_t st) {
     const long long units = (long long)(a->batch * a->heads_v);
     if (units > 0x7fffffffll) return set_error(KAI_GDN_ERR_UNSUPPORTED, "chunk_tc: too many heads");
-    void *flag = nullptr;
-    int rc = scratch_for_stream(st, 256, &flag);
+    int *flag = nullptr;
+    int rc = device_error_word(&flag);
     if (rc) return rc;
-    if ((rc = check_cuda(cudaMemsetAsync(flag, 0, sizeof(int), st), "chunk_tc: clear flag"))) return rc;
     const size_t smem = sizeof(TcSmem);
     if (a->in_dtype == KAI_GDN_BF16) {
         rc = check_cuda(cudaFuncSetAttribute(chunk_tc_kernel<__nv_bfloat16>,
@@ -682,7 +681,7 @@ int launch_chunk_tc(const kai_gdn_chunk_args *a, cudaStream_t st) {
                                              (int)cudaSharedmemCarveoutMaxShared),
                         "chunk_tc: carveout attribute");
         if (rc) return rc;
-        chunk_tc_kernel<__nv_bfloat16><<<(unsigned)units, NT, smem, st>>>(*a, static_cast<int *>(flag));
+        chunk_tc_kernel<__nv_bfloat16><<<(unsigned)units, NT, smem, st>>>(*a, flag);
     } else {
         rc = check_cuda(cudaFuncSetAttribute(chunk_tc_kernel<__half>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                              (int)smem),
@@ -693,7 +692,7 @@ int launch_chunk_tc(const kai_gdn_chunk_args *a, cudaStream_t st) {
                                              (int)cudaSharedmemCarveoutMaxShared),
                         "chunk_tc: carveout attribute");
         if (rc) return rc;
-        chunk_tc_kernel<__half><<<(unsigned)units, NT, smem, st>>>(*a, static_cast<int *>(flag));
+        chunk_tc_kernel<__half><<<(unsigned)units, NT, smem, st>>>(*a, flag);
     }
     return check_launch("chunk_delta_rule_tc");
 }

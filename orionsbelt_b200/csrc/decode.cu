@@ -61,7 +61,7 @@ __device__ __forceinline__ void st4(void *base, size_t idx, float4 v) {
 }
 
 template <int D, int SDT>
-__global__ void __launch_bounds__(THREADS, 2) decode_step_kernel(kai_gdn_decode_args p) {
+__global__ void __launch_bounds__(THREADS, 3) decode_step_kernel(kai_gdn_decode_args p) {
     constexpr int DK = D, DV = D;
     constexpr int CPR = DV / 4;          // threads per row
     constexpr int RPP = THREADS / CPR;   // rows per pass

@@ -19,6 +19,9 @@ int check_cuda(cudaError_t err, const char *what);
 // Check the launch that was just issued.
 int check_launch(const char *kernel);
 
+// Device word where kernels with bounded waits record a timeout (no allocation).
+int device_error_word(int **out);
+
 // Number of SMs of the current device (cached per device).
 int sm_count();
 

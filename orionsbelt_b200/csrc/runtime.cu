@@ -55,6 +55,33 @@ int sm_count() {
     return cache[dev];
 }
 
+// -------------------------------------------------------- device error word
+// Kernels with bounded waits (the tensor-core chunk scan, the bulk-copy decode
+// step) record a timeout here instead of hanging.  A file-scope device word,
+// so launching needs no allocation (and can be captured in a CUDA graph); its
+// address is looked up once per device.
+namespace {
+__device__ int g_wait_timeout;
+std::mutex g_errword_mu;
+int *g_errword[64] = {nullptr};
+}  // namespace
+
+int device_error_word(int **out) {
+    int dev = 0;
+    int rc = check_cuda(cudaGetDevice(&dev), "error word: cudaGetDevice");
+    if (rc) return rc;
+    if (dev < 0 || dev >= 64) return set_error(KAI_GDN_ERR_UNSUPPORTED, "error word: device %d", dev);
+    std::lock_guard<std::mutex> lock(g_errword_mu);
+    if (!g_errword[dev]) {
+        void *p = nullptr;
+        rc = check_cuda(cudaGetSymbolAddress(&p, g_wait_timeout), "error word: cudaGetSymbolAddress");
+        if (rc) return rc;
+        g_errword[dev] = static_cast<int *>(p);
+    }
+    *out = g_errword[dev];
+    return KAI_GDN_OK;
+}
+
 // ----------------------------------------------------------------- scratch
 namespace {
 struct ScratchEntry {
