@@ -406,7 +406,7 @@ def run_chunk_bench(args, world, barrier, peaks, seed):
     tok = c["B"] * c["T"] * world / (ms / 1e3)
     return {"workload": "config 2 shard per GPU: B=8, T=32768, 16/32 heads, 128x128, bf16 q/k/v/o, fp32 state "
                         "(aggregate tokens/s and TF/s over all GPUs; fractions per GPU)",
-            "kernel": "chunk_tc_kernel<bf16> (tcgen05 MMAs, fp32 state in TMEM)",
+            "kernel": "chunk_ws_kernel<bf16> (warp-specialised: TMA loads, tcgen05 MMAs, fp32 state in TMEM)",
             "tokens_per_s": round(tok, 1), "ms": round(ms, 3),
             "tflops": round(flops / (ms / 1e3) / 1e12, 2), "gbs": round(nbytes / (ms / 1e3) / 1e9, 1),
             "tensor_frac_of_bf16_peak": round(flops / world / (ms / 1e3) / 1e12 / peaks["bf16_tflops"], 4),
@@ -506,7 +506,7 @@ def run_rows(args, peaks) -> dict:
             ("a6_chunk_cfg0", dict(B=1, T=2048, g=0.1), torch.float32, torch.float32,
              "chunk_scan_fp32_kernel (fp32 CUDA cores)"),
             ("a6_chunk_cfg3", dict(B=32, T=8192, g=1.0), torch.float16, torch.float16,
-             "chunk_tc_kernel<f16> (tcgen05)")]:
+             "chunk_ws_kernel<f16> (warp-specialised, tcgen05)")]:
         d = synth.device_gdn(c["B"], c["T"], 16, 32, 128, 128, g_scale=c["g"], seed=14, in_dtype=dt,
                              state_dtype=sdt)
         oo = torch.empty_like(d["v"])

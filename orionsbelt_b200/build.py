@@ -79,7 +79,7 @@ def build(verbose: bool = False, force: bool = False) -> Path:
 def build_selftest(verbose: bool = False) -> Path:
     """Test-only library checking the tcgen05 building blocks (tests/c/umma_selftest.cu)."""
     SELFTEST_LIB.parent.mkdir(parents=True, exist_ok=True)
-    deps = [SELFTEST_SRC, CSRC / "umma.cuh"]
+    deps = [SELFTEST_SRC, CSRC / "umma.cuh", CSRC / "tma.cuh"]
     if SELFTEST_LIB.exists() and SELFTEST_LIB.stat().st_mtime >= max(d.stat().st_mtime for d in deps):
         return SELFTEST_LIB
     cmd = [nvcc(), *NVCC_FLAGS, "-shared", "-cudart", "static", str(SELFTEST_SRC), "-o", str(SELFTEST_LIB)]

@@ -325,7 +325,7 @@ int launch_chunk(const kai_gdn_chunk_args *a, cudaStream_t st) {
         return set_error(KAI_GDN_ERR_UNSUPPORTED, "chunk: chunk length %zu (supported: 64)", a->chunk);
     // bf16 / fp16 inputs at the model's head size run on the tensor cores;
     // fp32 inputs (and other head sizes) take the fp32 CUDA-core kernel.
-    if (chunk_tc_supported(a)) return launch_chunk_tc(a, st);
+    if (chunk_ws_supported(a)) return launch_chunk_ws(a, st);
     return launch_chunk_fp32(a, st);
 }
 

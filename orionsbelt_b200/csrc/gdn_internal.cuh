@@ -52,9 +52,10 @@ int launch_matmul(const float *A, const float *B, float *C, size_t M, size_t K,
                   size_t N, cudaStream_t st);
 int launch_decode(const kai_gdn_decode_args *a, cudaStream_t st);
 int launch_chunk(const kai_gdn_chunk_args *a, cudaStream_t st);
-// Tensor-core chunk scan (chunk_tc.cu): bf16/fp16 inputs, dk = dv = 128, chunk 64.
-bool chunk_tc_supported(const kai_gdn_chunk_args *a);
-int launch_chunk_tc(const kai_gdn_chunk_args *a, cudaStream_t st);
+// Warp-specialised tensor-core chunk scan (chunk_ws.cu): bf16/fp16 q, k, v,
+// dk = dv = 128, chunk 64; TMA-fed, tcgen05 MMAs, fp32 state in TMEM.
+bool chunk_ws_supported(const kai_gdn_chunk_args *a);
+int launch_chunk_ws(const kai_gdn_chunk_args *a, cudaStream_t st);
 
 // --------------------------------------------------- storage conversions
 // Loads widen to fp32 exactly; stores round to nearest even.

@@ -39,6 +39,16 @@ __host__ __device__ constexpr uint64_t smem_desc(uint32_t saddr, uint32_t lbo, u
            ((uint64_t)((sbo >> 4) & 0x3FFFu) << 32) | (1ull << 46);  // version 1, no swizzle
 }
 
+// The same with the 128-byte swizzle layout (tile base 1024-byte aligned).
+//   K-major: 8 rows of 128 bytes (64 16-bit k's) per 1024-byte atom, 16-byte
+//            chunk j of row r stored at chunk j ^ (r % 8); SBO = next 8 rows;
+//            LBO unused; a K step of 16 advances the start address 32 bytes.
+//   MN-major: 8 k-rows of 128 bytes (64 mn's) per atom, same permutation;
+//            LBO = next 64 mn's (next atom column), SBO = next 8 k's.
+__host__ __device__ constexpr uint64_t smem_desc_sw128(uint32_t saddr, uint32_t lbo, uint32_t sbo) {
+    return smem_desc(saddr, lbo, sbo) | (2ull << 61);
+}
+
 enum Fmt : uint32_t { F16 = 0, BF16 = 1, TF32 = 2 };
 
 // kind::f16 / kind::tf32 instruction descriptor, fp32 accumulate.
@@ -75,6 +85,16 @@ __device__ __forceinline__ void mma_f16(uint32_t d_tmem, uint64_t adesc, uint64_
         "setp.ne.b32 p, %4, 0;\n\t"
         "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}\n" ::"r"(d_tmem),
         "l"(adesc), "l"(bdesc), "r"(id), "r"(accumulate ? 1u : 0u));
+}
+// A operand from TMEM (M = 128 rows in lanes 0..127; a K = 16 step spans 8
+// columns, two 16-bit values per column, the lower k in the low half).
+__device__ __forceinline__ void mma_f16_ta(uint32_t d_tmem, uint32_t a_tmem, uint64_t bdesc, uint32_t id,
+                                           bool accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}\n" ::"r"(d_tmem),
+        "r"(a_tmem), "l"(bdesc), "r"(id), "r"(accumulate ? 1u : 0u));
 }
 __device__ __forceinline__ void mma_tf32(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t id,
                                          bool accumulate) {
@@ -167,7 +187,23 @@ __device__ __forceinline__ void tmem_st16(uint32_t taddr, const float (&v)[16]) 
         "r"(__float_as_uint(v[12])), "r"(__float_as_uint(v[13])), "r"(__float_as_uint(v[14])),
         "r"(__float_as_uint(v[15])));
 }
+__device__ __forceinline__ void tmem_st16u(uint32_t taddr, const uint32_t (&v)[16]) {
+    asm volatile(
+        "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], "
+        "{%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};" ::"r"(taddr),
+        "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7]), "r"(v[8]),
+        "r"(v[9]), "r"(v[10]), "r"(v[11]), "r"(v[12]), "r"(v[13]), "r"(v[14]), "r"(v[15]));
+}
 __device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+// After tmem_wait_ld: make later uses of registers filled by tcgen05.ld depend
+// on a statement that follows the wait, so the compiler cannot hoist them
+// above it (the wait itself names no registers).
+__device__ __forceinline__ void reg_fence16(float *v) {
+    asm volatile(""
+                 : "+f"(v[0]), "+f"(v[1]), "+f"(v[2]), "+f"(v[3]), "+f"(v[4]), "+f"(v[5]), "+f"(v[6]), "+f"(v[7]),
+                   "+f"(v[8]), "+f"(v[9]), "+f"(v[10]), "+f"(v[11]), "+f"(v[12]), "+f"(v[13]), "+f"(v[14]),
+                   "+f"(v[15]));
+}
 __device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
 
 // TMEM address of (lane, column).

@@ -1,5 +1,6 @@
-"""The tensor-core chunked scan (csrc/chunk_tc.cu, bf16/fp16 q/k/v, fp32 state
-in TMEM) against the oracle token loop and against the fp32 CUDA-core kernel.
+"""The warp-specialised tensor-core chunked scan (csrc/chunk_ws.cu: bf16/fp16
+q/k/v by TMA, tcgen05 MMAs, fp32 state in TMEM) against the oracle token loop
+and against the fp32 CUDA-core kernel.
 
 Tolerance: 2e-2 relative L2 on outputs and final state (the build's bar for
 bf16 / fp16 paths); both kernels see the same rounded inputs.

@@ -81,3 +81,72 @@ def test_m64_upper_lane_half(cuda, selftest, N, b_mn):
     assert err.item() == 0
     want = _bf16(A).astype(np.float64) @ _bf16(B).astype(np.float64)
     assert rel_l2(D.cpu().numpy(), want) < 1e-5
+
+
+# ---------------------------------------------------------------- layout modes
+# 0/1 K-/MN-major (k-groups / mn-groups inner), 2/3 the TMA-order variants,
+# 5/6 K-/MN-major with the 128-byte swizzle, 4 = A operand in TMEM.
+MODE_CASES = [
+    (128, 64, 64, 2, 2), (128, 64, 128, 2, 3), (64, 64, 128, 2, 2), (128, 128, 64, 3, 3), (128, 64, 64, 3, 0),
+    (128, 64, 128, 4, 2), (128, 128, 64, 4, 3), (128, 64, 64, 4, 0), (128, 128, 128, 4, 1),
+    (128, 64, 128, 5, 5), (64, 64, 128, 5, 5), (128, 128, 64, 6, 6), (128, 64, 128, 6, 5), (128, 128, 64, 4, 6),
+    (128, 64, 128, 4, 5),
+]
+
+
+@pytest.fixture(scope="module")
+def selftest2(selftest):
+    selftest.umma_selftest_gemm2.restype = C.c_int
+    selftest.umma_selftest_gemm2.argtypes = [C.c_void_p] * 3 + [C.c_int] * 5 + [C.c_void_p]
+    selftest.umma_selftest_tma.restype = C.c_int
+    selftest.umma_selftest_tma.argtypes = [C.c_void_p, C.c_void_p] + [C.c_int] * 8 + [C.c_void_p]
+    return selftest
+
+
+@pytest.mark.parametrize("M,N,K,a_mode,b_mode", MODE_CASES)
+def test_layout_modes(cuda, selftest2, M, N, K, a_mode, b_mode):
+    r = np.random.default_rng(7 * M + 3 * N + K + 100 * a_mode + 10 * b_mode)
+    A = r.standard_normal((M, K)).astype(np.float32)
+    B = r.standard_normal((K, N)).astype(np.float32)
+    Ad, Bd = cuda.from_numpy(A).cuda(), cuda.from_numpy(B).cuda()
+    D = cuda.full((M, N), float("nan"), device="cuda")
+    err = cuda.zeros(1, dtype=cuda.int32, device="cuda")
+    rc = selftest2.umma_selftest_gemm2(Ad.data_ptr(), Bd.data_ptr(), D.data_ptr(), M, N, K, a_mode, b_mode,
+                                       err.data_ptr())
+    assert rc == 0 and err.item() == 0
+    want = _bf16(A).astype(np.float64) @ _bf16(B).astype(np.float64)
+    got = D.cpu().numpy()
+    if M == 64:
+        got = got[:64]
+    assert rel_l2(got, want) < 1e-5
+
+
+def _tile_expected(x, b, t0, h, swz):
+    """Byte layout the TMA chunk load should produce (uint16 view, 8192 entries)."""
+    T = x.shape[1]
+    out = np.zeros(8192, np.uint16)
+    for t in range(64):
+        for d in range(128):
+            v = x[b, t0 + t, h, d] if t0 + t < T else 0
+            if not swz:
+                off = (d // 8) * 1024 + (t // 8) * 128 + (t % 8) * 16 + (d % 8) * 2
+            else:
+                chunk = (d % 64) // 8
+                off = (d // 64) * 8192 + t * 128 + ((chunk ^ (t % 8)) * 16) + (d % 8) * 2
+            out[off // 2] = v
+    return out
+
+
+@pytest.mark.parametrize("swz", [0, 1])
+@pytest.mark.parametrize("t0", [0, 64, 100])
+def test_tma_chunk_tile(cuda, selftest2, swz, t0):
+    B, T, H = 2, 130, 3
+    r = np.random.default_rng(5)
+    x = r.integers(1, 60000, size=(B, T, H, 128), dtype=np.uint16)
+    src = cuda.from_numpy(x.view(np.int16)).cuda()
+    out = cuda.zeros(8192, dtype=cuda.int16, device="cuda")
+    err = cuda.zeros(1, dtype=cuda.int32, device="cuda")
+    rc = selftest2.umma_selftest_tma(src.data_ptr(), out.data_ptr(), 1, B, T, H, t0, 2, 1, swz, err.data_ptr())
+    assert rc == 0 and err.item() == 0
+    got = out.cpu().numpy().view(np.uint16)
+    np.testing.assert_array_equal(got, _tile_expected(x, 1, t0, 2, swz))
