@@ -16,15 +16,18 @@
 //
 // Longer sequences: a single pass with decoupled look-back.  A tile is
 // 8*RPW rows x 32 channels; each of its 256 threads holds RPW rows of one
-// channel in registers.  The tile's aggregate (the product, the sum, or the
-// affine map s -> A*s + B) is published per channel; the tile then walks back
-// over its predecessors' records, eight at a time (one per warp), composing
-// their aggregates until it finds one that already holds its inclusive prefix,
-// publishes its own inclusive prefix and writes its outputs from registers.  Tiles are numbered by an
-// atomic counter in the order blocks start, so a tile only ever waits for
-// tiles that are already running; every wait is bounded and a timeout sets an
-// error word instead of hanging.  HBM traffic is the algorithmic one (read
-// once, write once) plus a 16-byte record per tile and channel.
+// channel in registers.  A tile issues its loads, and while they are in
+// flight walks back over its predecessors' records (eight per round, one per
+// warp), composing their aggregates (the product, the sum, or the affine map
+// s -> A*s + B) until it finds one that holds its inclusive prefix.  If a
+// predecessor has published nothing yet, the tile instead publishes its own
+// aggregate as soon as its loads have landed, so that successors can look
+// past it, and then looks back again, waiting.  It then publishes its
+// inclusive prefix and writes its outputs from registers.  Tiles are numbered
+// by an atomic counter in the order blocks start, so a tile only ever waits
+// for tiles that are already running; every wait is bounded and a timeout
+// sets an error word instead of hanging.  HBM traffic is the algorithmic one
+// (read once, write once) plus a 16-byte record per tile and channel.
 #include <mutex>
 
 #include "gdn_internal.cuh"
@@ -141,44 +144,94 @@ __global__ void __launch_bounds__(256) scan_walk_kernel(ScanParams p) {
 }
 
 // ------------------------------------------------ single pass, look-back
-struct __align__(16) TileRecord {
+// A lane owns VEC consecutive channels (VEC = 4: 16-byte loads and stores);
+// its look-back record carries one flag for all of them.
+template <int VEC> struct __align__(16) TileRecord {
     unsigned int flag;  // 0 empty, 1 aggregate (A, B) ready, 2 inclusive prefix P ready too
-    float A, B;         // the tile's aggregate map (never rewritten once flag is set)
-    float P;            // the carried value after the tile
+    float A[VEC], B[VEC];  // the tile's aggregate maps (never rewritten once flag is set)
+    float P[VEC];          // the carried values after the tile
 };
 
 struct Lookback {
     unsigned int *counter;  // tile ticket, zeroed before the launch
     int *err;               // set when a wait runs out
-    TileRecord *rec;        // [ntiles][32], zeroed before the launch
+    void *rec;              // [ntiles][32] TileRecord<VEC>, zeroed before the launch
     long long nct, ntr, batch;
+    unsigned int first_spin;  // polls per record in the overlapped first look-back pass
 };
 
 constexpr uint32_t SPIN_LIMIT = 1u << 22;
+// Polls of an unpublished record in the first (overlapped) look-back pass
+// before a tile falls back to publishing its aggregate.  Worth waiting for
+// when many independent chains separate a tile from its predecessor (the
+// predecessor has usually finished); with few chains the predecessors run
+// concurrently and publishing the aggregate at once lets the chain advance.
+__host__ __device__ constexpr uint32_t first_spin(long long chains) { return chains >= 64 ? 16u : 0u; }
 
-__device__ __forceinline__ unsigned int ld_flag(const TileRecord *r) {
-    return *reinterpret_cast<const volatile unsigned int *>(&r->flag);
+template <int VEC> __device__ __forceinline__ unsigned int ld_flag(const TileRecord<VEC> *r) {
+    unsigned int f;
+    asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(f) : "l"(&r->flag) : "memory");
+    return f;
 }
 
-__device__ __forceinline__ void publish_aggregate(TileRecord *r, float A, float B) {
-    *reinterpret_cast<volatile float *>(&r->A) = A;
-    *reinterpret_cast<volatile float *>(&r->B) = B;
-    __threadfence();
-    *reinterpret_cast<volatile unsigned int *>(&r->flag) = 1u;
-}
-__device__ __forceinline__ void publish_prefix(TileRecord *r, float P) {
-    *reinterpret_cast<volatile float *>(&r->P) = P;
-    __threadfence();
-    *reinterpret_cast<volatile unsigned int *>(&r->flag) = 2u;
+// Records are published with release stores of the flag (readers acquire the
+// flag, then read the values): flag 1 = aggregate maps, flag 2 = aggregate
+// maps and inclusive prefix.
+template <int VEC>
+__device__ __forceinline__ void publish(TileRecord<VEC> *r, const float *A, const float *B, const float *P,
+                                        unsigned int flag) {
+#pragma unroll
+    for (int k = 0; k < VEC; ++k) {
+        r->A[k] = A[k];
+        r->B[k] = B[k];
+        if (flag == 2u) r->P[k] = P[k];
+    }
+    asm volatile("st.release.gpu.global.u32 [%0], %1;" ::"l"(&r->flag), "r"(flag) : "memory");
 }
 
-template <int OP, int ODT, int SDT, int RPW>
-__global__ void __launch_bounds__(256) scan_lookback_kernel(ScanParams p, Lookback lb) {
-    constexpr int NIN = Nin<OP>::n, TROWS = 8 * RPW;
+// VEC consecutive fp32 values at p (16-byte aligned when VEC = 4).  The loads
+// are volatile so they stay ahead of the look-back, which overlaps them.
+template <int VEC> __device__ __forceinline__ void ldv(const float *p, float *v) {
+    if (VEC == 4) {
+        asm volatile("ld.global.nc.v4.f32 {%0, %1, %2, %3}, [%4];"
+                     : "=f"(v[0]), "=f"(v[1]), "=f"(v[2]), "=f"(v[3])
+                     : "l"(p));
+    } else {
+        asm volatile("ld.global.nc.f32 %0, [%1];" : "=f"(v[0]) : "l"(p));
+    }
+}
+template <int ODT, int VEC> __device__ __forceinline__ void stv(void *base, size_t idx, const float *v) {
+    using O = Store<ODT>;
+    typename O::T *out = reinterpret_cast<typename O::T *>(base) + idx;
+    if (VEC == 4 && ODT == KAI_GDN_F32) {
+        *reinterpret_cast<float4 *>(out) = make_float4(v[0], v[1], v[2], v[3]);
+    } else if (VEC == 4) {
+        uint2 u;
+        typename O::T *h = reinterpret_cast<typename O::T *>(&u);
+#pragma unroll
+        for (int k = 0; k < 4; ++k) O::store(h + k, v[k]);
+        *reinterpret_cast<uint2 *>(out) = u;
+    } else {
+        O::store(out, v[0]);
+    }
+}
+
+// Tile: W*RPW rows x 32*VEC channels of one batch; warp w holds rows
+// row0 + w*RPW .. + RPW-1, lane l channels l*VEC .. l*VEC + VEC-1.
+// Order of work: issue the tile's loads; while they are in flight, try to find
+// the carry into the tile from the predecessors' records (composing their
+// aggregate maps until one holds its inclusive prefix, giving up at a record
+// not yet published); reduce the tile; if the carry is still unknown, publish
+// the tile's aggregate and look back again, waiting this time; publish the
+// inclusive prefix and write the outputs from registers.
+template <int OP, int ODT, int SDT, int VEC, int RPW, int W>
+__global__ void __launch_bounds__(32 * W, 16 / W) scan_lookback_kernel(ScanParams p, Lookback lb) {
+    constexpr int NIN = Nin<OP>::n, TROWS = W * RPW, TC = 32 * VEC;
+    using Rec = TileRecord<VEC>;
     __shared__ long long s_tile;
-    __shared__ float s_A[8][32], s_B[8][32], s_carry[32], s_tile_agg[2][32], s_acc[2][32];
-    __shared__ float s_rA[8][32], s_rB[8][32], s_rP[8][32];
-    __shared__ unsigned int s_rf[8][32];
+    __shared__ float s_A[W][TC], s_B[W][TC], s_carry[TC], s_acc[2][TC];
+    __shared__ float s_rA[W][TC], s_rB[W][TC], s_rP[W][TC];
+    __shared__ unsigned int s_rf[W][32];
     __shared__ int s_done[32];
     const int lane = threadIdx.x % 32, w = threadIdx.x / 32;
     if (threadIdx.x == 0) s_tile = (long long)atomicAdd(lb.counter, 1u);
@@ -186,123 +239,226 @@ __global__ void __launch_bounds__(256) scan_lookback_kernel(ScanParams p, Lookba
     const long long id = s_tile;
     const long long chains = lb.batch * lb.nct;
     const long long tr = id / chains, chain = id % chains, b = chain / lb.nct, ct = chain % lb.nct;
-    const long long c = ct * 32 + lane;
+    const long long c = ct * TC + (long long)lane * VEC;  // first channel of this lane
     const bool live_c = c < p.ch;
     const long long row0 = tr * TROWS + (long long)w * RPW;
-    const size_t base = (size_t)b * p.seq * p.ch + (size_t)c;
+    Rec *rec = static_cast<Rec *>(lb.rec);
 
     // rows of this thread that exist (the last tile of a sequence is ragged)
     const int nrow = live_c ? (int)max(0ll, min((long long)RPW, p.seq - row0)) : 0;
-    const size_t first = base + (size_t)row0 * p.ch;
+    const size_t first = (size_t)b * p.seq * p.ch + (size_t)row0 * p.ch + (size_t)c;
     const size_t stride = (size_t)p.ch;
-    float v[RPW][NIN];
+    float v[RPW][NIN][VEC];
 #pragma unroll
     for (int r = 0; r < RPW; ++r) {
         if (r < nrow) {
-            float t4[4];
-            load_row<OP>(p, first + (size_t)r * stride, t4);
-#pragma unroll
-            for (int k = 0; k < NIN; ++k) v[r][k] = t4[k];
+            const size_t idx = first + (size_t)r * stride;
+            ldv<VEC>(p.x + idx, v[r][0]);
+            if (OP == AFFINE || OP == GDN2) ldv<VEC>(p.g + idx, v[r][1]);
+            if (OP == GDN2) {
+                ldv<VEC>(p.b + idx, v[r][2]);
+                ldv<VEC>(p.w + idx, v[r][3]);
+            }
         }
     }
-    Agg a = agg_identity<OP>();
-#pragma unroll
-    for (int r = 0; r < RPW; ++r)
-        if (r < nrow) a = agg_push<OP>(a, v[r]);
-    s_A[w][lane] = a.A;
-    s_B[w][lane] = a.B;
-    __syncthreads();
 
-    // Tile aggregate per channel, published at once so that successors can
-    // look past this tile while it looks back itself.
-    if (w == 0) {
-        Agg tile = agg_identity<OP>();
+    // Walk back over the predecessors' records, W per round (one per warp),
+    // nearest first, composing aggregate maps until one holds its inclusive
+    // prefix.  With `blocking` false a record that is not published yet ends
+    // the walk without a result (first pass, while this tile's loads are in
+    // flight); with `blocking` true every wait is bounded by SPIN_LIMIT.
+    auto look_back = [&](bool blocking) {
+        if (w == 0) {
 #pragma unroll
-        for (int ww = 0; ww < 8; ++ww) tile = agg_then<OP>(tile, {s_A[ww][lane], s_B[ww][lane]});
-        s_tile_agg[0][lane] = tile.A;
-        s_tile_agg[1][lane] = tile.B;
-        if (tr == 0) s_carry[lane] = live_c ? initial_carry<OP, SDT>(p, b, c) : 0.0f;
-        else publish_aggregate(lb.rec + (size_t)id * 32 + lane, tile.A, tile.B);
-        s_acc[0][lane] = 1.0f;  // composed maps of the predecessors walked so far
-        s_acc[1][lane] = 0.0f;
-        s_done[lane] = tr == 0;
-    }
-    __syncthreads();
-    // Look back 8 predecessors per round, one per warp, nearest first.
-    for (long long base = tr - 1; base >= 0; base -= 8) {
-        if (__syncthreads_and(s_done[lane] != 0) ) break;
-        const long long k = base - w;
-        unsigned int f = 2u;
-        float pA = 1.0f, pB = 0.0f, pP = 0.0f;
-        if (k >= 0 && !s_done[lane]) {
-            const TileRecord *pr = lb.rec + (size_t)(k * chains + chain) * 32 + lane;
-            f = 0;
-            for (uint32_t it = 0; it < SPIN_LIMIT; ++it) {
-                f = ld_flag(pr);
-                if (f) break;
-                __nanosleep(32);
+            for (int k = 0; k < VEC; ++k) {
+                const int cc = lane * VEC + k;
+                if (tr == 0) s_carry[cc] = live_c ? initial_carry<OP, SDT>(p, b, c + k) : 0.0f;
+                s_acc[0][cc] = 1.0f;  // composed maps of the predecessors walked so far
+                s_acc[1][cc] = 0.0f;
             }
-            if (!f) {
-                atomicExch(lb.err, 1);
-                f = 2u;  // give up on this chain: treat as a prefix of 0
-            }
-            __threadfence();
-            pA = *reinterpret_cast<const volatile float *>(&pr->A);
-            pB = *reinterpret_cast<const volatile float *>(&pr->B);
-            pP = *reinterpret_cast<const volatile float *>(&pr->P);
+            s_done[lane] = tr == 0 ? 1 : 0;  // 1 carry known, 2 gave up (blocking == false)
         }
-        s_rf[w][lane] = f;
-        s_rA[w][lane] = pA;
-        s_rB[w][lane] = pB;
-        s_rP[w][lane] = pP;
         __syncthreads();
-        if (w == 0 && !s_done[lane]) {
-            Agg acc = {s_acc[0][lane], s_acc[1][lane]};
-            for (int ww = 0; ww < 8; ++ww) {
-                if (base - ww < 0) break;
-                if (s_rf[ww][lane] == 2u) {
-                    s_carry[lane] = agg_apply<OP>(acc, s_rP[ww][lane]);
-                    s_done[lane] = 1;
-                    break;
-                }
-                acc = agg_then<OP>({s_rA[ww][lane], s_rB[ww][lane]}, acc);
+        for (long long base = tr - 1; base >= 0; base -= W) {
+            if (__syncthreads_and(s_done[lane] != 0)) break;
+            const long long kt = base - w;
+            unsigned int f = 2u;
+            float pA[VEC], pB[VEC], pP[VEC];
+#pragma unroll
+            for (int k = 0; k < VEC; ++k) {
+                pA[k] = 1.0f;
+                pB[k] = 0.0f;
+                pP[k] = 0.0f;
             }
-            s_acc[0][lane] = acc.A;
-            s_acc[1][lane] = acc.B;
+            if (kt >= 0 && !s_done[lane]) {
+                const Rec *pr = rec + (size_t)(kt * chains + chain) * 32 + lane;
+                f = ld_flag<VEC>(pr);
+                for (uint32_t it = 0; !f && it < (blocking ? SPIN_LIMIT : lb.first_spin); ++it) {
+                    __nanosleep(32);
+                    f = ld_flag<VEC>(pr);
+                }
+                if (blocking) {
+                    if (!f) {
+                        atomicExch(lb.err, 1);
+                        f = 2u;  // give up on this chain: treat as a prefix of 0
+                    }
+                }
+                if (f) {
+#pragma unroll
+                    for (int k = 0; k < VEC; ++k) {
+                        pA[k] = pr->A[k];
+                        pB[k] = pr->B[k];
+                        pP[k] = pr->P[k];
+                    }
+                }
+            }
+            s_rf[w][lane] = f;
+#pragma unroll
+            for (int k = 0; k < VEC; ++k) {
+                s_rA[w][lane * VEC + k] = pA[k];
+                s_rB[w][lane * VEC + k] = pB[k];
+                s_rP[w][lane * VEC + k] = pP[k];
+            }
+            __syncthreads();
+            if (w == 0 && !s_done[lane]) {
+                Agg acc[VEC];
+#pragma unroll
+                for (int k = 0; k < VEC; ++k) acc[k] = {s_acc[0][lane * VEC + k], s_acc[1][lane * VEC + k]};
+                for (int ww = 0; ww < W; ++ww) {
+                    if (base - ww < 0) break;
+                    const unsigned int fw = s_rf[ww][lane];
+                    if (fw == 0u) {  // not published yet (first pass only)
+                        s_done[lane] = 2;
+                        break;
+                    }
+                    if (fw == 2u) {
+#pragma unroll
+                        for (int k = 0; k < VEC; ++k)
+                            s_carry[lane * VEC + k] = agg_apply<OP>(acc[k], s_rP[ww][lane * VEC + k]);
+                        s_done[lane] = 1;
+                        break;
+                    }
+#pragma unroll
+                    for (int k = 0; k < VEC; ++k)
+                        acc[k] = agg_then<OP>({s_rA[ww][lane * VEC + k], s_rB[ww][lane * VEC + k]}, acc[k]);
+                }
+#pragma unroll
+                for (int k = 0; k < VEC; ++k) {
+                    s_acc[0][lane * VEC + k] = acc[k].A;
+                    s_acc[1][lane * VEC + k] = acc[k].B;
+                }
+            }
         }
+        __syncthreads();
+    };
+    look_back(false);  // overlaps this tile's loads
+    // The tile's own aggregate (the loads land here).
+#pragma unroll
+    for (int k = 0; k < VEC; ++k) {
+        Agg a = agg_identity<OP>();
+#pragma unroll
+        for (int r = 0; r < RPW; ++r)
+            if (r < nrow) {
+                float e[4];
+#pragma unroll
+                for (int q = 0; q < NIN; ++q) e[q] = v[r][q][k];
+                a = agg_push<OP>(a, e);
+            }
+        s_A[w][lane * VEC + k] = a.A;
+        s_B[w][lane * VEC + k] = a.B;
     }
     __syncthreads();
-    if (w == 0)
-        publish_prefix(lb.rec + (size_t)id * 32 + lane,
-                       agg_apply<OP>({s_tile_agg[0][lane], s_tile_agg[1][lane]}, s_carry[lane]));
-    float run = s_carry[lane];
-    for (int ww = 0; ww < w; ++ww) run = agg_apply<OP>({s_A[ww][lane], s_B[ww][lane]}, run);
-    using O = Store<ODT>;
-    typename O::T *out = reinterpret_cast<typename O::T *>(p.out);
+    const bool known = __syncthreads_and(s_done[lane] == 1);
+    float tA[VEC], tB[VEC];
+    if (w == 0) {
+#pragma unroll
+        for (int k = 0; k < VEC; ++k) {
+            const int cc = lane * VEC + k;
+            Agg tile = agg_identity<OP>();
+#pragma unroll
+            for (int ww = 0; ww < W; ++ww) tile = agg_then<OP>(tile, {s_A[ww][cc], s_B[ww][cc]});
+            tA[k] = tile.A;
+            tB[k] = tile.B;
+        }
+        // Successors can look past this tile while it is still looking back.
+        if (!known) publish<VEC>(rec + (size_t)id * 32 + lane, tA, tB, tB, 1u);
+    }
+    if (!known) look_back(true);
+    if (w == 0) {
+        float P[VEC];
+#pragma unroll
+        for (int k = 0; k < VEC; ++k) P[k] = agg_apply<OP>({tA[k], tB[k]}, s_carry[lane * VEC + k]);
+        publish<VEC>(rec + (size_t)id * 32 + lane, tA, tB, P, 2u);
+    }
+    float run[VEC];
+#pragma unroll
+    for (int k = 0; k < VEC; ++k) {
+        const int cc = lane * VEC + k;
+        run[k] = s_carry[cc];
+        for (int ww = 0; ww < w; ++ww) run[k] = agg_apply<OP>({s_A[ww][cc], s_B[ww][cc]}, run[k]);
+    }
 #pragma unroll
     for (int r = 0; r < RPW; ++r) {
         if (r < nrow) {
-            run = step<OP>(run, v[r]);
-            O::store(out + first + (size_t)r * stride, run);
+            const size_t o = first + (size_t)r * stride;
+#pragma unroll
+            for (int k = 0; k < VEC; ++k) {
+                float e[4];
+#pragma unroll
+                for (int q = 0; q < NIN; ++q) e[q] = v[r][q][k];
+                run[k] = step<OP>(run[k], e);
+            }
+            stv<ODT, VEC>(p.out, o, run);
             if ((OP == AFFINE || OP == GDN2) && row0 + r == p.seq - 1) {
                 using S = Store<SDT>;
-                S::store(reinterpret_cast<typename S::T *>(p.state) + b * p.ch + c, run);
+#pragma unroll
+                for (int k = 0; k < VEC; ++k)
+                    S::store(reinterpret_cast<typename S::T *>(p.state) + b * p.ch + c + k, run[k]);
             }
         }
     }
 }
 
-template <int OP> constexpr int rows_per_warp() { return OP == GDN2 ? 16 : 32; }
+// Geometry of a look-back launch: channels per lane, rows per warp, warps.
+struct Geo {
+    int vec, rpw, w;
+};
+// 8 warps of 32 rows (16 for gdn2) x 32 channels: 256-row tiles (128 for gdn2),
+// one 128-byte line per warp and row.  Measured on B200 against taller,
+// shorter and four-channels-per-lane tiles, this keeps the most tiles of
+// independent chains in flight per SM.  The allocation-free entry point uses
+// it too, so its scratch bound is fixed.
+template <int OP> constexpr Geo narrow_geo() { return {1, OP == GDN2 ? 16 : 32, 8}; }
 
 // Scratch bytes of a look-back launch: ticket + error word, then the records.
-size_t lookback_bytes(size_t batch, long long seq, long long ch, int rpw) {
-    const long long ntr = (seq + 8 * rpw - 1) / (8 * rpw), nct = (ch + 31) / 32;
-    return 256 + (size_t)ntr * (size_t)nct * batch * 32 * sizeof(TileRecord);
+size_t lookback_bytes(size_t batch, long long seq, long long ch, Geo g) {
+    const long long ntr = (seq + g.w * g.rpw - 1) / (g.w * g.rpw), nct = (ch + 32 * g.vec - 1) / (32 * g.vec);
+    const size_t rec = g.vec == 4 ? sizeof(TileRecord<4>) : sizeof(TileRecord<1>);
+    return 256 + (size_t)ntr * (size_t)nct * batch * 32 * rec;
+}
+
+template <int OP, int ODT, int SDT, int VEC, int RPW, int W>
+int launch_lookback(ScanParams p, size_t batch, cudaStream_t st, const char *name, void *scratch) {
+    constexpr Geo g{VEC, RPW, W};
+    Lookback lb;
+    lb.ntr = (p.seq + W * RPW - 1) / (W * RPW);
+    lb.nct = (p.ch + 32 * VEC - 1) / (32 * VEC);
+    lb.batch = (long long)batch;
+    lb.first_spin = first_spin(lb.nct * lb.batch);
+    const long long tiles = lb.ntr * lb.nct * lb.batch;
+    if (tiles > 0x7fffffffll) return set_error(KAI_GDN_ERR_UNSUPPORTED, "%s: shape too large", name);
+    const size_t bytes = lookback_bytes(batch, p.seq, p.ch, g);
+    int rc = check_cuda(cudaMemsetAsync(scratch, 0, bytes, st), name);
+    if (rc) return rc;
+    lb.counter = static_cast<unsigned int *>(scratch);
+    lb.err = reinterpret_cast<int *>(static_cast<char *>(scratch) + 16);
+    lb.rec = static_cast<char *>(scratch) + 256;
+    scan_lookback_kernel<OP, ODT, SDT, VEC, RPW, W><<<(unsigned)tiles, 32 * W, 0, st>>>(p, lb);
+    return check_launch(name);
 }
 
 template <int OP, int ODT, int SDT>
 int run_scan_with(ScanParams p, size_t batch, cudaStream_t st, const char *name, void *scratch) {
-    constexpr int RPW = rows_per_warp<OP>();
     if (p.seq <= SEG_LEN) {
         if (batch > 65535) return set_error(KAI_GDN_ERR_UNSUPPORTED, "%s: batch %zu > 65535", name, batch);
         long long gx = (p.ch + 255) / 256;
@@ -310,27 +466,15 @@ int run_scan_with(ScanParams p, size_t batch, cudaStream_t st, const char *name,
         scan_walk_kernel<OP, ODT, SDT><<<dim3((unsigned)gx, 1, (unsigned)batch), dim3(32, 8), 0, st>>>(p);
         return check_launch(name);
     }
-    Lookback lb;
-    lb.ntr = (p.seq + 8 * RPW - 1) / (8 * RPW);
-    lb.nct = (p.ch + 31) / 32;
-    lb.batch = (long long)batch;
-    const long long tiles = lb.ntr * lb.nct * lb.batch;
-    if (tiles > 0x7fffffffll) return set_error(KAI_GDN_ERR_UNSUPPORTED, "%s: shape too large", name);
-    const size_t bytes = lookback_bytes(batch, p.seq, p.ch, RPW);
-    int rc = check_cuda(cudaMemsetAsync(scratch, 0, bytes, st), name);
-    if (rc) return rc;
-    lb.counter = static_cast<unsigned int *>(scratch);
-    lb.err = reinterpret_cast<int *>(static_cast<char *>(scratch) + 16);
-    lb.rec = reinterpret_cast<TileRecord *>(static_cast<char *>(scratch) + 256);
-    scan_lookback_kernel<OP, ODT, SDT, RPW><<<(unsigned)tiles, 256, 0, st>>>(p, lb);
-    return check_launch(name);
+    constexpr Geo g = narrow_geo<OP>();
+    return launch_lookback<OP, ODT, SDT, g.vec, g.rpw, g.w>(p, batch, st, name, scratch);
 }
 
 template <int OP, int ODT, int SDT>
 int run_scan(ScanParams p, size_t batch, cudaStream_t st, const char *name) {
     void *scr = nullptr;
     if (p.seq > SEG_LEN) {
-        int rc = scratch_for_stream(st, lookback_bytes(batch, p.seq, p.ch, rows_per_warp<OP>()), &scr);
+        int rc = scratch_for_stream(st, lookback_bytes(batch, p.seq, p.ch, narrow_geo<OP>()), &scr);
         if (rc) return rc;
     }
     return run_scan_with<OP, ODT, SDT>(p, batch, st, name, scr);
@@ -455,7 +599,7 @@ int run_scan_noalloc(ScanParams p, size_t batch, cudaStream_t st) {
     const char *name = "gated_scan_noalloc";
     float *scr = nullptr;
     if (p.seq > SEG_LEN) {
-        const size_t need = lookback_bytes(batch, p.seq, p.ch, rows_per_warp<AFFINE>());
+        const size_t need = lookback_bytes(batch, p.seq, p.ch, narrow_geo<AFFINE>());
         if (need > (size_t)KAI_GDN_NOALLOC_SCRATCH_BYTES)
             return set_error(KAI_GDN_ERR_INVALID,
                              "%s: batch %zu x seq %lld x channels %lld needs %zu bytes of scratch; the static "
