@@ -47,6 +47,8 @@ extern "C" {
 #define KAI_GDN_ERR_CUDA 2        /* a CUDA runtime call or a launch failed   */
 #define KAI_GDN_ERR_UNSUPPORTED 3 /* valid but not implemented (e.g. dk>256)  */
 #define KAI_GDN_ERR_NOMEM 4       /* device or pinned allocation failed       */
+#define KAI_GDN_ERR_TIMEOUT 5     /* a kernel's bounded wait ran out (see     */
+                                  /* kai_gdn_cuda_device_status)              */
 
 /* --------------------------------------------------------- storage types */
 #define KAI_GDN_F32 0
@@ -222,6 +224,17 @@ KAI_GDN_API int kai_gdn_cuda_device_count(void);
 KAI_GDN_API int kai_gdn_cuda_last_status(void);
 KAI_GDN_API const char *kai_gdn_cuda_last_error(void);
 KAI_GDN_API void kai_gdn_cuda_clear_error(void);
+
+/* Kernels that wait on work of other threads of the same kernel (the
+ * tensor-core chunk scan's hand-overs, the long scans' look-back) bound every
+ * wait; a wait that runs out records it in a word on the current device and
+ * the kernel finishes without its result.  The stream-ordered entry points
+ * return before their kernels run, so they cannot see it: this call
+ * synchronises `stream`, reads and clears the word, and returns
+ * KAI_GDN_ERR_TIMEOUT (with a message) if any wait of the kernels before it
+ * ran out, else KAI_GDN_OK.  The synchronous drop-in entry points check it
+ * themselves.  No reference counterpart (the reference has no such waits). */
+KAI_GDN_API int kai_gdn_cuda_device_status(void *stream);
 /* Library version string. */
 KAI_GDN_API const char *kai_gdn_cuda_version(void);
 

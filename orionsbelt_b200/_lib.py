@@ -11,7 +11,7 @@ from pathlib import Path
 
 LIB_PATH = Path(__file__).resolve().parent / "libkai_gdn_cuda.so"
 
-OK, ERR_INVALID, ERR_CUDA, ERR_UNSUPPORTED, ERR_NOMEM = 0, 1, 2, 3, 4
+OK, ERR_INVALID, ERR_CUDA, ERR_UNSUPPORTED, ERR_NOMEM, ERR_TIMEOUT = 0, 1, 2, 3, 4, 5
 F32, BF16, F16 = 0, 1, 2
 
 _sz = C.c_size_t
@@ -67,6 +67,7 @@ SIGNATURES = {
     "kai_gdn_cuda_last_error": (C.c_char_p, []),
     "kai_gdn_cuda_clear_error": (None, []),
     "kai_gdn_cuda_version": (C.c_char_p, []),
+    "kai_gdn_cuda_device_status": (C.c_int, [C.c_void_p]),
 }
 
 

@@ -21,6 +21,8 @@ int check_launch(const char *kernel);
 
 // Device word where kernels with bounded waits record a timeout (no allocation).
 int device_error_word(int **out);
+// Synchronise `st`, read and clear the word: KAI_GDN_ERR_TIMEOUT if it was set.
+int check_device_word(cudaStream_t st);
 
 // Number of SMs of the current device (cached per device).
 int sm_count();

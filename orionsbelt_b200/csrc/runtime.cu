@@ -56,8 +56,8 @@ int sm_count() {
 }
 
 // -------------------------------------------------------- device error word
-// Kernels with bounded waits (the tensor-core chunk scan, the bulk-copy decode
-// step) record a timeout here instead of hanging.  A file-scope device word,
+// Kernels with bounded waits (the tensor-core chunk scan, the long scans'
+// look-back) record a timeout here instead of hanging.  A file-scope device word,
 // so launching needs no allocation (and can be captured in a CUDA graph); its
 // address is looked up once per device.
 namespace {
@@ -80,6 +80,21 @@ int device_error_word(int **out) {
     }
     *out = g_errword[dev];
     return KAI_GDN_OK;
+}
+
+// Synchronise `st`, read and clear the word; KAI_GDN_ERR_TIMEOUT if it was set.
+int check_device_word(cudaStream_t st) {
+    int *w = nullptr;
+    int rc = device_error_word(&w);
+    if (rc) return rc;
+    if ((rc = check_cuda(cudaStreamSynchronize(st), "device status: synchronize"))) return rc;
+    int v = 0;
+    if ((rc = check_cuda(cudaMemcpy(&v, w, sizeof(int), cudaMemcpyDeviceToHost), "device status: read"))) return rc;
+    if (!v) return KAI_GDN_OK;
+    const int zero = 0;
+    if ((rc = check_cuda(cudaMemcpy(w, &zero, sizeof(int), cudaMemcpyHostToDevice), "device status: clear")))
+        return rc;
+    return set_error(KAI_GDN_ERR_TIMEOUT, "a bounded wait inside a kernel ran out; its outputs are not valid");
 }
 
 // ----------------------------------------------------------------- scratch
@@ -200,7 +215,8 @@ int stage_out(Arg *args, int n, cudaStream_t st) {
             if (rc) return rc;
         }
     }
-    return check_cuda(cudaStreamSynchronize(st), "stage: synchronize");
+    int rc = check_cuda(cudaStreamSynchronize(st), "stage: synchronize");
+    return rc ? rc : check_device_word(st);
 }
 
 constexpr cudaStream_t kLegacy = 0;
@@ -398,5 +414,6 @@ void kai_gdn_cuda_clear_error(void) {
     t_msg[0] = '\0';
 }
 const char *kai_gdn_cuda_version(void) { return "kai_gdn_cuda 0.1.0 (sm_100a)"; }
+int kai_gdn_cuda_device_status(void *stream) { return gdn::check_device_word((cudaStream_t)stream); }
 
 }  // extern "C"

@@ -154,7 +154,7 @@ template <int VEC> struct __align__(16) TileRecord {
 
 struct Lookback {
     unsigned int *counter;  // tile ticket, zeroed before the launch
-    int *err;               // set when a wait runs out
+    int *err;               // the library's device error word: set when a wait runs out
     void *rec;              // [ntiles][32] TileRecord<VEC>, zeroed before the launch
     long long nct, ntr, batch;
     unsigned int first_spin;  // polls per record in the overlapped first look-back pass
@@ -430,7 +430,7 @@ struct Geo {
 // it too, so its scratch bound is fixed.
 template <int OP> constexpr Geo narrow_geo() { return {1, OP == GDN2 ? 16 : 32, 8}; }
 
-// Scratch bytes of a look-back launch: ticket + error word, then the records.
+// Scratch bytes of a look-back launch: the ticket, then the records.
 size_t lookback_bytes(size_t batch, long long seq, long long ch, Geo g) {
     const long long ntr = (seq + g.w * g.rpw - 1) / (g.w * g.rpw), nct = (ch + 32 * g.vec - 1) / (32 * g.vec);
     const size_t rec = g.vec == 4 ? sizeof(TileRecord<4>) : sizeof(TileRecord<1>);
@@ -451,7 +451,8 @@ int launch_lookback(ScanParams p, size_t batch, cudaStream_t st, const char *nam
     int rc = check_cuda(cudaMemsetAsync(scratch, 0, bytes, st), name);
     if (rc) return rc;
     lb.counter = static_cast<unsigned int *>(scratch);
-    lb.err = reinterpret_cast<int *>(static_cast<char *>(scratch) + 16);
+    rc = device_error_word(&lb.err);
+    if (rc) return rc;
     lb.rec = static_cast<char *>(scratch) + 256;
     scan_lookback_kernel<OP, ODT, SDT, VEC, RPW, W><<<(unsigned)tiles, 32 * W, 0, st>>>(p, lb);
     return check_launch(name);

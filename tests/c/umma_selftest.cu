@@ -276,3 +276,22 @@ extern "C" __attribute__((visibility("default"))) int umma_selftest_tma(const vo
     e = cudaDeviceSynchronize();
     return e == cudaSuccess ? 0 : 3;
 }
+
+// A bounded mbarrier wait on a barrier nothing arrives on: the wait must run
+// out after `limit` polls, set *err and let the kernel finish.
+__global__ void timeout_kernel(int *err, int *done, unsigned limit) {
+    __shared__ __align__(8) uint64_t bar;
+    if (threadIdx.x == 0) mbar_init(&bar, 1);
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    __syncthreads();
+    const bool ok = mbar_wait(&bar, 0, err, limit);
+    if (threadIdx.x == 0) *done = ok ? 2 : 1;
+}
+
+extern "C" __attribute__((visibility("default"))) int umma_selftest_timeout(int *err, int *done) {
+    timeout_kernel<<<1, 32>>>(err, done, 1u << 12);
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return 2;
+    e = cudaDeviceSynchronize();
+    return e == cudaSuccess ? 0 : 3;
+}

@@ -100,3 +100,23 @@ def test_tc_continuity(cuda):
                          part(d["g"], 256, 512), part(d["beta"], 256, 512), S, o_b, scale=0.1)
     rl = lambda a, b: (torch.linalg.norm(a.float() - b.float()) / torch.linalg.norm(b.float())).item()  # noqa: E731
     assert rl(torch.cat([o_a, o_b], 1), o_full) < 1e-3 and rl(S, S_full) < 1e-3
+
+
+def test_no_wait_ran_out(cuda):
+    """After a chunk scan and a long look-back scan on a stream, the device
+    status query synchronises the stream and finds no bounded wait that ran
+    out (the kernels' timeout word stays clear on normal work)."""
+    from orionsbelt_b200 import _lib
+
+    dt = cuda.bfloat16
+    d = synth.host_gdn(1, 300, 2, 4, 128, 128, g_scale=0.3, seed=11, state_std=0.05)
+    S = cuda.from_numpy(d["S0"]).cuda()
+    o = cuda.empty(d["v"].shape, dtype=cuda.float32, device="cuda")
+    ops.chunk_delta_rule(_dev(cuda, d["q"], dt), _dev(cuda, d["k"], dt), _dev(cuda, d["v"], dt),
+                         cuda.from_numpy(d["g"]).cuda(), cuda.from_numpy(d["beta"]).cuda(), S, o, scale=0.088)
+    g = cuda.rand((1, 5000, 256), device="cuda")
+    x = cuda.randn((1, 5000, 256), device="cuda")
+    s = cuda.empty_like(x)
+    st = cuda.zeros((1, 256), device="cuda")
+    ops.gated_scan(g, x, s, st)
+    assert _lib.lib().kai_gdn_cuda_device_status(cuda.cuda.current_stream().cuda_stream) == _lib.OK

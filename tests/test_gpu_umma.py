@@ -150,3 +150,15 @@ def test_tma_chunk_tile(cuda, selftest2, swz, t0):
     assert rc == 0 and err.item() == 0
     got = out.cpu().numpy().view(np.uint16)
     np.testing.assert_array_equal(got, _tile_expected(x, 1, t0, 2, swz))
+
+
+def test_bounded_wait_runs_out(cuda, selftest):
+    """A wait on an mbarrier that nothing completes gives up after its poll
+    limit, records the timeout in the error word and lets the kernel finish
+    (the pattern every wait of the chunk scan uses)."""
+    selftest.umma_selftest_timeout.restype = C.c_int
+    selftest.umma_selftest_timeout.argtypes = [C.c_void_p, C.c_void_p]
+    err = cuda.zeros(1, dtype=cuda.int32, device="cuda")
+    done = cuda.zeros(1, dtype=cuda.int32, device="cuda")
+    assert selftest.umma_selftest_timeout(err.data_ptr(), done.data_ptr()) == 0
+    assert err.item() == 1 and done.item() == 1
