@@ -9,34 +9,37 @@
 //   P   = scale (q_r.k_s) exp(G_r - G_s), s <= r
 //   T   = (I + A)^-1,  Tb = T diag(beta),  Tbg = T diag(beta exp(G))
 //   V'  = Tb V - Tbg (K S)                  (= U - W S of the WY form)
-//   O   = (scale Q exp(G)) S + P V'
+//   O   = scale exp(G) (Q S) + P V'
 //   S  <- gamma S + (K exp(G_63 - G))^T V'
 // Everything except the last three lines is independent of the state, so it
 // runs one chunk AHEAD of the recurrence, in three warp groups:
 //   key group    (warps 0-7):   TMA loads, [K;Q] K^T, A and P, the inverse,
-//                               Tb / Tbg, Q -> scale Q exp(G) in place;
+//                               Tb / Tbg;
 //   state group  (warps 8-11):  the recurrence, with the state held TRANSPOSED
 //                               in TMEM (lane = value index i, column = key
 //                               index j), so every state-side MMA has M = 128
 //                               and reads the 16-bit state copy from TMEM:
-//     M3a  (K S)^T   = S^T K^T,   O^T = S^T Qg^T      A: S^T (TMEM)  B: K, Qg
+//     M3a  [(K S)^T | X^T] = S^T [K; Q]^T    one N = 128 chain, A: S^T
+//                                            (TMEM), B: the [K;Q] tile
 //     M3b  V'^T      = V^T Tb^T - (K S)^T Tbg^T
-//     M4   S^T      += (V' exp(G_63 - G))^T K,   O^T += V'^T P^T
-//   output group (warps 12-15): O^T from TMEM to global memory, off the
-//                               recurrence's critical path (O^T is double
-//                               buffered in TMEM).
+//     M4   S^T      += (V' exp(G_63 - G))^T K,   Y^T = V'^T P^T
+//   output group (warps 12-15): O = scale exp(G_r) X + Y from TMEM to global
+//                               memory, off the recurrence's critical path
+//                               (it evaluates the row factors itself).
 // The groups hand chunks over through mbarriers (key_ready / key_free,
 // o_full / o_empty); q, k, v arrive by TMA into a three-deep ring, the
-// key-side tiles are double buffered.  One CTA (512 threads, ~225 KB of shared
+// key-side tiles are double buffered.  Every MMA is issued by one elected
+// lane of a converged warp.  One CTA (512 threads, ~225 KB of shared
 // memory, all 512 TMEM columns) per (b, h); every wait is bounded (a timeout
 // sets *err and all groups leave after their outstanding copies and MMAs have
 // completed).
 //
 // TMEM columns (fp32 unless noted; "16-bit" = two values per column):
 //   [  0,128) S^T                 [128,192) S^T 16-bit (A operand)
-//   [192,256) (K S)^T, then V'^T  [256,384) O^T, two buffers
-//   [384,416) -(K S)^T 16-bit, then V'^T 16-bit    [416,448) V''^T 16-bit
-//   [448,512) [K;Q] K^T  (lanes 0-63: K K^T, 64-127: Q K^T)
+//   [192,256) (K S)^T, then V'^T, then Y^T     [256,320) X^T (M3a writes
+//             (K S)^T and X^T at once)
+//   [320,352) -(K S)^T 16-bit, then V'^T 16-bit    [352,384) V''^T 16-bit
+//   [384,448) [K;Q] K^T  (lanes 0-63: K K^T, 64-127: Q K^T)
 // Shared memory: per input stage K and Q interleaved by 64-feature block
 // ([K blk0 | Q blk0 | K blk1 | Q blk1], 128-byte swizzle, so [K;Q] is one
 // M = 128 operand) and V (128-byte swizzle); per key stage P, Tb, Tbg (no
@@ -54,8 +57,9 @@ constexpr int C = 64, D = 128;
 constexpr int KG = 256, SG = 128, OG = 128, NT = KG + SG + OG;
 constexpr int NS_IN = 3, NS_K = 2;
 
-constexpr uint32_t COL_ST = 0, COL_SB = 128, COL_VA = 192, COL_OA = 256, COL_KSB = 384, COL_VB = 384,
-                   COL_VB2 = 416, COL_KQ = 448;
+constexpr uint32_t COL_ST = 0, COL_SB = 128, COL_VA = 192, COL_OA = 256, COL_KSB = 320, COL_VB = 320,
+                   COL_VB2 = 352, COL_KQ = 384;
+static_assert(COL_OA == COL_VA + 64, "M3a writes (K S)^T and O^T as one N = 128 accumulator");
 
 // Block-packed lower triangle of a 64 x 64 fp32 matrix: the ten 16 x 16
 // blocks (bi >= bj) at id = bi(bi+1)/2 + bj, rows padded to 20 floats.
@@ -85,7 +89,8 @@ struct WsSmem {
     Factors fac[NS_F];
     float Af[10 * BSZ];
     float Tf[10 * BSZ];
-    uint64_t full_in[NS_IN], key_ready[NS_K], key_free[NS_K], o_full[2], o_empty[2], bar_k, bar_s;
+    float ofs[2][C];  // scale exp(G_r) of the chunk the output group writes
+    uint64_t full_in[NS_IN], key_ready[NS_K], key_free[NS_K], o_full, o_empty, bar_k, bar_s;
     uint32_t tmem;
     int stop;
 };
@@ -263,39 +268,63 @@ __device__ __forceinline__ void store16(float *__restrict__ Z, const float (&acc
     }
 }
 
-// Runs on key-group warps 0-3 (t < 128).
-__device__ void invert_unit_lower(float *__restrict__ A, float *__restrict__ T, int t) {
+// Tb / Tbg entries of the 16 x 16 block (bi, bj) of T, held as an m16n8
+// accumulator pair times `sign`, rounded straight into the operand tiles.
+template <typename IT>
+__device__ __forceinline__ void store_tb16(KeyStage &ks, const Factors &fa, const float (&acc)[2][4], float sign,
+                                           int bi, int bj, Frag f) {
+#pragma unroll
+    for (int nn = 0; nn < 2; ++nn) {
+        const int s = 16 * bj + 8 * nn + 2 * f.q;
+        const float b0 = fa.beta[s], b1 = fa.beta[s + 1];
+        const float g0 = b0 * fa.eG[s], g1 = b1 * fa.eG[s + 1];
+#pragma unroll
+        for (int hh = 0; hh < 2; ++hh) {
+            const int r = 16 * bi + f.g + 8 * hh;
+            const float x0 = sign * acc[nn][2 * hh], x1 = sign * acc[nn][2 * hh + 1];
+            *reinterpret_cast<uint32_t *>(ks.Tb + kmaj16(r, s, C)) = pack2<IT>(x0 * b0, x1 * b1);
+            *reinterpret_cast<uint32_t *>(ks.Tbg + kmaj16(r, s, C)) = pack2<IT>(x0 * g0, x1 * g1);
+        }
+    }
+}
+
+// Runs on key-group warps 0-3 (t < 128).  The last step's four blocks go
+// straight into Tb / Tbg; the others stay in T for the helper warps.
+template <typename IT>
+__device__ __forceinline__ void invert_unit_lower(float *__restrict__ A, float *__restrict__ T, KeyStage &ks,
+                                                  const Factors &fa,
+                                  int t) {
     const int warp = t / 32;
     const Frag f{(t % 32) / 4, t % 4};
     auto MB = [&](int n) { return A + blk(n, n); };
     if (t < 64) {
-        // column j of T_bb: x_r = delta_rj - sum_{k<r} A_rk x_k  (x_k = 0 for k < j);
-        // the next row of A is loaded while the current one is reduced.
+        // column j of T_bb by substitution, right-looking in panels of four
+        // columns: once s_k (k in the panel) is final it is x_k, and the rows
+        // below take the panel's update as one 4-term dot product.  x_k = 0
+        // for k < j without special cases (s starts as e_j).
         const int bb = t / 16, j = t % 16, o = blk(bb, bb);
-        float x[16];
-        float4 cur[4], nxt[4];
+        float sx[16];
 #pragma unroll
-        for (int q = 0; q < 4; ++q) cur[q] = *reinterpret_cast<const float4 *>(A + o + 1 * BLD + 4 * q);
-        x[0] = j == 0 ? 1.f : 0.f;
+        for (int r = 0; r < 16; ++r) sx[r] = r == j ? 1.f : 0.f;
 #pragma unroll
-        for (int r = 1; r < 16; ++r) {
-            if (r + 1 < 16)
+        for (int pn = 0; pn < 4; ++pn) {
+            float4 a[16];
 #pragma unroll
-                for (int q = 0; q < 4; ++q) nxt[q] = *reinterpret_cast<const float4 *>(A + o + (r + 1) * BLD + 4 * q);
-            float s[4] = {0.f, 0.f, 0.f, 0.f};
+            for (int r = 4 * pn + 1; r < 16; ++r) a[r] = *reinterpret_cast<const float4 *>(A + o + r * BLD + 4 * pn);
 #pragma unroll
-            for (int k = 0; k < r; ++k) {
-                const float4 a4 = cur[k / 4];
-                const float a = (k % 4 == 0) ? a4.x : (k % 4 == 1) ? a4.y : (k % 4 == 2) ? a4.z : a4.w;
-                s[k % 4] = fmaf(a, x[k], s[k % 4]);
+            for (int u = 1; u < 4; ++u) {
+                const int r = 4 * pn + u;
+                const float av[4] = {a[r].x, a[r].y, a[r].z, a[r].w};
+#pragma unroll
+                for (int w = 0; w < u; ++w) sx[r] = fmaf(-av[w], sx[4 * pn + w], sx[r]);
             }
-            x[r] = r < j ? 0.f : (r == j ? 1.f : -((s[0] + s[1]) + (s[2] + s[3])));
-            if (r + 1 < 16)
 #pragma unroll
-                for (int q = 0; q < 4; ++q) cur[q] = nxt[q];
+            for (int r = 4 * pn + 4; r < 16; ++r)
+                sx[r] -= fmaf(a[r].x, sx[4 * pn],
+                              fmaf(a[r].y, sx[4 * pn + 1], fmaf(a[r].z, sx[4 * pn + 2], a[r].w * sx[4 * pn + 3])));
         }
 #pragma unroll
-        for (int r = 0; r < 16; ++r) T[o + r * BLD + j] = x[r];
+        for (int r = 0; r < 16; ++r) T[o + r * BLD + j] = sx[r];
     }
     inv_sync();
     if (warp < 2) {  // L1 for the pair (b0 + 1, b0), b0 = 2 * warp
@@ -324,7 +353,7 @@ __device__ void invert_unit_lower(float *__restrict__ A, float *__restrict__ T, 
         float acc[2][4] = {};
         mma16(acc, T + blk(2 + tr, 2), MB(tc), f);
         if (tr == 1) mma16(acc, T + blk(3, 3), MB(2 + tc), f);
-        store16(T + blk(2 + tr, tc), acc, -1.f, f);
+        store_tb16<IT>(ks, fa, acc, -1.f, 2 + tr, tc, f);
     }
 }
 
@@ -346,19 +375,13 @@ __device__ __forceinline__ void tb_chunk(const float *Tf, KeyStage &ks, const Fa
     st_vec8<IT>(ks.Tb, kmaj16(r, s0, C), a);
     st_vec8<IT>(ks.Tbg, kmaj16(r, s0, C), g8);
 }
-// Chunk e of the Tb / Tbg blocks that become final together:
-//   early (e < 192): the diagonal blocks and T10, T32;   late (e < 128): T20, T21, T30, T31.
+// Chunk e (< 192) of the Tb / Tbg blocks the inverse finishes early: the
+// diagonal blocks and T10, T32 (the last step writes its own blocks).
 template <typename IT>
-__device__ __forceinline__ void tb_blocks(const float *Tf, KeyStage &ks, const Factors &fa, bool late, int e) {
+__device__ __forceinline__ void tb_blocks(const float *Tf, KeyStage &ks, const Factors &fa, int e) {
     const int n = e / 32, row = (e % 32) / 2, half = e % 2;
-    int bi, bj;
-    if (late) {
-        bi = 2 + n / 2;
-        bj = n % 2;
-    } else {
-        bi = n < 4 ? n : (n == 4 ? 1 : 3);
-        bj = n < 4 ? n : (n == 4 ? 0 : 2);
-    }
+    const int bi = n < 4 ? n : (n == 4 ? 1 : 3);
+    const int bj = n < 4 ? n : (n == 4 ? 0 : 2);
     tb_chunk<IT>(Tf, ks, fa, 16 * bi + row, 16 * bj + 8 * half);
 }
 
@@ -469,6 +492,20 @@ __device__ __forceinline__ float chunk_gamma(const Gates &gt, int lane) {
     return expf(__shfl_sync(0xffffffffu, incl, 31));
 }
 
+// scale exp(G_r) for the tokens r = 2 lane, 2 lane + 1 of the chunk whose
+// gates the lane holds (the same sums as chunk_gates), into ofs[r].
+__device__ __forceinline__ void out_scales(float *ofs, const Gates &gt, float scale, int lane) {
+    const float pair = gt.g0 + gt.g1;
+    float incl = pair;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+        const float u = __shfl_up_sync(0xffffffffu, incl, o);
+        if (lane >= o) incl += u;
+    }
+    const float G0 = (incl - pair) + gt.g0, G1 = incl;
+    *reinterpret_cast<float2 *>(ofs + 2 * lane) = make_float2(scale * expf(G0), scale * expf(G1));
+}
+
 __device__ __forceinline__ float ex2(float x) {
     float y;
     asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
@@ -480,8 +517,10 @@ template <typename IT>
 __global__ void __launch_bounds__(NT, 1)
     chunk_ws_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_constant__ CUtensorMap map_k,
                     const __grid_constant__ CUtensorMap map_v, kai_gdn_chunk_args p, int *err) {
+    // 1024-byte aligned by pointer arithmetic on the shared array itself, so
+    // the compiler keeps every access in the shared address space.
     extern __shared__ unsigned char smem_raw[];
-    WsSmem &sm = *reinterpret_cast<WsSmem *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    WsSmem &sm = *reinterpret_cast<WsSmem *>(smem_raw + ((1024u - (umma::smem_addr(smem_raw) & 1023u)) & 1023u));
     using TR = InT<IT>;
 
     const int t = threadIdx.x, warp = t / 32, lane = t % 32;
@@ -497,10 +536,8 @@ __global__ void __launch_bounds__(NT, 1)
             mbar_init(&sm.key_ready[s], 1);
             mbar_init(&sm.key_free[s], 1);
         }
-        for (int s = 0; s < 2; ++s) {
-            mbar_init(&sm.o_full[s], 1);
-            mbar_init(&sm.o_empty[s], 1);
-        }
+        mbar_init(&sm.o_full, 1);
+        mbar_init(&sm.o_empty, 1);
         mbar_init(&sm.bar_k, 1);
         mbar_init(&sm.bar_s, 1);
         sm.stop = 0;
@@ -547,22 +584,26 @@ __global__ void __launch_bounds__(NT, 1)
     if (t < KG) {
         // =============================================================== key group
         // Per chunk c:  all 8 warps: E1 (A and P from [K;Q] K^T);
-        //   warps 0-3: the inverse;
-        //   warps 4-7 meanwhile: Q -> scale Q exp(G), the gates of chunk c+1,
-        //     the TMA loads and the [K;Q] K^T MMA of chunk c+1 (thread KT),
-        //     and Tb / Tbg of the blocks the inverse has finished;
-        //   all: Tb / Tbg of the last four blocks, then hand the chunk over.
-        constexpr int KT = 224, GW = 4;  // MMA / TMA thread; the warp computing gates
+        //   warps 0-3: the inverse, whose last step writes its four blocks
+        //     of Tb / Tbg directly;
+        //   warps 4-7 meanwhile: the gates of chunk c+1, the [K;Q] K^T MMA
+        //     of chunk c+1 (warp KW), and Tb / Tbg of the blocks the inverse
+        //     finished early;
+        //   then hand the chunk over.
+        constexpr int KT = 224, KW = KT / 32, GW = 4;  // TMA thread and its warp (MMA); the warp computing gates
         int loaded = 0;  // chunks whose loads were issued (thread KT)
         bool fail = false;  // a wait of this thread ran out
-        auto issue_m1 = [&](int cc) {  // thread KT, loads of chunk cc complete
+        auto issue_m1 = [&](int cc) {  // warp KW (converged), loads of chunk cc complete
             fence_after_sync();
-            const uint32_t id = idesc(128, 64, TR::fmt, false, false);
-            const unsigned char *kq = sm.in[cc % NS_IN].KQ;
+            if (elect_one()) {
+                const uint32_t id = idesc(128, 64, TR::fmt, false, false);
+                const unsigned char *kq = sm.in[cc % NS_IN].KQ;
 #pragma unroll
-            for (int ks = 0; ks < D / 16; ++ks)
-                mma_f16(tm + COL_KQ, desc_kq_kmaj(kq, 0, ks), desc_kq_kmaj(kq, 0, ks), id, ks > 0);
-            commit(&sm.bar_k);
+                for (int ks = 0; ks < D / 16; ++ks)
+                    mma_f16(tm + COL_KQ, desc_kq_kmaj(kq, 0, ks), desc_kq_kmaj(kq, 0, ks), id, ks > 0);
+                commit(&sm.bar_k);
+            }
+            __syncwarp();
         };
         // The upper blocks of Tb / Tbg stay zero; write them once.
         for (int e = t; e < NS_K * 2 * 6 * 32; e += KG) {
@@ -576,6 +617,8 @@ __global__ void __launch_bounds__(NT, 1)
         if (t == KT && nch > 0) {
             issue_loads(0);
             loaded = 1;
+        }
+        if (warp == KW && nch > 0) {
             if (!mbar_wait(&sm.full_in[0], 0, err)) fail = true;
             issue_m1(0);
         }
@@ -589,7 +632,6 @@ __global__ void __launch_bounds__(NT, 1)
         int c = 0;
         for (; c < nch; ++c) {
             const int si = c % NS_IN, sk = c % NS_K;
-            InStage &ist = sm.in[si];
             KeyStage &kst = sm.ks[sk];
             const Factors &fa = sm.fac[c % NS_F];
             if (c >= NS_K && !mbar_wait(&sm.key_free[sk], ((c / NS_K) & 1) ^ 1, err)) fail = true;
@@ -658,10 +700,10 @@ __global__ void __launch_bounds__(NT, 1)
             kg_sync();
             if (warp < 4) {
                 // ------------------------------------------ INV (warps 0-3)
-                invert_unit_lower(sm.Af, sm.Tf, t);
+                invert_unit_lower<IT>(sm.Af, sm.Tf, kst, fa, t);
             } else {
                 // ------------------------------------------ helpers (warps 4-7)
-                if (t == KT && c + 1 < nch) {  // the TMEM tile was read; start the next chunk's [K;Q] K^T
+                if (warp == KW && c + 1 < nch) {  // the TMEM tile was read; start the next chunk's [K;Q] K^T
                     if (!mbar_wait(&sm.full_in[(c + 1) % NS_IN], ((c + 1) / NS_IN) & 1, err)) fail = true;
                     issue_m1(c + 1);
                 }
@@ -669,27 +711,9 @@ __global__ void __launch_bounds__(NT, 1)
                     chunk_gates(sm.fac[(c + 1) % NS_F], gt, lane);
                     if (c + 2 < nch) load_gates(gt, p, b, h, (long long)(c + 2) * C, lane);
                 }
-                // Q -> scale Q exp(G) in place (M1 has read Q); rows keep their 128-byte lines under the swizzle.
                 const int ht = t - 128;
-#pragma unroll
-                for (int k = 0; k < 8; ++k) {
-                    const int m = ht + 128 * k;  // 16-byte chunk 0..1023
-                    const int blkq = m / 512, row = (m % 512) / 8, pos = m % 8;
-                    unsigned char *ptr = ist.KQ + blkq * 16384 + 8192 + row * 128 + pos * 16;
-                    const float f = scale * fa.eG[row];
-                    uint4 u = *reinterpret_cast<const uint4 *>(ptr);
-                    const IT *hh = reinterpret_cast<const IT *>(&u);
-                    uint32_t w[4];
-#pragma unroll
-                    for (int x = 0; x < 4; ++x) w[x] = pack2<IT>(TR::to_f(hh[2 * x]) * f, TR::to_f(hh[2 * x + 1]) * f);
-                    *reinterpret_cast<uint4 *>(ptr) = make_uint4(w[0], w[1], w[2], w[3]);
-                }
                 inv_await();  // diagonal blocks, T10 and T32 are final
-                for (int e = ht; e < 6 * 32; e += 128) tb_blocks<IT>(sm.Tf, kst, fa, false, e);
-            }
-            kg_sync();
-            if (t < 128) {  // the four blocks of the last step
-                tb_blocks<IT>(sm.Tf, kst, fa, true, t);
+                for (int e = ht; e < 6 * 32; e += 128) tb_blocks<IT>(sm.Tf, kst, fa, e);
             }
             fence_smem_to_async();
             kg_sync();
@@ -733,25 +757,25 @@ __global__ void __launch_bounds__(NT, 1)
         bool fail = false;  // a wait of this thread ran out
         int c = 0;
         for (; c < nch; ++c) {
-            const int si = c % NS_IN, sk = c % NS_K, ob = c & 1;
+            const int si = c % NS_IN, sk = c % NS_K;
             InStage &ist = sm.in[si];
             KeyStage &kst = sm.ks[sk];
             if (!mbar_wait(&sm.key_ready[sk], (c / NS_K) & 1, err)) fail = true;
+            if (c >= 1 && !mbar_wait(&sm.o_empty, (c - 1) & 1, err)) fail = true;  // O^T of chunk c-1 was read out
             if (sg_any(fail || *stop)) break;
-            // ------------------------------------------ M3a: (K S)^T = S^T K^T;  then O^T = S^T Qg^T
-            if (st == 0) {
+            // ------------------------------------------ M3a: [(K S)^T | X^T] = S^T [K; Q]^T
+            // Each 64-feature block of the [K;Q] tile holds the K rows and then
+            // the Q rows, so one N = 128 operand covers both products.
+            if (sq == 0) {
                 fence_after_sync();
-                const uint32_t id = idesc(128, 64, TR::fmt, false, false);
+                if (elect_one()) {
+                    const uint32_t id = idesc(128, 128, TR::fmt, false, false);
 #pragma unroll
-                for (int ks = 0; ks < D / 16; ++ks)
-                    mma_f16_ta(tm + COL_VA, tm + COL_SB + ks * 8, desc_kq_kmaj(ist.KQ, 0, ks), id, ks > 0);
-                commit(&sm.bar_s);
-                // O buffer `ob` was read out for chunk c - 2
-                if (c >= 2 && !mbar_wait(&sm.o_empty[ob], ((c / 2) & 1) ^ 1, err)) fail = true;
-                fence_after_sync();
-#pragma unroll
-                for (int ks = 0; ks < D / 16; ++ks)
-                    mma_f16_ta(tm + COL_OA + 64 * ob, tm + COL_SB + ks * 8, desc_kq_kmaj(ist.KQ, 1, ks), id, ks > 0);
+                    for (int ks = 0; ks < D / 16; ++ks)
+                        mma_f16_ta(tm + COL_VA, tm + COL_SB + ks * 8, desc_kq_kmaj(ist.KQ, 0, ks), id, ks > 0);
+                    commit(&sm.bar_s);
+                }
+                __syncwarp();
             }
             const bool more = c + 1 < nch;
             float gamma_next = 1.f;
@@ -780,17 +804,20 @@ __global__ void __launch_bounds__(NT, 1)
             fence_before_sync();
             sg_sync();
             // ------------------------------------------ M3b: V'^T = V^T Tb^T - (K S)^T Tbg^T
-            if (st == 0) {
+            if (sq == 0) {
                 fence_after_sync();
-                const uint32_t id_v = idesc(128, 64, TR::fmt, true, false);
-                const uint32_t id_t = idesc(128, 64, TR::fmt, false, false);
+                if (elect_one()) {
+                    const uint32_t id_v = idesc(128, 64, TR::fmt, true, false);
+                    const uint32_t id_t = idesc(128, 64, TR::fmt, false, false);
 #pragma unroll
-                for (int ks = 0; ks < C / 16; ++ks)
-                    mma_f16(tm + COL_VA, desc_v_mn(ist.V, ks), desc_kmaj16(kst.Tb, C, ks), id_v, ks > 0);
+                    for (int ks = 0; ks < C / 16; ++ks)
+                        mma_f16(tm + COL_VA, desc_v_mn(ist.V, ks), desc_kmaj16(kst.Tb, C, ks), id_v, ks > 0);
 #pragma unroll
-                for (int ks = 0; ks < C / 16; ++ks)
-                    mma_f16_ta(tm + COL_VA, tm + COL_KSB + ks * 8, desc_kmaj16(kst.Tbg, C, ks), id_t, true);
-                commit(&sm.bar_s);
+                    for (int ks = 0; ks < C / 16; ++ks)
+                        mma_f16_ta(tm + COL_VA, tm + COL_KSB + ks * 8, desc_kmaj16(kst.Tbg, C, ks), id_t, true);
+                    commit(&sm.bar_s);
+                }
+                __syncwarp();
             }
             if (!mbar_wait(&sm.bar_s, ph, err)) fail = true;
             ph ^= 1;
@@ -819,20 +846,23 @@ __global__ void __launch_bounds__(NT, 1)
             tmem_wait_st();
             fence_before_sync();
             sg_sync();
-            // ------------------------------------------ M4: S^T update, O^T += V'^T P^T
-            if (st == 0) {
+            // ------------------------------------------ M4: S^T update;  Y^T = V'^T P^T (V'^T was read)
+            if (sq == 0) {
                 fence_after_sync();
-                const uint32_t id_o = idesc(128, 64, TR::fmt, false, false);
-                const uint32_t id_s = idesc(128, 128, TR::fmt, false, true);
+                if (elect_one()) {
+                    const uint32_t id_o = idesc(128, 64, TR::fmt, false, false);
+                    const uint32_t id_s = idesc(128, 128, TR::fmt, false, true);
 #pragma unroll
-                for (int ks = 0; ks < C / 16; ++ks)
-                    mma_f16_ta(tm + COL_ST, tm + COL_VB2 + ks * 8, desc_k_mn(ist.KQ, ks), id_s, true);
-                commit(&sm.bar_s);
+                    for (int ks = 0; ks < C / 16; ++ks)
+                        mma_f16_ta(tm + COL_ST, tm + COL_VB2 + ks * 8, desc_k_mn(ist.KQ, ks), id_s, true);
+                    commit(&sm.bar_s);
 #pragma unroll
-                for (int ks = 0; ks < C / 16; ++ks)
-                    mma_f16_ta(tm + COL_OA + 64 * ob, tm + COL_VB + ks * 8, desc_kmaj16(kst.P, C, ks), id_o, true);
-                commit(&sm.key_free[sk]);
-                commit(&sm.o_full[ob]);
+                    for (int ks = 0; ks < C / 16; ++ks)
+                        mma_f16_ta(tm + COL_VA, tm + COL_VB + ks * 8, desc_kmaj16(kst.P, C, ks), id_o, ks > 0);
+                    commit(&sm.key_free[sk]);
+                    commit(&sm.o_full);
+                }
+                __syncwarp();
             }
             if (!mbar_wait(&sm.bar_s, ph, err)) fail = true;
             ph ^= 1;
@@ -888,34 +918,56 @@ __global__ void __launch_bounds__(NT, 1)
         fence_before_sync();
     } else {
         // =============================================================== output group
+        // O = scale exp(G_r) X + Y: X^T (M3a) and Y^T (M4) sit in separate
+        // accumulators; warp 12 evaluates the row factors from the gates (the
+        // same sums as the key group) into a double buffer, which the group's
+        // barrier at the top of the chunk publishes to the other three warps.
         const int ot = t - KG - SG, oq = ot / 32, i = 32 * oq + lane;
         const uint32_t lb = 32u * oq;
         const size_t orow = (size_t)Hv * D;  // output row stride (elements)
+        Gates go;
+        if (oq == 0) load_gates(go, p, b, h, 0, lane);
         bool fail = false;
         int c = 0;
         for (; c < nch; ++c) {
-            const int ob = c & 1;
-            if (!mbar_wait(&sm.o_full[ob], (c / 2) & 1, err)) fail = true;
+            float *ofs = sm.ofs[c & 1];
+            if (oq == 0) {
+                out_scales(ofs, go, scale, lane);
+                if (c + 1 < nch) load_gates(go, p, b, h, (long long)(c + 1) * C, lane);
+            }
+            if (!mbar_wait(&sm.o_full, c & 1, err)) fail = true;
             if (og_any(fail || *stop)) break;
             fence_after_sync();
             const long long t0 = (long long)c * C;
             const size_t obase = ((size_t)(b * T + t0) * Hv + h) * D;
             const int nvalid = (int)min((long long)C, T - t0);
-            float v[2][32];
-            tmem_ld16(taddr(tm + COL_OA + 64 * ob, lb, 0), *reinterpret_cast<float(*)[16]>(&v[0][0]));
-            tmem_ld16(taddr(tm + COL_OA + 64 * ob, lb, 16), *reinterpret_cast<float(*)[16]>(&v[0][16]));
-            tmem_ld16(taddr(tm + COL_OA + 64 * ob, lb, 32), *reinterpret_cast<float(*)[16]>(&v[1][0]));
-            tmem_ld16(taddr(tm + COL_OA + 64 * ob, lb, 48), *reinterpret_cast<float(*)[16]>(&v[1][16]));
-            tmem_wait_ld();
-            reg_fence16(&v[0][0]);
-            reg_fence16(&v[0][16]);
-            reg_fence16(&v[1][0]);
-            reg_fence16(&v[1][16]);
-            fence_before_sync();
-            og_sync();
-            if (ot == 0) mbar_arrive(&sm.o_empty[ob]);  // the MMAs may overwrite the buffer now
-            store_o(p, obase, orow, nvalid, 0, i, lane, v[0]);
-            store_o(p, obase, orow, nvalid, 32, i, lane, v[1]);
+#pragma unroll
+            for (int half = 0; half < 2; ++half) {
+                float x[32], y[32];
+                tmem_ld16(taddr(tm + COL_OA, lb, 32 * half), *reinterpret_cast<float(*)[16]>(&x[0]));
+                tmem_ld16(taddr(tm + COL_OA, lb, 32 * half + 16), *reinterpret_cast<float(*)[16]>(&x[16]));
+                tmem_ld16(taddr(tm + COL_VA, lb, 32 * half), *reinterpret_cast<float(*)[16]>(&y[0]));
+                tmem_ld16(taddr(tm + COL_VA, lb, 32 * half + 16), *reinterpret_cast<float(*)[16]>(&y[16]));
+                tmem_wait_ld();
+                reg_fence16(&x[0]);
+                reg_fence16(&x[16]);
+                reg_fence16(&y[0]);
+                reg_fence16(&y[16]);
+#pragma unroll
+                for (int r = 0; r < 32; r += 4) {
+                    const float4 f = *reinterpret_cast<const float4 *>(ofs + 32 * half + r);
+                    x[r] = fmaf(f.x, x[r], y[r]);
+                    x[r + 1] = fmaf(f.y, x[r + 1], y[r + 1]);
+                    x[r + 2] = fmaf(f.z, x[r + 2], y[r + 2]);
+                    x[r + 3] = fmaf(f.w, x[r + 3], y[r + 3]);
+                }
+                if (half == 1) {
+                    fence_before_sync();
+                    og_sync();
+                    if (ot == 0) mbar_arrive(&sm.o_empty);  // the MMAs may overwrite X^T and Y^T now
+                }
+                store_o(p, obase, orow, nvalid, 32 * half, i, lane, x);
+            }
         }
         if (c < nch) *stop = 1;
         fence_before_sync();

@@ -78,6 +78,18 @@ __device__ __forceinline__ void fence_after_sync() { asm volatile("tcgen05.fence
 __device__ __forceinline__ void fence_smem_to_async() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
 
 // ------------------------------------------------------------------- MMA
+// One lane of a converged warp (elect.sync over the full mask).  MMAs are
+// issued by the elected lane with the rest of its warp waiting at the
+// following __syncwarp(), which issues faster than a lone divergent thread.
+__device__ __forceinline__ bool elect_one() {
+    uint32_t pred = 0;
+    asm volatile(
+        "{\n\t.reg .pred P;\n\t"
+        "elect.sync _|P, 0xffffffff;\n\t"
+        "selp.b32 %0, 1, 0, P;\n\t}"
+        : "=r"(pred));
+    return pred != 0;
+}
 __device__ __forceinline__ void mma_f16(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t id,
                                         bool accumulate) {
     asm volatile(
@@ -115,19 +127,25 @@ __device__ __forceinline__ void commit(uint64_t *bar) {
 __device__ __forceinline__ void mbar_init(uint64_t *bar, uint32_t count) {
     asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_addr(bar)), "r"(count) : "memory");
 }
-__device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, uint32_t phase) {
+// One poll.  When the phase is still open the thread is suspended in
+// hardware until it completes or about `suspend_ns` nanoseconds pass, so
+// waiting warps leave the issue slots and the shared-memory pipe to the
+// warps that work.
+__device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, uint32_t phase, uint32_t suspend_ns = 1000) {
     uint32_t ok;
     asm volatile(
         "{\n\t.reg .pred p;\n\t"
-        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
         "selp.u32 %0, 1, 0, p;\n\t}\n"
         : "=r"(ok)
-        : "r"(smem_addr(bar)), "r"(phase)
+        : "r"(smem_addr(bar)), "r"(phase), "r"(suspend_ns)
         : "memory");
     return ok != 0;
 }
-// Wait for the phase with parity `phase` to complete, at most `limit` polls.
-__device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t phase, int *err, uint32_t limit = 1u << 26) {
+// Wait for the phase with parity `phase` to complete, at most `limit` polls
+// (about a second with the suspension honoured, far less if every poll
+// returns at once).
+__device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t phase, int *err, uint32_t limit = 1u << 20) {
     for (uint32_t i = 0; i < limit; ++i)
         if (mbar_try_wait(bar, phase)) return true;
     if (err) atomicExch(err, 1);
