@@ -7,21 +7,21 @@
 // G = in-chunk cumulative log decay, gamma = exp(G_63):
 //   A   = beta_r (k_r.k_s) exp(G_r - G_s), s <  r
 //   P   = scale (q_r.k_s) exp(G_r - G_s), s <= r
-//   T   = (I + A)^-1,  Tb = T diag(beta),  Tbg = T diag(beta exp(G))
-//   V'  = Tb V - Tbg (K S)                  (= U - W S of the WY form)
+//   T   = (I + A)^-1,  Tb = T diag(beta)
+//   V'  = Tb (V - exp(G) (K S))             (= U - W S of the WY form)
 //   O   = scale exp(G) (Q S) + P V'
 //   S  <- gamma S + (K exp(G_63 - G))^T V'
 // Everything except the last three lines is independent of the state, so it
 // runs one chunk AHEAD of the recurrence, in three warp groups:
 //   key group    (warps 0-7):   TMA loads, [K;Q] K^T, A and P, the inverse,
-//                               Tb / Tbg;
+//                               Tb;
 //   state group  (warps 8-11):  the recurrence, with the state held TRANSPOSED
 //                               in TMEM (lane = value index i, column = key
 //                               index j), so every state-side MMA has M = 128
 //                               and reads the 16-bit state copy from TMEM:
 //     M3a  [(K S)^T | X^T] = S^T [K; Q]^T    one N = 128 chain, A: S^T
 //                                            (TMEM), B: the [K;Q] tile
-//     M3b  V'^T      = V^T Tb^T - (K S)^T Tbg^T
+//     M3b  V'^T      = V^T Tb^T - ((K S)^T exp(G)) Tb^T
 //     M4   S^T      += (V' exp(G_63 - G))^T K,   Y^T = V'^T P^T
 //   output group (warps 12-15): O = scale exp(G_r) X + Y from TMEM to global
 //                               memory, off the recurrence's critical path
@@ -38,11 +38,11 @@
 //   [  0,128) S^T                 [128,192) S^T 16-bit (A operand)
 //   [192,256) (K S)^T, then V'^T, then Y^T     [256,320) X^T (M3a writes
 //             (K S)^T and X^T at once)
-//   [320,352) -(K S)^T 16-bit, then V'^T 16-bit    [352,384) V''^T 16-bit
+//   [320,352) -(K S)^T exp(G) 16-bit, then V'^T 16-bit    [352,384) V''^T 16-bit
 //   [384,448) [K;Q] K^T  (lanes 0-63: K K^T, 64-127: Q K^T)
 // Shared memory: per input stage K and Q interleaved by 64-feature block
 // ([K blk0 | Q blk0 | K blk1 | Q blk1], 128-byte swizzle, so [K;Q] is one
-// M = 128 operand) and V (128-byte swizzle); per key stage P, Tb, Tbg (no
+// M = 128 operand) and V (128-byte swizzle); per key stage P and Tb (no
 // swizzle, K-major) and the gate factors; the fp32 inverse workspace.
 #include "gdn_internal.cuh"
 #include "tma.cuh"
@@ -73,7 +73,6 @@ struct InStage {
 struct KeyStage {
     unsigned char P[C * C * 2];
     unsigned char Tb[C * C * 2];
-    unsigned char Tbg[C * C * 2];
 };
 // Gate factors of one chunk (a three-deep ring: the key group fills chunk
 // c+1's while it works on chunk c and the state group may still read c-1's).
@@ -268,8 +267,8 @@ __device__ __forceinline__ void store16(float *__restrict__ Z, const float (&acc
     }
 }
 
-// Tb / Tbg entries of the 16 x 16 block (bi, bj) of T, held as an m16n8
-// accumulator pair times `sign`, rounded straight into the operand tiles.
+// Tb entries of the 16 x 16 block (bi, bj) of T, held as an m16n8
+// accumulator pair times `sign`, rounded straight into the operand tile.
 template <typename IT>
 __device__ __forceinline__ void store_tb16(KeyStage &ks, const Factors &fa, const float (&acc)[2][4], float sign,
                                            int bi, int bj, Frag f) {
@@ -277,19 +276,17 @@ __device__ __forceinline__ void store_tb16(KeyStage &ks, const Factors &fa, cons
     for (int nn = 0; nn < 2; ++nn) {
         const int s = 16 * bj + 8 * nn + 2 * f.q;
         const float b0 = fa.beta[s], b1 = fa.beta[s + 1];
-        const float g0 = b0 * fa.eG[s], g1 = b1 * fa.eG[s + 1];
 #pragma unroll
         for (int hh = 0; hh < 2; ++hh) {
             const int r = 16 * bi + f.g + 8 * hh;
             const float x0 = sign * acc[nn][2 * hh], x1 = sign * acc[nn][2 * hh + 1];
             *reinterpret_cast<uint32_t *>(ks.Tb + kmaj16(r, s, C)) = pack2<IT>(x0 * b0, x1 * b1);
-            *reinterpret_cast<uint32_t *>(ks.Tbg + kmaj16(r, s, C)) = pack2<IT>(x0 * g0, x1 * g1);
         }
     }
 }
 
 // Runs on key-group warps 0-3 (t < 128).  The last step's four blocks go
-// straight into Tb / Tbg; the others stay in T for the helper warps.
+// straight into Tb; the others stay in T for the helper warps.
 template <typename IT>
 __device__ __forceinline__ void invert_unit_lower(float *__restrict__ A, float *__restrict__ T, KeyStage &ks,
                                                   const Factors &fa,
@@ -357,25 +354,20 @@ __device__ __forceinline__ void invert_unit_lower(float *__restrict__ A, float *
     }
 }
 
-// Tb = T diag(beta), Tbg = T diag(beta exp(G)) for 8 columns s0 .. s0+7 of
-// row r (a lower block), rounded into the K-major operand tiles.
+// Tb = T diag(beta) for 8 columns s0 .. s0+7 of row r (a lower block),
+// rounded into the K-major operand tile.
 template <typename IT>
 __device__ __forceinline__ void tb_chunk(const float *Tf, KeyStage &ks, const Factors &fa, int r, int s0) {
     const float *src = Tf + blk(r / 16, s0 / 16) + (r % 16) * BLD + (s0 % 16);
     const float4 x0 = *reinterpret_cast<const float4 *>(src);
     const float4 x1 = *reinterpret_cast<const float4 *>(src + 4);
     const float x[8] = {x0.x, x0.y, x0.z, x0.w, x1.x, x1.y, x1.z, x1.w};
-    float a[8], g8[8];
+    float a[8];
 #pragma unroll
-    for (int u = 0; u < 8; ++u) {
-        const float bs = fa.beta[s0 + u];
-        a[u] = x[u] * bs;
-        g8[u] = x[u] * (bs * fa.eG[s0 + u]);
-    }
+    for (int u = 0; u < 8; ++u) a[u] = x[u] * fa.beta[s0 + u];
     st_vec8<IT>(ks.Tb, kmaj16(r, s0, C), a);
-    st_vec8<IT>(ks.Tbg, kmaj16(r, s0, C), g8);
 }
-// Chunk e (< 192) of the Tb / Tbg blocks the inverse finishes early: the
+// Chunk e (< 192) of the Tb blocks the inverse finishes early: the
 // diagonal blocks and T10, T32 (the last step writes its own blocks).
 template <typename IT>
 __device__ __forceinline__ void tb_blocks(const float *Tf, KeyStage &ks, const Factors &fa, int e) {
@@ -585,9 +577,9 @@ __global__ void __launch_bounds__(NT, 1)
         // =============================================================== key group
         // Per chunk c:  all 8 warps: E1 (A and P from [K;Q] K^T);
         //   warps 0-3: the inverse, whose last step writes its four blocks
-        //     of Tb / Tbg directly;
+        //     of Tb directly;
         //   warps 4-7 meanwhile: the gates of chunk c+1, the [K;Q] K^T MMA
-        //     of chunk c+1 (warp KW), and Tb / Tbg of the blocks the inverse
+        //     of chunk c+1 (warp KW), and Tb of the blocks the inverse
         //     finished early;
         //   then hand the chunk over.
         constexpr int KT = 224, KW = KT / 32, GW = 4;  // TMA thread and its warp (MMA); the warp computing gates
@@ -605,14 +597,13 @@ __global__ void __launch_bounds__(NT, 1)
             }
             __syncwarp();
         };
-        // The upper blocks of Tb / Tbg stay zero; write them once.
-        for (int e = t; e < NS_K * 2 * 6 * 32; e += KG) {
-            const int st2 = e / (2 * 6 * 32), which = (e / (6 * 32)) % 2, n = (e % (6 * 32)) / 32, x = e % 32;
+        // The upper blocks of Tb stay zero; write them once.
+        for (int e = t; e < NS_K * 6 * 32; e += KG) {
+            const int st2 = e / (6 * 32), n = (e % (6 * 32)) / 32, x = e % 32;
             // upper blocks (0,1) (0,2) (0,3) (1,2) (1,3) (2,3)
             const int ubi = n < 3 ? 0 : (n < 5 ? 1 : 2), ubj = n < 3 ? n + 1 : (n < 5 ? n - 1 : 3);
             const int r = 16 * ubi + x / 2, s0 = 16 * ubj + 8 * (x % 2);
-            *reinterpret_cast<uint4 *>((which ? sm.ks[st2].Tbg : sm.ks[st2].Tb) + kmaj16(r, s0, C)) =
-                make_uint4(0, 0, 0, 0);
+            *reinterpret_cast<uint4 *>(sm.ks[st2].Tb + kmaj16(r, s0, C)) = make_uint4(0, 0, 0, 0);
         }
         if (t == KT && nch > 0) {
             issue_loads(0);
@@ -786,24 +777,31 @@ __global__ void __launch_bounds__(NT, 1)
             if (!mbar_wait(&sm.bar_s, ph, err)) fail = true;
             ph ^= 1;
             fence_after_sync();
-            // ------------------------------------------ E3a: -(K S)^T -> 16-bit A operand
+            // ------------------------------------------ E3a: -(K S)^T exp(G) -> 16-bit A operand
+            {
+                const float *eg = sm.fac[c % NS_F].eG;
 #pragma unroll
-            for (int half = 0; half < 2; ++half) {
-                float v[32];
-                tmem_ld16(taddr(tm + COL_VA, lb, 32 * half), *reinterpret_cast<float(*)[16]>(&v[0]));
-                tmem_ld16(taddr(tm + COL_VA, lb, 32 * half + 16), *reinterpret_cast<float(*)[16]>(&v[16]));
-                tmem_wait_ld();
-                reg_fence16(&v[0]);
-                reg_fence16(&v[16]);
-                uint32_t u[16];
+                for (int half = 0; half < 2; ++half) {
+                    float v[32];
+                    tmem_ld16(taddr(tm + COL_VA, lb, 32 * half), *reinterpret_cast<float(*)[16]>(&v[0]));
+                    tmem_ld16(taddr(tm + COL_VA, lb, 32 * half + 16), *reinterpret_cast<float(*)[16]>(&v[16]));
+                    tmem_wait_ld();
+                    reg_fence16(&v[0]);
+                    reg_fence16(&v[16]);
+                    uint32_t u[16];
 #pragma unroll
-                for (int x = 0; x < 16; ++x) u[x] = pack2<IT>(-v[2 * x], -v[2 * x + 1]);
-                tmem_st16u(taddr(tm + COL_KSB, lb, 16 * half), u);
+                    for (int x = 0; x < 16; x += 2) {
+                        const float4 e = *reinterpret_cast<const float4 *>(eg + 32 * half + 2 * x);
+                        u[x] = pack2<IT>(-v[2 * x] * e.x, -v[2 * x + 1] * e.y);
+                        u[x + 1] = pack2<IT>(-v[2 * x + 2] * e.z, -v[2 * x + 3] * e.w);
+                    }
+                    tmem_st16u(taddr(tm + COL_KSB, lb, 16 * half), u);
+                }
             }
             tmem_wait_st();
             fence_before_sync();
             sg_sync();
-            // ------------------------------------------ M3b: V'^T = V^T Tb^T - (K S)^T Tbg^T
+            // ------------------------------------------ M3b: V'^T = V^T Tb^T - ((K S)^T exp(G)) Tb^T
             if (sq == 0) {
                 fence_after_sync();
                 if (elect_one()) {
@@ -814,7 +812,7 @@ __global__ void __launch_bounds__(NT, 1)
                         mma_f16(tm + COL_VA, desc_v_mn(ist.V, ks), desc_kmaj16(kst.Tb, C, ks), id_v, ks > 0);
 #pragma unroll
                     for (int ks = 0; ks < C / 16; ++ks)
-                        mma_f16_ta(tm + COL_VA, tm + COL_KSB + ks * 8, desc_kmaj16(kst.Tbg, C, ks), id_t, true);
+                        mma_f16_ta(tm + COL_VA, tm + COL_KSB + ks * 8, desc_kmaj16(kst.Tb, C, ks), id_t, true);
                     commit(&sm.bar_s);
                 }
                 __syncwarp();
