@@ -30,18 +30,58 @@ namespace {
 constexpr int CH = 64;        // chunk length
 constexpr int THREADS = 256;  // 16 x 16
 
-__device__ __forceinline__ float ld_any(const void *p, size_t i, int dt) {
-    switch (dt) {
-        case KAI_GDN_BF16: return __bfloat162float(static_cast<const __nv_bfloat16 *>(p)[i]);
-        case KAI_GDN_F16: return __half2float(static_cast<const __half *>(p)[i]);
-        default: return static_cast<const float *>(p)[i];
-    }
-}
 __device__ __forceinline__ void st_any(void *p, size_t i, int dt, float v) {
     switch (dt) {
         case KAI_GDN_BF16: static_cast<__nv_bfloat16 *>(p)[i] = __float2bfloat16_rn(v); break;
         case KAI_GDN_F16: static_cast<__half *>(p)[i] = __float2half_rn(v); break;
         default: static_cast<float *>(p)[i] = v;
+    }
+}
+
+__device__ __forceinline__ float to_f(float x) { return x; }
+__device__ __forceinline__ float to_f(__half x) { return __half2float(x); }
+__device__ __forceinline__ float to_f(__nv_bfloat16 x) { return __bfloat162float(x); }
+
+// One chunk's k, q (CH x DK, q times `scale`) and v (CH x DVB) tiles into
+// shared memory.  Every load of the thread is issued before the first store,
+// so a chunk waits for one global-memory latency rather than one per element;
+// rows past T read as zeros.
+template <typename ET, int DK, int DVB, int LDK, int LDV>
+__device__ __forceinline__ void load_chunk_tiles(const kai_gdn_chunk_args &p, float *K, float *Q, float *V, long long b,
+                                                 long long h, long long hk, long long c0, long long v0, int t) {
+    constexpr int NKQ = CH * DK / THREADS, NV = CH * DVB / THREADS;
+    const long long T = (long long)p.seq, Hv = (long long)p.heads_v, Hk = (long long)p.heads_k;
+    const long long DV = (long long)p.dv;
+    const ET *kp = static_cast<const ET *>(p.k), *qp = static_cast<const ET *>(p.q), *vp = static_cast<const ET *>(p.v);
+    float kr[NKQ], qr[NKQ], vr[NV];
+#pragma unroll
+    for (int u = 0; u < NKQ; ++u) {
+        const int e = t + u * THREADS, r = e / DK, d = e % DK;
+        const long long tok = c0 + r;
+        kr[u] = 0.f;
+        qr[u] = 0.f;
+        if (tok < T) {
+            const size_t i = ((size_t)(b * T + tok) * Hk + hk) * DK + d;
+            kr[u] = to_f(kp[i]);
+            qr[u] = to_f(qp[i]);
+        }
+    }
+#pragma unroll
+    for (int u = 0; u < NV; ++u) {
+        const int e = t + u * THREADS, r = e / DVB, n = e % DVB;
+        const long long tok = c0 + r;
+        vr[u] = tok < T ? to_f(vp[((size_t)(b * T + tok) * Hv + h) * DV + v0 + n]) : 0.f;
+    }
+#pragma unroll
+    for (int u = 0; u < NKQ; ++u) {
+        const int e = t + u * THREADS, r = e / DK, d = e % DK;
+        K[r * LDK + d] = kr[u];
+        Q[r * LDK + d] = qr[u] * p.scale;
+    }
+#pragma unroll
+    for (int u = 0; u < NV; ++u) {
+        const int e = t + u * THREADS, r = e / DVB, n = e % DVB;
+        V[r * LDV + n] = vr[u];
     }
 }
 
@@ -65,6 +105,56 @@ __device__ __forceinline__ void mm(float (&acc)[MI][NJ], const float *A, int lda
     }
 }
 
+// The same with A row-major (not transposed) read four k at a time: rows of
+// A 16-byte aligned, lda and kd multiples of 4.  The sums run in k order.
+template <int MI, int NJ>
+__device__ __forceinline__ void mm_k4(float (&acc)[MI][NJ], const float *A, int lda, const float *B, int ldb, int kd) {
+    const int tx = threadIdx.x % 16, ty = threadIdx.x / 16;
+#pragma unroll 2
+    for (int k = 0; k < kd; k += 4) {
+        float4 a[MI];
+#pragma unroll
+        for (int i = 0; i < MI; ++i) a[i] = *reinterpret_cast<const float4 *>(A + (ty + 16 * i) * lda + k);
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+            float b[NJ];
+#pragma unroll
+            for (int j = 0; j < NJ; ++j) b[j] = B[(k + u) * ldb + tx + 16 * j];
+#pragma unroll
+            for (int i = 0; i < MI; ++i) {
+                const float av = u == 0 ? a[i].x : u == 1 ? a[i].y : u == 2 ? a[i].z : a[i].w;
+#pragma unroll
+                for (int j = 0; j < NJ; ++j) acc[i][j] = fmaf(av, b[j], acc[i][j]);
+            }
+        }
+    }
+}
+// acc[i][j] += sum_k A[k*lda + MI ty + i] * B[k*ldb + tx + 16 j]: A transposed,
+// each thread on MI CONSECUTIVE rows (read as float4), MI a multiple of 4.
+template <int MI, int NJ>
+__device__ __forceinline__ void mm_t4(float (&acc)[MI][NJ], const float *A, int lda, const float *B, int ldb, int kd) {
+    static_assert(MI % 4 == 0, "rows in 16-byte groups");
+    const int tx = threadIdx.x % 16, ty = threadIdx.x / 16;
+#pragma unroll 4
+    for (int k = 0; k < kd; ++k) {
+        float a[MI], b[NJ];
+#pragma unroll
+        for (int i = 0; i < MI; i += 4) {
+            const float4 v = *reinterpret_cast<const float4 *>(A + k * lda + MI * ty + i);
+            a[i] = v.x;
+            a[i + 1] = v.y;
+            a[i + 2] = v.z;
+            a[i + 3] = v.w;
+        }
+#pragma unroll
+        for (int j = 0; j < NJ; ++j) b[j] = B[k * ldb + tx + 16 * j];
+#pragma unroll
+        for (int i = 0; i < MI; ++i)
+#pragma unroll
+            for (int j = 0; j < NJ; ++j) acc[i][j] = fmaf(a[i], b[j], acc[i][j]);
+    }
+}
+
 template <int MI, int NJ>
 __device__ __forceinline__ void zero(float (&acc)[MI][NJ]) {
 #pragma unroll
@@ -75,13 +165,12 @@ __device__ __forceinline__ void zero(float (&acc)[MI][NJ]) {
 
 template <int DK, int DVB>
 struct Smem {
-    static constexpr int LDK = DK + 1;   // odd strides: conflict-free column reads
+    static constexpr int LDK = DK + 4;   // rows 16-byte aligned; 4 banks apart, so 8 rows fill the 32 banks
     static constexpr int LDV = DVB + 1;
-    static constexpr int LDP = CH + 1;
+    static constexpr int LDP = CH + 4;   // rows 16-byte aligned
     float K[CH * LDK];     // K, later K * exp(G_last - G)
     float Q[CH * LDK];     // scale * Q, later * exp(G)
-    float W[CH * LDK];     // beta * K * exp(G), then W
-    float V[CH * LDV];     // V, beta * V, U, then V'
+    float V[CH * LDV];     // V, then beta (V - exp(G) K S), then V'
     float A[CH * LDP];     // strictly lower A
     float P[CH * LDP];     // lower-with-diagonal P
     float S[DK * LDV];     // state block [DK][DVB]
@@ -114,23 +203,12 @@ __global__ void __launch_bounds__(THREADS, 1) chunk_scan_fp32_kernel(kai_gdn_chu
 
     for (long long c0 = 0; c0 < T; c0 += CH) {
         // ---- loads (rows past T are zero padding with g = beta = 0)
-        for (int e = t; e < CH * DK; e += THREADS) {
-            int r = e / DK, d = e % DK;
-            long long tok = c0 + r;
-            float kv = 0.f, qv = 0.f;
-            if (tok < T) {
-                size_t i = ((size_t)(b * T + tok) * Hk + hk) * DK + d;
-                kv = ld_any(p.k, i, p.in_dtype);
-                qv = ld_any(p.q, i, p.in_dtype) * p.scale;
-            }
-            sm.K[r * LDK + d] = kv;
-            sm.Q[r * LDK + d] = qv;
-        }
-        for (int e = t; e < CH * DVB; e += THREADS) {
-            int r = e / DVB, n = e % DVB;
-            long long tok = c0 + r;
-            sm.V[r * LDV + n] =
-                tok < T ? ld_any(p.v, ((size_t)(b * T + tok) * Hv + h) * DV + v0 + n, p.in_dtype) : 0.f;
+        switch (p.in_dtype) {
+            case KAI_GDN_BF16:
+                load_chunk_tiles<__nv_bfloat16, DK, DVB, LDK, LDV>(p, sm.K, sm.Q, sm.V, b, h, hk, c0, v0, t);
+                break;
+            case KAI_GDN_F16: load_chunk_tiles<__half, DK, DVB, LDK, LDV>(p, sm.K, sm.Q, sm.V, b, h, hk, c0, v0, t); break;
+            default: load_chunk_tiles<float, DK, DVB, LDK, LDV>(p, sm.K, sm.Q, sm.V, b, h, hk, c0, v0, t);
         }
         if (t < 32) {
             // In-chunk inclusive cumsum of g (2 rows per lane), beta.
@@ -160,22 +238,28 @@ __global__ void __launch_bounds__(THREADS, 1) chunk_scan_fp32_kernel(kai_gdn_chu
             float kk[4][4], qk[4][4];
             zero(kk);
             zero(qk);
-            const int tx_ = tx, ty_ = ty;
+            // four features per 16-byte load; the sums still run in feature order
 #pragma unroll 2
-            for (int d = 0; d < DK; ++d) {
-                float kr[4], qr[4], ks[4];
+            for (int d = 0; d < DK; d += 4) {
+                float4 kr[4], qr[4], ks[4];
 #pragma unroll
                 for (int i = 0; i < 4; ++i) {
-                    kr[i] = sm.K[(ty_ + 16 * i) * LDK + d];
-                    qr[i] = sm.Q[(ty_ + 16 * i) * LDK + d];
-                    ks[i] = sm.K[(tx_ + 16 * i) * LDK + d];
+                    kr[i] = *reinterpret_cast<const float4 *>(&sm.K[(ty + 16 * i) * LDK + d]);
+                    qr[i] = *reinterpret_cast<const float4 *>(&sm.Q[(ty + 16 * i) * LDK + d]);
+                    ks[i] = *reinterpret_cast<const float4 *>(&sm.K[(tx + 16 * i) * LDK + d]);
                 }
 #pragma unroll
                 for (int i = 0; i < 4; ++i)
 #pragma unroll
                     for (int j = 0; j < 4; ++j) {
-                        kk[i][j] = fmaf(kr[i], ks[j], kk[i][j]);
-                        qk[i][j] = fmaf(qr[i], ks[j], qk[i][j]);
+                        kk[i][j] = fmaf(kr[i].x, ks[j].x, kk[i][j]);
+                        kk[i][j] = fmaf(kr[i].y, ks[j].y, kk[i][j]);
+                        kk[i][j] = fmaf(kr[i].z, ks[j].z, kk[i][j]);
+                        kk[i][j] = fmaf(kr[i].w, ks[j].w, kk[i][j]);
+                        qk[i][j] = fmaf(qr[i].x, ks[j].x, qk[i][j]);
+                        qk[i][j] = fmaf(qr[i].y, ks[j].y, qk[i][j]);
+                        qk[i][j] = fmaf(qr[i].z, ks[j].z, qk[i][j]);
+                        qk[i][j] = fmaf(qr[i].w, ks[j].w, qk[i][j]);
                     }
             }
 #pragma unroll
@@ -189,37 +273,52 @@ __global__ void __launch_bounds__(THREADS, 1) chunk_scan_fp32_kernel(kai_gdn_chu
                 }
         }
         __syncthreads();
-        // ---- right-hand sides: beta K exp(G) into W, beta V in place
-        for (int e = t; e < CH * DK; e += THREADS) {
-            int r = e / DK, d = e % DK;
-            sm.W[r * LDK + d] = sm.beta[r] * sm.K[r * LDK + d] * sm.eG[r];
-        }
-        for (int e = t; e < CH * DVB; e += THREADS) {
-            int r = e / DVB, n = e % DVB;
-            sm.V[r * LDV + n] *= sm.beta[r];
-        }
-        __syncthreads();
-        // ---- forward substitution X_r = R_r - sum_{s<r} A[r][s] X_s, per column
-        for (int col = t; col < DK + DVB; col += THREADS) {
-            float *X = col < DK ? sm.W + col : sm.V + (col - DK);
-            const int ld = col < DK ? LDK : LDV;
-            for (int r = 1; r < CH; ++r) {
-                float acc = X[r * ld];
-                for (int s = 0; s < r; ++s) acc = fmaf(-sm.A[r * LDP + s], X[s * ld], acc);
-                X[r * ld] = acc;
+        // ---- right-hand side R = beta (V - exp(G) (K S)), in place over V
+        {
+            float ks[4][DVB / 16];
+            zero(ks);
+            mm_k4<4, DVB / 16>(ks, sm.K, LDK, sm.S, LDV, DK);
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                const int r = ty + 16 * i;
+                const float br = sm.beta[r], bg = br * sm.eG[r];
+#pragma unroll
+                for (int j = 0; j < DVB / 16; ++j) {
+                    float &x = sm.V[r * LDV + tx + 16 * j];
+                    x = br * x - bg * ks[i][j];
+                }
             }
         }
         __syncthreads();
-        // ---- V' = U - W S (in place over U);  Q *= exp(G);  K *= exp(G_last - G)
+        // ---- V' = (I + A)^-1 R: right-looking substitution, a group of GT
+        // consecutive lanes per column, rows r = j + GT m held by thread j of
+        // the group; x_r is final when step r starts and is broadcast to the
+        // group by a shuffle.
         {
-            float ws[4][DVB / 16];
-            zero(ws);
-            mm<4, DVB / 16, false, false>(ws, sm.W, LDK, sm.S, LDV, DK);
+            constexpr int GT = THREADS / DVB, RPT = CH / GT;
+            static_assert(GT <= 32 && 32 % GT == 0, "column groups inside a warp");
+            const int n = t / GT, j = t % GT, lane = t % 32;
+            float x[RPT];
 #pragma unroll
-            for (int i = 0; i < 4; ++i)
+            for (int m = 0; m < RPT; ++m) x[m] = sm.V[(j + GT * m) * LDV + n];
+#pragma unroll 1
+            for (int r = 0; r < CH - 1; ++r) {
+                const int owner = r % GT, mr = r / GT;
+                float xr = 0.f;
 #pragma unroll
-                for (int j = 0; j < DVB / 16; ++j) sm.V[(ty + 16 * i) * LDV + tx + 16 * j] -= ws[i][j];
+                for (int m = 0; m < RPT; ++m)
+                    if (m == mr) xr = x[m];
+                xr = __shfl_sync(0xffffffffu, xr, lane - j + owner);
+#pragma unroll
+                for (int m = 0; m < RPT; ++m) {
+                    const int i = j + GT * m;
+                    if (i > r) x[m] = fmaf(-sm.A[i * LDP + r], xr, x[m]);
+                }
+            }
+#pragma unroll
+            for (int m = 0; m < RPT; ++m) sm.V[(j + GT * m) * LDV + n] = x[m];
         }
+        // ---- Q *= exp(G);  K *= exp(G_last - G)
         for (int e = t; e < CH * DK; e += THREADS) {
             int r = e / DK, d = e % DK;
             sm.Q[r * LDK + d] *= sm.eG[r];
@@ -230,8 +329,8 @@ __global__ void __launch_bounds__(THREADS, 1) chunk_scan_fp32_kernel(kai_gdn_chu
         {
             float o[4][DVB / 16];
             zero(o);
-            mm<4, DVB / 16, false, false>(o, sm.Q, LDK, sm.S, LDV, DK);
-            mm<4, DVB / 16, false, false>(o, sm.P, LDP, sm.V, LDV, CH);
+            mm_k4<4, DVB / 16>(o, sm.Q, LDK, sm.S, LDV, DK);
+            mm_k4<4, DVB / 16>(o, sm.P, LDP, sm.V, LDV, CH);
 #pragma unroll
             for (int i = 0; i < 4; ++i) {
                 long long tok = c0 + ty + 16 * i;
@@ -246,18 +345,24 @@ __global__ void __launch_bounds__(THREADS, 1) chunk_scan_fp32_kernel(kai_gdn_chu
         __syncthreads();
         // ---- S = exp(G_last) S + (K exp(G_last - G))^T V'
         {
+            // thread rows MI ty .. MI ty + MI-1 when MI is a multiple of 4, else ty + 16 i
             constexpr int MI = DK / 16, NJ = DVB / 16;
+            constexpr bool V4 = MI % 4 == 0;
+            auto row = [&](int i) { return V4 ? MI * ty + i : ty + 16 * i; };
             float acc[MI][NJ];
             const float egl = sm.eG[CH - 1];
 #pragma unroll
             for (int i = 0; i < MI; ++i)
 #pragma unroll
-                for (int j = 0; j < NJ; ++j) acc[i][j] = egl * sm.S[(ty + 16 * i) * LDV + tx + 16 * j];
-            mm<MI, NJ, true, false>(acc, sm.K, LDK, sm.V, LDV, CH);
+                for (int j = 0; j < NJ; ++j) acc[i][j] = egl * sm.S[row(i) * LDV + tx + 16 * j];
+            if constexpr (V4)
+                mm_t4<MI, NJ>(acc, sm.K, LDK, sm.V, LDV, CH);
+            else
+                mm<MI, NJ, true, false>(acc, sm.K, LDK, sm.V, LDV, CH);
 #pragma unroll
             for (int i = 0; i < MI; ++i)
 #pragma unroll
-                for (int j = 0; j < NJ; ++j) sm.S[(ty + 16 * i) * LDV + tx + 16 * j] = acc[i][j];
+                for (int j = 0; j < NJ; ++j) sm.S[row(i) * LDV + tx + 16 * j] = acc[i][j];
         }
         __syncthreads();
     }
@@ -302,7 +407,10 @@ int run_chunk(const kai_gdn_chunk_args *a, cudaStream_t st) {
 }  // namespace
 
 int launch_chunk_fp32(const kai_gdn_chunk_args *a, cudaStream_t st) {
-    if (a->dk == 128 && a->dv % 64 == 0) return run_chunk<128, 64>(a, st);
+    // 64 value columns per CTA halve the recomputed key side; with too few
+    // (batch, head) units to fill the SMs, 32 columns double the CTAs.
+    const bool few = (long long)(a->batch * a->heads_v) * (long long)(a->dv / 64) < 148;
+    if (a->dk == 128 && a->dv % 64 == 0 && !few) return run_chunk<128, 64>(a, st);
     if (a->dk == 64 && a->dv % 64 == 0) return run_chunk<64, 64>(a, st);
     if (a->dk == 32 && a->dv % 32 == 0) return run_chunk<32, 32>(a, st);
     if (a->dk == 64 && a->dv % 32 == 0) return run_chunk<64, 32>(a, st);
