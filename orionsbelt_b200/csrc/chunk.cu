@@ -42,7 +42,7 @@ __device__ __forceinline__ float to_f(float x) { return x; }
 __device__ __forceinline__ float to_f(__half x) { return __half2float(x); }
 __device__ __forceinline__ float to_f(__nv_bfloat16 x) { return __bfloat162float(x); }
 
-// One chunk's k, q (CH x DK, q times `scale`) and v (CH x DVB) tiles into
+// One chunk's k, q (CH x DK) and v (CH x DVB) tiles into
 // shared memory.  Every load of the thread is issued before the first store,
 // so a chunk waits for one global-memory latency rather than one per element;
 // rows past T read as zeros.
@@ -76,12 +76,53 @@ __device__ __forceinline__ void load_chunk_tiles(const kai_gdn_chunk_args &p, fl
     for (int u = 0; u < NKQ; ++u) {
         const int e = t + u * THREADS, r = e / DK, d = e % DK;
         K[r * LDK + d] = kr[u];
-        Q[r * LDK + d] = qr[u] * p.scale;
+        Q[r * LDK + d] = qr[u];
     }
 #pragma unroll
     for (int u = 0; u < NV; ++u) {
         const int e = t + u * THREADS, r = e / DVB, n = e % DVB;
         V[r * LDV + n] = vr[u];
+    }
+}
+
+// fp32 inputs: the same tiles by asynchronous 16-byte copies (cp.async), so
+// the next chunk's tiles land while this chunk computes; rows past T are
+// zero-filled (source size 0).  Pointers 16-byte aligned.
+__device__ __forceinline__ void cp_async16(void *dst, const void *src, bool valid) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(
+                     static_cast<uint32_t>(__cvta_generic_to_shared(dst))),
+                 "l"(src), "r"(valid ? 16 : 0)
+                 : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N> __device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
+template <int DK, int DVB, int LDK, int LDV>
+__device__ __forceinline__ void copy_chunk_tiles(const kai_gdn_chunk_args &p, float *K, float *Q, float *V, long long b,
+                                                 long long h, long long hk, long long c0, long long v0, int t) {
+    const long long T = (long long)p.seq, Hv = (long long)p.heads_v, Hk = (long long)p.heads_k;
+    const long long DV = (long long)p.dv;
+    const float *kp = static_cast<const float *>(p.k), *qp = static_cast<const float *>(p.q);
+    const float *vp = static_cast<const float *>(p.v);
+    constexpr int QK = DK / 4, QV = DVB / 4;  // 16-byte pieces per row
+#pragma unroll
+    for (int u = 0; u < CH * QK / THREADS; ++u) {
+        const int e = t + u * THREADS, r = e / QK, q = e % QK;
+        const long long tok = c0 + r;
+        const bool ok = tok < T;
+        const size_t i = ok ? ((size_t)(b * T + tok) * Hk + hk) * DK + 4 * q : 0;
+        cp_async16(K + r * LDK + 4 * q, kp + i, ok);
+        cp_async16(Q + r * LDK + 4 * q, qp + i, ok);
+    }
+#pragma unroll
+    for (int u = 0; u < (CH * QV + THREADS - 1) / THREADS; ++u) {
+        const int e = t + u * THREADS;
+        if (e < CH * QV) {
+            const int r = e / QV, q = e % QV;
+            const long long tok = c0 + r;
+            const bool ok = tok < T;
+            const size_t i = ok ? ((size_t)(b * T + tok) * Hv + h) * DV + v0 + 4 * q : 0;
+            cp_async16(V + r * LDV + 4 * q, vp + i, ok);
+        }
     }
 }
 
@@ -163,24 +204,35 @@ __device__ __forceinline__ void zero(float (&acc)[MI][NJ]) {
         for (int j = 0; j < NJ; ++j) acc[i][j] = 0.f;
 }
 
+// Rows of every tile 16-byte aligned (cp.async and float4 reads); K, Q, V
+// double-buffered when two sets fit in shared memory (the next chunk's
+// tiles are copied in while this one computes).
+template <int DK, int DVB>
+struct Geom {
+    static constexpr int LDK = DK + 4;   // 4 banks apart: 8 rows fill the 32 banks
+    static constexpr int LDV = DVB + 4;
+    static constexpr int LDP = CH + 4;
+    static constexpr size_t one = sizeof(float) * (2 * CH * LDK + CH * LDV);
+    static constexpr size_t rest = sizeof(float) * (2 * CH * LDP + DK * LDV + 4 * CH);
+    static constexpr int NB = 2 * one + rest <= 227 * 1024 ? 2 : 1;
+};
 template <int DK, int DVB>
 struct Smem {
-    static constexpr int LDK = DK + 4;   // rows 16-byte aligned; 4 banks apart, so 8 rows fill the 32 banks
-    static constexpr int LDV = DVB + 1;
-    static constexpr int LDP = CH + 4;   // rows 16-byte aligned
-    float K[CH * LDK];     // K, later K * exp(G_last - G)
-    float Q[CH * LDK];     // scale * Q, later * exp(G)
-    float V[CH * LDV];     // V, then beta (V - exp(G) K S), then V'
-    float A[CH * LDP];     // strictly lower A
-    float P[CH * LDP];     // lower-with-diagonal P
-    float S[DK * LDV];     // state block [DK][DVB]
+    using Gm = Geom<DK, DVB>;
+    static constexpr int LDK = Gm::LDK, LDV = Gm::LDV, LDP = Gm::LDP, NB = Gm::NB;
+    float K[NB][CH * LDK];
+    float Q[NB][CH * LDK];
+    float V[NB][CH * LDV];  // V, then beta (V - exp(G) K S), then V', then V' exp(G_last - G)
+    float A[CH * LDP];      // strictly lower A
+    float P[CH * LDP];      // lower-with-diagonal P (times scale)
+    float S[DK * LDV];      // state block [DK][DVB]
     float G[CH], eG[CH], eGl[CH], beta[CH];
 };
 
 template <int DK, int DVB, int SDT>
 __global__ void __launch_bounds__(THREADS, 1) chunk_scan_fp32_kernel(kai_gdn_chunk_args p) {
     using SM = Smem<DK, DVB>;
-    constexpr int LDK = SM::LDK, LDV = SM::LDV, LDP = SM::LDP;
+    constexpr int LDK = SM::LDK, LDV = SM::LDV, LDP = SM::LDP, NB = SM::NB;
     extern __shared__ __align__(16) unsigned char smem_raw[];
     SM &sm = *reinterpret_cast<SM *>(smem_raw);
 
@@ -201,21 +253,61 @@ __global__ void __launch_bounds__(THREADS, 1) chunk_scan_fp32_kernel(kai_gdn_chu
         sm.S[d * LDV + n] = S::load(st_in + (size_t)d * DV + v0 + n);
     }
 
-    for (long long c0 = 0; c0 < T; c0 += CH) {
-        // ---- loads (rows past T are zero padding with g = beta = 0)
+    // fp32 inputs with 16-byte aligned pointers are copied asynchronously,
+    // one chunk ahead when the tiles are double-buffered; others go through
+    // registers.
+    const bool async = p.in_dtype == KAI_GDN_F32 && ((reinterpret_cast<uintptr_t>(p.q) |
+                                                      reinterpret_cast<uintptr_t>(p.k) |
+                                                      reinterpret_cast<uintptr_t>(p.v)) % 16) == 0;
+    auto load_tiles = [&](long long cc0, int bi) {
+        if (async) {
+            copy_chunk_tiles<DK, DVB, LDK, LDV>(p, sm.K[bi], sm.Q[bi], sm.V[bi], b, h, hk, cc0, v0, t);
+            cp_async_commit();
+            return;
+        }
         switch (p.in_dtype) {
             case KAI_GDN_BF16:
-                load_chunk_tiles<__nv_bfloat16, DK, DVB, LDK, LDV>(p, sm.K, sm.Q, sm.V, b, h, hk, c0, v0, t);
+                load_chunk_tiles<__nv_bfloat16, DK, DVB, LDK, LDV>(p, sm.K[bi], sm.Q[bi], sm.V[bi], b, h, hk, cc0, v0, t);
                 break;
-            case KAI_GDN_F16: load_chunk_tiles<__half, DK, DVB, LDK, LDV>(p, sm.K, sm.Q, sm.V, b, h, hk, c0, v0, t); break;
-            default: load_chunk_tiles<float, DK, DVB, LDK, LDV>(p, sm.K, sm.Q, sm.V, b, h, hk, c0, v0, t);
+            case KAI_GDN_F16:
+                load_chunk_tiles<__half, DK, DVB, LDK, LDV>(p, sm.K[bi], sm.Q[bi], sm.V[bi], b, h, hk, cc0, v0, t);
+                break;
+            default: load_chunk_tiles<float, DK, DVB, LDK, LDV>(p, sm.K[bi], sm.Q[bi], sm.V[bi], b, h, hk, cc0, v0, t);
+        }
+    };
+    // gates of the next chunk, held by warp 0 (tokens 2 lane, 2 lane + 1)
+    float gn0 = 0.f, gn1 = 0.f, bn0 = 0.f, bn1 = 0.f;
+    auto load_gates = [&](long long cc0) {
+        const long long r0 = cc0 + 2 * t, r1 = r0 + 1;
+        gn0 = r0 < T ? p.g[(size_t)(b * T + r0) * Hv + h] : 0.f;
+        bn0 = r0 < T ? p.beta[(size_t)(b * T + r0) * Hv + h] : 0.f;
+        gn1 = r1 < T ? p.g[(size_t)(b * T + r1) * Hv + h] : 0.f;
+        bn1 = r1 < T ? p.beta[(size_t)(b * T + r1) * Hv + h] : 0.f;
+    };
+    if (NB == 2) load_tiles(0, 0);
+    if (t < 32) load_gates(0);
+
+    for (long long c0 = 0; c0 < T; c0 += CH) {
+        const int bi = NB == 2 ? (int)((c0 / CH) & 1) : 0;
+        float *const cK = sm.K[bi], *const cQ = sm.Q[bi], *const cV = sm.V[bi];
+        // ---- loads (rows past T are zero padding with g = beta = 0)
+        if (NB == 2) {
+            // this chunk's tiles were requested one chunk ago; request the next
+            // chunk's into the other buffer (last read by the previous chunk)
+            if (c0 + CH < T) {
+                load_tiles(c0 + CH, bi ^ 1);
+                if (async) cp_async_wait<1>();
+            } else if (async) {
+                cp_async_wait<0>();
+            }
+        } else {
+            load_tiles(c0, 0);
+            if (async) cp_async_wait<0>();
         }
         if (t < 32) {
             // In-chunk inclusive cumsum of g (2 rows per lane), beta.
-            float g0 = 0.f, g1 = 0.f, b0 = 0.f, b1 = 0.f;
-            long long r0 = c0 + 2 * t, r1 = r0 + 1;
-            if (r0 < T) { g0 = p.g[(size_t)(b * T + r0) * Hv + h]; b0 = p.beta[(size_t)(b * T + r0) * Hv + h]; }
-            if (r1 < T) { g1 = p.g[(size_t)(b * T + r1) * Hv + h]; b1 = p.beta[(size_t)(b * T + r1) * Hv + h]; }
+            const float g0 = gn0, g1 = gn1, b0 = bn0, b1 = bn1;
+            if (c0 + CH < T) load_gates(c0 + CH);
             float pair = g0 + g1, incl = pair;
 #pragma unroll
             for (int o = 1; o < 32; o <<= 1) {
@@ -233,7 +325,7 @@ __global__ void __launch_bounds__(THREADS, 1) chunk_scan_fp32_kernel(kai_gdn_chu
             sm.eG[t] = expf(sm.G[t]);
             sm.eGl[t] = expf(sm.G[CH - 1] - sm.G[t]);
         }
-        // ---- A = beta K K^T decay (s < r), P = Q K^T decay (s <= r)
+        // ---- A = beta K K^T decay (s < r), P = scale Q K^T decay (s <= r)
         {
             float kk[4][4], qk[4][4];
             zero(kk);
@@ -244,9 +336,9 @@ __global__ void __launch_bounds__(THREADS, 1) chunk_scan_fp32_kernel(kai_gdn_chu
                 float4 kr[4], qr[4], ks[4];
 #pragma unroll
                 for (int i = 0; i < 4; ++i) {
-                    kr[i] = *reinterpret_cast<const float4 *>(&sm.K[(ty + 16 * i) * LDK + d]);
-                    qr[i] = *reinterpret_cast<const float4 *>(&sm.Q[(ty + 16 * i) * LDK + d]);
-                    ks[i] = *reinterpret_cast<const float4 *>(&sm.K[(tx + 16 * i) * LDK + d]);
+                    kr[i] = *reinterpret_cast<const float4 *>(&cK[(ty + 16 * i) * LDK + d]);
+                    qr[i] = *reinterpret_cast<const float4 *>(&cQ[(ty + 16 * i) * LDK + d]);
+                    ks[i] = *reinterpret_cast<const float4 *>(&cK[(tx + 16 * i) * LDK + d]);
                 }
 #pragma unroll
                 for (int i = 0; i < 4; ++i)
@@ -269,7 +361,7 @@ __global__ void __launch_bounds__(THREADS, 1) chunk_scan_fp32_kernel(kai_gdn_chu
                     int r = ty + 16 * i, s = tx + 16 * j;
                     float dec = r >= s ? expf(sm.G[r] - sm.G[s]) : 0.f;
                     sm.A[r * LDP + s] = r > s ? sm.beta[r] * kk[i][j] * dec : 0.f;
-                    sm.P[r * LDP + s] = qk[i][j] * dec;
+                    sm.P[r * LDP + s] = p.scale * qk[i][j] * dec;
                 }
         }
         __syncthreads();
@@ -277,14 +369,14 @@ __global__ void __launch_bounds__(THREADS, 1) chunk_scan_fp32_kernel(kai_gdn_chu
         {
             float ks[4][DVB / 16];
             zero(ks);
-            mm_k4<4, DVB / 16>(ks, sm.K, LDK, sm.S, LDV, DK);
+            mm_k4<4, DVB / 16>(ks, cK, LDK, sm.S, LDV, DK);
 #pragma unroll
             for (int i = 0; i < 4; ++i) {
                 const int r = ty + 16 * i;
                 const float br = sm.beta[r], bg = br * sm.eG[r];
 #pragma unroll
                 for (int j = 0; j < DVB / 16; ++j) {
-                    float &x = sm.V[r * LDV + tx + 16 * j];
+                    float &x = cV[r * LDV + tx + 16 * j];
                     x = br * x - bg * ks[i][j];
                 }
             }
@@ -300,7 +392,7 @@ __global__ void __launch_bounds__(THREADS, 1) chunk_scan_fp32_kernel(kai_gdn_chu
             const int n = t / GT, j = t % GT, lane = t % 32;
             float x[RPT];
 #pragma unroll
-            for (int m = 0; m < RPT; ++m) x[m] = sm.V[(j + GT * m) * LDV + n];
+            for (int m = 0; m < RPT; ++m) x[m] = cV[(j + GT * m) * LDV + n];
 #pragma unroll 1
             for (int r = 0; r < CH - 1; ++r) {
                 const int owner = r % GT, mr = r / GT;
@@ -316,21 +408,21 @@ __global__ void __launch_bounds__(THREADS, 1) chunk_scan_fp32_kernel(kai_gdn_chu
                 }
             }
 #pragma unroll
-            for (int m = 0; m < RPT; ++m) sm.V[(j + GT * m) * LDV + n] = x[m];
-        }
-        // ---- Q *= exp(G);  K *= exp(G_last - G)
-        for (int e = t; e < CH * DK; e += THREADS) {
-            int r = e / DK, d = e % DK;
-            sm.Q[r * LDK + d] *= sm.eG[r];
-            sm.K[r * LDK + d] *= sm.eGl[r];
+            for (int m = 0; m < RPT; ++m) cV[(j + GT * m) * LDV + n] = x[m];
         }
         __syncthreads();
-        // ---- O = (Q exp(G)) S + P V'
+        // ---- O = scale exp(G) (Q S) + P V'
         {
             float o[4][DVB / 16];
             zero(o);
-            mm_k4<4, DVB / 16>(o, sm.Q, LDK, sm.S, LDV, DK);
-            mm_k4<4, DVB / 16>(o, sm.P, LDP, sm.V, LDV, CH);
+            mm_k4<4, DVB / 16>(o, cQ, LDK, sm.S, LDV, DK);
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                const float f = p.scale * sm.eG[ty + 16 * i];
+#pragma unroll
+                for (int j = 0; j < DVB / 16; ++j) o[i][j] *= f;
+            }
+            mm_k4<4, DVB / 16>(o, sm.P, LDP, cV, LDV, CH);
 #pragma unroll
             for (int i = 0; i < 4; ++i) {
                 long long tok = c0 + ty + 16 * i;
@@ -343,7 +435,13 @@ __global__ void __launch_bounds__(THREADS, 1) chunk_scan_fp32_kernel(kai_gdn_chu
             }
         }
         __syncthreads();
-        // ---- S = exp(G_last) S + (K exp(G_last - G))^T V'
+        // V'' = V' exp(G_last - G) in place (O has read V')
+        for (int e = t; e < CH * DVB; e += THREADS) {
+            const int r = e / DVB, n = e % DVB;
+            cV[r * LDV + n] *= sm.eGl[r];
+        }
+        __syncthreads();
+        // ---- S = exp(G_last) S + K^T V''
         {
             // thread rows MI ty .. MI ty + MI-1 when MI is a multiple of 4, else ty + 16 i
             constexpr int MI = DK / 16, NJ = DVB / 16;
@@ -356,9 +454,9 @@ __global__ void __launch_bounds__(THREADS, 1) chunk_scan_fp32_kernel(kai_gdn_chu
 #pragma unroll
                 for (int j = 0; j < NJ; ++j) acc[i][j] = egl * sm.S[row(i) * LDV + tx + 16 * j];
             if constexpr (V4)
-                mm_t4<MI, NJ>(acc, sm.K, LDK, sm.V, LDV, CH);
+                mm_t4<MI, NJ>(acc, cK, LDK, cV, LDV, CH);
             else
-                mm<MI, NJ, true, false>(acc, sm.K, LDK, sm.V, LDV, CH);
+                mm<MI, NJ, true, false>(acc, cK, LDK, cV, LDV, CH);
 #pragma unroll
             for (int i = 0; i < MI; ++i)
 #pragma unroll
