@@ -24,8 +24,9 @@
 //     M3b  V'^T      = V^T Tb^T - ((K S)^T exp(G)) Tb^T
 //     M4   S^T      += (V' exp(G_63 - G))^T K,   Y^T = V'^T P^T
 //   output group (warps 12-15): O = scale exp(G_r) X + Y from TMEM to global
-//                               memory, off the recurrence's critical path
-//                               (it evaluates the row factors itself).
+//                               memory, off the recurrence's critical path;
+//                               warp 12 also computes every chunk's gate
+//                               factors three chunks ahead.
 // The groups hand chunks over through mbarriers (key_ready / key_free,
 // o_full / o_empty); q, k, v arrive by TMA into a three-deep ring, the
 // key-side tiles are double buffered.  Every MMA is issued by one elected
@@ -74,22 +75,21 @@ struct KeyStage {
     unsigned char P[C * C * 2];
     unsigned char Tb[C * C * 2];
 };
-// Gate factors of one chunk (a three-deep ring: the key group fills chunk
-// c+1's while it works on chunk c and the state group may still read c-1's).
+// Gate factors of one chunk, in a four-deep ring filled three chunks ahead by
+// the output group (fac_full[slot] marks a slot published).
 struct Factors {
     float G[C], beta[C], eG[C], eGl[C];
     float u[C];       // exp(G_r - G_{16 floor(r/16)})
     float w[3][C];    // w[b-1][s] = exp(G_{16b} - G_s) for s < 16b
 };
-constexpr int NS_F = 3;
+constexpr int NS_F = 4;
 struct WsSmem {
     InStage in[NS_IN];
     KeyStage ks[NS_K];
     Factors fac[NS_F];
     float Af[10 * BSZ];
     float Tf[10 * BSZ];
-    float ofs[2][C];  // scale exp(G_r) of the chunk the output group writes
-    uint64_t full_in[NS_IN], key_ready[NS_K], key_free[NS_K], o_full, o_empty, bar_k, bar_s;
+    uint64_t full_in[NS_IN], key_ready[NS_K], key_free[NS_K], o_full, o_empty, bar_k, bar_s, fac_full[NS_F];
     uint32_t tmem;
     int stop;
 };
@@ -471,33 +471,6 @@ __device__ __forceinline__ void store_o(const kai_gdn_chunk_args &p, size_t base
     }
 }
 
-// exp(gl) of the chunk whose gates the lane holds: the same sums in the same
-// order as chunk_gates, so the state group's decay equals the key group's.
-__device__ __forceinline__ float chunk_gamma(const Gates &gt, int lane) {
-    const float pair = gt.g0 + gt.g1;
-    float incl = pair;
-#pragma unroll
-    for (int o = 1; o < 32; o <<= 1) {
-        const float u = __shfl_up_sync(0xffffffffu, incl, o);
-        if (lane >= o) incl += u;
-    }
-    return expf(__shfl_sync(0xffffffffu, incl, 31));
-}
-
-// scale exp(G_r) for the tokens r = 2 lane, 2 lane + 1 of the chunk whose
-// gates the lane holds (the same sums as chunk_gates), into ofs[r].
-__device__ __forceinline__ void out_scales(float *ofs, const Gates &gt, float scale, int lane) {
-    const float pair = gt.g0 + gt.g1;
-    float incl = pair;
-#pragma unroll
-    for (int o = 1; o < 32; o <<= 1) {
-        const float u = __shfl_up_sync(0xffffffffu, incl, o);
-        if (lane >= o) incl += u;
-    }
-    const float G0 = (incl - pair) + gt.g0, G1 = incl;
-    *reinterpret_cast<float2 *>(ofs + 2 * lane) = make_float2(scale * expf(G0), scale * expf(G1));
-}
-
 __device__ __forceinline__ float ex2(float x) {
     float y;
     asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
@@ -530,6 +503,7 @@ __global__ void __launch_bounds__(NT, 1)
         }
         mbar_init(&sm.o_full, 1);
         mbar_init(&sm.o_empty, 1);
+        for (int s = 0; s < NS_F; ++s) mbar_init(&sm.fac_full[s], 1);
         mbar_init(&sm.bar_k, 1);
         mbar_init(&sm.bar_s, 1);
         sm.stop = 0;
@@ -578,11 +552,10 @@ __global__ void __launch_bounds__(NT, 1)
         // Per chunk c:  all 8 warps: E1 (A and P from [K;Q] K^T);
         //   warps 0-3: the inverse, whose last step writes its four blocks
         //     of Tb directly;
-        //   warps 4-7 meanwhile: the gates of chunk c+1, the [K;Q] K^T MMA
-        //     of chunk c+1 (warp KW), and Tb of the blocks the inverse
-        //     finished early;
+        //   warps 4-7 meanwhile: the [K;Q] K^T MMA of chunk c+1 (warp KW)
+        //     and Tb of the blocks the inverse finished early;
         //   then hand the chunk over.
-        constexpr int KT = 224, KW = KT / 32, GW = 4;  // TMA thread and its warp (MMA); the warp computing gates
+        constexpr int KT = 224, KW = KT / 32;  // TMA thread and its warp (MMA)
         int loaded = 0;  // chunks whose loads were issued (thread KT)
         bool fail = false;  // a wait of this thread ran out
         auto issue_m1 = [&](int cc) {  // warp KW (converged), loads of chunk cc complete
@@ -613,12 +586,6 @@ __global__ void __launch_bounds__(NT, 1)
             if (!mbar_wait(&sm.full_in[0], 0, err)) fail = true;
             issue_m1(0);
         }
-        Gates gt;
-        if (warp == GW) {
-            load_gates(gt, p, b, h, 0, lane);
-            chunk_gates(sm.fac[0], gt, lane);
-            if (nch > 1) load_gates(gt, p, b, h, C, lane);
-        }
         const int q4 = warp & 3, hc = warp >> 2;
         int c = 0;
         for (; c < nch; ++c) {
@@ -632,6 +599,7 @@ __global__ void __launch_bounds__(NT, 1)
             }
             if (!mbar_wait(&sm.full_in[si], (c / NS_IN) & 1, err)) fail = true;
             if (!mbar_wait(&sm.bar_k, c & 1, err)) fail = true;  // [K;Q] K^T of this chunk
+            if (!mbar_wait(&sm.fac_full[c % NS_F], (c / NS_F) & 1, err)) fail = true;  // its gate factors
             if (kg_any(fail || *stop)) break;
             fence_after_sync();
             // ------------------------------------------ E1: A (fp32, block-packed) and P (tile)
@@ -698,10 +666,6 @@ __global__ void __launch_bounds__(NT, 1)
                     if (!mbar_wait(&sm.full_in[(c + 1) % NS_IN], ((c + 1) / NS_IN) & 1, err)) fail = true;
                     issue_m1(c + 1);
                 }
-                if (warp == GW && c + 1 < nch) {
-                    chunk_gates(sm.fac[(c + 1) % NS_F], gt, lane);
-                    if (c + 2 < nch) load_gates(gt, p, b, h, (long long)(c + 2) * C, lane);
-                }
                 const int ht = t - 128;
                 inv_await();  // diagonal blocks, T10 and T32 are final
                 for (int e = ht; e < 6 * 32; e += 128) tb_blocks<IT>(sm.Tf, kst, fa, e);
@@ -719,12 +683,10 @@ __global__ void __launch_bounds__(NT, 1)
         // =============================================================== state group
         const int st = t - KG, sq = st / 32, i = 32 * sq + lane;  // i = value index = TMEM lane
         const uint32_t lb = 32u * sq;
-        // Decay of the next chunk, computed here from the gates (the same sums
-        // as the key group) so that E4 can write gamma S back in its one pass.
-        Gates gn;
-        load_gates(gn, p, b, h, 0, lane);
-        const float gamma0 = chunk_gamma(gn, lane);
-        if (nch > 1) load_gates(gn, p, b, h, C, lane);
+        // The decay exp(G_63) of a chunk is the last entry of its exp(G) factors.
+        bool fail = false;  // a wait of this thread ran out
+        if (nch > 0 && !mbar_wait(&sm.fac_full[0], 0, err)) fail = true;
+        const float gamma0 = nch > 0 ? sm.fac[0].eG[C - 1] : 1.f;
         // initial state: gamma_0 S^T into TMEM, the unscaled 16-bit copy beside it
         {
             const size_t sb = (size_t)unit * D * D + i;
@@ -745,7 +707,6 @@ __global__ void __launch_bounds__(NT, 1)
         }
         fence_before_sync();
         uint32_t ph = 0;
-        bool fail = false;  // a wait of this thread ran out
         int c = 0;
         for (; c < nch; ++c) {
             const int si = c % NS_IN, sk = c % NS_K;
@@ -771,8 +732,8 @@ __global__ void __launch_bounds__(NT, 1)
             const bool more = c + 1 < nch;
             float gamma_next = 1.f;
             if (more) {
-                gamma_next = chunk_gamma(gn, lane);
-                if (c + 2 < nch) load_gates(gn, p, b, h, (long long)(c + 2) * C, lane);
+                if (!mbar_wait(&sm.fac_full[(c + 1) % NS_F], ((c + 1) / NS_F) & 1, err)) fail = true;
+                gamma_next = sm.fac[(c + 1) % NS_F].eG[C - 1];
             }
             if (!mbar_wait(&sm.bar_s, ph, err)) fail = true;
             ph ^= 1;
@@ -917,22 +878,29 @@ __global__ void __launch_bounds__(NT, 1)
     } else {
         // =============================================================== output group
         // O = scale exp(G_r) X + Y: X^T (M3a) and Y^T (M4) sit in separate
-        // accumulators; warp 12 evaluates the row factors from the gates (the
-        // same sums as the key group) into a double buffer, which the group's
-        // barrier at the top of the chunk publishes to the other three warps.
+        // accumulators.  Warp 12 also computes every chunk's gate factors,
+        // NS_F - 1 chunks ahead (its gates loaded one chunk before that), and
+        // publishes them on fac_full.
         const int ot = t - KG - SG, oq = ot / 32, i = 32 * oq + lane;
         const uint32_t lb = 32u * oq;
         const size_t orow = (size_t)Hv * D;  // output row stride (elements)
-        Gates go;
-        if (oq == 0) load_gates(go, p, b, h, 0, lane);
+        Gates go{};
+        auto publish_factors = [&](int cc) {  // warp 12; go holds chunk cc's gates
+            const Gates cur = go;
+            if (cc + 1 < nch) load_gates(go, p, b, h, (long long)(cc + 1) * C, lane);
+            chunk_gates(sm.fac[cc % NS_F], cur, lane);
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&sm.fac_full[cc % NS_F]);
+        };
+        if (oq == 0 && nch > 0) {
+            load_gates(go, p, b, h, 0, lane);
+            for (int cc = 0; cc < NS_F - 1 && cc < nch; ++cc) publish_factors(cc);
+        }
         bool fail = false;
         int c = 0;
         for (; c < nch; ++c) {
-            float *ofs = sm.ofs[c & 1];
-            if (oq == 0) {
-                out_scales(ofs, go, scale, lane);
-                if (c + 1 < nch) load_gates(go, p, b, h, (long long)(c + 1) * C, lane);
-            }
+            if (oq == 0 && c + NS_F - 1 < nch) publish_factors(c + NS_F - 1);
+            const float *eg = sm.fac[c % NS_F].eG;  // published NS_F - 1 chunks ago
             if (!mbar_wait(&sm.o_full, c & 1, err)) fail = true;
             if (og_any(fail || *stop)) break;
             fence_after_sync();
@@ -953,11 +921,11 @@ __global__ void __launch_bounds__(NT, 1)
                 reg_fence16(&y[16]);
 #pragma unroll
                 for (int r = 0; r < 32; r += 4) {
-                    const float4 f = *reinterpret_cast<const float4 *>(ofs + 32 * half + r);
-                    x[r] = fmaf(f.x, x[r], y[r]);
-                    x[r + 1] = fmaf(f.y, x[r + 1], y[r + 1]);
-                    x[r + 2] = fmaf(f.z, x[r + 2], y[r + 2]);
-                    x[r + 3] = fmaf(f.w, x[r + 3], y[r + 3]);
+                    const float4 f = *reinterpret_cast<const float4 *>(eg + 32 * half + r);
+                    x[r] = fmaf(scale * f.x, x[r], y[r]);
+                    x[r + 1] = fmaf(scale * f.y, x[r + 1], y[r + 1]);
+                    x[r + 2] = fmaf(scale * f.z, x[r + 2], y[r + 2]);
+                    x[r + 3] = fmaf(scale * f.w, x[r + 3], y[r + 3]);
                 }
                 if (half == 1) {
                     fence_before_sync();
