@@ -514,14 +514,38 @@ def run_rows(args, peaks) -> dict:
     av, B1 = torch.randn(128, device="cuda"), torch.randn((128, 4096), device="cuda")
     cv = torch.empty(4096, device="cuda")
     ms = _time(lambda: ops.matmul(av[None], B1, cv[None]), reps, flush)
-    bw_row("a4_gemv", "GEMV K=128 N=4096 fp32", metrics.matmul_bytes(1, 128, 4096), ms, "gemv_rows_kernel")
+    bw_row("a4_gemv", "GEMV K=128 N=4096 fp32", metrics.matmul_bytes(1, 128, 4096), ms, "gemv_slab_kernel")
     Am, Bm = torch.randn((64, 128), device="cuda"), torch.randn((128, 2048), device="cuda")
     Cm = torch.empty((64, 2048), device="cuda")
     ms = _time(lambda: ops.matmul(Am, Bm, Cm), reps, flush)
     bw_row("a4_matmul", "matmul M=64 K=128 N=2048 fp32 (reference op order)", metrics.matmul_bytes(64, 128, 2048),
-           ms, "sgemm_tile_kernel")
+           ms, "sgemm_fullk_kernel")
     out["a4_matmul"]["tflops"] = round(2 * 64 * 128 * 2048 / (ms / 1e3) / 1e12, 3)
     del av, B1, cv, Am, Bm, Cm
+    # a5: the GDN-1 decode step on one config-1 layer, timed like the f4 row
+    # (one launch after the L2 flush) for the comparison; the headline times 24
+    d = synth.device_gdn(64, 1, 16, 32, 128, 128, g_scale=0.1, seed=15, in_dtype=torch.bfloat16, state_std=0.02)
+    q1, k1, v1, g1, b1 = (d[n][:, 0].contiguous() for n in ("q", "k", "v", "g", "beta"))
+    o1 = torch.empty((64, 32, 128), dtype=torch.bfloat16, device="cuda")
+    S1 = d["S0"]
+    ms = _time(lambda: ops.delta_rule_decode(S1, q1, k1, v1, g1, b1, o1, scale=1.0), reps, flush)
+    bw_row("a5_decode_cfg1_layer", "GDN-1 decode step, one config-1 layer, one launch after the L2 flush",
+           metrics.decode_bytes(64, 16, 32, 128, 128), ms, "decode_step_kernel<128, f32>")
+    del d, q1, k1, v1, g1, b1, o1, S1
+    # f4: the GDN-2 decode step (per-channel decay, erase and write gates) on
+    # one config-1 layer: B=64, 16 key / 32 value heads, 128x128 fp32 state
+    d = synth.device_gdn(64, 1, 16, 32, 128, 128, g_scale=0.1, seed=15, in_dtype=torch.bfloat16, state_std=0.02)
+    g2 = -torch.nn.functional.softplus(synth.device_normal((64, 32, 128), 15, 1)) * 0.1
+    bg2 = torch.sigmoid(synth.device_normal((64, 32, 128), 15, 2))
+    wg2 = torch.sigmoid(synth.device_normal((64, 32, 128), 15, 3))
+    o2 = torch.empty((64, 32, 128), dtype=torch.bfloat16, device="cuda")
+    q2, k2, v2 = (d[n][:, 0].contiguous() for n in ("q", "k", "v"))
+    S2 = d["S0"]
+    ms = _time(lambda: ops.gdn2_delta_rule_decode(S2, q2, k2, v2, g2, bg2, wg2, o2, scale=1.0), reps, flush)
+    bw_row("f4_gdn2_decode_cfg1", "GDN-2 decode step, one config-1 layer (B=64, 16/32 heads, 128x128 fp32 state, "
+           "bf16 q/k/v/o, fp32 per-channel gates)", metrics.gdn2_decode_bytes(64, 16, 32, 128, 128), ms,
+           "decode_step_kernel<128, f32, GDN-2>")
+    del d, g2, bg2, wg2, o2, q2, k2, v2, S2
     # a6: chunk scan at config 0 (fp32 throughout) and config 3 (fp16 in, fp16 state, strong decay)
     for name, c, dt, sdt, kern in [
             ("a6_chunk_cfg0", dict(B=1, T=2048, g=0.1), torch.float32, torch.float32,

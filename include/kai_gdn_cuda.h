@@ -189,6 +189,29 @@ typedef struct kai_gdn_decode_args {
 } kai_gdn_decode_args;
 KAI_GDN_API int kai_run_gdn_delta_rule_decode_sm100a(const kai_gdn_decode_args *args, void *stream);
 
+/* Single-token matrix-state step of the GDN-2 form (decoupled gating) for
+ * every (batch, value head), the recurrence of bench/gdn2_reference.py:58-145
+ * (gdn2_recurrent, one token, no q/k normalisation).  Per (b, h), with key
+ * head hk = h / (heads_v / heads_k):
+ *   S[j][:] *= exp(g[j]);  erase = S^T (b_gate . k);  write = w_gate . v;
+ *   S += k (write - erase)^T;  o = scale * S^T q
+ * The gates are per channel: g and b_gate per key channel, w_gate per value
+ * channel.  Shapes, dtypes and alignment as kai_gdn_decode_args. */
+typedef struct kai_gdn2_decode_args {
+    void *state;         /* [batch][heads_v][dk][dv], state_dtype, in place */
+    const void *q;       /* [batch][heads_k][dk], in_dtype                  */
+    const void *k;       /* [batch][heads_k][dk], in_dtype                  */
+    const void *v;       /* [batch][heads_v][dv], in_dtype                  */
+    const float *g;      /* [batch][heads_v][dk] log-decay per key channel  */
+    const float *b_gate; /* [batch][heads_v][dk] erase gate                 */
+    const float *w_gate; /* [batch][heads_v][dv] write gate                 */
+    void *o;             /* [batch][heads_v][dv], out_dtype                 */
+    size_t batch, heads_k, heads_v, dk, dv;
+    float scale;
+    int in_dtype, state_dtype, out_dtype;
+} kai_gdn2_decode_args;
+KAI_GDN_API int kai_run_gdn2_delta_rule_decode_sm100a(const kai_gdn2_decode_args *args, void *stream);
+
 /* Chunkwise (WY / UT-transform) gated delta-rule scan over a whole sequence,
  * for every (batch, value head), chunk length `chunk` (64).  Equal, up to
  * rounding, to applying the decode step above for t = 0 .. seq-1 with

@@ -219,6 +219,32 @@ class _Oracle(_Kernels):
                                     C.c_float(scale), C.c_int(nthreads))
         return S, o
 
+    def gdn2_decode(self, S, q, k, v, g, bgate, wgate, scale=1.0, nthreads=0):
+        """GDN-2 step.  S [B][Hv][dk][dv], q,k [B][Hk][dk], v,wgate [B][Hv][dv], g,bgate [B][Hv][dk]."""
+        S = _f32(S).copy()
+        q, k, v, g, bgate, wgate = map(_f32, (q, k, v, g, bgate, wgate))
+        B, Hv, dk, dv = S.shape
+        Hk = q.shape[1]
+        o = np.empty((B, Hv, dv), np.float32)
+        self.lib.orc_gdn2_decode(_p(S, np.float32), _p(q, np.float32), _p(k, np.float32), _p(v, np.float32),
+                                 _p(g, np.float32), _p(bgate, np.float32), _p(wgate, np.float32),
+                                 _p(o, np.float32), _sz(B), _sz(Hk), _sz(Hv), _sz(dk), _sz(dv),
+                                 C.c_float(scale), C.c_int(nthreads))
+        return S, o
+
+    def gdn2_seq(self, S, q, k, v, g, bgate, wgate, scale=1.0, nthreads=0):
+        """GDN-2 token loop.  q,k [B][T][Hk][dk], v,wgate [B][T][Hv][dv], g,bgate [B][T][Hv][dk]."""
+        S = _f32(S).copy()
+        q, k, v, g, bgate, wgate = map(_f32, (q, k, v, g, bgate, wgate))
+        B, T, Hk, dk = q.shape
+        Hv, dv = v.shape[2], v.shape[3]
+        o = np.empty((B, T, Hv, dv), np.float32)
+        self.lib.orc_gdn2_seq(_p(S, np.float32), _p(q, np.float32), _p(k, np.float32), _p(v, np.float32),
+                              _p(g, np.float32), _p(bgate, np.float32), _p(wgate, np.float32),
+                              _p(o, np.float32), _sz(B), _sz(T), _sz(Hk), _sz(Hv), _sz(dk), _sz(dv),
+                              C.c_float(scale), C.c_int(nthreads))
+        return S, o
+
     def chunk_wy(self, S, q, k, v, g, beta, scale=1.0, chunk=64, nthreads=0):
         """Chunked WY form in float64 (same layouts as delta_rule_seq)."""
         S = _f32(S).copy()

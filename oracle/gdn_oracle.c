@@ -314,6 +314,80 @@ void orc_delta_rule_seq(float *S, const float *q, const float *k, const float *v
 }
 
 /* ------------------------------------------------------------------------
+ * f4: GDN-2 (decoupled gating) matrix-state step for one head, S[dk][dv]
+ * row-major; bench/gdn2_reference.py:58-145 (gdn2_recurrent), per token:
+ *   S[j,i] *= exp(g_j);  erase_i = sum_j (b_j k_j) S[j,i];
+ *   vn_i = w_i v_i - erase_i;  S[j,i] += k_j vn_i;  o_i = sum_j q_j S[j,i].
+ * g is the per-key-channel log-decay, b the erase gate, w the write gate (all
+ * already activated, as the reference takes them); `q` is used as given.
+ * ---------------------------------------------------------------------- */
+void orc_gdn2_step(float *S, const float *k, const float *v, const float *q, const float *g,
+                   const float *bgate, const float *wgate, float *out, size_t dk, size_t dv) {
+    for (size_t j = 0; j < dk; j++) {
+        const float a = expf(g[j]);
+        for (size_t i = 0; i < dv; i++) S[j * dv + i] *= a;
+    }
+    for (size_t i = 0; i < dv; i++) {
+        float erase = 0.0f;
+        for (size_t j = 0; j < dk; j++) erase += (bgate[j] * k[j]) * S[j * dv + i];
+        const float vn = wgate[i] * v[i] - erase;
+        for (size_t j = 0; j < dk; j++) S[j * dv + i] += k[j] * vn;
+        float o = 0.0f;
+        for (size_t j = 0; j < dk; j++) o += q[j] * S[j * dv + i];
+        out[i] = o;
+    }
+}
+
+/* Batched GDN-2 decode step with grouped value heads:
+ *   S: [B][Hv][dk][dv], q,k: [B][Hk][dk], v: [B][Hv][dv], g,bgate: [B][Hv][dk],
+ *   wgate: [B][Hv][dv], o: [B][Hv][dv].  q is multiplied by `scale`. */
+void orc_gdn2_decode(float *S, const float *q, const float *k, const float *v, const float *g,
+                     const float *bgate, const float *wgate, float *o, size_t B, size_t Hk, size_t Hv,
+                     size_t dk, size_t dv, float scale, int nthreads) {
+    size_t group = Hv / Hk;
+    long units = (long)(B * Hv);
+#ifdef _OPENMP
+    int nt = nthreads > 0 ? nthreads : omp_get_max_threads();
+#pragma omp parallel for schedule(static) num_threads(nt)
+#endif
+    for (long u = 0; u < units; ++u) {
+        size_t b = (size_t)u / Hv, h = (size_t)u % Hv, hk = h / group;
+        float qs[512];
+        const float *qh = q + (b * Hk + hk) * dk;
+        for (size_t j = 0; j < dk; ++j) qs[j] = qh[j] * scale;
+        orc_gdn2_step(S + (b * Hv + h) * dk * dv, k + (b * Hk + hk) * dk, v + (b * Hv + h) * dv, qs,
+                      g + (b * Hv + h) * dk, bgate + (b * Hv + h) * dk, wgate + (b * Hv + h) * dv,
+                      o + (b * Hv + h) * dv, dk, dv);
+    }
+}
+
+/* Token loop of the GDN-2 step (gdn2_recurrent itself):
+ *   q,k: [B][T][Hk][dk], v,wgate: [B][T][Hv][dv], g,bgate: [B][T][Hv][dk],
+ *   S: [B][Hv][dk][dv] (initial in, final out), o: [B][T][Hv][dv]. */
+void orc_gdn2_seq(float *S, const float *q, const float *k, const float *v, const float *g,
+                  const float *bgate, const float *wgate, float *o, size_t B, size_t T, size_t Hk,
+                  size_t Hv, size_t dk, size_t dv, float scale, int nthreads) {
+    size_t group = Hv / Hk;
+    long units = (long)(B * Hv);
+#ifdef _OPENMP
+    int nt = nthreads > 0 ? nthreads : omp_get_max_threads();
+#pragma omp parallel for schedule(dynamic, 1) num_threads(nt)
+#endif
+    for (long u = 0; u < units; ++u) {
+        size_t b = (size_t)u / Hv, h = (size_t)u % Hv, hk = h / group;
+        float qs[512];
+        float *Sh = S + (b * Hv + h) * dk * dv;
+        for (size_t t = 0; t < T; ++t) {
+            const float *qt = q + ((b * T + t) * Hk + hk) * dk;
+            for (size_t j = 0; j < dk; ++j) qs[j] = qt[j] * scale;
+            const size_t vi = (b * T + t) * Hv + h;
+            orc_gdn2_step(Sh, k + ((b * T + t) * Hk + hk) * dk, v + vi * dv, qs, g + vi * dk, bgate + vi * dk,
+                          wgate + vi * dv, o + vi * dv, dk, dv);
+        }
+    }
+}
+
+/* ------------------------------------------------------------------------
  * a6: chunkwise WY form, in double, written from the math of
  * docs/GDN_ARCHITECTURE_AUDIT.md:142-153 (the reference has no code for it; it
  * reaches it through HF transformers' torch_chunk_gated_delta_rule).  Per

@@ -27,6 +27,13 @@ class DecodeArgs(C.Structure):
                 ("scale", _f), ("in_dtype", _i), ("state_dtype", _i), ("out_dtype", _i)]
 
 
+class Gdn2DecodeArgs(C.Structure):
+    """struct kai_gdn2_decode_args."""
+    _fields_ = [("state", _vp), ("q", _vp), ("k", _vp), ("v", _vp), ("g", _vp), ("b_gate", _vp), ("w_gate", _vp),
+                ("o", _vp), ("batch", _sz), ("heads_k", _sz), ("heads_v", _sz), ("dk", _sz), ("dv", _sz),
+                ("scale", _f), ("in_dtype", _i), ("state_dtype", _i), ("out_dtype", _i)]
+
+
 class ChunkArgs(C.Structure):
     """struct kai_gdn_chunk_args."""
     _fields_ = [("q", _vp), ("k", _vp), ("v", _vp), ("g", _vp), ("beta", _vp), ("state", _vp), ("o", _vp),
@@ -59,6 +66,7 @@ SIGNATURES = {
     "kai_run_gdn_causal_dwconv1d_k4_sm100a": (_i, [_vp, _vp, _vp, _vp, _i, _sz, _sz, _sz, _vp]),
     "kai_run_gdn_matmul_f32_sm100a": (_i, [_vp, _vp, _vp, _sz, _sz, _sz, _vp]),
     "kai_run_gdn_delta_rule_decode_sm100a": (_i, [C.POINTER(DecodeArgs), _vp]),
+    "kai_run_gdn2_delta_rule_decode_sm100a": (_i, [C.POINTER(Gdn2DecodeArgs), _vp]),
     "kai_run_gdn_chunk_delta_rule_sm100a": (_i, [C.POINTER(ChunkArgs), _vp]),
     # control
     "kai_gdn_cuda_set_device": (_i, [_i]),

@@ -10,6 +10,11 @@
 // 128 x 64), so the kernel is bound by 2 * dk * dv * sizeof(state) bytes per
 // head.
 //
+// The GDN-2 form (decoupled gating, bench/gdn2_reference.py:58-145) runs in
+// the same kernel: per-key-channel decay exp(g_j) instead of one scalar, the
+// erase vector b_j k_j in the retrieve, and delta_i = w_i v_i - erase_i (no
+// beta).
+//
 // Thread layout: DVB/4 threads cover one row of the block with 16-byte
 // accesses (16 threads, 256 contiguous bytes at DVB = 64), and the 256 threads
 // take rows j = rg, rg + RPP, ...  Column sums over j are per-thread partials
@@ -59,13 +64,27 @@ __device__ __forceinline__ void st4(void *base, size_t idx, float4 v) {
     *reinterpret_cast<uint2 *>(static_cast<uint16_t *>(base) + idx) = u;
 }
 
+// Kernel parameters of both forms: beta (GDN-1) or the erase gate b and the
+// write gate w (GDN-2).
+struct DecodeP {
+    void *state;
+    const void *q, *k, *v;
+    const float *g;     // GDN-1: [B][Hv];  GDN-2: [B][Hv][dk]
+    const float *beta;  // GDN-1: [B][Hv];  GDN-2: erase gate [B][Hv][dk]
+    const float *w;     // GDN-2: write gate [B][Hv][dv]
+    void *o;
+    long long heads_k, heads_v;
+    float scale;
+    int in_dtype, out_dtype;
+};
+
 // One CTA per (b, value head, block of DVB value columns).  The value
 // columns of S are independent (kv_i and o_i use only column i), so a head
 // splits into D/DVB CTAs with no exchange; each reads the head's whole k and
 // q.  Smaller blocks make more, shorter CTAs: the last wave of a launch is
 // less empty.
-template <int D, int DVB, int NTH, int MINB, int SDT>
-__global__ void __launch_bounds__(NTH, MINB) decode_step_kernel(kai_gdn_decode_args p) {
+template <int D, int DVB, int NTH, int MINB, int SDT, bool G2>
+__global__ void __launch_bounds__(NTH, MINB) decode_step_kernel(DecodeP p) {
     constexpr int DK = D, DV = D;
     constexpr int CPR = DVB / 4;       // threads per row
     constexpr int RPP = NTH / CPR;     // rows per pass
@@ -74,6 +93,7 @@ __global__ void __launch_bounds__(NTH, MINB) decode_step_kernel(kai_gdn_decode_a
     static_assert(RPT >= 1 && DK % RPP == 0, "shape");
 
     __shared__ float ks[DK], qs[DK], vs[DVB], dl[DVB];
+    __shared__ float eg[G2 ? DK : 1], bk[G2 ? DK : 1];  // GDN-2: exp(g_j), b_j k_j
     __shared__ float red[RPP][DVB + 4];
 
     const long long unit = blockIdx.x / NB;   // b * Hv + h
@@ -92,21 +112,29 @@ __global__ void __launch_bounds__(NTH, MINB) decode_step_kernel(kai_gdn_decode_a
     for (int j = t; j < DK; j += NTH) {
         ks[j] = load_any(p.k, kq + j, p.in_dtype);
         qs[j] = __fmul_rn(load_any(p.q, kq + j, p.in_dtype), p.scale);
+        if (G2) {
+            eg[j] = expf(p.g[(size_t)unit * DK + j]);
+            bk[j] = __fmul_rn(p.beta[(size_t)unit * DK + j], ks[j]);
+        }
     }
-    for (int i = t; i < DVB; i += NTH) vs[i] = load_any(p.v, (size_t)unit * DV + cb + i, p.in_dtype);
-    const float a = expf(p.g[unit]);
-    const float beta = p.beta[unit];
+    for (int i = t; i < DVB; i += NTH) {
+        const float vi = load_any(p.v, (size_t)unit * DV + cb + i, p.in_dtype);
+        vs[i] = G2 ? __fmul_rn(p.w[(size_t)unit * DV + cb + i], vi) : vi;
+    }
+    const float a = G2 ? 1.f : expf(p.g[unit]);
+    const float beta = G2 ? 1.f : p.beta[unit];
     __syncthreads();
 
     // Decay and retrieve: kv partial over this thread's rows.
     float4 kv = make_float4(0.f, 0.f, 0.f, 0.f);
 #pragma unroll
     for (int r = 0; r < RPT; ++r) {
-        const float kj = ks[rg + RPP * r];
-        s[r].x = __fmul_rn(s[r].x, a);
-        s[r].y = __fmul_rn(s[r].y, a);
-        s[r].z = __fmul_rn(s[r].z, a);
-        s[r].w = __fmul_rn(s[r].w, a);
+        const int j = rg + RPP * r;
+        const float kj = G2 ? bk[j] : ks[j], aj = G2 ? eg[j] : a;
+        s[r].x = __fmul_rn(s[r].x, aj);
+        s[r].y = __fmul_rn(s[r].y, aj);
+        s[r].z = __fmul_rn(s[r].z, aj);
+        s[r].w = __fmul_rn(s[r].w, aj);
         kv.x = fmaf(s[r].x, kj, kv.x);
         kv.y = fmaf(s[r].y, kj, kv.y);
         kv.z = fmaf(s[r].z, kj, kv.z);
@@ -118,7 +146,7 @@ __global__ void __launch_bounds__(NTH, MINB) decode_step_kernel(kai_gdn_decode_a
         float acc = 0.f;
 #pragma unroll
         for (int g2 = 0; g2 < RPP; ++g2) acc += red[g2][i];
-        dl[i] = (vs[i] - acc) * beta;
+        dl[i] = G2 ? vs[i] - acc : (vs[i] - acc) * beta;
     }
     __syncthreads();
 
@@ -159,23 +187,49 @@ template <> struct DecodeGeo<32> { static constexpr int DVB = 32, NTH = 256, MIN
 template <> struct DecodeGeo<64> { static constexpr int DVB = 64, NTH = 256, MINB = 3; };
 template <> struct DecodeGeo<128> { static constexpr int DVB = 64, NTH = 256, MINB = 3; };
 
-template <int D>
-int run_decode(const kai_gdn_decode_args *a, cudaStream_t st) {
+template <int D, bool G2>
+int run_decode(const DecodeP &p, size_t units, int state_dtype, cudaStream_t st) {
     using G = DecodeGeo<D>;
-    const long long ctas = (long long)(a->batch * a->heads_v) * (D / G::DVB);
+    const long long ctas = (long long)units * (D / G::DVB);
     if (ctas > 0x7fffffffll) return set_error(KAI_GDN_ERR_UNSUPPORTED, "decode: too many heads");
-    switch (a->state_dtype) {
+    switch (state_dtype) {
         case KAI_GDN_F32:
-            decode_step_kernel<D, G::DVB, G::NTH, G::MINB, KAI_GDN_F32><<<(unsigned)ctas, G::NTH, 0, st>>>(*a);
+            decode_step_kernel<D, G::DVB, G::NTH, G::MINB, KAI_GDN_F32, G2><<<(unsigned)ctas, G::NTH, 0, st>>>(p);
             break;
         case KAI_GDN_F16:
-            decode_step_kernel<D, G::DVB, G::NTH, G::MINB, KAI_GDN_F16><<<(unsigned)ctas, G::NTH, 0, st>>>(*a);
+            decode_step_kernel<D, G::DVB, G::NTH, G::MINB, KAI_GDN_F16, G2><<<(unsigned)ctas, G::NTH, 0, st>>>(p);
             break;
         case KAI_GDN_BF16:
-            decode_step_kernel<D, G::DVB, G::NTH, G::MINB, KAI_GDN_BF16><<<(unsigned)ctas, G::NTH, 0, st>>>(*a);
+            decode_step_kernel<D, G::DVB, G::NTH, G::MINB, KAI_GDN_BF16, G2><<<(unsigned)ctas, G::NTH, 0, st>>>(p);
             break;
     }
-    return check_launch("delta_rule_decode");
+    return check_launch(G2 ? "gdn2_delta_rule_decode" : "delta_rule_decode");
+}
+
+// Shape, dtype and alignment checks shared by both forms.
+int check_decode_shape(const char *name, size_t heads_k, size_t heads_v, int in_dt, int state_dt, int out_dt,
+                       const void *state, size_t dk, size_t dv) {
+    if (heads_k == 0 || heads_v % heads_k)
+        return set_error(KAI_GDN_ERR_INVALID, "%s: heads_v %zu not a multiple of heads_k %zu", name, heads_v,
+                         heads_k);
+    if (!valid_dtype(in_dt) || !valid_dtype(state_dt) || !valid_dtype(out_dt))
+        return set_error(KAI_GDN_ERR_INVALID, "%s: bad dtype", name);
+    size_t es = dtype_size(state_dt);
+    if ((uintptr_t)state % (4 * es))
+        return set_error(KAI_GDN_ERR_INVALID, "%s: state must be %zu-byte aligned", name, 4 * es);
+    if (dk != dv) return set_error(KAI_GDN_ERR_UNSUPPORTED, "%s: dk %zu != dv %zu", name, dk, dv);
+    if (dk != 32 && dk != 64 && dk != 128)
+        return set_error(KAI_GDN_ERR_UNSUPPORTED, "%s: head dim %zu (supported: 32, 64, 128)", name, dk);
+    return KAI_GDN_OK;
+}
+
+template <bool G2>
+int dispatch_decode(const DecodeP &p, size_t units, size_t d, int state_dtype, cudaStream_t st) {
+    switch (d) {
+        case 32: return run_decode<32, G2>(p, units, state_dtype, st);
+        case 64: return run_decode<64, G2>(p, units, state_dtype, st);
+        default: return run_decode<128, G2>(p, units, state_dtype, st);
+    }
 }
 
 }  // namespace
@@ -185,22 +239,25 @@ int launch_decode(const kai_gdn_decode_args *a, cudaStream_t st) {
     if (a->batch == 0 || a->heads_v == 0) return KAI_GDN_OK;
     if (!a->state || !a->q || !a->k || !a->v || !a->g || !a->beta || !a->o)
         return set_error(KAI_GDN_ERR_INVALID, "decode: null pointer");
-    if (a->heads_k == 0 || a->heads_v % a->heads_k)
-        return set_error(KAI_GDN_ERR_INVALID, "decode: heads_v %zu not a multiple of heads_k %zu",
-                         a->heads_v, a->heads_k);
-    if (!valid_dtype(a->in_dtype) || !valid_dtype(a->state_dtype) || !valid_dtype(a->out_dtype))
-        return set_error(KAI_GDN_ERR_INVALID, "decode: bad dtype");
-    size_t es = dtype_size(a->state_dtype);
-    if ((uintptr_t)a->state % (4 * es))
-        return set_error(KAI_GDN_ERR_INVALID, "decode: state must be %zu-byte aligned", 4 * es);
-    if (a->dk != a->dv)
-        return set_error(KAI_GDN_ERR_UNSUPPORTED, "decode: dk %zu != dv %zu", a->dk, a->dv);
-    switch (a->dk) {
-        case 32: return run_decode<32>(a, st);
-        case 64: return run_decode<64>(a, st);
-        case 128: return run_decode<128>(a, st);
-    }
-    return set_error(KAI_GDN_ERR_UNSUPPORTED, "decode: head dim %zu (supported: 32, 64, 128)", a->dk);
+    int rc = check_decode_shape("decode", a->heads_k, a->heads_v, a->in_dtype, a->state_dtype, a->out_dtype,
+                                a->state, a->dk, a->dv);
+    if (rc) return rc;
+    const DecodeP p{a->state, a->q, a->k, a->v, a->g, a->beta, nullptr, a->o, (long long)a->heads_k,
+                    (long long)a->heads_v, a->scale, a->in_dtype, a->out_dtype};
+    return dispatch_decode<false>(p, a->batch * a->heads_v, a->dk, a->state_dtype, st);
+}
+
+int launch_gdn2_decode(const kai_gdn2_decode_args *a, cudaStream_t st) {
+    if (!a) return set_error(KAI_GDN_ERR_INVALID, "gdn2_decode: null args");
+    if (a->batch == 0 || a->heads_v == 0) return KAI_GDN_OK;
+    if (!a->state || !a->q || !a->k || !a->v || !a->g || !a->b_gate || !a->w_gate || !a->o)
+        return set_error(KAI_GDN_ERR_INVALID, "gdn2_decode: null pointer");
+    int rc = check_decode_shape("gdn2_decode", a->heads_k, a->heads_v, a->in_dtype, a->state_dtype, a->out_dtype,
+                                a->state, a->dk, a->dv);
+    if (rc) return rc;
+    const DecodeP p{a->state, a->q, a->k, a->v, a->g, a->b_gate, a->w_gate, a->o, (long long)a->heads_k,
+                    (long long)a->heads_v, a->scale, a->in_dtype, a->out_dtype};
+    return dispatch_decode<true>(p, a->batch * a->heads_v, a->dk, a->state_dtype, st);
 }
 
 }  // namespace gdn

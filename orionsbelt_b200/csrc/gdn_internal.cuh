@@ -53,6 +53,7 @@ int launch_conv(const void *in, const float *w, void *out, void *hist, int io_dt
 int launch_matmul(const float *A, const float *B, float *C, size_t M, size_t K,
                   size_t N, cudaStream_t st);
 int launch_decode(const kai_gdn_decode_args *a, cudaStream_t st);
+int launch_gdn2_decode(const kai_gdn2_decode_args *a, cudaStream_t st);
 int launch_chunk(const kai_gdn_chunk_args *a, cudaStream_t st);
 // Warp-specialised tensor-core chunk scan (chunk_ws.cu): bf16/fp16 q, k, v,
 // dk = dv = 128, chunk 64; TMA-fed, tcgen05 MMAs, fp32 state in TMEM.

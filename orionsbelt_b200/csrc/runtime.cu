@@ -389,6 +389,10 @@ int kai_run_gdn_delta_rule_decode_sm100a(const kai_gdn_decode_args *args, void *
     return launch_decode(args, (cudaStream_t)stream);
 }
 
+int kai_run_gdn2_delta_rule_decode_sm100a(const kai_gdn2_decode_args *args, void *stream) {
+    return launch_gdn2_decode(args, (cudaStream_t)stream);
+}
+
 int kai_run_gdn_chunk_delta_rule_sm100a(const kai_gdn_chunk_args *args, void *stream) {
     return launch_chunk(args, (cudaStream_t)stream);
 }

@@ -38,6 +38,13 @@ def decode_bytes(B, Hk, Hv, dk, dv, e_state=4, e_in=2, e_out=2):
             + 2 * B * Hv * 4)
 
 
+def gdn2_decode_bytes(B, Hk, Hv, dk, dv, e_state=4, e_in=2, e_out=2):
+    """One GDN-2 decode step of one layer: as decode_bytes, with the gates per
+    channel (g and b per key channel, w per value channel, fp32)."""
+    return (2 * B * Hv * dk * dv * e_state + B * (2 * Hk * dk + Hv * dv) * e_in + B * Hv * dv * e_out
+            + B * Hv * (2 * dk + dv) * 4)
+
+
 def chunk_flops(B, T, Hv, d, C=64):
     """Chunkwise scan FLOPs: per (chunk, value head) 6*C*d^2 (W S, Q S, K^T V')
     + 10*C^2*d (K K^T, Q K^T, W, U, P V') + (2/3) C^3 (triangular solve)."""

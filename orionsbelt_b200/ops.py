@@ -10,7 +10,7 @@ Two layers, both calling the C ABI (include/kai_gdn_cuda.h) through ctypes:
 * The device layer takes CUDA tensors (torch is used only to own device memory
   and streams) and launches on the current torch stream: ``cumdecay``,
   ``cumsum``, ``gated_scan``, ``gdn2_gated_scan``, ``causal_dwconv1d``,
-  ``matmul``, ``delta_rule_decode`` and ``chunk_delta_rule``.
+  ``matmul``, ``delta_rule_decode``, ``gdn2_delta_rule_decode`` and ``chunk_delta_rule``.
 
 There is no CPU fallback anywhere: a missing library raises at import of the
 first call, and every failed call raises GdnError with the library's message.
@@ -177,6 +177,27 @@ def delta_rule_decode(state, q, k, v, g, beta, o, scale: float = 1.0, stream=Non
     """One token of the matrix-state gated delta rule for every (batch, value head)."""
     args = decode_args(state, q, k, v, g, beta, o, scale)
     check(lib().kai_run_gdn_delta_rule_decode_sm100a(args, _stream(stream)))
+
+
+def gdn2_decode_args(state, q, k, v, g, b_gate, w_gate, o, scale: float) -> _lib.Gdn2DecodeArgs:
+    """Pack struct kai_gdn2_decode_args from tensors: state [B][Hv][dk][dv],
+    q,k [B][Hk][dk], v [B][Hv][dv], g,b_gate [B][Hv][dk], w_gate [B][Hv][dv], o [B][Hv][dv]."""
+    torch = _torch()
+    B, Hv, dk, dv = state.shape
+    Hk = q.shape[1]
+    if q.dtype != k.dtype or v.dtype != q.dtype:
+        raise TypeError("q, k, v must share a dtype")
+    f = torch.float32
+    return _lib.Gdn2DecodeArgs(_dev(state), _dev(q), _dev(k), _dev(v), _dev(g, dtype=f), _dev(b_gate, dtype=f),
+                               _dev(w_gate, dtype=f), _dev(o), B, Hk, Hv, dk, dv, float(scale), _dt(q), _dt(state),
+                               _dt(o))
+
+
+def gdn2_delta_rule_decode(state, q, k, v, g, b_gate, w_gate, o, scale: float = 1.0, stream=None) -> None:
+    """One token of the GDN-2 recurrence (per-channel decay, erase and write gates)
+    for every (batch, value head); bench/gdn2_reference.py:58-145."""
+    args = gdn2_decode_args(state, q, k, v, g, b_gate, w_gate, o, scale)
+    check(lib().kai_run_gdn2_delta_rule_decode_sm100a(args, _stream(stream)))
 
 
 def chunk_args(q, k, v, g, beta, state, o, scale: float, chunk: int = 64) -> _lib.ChunkArgs:

@@ -12,6 +12,10 @@ Fixtures
                       erase/write gates (= GDN-1 with beta, the reduction
                       bench/gdn2_reference.py:293-351 tests), exercising the
                       reference's GDN-2 code path as a second anchor.
+  gdn2_general.npz    bench/gdn2_reference.py::gdn2_recurrent with channel-wise
+                      decay, erase and write gates (sigmoid / -softplus of
+                      N(0,1), as its make_synthetic_input), grouped heads and a
+                      non-zero initial state, d = 32: the GDN-2 decode step.
   hf_chunk.npz        HF transformers torch_chunk_gated_delta_rule (the chunkwise
                       WY form the reference reaches through bench/hf_backend.py)
                       on a multi-chunk case with a ragged last chunk.
@@ -45,12 +49,35 @@ def lcg_fill(n: int, lo: float, hi: float, state: list) -> np.ndarray:
     return out
 
 
-def main(ref_root: Path) -> None:
+def main(ref_root: Path, only=None) -> None:
     from orionsbelt_b200 import synth
 
     spec = importlib.util.spec_from_file_location("gdn2_reference", ref_root / "bench" / "gdn2_reference.py")
     G = importlib.util.module_from_spec(spec)
     spec.loader.exec_module(G)
+
+    # ---- gdn2_recurrent, general gates: T=5, Hk=2, Hv=4, K=V=32, S0 ~ N(0, 0.1)
+    if only is None or "gdn2_general" in only:
+        r = np.random.default_rng(14)
+        T, Hk, Hv, K = 5, 2, 4, 32
+        q = r.standard_normal((T, Hk, K)).astype(np.float32)
+        k = r.standard_normal((T, Hk, K)).astype(np.float32)
+        q /= np.linalg.norm(q, axis=-1, keepdims=True)
+        k /= np.linalg.norm(k, axis=-1, keepdims=True)
+        v = r.standard_normal((T, Hv, K)).astype(np.float32)
+        g = (-np.log1p(np.exp(r.standard_normal((T, Hv, K))))).astype(np.float32)
+        bg = (1.0 / (1.0 + np.exp(-r.standard_normal((T, Hv, K))))).astype(np.float32)
+        wg = (1.0 / (1.0 + np.exp(-r.standard_normal((T, Hv, K))))).astype(np.float32)
+        S0 = (0.1 * r.standard_normal((Hv, K, K))).astype(np.float32)
+        scale = np.float32(1.0 / np.sqrt(K))
+        og, Sg = G.gdn2_recurrent(q.astype(np.float64), k.astype(np.float64), v.astype(np.float64),
+                                  g.astype(np.float64), bg.astype(np.float64), wg.astype(np.float64),
+                                  scale=float(scale), initial_state=S0, use_qk_l2norm=False)
+        np.savez_compressed(HERE / "gdn2_general.npz", q=q, k=k, v=v, g=g, b_gate=bg, w_gate=wg, S0=S0,
+                            scale=scale, o=og, S=Sg)
+        if only is not None:
+            print("wrote gdn2_general.npz")
+            return
 
     # ---- gdn1_recurrent: B=1, T=70, Hk=2, Hv=4, d=32, S0 ~ N(0, 0.1)
     d = synth.host_gdn(1, 70, 2, 4, 32, 32, g_scale=0.5, seed=11, state_std=0.1)
@@ -114,4 +141,5 @@ def main(ref_root: Path) -> None:
 
 
 if __name__ == "__main__":
-    main(Path(sys.argv[1]) if len(sys.argv) > 1 else Path("/root/reference"))
+    # python make_golden.py [reference root] [fixture names to (re)write only]
+    main(Path(sys.argv[1]) if len(sys.argv) > 1 else Path("/root/reference"), set(sys.argv[2:]) or None)

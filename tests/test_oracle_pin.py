@@ -143,3 +143,52 @@ def test_integer_inputs_exact(orc):
     assert np.array_equal(o.astype(np.int64), want)
     g = r.integers(-3, 1, (100, 9)).astype(np.float32)
     assert np.array_equal(orc.cumsum(g).astype(np.int64), np.cumsum(g.astype(np.int64), axis=0))
+
+
+def test_gdn2_general_golden(orc, golden):
+    """bench/gdn2_reference.py::gdn2_recurrent (float64) with per-channel decay,
+    erase and write gates on grouped heads, token by token through the oracle."""
+    d = golden("gdn2_general.npz")
+    sc = float(d["scale"])
+    S = d["S0"][None]
+    for t in range(d["q"].shape[0]):
+        S, o = orc.gdn2_decode(S, d["q"][t][None], d["k"][t][None], d["v"][t][None], d["g"][t][None],
+                               d["b_gate"][t][None], d["w_gate"][t][None], scale=sc)
+        o_t = o[0]
+    assert rel_l2(o_t, d["o"][-1]) < 1e-5
+    assert rel_l2(S[0], d["S"]) < 1e-5
+    T = d["q"].shape[0]
+    S2, o2 = orc.gdn2_seq(d["S0"][None], d["q"][None], d["k"][None], d["v"][None], d["g"][None],
+                          d["b_gate"][None], d["w_gate"][None], scale=sc)
+    assert rel_l2(o2[0], d["o"]) < 1e-5 and rel_l2(S2[0], d["S"]) < 1e-5
+    assert o2.shape == (1, T, 4, 32)
+
+
+def test_gdn2_uniform_gates_equal_gdn1(orc, golden):
+    """GDN-2 with g_j = g, b_j = w_i = beta is GDN-1 (the reduction the reference
+    tests at bench/gdn2_reference.py:293-349), on its uniform-gate vectors."""
+    d = golden("gdn2_uniform.npz")
+    B, T, Hv = d["g"].shape
+    dk, dv = d["k"].shape[-1], d["v"].shape[-1]
+    g = np.repeat(d["g"][..., None], dk, -1)
+    bg = np.repeat(d["beta"][..., None], dk, -1)
+    wg = np.repeat(d["beta"][..., None], dv, -1)
+    S, o = orc.gdn2_seq(d["S0"], d["q"], d["k"], d["v"], g, bg, wg, scale=1.0)
+    assert rel_l2(o[0], d["o"]) < 1e-5 and rel_l2(S[0], d["S"]) < 1e-5
+
+
+def test_gdn2_known_answer(orc):
+    """dk = dv = 2 by hand.  From S0 = 0 only the write gate acts: S = k (w v)^T.
+    With w = 0 only decay and erase act: S = D S0 - k (S0^T D (b k))^T."""
+    k = np.array([[[0.8, 0.6]]], np.float32)
+    q = np.array([[[0.6, 0.8]]], np.float32)
+    v = np.array([[[1.0, 2.0]]], np.float32)
+    S, o = orc.gdn2_decode(np.zeros((1, 1, 2, 2), np.float32), q, k, v, np.zeros((1, 1, 2), np.float32),
+                           np.ones((1, 1, 2), np.float32), np.array([[[0.5, 1.0]]], np.float32))
+    assert np.allclose(S[0, 0], [[0.4, 1.6], [0.3, 1.2]], atol=1e-7)
+    assert np.allclose(o[0, 0], [0.48, 1.92], atol=1e-6)
+    S0 = np.array([[[[1.0, 2.0], [3.0, 4.0]]]], np.float32)
+    S, o = orc.gdn2_decode(S0, q, k, v, np.log(np.array([[[0.5, 1.0]]], np.float32)),
+                           np.array([[[1.0, 0.0]]], np.float32), np.zeros((1, 1, 2), np.float32))
+    assert np.allclose(S[0, 0], [[0.18, 0.36], [2.76, 3.52]], atol=1e-6)
+    assert np.allclose(o[0, 0], [2.316, 3.032], atol=1e-5)
