@@ -546,6 +546,20 @@ def run_rows(args, peaks) -> dict:
            "bf16 q/k/v/o, fp32 per-channel gates)", metrics.gdn2_decode_bytes(64, 16, 32, 128, 128), ms,
            "decode_step_kernel<128, f32, GDN-2>")
     del d, g2, bg2, wg2, o2, q2, k2, v2, S2
+    # f2: int8-weight GEMV / small GEMM at the config-4 FFN shapes (hidden
+    # 2560, FFN 9216): up / gate projection, down projection, batch 16
+    for name, (M, K, N) in [("f2_int8_gemv_ffn_up", (1, 2560, 9216)), ("f2_int8_gemv_ffn_down", (1, 9216, 2560)),
+                            ("f2_int8_gemm_b16_ffn_up", (16, 2560, 9216))]:
+        W = synth.device_normal((K, N), 16, 1, std=0.05)
+        q8 = torch.empty((K, N), dtype=torch.int8, device="cuda")
+        s8 = torch.empty(N, device="cuda")
+        ops.quantize_int8(W, q8, s8)
+        A8 = synth.device_normal((M, K), 16, 2)
+        C8 = torch.empty((M, N), device="cuda")
+        ms = _time(lambda A8=A8, q8=q8, s8=s8, C8=C8: ops.matmul_int8(A8, q8, s8, C8), reps, flush)
+        bw_row(name, f"int8 weights x fp32 activations, M={M} K={K} N={N} (per-column scales)",
+               metrics.int8_matmul_bytes(M, K, N), ms, "matmul_int8_stream_kernel (cluster split-K)")
+        del W, q8, s8, A8, C8
     # a6: chunk scan at config 0 (fp32 throughout) and config 3 (fp16 in, fp16 state, strong decay)
     for name, c, dt, sdt, kern in [
             ("a6_chunk_cfg0", dict(B=1, T=2048, g=0.1), torch.float32, torch.float32,

@@ -212,6 +212,25 @@ typedef struct kai_gdn2_decode_args {
 } kai_gdn2_decode_args;
 KAI_GDN_API int kai_run_gdn2_delta_rule_decode_sm100a(const kai_gdn2_decode_args *args, void *stream);
 
+/* int8 weights with one fp32 scale per output column (symmetric), the
+ * weight format of the reference's INT8_WEIGHTS decode path
+ * (src/orionsbelt/engines/cpu/kernels/gdn_e2e_decode.c).
+ *
+ * Quantize B [K][N] fp32 (row-major) into q [K][N] int8 and s [N]:
+ *   s[n] = max_k |B[k][n]| / 127 (1 for an all-zero column),
+ *   q[k][n] = clamp(lroundf(B[k][n] * (1 / s[n])), -128, 127),
+ * bit-identical to quantize_weight (gdn_e2e_decode.c:175-199). */
+KAI_GDN_API int kai_run_gdn_quantize_int8_sm100a(const float *B, int8_t *q, float *s, size_t K, size_t N,
+                                                 void *stream);
+/* C [M][N] = (A [M][K] . q) * s[n], fp32: matmul_int8 (gdn_e2e_decode.c:681),
+ * i.e. gemv_int8_neon (:296) for M = 1 and gemm_int8_neon (:608) for M > 1.
+ * The products are summed in a different order than the reference's (split
+ * over K, fused multiply-add); the reference's own accuracy rule
+ * (test_gdn_e2e_int8.c: |C - A.B| <= s * sum|a| against the fp32 product)
+ * holds.  Deterministic. */
+KAI_GDN_API int kai_run_gdn_matmul_int8_sm100a(const float *A, const int8_t *q, const float *s, float *C, size_t M,
+                                               size_t K, size_t N, void *stream);
+
 /* Chunkwise (WY / UT-transform) gated delta-rule scan over a whole sequence,
  * for every (batch, value head), chunk length `chunk` (64).  Equal, up to
  * rounding, to applying the decode step above for t = 0 .. seq-1 with

@@ -29,6 +29,7 @@ import numpy as np
 HERE = Path(__file__).resolve().parent
 ORACLE_SO = HERE / "liboracle.so"
 REF_SO = HERE / "_ref" / "libgdnref.so"
+INT8_REF_SO = HERE / "_ref" / "libint8ref.so"
 
 _f = C.POINTER(C.c_float)
 _u16 = C.POINTER(C.c_uint16)
@@ -50,6 +51,8 @@ def _load(path: Path):
 
 def _p(a: np.ndarray, dtype) -> C.POINTER:
     assert a.flags["C_CONTIGUOUS"] and a.dtype == dtype, (a.dtype, dtype)
+    if dtype == np.int8:
+        return a.ctypes.data_as(C.POINTER(C.c_int8))
     return a.ctypes.data_as(_f if dtype == np.float32 else _u16)
 
 
@@ -245,6 +248,26 @@ class _Oracle(_Kernels):
                               C.c_float(scale), C.c_int(nthreads))
         return S, o
 
+    def quantize_int8(self, B):
+        """B [K][N] fp32 -> (q [K][N] int8, s [N] fp32): gdn_e2e_decode.c:175-199."""
+        B = _f32(B)
+        K, N = B.shape
+        q = np.empty((K, N), np.int8)
+        s = np.empty((N,), np.float32)
+        self.lib.orc_quantize_int8(_p(B, np.float32), _p(q, np.int8), _p(s, np.float32), _sz(K), _sz(N))
+        return q, s
+
+    def matmul_int8(self, A, q, s, nthreads=0):
+        """A [M][K] fp32, q [K][N] int8, s [N] -> C [M][N] (k-ordered sums, then * s)."""
+        A, s = _f32(A), _f32(s)
+        q = np.ascontiguousarray(q, dtype=np.int8)
+        M, K = A.shape
+        N = q.shape[1]
+        Cm = np.empty((M, N), np.float32)
+        self.lib.orc_matmul_int8(_p(A, np.float32), _p(q, np.int8), _p(s, np.float32), _p(Cm, np.float32),
+                                 _sz(M), _sz(K), _sz(N), C.c_int(nthreads))
+        return Cm
+
     def chunk_wy(self, S, q, k, v, g, beta, scale=1.0, chunk=64, nthreads=0):
         """Chunked WY form in float64 (same layouts as delta_rule_seq)."""
         S = _f32(S).copy()
@@ -287,6 +310,39 @@ u16_to_f32 = _u16_to_f32
 orc = _Oracle(_load(ORACLE_SO)) if ORACLE_SO.exists() else None
 _ref_lib = _load(REF_SO)
 ref = _Ref(_ref_lib) if _ref_lib is not None else None
+
+
+class _RefInt8:
+    """The reference's static int8 functions, exported by ref_int8_shim.c."""
+
+    def __init__(self, lib):
+        self.lib = lib
+
+    def quantize_int8(self, B):
+        B = _f32(B)
+        K, N = B.shape
+        q = np.empty((K, N), np.int8)
+        s = np.empty((N,), np.float32)
+        self.lib.ref_quantize_int8(_p(B, np.float32), _p(q, np.int8), _p(s, np.float32), _sz(K), _sz(N))
+        return q, s
+
+    def matmul_int8(self, A, q, s):
+        A, s = _f32(A), _f32(s)
+        q = np.ascontiguousarray(q, dtype=np.int8)
+        M, K = A.shape
+        N = q.shape[1]
+        Cm = np.empty((M, N), np.float32)
+        if M == 1:
+            self.lib.ref_gemv_int8(_p(A, np.float32), _p(q, np.int8), _p(s, np.float32), _p(Cm, np.float32),
+                                   _sz(K), _sz(N))
+        else:
+            self.lib.ref_gemm_int8(_p(A, np.float32), _p(q, np.int8), _p(s, np.float32), _p(Cm, np.float32),
+                                   _sz(M), _sz(K), _sz(N))
+        return Cm
+
+
+_int8_lib = _load(INT8_REF_SO)
+ref_int8 = _RefInt8(_int8_lib) if _int8_lib is not None else None
 
 
 def require():

@@ -511,6 +511,47 @@ void orc_gdn2_gated_scan_f32(const float *g, const float *bg, const float *wg,
     }
 }
 
+/* ------------------------------------------------------------------------
+ * f2: int8 weights with one scale per output column.
+ * quantize_weight: src/orionsbelt/engines/cpu/kernels/gdn_e2e_decode.c:175-199.
+ * ---------------------------------------------------------------------- */
+void orc_quantize_int8(const float *B, int8_t *q, float *s, size_t K, size_t N) {
+    for (size_t n = 0; n < N; ++n) {
+        float mx = 0.0f;
+        for (size_t k = 0; k < K; ++k) {
+            float a = fabsf(B[k * N + n]);
+            if (a > mx) mx = a;
+        }
+        s[n] = mx > 0.0f ? mx / 127.0f : 1.0f;
+        float inv = 1.0f / s[n];
+        for (size_t k = 0; k < K; ++k) {
+            long v = lroundf(B[k * N + n] * inv);
+            q[k * N + n] = (int8_t)(v > 127 ? 127 : (v < -128 ? -128 : v));
+        }
+    }
+}
+
+/* C = (A q) diag(s), each element summed k by k from 0 with one rounding per
+ * product and per sum, then scaled: the portable loops of gemv_int8_neon
+ * (gdn_e2e_decode.c:296-358, M = 1) and gemm_int8_neon (:608-678, M > 1). */
+void orc_matmul_int8(const float *A, const int8_t *q, const float *s, float *C, size_t M, size_t K,
+                     size_t N, int nthreads) {
+#ifdef _OPENMP
+    int nt = nthreads > 0 ? nthreads : omp_get_max_threads();
+#pragma omp parallel for schedule(static) num_threads(nt)
+#endif
+    for (size_t m = 0; m < M; ++m) {
+        float *c = C + m * N;
+        for (size_t n = 0; n < N; ++n) c[n] = 0.0f;
+        for (size_t k = 0; k < K; ++k) {
+            float a = A[m * K + k];
+            const int8_t *row = q + k * N;
+            for (size_t n = 0; n < N; ++n) c[n] += a * (float)row[n];
+        }
+        for (size_t n = 0; n < N; ++n) c[n] *= s[n];
+    }
+}
+
 int orc_num_threads(void) {
 #ifdef _OPENMP
     return omp_get_max_threads();

@@ -67,6 +67,8 @@ SIGNATURES = {
     "kai_run_gdn_matmul_f32_sm100a": (_i, [_vp, _vp, _vp, _sz, _sz, _sz, _vp]),
     "kai_run_gdn_delta_rule_decode_sm100a": (_i, [C.POINTER(DecodeArgs), _vp]),
     "kai_run_gdn2_delta_rule_decode_sm100a": (_i, [C.POINTER(Gdn2DecodeArgs), _vp]),
+    "kai_run_gdn_quantize_int8_sm100a": (_i, [_vp, _vp, _vp, _sz, _sz, _vp]),
+    "kai_run_gdn_matmul_int8_sm100a": (_i, [_vp, _vp, _vp, _vp, _sz, _sz, _sz, _vp]),
     "kai_run_gdn_chunk_delta_rule_sm100a": (_i, [C.POINTER(ChunkArgs), _vp]),
     # control
     "kai_gdn_cuda_set_device": (_i, [_i]),

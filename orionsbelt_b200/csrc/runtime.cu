@@ -393,6 +393,15 @@ int kai_run_gdn2_delta_rule_decode_sm100a(const kai_gdn2_decode_args *args, void
     return launch_gdn2_decode(args, (cudaStream_t)stream);
 }
 
+int kai_run_gdn_quantize_int8_sm100a(const float *B, int8_t *q, float *s, size_t K, size_t N, void *stream) {
+    return launch_quantize_int8(B, q, s, K, N, (cudaStream_t)stream);
+}
+
+int kai_run_gdn_matmul_int8_sm100a(const float *A, const int8_t *q, const float *s, float *C, size_t M, size_t K,
+                                   size_t N, void *stream) {
+    return launch_matmul_int8(A, q, s, C, M, K, N, (cudaStream_t)stream);
+}
+
 int kai_run_gdn_chunk_delta_rule_sm100a(const kai_gdn_chunk_args *args, void *stream) {
     return launch_chunk(args, (cudaStream_t)stream);
 }

@@ -45,6 +45,11 @@ def gdn2_decode_bytes(B, Hk, Hv, dk, dv, e_state=4, e_in=2, e_out=2):
             + B * Hv * (2 * dk + dv) * 4)
 
 
+def int8_matmul_bytes(M, K, N):
+    """int8 weights [K][N] and their fp32 column scales, fp32 A [M][K] and C [M][N]."""
+    return K * N + 4 * N + 4 * M * K + 4 * M * N
+
+
 def chunk_flops(B, T, Hv, d, C=64):
     """Chunkwise scan FLOPs: per (chunk, value head) 6*C*d^2 (W S, Q S, K^T V')
     + 10*C^2*d (K K^T, Q K^T, W, U, P V') + (2/3) C^3 (triangular solve)."""

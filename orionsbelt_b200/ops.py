@@ -10,7 +10,8 @@ Two layers, both calling the C ABI (include/kai_gdn_cuda.h) through ctypes:
 * The device layer takes CUDA tensors (torch is used only to own device memory
   and streams) and launches on the current torch stream: ``cumdecay``,
   ``cumsum``, ``gated_scan``, ``gdn2_gated_scan``, ``causal_dwconv1d``,
-  ``matmul``, ``delta_rule_decode``, ``gdn2_delta_rule_decode`` and ``chunk_delta_rule``.
+  ``matmul``, ``quantize_int8``, ``matmul_int8``, ``delta_rule_decode``,
+  ``gdn2_delta_rule_decode`` and ``chunk_delta_rule``.
 
 There is no CPU fallback anywhere: a missing library raises at import of the
 first call, and every failed call raises GdnError with the library's message.
@@ -158,6 +159,25 @@ def matmul(A, B, Cm, stream=None) -> None:
     N = B.shape[1]
     check(lib().kai_run_gdn_matmul_f32_sm100a(_dev(A, dtype=f), _dev(B, dtype=f), _dev(Cm, dtype=f), M, K, N,
                                               _stream(stream)))
+
+
+def quantize_int8(B, q, s, stream=None) -> None:
+    """B [K][N] fp32 -> q [K][N] int8, s [N] fp32 (per-column symmetric scale),
+    bit-identical to quantize_weight (gdn_e2e_decode.c:175-199)."""
+    torch = _torch()
+    K, N = B.shape
+    check(lib().kai_run_gdn_quantize_int8_sm100a(_dev(B, dtype=torch.float32), _dev(q, dtype=torch.int8),
+                                                 _dev(s, dtype=torch.float32), K, N, _stream(stream)))
+
+
+def matmul_int8(A, q, s, Cm, stream=None) -> None:
+    """Cm [M][N] = (A [M][K] . q [K][N]) * s[n]: matmul_int8 (gdn_e2e_decode.c:681)."""
+    torch = _torch()
+    f = torch.float32
+    M, K = A.shape
+    N = q.shape[1]
+    check(lib().kai_run_gdn_matmul_int8_sm100a(_dev(A, dtype=f), _dev(q, dtype=torch.int8), _dev(s, dtype=f),
+                                               _dev(Cm, dtype=f), M, K, N, _stream(stream)))
 
 
 def decode_args(state, q, k, v, g, beta, o, scale: float) -> _lib.DecodeArgs:

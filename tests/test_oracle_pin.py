@@ -192,3 +192,43 @@ def test_gdn2_known_answer(orc):
                            np.array([[[1.0, 0.0]]], np.float32), np.zeros((1, 1, 2), np.float32))
     assert np.allclose(S[0, 0], [[0.18, 0.36], [2.76, 3.52]], atol=1e-6)
     assert np.allclose(o[0, 0], [2.316, 3.032], atol=1e-5)
+
+
+@pytest.mark.parametrize("K,N", [(128, 256), (64, 130), (2560, 1024), (7, 3)])
+def test_int8_bit_identical_to_reference(orc, K, N):
+    """quantize_weight, gemv_int8_neon and gemm_int8_neon (gdn_e2e_decode.c:175,
+    296, 608; built from the reference tree by oracle/ref_int8_shim.c) against
+    the oracle: same codes, scales and outputs, bit for bit.  Includes an
+    all-zero column (scale 1), ragged N and values on a rounding tie."""
+    import oracle
+    if oracle.ref_int8 is None:
+        pytest.skip("oracle/_ref/libint8ref.so not built (needs the reference tree)")
+    r = np.random.default_rng(K * 7 + N)
+    B = r.uniform(-1, 1, (K, N)).astype(np.float32)
+    B[:, 0] = 0.0
+    if N > 2:
+        B[0, 2], B[1, 2] = 1.0, 0.5 / 127.0  # q = 127 and a half-way code
+    q1, s1 = orc.quantize_int8(B)
+    q2, s2 = oracle.ref_int8.quantize_int8(B)
+    assert np.array_equal(q1, q2) and np.array_equal(s1, s2)
+    for M in (1, 3):
+        A = r.uniform(-1, 1, (M, K)).astype(np.float32)
+        assert np.array_equal(orc.matmul_int8(A, q1, s1), oracle.ref_int8.matmul_int8(A, q1, s1))
+
+
+def test_int8_reference_accuracy_rules(orc):
+    """The reference test's own rules on the oracle (test_gdn_e2e_int8.c:57-161):
+    scale = max|col| / 127, |C - A.B| <= s * 0.5 * sum|a| (x2 margin), mean
+    relative error < 2% where |A.B| > 1."""
+    r = np.random.default_rng(42)
+    K, N = 128, 256
+    W = r.uniform(-1, 1, (K, N)).astype(np.float32)
+    q, s = orc.quantize_int8(W)
+    assert np.allclose(s, np.abs(W).max(0) / np.float32(127), rtol=1e-6, atol=0)
+    a = r.uniform(-1, 1, (1, K)).astype(np.float32)
+    c = orc.matmul_int8(a, q, s)[0]
+    c32 = (a.astype(np.float64) @ W.astype(np.float64))[0]
+    bound = s.astype(np.float64) * 0.5 * np.abs(a).sum()
+    assert (np.abs(c - c32) <= 2 * bound).all()
+    big = np.abs(c32) > 1.0
+    assert np.mean(np.abs(c[big] - c32[big]) / np.abs(c32[big])) < 0.02
