@@ -24,19 +24,23 @@
 namespace gdn {
 namespace {
 
-__device__ __forceinline__ float load_any(const void *p, size_t i, int dt) {
-    switch (dt) {
-        case KAI_GDN_BF16: return __bfloat162float(static_cast<const __nv_bfloat16 *>(p)[i]);
-        case KAI_GDN_F16: return __half2float(static_cast<const __half *>(p)[i]);
-        default: return static_cast<const float *>(p)[i];
-    }
-}
 __device__ __forceinline__ void store_any(void *p, size_t i, int dt, float v) {
     switch (dt) {
         case KAI_GDN_BF16: static_cast<__nv_bfloat16 *>(p)[i] = __float2bfloat16_rn(v); break;
         case KAI_GDN_F16: static_cast<__half *>(p)[i] = __float2half_rn(v); break;
         default: static_cast<float *>(p)[i] = v;
     }
+}
+
+// q, k (one key channel) and v (one value column) of this thread, widened.
+template <typename T, int DK, int DVB, typename P>
+__device__ __forceinline__ void load_inputs(const P &p, int t, size_t kq, size_t vo, float &kj, float &qj, float &vi) {
+    const T *k = static_cast<const T *>(p.k), *q = static_cast<const T *>(p.q), *v = static_cast<const T *>(p.v);
+    if (t < DK) {
+        kj = static_cast<float>(k[kq + t]);
+        qj = static_cast<float>(q[kq + t]);
+    }
+    if (t < DVB) vi = static_cast<float>(v[vo + t]);
 }
 
 // 4 consecutive state elements.
@@ -108,19 +112,35 @@ __global__ void __launch_bounds__(NTH, MINB) decode_step_kernel(DecodeP p) {
 #pragma unroll
     for (int r = 0; r < RPT; ++r) s[r] = ld4<SDT>(p.state, sbase + (size_t)(rg + RPP * r) * DV + 4 * cq);
 
-    const size_t kq = (size_t)(b * Hk + hk) * DK;
-    for (int j = t; j < DK; j += NTH) {
-        ks[j] = load_any(p.k, kq + j, p.in_dtype);
-        qs[j] = __fmul_rn(load_any(p.q, kq + j, p.in_dtype), p.scale);
+    // The vector loads of the prologue are all issued before its first
+    // shared-memory store, so they are in flight together (a load through a
+    // generic pointer may not move past a shared-memory store): GDN-2 step
+    // 55.2 -> 53.0 us per config-1 layer.  GDN-1's two scalar gates are read
+    // after the stores, which measured 1.5% faster than reading them first.
+    static_assert(DK <= NTH && DVB <= NTH, "one prologue element per thread");
+    const size_t kq = (size_t)(b * Hk + hk) * DK, vo = (size_t)unit * DV + cb;
+    float kj = 0.f, qj = 0.f, vi = 0.f, gj = 0.f, bj = 0.f, wi = 0.f;
+    switch (p.in_dtype) {
+        case KAI_GDN_BF16: load_inputs<__nv_bfloat16, DK, DVB>(p, t, kq, vo, kj, qj, vi); break;
+        case KAI_GDN_F16: load_inputs<__half, DK, DVB>(p, t, kq, vo, kj, qj, vi); break;
+        default: load_inputs<float, DK, DVB>(p, t, kq, vo, kj, qj, vi);
+    }
+    if (G2) {
+        if (t < DK) {
+            gj = __ldg(p.g + (size_t)unit * DK + t);
+            bj = __ldg(p.beta + (size_t)unit * DK + t);
+        }
+        if (t < DVB) wi = __ldg(p.w + vo + t);
+    }
+    if (t < DK) {
+        ks[t] = kj;
+        qs[t] = __fmul_rn(qj, p.scale);
         if (G2) {
-            eg[j] = expf(p.g[(size_t)unit * DK + j]);
-            bk[j] = __fmul_rn(p.beta[(size_t)unit * DK + j], ks[j]);
+            eg[t] = expf(gj);
+            bk[t] = __fmul_rn(bj, kj);
         }
     }
-    for (int i = t; i < DVB; i += NTH) {
-        const float vi = load_any(p.v, (size_t)unit * DV + cb + i, p.in_dtype);
-        vs[i] = G2 ? __fmul_rn(p.w[(size_t)unit * DV + cb + i], vi) : vi;
-    }
+    if (t < DVB) vs[t] = G2 ? __fmul_rn(wi, vi) : vi;
     const float a = G2 ? 1.f : expf(p.g[unit]);
     const float beta = G2 ? 1.f : p.beta[unit];
     __syncthreads();
