@@ -560,6 +560,31 @@ def run_rows(args, peaks) -> dict:
         bw_row(name, f"int8 weights x fp32 activations, M={M} K={K} N={N} (per-column scales)",
                metrics.int8_matmul_bytes(M, K, N), ms, "matmul_int8_stream_kernel (cluster split-K)")
         del W, q8, s8, A8, C8
+    # f3: GQA attention decode at the config-4 geometry (16 query / 4 kv
+    # heads, head_dim 256) over a 32768-token cache: bf16 at batch 1 and 16,
+    # int8 (per-head scales) at batch 1
+    for name, B, cdt, ctx in [("f3_attn_decode_bf16_b1", 1, torch.bfloat16, 32768),
+                              ("f3_attn_decode_bf16_b16", 16, torch.bfloat16, 32768),
+                              ("f3_attn_decode_int8_b1", 1, torch.int8, 32768)]:
+        H, Hkv, D = 16, 4, 256
+        if cdt == torch.int8:
+            kc = torch.randint(-128, 128, (B, ctx, Hkv, D), dtype=torch.int8, device="cuda")
+            vc = torch.randint(-128, 128, (B, ctx, Hkv, D), dtype=torch.int8, device="cuda")
+            ksc = torch.full((B, Hkv), 0.01, device="cuda")
+            vsc = torch.full((B, Hkv), 0.01, device="cuda")
+        else:
+            kc = synth.device_normal((B, ctx, Hkv, D), 17, 1, dtype=cdt)
+            vc = synth.device_normal((B, ctx, Hkv, D), 17, 2, dtype=cdt)
+            ksc = vsc = None
+        qa = synth.device_normal((B, H, D), 17, 3)
+        kna, vna = synth.device_normal((B, Hkv, D), 17, 4), synth.device_normal((B, Hkv, D), 17, 5)
+        oa = torch.empty((B, H, D), device="cuda")
+        ms = _time(lambda: ops.attention_decode(qa, kna, vna, kc, vc, oa, ctx - 1, 0.0625, ksc, vsc), reps, flush)
+        bw_row(name, f"GQA decode, B={B}, 16 q / 4 kv heads x 256, {ctx}-token {cdt} KV cache",
+               metrics.attn_decode_bytes(B, ctx, H, Hkv, D, kc.element_size()), ms,
+               "attn_chunk_kernel + attn_combine_kernel")
+        del kc, vc, qa, kna, vna, oa
+    torch.cuda.empty_cache()
     # a6: chunk scan at config 0 (fp32 throughout) and config 3 (fp16 in, fp16 state, strong decay)
     for name, c, dt, sdt, kern in [
             ("a6_chunk_cfg0", dict(B=1, T=2048, g=0.1), torch.float32, torch.float32,

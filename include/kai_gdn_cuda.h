@@ -54,6 +54,7 @@ extern "C" {
 #define KAI_GDN_F32 0
 #define KAI_GDN_BF16 1 /* bfloat16, round-to-nearest-even on store */
 #define KAI_GDN_F16 2  /* IEEE binary16, round-to-nearest-even on store */
+#define KAI_GDN_I8 3   /* int8 with one fp32 scale per kv head (attention KV cache only) */
 
 /* ======================================================================
  * 1. Drop-in replacements (host or device pointers, synchronous)
@@ -230,6 +231,33 @@ KAI_GDN_API int kai_run_gdn_quantize_int8_sm100a(const float *B, int8_t *q, floa
  * holds.  Deterministic. */
 KAI_GDN_API int kai_run_gdn_matmul_int8_sm100a(const float *A, const int8_t *q, const float *s, float *C, size_t M,
                                                size_t K, size_t N, void *stream);
+
+/* Grouped-query attention decode with a growing KV cache, the full-attention
+ * layer of the reference's hybrid decode: full_attn_real_forward
+ * (src/orionsbelt/engines/cpu/kernels/gdn_e2e_decode.c:1532-1634, fp32 cache)
+ * and full_attn_real_forward_int8kv (:1652-1830, int8 cache with one scale
+ * per kv head); bf16 caches store round-to-nearest-even values.  For every
+ * sequence b: this token's k_new, v_new are written into the caches at `pos`
+ * (int8: clamp(lroundf(x * (1 / scale)), -128, 127)), then query head h
+ * (kv head h / (heads / kv_heads)) attends over positions 0..pos:
+ *   s_t = (q_h . k_t) * scale   (int8: * (k_scale * scale)),
+ *   o_h = sum_t softmax(s)_t v_t   (int8: * v_scale).
+ * All sequences are at the same position.  head_dim 128 or 256; 1, 2, 4 or 8
+ * query heads per kv head; caches and q 16-byte aligned. */
+typedef struct kai_gdn_attn_decode_args {
+    const float *q;       /* [batch][heads][head_dim]                        */
+    const float *k_new;   /* [batch][kv_heads][head_dim]                     */
+    const float *v_new;   /* [batch][kv_heads][head_dim]                     */
+    void *k_cache;        /* [batch][max_ctx][kv_heads][head_dim], cache_dtype */
+    void *v_cache;        /* same                                            */
+    const float *k_scale; /* KAI_GDN_I8: [batch][kv_heads]; otherwise unused */
+    const float *v_scale; /* KAI_GDN_I8: [batch][kv_heads]; otherwise unused */
+    float *o;             /* [batch][heads][head_dim]                        */
+    size_t batch, heads, kv_heads, head_dim, pos, max_ctx;
+    float scale;          /* 1 / sqrt(head_dim) in the reference             */
+    int cache_dtype;      /* KAI_GDN_F32, KAI_GDN_BF16 or KAI_GDN_I8         */
+} kai_gdn_attn_decode_args;
+KAI_GDN_API int kai_run_gdn_attention_decode_sm100a(const kai_gdn_attn_decode_args *args, void *stream);
 
 /* Chunkwise (WY / UT-transform) gated delta-rule scan over a whole sequence,
  * for every (batch, value head), chunk length `chunk` (64).  Equal, up to

@@ -30,6 +30,8 @@ HERE = Path(__file__).resolve().parent
 ORACLE_SO = HERE / "liboracle.so"
 REF_SO = HERE / "_ref" / "libgdnref.so"
 INT8_REF_SO = HERE / "_ref" / "libint8ref.so"
+ATTN_REF_SO = HERE / "_ref" / "libattnref.so"
+ATTN_I8_REF_SO = HERE / "_ref" / "libattnref_i8.so"
 
 _f = C.POINTER(C.c_float)
 _u16 = C.POINTER(C.c_uint16)
@@ -268,6 +270,27 @@ class _Oracle(_Kernels):
                                  _sz(M), _sz(K), _sz(N), C.c_int(nthreads))
         return Cm
 
+    def attn_decode(self, q, k_new, v_new, k_cache, v_cache, pos, scale, k_scale=None, v_scale=None,
+                    nthreads=0):
+        """GQA attention decode.  q [B][H][D], k_new/v_new [B][Hkv][D] fp32; caches
+        [B][max_ctx][Hkv][D] as float32, uint16 (bf16 bits) or int8 (with scales
+        [B][Hkv]), updated in place at pos.  Returns o [B][H][D]."""
+        q, k_new, v_new = map(_f32, (q, k_new, v_new))
+        B, H, D = q.shape
+        Hkv = k_new.shape[1]
+        max_ctx = k_cache.shape[1]
+        dt = {np.dtype(np.float32): 0, np.dtype(np.uint16): 1, np.dtype(np.int8): 3}[k_cache.dtype]
+        assert k_cache.flags["C_CONTIGUOUS"] and v_cache.flags["C_CONTIGUOUS"] and v_cache.dtype == k_cache.dtype
+        ks = _f32(k_scale) if k_scale is not None else np.ones((B, Hkv), np.float32)
+        vs = _f32(v_scale) if v_scale is not None else np.ones((B, Hkv), np.float32)
+        o = np.empty((B, H, D), np.float32)
+        self.lib.orc_attn_decode(_p(q, np.float32), _p(k_new, np.float32), _p(v_new, np.float32),
+                                 k_cache.ctypes.data_as(C.c_void_p), v_cache.ctypes.data_as(C.c_void_p),
+                                 _p(ks, np.float32), _p(vs, np.float32), _p(o, np.float32), _sz(B), _sz(H),
+                                 _sz(Hkv), _sz(D), _sz(pos), _sz(max_ctx), C.c_float(scale), C.c_int(dt),
+                                 C.c_int(nthreads))
+        return o
+
     def chunk_wy(self, S, q, k, v, g, beta, scale=1.0, chunk=64, nthreads=0):
         """Chunked WY form in float64 (same layouts as delta_rule_seq)."""
         S = _f32(S).copy()
@@ -340,6 +363,33 @@ class _RefInt8:
                                    _sz(M), _sz(K), _sz(N))
         return Cm
 
+
+class _RefAttn:
+    """The reference's GQA attention decode (one sequence), via ref_attn_shim.c."""
+
+    def __init__(self, lib, int8: bool):
+        self.lib, self.int8 = lib, int8
+        h, kvh, d = _sz(), _sz(), _sz()
+        lib.ref_attn_geometry(C.byref(h), C.byref(kvh), C.byref(d))
+        self.heads, self.kv_heads, self.head_dim = h.value, kvh.value, d.value
+
+    def attn_decode(self, q, k_new, v_new, k_cache, v_cache, pos, k_scale=None, v_scale=None):
+        """q [H*D], k_new/v_new [Hkv*D]; caches [max_ctx][Hkv*D] updated in place."""
+        q, k_new, v_new = map(_f32, (q, k_new, v_new))
+        o = np.empty(self.heads * self.head_dim, np.float32)
+        ks = _f32(k_scale) if k_scale is not None else np.ones(self.kv_heads, np.float32)
+        vs = _f32(v_scale) if v_scale is not None else np.ones(self.kv_heads, np.float32)
+        self.lib.ref_attn_decode(_p(q, np.float32), _p(k_new, np.float32), _p(v_new, np.float32),
+                                 k_cache.ctypes.data_as(C.c_void_p), v_cache.ctypes.data_as(C.c_void_p),
+                                 _p(ks, np.float32), _p(vs, np.float32), _sz(pos), _sz(k_cache.shape[0]),
+                                 _p(o, np.float32))
+        return o
+
+
+_attn_lib = _load(ATTN_REF_SO)
+ref_attn = _RefAttn(_attn_lib, False) if _attn_lib is not None else None
+_attn_i8_lib = _load(ATTN_I8_REF_SO)
+ref_attn_i8 = _RefAttn(_attn_i8_lib, True) if _attn_i8_lib is not None else None
 
 _int8_lib = _load(INT8_REF_SO)
 ref_int8 = _RefInt8(_int8_lib) if _int8_lib is not None else None

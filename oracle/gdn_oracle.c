@@ -552,6 +552,108 @@ void orc_matmul_int8(const float *A, const int8_t *q, const float *s, float *C, 
     }
 }
 
+/* ------------------------------------------------------------------------
+ * f3: GQA attention decode over a growing KV cache.
+ * full_attn_real_forward (src/orionsbelt/engines/cpu/kernels/gdn_e2e_decode.c
+ * :1532-1634, fp32 cache) and full_attn_real_forward_int8kv (:1652-1830, int8
+ * cache with one scale per kv head, its portable scoring branch :1752-1776);
+ * a bf16 cache (not in the reference) stores round-to-nearest-even bf16 and
+ * reads it widened.  Per batch element: the new token's k and v are written at
+ * position pos (int8: lroundf(x * (1 / scale)) clamped to [-128, 127],
+ * :1668-1684), then every query head h attends over t = 0..pos of kv head
+ * h / (H / Hkv).  Cache layout [B][max_ctx][Hkv][D].  dtype 0 f32, 1 bf16, 3 int8.
+ * ---------------------------------------------------------------------- */
+static float orc_bf16_round(float x) {
+    uint32_t u;
+    memcpy(&u, &x, 4);
+    u = (u + 0x7FFFu + ((u >> 16) & 1u)) & 0xFFFF0000u;
+    memcpy(&x, &u, 4);
+    return x;
+}
+
+void orc_attn_decode(const float *q, const float *k_new, const float *v_new, void *k_cache, void *v_cache,
+                     const float *k_scale, const float *v_scale, float *o, size_t B, size_t H, size_t Hkv,
+                     size_t D, size_t pos, size_t max_ctx, float scale, int dtype, int nthreads) {
+    const size_t kv_dim = Hkv * D, groups = H / Hkv, ctx = pos + 1;
+    /* append */
+    for (size_t b = 0; b < B; ++b)
+        for (size_t kh = 0; kh < Hkv; ++kh)
+            for (size_t d = 0; d < D; ++d) {
+                const size_t src = (b * Hkv + kh) * D + d;
+                const size_t dst = (b * max_ctx + pos) * kv_dim + kh * D + d;
+                if (dtype == 0) {
+                    ((float *)k_cache)[dst] = k_new[src];
+                    ((float *)v_cache)[dst] = v_new[src];
+                } else if (dtype == 1) {
+                    float kr = orc_bf16_round(k_new[src]), vr = orc_bf16_round(v_new[src]);
+                    uint32_t ku, vu;
+                    memcpy(&ku, &kr, 4);
+                    memcpy(&vu, &vr, 4);
+                    ((uint16_t *)k_cache)[dst] = (uint16_t)(ku >> 16);
+                    ((uint16_t *)v_cache)[dst] = (uint16_t)(vu >> 16);
+                } else {
+                    float inv_ks = 1.0f / k_scale[b * Hkv + kh], inv_vs = 1.0f / v_scale[b * Hkv + kh];
+                    long kq = lroundf(k_new[src] * inv_ks), vq = lroundf(v_new[src] * inv_vs);
+                    ((int8_t *)k_cache)[dst] = (int8_t)(kq > 127 ? 127 : (kq < -128 ? -128 : kq));
+                    ((int8_t *)v_cache)[dst] = (int8_t)(vq > 127 ? 127 : (vq < -128 ? -128 : vq));
+                }
+            }
+    long units = (long)(B * H);
+#ifdef _OPENMP
+    int nt = nthreads > 0 ? nthreads : omp_get_max_threads();
+#pragma omp parallel for schedule(static) num_threads(nt)
+#endif
+    for (long u = 0; u < units; ++u) {
+        const size_t b = (size_t)u / H, h = (size_t)u % H, kh = h / groups;
+        const float *qh = q + (b * H + h) * D;
+        float *scores = (float *)malloc(ctx * sizeof(float));
+        float max_s = -INFINITY;
+        for (size_t t = 0; t < ctx; ++t) {
+            const size_t base = (b * max_ctx + t) * kv_dim + kh * D;
+            float s = 0.0f;
+            for (size_t d = 0; d < D; ++d) {
+                float kd;
+                if (dtype == 0) kd = ((const float *)k_cache)[base + d];
+                else if (dtype == 1) {
+                    uint32_t w = (uint32_t)((const uint16_t *)k_cache)[base + d] << 16;
+                    memcpy(&kd, &w, 4);
+                } else kd = (float)((const int8_t *)k_cache)[base + d];
+                s += qh[d] * kd;
+            }
+            if (dtype == 3) s *= k_scale[b * Hkv + kh] * scale;
+            else s *= scale;
+            scores[t] = s;
+            if (s > max_s) max_s = s;
+        }
+        float sum_exp = 0.0f;
+        for (size_t t = 0; t < ctx; ++t) {
+            scores[t] = expf(scores[t] - max_s);
+            sum_exp += scores[t];
+        }
+        float *out = o + (b * H + h) * D;
+        for (size_t d = 0; d < D; ++d) out[d] = 0.0f;
+        for (size_t t = 0; t < ctx; ++t) {
+            const size_t base = (b * max_ctx + t) * kv_dim + kh * D;
+            if (dtype == 3) {
+                float ew = scores[t] / sum_exp * v_scale[b * Hkv + kh];
+                for (size_t d = 0; d < D; ++d) out[d] += ew * (float)((const int8_t *)v_cache)[base + d];
+            } else {
+                float weight = scores[t] / sum_exp;
+                for (size_t d = 0; d < D; ++d) {
+                    float vd;
+                    if (dtype == 0) vd = ((const float *)v_cache)[base + d];
+                    else {
+                        uint32_t w = (uint32_t)((const uint16_t *)v_cache)[base + d] << 16;
+                        memcpy(&vd, &w, 4);
+                    }
+                    out[d] += weight * vd;
+                }
+            }
+        }
+        free(scores);
+    }
+}
+
 int orc_num_threads(void) {
 #ifdef _OPENMP
     return omp_get_max_threads();

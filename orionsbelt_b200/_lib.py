@@ -12,7 +12,7 @@ from pathlib import Path
 LIB_PATH = Path(__file__).resolve().parent / "libkai_gdn_cuda.so"
 
 OK, ERR_INVALID, ERR_CUDA, ERR_UNSUPPORTED, ERR_NOMEM, ERR_TIMEOUT = 0, 1, 2, 3, 4, 5
-F32, BF16, F16 = 0, 1, 2
+F32, BF16, F16, I8 = 0, 1, 2, 3
 
 _sz = C.c_size_t
 _vp = C.c_void_p
@@ -32,6 +32,13 @@ class Gdn2DecodeArgs(C.Structure):
     _fields_ = [("state", _vp), ("q", _vp), ("k", _vp), ("v", _vp), ("g", _vp), ("b_gate", _vp), ("w_gate", _vp),
                 ("o", _vp), ("batch", _sz), ("heads_k", _sz), ("heads_v", _sz), ("dk", _sz), ("dv", _sz),
                 ("scale", _f), ("in_dtype", _i), ("state_dtype", _i), ("out_dtype", _i)]
+
+
+class AttnDecodeArgs(C.Structure):
+    """struct kai_gdn_attn_decode_args."""
+    _fields_ = [("q", _vp), ("k_new", _vp), ("v_new", _vp), ("k_cache", _vp), ("v_cache", _vp), ("k_scale", _vp),
+                ("v_scale", _vp), ("o", _vp), ("batch", _sz), ("heads", _sz), ("kv_heads", _sz), ("head_dim", _sz),
+                ("pos", _sz), ("max_ctx", _sz), ("scale", _f), ("cache_dtype", _i)]
 
 
 class ChunkArgs(C.Structure):
@@ -68,6 +75,7 @@ SIGNATURES = {
     "kai_run_gdn_delta_rule_decode_sm100a": (_i, [C.POINTER(DecodeArgs), _vp]),
     "kai_run_gdn2_delta_rule_decode_sm100a": (_i, [C.POINTER(Gdn2DecodeArgs), _vp]),
     "kai_run_gdn_quantize_int8_sm100a": (_i, [_vp, _vp, _vp, _sz, _sz, _vp]),
+    "kai_run_gdn_attention_decode_sm100a": (_i, [C.POINTER(AttnDecodeArgs), _vp]),
     "kai_run_gdn_matmul_int8_sm100a": (_i, [_vp, _vp, _vp, _vp, _sz, _sz, _sz, _vp]),
     "kai_run_gdn_chunk_delta_rule_sm100a": (_i, [C.POINTER(ChunkArgs), _vp]),
     # control

@@ -54,6 +54,7 @@ int launch_matmul(const float *A, const float *B, float *C, size_t M, size_t K,
                   size_t N, cudaStream_t st);
 int launch_decode(const kai_gdn_decode_args *a, cudaStream_t st);
 int launch_gdn2_decode(const kai_gdn2_decode_args *a, cudaStream_t st);
+int launch_attn_decode(const kai_gdn_attn_decode_args *a, cudaStream_t st);
 int launch_quantize_int8(const float *B, int8_t *q, float *s, size_t K, size_t N, cudaStream_t st);
 int launch_matmul_int8(const float *A, const int8_t *q, const float *s, float *C, size_t M, size_t K, size_t N,
                        cudaStream_t st);

@@ -393,6 +393,10 @@ int kai_run_gdn2_delta_rule_decode_sm100a(const kai_gdn2_decode_args *args, void
     return launch_gdn2_decode(args, (cudaStream_t)stream);
 }
 
+int kai_run_gdn_attention_decode_sm100a(const kai_gdn_attn_decode_args *args, void *stream) {
+    return launch_attn_decode(args, (cudaStream_t)stream);
+}
+
 int kai_run_gdn_quantize_int8_sm100a(const float *B, int8_t *q, float *s, size_t K, size_t N, void *stream) {
     return launch_quantize_int8(B, q, s, K, N, (cudaStream_t)stream);
 }

@@ -50,6 +50,12 @@ def int8_matmul_bytes(M, K, N):
     return K * N + 4 * N + 4 * M * K + 4 * M * N
 
 
+def attn_decode_bytes(B, ctx, H, Hkv, D, e_cache):
+    """One decode step of one attention layer: the K and V caches read once
+    (ctx tokens), q and o (fp32), the appended token (read fp32, written)."""
+    return 2 * B * ctx * Hkv * D * e_cache + 2 * B * H * D * 4 + 2 * B * Hkv * D * (4 + e_cache)
+
+
 def chunk_flops(B, T, Hv, d, C=64):
     """Chunkwise scan FLOPs: per (chunk, value head) 6*C*d^2 (W S, Q S, K^T V')
     + 10*C^2*d (K K^T, Q K^T, W, U, P V') + (2/3) C^3 (triangular solve)."""

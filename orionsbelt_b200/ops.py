@@ -10,7 +10,7 @@ Two layers, both calling the C ABI (include/kai_gdn_cuda.h) through ctypes:
 * The device layer takes CUDA tensors (torch is used only to own device memory
   and streams) and launches on the current torch stream: ``cumdecay``,
   ``cumsum``, ``gated_scan``, ``gdn2_gated_scan``, ``causal_dwconv1d``,
-  ``matmul``, ``quantize_int8``, ``matmul_int8``, ``delta_rule_decode``,
+  ``matmul``, ``quantize_int8``, ``matmul_int8``, ``attention_decode``, ``delta_rule_decode``,
   ``gdn2_delta_rule_decode`` and ``chunk_delta_rule``.
 
 There is no CPU fallback anywhere: a missing library raises at import of the
@@ -178,6 +178,31 @@ def matmul_int8(A, q, s, Cm, stream=None) -> None:
     N = q.shape[1]
     check(lib().kai_run_gdn_matmul_int8_sm100a(_dev(A, dtype=f), _dev(q, dtype=torch.int8), _dev(s, dtype=f),
                                                _dev(Cm, dtype=f), M, K, N, _stream(stream)))
+
+
+def attn_decode_args(q, k_new, v_new, k_cache, v_cache, o, pos: int, scale: float, k_scale=None,
+                     v_scale=None) -> _lib.AttnDecodeArgs:
+    """Pack struct kai_gdn_attn_decode_args: q [B][H][D], k_new/v_new [B][Hkv][D] fp32,
+    caches [B][max_ctx][Hkv][D] (fp32, bf16 or int8 with scales [B][Hkv]), o [B][H][D]."""
+    torch = _torch()
+    f = torch.float32
+    B, H, D = q.shape
+    Hkv, max_ctx = k_new.shape[1], k_cache.shape[1]
+    if k_cache.dtype != v_cache.dtype:
+        raise TypeError("k_cache and v_cache must share a dtype")
+    dt = {torch.float32: F32, torch.bfloat16: BF16, torch.int8: _lib.I8}[k_cache.dtype]
+    ks = _dev(k_scale, dtype=f) if dt == _lib.I8 else None
+    vs = _dev(v_scale, dtype=f) if dt == _lib.I8 else None
+    return _lib.AttnDecodeArgs(_dev(q, dtype=f), _dev(k_new, dtype=f), _dev(v_new, dtype=f), _dev(k_cache),
+                               _dev(v_cache), ks, vs, _dev(o, dtype=f), B, H, Hkv, D, int(pos), max_ctx,
+                               float(scale), dt)
+
+
+def attention_decode(q, k_new, v_new, k_cache, v_cache, o, pos: int, scale: float, k_scale=None, v_scale=None,
+                     stream=None) -> None:
+    """GQA attention decode with KV-cache append (gdn_e2e_decode.c:1532-1634, int8 cache :1652-1830)."""
+    args = attn_decode_args(q, k_new, v_new, k_cache, v_cache, o, pos, scale, k_scale, v_scale)
+    check(lib().kai_run_gdn_attention_decode_sm100a(args, _stream(stream)))
 
 
 def decode_args(state, q, k, v, g, beta, o, scale: float) -> _lib.DecodeArgs:

@@ -2,7 +2,7 @@
 
     python -m orionsbelt_b200.profile_cases decode [--launches 3]
     python -m orionsbelt_b200.profile_cases chunk  [--launches 1]
-    python -m orionsbelt_b200.profile_cases conv | cumsum | scan
+    python -m orionsbelt_b200.profile_cases conv | cumsum | scan | attn | int8
 
 Each case holds a few hundred MB to a few GB on the device (inputs larger
 than the 126 MB L2, so DRAM counters mean something), runs a few launches of
@@ -13,6 +13,9 @@ its kernel through the C ABI, and exits.  Cases:
   conv    config-0 Conv1D: T=2048, 8192 channels, fp32 (134 MB)
   cumsum  config-2 decay cumsum: 8 x 32768 x 32 log-decays, fp32
   scan    gated scan, 4096 tokens x 8192 channels, fp32
+  attn    GQA attention decode, config-4 heads (16 q / 4 kv x 256), B=4 over a
+          32768-token bf16 KV cache (537 MB)
+  int8    int8-weight GEMV, M=1, K=2560, N=9216 (23.6 MB of weights)
 """
 from __future__ import annotations
 
@@ -25,7 +28,7 @@ from . import _lib, ops, synth
 
 def main() -> None:
     ap = argparse.ArgumentParser()
-    ap.add_argument("case", choices=["decode", "chunk", "conv", "cumsum", "scan"])
+    ap.add_argument("case", choices=["decode", "chunk", "conv", "cumsum", "scan", "attn", "int8"])
     ap.add_argument("--launches", type=int, default=3)
     a = ap.parse_args()
     torch.cuda.set_device(0)
@@ -52,6 +55,21 @@ def main() -> None:
         g = -torch.nn.functional.softplus(synth.device_normal((8, 32768, 32), 4, 1)) * 0.1
         out = torch.empty_like(g)
         fn = lambda: ops.cumsum(g, out)  # noqa: E731
+    elif a.case == "attn":
+        kc = synth.device_normal((4, 32768, 4, 256), 6, 1, dtype=torch.bfloat16)
+        vc = synth.device_normal((4, 32768, 4, 256), 6, 2, dtype=torch.bfloat16)
+        q = synth.device_normal((4, 16, 256), 6, 3)
+        kn, vn = synth.device_normal((4, 4, 256), 6, 4), synth.device_normal((4, 4, 256), 6, 5)
+        o = torch.empty((4, 16, 256), device="cuda")
+        fn = lambda: ops.attention_decode(q, kn, vn, kc, vc, o, 32767, 0.0625)  # noqa: E731
+    elif a.case == "int8":
+        W = synth.device_normal((2560, 9216), 7, 1, std=0.05)
+        q8 = torch.empty((2560, 9216), dtype=torch.int8, device="cuda")
+        s8 = torch.empty(9216, device="cuda")
+        ops.quantize_int8(W, q8, s8)
+        A = synth.device_normal((1, 2560), 7, 2)
+        Cm = torch.empty((1, 9216), device="cuda")
+        fn = lambda: ops.matmul_int8(A, q8, s8, Cm)  # noqa: E731
     else:
         g = torch.sigmoid(synth.device_normal((4096, 8192), 5, 1))
         x = synth.device_normal((4096, 8192), 5, 2)

@@ -232,3 +232,34 @@ def test_int8_reference_accuracy_rules(orc):
     assert (np.abs(c - c32) <= 2 * bound).all()
     big = np.abs(c32) > 1.0
     assert np.mean(np.abs(c[big] - c32[big]) / np.abs(c32[big])) < 0.02
+
+
+@pytest.mark.parametrize("pos,max_ctx", [(0, 1), (37, 64), (300, 301)])
+@pytest.mark.parametrize("kind", ["f32", "i8"])
+def test_attn_decode_bit_identical_to_reference(orc, pos, max_ctx, kind):
+    """The reference's own GQA attention decode (gdn_e2e_decode.c:1532-1634
+    full_attn_real_forward and, built with KV_INT8, :1652-1830
+    full_attn_real_forward_int8kv; run through oracle/ref_attn_shim.c) against
+    the oracle: same outputs and same appended cache entries, bit for bit."""
+    import oracle
+    ra = oracle.ref_attn if kind == "f32" else oracle.ref_attn_i8
+    if ra is None:
+        pytest.skip("oracle/_ref attention shims not built (need the reference tree)")
+    H, Hkv, D = ra.heads, ra.kv_heads, ra.head_dim
+    r = np.random.default_rng(pos + (7 if kind == "i8" else 0))
+    q = r.uniform(-1, 1, H * D).astype(np.float32)
+    kn, vn = (r.uniform(-1, 1, Hkv * D).astype(np.float32) for _ in range(2))
+    if kind == "f32":
+        kc, vc = (r.uniform(-1, 1, (max_ctx, Hkv * D)).astype(np.float32) for _ in range(2))
+        ks = vs = None
+    else:
+        kc, vc = (r.integers(-128, 128, (max_ctx, Hkv * D)).astype(np.int8) for _ in range(2))
+        ks, vs = (r.uniform(0.001, 0.02, Hkv).astype(np.float32) for _ in range(2))
+    kc2, vc2 = kc.copy(), vc.copy()
+    o_ref = ra.attn_decode(q, kn, vn, kc, vc, pos, ks, vs)
+    o = orc.attn_decode(q.reshape(1, H, D), kn.reshape(1, Hkv, D), vn.reshape(1, Hkv, D),
+                        kc2.reshape(1, max_ctx, Hkv, D), vc2.reshape(1, max_ctx, Hkv, D), pos,
+                        1.0 / np.sqrt(np.float32(D)), None if ks is None else ks[None],
+                        None if vs is None else vs[None])
+    assert np.array_equal(o.ravel(), o_ref)
+    assert np.array_equal(kc2, kc) and np.array_equal(vc2, vc)
