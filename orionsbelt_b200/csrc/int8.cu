@@ -33,22 +33,37 @@ namespace gdn {
 namespace {
 
 // ------------------------------------------------------------ quantization
-// One thread per column: the column's max |B|, then its 8-bit codes.
-__global__ void __launch_bounds__(128) quantize_int8_kernel(const float *__restrict__ B, int8_t *__restrict__ q,
+// A CTA per 32 columns, 8 row lanes: the column max over the lanes' rows
+// (order does not matter), then every lane quantizes its rows.
+__global__ void __launch_bounds__(256) quantize_int8_kernel(const float *__restrict__ B, int8_t *__restrict__ q,
                                                             float *__restrict__ s, long long K, long long N) {
-    const long long n = (long long)blockIdx.x * 128 + threadIdx.x;
-    if (n >= N) return;
+    __shared__ float part[8][32];
+    __shared__ float s_inv[32];
+    const int tx = threadIdx.x % 32, ty = threadIdx.x / 32;
+    const long long n = (long long)blockIdx.x * 32 + tx;
+    const bool live = n < N;
     float mx = 0.0f;
-#pragma unroll 8
-    for (long long k = 0; k < K; ++k) {
-        const float v = fabsf(B[k * N + n]);
-        if (v > mx) mx = v;
+    if (live) {
+#pragma unroll 4
+        for (long long k = ty; k < K; k += 8) {
+            const float v = fabsf(B[k * N + n]);
+            if (v > mx) mx = v;
+        }
     }
-    const float sc = mx > 0.0f ? mx / 127.0f : 1.0f;
-    const float inv = 1.0f / sc;
-    s[n] = sc;
-#pragma unroll 8
-    for (long long k = 0; k < K; ++k) {
+    part[ty][tx] = mx;
+    __syncthreads();
+    if (ty == 0) {
+#pragma unroll
+        for (int r = 1; r < 8; ++r) mx = fmaxf(mx, part[r][tx]);
+        const float sc = mx > 0.0f ? mx / 127.0f : 1.0f;
+        s_inv[tx] = 1.0f / sc;
+        if (live) s[n] = sc;
+    }
+    __syncthreads();
+    if (!live) return;
+    const float inv = s_inv[tx];
+#pragma unroll 4
+    for (long long k = ty; k < K; k += 8) {
         long v = lroundf(__fmul_rn(B[k * N + n], inv));
         v = v > 127 ? 127 : (v < -128 ? -128 : v);
         q[k * N + n] = (int8_t)v;
@@ -357,9 +372,9 @@ int launch_stream(const float *A, const int8_t *q, const float *s, float *C, lon
 int launch_quantize_int8(const float *B, int8_t *q, float *s, size_t K, size_t N, cudaStream_t st) {
     if (K == 0 || N == 0) return KAI_GDN_OK;
     if (!B || !q || !s) return set_error(KAI_GDN_ERR_INVALID, "quantize_int8: null pointer");
-    const long long grid = ((long long)N + 127) / 128;
+    const long long grid = ((long long)N + 31) / 32;
     if (grid > 0x7fffffffll) return set_error(KAI_GDN_ERR_UNSUPPORTED, "quantize_int8: N too large");
-    quantize_int8_kernel<<<(unsigned)grid, 128, 0, st>>>(B, q, s, (long long)K, (long long)N);
+    quantize_int8_kernel<<<(unsigned)grid, 256, 0, st>>>(B, q, s, (long long)K, (long long)N);
     return check_launch("quantize_int8_kernel");
 }
 
