@@ -259,6 +259,42 @@ typedef struct kai_gdn_attn_decode_args {
 } kai_gdn_attn_decode_args;
 KAI_GDN_API int kai_run_gdn_attention_decode_sm100a(const kai_gdn_attn_decode_args *args, void *stream);
 
+/* End-to-end hybrid decode: the reference's decode loop
+ * (src/orionsbelt/engines/cpu/kernels/gdn_e2e_decode.c:2775-2796) on the
+ * GPU, one token through every layer for `batch` independent sequences:
+ * GDN layers as gdn_layer_forward (:1426-1490: q/k/v projections, Conv1D over
+ * [q | 0], the per-channel gate as decay, gated scan of v, output projection,
+ * residual), attention layers as the loop's full_attn_layer_forward
+ * (:1492-1522: projections, the new K/V into a one-entry cache, output
+ * projection of q, residual), each followed by ffn_forward (:1834-1855:
+ * SwiGLU, residual).  One weight set (the reference's Weights, host fp32,
+ * row-major [in][out], conv weights [4][conv_dim]) serves every layer and is
+ * quantized to int8 with per-column scales at creation (the INT8_WEIGHTS
+ * build).  When value_dim > key_dim the reference's scan reads past its
+ * key_dim-long decay vector; the engine repeats the key_dim gates there.
+ * The engine captures a token into a CUDA graph on the caller's stream after
+ * one eager step on that stream and replays it afterwards. */
+typedef struct kai_gdn_e2e_config {
+    size_t hidden, key_dim, value_dim, conv_dim, inter;   /* HIDDEN, KEY_DIM, VALUE_DIM, CONV_DIM, INTER */
+    size_t full_heads, full_kv_heads, full_head_dim;      /* attention layer geometry            */
+    size_t layers;                                        /* NUM_LAYERS                          */
+    const unsigned char *is_gdn;                          /* [layers]: 1 GDN, 0 attention        */
+    size_t batch;                                         /* sequences decoded together          */
+} kai_gdn_e2e_config;
+typedef struct kai_gdn_e2e_weights {
+    const float *g_q_proj, *g_k_proj, *g_v_proj, *g_o_proj, *g_conv_w, *g_beta;
+    const float *f_q_proj, *f_k_proj, *f_v_proj, *f_o_proj;
+    const float *gate_proj, *up_proj, *down_proj;
+} kai_gdn_e2e_weights;
+KAI_GDN_API int kai_gdn_e2e_create(const kai_gdn_e2e_config *cfg, const kai_gdn_e2e_weights *weights,
+                                   void **engine);
+/* hidden_in, hidden_out: [batch][hidden] fp32, host or device memory. */
+KAI_GDN_API int kai_gdn_e2e_step(void *engine, const float *hidden_in, float *hidden_out, void *stream);
+/* Copy one GDN layer's recurrent state [batch][value_dim] and Conv1D history
+ * [batch][3][conv_dim] out (either may be NULL); synchronises the device. */
+KAI_GDN_API int kai_gdn_e2e_state(void *engine, size_t layer, float *gdn_state, float *conv_hist);
+KAI_GDN_API int kai_gdn_e2e_destroy(void *engine);
+
 /* Chunkwise (WY / UT-transform) gated delta-rule scan over a whole sequence,
  * for every (batch, value head), chunk length `chunk` (64).  Equal, up to
  * rounding, to applying the decode step above for t = 0 .. seq-1 with

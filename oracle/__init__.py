@@ -31,6 +31,7 @@ ORACLE_SO = HERE / "liboracle.so"
 REF_SO = HERE / "_ref" / "libgdnref.so"
 INT8_REF_SO = HERE / "_ref" / "libint8ref.so"
 ATTN_REF_SO = HERE / "_ref" / "libattnref.so"
+E2E_REF_SO = HERE / "_ref" / "libe2eref.so"
 ATTN_I8_REF_SO = HERE / "_ref" / "libattnref_i8.so"
 
 _f = C.POINTER(C.c_float)
@@ -291,6 +292,22 @@ class _Oracle(_Kernels):
                                  C.c_int(nthreads))
         return o
 
+    def e2e_decode(self, dims, is_gdn, weights, hidden_in, nthreads=0):
+        """The end-to-end decode loop.  dims = (hidden, key_dim, value_dim, conv_dim, inter,
+        full_heads, full_kv_heads, full_head_dim, layers); weights: dict of fp32 arrays named as
+        the reference's Weights; hidden_in [T][B][hidden].  Returns (hidden_out, gdn_state
+        [layers][B][value_dim])."""
+        hin = _f32(hidden_in)
+        T, B, H = hin.shape
+        d = (C.c_size_t * 9)(*dims)
+        g = np.ascontiguousarray(is_gdn, dtype=np.uint8)
+        w = [_f32(weights[n]) for n in E2E_WEIGHTS]
+        out = np.empty_like(hin)
+        st = np.zeros((dims[8], B, dims[2]), np.float32)
+        self.lib.orc_e2e_decode(d, g.ctypes.data_as(C.c_void_p), _sz(B), _sz(T), *[_p(x, np.float32) for x in w],
+                                _p(hin, np.float32), _p(out, np.float32), _p(st, np.float32), C.c_int(nthreads))
+        return out, st
+
     def chunk_wy(self, S, q, k, v, g, beta, scale=1.0, chunk=64, nthreads=0):
         """Chunked WY form in float64 (same layouts as delta_rule_seq)."""
         S = _f32(S).copy()
@@ -317,6 +334,24 @@ def _u16_to_f32(a, kind: str) -> np.ndarray:
     if kind == "f16":
         return a.view(np.float16).astype(np.float32)
     return (a.astype(np.uint32) << 16).view(np.float32)
+
+
+E2E_WEIGHTS = ("g_q_proj", "g_k_proj", "g_v_proj", "g_o_proj", "g_conv_w", "g_beta", "f_q_proj", "f_k_proj",
+               "f_v_proj", "f_o_proj", "gate_proj", "up_proj", "down_proj")
+
+
+def e2e_weight_shapes(dims):
+    """Shapes of the reference's Weights (row-major [in][out]; conv [4][conv_dim])."""
+    H, KD, VD, CD, I, FH, FKV, FD = dims[:8]
+    return {"g_q_proj": (H, KD), "g_k_proj": (H, KD), "g_v_proj": (H, VD), "g_o_proj": (VD, H),
+            "g_conv_w": (4, CD), "g_beta": (KD,), "f_q_proj": (H, FH * FD), "f_k_proj": (H, FKV * FD),
+            "f_v_proj": (H, FKV * FD), "f_o_proj": (FH * FD, H), "gate_proj": (H, I), "up_proj": (H, I),
+            "down_proj": (I, H)}
+
+
+def e2e_layer_pattern(layers):
+    """Blocks of 3 GDN layers and 1 attention layer (gdn_e2e_decode.c:2414-2417)."""
+    return np.array([1 if (l % 4) < 3 else 0 for l in range(layers)], np.uint8)
 
 
 def f32_to_u16(a, kind: str) -> np.ndarray:
@@ -385,6 +420,29 @@ class _RefAttn:
                                  _p(o, np.float32))
         return o
 
+
+class _RefE2E:
+    """The reference's end-to-end decode loop (0.8B geometry, int8 weights), via ref_e2e_shim.c."""
+
+    def __init__(self, lib):
+        self.lib = lib
+        d = (C.c_size_t * 9)()
+        lib.ref_e2e_geometry(d)
+        self.dims = tuple(int(x) for x in d)
+
+    def e2e_decode(self, weights, hidden_in):
+        """hidden_in [T][hidden] -> (hidden_out [T][hidden], gdn_state [layers][value_dim])."""
+        hin = _f32(hidden_in)
+        out = np.empty_like(hin)
+        st = np.zeros((self.dims[8], self.dims[2]), np.float32)
+        w = [_f32(weights[n]) for n in E2E_WEIGHTS]
+        self.lib.ref_e2e_decode(*[_p(x, np.float32) for x in w], _p(hin, np.float32), _p(out, np.float32),
+                                _sz(hin.shape[0]), _p(st, np.float32))
+        return out, st
+
+
+_e2e_lib = _load(E2E_REF_SO)
+ref_e2e = _RefE2E(_e2e_lib) if _e2e_lib is not None else None
 
 _attn_lib = _load(ATTN_REF_SO)
 ref_attn = _RefAttn(_attn_lib, False) if _attn_lib is not None else None

@@ -654,6 +654,86 @@ void orc_attn_decode(const float *q, const float *k_new, const float *v_new, voi
     }
 }
 
+/* ------------------------------------------------------------------------
+ * f1: the end-to-end hybrid decode loop (gdn_e2e_decode.c:2775-2796) with the
+ * INT8_WEIGHTS build's projections: per token and sequence, every layer runs
+ * gdn_layer_forward (:1426-1490) or the loop's full_attn_layer_forward
+ * (:1492-1522), then ffn_forward (:1834-1855).  One weight set serves all
+ * layers (:2295-2321).  dims = {hidden, key_dim, value_dim, conv_dim, inter,
+ * full_heads, full_kv_heads, full_head_dim, layers}.  hidden_in / hidden_out
+ * [T][B][hidden]; the GDN state after the last token goes to gdn_state_out
+ * [layers][B][value_dim] (attention layers' rows untouched).  When value_dim >
+ * key_dim the reference scans past its key_dim-long decay vector; here the
+ * key_dim gates repeat there (decay[c] = beta[c mod key_dim]).
+ * ---------------------------------------------------------------------- */
+void orc_e2e_decode(const size_t *dims, const unsigned char *is_gdn, size_t B, size_t T, const float *g_q,
+                    const float *g_k, const float *g_v, const float *g_o, const float *g_conv_w,
+                    const float *g_beta, const float *f_q, const float *f_k, const float *f_v, const float *f_o,
+                    const float *gate_w, const float *up_w, const float *down_w, const float *hidden_in,
+                    float *hidden_out, float *gdn_state_out, int nthreads) {
+    const size_t H = dims[0], KD = dims[1], VD = dims[2], CD = dims[3], I = dims[4];
+    const size_t QD = dims[5] * dims[7], KVD = dims[6] * dims[7], L = dims[8];
+    struct { const float *w; size_t K, N; int8_t *q; float *s; } qw[11] = {
+        {g_q, H, KD}, {g_k, H, KD}, {g_v, H, VD}, {g_o, VD, H}, {f_q, H, QD}, {f_k, H, KVD},
+        {f_v, H, KVD}, {f_o, QD, H}, {gate_w, H, I}, {up_w, H, I}, {down_w, I, H}};
+    for (int i = 0; i < 11; ++i) {
+        qw[i].q = (int8_t *)malloc(qw[i].K * qw[i].N);
+        qw[i].s = (float *)malloc(qw[i].N * sizeof(float));
+        orc_quantize_int8(qw[i].w, qw[i].q, qw[i].s, qw[i].K, qw[i].N);
+    }
+#define ORC_MM(x, i, y) orc_matmul_int8((x), qw[i].q, qw[i].s, (y), 1, qw[i].K, qw[i].N, nthreads)
+    float *state = (float *)calloc(L * B * VD, sizeof(float));
+    float *hist = (float *)calloc(L * B * 3 * CD, sizeof(float));
+    float *h = (float *)malloc(H * 4), *h2 = (float *)malloc(H * 4), *proj = (float *)malloc(H * 4);
+    float *q = (float *)malloc(KD * 4), *k = (float *)malloc(KD * 4), *v = (float *)malloc(VD * 4);
+    float *cin = (float *)calloc(CD, 4), *cout = (float *)malloc(CD * 4), *beta = (float *)malloc(VD * 4);
+    float *decay = (float *)malloc(VD * 4), *scanned = (float *)malloc(VD * 4);
+    float *aq = (float *)malloc(QD * 4), *ak = (float *)malloc(KVD * 4), *av = (float *)malloc(KVD * 4);
+    float *gt = (float *)malloc(I * 4), *up = (float *)malloc(I * 4), *act = (float *)malloc(I * 4);
+    for (size_t c = 0; c < VD; ++c) beta[c] = g_beta[c % KD];
+    for (size_t t = 0; t < T; ++t)
+        for (size_t b = 0; b < B; ++b) {
+            memcpy(h, hidden_in + (t * B + b) * H, H * 4);
+            for (size_t l = 0; l < L; ++l) {
+                if (is_gdn[l]) {
+                    ORC_MM(h, 0, q);
+                    ORC_MM(h, 1, k);
+                    ORC_MM(h, 2, v);
+                    memcpy(cin, q, (KD < CD ? KD : CD) * 4);
+                    orc_causal_dwconv1d_f32(cin, g_conv_w, cout, hist + (l * B + b) * 3 * CD, 1, CD);
+                    orc_cumdecay_f32(beta, decay, 1, VD);
+                    orc_gated_scan_f32(decay, v, scanned, state + (l * B + b) * VD, 1, VD);
+                    ORC_MM(scanned, 3, proj);
+                } else {
+                    ORC_MM(h, 4, aq);
+                    ORC_MM(h, 5, ak);
+                    ORC_MM(h, 6, av);
+                    ORC_MM(aq, 7, proj);
+                }
+                for (size_t i = 0; i < H; ++i) h2[i] = h[i] + proj[i];
+                ORC_MM(h2, 8, gt);
+                ORC_MM(h2, 9, up);
+                for (size_t i = 0; i < I; ++i) {
+                    float g = gt[i];
+                    act[i] = g / (1.0f + expf(-g)) * up[i];
+                }
+                ORC_MM(act, 10, proj);
+                for (size_t i = 0; i < H; ++i) h[i] = h2[i] + proj[i];
+            }
+            memcpy(hidden_out + (t * B + b) * H, h, H * 4);
+        }
+#undef ORC_MM
+    if (gdn_state_out)
+        for (size_t l = 0; l < L; ++l)
+            if (is_gdn[l]) memcpy(gdn_state_out + l * B * VD, state + l * B * VD, B * VD * 4);
+    for (int i = 0; i < 11; ++i) {
+        free(qw[i].q);
+        free(qw[i].s);
+    }
+    free(state); free(hist); free(h); free(h2); free(proj); free(q); free(k); free(v); free(cin); free(cout);
+    free(beta); free(decay); free(scanned); free(aq); free(ak); free(av); free(gt); free(up); free(act);
+}
+
 int orc_num_threads(void) {
 #ifdef _OPENMP
     return omp_get_max_threads();

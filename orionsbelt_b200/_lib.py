@@ -41,6 +41,19 @@ class AttnDecodeArgs(C.Structure):
                 ("pos", _sz), ("max_ctx", _sz), ("scale", _f), ("cache_dtype", _i)]
 
 
+class E2EConfig(C.Structure):
+    """struct kai_gdn_e2e_config."""
+    _fields_ = [("hidden", _sz), ("key_dim", _sz), ("value_dim", _sz), ("conv_dim", _sz), ("inter", _sz),
+                ("full_heads", _sz), ("full_kv_heads", _sz), ("full_head_dim", _sz), ("layers", _sz),
+                ("is_gdn", _vp), ("batch", _sz)]
+
+
+class E2EWeights(C.Structure):
+    """struct kai_gdn_e2e_weights."""
+    _fields_ = [(n, _vp) for n in ("g_q_proj", "g_k_proj", "g_v_proj", "g_o_proj", "g_conv_w", "g_beta", "f_q_proj",
+                                   "f_k_proj", "f_v_proj", "f_o_proj", "gate_proj", "up_proj", "down_proj")]
+
+
 class ChunkArgs(C.Structure):
     """struct kai_gdn_chunk_args."""
     _fields_ = [("q", _vp), ("k", _vp), ("v", _vp), ("g", _vp), ("beta", _vp), ("state", _vp), ("o", _vp),
@@ -76,6 +89,10 @@ SIGNATURES = {
     "kai_run_gdn2_delta_rule_decode_sm100a": (_i, [C.POINTER(Gdn2DecodeArgs), _vp]),
     "kai_run_gdn_quantize_int8_sm100a": (_i, [_vp, _vp, _vp, _sz, _sz, _vp]),
     "kai_run_gdn_attention_decode_sm100a": (_i, [C.POINTER(AttnDecodeArgs), _vp]),
+    "kai_gdn_e2e_create": (_i, [C.POINTER(E2EConfig), C.POINTER(E2EWeights), C.POINTER(_vp)]),
+    "kai_gdn_e2e_step": (_i, [_vp, _vp, _vp, _vp]),
+    "kai_gdn_e2e_state": (_i, [_vp, _sz, _vp, _vp]),
+    "kai_gdn_e2e_destroy": (_i, [_vp]),
     "kai_run_gdn_matmul_int8_sm100a": (_i, [_vp, _vp, _vp, _vp, _sz, _sz, _sz, _vp]),
     "kai_run_gdn_chunk_delta_rule_sm100a": (_i, [C.POINTER(ChunkArgs), _vp]),
     # control

@@ -55,6 +55,10 @@ int launch_matmul(const float *A, const float *B, float *C, size_t M, size_t K,
 int launch_decode(const kai_gdn_decode_args *a, cudaStream_t st);
 int launch_gdn2_decode(const kai_gdn2_decode_args *a, cudaStream_t st);
 int launch_attn_decode(const kai_gdn_attn_decode_args *a, cudaStream_t st);
+int e2e_create(const kai_gdn_e2e_config *cfg, const kai_gdn_e2e_weights *w, void **out);
+int e2e_step(void *engine, const float *hidden_in, float *hidden_out, cudaStream_t st);
+int e2e_state(void *engine, size_t layer, float *gdn_state, float *conv_hist);
+int e2e_destroy(void *engine);
 int launch_quantize_int8(const float *B, int8_t *q, float *s, size_t K, size_t N, cudaStream_t st);
 int launch_matmul_int8(const float *A, const int8_t *q, const float *s, float *C, size_t M, size_t K, size_t N,
                        cudaStream_t st);

@@ -397,6 +397,20 @@ int kai_run_gdn_attention_decode_sm100a(const kai_gdn_attn_decode_args *args, vo
     return launch_attn_decode(args, (cudaStream_t)stream);
 }
 
+int kai_gdn_e2e_create(const kai_gdn_e2e_config *cfg, const kai_gdn_e2e_weights *weights, void **engine) {
+    return e2e_create(cfg, weights, engine);
+}
+
+int kai_gdn_e2e_step(void *engine, const float *hidden_in, float *hidden_out, void *stream) {
+    return e2e_step(engine, hidden_in, hidden_out, (cudaStream_t)stream);
+}
+
+int kai_gdn_e2e_state(void *engine, size_t layer, float *gdn_state, float *conv_hist) {
+    return e2e_state(engine, layer, gdn_state, conv_hist);
+}
+
+int kai_gdn_e2e_destroy(void *engine) { return e2e_destroy(engine); }
+
 int kai_run_gdn_quantize_int8_sm100a(const float *B, int8_t *q, float *s, size_t K, size_t N, void *stream) {
     return launch_quantize_int8(B, q, s, K, N, (cudaStream_t)stream);
 }

@@ -10,7 +10,7 @@ Two layers, both calling the C ABI (include/kai_gdn_cuda.h) through ctypes:
 * The device layer takes CUDA tensors (torch is used only to own device memory
   and streams) and launches on the current torch stream: ``cumdecay``,
   ``cumsum``, ``gated_scan``, ``gdn2_gated_scan``, ``causal_dwconv1d``,
-  ``matmul``, ``quantize_int8``, ``matmul_int8``, ``attention_decode``, ``delta_rule_decode``,
+  ``matmul``, ``quantize_int8``, ``matmul_int8``, ``attention_decode``, ``E2EEngine``, ``delta_rule_decode``,
   ``gdn2_delta_rule_decode`` and ``chunk_delta_rule``.
 
 There is no CPU fallback anywhere: a missing library raises at import of the
@@ -203,6 +203,50 @@ def attention_decode(q, k_new, v_new, k_cache, v_cache, o, pos: int, scale: floa
     """GQA attention decode with KV-cache append (gdn_e2e_decode.c:1532-1634, int8 cache :1652-1830)."""
     args = attn_decode_args(q, k_new, v_new, k_cache, v_cache, o, pos, scale, k_scale, v_scale)
     check(lib().kai_run_gdn_attention_decode_sm100a(args, _stream(stream)))
+
+
+class E2EEngine:
+    """The end-to-end hybrid decode engine (kai_gdn_e2e_*): the reference's decode loop
+    (gdn_e2e_decode.c:2775-2796) for `batch` sequences.  dims = (hidden, key_dim, value_dim,
+    conv_dim, inter, full_heads, full_kv_heads, full_head_dim, layers); weights: dict of host
+    fp32 numpy arrays named as the reference's Weights."""
+
+    NAMES = ("g_q_proj", "g_k_proj", "g_v_proj", "g_o_proj", "g_conv_w", "g_beta", "f_q_proj", "f_k_proj",
+             "f_v_proj", "f_o_proj", "gate_proj", "up_proj", "down_proj")
+
+    def __init__(self, dims, is_gdn, batch: int, weights):
+        import ctypes as C
+        self._is_gdn = np.ascontiguousarray(is_gdn, dtype=np.uint8)
+        self.dims, self.batch = tuple(int(x) for x in dims), int(batch)
+        H, KD, VD, CD, I, FH, FKV, FD, L = self.dims
+        cfg = _lib.E2EConfig(H, KD, VD, CD, I, FH, FKV, FD, L, self._is_gdn.ctypes.data, self.batch)
+        arrs = [np.ascontiguousarray(weights[n], dtype=np.float32) for n in self.NAMES]
+        w = _lib.E2EWeights(*[a.ctypes.data for a in arrs])
+        h = C.c_void_p()
+        check(lib().kai_gdn_e2e_create(cfg, w, C.byref(h)))
+        self._h = h
+
+    def step(self, hidden_in, hidden_out, stream=None) -> None:
+        """hidden_in, hidden_out: [batch][hidden] fp32 CUDA tensors."""
+        torch = _torch()
+        check(lib().kai_gdn_e2e_step(self._h, _dev(hidden_in, dtype=torch.float32),
+                                     _dev(hidden_out, dtype=torch.float32), _stream(stream)))
+
+    def gdn_state(self, layer: int):
+        st = np.empty((self.batch, self.dims[2]), np.float32)
+        check(lib().kai_gdn_e2e_state(self._h, layer, st.ctypes.data, None))
+        return st
+
+    def close(self) -> None:
+        if self._h:
+            lib().kai_gdn_e2e_destroy(self._h)
+            self._h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
 
 
 def decode_args(state, q, k, v, g, beta, o, scale: float) -> _lib.DecodeArgs:

@@ -98,3 +98,21 @@ def device_gdn(B, T, Hk, Hv, dk, dv, g_scale=0.1, seed=0, in_dtype=None, state_s
     else:
         S0 = torch.zeros((B, Hv, dk, dv), device="cuda", dtype=state_dtype or torch.float32)
     return dict(q=q, k=k, v=v, g=g.contiguous(), beta=beta.contiguous(), S0=S0)
+
+
+def e2e_weight_shapes(dims):
+    """Shapes of the end-to-end engine's weights, the reference's Weights
+    (gdn_e2e_decode.c:1395-1424): row-major [in][out], conv weights
+    [4][conv_dim], the GDN gate [key_dim].  dims = (hidden, key_dim,
+    value_dim, conv_dim, inter, full_heads, full_kv_heads, full_head_dim, layers)."""
+    H, KD, VD, CD, I, FH, FKV, FD = dims[:8]
+    return {"g_q_proj": (H, KD), "g_k_proj": (H, KD), "g_v_proj": (H, VD), "g_o_proj": (VD, H),
+            "g_conv_w": (4, CD), "g_beta": (KD,), "f_q_proj": (H, FH * FD), "f_k_proj": (H, FKV * FD),
+            "f_v_proj": (H, FKV * FD), "f_o_proj": (FH * FD, H), "gate_proj": (H, I), "up_proj": (H, I),
+            "down_proj": (I, H)}
+
+
+def e2e_layer_pattern(layers):
+    """Blocks of 3 GDN layers and 1 attention layer (gdn_e2e_decode.c:2414-2417)."""
+    return np.array([1 if (l % 4) < 3 else 0 for l in range(layers)], np.uint8)
+

@@ -263,3 +263,32 @@ def test_attn_decode_bit_identical_to_reference(orc, pos, max_ctx, kind):
                         None if vs is None else vs[None])
     assert np.array_equal(o.ravel(), o_ref)
     assert np.array_equal(kc2, kc) and np.array_equal(vc2, vc)
+
+
+def e2e_weights(dims, seed, sigma=0.007):
+    """Seeded weights for the end-to-end loop: projections N(0, sigma) (one set
+    serves every layer, so larger weights overflow within a few layers), conv
+    weights N(0, 1/4), gates U(0, 1)."""
+    import oracle
+    shapes = oracle.e2e_weight_shapes(dims)
+    r = np.random.default_rng(seed)
+    W = {n: (r.standard_normal(s) * sigma).astype(np.float32) for n, s in shapes.items()}
+    W["g_conv_w"] = (r.standard_normal(shapes["g_conv_w"]) * 0.5).astype(np.float32)
+    W["g_beta"] = r.uniform(0, 1, shapes["g_beta"]).astype(np.float32)
+    return W
+
+
+def test_e2e_decode_bit_identical_to_reference(orc):
+    """The reference's own end-to-end decode loop (gdn_e2e_decode.c:2775-2796,
+    INT8_WEIGHTS, 0.8B geometry; run through oracle/ref_e2e_shim.c) against the
+    oracle over three tokens: same hidden outputs and GDN states, bit for bit."""
+    import oracle
+    if oracle.ref_e2e is None:
+        pytest.skip("oracle/_ref/libe2eref.so not built (needs the reference tree)")
+    dims = oracle.ref_e2e.dims
+    W = e2e_weights(dims, 0)
+    hin = np.random.default_rng(1).standard_normal((3, dims[0])).astype(np.float32)
+    o_ref, st_ref = oracle.ref_e2e.e2e_decode(W, hin)
+    o, st = orc.e2e_decode(dims, oracle.e2e_layer_pattern(dims[8]), W, hin[:, None, :])
+    assert np.isfinite(o_ref).all()
+    assert np.array_equal(o[:, 0], o_ref) and np.array_equal(st[:, 0], st_ref)
