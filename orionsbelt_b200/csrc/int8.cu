@@ -236,6 +236,132 @@ __global__ void __launch_bounds__(NT)
     if (t == 0) ctr[slab] = 0u;  // ready for the next call on this stream
 }
 
+// ------------------------------------------- weight streaming, 4 < M <= 16
+// One pass for up to 16 activation rows: a thread owns 8 columns of one
+// weight row per step (8 bytes) and keeps all 16 rows' sums as packed fp32
+// pairs (fma.rn.f32x2); a warp covers 256 columns of a row, the 8 warps 8
+// rows.  The CTA's K range of A is staged transposed in shared memory first
+// (At[k][m]), so the 16 activations of a weight row are one broadcast read.
+// Weights stream through the per-thread cp.async ring; K parts of a slab meet
+// in the serial fix-up as in the kernel above.
+constexpr int SW16 = 256;   // columns per slab
+constexpr int UR16 = 16;    // weight rows per thread and ring stage (96 KB in flight per CTA)
+constexpr int KMAX16 = 768; // largest K range per CTA (At: 768 x 16 floats = 48 KB)
+
+__global__ void __launch_bounds__(NT, 1)
+    matmul_int8_m16_kernel(const float *__restrict__ A, const int8_t *__restrict__ q, const float *__restrict__ s,
+                           float *__restrict__ C, long long M, long long K, long long N, float *__restrict__ part,
+                           unsigned int *__restrict__ ctr) {
+    extern __shared__ __align__(16) unsigned char dsm[];
+    float *At = reinterpret_cast<float *>(dsm);                  // [KMAX16][16]
+    uint2 *wbuf = reinterpret_cast<uint2 *>(At + KMAX16 * 16);   // [ST][UR16][NT]
+    float *red = At;                                             // [8][16][SW16] after the loop
+    __shared__ bool s_last;
+    const int ksplit = (int)gridDim.y, rank = (int)blockIdx.y;
+    const long long slab = blockIdx.x;
+    const int t = threadIdx.x, lane = t % 32, w = t / 32;
+    const long long c0 = slab * SW16 + lane * 8;  // columns c0 .. c0 + 7
+    const bool live = c0 < N;                     // N % 16 == 0: eight columns are whole or absent
+    const long long kper = ((K + ksplit - 1) / ksplit + 7) / 8 * 8;
+    const long long k0 = (long long)rank * kper, k1 = min(K, k0 + kper);
+    const int nk = (int)max(0ll, k1 - k0);
+
+    for (int i = t; i < nk * 16; i += NT) {  // At[k][m] = A[m][k0 + k] (0 past M), reads along k
+        const int m = i / nk, kk = i % nk;
+        At[kk * 16 + m] = m < M ? A[(long long)m * K + k0 + kk] : 0.0f;
+    }
+    __syncthreads();
+
+    float2 acc[16][4];
+#pragma unroll
+    for (int m = 0; m < 16; ++m)
+#pragma unroll
+        for (int j = 0; j < 4; ++j) acc[m][j] = make_float2(0.0f, 0.0f);
+    const int nsteps = (live && w < nk) ? (nk - w + 7) / 8 : 0;  // rows w, w + 8, ... of the range
+    const int ngroups = (nsteps + UR16 - 1) / UR16;
+    auto issue = [&](int g) {
+        if (g < ngroups) {
+            const int st = g % ST;
+#pragma unroll
+            for (int u = 0; u < UR16; ++u) {
+                const int kk = w + (g * UR16 + u) * 8;
+                if (kk < nk)
+                    asm volatile("cp.async.ca.shared.global [%0], [%1], 8;" ::"r"(
+                                     (unsigned)__cvta_generic_to_shared(&wbuf[(st * UR16 + u) * NT + t])),
+                                 "l"(q + (k0 + kk) * N + c0)
+                                 : "memory");
+            }
+        }
+        cp_async_commit();
+    };
+#pragma unroll
+    for (int g = 0; g < ST - 1; ++g) issue(g);
+    for (int g = 0; g < ngroups; ++g) {
+        issue(g + ST - 1);
+        cp_async_wait<ST - 1>();
+        const int st = g % ST;
+#pragma unroll
+        for (int u = 0; u < UR16; ++u) {
+            const int kk = w + (g * UR16 + u) * 8;
+            if (kk >= nk) break;
+            const uint2 wv = wbuf[(st * UR16 + u) * NT + t];
+            float f[8];
+            deq4(wv.x, f[0], f[1], f[2], f[3]);
+            deq4(wv.y, f[4], f[5], f[6], f[7]);
+            const float2 w2[4] = {make_float2(f[0], f[1]), make_float2(f[2], f[3]), make_float2(f[4], f[5]),
+                                  make_float2(f[6], f[7])};
+            const float4 *a4 = reinterpret_cast<const float4 *>(At + kk * 16);
+#pragma unroll
+            for (int mq = 0; mq < 4; ++mq) {
+                const float4 a = a4[mq];
+                const float av[4] = {a.x, a.y, a.z, a.w};
+#pragma unroll
+                for (int mm = 0; mm < 4; ++mm) {
+                    const float2 a2 = make_float2(av[mm], av[mm]);
+#pragma unroll
+                    for (int j = 0; j < 4; ++j) acc[mq * 4 + mm][j] = __ffma2_rn(a2, w2[j], acc[mq * 4 + mm][j]);
+                }
+            }
+        }
+    }
+    cp_async_wait<0>();
+    __syncthreads();  // At and the ring are done: red reuses them
+#pragma unroll
+    for (int m = 0; m < 16; ++m)
+#pragma unroll
+        for (int j = 0; j < 4; ++j)
+            *reinterpret_cast<float2 *>(&red[(w * 16 + m) * SW16 + lane * 8 + 2 * j]) = acc[m][j];
+    __syncthreads();
+    const long long col = slab * SW16 + t;  // NT == SW16: one column per thread
+    if (col < N) {
+        for (int m = 0; m < M; ++m) {
+            float v = 0.0f;
+#pragma unroll
+            for (int ww = 0; ww < 8; ++ww) v += red[(ww * 16 + m) * SW16 + t];
+            if (ksplit == 1)
+                C[m * N + col] = v * s[col];
+            else
+                part[((long long)rank * M + m) * N + col] = v;
+        }
+    }
+    if (ksplit == 1) return;
+    __threadfence();
+    __syncthreads();
+    if (t == 0) s_last = atomicAdd(&ctr[slab], 1u) == (unsigned)ksplit - 1;
+    __syncthreads();
+    if (!s_last) return;
+    __threadfence();
+    for (long long i = t; i < M * SW16; i += NT) {
+        const long long m = i / SW16, col = slab * SW16 + i % SW16;
+        if (col >= N) continue;
+        float v = 0.0f;
+        for (int r = 0; r < ksplit; ++r) v += __ldcg(part + ((long long)r * M + m) * N + col);
+        C[m * N + col] = v * s[col];
+    }
+    if (t == 0) ctr[slab] = 0u;
+}
+static_assert(NT == SW16, "one output column per thread in the epilogue");
+
 // -------------------------------------------------- tiled GEMM, M > 16
 // 64 x 64 tile of C per CTA, 256 threads with 4 x 4 each; K in steps of 32,
 // A and the dequantized weights staged in shared memory.
@@ -367,6 +493,34 @@ int launch_stream(const float *A, const int8_t *q, const float *s, float *C, lon
     return check_launch("matmul_int8_stream_kernel");
 }
 
+int launch_m16(const float *A, const int8_t *q, const float *s, float *C, long long M, long long K, long long N,
+               cudaStream_t st) {
+    const size_t smem = std::max((size_t)KMAX16 * 16 * 4 + (size_t)ST * UR16 * NT * 8, (size_t)8 * 16 * SW16 * 4);
+    static std::atomic<unsigned long long> attr_set{0};  // per device
+    int dev = 0;
+    int rc = check_cuda(cudaGetDevice(&dev), "matmul_int8: cudaGetDevice");
+    if (rc) return rc;
+    const unsigned long long bit = 1ull << (dev & 63);
+    if (!(attr_set.load() & bit)) {
+        rc = check_cuda(cudaFuncSetAttribute(matmul_int8_m16_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             (int)smem),
+                        "matmul_int8: smem attribute");
+        if (rc) return rc;
+        attr_set.fetch_or(bit);
+    }
+    const long long slabs = (N + SW16 - 1) / SW16;
+    // One CTA per SM (registers): split K until the CTAs come close to one
+    // wave, and until every part fits the staged A.
+    int ks = 1;
+    while (ks < 64 && (10 * slabs * ks < 9ll * sm_count() || (K + ks - 1) / ks > KMAX16 - 8)) ks *= 2;
+    if ((K + ks - 1) / ks > KMAX16 - 8) return set_error(KAI_GDN_ERR_UNSUPPORTED, "matmul_int8: K too large");
+    unsigned int *ctr = nullptr;
+    float *part = nullptr;
+    if (ks > 1 && (rc = split_workspace(st, (size_t)slabs, (size_t)ks * M * N, &ctr, &part))) return rc;
+    matmul_int8_m16_kernel<<<dim3((unsigned)slabs, (unsigned)ks), NT, smem, st>>>(A, q, s, C, M, K, N, part, ctr);
+    return check_launch("matmul_int8_m16_kernel");
+}
+
 }  // namespace
 
 int launch_quantize_int8(const float *B, int8_t *q, float *s, size_t K, size_t N, cudaStream_t st) {
@@ -389,7 +543,8 @@ int launch_matmul_int8(const float *A, const int8_t *q, const float *s, float *C
     if (M <= 16 && vec) {
         if (M == 1) return launch_stream<1>(A, q, s, C, m, k, n, st);
         if (M == 2) return launch_stream<2>(A, q, s, C, m, k, n, st);
-        return launch_stream<4>(A, q, s, C, m, k, n, st);
+        if (M <= 4) return launch_stream<4>(A, q, s, C, m, k, n, st);
+        return launch_m16(A, q, s, C, m, k, n, st);
     }
     const long long gy = (m + TM - 1) / TM, gx = (n + TN - 1) / TN;
     if (gy > 65535 || gx > 0x7fffffffll) return set_error(KAI_GDN_ERR_UNSUPPORTED, "matmul_int8: shape too large");
