@@ -8,11 +8,14 @@
 //   weights              one set shared by all layers, int8 with per-column
 //                        scales (the INT8_WEIGHTS build, :2311-2321)
 // Per token and layer the engine launches the library's own kernels: the int8
-// matmul for every projection (M = batch), the causal Conv1D, the prefix
-// product and the gated scan of the GDN stand-in, and two elementwise kernels
-// (residual add, SiLU(gate) * up).  The whole token is captured once into a
-// CUDA graph on the caller's stream and replayed, so the ~430 launches of a
-// 32-layer token cost one graph launch.
+// matmul for the projections (M = batch; the q/k/v projections of a layer and
+// the FFN's gate/up pair each as one matmul over their concatenated columns,
+// which quantize to the same codes and scales as the separate matrices), the
+// causal Conv1D and the gated scan of the GDN stand-in, and two elementwise
+// kernels (residual add, SiLU(gate) * up).  The GDN decay is the prefix
+// product of one token's constant gate, i.e. the gate itself, so it is formed
+// once.  The whole token is captured into a CUDA graph on the caller's stream
+// and replayed (~330 launches for a 32-layer token, one graph launch).
 //
 // The reference's GDN stand-in scans VALUE_DIM channels with a decay vector of
 // KEY_DIM entries (:1472-1476); when VALUE_DIM > KEY_DIM (its 4B geometry) it
@@ -20,6 +23,8 @@
 // the value channels there (decay[c] = beta[c mod KEY_DIM]); with KEY_DIM ==
 // VALUE_DIM (the 0.8B geometry) it is the reference's computation.
 #include <algorithm>
+#include <initializer_list>
+#include <utility>
 #include <vector>
 
 #include "gdn_internal.cuh"
@@ -33,13 +38,13 @@ __global__ void add_kernel(float *__restrict__ out, const float *__restrict__ a,
         out[i] = __fadd_rn(a[i], b[i]);
 }
 
-// act = g / (1 + exp(-g)) * up  (ffn_forward :1844-1847)
-__global__ void silu_mul_kernel(float *__restrict__ out, const float *__restrict__ g, const float *__restrict__ u,
-                                long long n) {
+// act = g / (1 + exp(-g)) * up  (ffn_forward :1844-1847); gu rows are [gate | up]
+__global__ void silu_mul_kernel(float *__restrict__ out, const float *__restrict__ gu, long long inter, long long n) {
     for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n;
          i += (long long)gridDim.x * blockDim.x) {
-        const float x = g[i];
-        out[i] = __fmul_rn(__fdiv_rn(x, __fadd_rn(1.0f, expf(-x))), u[i]);
+        const long long b = i / inter, c = i % inter;
+        const float x = gu[b * 2 * inter + c];
+        out[i] = __fmul_rn(__fdiv_rn(x, __fadd_rn(1.0f, expf(-x))), gu[b * 2 * inter + inter + c]);
     }
 }
 
@@ -57,12 +62,11 @@ struct E2EEngine {
     kai_gdn_e2e_config cfg{};
     std::vector<unsigned char> is_gdn;
     int device = 0;
-    QWd gq, gk, gv, go, fq, fk, fv, fo, up, gate, down;
+    QWd gqkv, go, fqkv, fo, gu, down;  // [q | k | v] and [gate | up] concatenated by columns
     float *conv_w = nullptr, *beta_b = nullptr;  // [4][conv_dim]; [batch][value_dim]
     std::vector<float *> gdn_state, conv_hist, kv_k, kv_v;
-    float *h = nullptr, *h2 = nullptr, *q = nullptr, *k = nullptr, *v = nullptr, *conv_in = nullptr,
-          *conv_out = nullptr, *decay = nullptr, *scanned = nullptr, *proj = nullptr, *aq = nullptr, *ak = nullptr,
-          *av = nullptr, *g_out = nullptr, *u_out = nullptr, *act = nullptr;
+    float *h = nullptr, *h2 = nullptr, *qkv = nullptr, *v = nullptr, *conv_in = nullptr, *conv_out = nullptr,
+          *scanned = nullptr, *proj = nullptr, *aqkv = nullptr, *aq = nullptr, *gu_out = nullptr, *act = nullptr;
     std::vector<void *> allocs;
     cudaGraphExec_t exec = nullptr;
     cudaStream_t graph_stream = nullptr, last_stream = nullptr;
@@ -79,12 +83,24 @@ int dalloc(E2EEngine *e, void **p, size_t bytes, bool zero) {
     return rc;
 }
 
-int make_qw(E2EEngine *e, QWd *w, const float *host, size_t K, size_t N) {
-    if (!host) return set_error(KAI_GDN_ERR_INVALID, "e2e: null weight");
+// Quantize the column concatenation of host matrices [K][N_i] into one [K][sum N_i].
+int make_qw(E2EEngine *e, QWd *w, std::initializer_list<std::pair<const float *, size_t>> parts, size_t K) {
+    size_t N = 0;
+    for (auto &pt : parts) {
+        if (!pt.first) return set_error(KAI_GDN_ERR_INVALID, "e2e: null weight");
+        N += pt.second;
+    }
     float *tmp = nullptr;
     int rc = check_cuda(cudaMalloc(&tmp, K * N * sizeof(float)), "e2e: cudaMalloc");
     if (rc) return rc;
-    rc = check_cuda(cudaMemcpy(tmp, host, K * N * sizeof(float), cudaMemcpyHostToDevice), "e2e: weight upload");
+    size_t col = 0;
+    for (auto &pt : parts) {
+        if (!rc)
+            rc = check_cuda(cudaMemcpy2D(tmp + col, N * sizeof(float), pt.first, pt.second * sizeof(float),
+                                         pt.second * sizeof(float), K, cudaMemcpyHostToDevice),
+                            "e2e: weight upload");
+        col += pt.second;
+    }
     if (!rc) rc = dalloc(e, (void **)&w->q, K * N, false);
     if (!rc) rc = dalloc(e, (void **)&w->s, N * sizeof(float), false);
     if (!rc) rc = launch_quantize_int8(tmp, w->q, w->s, K, N, 0);
@@ -109,38 +125,42 @@ int run_token(E2EEngine *e, cudaStream_t st) {
     do {                    \
         if ((rc = (x))) return rc; \
     } while (0)
+    const size_t GQ = 2 * KD + VD, AQ = qd + 2 * kvd;  // widths of the concatenated projections
     for (size_t l = 0; l < c.layers; ++l) {
         if (e->is_gdn[l]) {
-            // gdn_layer_forward: projections, Conv1D over [q | 0], decay, gated scan, output, residual
-            E2E_TRY(mm(e->h, e->gq, e->q, B, st));
-            E2E_TRY(mm(e->h, e->gk, e->k, B, st));
-            E2E_TRY(mm(e->h, e->gv, e->v, B, st));
-            E2E_TRY(check_cuda(cudaMemcpy2DAsync(e->conv_in, CD * sizeof(float), e->q, KD * sizeof(float),
+            // gdn_layer_forward: projections, Conv1D over [q | 0], gated scan of v with the gate
+            // as decay, output projection, residual
+            E2E_TRY(mm(e->h, e->gqkv, e->qkv, B, st));
+            E2E_TRY(check_cuda(cudaMemcpy2DAsync(e->conv_in, CD * sizeof(float), e->qkv, GQ * sizeof(float),
                                                  std::min(KD, CD) * sizeof(float), B, cudaMemcpyDeviceToDevice, st),
                                "e2e: conv input"));
+            E2E_TRY(check_cuda(cudaMemcpy2DAsync(e->v, VD * sizeof(float), e->qkv + 2 * KD, GQ * sizeof(float),
+                                                 VD * sizeof(float), B, cudaMemcpyDeviceToDevice, st),
+                               "e2e: v"));
             E2E_TRY(launch_conv(e->conv_in, e->conv_w, e->conv_out, e->conv_hist[l], KAI_GDN_F32, B, 1, CD, st));
-            E2E_TRY(launch_cumdecay(e->beta_b, e->decay, KAI_GDN_F32, B, 1, VD, st));
-            E2E_TRY(launch_gated_scan(e->decay, e->v, e->scanned, e->gdn_state[l], KAI_GDN_F32, B, 1, VD, st));
+            E2E_TRY(launch_gated_scan(e->beta_b, e->v, e->scanned, e->gdn_state[l], KAI_GDN_F32, B, 1, VD, st));
             E2E_TRY(mm(e->scanned, e->go, e->proj, B, st));
         } else {
             // full_attn_layer_forward: projections, the new K/V into the one-entry cache,
             // output projection of q (the loop's simulated attention), residual
-            E2E_TRY(mm(e->h, e->fq, e->aq, B, st));
-            E2E_TRY(mm(e->h, e->fk, e->ak, B, st));
-            E2E_TRY(mm(e->h, e->fv, e->av, B, st));
-            E2E_TRY(check_cuda(cudaMemcpyAsync(e->kv_k[l], e->ak, B * kvd * sizeof(float), cudaMemcpyDeviceToDevice, st),
+            E2E_TRY(mm(e->h, e->fqkv, e->aqkv, B, st));
+            E2E_TRY(check_cuda(cudaMemcpy2DAsync(e->kv_k[l], kvd * sizeof(float), e->aqkv + qd, AQ * sizeof(float),
+                                                 kvd * sizeof(float), B, cudaMemcpyDeviceToDevice, st),
                                "e2e: kv"));
-            E2E_TRY(check_cuda(cudaMemcpyAsync(e->kv_v[l], e->av, B * kvd * sizeof(float), cudaMemcpyDeviceToDevice, st),
+            E2E_TRY(check_cuda(cudaMemcpy2DAsync(e->kv_v[l], kvd * sizeof(float), e->aqkv + qd + kvd,
+                                                 AQ * sizeof(float), kvd * sizeof(float), B,
+                                                 cudaMemcpyDeviceToDevice, st),
                                "e2e: kv"));
+            E2E_TRY(check_cuda(cudaMemcpy2DAsync(e->aq, qd * sizeof(float), e->aqkv, AQ * sizeof(float),
+                                                 qd * sizeof(float), B, cudaMemcpyDeviceToDevice, st),
+                               "e2e: q"));
             E2E_TRY(mm(e->aq, e->fo, e->proj, B, st));
-            (void)qd;
         }
         add_kernel<<<ew_grid((long long)(B * H)), 256, 0, st>>>(e->h2, e->h, e->proj, (long long)(B * H));
         E2E_TRY(check_launch("add_kernel"));
         // ffn_forward: SwiGLU, residual
-        E2E_TRY(mm(e->h2, e->gate, e->g_out, B, st));
-        E2E_TRY(mm(e->h2, e->up, e->u_out, B, st));
-        silu_mul_kernel<<<ew_grid((long long)(B * c.inter)), 256, 0, st>>>(e->act, e->g_out, e->u_out,
+        E2E_TRY(mm(e->h2, e->gu, e->gu_out, B, st));
+        silu_mul_kernel<<<ew_grid((long long)(B * c.inter)), 256, 0, st>>>(e->act, e->gu_out, (long long)c.inter,
                                                                          (long long)(B * c.inter));
         E2E_TRY(check_launch("silu_mul_kernel"));
         E2E_TRY(mm(e->act, e->down, e->proj, B, st));
@@ -172,23 +192,18 @@ int e2e_create(const kai_gdn_e2e_config *cfg, const kai_gdn_e2e_weights *w, void
     const size_t B = c.batch, H = c.hidden, KD = c.key_dim, VD = c.value_dim, CD = c.conv_dim, I = c.inter;
     const size_t qd = c.full_heads * c.full_head_dim, kvd = c.full_kv_heads * c.full_head_dim;
     int rc = 0;
-    if (!rc) rc = make_qw(e, &e->gq, w->g_q_proj, H, KD);
-    if (!rc) rc = make_qw(e, &e->gk, w->g_k_proj, H, KD);
-    if (!rc) rc = make_qw(e, &e->gv, w->g_v_proj, H, VD);
-    if (!rc) rc = make_qw(e, &e->go, w->g_o_proj, VD, H);
-    if (!rc) rc = make_qw(e, &e->fq, w->f_q_proj, H, qd);
-    if (!rc) rc = make_qw(e, &e->fk, w->f_k_proj, H, kvd);
-    if (!rc) rc = make_qw(e, &e->fv, w->f_v_proj, H, kvd);
-    if (!rc) rc = make_qw(e, &e->fo, w->f_o_proj, qd, H);
-    if (!rc) rc = make_qw(e, &e->gate, w->gate_proj, H, I);
-    if (!rc) rc = make_qw(e, &e->up, w->up_proj, H, I);
-    if (!rc) rc = make_qw(e, &e->down, w->down_proj, I, H);
+    if (!rc) rc = make_qw(e, &e->gqkv, {{w->g_q_proj, KD}, {w->g_k_proj, KD}, {w->g_v_proj, VD}}, H);
+    if (!rc) rc = make_qw(e, &e->go, {{w->g_o_proj, H}}, VD);
+    if (!rc) rc = make_qw(e, &e->fqkv, {{w->f_q_proj, qd}, {w->f_k_proj, kvd}, {w->f_v_proj, kvd}}, H);
+    if (!rc) rc = make_qw(e, &e->fo, {{w->f_o_proj, H}}, qd);
+    if (!rc) rc = make_qw(e, &e->gu, {{w->gate_proj, I}, {w->up_proj, I}}, H);
+    if (!rc) rc = make_qw(e, &e->down, {{w->down_proj, H}}, I);
     if (!rc && (!w->g_conv_w || !w->g_beta)) rc = set_error(KAI_GDN_ERR_INVALID, "e2e_create: null weight");
     if (!rc) rc = dalloc(e, (void **)&e->conv_w, 4 * CD * sizeof(float), false);
     if (!rc)
         rc = check_cuda(cudaMemcpy(e->conv_w, w->g_conv_w, 4 * CD * sizeof(float), cudaMemcpyHostToDevice),
                         "e2e: conv weights");
-    if (!rc) {  // the per-channel gate, one copy per sequence (repeated past key_dim)
+    if (!rc) {  // the per-channel gate = the one-token decay, per sequence (repeated past key_dim)
         std::vector<float> bb(B * VD);
         for (size_t b = 0; b < B; ++b)
             for (size_t ch = 0; ch < VD; ++ch) bb[b * VD + ch] = w->g_beta[ch % KD];
@@ -214,10 +229,10 @@ int e2e_create(const kai_gdn_e2e_config *cfg, const kai_gdn_e2e_weights *w, void
     struct Buf {
         float **p;
         size_t n;
-    } bufs[] = {{&e->h, B * H},        {&e->h2, B * H},      {&e->q, B * KD},       {&e->k, B * KD},
-                {&e->v, B * VD},       {&e->conv_in, B * CD}, {&e->conv_out, B * CD}, {&e->decay, B * VD},
-                {&e->scanned, B * VD}, {&e->proj, B * H},    {&e->aq, B * qd},      {&e->ak, B * kvd},
-                {&e->av, B * kvd},     {&e->g_out, B * I},   {&e->u_out, B * I},    {&e->act, B * I}};
+    } bufs[] = {{&e->h, B * H},          {&e->h2, B * H},          {&e->qkv, B * (2 * KD + VD)},
+                {&e->v, B * VD},          {&e->conv_in, B * CD},    {&e->conv_out, B * CD},
+                {&e->scanned, B * VD},    {&e->proj, B * H},        {&e->aqkv, B * (qd + 2 * kvd)},
+                {&e->aq, B * qd},         {&e->gu_out, B * 2 * I},  {&e->act, B * I}};
     for (auto &bf : bufs)
         if (!rc) rc = dalloc(e, (void **)bf.p, bf.n * sizeof(float), true);
     if (rc) {
