@@ -62,6 +62,11 @@ int e2e_destroy(void *engine);
 int launch_quantize_int8(const float *B, int8_t *q, float *s, size_t K, size_t N, cudaStream_t st);
 int launch_matmul_int8(const float *A, const int8_t *q, const float *s, float *C, size_t M, size_t K, size_t N,
                        cudaStream_t st);
+int launch_matmul_int8_tc(const float *A, const int8_t *q, const float *s, float *C, size_t M, size_t K, size_t N,
+                          cudaStream_t st);
+// Per-stream split-K workspace of the int8 matmuls: slab counters (zero
+// between calls: each kernel's last CTA resets its counter) and partial sums.
+int split_workspace(cudaStream_t st, size_t nctr, size_t npart, unsigned int **ctr, float **part);
 int launch_chunk(const kai_gdn_chunk_args *a, cudaStream_t st);
 // Warp-specialised tensor-core chunk scan (chunk_ws.cu): bf16/fp16 q, k, v,
 // dk = dv = 128, chunk 64; TMA-fed, tcgen05 MMAs, fp32 state in TMEM.

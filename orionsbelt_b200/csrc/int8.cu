@@ -417,53 +417,6 @@ __global__ void __launch_bounds__(256) matmul_int8_tiled_kernel(const float *__r
     }
 }
 
-// Split-K workspace per (device, stream): the slab counters (zeroed once at
-// allocation, reset by the kernels) and the partial sums.
-struct SplitWs {
-    int device;
-    cudaStream_t stream;
-    unsigned int *ctr;
-    float *part;
-    size_t nctr, npart;
-};
-std::mutex g_ws_mu;
-std::vector<SplitWs> g_ws;
-
-int split_workspace(cudaStream_t st, size_t nctr, size_t npart, unsigned int **ctr, float **part) {
-    int dev = 0;
-    int rc = check_cuda(cudaGetDevice(&dev), "matmul_int8: cudaGetDevice");
-    if (rc) return rc;
-    std::lock_guard<std::mutex> lock(g_ws_mu);
-    SplitWs *e = nullptr;
-    for (auto &x : g_ws)
-        if (x.device == dev && x.stream == st) e = &x;
-    if (!e) {
-        g_ws.push_back({dev, st, nullptr, nullptr, 0, 0});
-        e = &g_ws.back();
-    }
-    if (e->nctr < nctr) {
-        if ((rc = check_cuda(cudaFree(e->ctr), "matmul_int8: cudaFree"))) return rc;  // waits for the device
-        e->ctr = nullptr;
-        e->nctr = 0;
-        const size_t n = std::max<size_t>(nctr, 4096);
-        if ((rc = check_cuda(cudaMalloc(&e->ctr, n * sizeof(unsigned int)), "matmul_int8: cudaMalloc"))) return rc;
-        if ((rc = check_cuda(cudaMemsetAsync(e->ctr, 0, n * sizeof(unsigned int), st), "matmul_int8: memset")))
-            return rc;
-        e->nctr = n;
-    }
-    if (e->npart < npart) {
-        if ((rc = check_cuda(cudaFree(e->part), "matmul_int8: cudaFree"))) return rc;
-        e->part = nullptr;
-        e->npart = 0;
-        const size_t n = std::max<size_t>(npart + npart / 2, 1 << 18);
-        if ((rc = check_cuda(cudaMalloc(&e->part, n * sizeof(float)), "matmul_int8: cudaMalloc"))) return rc;
-        e->npart = n;
-    }
-    *ctr = e->ctr;
-    *part = e->part;
-    return KAI_GDN_OK;
-}
-
 template <int MB>
 int launch_stream(const float *A, const int8_t *q, const float *s, float *C, long long M, long long K, long long N,
                   cudaStream_t st) {
@@ -523,6 +476,53 @@ int launch_m16(const float *A, const int8_t *q, const float *s, float *C, long l
 
 }  // namespace
 
+// Split-K workspace per (device, stream): the slab counters (zeroed once at
+// allocation, reset by the kernels) and the partial sums.
+struct SplitWs {
+    int device;
+    cudaStream_t stream;
+    unsigned int *ctr;
+    float *part;
+    size_t nctr, npart;
+};
+static std::mutex g_ws_mu;
+static std::vector<SplitWs> g_ws;
+
+int split_workspace(cudaStream_t st, size_t nctr, size_t npart, unsigned int **ctr, float **part) {
+    int dev = 0;
+    int rc = check_cuda(cudaGetDevice(&dev), "matmul_int8: cudaGetDevice");
+    if (rc) return rc;
+    std::lock_guard<std::mutex> lock(g_ws_mu);
+    SplitWs *e = nullptr;
+    for (auto &x : g_ws)
+        if (x.device == dev && x.stream == st) e = &x;
+    if (!e) {
+        g_ws.push_back({dev, st, nullptr, nullptr, 0, 0});
+        e = &g_ws.back();
+    }
+    if (e->nctr < nctr) {
+        if ((rc = check_cuda(cudaFree(e->ctr), "matmul_int8: cudaFree"))) return rc;  // waits for the device
+        e->ctr = nullptr;
+        e->nctr = 0;
+        const size_t n = std::max<size_t>(nctr, 4096);
+        if ((rc = check_cuda(cudaMalloc(&e->ctr, n * sizeof(unsigned int)), "matmul_int8: cudaMalloc"))) return rc;
+        if ((rc = check_cuda(cudaMemsetAsync(e->ctr, 0, n * sizeof(unsigned int), st), "matmul_int8: memset")))
+            return rc;
+        e->nctr = n;
+    }
+    if (e->npart < npart) {
+        if ((rc = check_cuda(cudaFree(e->part), "matmul_int8: cudaFree"))) return rc;
+        e->part = nullptr;
+        e->npart = 0;
+        const size_t n = std::max<size_t>(npart + npart / 2, 1 << 18);
+        if ((rc = check_cuda(cudaMalloc(&e->part, n * sizeof(float)), "matmul_int8: cudaMalloc"))) return rc;
+        e->npart = n;
+    }
+    *ctr = e->ctr;
+    *part = e->part;
+    return KAI_GDN_OK;
+}
+
 int launch_quantize_int8(const float *B, int8_t *q, float *s, size_t K, size_t N, cudaStream_t st) {
     if (K == 0 || N == 0) return KAI_GDN_OK;
     if (!B || !q || !s) return set_error(KAI_GDN_ERR_INVALID, "quantize_int8: null pointer");
@@ -544,8 +544,9 @@ int launch_matmul_int8(const float *A, const int8_t *q, const float *s, float *C
         if (M == 1) return launch_stream<1>(A, q, s, C, m, k, n, st);
         if (M == 2) return launch_stream<2>(A, q, s, C, m, k, n, st);
         if (M <= 4) return launch_stream<4>(A, q, s, C, m, k, n, st);
-        return launch_m16(A, q, s, C, m, k, n, st);
+        if (M < 16) return launch_m16(A, q, s, C, m, k, n, st);
     }
+    if (M >= 16 && vec && K % 4 == 0 && (uintptr_t)A % 16 == 0) return launch_matmul_int8_tc(A, q, s, C, M, K, N, st);
     const long long gy = (m + TM - 1) / TM, gx = (n + TN - 1) / TN;
     if (gy > 65535 || gx > 0x7fffffffll) return set_error(KAI_GDN_ERR_UNSUPPORTED, "matmul_int8: shape too large");
     matmul_int8_tiled_kernel<<<dim3((unsigned)gx, (unsigned)gy), 256, 0, st>>>(A, q, s, C, m, k, n);

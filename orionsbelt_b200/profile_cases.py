@@ -16,6 +16,7 @@ its kernel through the C ABI, and exits.  Cases:
   attn    GQA attention decode, config-4 heads (16 q / 4 kv x 256), B=4 over a
           32768-token bf16 KV cache (537 MB)
   int8    int8-weight GEMV, M=1, K=2560, N=9216 (23.6 MB of weights)
+  int8m16 the same weights, M=16 (the tensor-core path)
 """
 from __future__ import annotations
 
@@ -28,7 +29,7 @@ from . import _lib, ops, synth
 
 def main() -> None:
     ap = argparse.ArgumentParser()
-    ap.add_argument("case", choices=["decode", "chunk", "conv", "cumsum", "scan", "attn", "int8"])
+    ap.add_argument("case", choices=["decode", "chunk", "conv", "cumsum", "scan", "attn", "int8", "int8m16"])
     ap.add_argument("--launches", type=int, default=3)
     a = ap.parse_args()
     torch.cuda.set_device(0)
@@ -62,13 +63,14 @@ def main() -> None:
         kn, vn = synth.device_normal((4, 4, 256), 6, 4), synth.device_normal((4, 4, 256), 6, 5)
         o = torch.empty((4, 16, 256), device="cuda")
         fn = lambda: ops.attention_decode(q, kn, vn, kc, vc, o, 32767, 0.0625)  # noqa: E731
-    elif a.case == "int8":
+    elif a.case in ("int8", "int8m16"):
         W = synth.device_normal((2560, 9216), 7, 1, std=0.05)
         q8 = torch.empty((2560, 9216), dtype=torch.int8, device="cuda")
         s8 = torch.empty(9216, device="cuda")
         ops.quantize_int8(W, q8, s8)
-        A = synth.device_normal((1, 2560), 7, 2)
-        Cm = torch.empty((1, 9216), device="cuda")
+        M = 16 if a.case == "int8m16" else 1
+        A = synth.device_normal((M, 2560), 7, 2)
+        Cm = torch.empty((M, 9216), device="cuda")
         fn = lambda: ops.matmul_int8(A, q8, s8, Cm)  # noqa: E731
     else:
         g = torch.sigmoid(synth.device_normal((4096, 8192), 5, 1))
