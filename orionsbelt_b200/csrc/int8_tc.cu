@@ -13,7 +13,7 @@
 //              24 mantissa bits between them), K-major, as 3*MT rows;
 //   D          fp32 in TMEM, 128 lanes (columns n) x 3*MT columns; the
 //              epilogue adds the three terms and applies the column scale.
-// A CTA of 128 threads streams its K range: int8 weights and fp32 activations
+// A CTA of 256 threads streams its K range: int8 weights and fp32 activations
 // of four 64-k chunks in flight through a cp.async ring, each chunk converted
 // into one of two operand buffers while the tensor core works on the other,
 // four K=16 MMAs per chunk issued by one elected thread and committed to the
@@ -32,7 +32,7 @@ namespace {
 
 using namespace umma;
 
-constexpr int TN = 128, KC = 64, NST = 4, TCT = 128;
+constexpr int TN = 128, KC = 64, NST = 4, TCT = 256;
 
 __device__ __forceinline__ void cp16z(void *dst, const void *src, bool full) {
     asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"((unsigned)__cvta_generic_to_shared(dst)),
@@ -217,9 +217,11 @@ __global__ void __launch_bounds__(TCT, 1)
     bad = __syncthreads_or(bad);
     fence_after_sync();
 
-    // epilogue: lane n = 32 warp + lane of the tile; columns m, MT + m, 2 MT + m
-    const long long n = n0 + 32 * warp + lane;
-    if (!bad) {
+    // epilogue (warps 0-3, one TMEM lane quarter each): lane n = 32 warp + lane
+    // of the tile; columns m, MT + m, 2 MT + m
+    const int wq = warp & 3, wh = warp >> 2;
+    const long long n = n0 + 32 * wq + lane;
+    if (!bad && wh == 0) {
 #pragma unroll
         for (int mc = 0; mc < MT; mc += 16) {
             float h[16], md[16], lw[16];
@@ -259,7 +261,7 @@ __global__ void __launch_bounds__(TCT, 1)
     if (!s_last) return;
     __threadfence();
     if (n < N) {
-        for (int i = 0; i < MT; ++i) {
+        for (int i = wh; i < MT; i += TCT / 128) {
             const long long m = m0 + i;
             if (m >= M) break;
             float v = 0.0f;
