@@ -344,19 +344,38 @@ __global__ void __launch_bounds__(AT, G == 8 ? 1 : 2) attn_split_kernel(AttnP p)
 }
 
 // Merge the chunks of one (b, query head): o = sum_c e^(m_c - M) acc_c /
-// sum_c e^(m_c - M) l_c (times the int8 value scale), in chunk order.
+// sum_c e^(m_c - M) l_c (times the int8 value scale), in chunk order.  The
+// chunks' maxima and sums are read in parallel into shared memory first, so
+// the weighted sum's loads are independent of one another.
 template <int D, int G>
 __global__ void __launch_bounds__(D) attn_combine_kernel(AttnP p) {
+    extern __shared__ float cs[];  // [nch] weights e^(m_c - M), then [nch] sums l_c
+    __shared__ float s_max[D / 32];
     const long long h = blockIdx.x, b = blockIdx.y, kh = h / G;
-    const int g = (int)(h % G), d = threadIdx.x;
+    const int g = (int)(h % G), d = threadIdx.x, nch = (int)p.nch;
     const float *rec = p.part + ((b * p.Hkv + kh) * p.nch) * (G * (D + 2)) + g * (D + 2);
     const long long stride = G * (D + 2);
-    float M = -INFINITY;
-    for (long long c = 0; c < p.nch; ++c) M = fmaxf(M, rec[c * stride]);
+    float mx = -INFINITY;
+    for (int c = d; c < nch; c += D) {
+        const float m = rec[c * stride];
+        cs[c] = m;
+        cs[nch + c] = rec[c * stride + 1];
+        mx = fmaxf(mx, m);
+    }
+#pragma unroll
+    for (int mask = 16; mask >= 1; mask >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, mask));
+    if (d % 32 == 0) s_max[d / 32] = mx;
+    __syncthreads();
+    float M = s_max[0];
+#pragma unroll
+    for (int w = 1; w < D / 32; ++w) M = fmaxf(M, s_max[w]);
+    for (int c = d; c < nch; c += D) cs[c] = expf(cs[c] - M);
+    __syncthreads();
     float L = 0.0f, acc = 0.0f;
-    for (long long c = 0; c < p.nch; ++c) {
-        const float f = expf(rec[c * stride] - M);
-        L = fmaf(f, rec[c * stride + 1], L);
+#pragma unroll 16
+    for (int c = 0; c < nch; ++c) {
+        const float f = cs[c];
+        L = fmaf(f, cs[nch + c], L);
         acc = fmaf(f, rec[c * stride + 2 + d], acc);
     }
     const float vs = p.v_scale ? p.v_scale[b * p.Hkv + kh] : 1.0f;
@@ -396,7 +415,8 @@ int run_attn(AttnP p, long long B, cudaStream_t st) {
     attn_split_kernel<D, G, CDT><<<dim3((unsigned)p.nch, (unsigned)p.Hkv, (unsigned)B), AT, smem, st>>>(p);
     rc = check_launch("attn_split_kernel");
     if (rc || p.nch == 1) return rc;
-    attn_combine_kernel<D, G><<<dim3((unsigned)p.H, (unsigned)B), D, 0, st>>>(p);
+    if (p.nch > 6000) return set_error(KAI_GDN_ERR_UNSUPPORTED, "attention_decode: too many splits");
+    attn_combine_kernel<D, G><<<dim3((unsigned)p.H, (unsigned)B), D, 2 * p.nch * sizeof(float), st>>>(p);
     return check_launch("attn_combine_kernel");
 }
 
