@@ -99,6 +99,41 @@ def test_gated_scan(cuda, orc, seq, ch):
         assert validate_pass(s.cpu().numpy(), s_want) and validate_pass(st_d.cpu().numpy(), st_want)
 
 
+# Long chains: more than 256 tiles of 256 rows per chain, a ragged last
+# channel tile, and inputs larger than 64 MiB.
+LONG_CHAINS = [
+    ("cumsum", 65536, 32),
+    ("cumsum", 65537, 32),
+    ("cumdecay", 70000, 40),
+    ("gated", 65537, 33),
+    ("gated", 9000, 1000),
+]
+
+
+@pytest.mark.parametrize("op,seq,ch", LONG_CHAINS)
+def test_scan_long_chains(cuda, orc, op, seq, ch):
+    r = np.random.default_rng(seq + ch)
+    if op == "cumsum":
+        g = (-np.log1p(np.exp(r.standard_normal((seq, ch))))).astype(np.float32)
+        out = cuda.empty((seq, ch), dtype=cuda.float32, device="cuda")
+        ops.cumsum(_t(cuda, g), out)
+        assert rel_l2(out.cpu().numpy(), orc.cumsum(g)) < 1e-5
+    elif op == "cumdecay":
+        a = r.uniform(0.999, 1.001, (seq, ch)).astype(np.float32)  # the product stays in range at 70000 rows
+        out = cuda.empty((seq, ch), dtype=cuda.float32, device="cuda")
+        ops.cumdecay(_t(cuda, a), out)
+        assert kai_close(out.cpu().numpy(), orc.cumdecay(a), 1e-5, 1e-4)
+    else:
+        g = r.uniform(0.5, 0.99, (seq, ch)).astype(np.float32)
+        x = (r.uniform(0, 1, (seq, ch)) - 0.5).astype(np.float32)
+        st = r.uniform(-1, 1, ch).astype(np.float32)
+        s_want, st_want = orc.gated_scan(g, x, st)
+        s = cuda.empty((seq, ch), dtype=cuda.float32, device="cuda")
+        st_d = _t(cuda, st)
+        ops.gated_scan(_t(cuda, g), _t(cuda, x), s, st_d)
+        assert validate_pass(s.cpu().numpy(), s_want) and validate_pass(st_d.cpu().numpy(), st_want)
+
+
 @pytest.mark.parametrize("kind", ["f16", "bf16"])
 def test_gated_scan_narrow_state(cuda, orc, kind):
     seq, ch = 64, 2051
