@@ -344,42 +344,99 @@ __global__ void __launch_bounds__(AT, G == 8 ? 1 : 2) attn_split_kernel(AttnP p)
 }
 
 // Merge the chunks of one (b, query head): o = sum_c e^(m_c - M) acc_c /
-// sum_c e^(m_c - M) l_c (times the int8 value scale), in chunk order.  The
-// chunks' maxima and sums are read in parallel into shared memory first, so
-// the weighted sum's loads are independent of one another.
+// sum_c e^(m_c - M) l_c (times the int8 value scale).  Warp w folds chunks
+// w, w + 8, ... into a running (max, sum, output) of its own, rescaling by
+// e^(m_old - m_new) as the maximum grows, with the records of CU chunks in
+// flight at once; the eight warps' states are merged in warp order at the
+// end.  No step waits on a whole-block quantity before the loads are issued,
+// so a merge of many chunks costs about one round of loads.
 template <int D, int G>
-__global__ void __launch_bounds__(D) attn_combine_kernel(AttnP p) {
-    extern __shared__ float cs[];  // [nch] weights e^(m_c - M), then [nch] sums l_c
-    __shared__ float s_max[D / 32];
+__global__ void __launch_bounds__(256) attn_combine_kernel(AttnP p) {
+    constexpr int NW = 8, J = D / 64, CU = 4;  // J float2 per lane and chunk
+    __shared__ float s_m[NW], s_l[NW], s_acc[NW][D];
     const long long h = blockIdx.x, b = blockIdx.y, kh = h / G;
-    const int g = (int)(h % G), d = threadIdx.x, nch = (int)p.nch;
+    const int g = (int)(h % G), lane = threadIdx.x % 32, w = threadIdx.x / 32, nch = (int)p.nch;
     const float *rec = p.part + ((b * p.Hkv + kh) * p.nch) * (G * (D + 2)) + g * (D + 2);
     const long long stride = G * (D + 2);
-    float mx = -INFINITY;
-    for (int c = d; c < nch; c += D) {
-        const float m = rec[c * stride];
-        cs[c] = m;
-        cs[nch + c] = rec[c * stride + 1];
-        mx = fmaxf(mx, m);
+    float m = -INFINITY, l = 0.0f;
+    float2 acc[J];
+#pragma unroll
+    for (int j = 0; j < J; ++j) acc[j] = make_float2(0.0f, 0.0f);
+    for (int c0 = w; c0 < nch; c0 += NW * CU) {
+        float mc[CU], lc[CU];
+        float2 ac[CU][J];
+#pragma unroll
+        for (int u = 0; u < CU; ++u) {
+            const int c = c0 + u * NW;
+            if (c < nch) {
+                const float *r = rec + c * stride;
+                mc[u] = r[0];
+                lc[u] = r[1];
+#pragma unroll
+                for (int j = 0; j < J; ++j) ac[u][j] = *reinterpret_cast<const float2 *>(r + 2 + 64 * j + 2 * lane);
+            }
+        }
+#pragma unroll
+        for (int u = 0; u < CU; ++u) {
+            if (c0 + u * NW < nch) {  // every chunk holds a token: mc is finite
+                const float mn = fmaxf(m, mc[u]);
+                const float a = expf(m - mn), f = expf(mc[u] - mn);  // a = 0 on the first chunk
+                l = fmaf(lc[u], f, l * a);
+#pragma unroll
+                for (int j = 0; j < J; ++j) {
+                    acc[j].x = fmaf(ac[u][j].x, f, acc[j].x * a);
+                    acc[j].y = fmaf(ac[u][j].y, f, acc[j].y * a);
+                }
+                m = mn;
+            }
+        }
+    }
+    if (lane == 0) {
+        s_m[w] = m;
+        s_l[w] = l;
     }
 #pragma unroll
-    for (int mask = 16; mask >= 1; mask >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, mask));
-    if (d % 32 == 0) s_max[d / 32] = mx;
+    for (int j = 0; j < J; ++j) *reinterpret_cast<float2 *>(&s_acc[w][64 * j + 2 * lane]) = acc[j];
     __syncthreads();
-    float M = s_max[0];
+    const int d = threadIdx.x;
+    if (d >= D) return;
+    float M = s_m[0];
 #pragma unroll
-    for (int w = 1; w < D / 32; ++w) M = fmaxf(M, s_max[w]);
-    for (int c = d; c < nch; c += D) cs[c] = expf(cs[c] - M);
-    __syncthreads();
-    float L = 0.0f, acc = 0.0f;
-#pragma unroll 16
-    for (int c = 0; c < nch; ++c) {
-        const float f = cs[c];
-        L = fmaf(f, cs[nch + c], L);
-        acc = fmaf(f, rec[c * stride + 2 + d], acc);
+    for (int ww = 1; ww < NW; ++ww) M = fmaxf(M, s_m[ww]);
+    float L = 0.0f, o = 0.0f;
+#pragma unroll
+    for (int ww = 0; ww < NW; ++ww) {
+        if (ww < nch) {  // warps without a chunk hold no state
+            const float f = expf(s_m[ww] - M);
+            L = fmaf(s_l[ww], f, L);
+            o = fmaf(s_acc[ww][d], f, o);
+        }
     }
     const float vs = p.v_scale ? p.v_scale[b * p.Hkv + kh] : 1.0f;
-    p.o[(b * p.H + h) * D + d] = acc / L * vs;
+    p.o[(b * p.H + h) * D + d] = o / L * vs;
+}
+
+// Splits per (b, kv head).  The split kernel runs in waves of `slots`
+// resident CTAs, and a CTA's time goes with its tiles, so the launch takes
+// about waves x (tiles per CTA + RAMP), RAMP standing for a CTA's start-up
+// (first loads, final merge) in tiles.  The smallest such cost wins, the
+// fewest splits on a tie; a count just above a multiple of the slots (a
+// nearly empty last wave of full-length CTAs) is what this avoids.
+long long choose_splits(long long pairs, long long tiles, long long slots) {
+    constexpr long long RAMP = 2;
+    const long long max_n = std::min(tiles, std::max(1ll, 4 * ((slots + pairs - 1) / pairs)));
+    long long best = 1, best_cost = -1;
+    for (long long n = 1; n <= max_n; ++n) {
+        const long long per = (tiles + n - 1) / n;
+        const long long nch = (tiles + per - 1) / per;  // splits in whole tiles
+        if (nch != n) continue;
+        const long long cost = ((pairs * nch + slots - 1) / slots) * (per + RAMP);
+        if (best_cost < 0 || cost < best_cost) {
+            best = nch;
+            best_cost = cost;
+        }
+    }
+    return best;
 }
 
 template <int D, int G, int CDT>
@@ -398,10 +455,18 @@ int run_attn(AttnP p, long long B, cudaStream_t st) {
         if (rc) return rc;
         attr_set.fetch_or(bit);
     }
-    // Split the context so that about two CTAs per SM are busy, in whole tiles.
-    const long long pairs = B * p.Hkv, target = 2ll * sm_count();
-    long long tiles = (p.ctx + Geo::TT - 1) / Geo::TT;
-    long long per = std::max(1ll, (pairs * tiles + target - 1) / target);
+    static std::atomic<int> per_sm[64];  // resident split CTAs per SM, per device (0: not asked yet)
+    int nb = per_sm[dev & 63].load();
+    if (nb == 0) {
+        rc = check_cuda(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&nb, attn_split_kernel<D, G, CDT>, AT, smem),
+                        "attention_decode: occupancy");
+        if (rc) return rc;
+        nb = std::max(nb, 1);
+        per_sm[dev & 63].store(nb);
+    }
+    const long long pairs = B * p.Hkv, tiles = (p.ctx + Geo::TT - 1) / Geo::TT;
+    const long long nsplit = choose_splits(pairs, tiles, (long long)nb * sm_count());
+    const long long per = (tiles + nsplit - 1) / nsplit;
     p.split = per * Geo::TT;
     p.nch = (p.ctx + p.split - 1) / p.split;
     if (p.nch > 1) {
@@ -415,8 +480,7 @@ int run_attn(AttnP p, long long B, cudaStream_t st) {
     attn_split_kernel<D, G, CDT><<<dim3((unsigned)p.nch, (unsigned)p.Hkv, (unsigned)B), AT, smem, st>>>(p);
     rc = check_launch("attn_split_kernel");
     if (rc || p.nch == 1) return rc;
-    if (p.nch > 6000) return set_error(KAI_GDN_ERR_UNSUPPORTED, "attention_decode: too many splits");
-    attn_combine_kernel<D, G><<<dim3((unsigned)p.H, (unsigned)B), D, 2 * p.nch * sizeof(float), st>>>(p);
+    attn_combine_kernel<D, G><<<dim3((unsigned)p.H, (unsigned)B), 256, 0, st>>>(p);
     return check_launch("attn_combine_kernel");
 }
 
