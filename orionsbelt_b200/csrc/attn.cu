@@ -22,6 +22,8 @@
 #include <atomic>
 
 #include "gdn_internal.cuh"
+#include "tma.cuh"
+#include "umma.cuh"
 
 namespace gdn {
 namespace {
@@ -416,6 +418,369 @@ __global__ void __launch_bounds__(256) attn_combine_kernel(AttnP p) {
     p.o[(b * p.H + h) * D + d] = o / L * vs;
 }
 
+// ------------------------------------------ tensor-core split kernel (bf16)
+// A bf16 cache takes both products through tcgen05, per tile of TC_TT = 64
+// tokens of one (b, kv head):
+//   S  = K Qs^T     M = 64 tokens, N = NQ, K = D.  A: the K tile; B: the G
+//                   query heads split into three bf16 terms (hi + mid + lo =
+//                   the fp32 q to 24 bits), rows t*G + h, zero rows after.
+//   O^T = V^T Ps^T  M = 128 head dims (D/128 MMAs), N = NQ, K = 64 tokens.
+//                   A: the V tile; B: the softmax weights in three terms.
+// Every product is exact in fp32 and summed in fp32: scores and outputs keep
+// fp32 accuracy.  K and V tiles arrive by TMA in the 128-byte-swizzle layout
+// of tma.cuh: features 64j .. 64j+63 in an 8 KB block at 8192j, token row t
+// at t*128 with its 16-byte chunks permuted by chunk ^= t % 8.  The S MMA
+// reads the K tile as K-major (a K step of 16 features: +32 bytes inside a
+// block), the O MMA the V tile as MN-major (next 64 features: the next block,
+// LBO 8192; next 8 tokens: SBO 1024).  A 3-stage ring; a token row of 128-byte
+// pieces per box keeps the copy engine's requests large.
+//
+// Warp specialised.  Warp 8 issues, per tile j: S(j+1) once its tile has
+// landed, the load of tile j+2 into the stage O(j-1) has released, then O(j)
+// once the weights of tile j are written.  Warps 0-7, per tile j: wait for
+// S(j); warps 0-3 (rows 16w .. 16w+15 of the M = 64 accumulator, lanes
+// 0-15) turn it into scores and the tile maximum; after one barrier of the
+// eight warps every thread knows the running maximum; every thread folds
+// O(j-2) from TMEM into its registers (one head dim, all G heads; issued two
+// tiles earlier, so it has long finished); the softmax threads write the
+// weights of tile j and all arrive on the weights-ready barrier.  S, O and
+// the weights are double-buffered.  Waits are bounded: a timeout sets the
+// library's error word and the CTA stops, frees its TMEM and exits.
+constexpr int TC_TT = 64;
+constexpr int TC_AT = 288;  // 8 softmax / fold warps + 1 issuing warp
+template <int D, int G> struct TcAttnGeo {
+    static constexpr int NQ = (3 * G + 15) / 16 * 16;  // MMA N: three terms of G heads, padded
+    static constexpr int KT = TC_TT * D * 2;            // bytes of a K (or V) tile
+    static constexpr int STAGE = 2 * KT;
+    static constexpr int NST = 3;
+    static constexpr int QOP = NQ * D * 2;              // Qs, K-major NQ x D
+    static constexpr int POP = NQ * TC_TT * 2;          // Ps, K-major NQ x 64
+    static constexpr int S_COL = 0, O_COL = 2 * NQ;     // TMEM: S buffers, then O buffers
+    static constexpr int OCOLS = (D / 128) * NQ;        // one O buffer
+    static constexpr int NCOL = O_COL + 2 * OCOLS;
+    static constexpr uint32_t TMEM_COLS = NCOL <= 32 ? 32 : NCOL <= 64 ? 64 : NCOL <= 128 ? 128 : 256;
+    static constexpr size_t SMEM = (size_t)NST * STAGE + QOP + 2 * (size_t)POP + 1024;
+    static_assert(NCOL <= 256 && SMEM <= 227 * 1024, "fits one SM");
+};
+
+__device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
+    const __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
+    return *reinterpret_cast<const uint32_t *>(&v);
+}
+// The three bf16 terms of x (hi + mid + lo, 24 significant bits).
+__device__ __forceinline__ void split3(float x, float &hi, float &mid, float &lo) {
+    hi = __bfloat162float(__float2bfloat16_rn(x));
+    const float r = x - hi;
+    mid = __bfloat162float(__float2bfloat16_rn(r));
+    lo = r - mid;
+}
+// Barrier 1 over the 256 threads of warps 0-7, OR-reducing a flag.
+__device__ __forceinline__ bool compute_sync_or(bool v) {
+    uint32_t r;
+    asm volatile(
+        "{\n\t.reg .pred p, q;\n\t"
+        "setp.ne.u32 p, %1, 0;\n\t"
+        "bar.red.or.pred q, 1, 256, p;\n\t"
+        "selp.u32 %0, 1, 0, q;\n\t}\n"
+        : "=r"(r)
+        : "r"((uint32_t)v)
+        : "memory");
+    return r != 0;
+}
+__device__ __forceinline__ void mbar_arrive(uint64_t *bar) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(umma::smem_addr(bar)) : "memory");
+}
+
+template <int D, int G>
+__global__ void __launch_bounds__(TC_AT, 1)
+    attn_tc_kernel(AttnP p, const __grid_constant__ CUtensorMap kmap, const __grid_constant__ CUtensorMap vmap,
+                   int *err) {
+    using namespace umma;
+    using Gm = TcAttnGeo<D, G>;
+    using T = __nv_bfloat16;
+    constexpr int TT = TC_TT, NQ = Gm::NQ, NH = D / 128, NST = Gm::NST;
+    extern __shared__ unsigned char dsm_raw[];
+    unsigned char *dsm = dsm_raw + ((1024u - (smem_addr(dsm_raw) & 1023u)) & 1023u);
+    unsigned char *ring = dsm;                            // [NST][K tile | V tile]
+    unsigned char *qop = ring + NST * Gm::STAGE;          // Qs
+    unsigned char *pop = qop + Gm::QOP;                   // [2] Ps
+    __shared__ uint64_t full[NST], bar_s[2], bar_o[2], pready[2];
+    __shared__ uint32_t tmem_slot;
+    __shared__ float s_red[2][4][G];
+
+    const int t = threadIdx.x, lane = t % 32, w = t / 32;
+    const long long c = blockIdx.x, kh = blockIdx.y, b = blockIdx.z;
+    const long long s0 = c * p.split, s1 = min(p.ctx, s0 + p.split);
+    const int ntile = (int)((s1 - s0 + TT - 1) / TT);
+    const long long kvd = p.Hkv * D;
+    const size_t head0 = ((size_t)b * p.max_ctx * p.Hkv + kh) * D;
+    const bool has_new = p.pos >= s0 && p.pos < s1;
+    const float *knew = p.k_new + (b * p.Hkv + kh) * D, *vnew = p.v_new + (b * p.Hkv + kh) * D;
+
+    if (w < 8) {
+        if (has_new) {  // the new token goes to the cache; the issuing warp patches it into its tile
+            T *kw = static_cast<T *>(p.k_cache) + head0 + p.pos * kvd;
+            T *vw = static_cast<T *>(p.v_cache) + head0 + p.pos * kvd;
+            for (int d = t; d < D; d += 256) {
+                kw[d] = __float2bfloat16_rn(knew[d]);
+                vw[d] = __float2bfloat16_rn(vnew[d]);
+            }
+        }
+        // Qs (rows t*G + h; rows >= 3G zero) and zeroed Ps buffers
+        const float *qg = p.q + (b * p.H + kh * G) * D;
+        for (int i = t; i < NQ * (D / 2); i += 256) {
+            const int n = i / (D / 2), k = 2 * (i % (D / 2));
+            float v0 = 0.0f, v1 = 0.0f;
+            if (n < 3 * G) {
+                const int term = n / G, h = n % G;
+                float hi, mid, lo;
+                split3(qg[h * D + k], hi, mid, lo);
+                v0 = term == 0 ? hi : term == 1 ? mid : lo;
+                split3(qg[h * D + k + 1], hi, mid, lo);
+                v1 = term == 0 ? hi : term == 1 ? mid : lo;
+            }
+            *reinterpret_cast<uint32_t *>(qop + kmaj16(n, k, D)) = pack_bf16x2(v0, v1);
+        }
+        for (int i = t; i < 2 * Gm::POP / 16; i += 256) reinterpret_cast<uint4 *>(pop)[i] = make_uint4(0, 0, 0, 0);
+        fence_smem_to_async();
+    } else {
+        if (lane == 0) {
+            for (int s = 0; s < NST; ++s) mbar_init(&full[s], 1);
+            for (int s = 0; s < 2; ++s) {
+                mbar_init(&bar_s[s], 1);
+                mbar_init(&bar_o[s], 1);
+                mbar_init(&pready[s], 256);
+            }
+            tma::prefetch_map(&kmap);
+            tma::prefetch_map(&vmap);
+        }
+        tmem_alloc(&tmem_slot, Gm::TMEM_COLS);
+    }
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    fence_before_sync();
+    __syncthreads();
+    fence_after_sync();
+    const uint32_t tmem = tmem_slot;
+    bool bad = false;
+
+    if (w == 8) {
+        // ------------------------------------------------------ issuing warp
+        const uint32_t id_s = idesc(64, NQ, BF16, false, false), id_o = idesc(128, NQ, BF16, true, false);
+        int nload = 0, nlanded = 0;  // tiles whose loads were issued / seen landed
+        auto load = [&](int tile) {  // elected lane
+            const int st = tile % NST;
+            unsigned char *kt = ring + st * Gm::STAGE;
+            mbar_arrive_expect_tx(&full[st], 2 * Gm::KT);
+            const int t0 = (int)(s0 + (long long)tile * TT);
+            tma::load_chunk_sw128(kt, &kmap, t0, (int)kh, (int)b, &full[st], D / 64);
+            tma::load_chunk_sw128(kt + Gm::KT, &vmap, t0, (int)kh, (int)b, &full[st], D / 64);
+        };
+        // Wait for tile `tile`, patch the new token in, issue its S MMAs.
+        auto issue_s = [&](int tile) -> bool {
+            const int st = tile % NST;
+            if (!__all_sync(0xffffffffu, mbar_wait(&full[st], (tile / NST) & 1, err))) return false;
+            nlanded = tile + 1;
+            unsigned char *kt = ring + st * Gm::STAGE;
+            const long long tb = s0 + (long long)tile * TT;
+            if (has_new && p.pos >= tb && p.pos < tb + TT) {
+                const int r = (int)(p.pos - tb);
+                for (int d = lane; d < D; d += 32) {
+                    const uint32_t off =
+                        (uint32_t)((d >> 6) * 8192 + r * 128 + ((((d & 63) >> 3) ^ (r & 7)) << 4) + (d & 7) * 2);
+                    *reinterpret_cast<T *>(kt + off) = __float2bfloat16_rn(knew[d]);
+                    *reinterpret_cast<T *>(kt + Gm::KT + off) = __float2bfloat16_rn(vnew[d]);
+                }
+                fence_smem_to_async();
+                __syncwarp();
+            }
+            if (elect_one()) {
+                const uint32_t ka = smem_addr(kt);
+#pragma unroll
+                for (int ks = 0; ks < D / 16; ++ks)
+                    mma_f16(tmem + Gm::S_COL + (tile & 1) * NQ, smem_desc_sw128(ka + (ks / 4) * 8192 + (ks % 4) * 32, 16, 1024),
+                            desc_kmaj16(qop, D, ks), id_s, ks > 0);
+                commit(&bar_s[tile & 1]);
+            }
+            __syncwarp();
+            return true;
+        };
+        if (elect_one())
+            for (int s = 0; s < NST && s < ntile; ++s) load(s);
+        __syncwarp();
+        nload = min(NST, ntile);
+        bad = !issue_s(0);
+        for (int j = 0; j < ntile && !bad; ++j) {
+            if (j + 1 < ntile && !issue_s(j + 1)) {
+                bad = true;
+                break;
+            }
+            if (j >= 1 && j + 2 < ntile) {  // O(j-1) has released its stage: tile j+2 goes there
+                if (!__all_sync(0xffffffffu, mbar_wait(&bar_o[(j - 1) & 1], ((j - 1) >> 1) & 1, err))) {
+                    bad = true;
+                    break;
+                }
+                if (elect_one()) load(j + 2);
+                __syncwarp();
+                nload = j + 3;
+            }
+            if (!__all_sync(0xffffffffu, mbar_wait(&pready[j & 1], (j >> 1) & 1, err))) {
+                bad = true;
+                break;
+            }
+            fence_after_sync();
+            if (elect_one()) {
+                const unsigned char *pb = pop + (j & 1) * Gm::POP;
+                const uint32_t va = smem_addr(ring + (j % NST) * Gm::STAGE + Gm::KT);
+#pragma unroll
+                for (int h2 = 0; h2 < NH; ++h2)
+#pragma unroll
+                    for (int ks = 0; ks < TT / 16; ++ks)
+                        mma_f16(tmem + Gm::O_COL + (j & 1) * Gm::OCOLS + h2 * NQ,
+                                smem_desc_sw128(va + h2 * 16384 + ks * 2048, 8192, 1024), desc_kmaj16(pb, TT, ks), id_o,
+                                ks > 0);
+                commit(&bar_o[j & 1]);
+            }
+            __syncwarp();
+        }
+        // After a timeout: let the loads still in flight land before the CTA exits.
+        for (int k = nlanded; k < nload; ++k) mbar_wait(&full[k % NST], (k / NST) & 1, nullptr, 1u << 16);
+    } else {
+        // ---------------------------------------------- softmax / fold warps
+        float m_run[G], a_even[G], a_odd[G], l_part[G], acc[G];  // a_*: rescale factors of even / odd tiles
+#pragma unroll
+        for (int h = 0; h < G; ++h) {
+            m_run[h] = -INFINITY;
+            a_even[h] = a_odd[h] = 0.0f;
+            l_part[h] = 0.0f;
+            acc[h] = 0.0f;
+        }
+        const int hm = w / 4;  // O half of this thread: head dim 128 hm + 32 (w % 4) + lane
+        const bool o_warp = hm < NH;
+        const int srow = 16 * w + lane;  // softmax row (token) of warps 0-3, lanes 0-15
+        const bool s_thread = w < 4 && lane < 16;
+        // fold O(k) (TMEM buffer k & 1) with its factor: acc = acc * a_k + O_k
+        auto fold = [&](int k) -> bool {
+            const bool ok = __all_sync(0xffffffffu, mbar_wait(&bar_o[k & 1], (k >> 1) & 1, err));
+            fence_after_sync();
+            if (!ok) return false;
+            if (o_warp) {
+                float ov[NQ];
+#pragma unroll
+                for (int q = 0; q < NQ; q += 16)
+                    tmem_ld16(taddr(tmem, 32 * (w % 4), Gm::O_COL + (k & 1) * Gm::OCOLS + hm * NQ + q),
+                              *reinterpret_cast<float(*)[16]>(ov + q));
+                tmem_wait_ld();
+#pragma unroll
+                for (int q = 0; q < NQ; q += 16) reg_fence16(ov + q);
+#pragma unroll
+                for (int h = 0; h < G; ++h)
+                    acc[h] = fmaf(acc[h], (k & 1) ? a_odd[h] : a_even[h], (ov[h] + ov[G + h]) + ov[2 * G + h]);
+            }
+            return true;
+        };
+        for (int j = 0; j < ntile; ++j) {
+            const long long tb = s0 + (long long)j * TT;
+            if (!mbar_wait(&bar_s[j & 1], (j >> 1) & 1, err)) bad = true;
+            fence_after_sync();
+            bad = __any_sync(0xffffffffu, bad);  // TMEM loads are warp-wide
+            const bool valid = s_thread && tb + srow < s1;
+            float sc[G];
+            if (w < 4 && !bad) {
+                float sv[NQ];
+#pragma unroll
+                for (int q = 0; q < NQ; q += 16)
+                    tmem_ld16(taddr(tmem, 32 * w, Gm::S_COL + (j & 1) * NQ + q),
+                              *reinterpret_cast<float(*)[16]>(sv + q));
+                tmem_wait_ld();
+#pragma unroll
+                for (int q = 0; q < NQ; q += 16) reg_fence16(sv + q);
+#pragma unroll
+                for (int h = 0; h < G; ++h) {
+                    sc[h] = valid ? ((sv[h] + sv[G + h]) + sv[2 * G + h]) * p.scale : -INFINITY;
+                    float mx = sc[h];
+#pragma unroll
+                    for (int mask = 16; mask >= 1; mask >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, mask));
+                    if (lane == 0) s_red[j & 1][w][h] = mx;
+                }
+            }
+            if (compute_sync_or(bad)) {
+                bad = true;
+                break;
+            }
+            float a[G];
+#pragma unroll
+            for (int h = 0; h < G; ++h) {
+                const float mt = fmaxf(fmaxf(s_red[j & 1][0][h], s_red[j & 1][1][h]),
+                                       fmaxf(s_red[j & 1][2][h], s_red[j & 1][3][h]));
+                const float mn = fmaxf(m_run[h], mt);  // finite: every tile holds a token
+                a[h] = expf(m_run[h] - mn);            // 0 on the first tile
+                m_run[h] = mn;
+            }
+            if (j >= 2 && !fold(j - 2)) bad = true;  // also frees the weights buffer j & 1
+#pragma unroll
+            for (int h = 0; h < G; ++h) {
+                if (j & 1)
+                    a_odd[h] = a[h];
+                else
+                    a_even[h] = a[h];
+            }
+            if (s_thread && !bad) {
+                unsigned char *pb = pop + (j & 1) * Gm::POP;
+#pragma unroll
+                for (int h = 0; h < G; ++h) {
+                    const float e = valid ? expf(sc[h] - m_run[h]) : 0.0f;
+                    l_part[h] = fmaf(l_part[h], a[h], e);
+                    float hi, mid, lo;
+                    split3(e, hi, mid, lo);
+                    *reinterpret_cast<T *>(pb + kmaj16(h, srow, TT)) = __float2bfloat16_rn(hi);
+                    *reinterpret_cast<T *>(pb + kmaj16(G + h, srow, TT)) = __float2bfloat16_rn(mid);
+                    *reinterpret_cast<T *>(pb + kmaj16(2 * G + h, srow, TT)) = __float2bfloat16_rn(lo);
+                }
+            }
+            fence_smem_to_async();
+            fence_before_sync();
+            mbar_arrive(&pready[j & 1]);
+        }
+        if (!bad) {
+            for (int k = ntile >= 2 ? ntile - 2 : 0; k < ntile; ++k)
+                if (!fold(k)) bad = true;
+        }
+        bad = compute_sync_or(bad);
+        if (!bad) {
+            if (w < 4) {  // sums of the softmax weights
+#pragma unroll
+                for (int h = 0; h < G; ++h) {
+                    float l = l_part[h];
+#pragma unroll
+                    for (int mask = 16; mask >= 1; mask >>= 1) l += __shfl_xor_sync(0xffffffffu, l, mask);
+                    if (lane == 0) s_red[0][w][h] = l;
+                }
+            }
+            compute_sync_or(false);
+            if (o_warp) {
+                const int d = 128 * hm + 32 * (w % 4) + lane;
+#pragma unroll
+                for (int h = 0; h < G; ++h) {
+                    const float L = (s_red[0][0][h] + s_red[0][1][h]) + (s_red[0][2][h] + s_red[0][3][h]);
+                    if (p.nch == 1) {
+                        p.o[((b * p.H) + kh * G + h) * D + d] = acc[h] / L;
+                    } else {
+                        float *rec = p.part + ((b * p.Hkv + kh) * p.nch + c) * (G * (D + 2)) + h * (D + 2);
+                        rec[2 + d] = acc[h];
+                        if (d == 0) {
+                            rec[0] = m_run[h];
+                            rec[1] = L;
+                        }
+                    }
+                }
+            }
+        }
+    }
+    fence_before_sync();
+    __syncthreads();
+    if (w == 8) tmem_dealloc(tmem, Gm::TMEM_COLS);
+}
+
 // Splits per (b, kv head).  The split kernel runs in waves of `slots`
 // resident CTAs, and a CTA's time goes with its tiles, so the launch takes
 // about waves x (tiles per CTA + RAMP), RAMP standing for a CTA's start-up
@@ -439,18 +804,26 @@ long long choose_splits(long long pairs, long long tiles, long long slots) {
     return best;
 }
 
+// bf16 caches take the tensor-core split kernel, fp32 and int8 caches the
+// CUDA-core one.
 template <int D, int G, int CDT>
 int run_attn(AttnP p, long long B, cudaStream_t st) {
+    constexpr bool TC = CDT == KAI_GDN_BF16;
     using Geo = AttnGeo<D, CDT>;
-    const size_t smem = 2ull * NSTAGE * Geo::TT * Geo::ROW;
+    constexpr int TT = TC ? TC_TT : Geo::TT;
+    const size_t smem = TC ? TcAttnGeo<D, G>::SMEM : 2ull * NSTAGE * Geo::TT * Geo::ROW;
+    const void *kern;
+    if constexpr (TC)
+        kern = reinterpret_cast<const void *>(attn_tc_kernel<D, G>);
+    else
+        kern = reinterpret_cast<const void *>(attn_split_kernel<D, G, CDT>);
     int dev = 0;
     int rc = check_cuda(cudaGetDevice(&dev), "attention_decode: cudaGetDevice");
     if (rc) return rc;
     static std::atomic<unsigned long long> attr_set{0};  // per device
     const unsigned long long bit = 1ull << (dev & 63);
     if (!(attr_set.load() & bit)) {
-        rc = check_cuda(cudaFuncSetAttribute(attn_split_kernel<D, G, CDT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                             (int)smem),
+        rc = check_cuda(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem),
                         "attention_decode: smem attribute");
         if (rc) return rc;
         attr_set.fetch_or(bit);
@@ -458,16 +831,16 @@ int run_attn(AttnP p, long long B, cudaStream_t st) {
     static std::atomic<int> per_sm[64];  // resident split CTAs per SM, per device (0: not asked yet)
     int nb = per_sm[dev & 63].load();
     if (nb == 0) {
-        rc = check_cuda(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&nb, attn_split_kernel<D, G, CDT>, AT, smem),
+        rc = check_cuda(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&nb, kern, TC ? TC_AT : AT, smem),
                         "attention_decode: occupancy");
         if (rc) return rc;
         nb = std::max(nb, 1);
         per_sm[dev & 63].store(nb);
     }
-    const long long pairs = B * p.Hkv, tiles = (p.ctx + Geo::TT - 1) / Geo::TT;
+    const long long pairs = B * p.Hkv, tiles = (p.ctx + TT - 1) / TT;
     const long long nsplit = choose_splits(pairs, tiles, (long long)nb * sm_count());
     const long long per = (tiles + nsplit - 1) / nsplit;
-    p.split = per * Geo::TT;
+    p.split = per * TT;
     p.nch = (p.ctx + p.split - 1) / p.split;
     if (p.nch > 1) {
         void *scr = nullptr;
@@ -477,8 +850,19 @@ int run_attn(AttnP p, long long B, cudaStream_t st) {
     }
     if (p.nch > 0x7fffffffll || p.Hkv > 65535 || B > 65535)
         return set_error(KAI_GDN_ERR_UNSUPPORTED, "attention_decode: shape too large");
-    attn_split_kernel<D, G, CDT><<<dim3((unsigned)p.nch, (unsigned)p.Hkv, (unsigned)B), AT, smem, st>>>(p);
-    rc = check_launch("attn_split_kernel");
+    const dim3 grid((unsigned)p.nch, (unsigned)p.Hkv, (unsigned)B);
+    if constexpr (TC) {
+        int *err = nullptr;
+        if ((rc = device_error_word(&err))) return rc;
+        CUtensorMap kmap, vmap;
+        if (tma::make_chunk_map(&kmap, p.k_cache, true, (uint64_t)B, (uint64_t)p.max_ctx, (uint64_t)p.Hkv, D, true) ||
+            tma::make_chunk_map(&vmap, p.v_cache, true, (uint64_t)B, (uint64_t)p.max_ctx, (uint64_t)p.Hkv, D, true))
+            return set_error(KAI_GDN_ERR_CUDA, "attention_decode: tensor map encoding failed");
+        attn_tc_kernel<D, G><<<grid, TC_AT, smem, st>>>(p, kmap, vmap, err);
+    } else {
+        attn_split_kernel<D, G, CDT><<<grid, AT, smem, st>>>(p);
+    }
+    rc = check_launch("attention split kernel");
     if (rc || p.nch == 1) return rc;
     attn_combine_kernel<D, G><<<dim3((unsigned)p.H, (unsigned)B), 256, 0, st>>>(p);
     return check_launch("attn_combine_kernel");

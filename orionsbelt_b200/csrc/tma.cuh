@@ -1,8 +1,9 @@
 // tma.cuh -- tensor-map (TMA) loads of one chunk of a [B][T][H][D] 16-bit
 // tensor (D = 128) into shared memory in a layout the tcgen05 MMAs read.
 //
-// A chunk tile holds rows t0 .. t0+63 (tokens) x all 128 features of one
-// (batch, head), in one of two layouts:
+// A chunk tile holds rows t0 .. t0+63 (tokens) x all D features of one
+// (batch, head) (D = 128; the swizzled form also D = 256), in one of two
+// layouts:
 //
 // Core-matrix (no swizzle), one box.  The map describes the tensor as five
 // dimensions, innermost first: d%8 (contiguous), t (stride H*D), d/8 (stride
@@ -90,14 +91,13 @@ __device__ __forceinline__ void load_chunk(void *dst, const CUtensorMap *map, in
         : "memory");
 }
 
-// 128-byte swizzle: features 64j .. 64j+63 (j = 0, 1) of tokens t0 .. t0+63
-// into `dst` + 8192*j (1024-byte aligned).
+// 128-byte swizzle: features 64j .. 64j+63 (j < nbox = D/64) of tokens
+// t0 .. t0+63 into `dst` + 8192*j (1024-byte aligned).
 __device__ __forceinline__ void load_chunk_sw128(void *dst, const CUtensorMap *map, int t0, int h, int b,
-                                                 uint64_t *bar) {
+                                                 uint64_t *bar, int nbox = 2) {
     const uint32_t d = static_cast<uint32_t>(__cvta_generic_to_shared(dst));
     const uint32_t m = static_cast<uint32_t>(__cvta_generic_to_shared(bar));
-#pragma unroll
-    for (int j = 0; j < 2; ++j)
+    for (int j = 0; j < nbox; ++j)
         asm volatile(
             "cp.async.bulk.tensor.4d.shared::cluster.global.tile.mbarrier::complete_tx::bytes "
             "[%0], [%1, {%2, %3, %4, %5}], [%6];" ::"r"(d + 8192u * j),
