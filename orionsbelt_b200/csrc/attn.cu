@@ -419,26 +419,30 @@ __global__ void __launch_bounds__(256) attn_combine_kernel(AttnP p) {
 }
 
 // ------------------------------------------ tensor-core split kernel (bf16)
-// A bf16 cache takes both products through tcgen05, per tile of TC_TT = 64
+// A bf16 cache takes both products through tcgen05, per tile of TC_TT = 48
 // tokens of one (b, kv head):
-//   S  = K Qs^T     M = 64 tokens, N = NQ, K = D.  A: the K tile; B: the G
+//   S  = K Qs^T     M = 64 rows (the 48 tokens; rows 48-63 read the next
+//                   block's bytes and are masked), N = NQ, K = D.  A: the K
+//                   tile; B: the G
 //                   query heads split into three bf16 terms (hi + mid + lo =
 //                   the fp32 q to 24 bits), rows t*G + h, zero rows after.
-//   O^T = V^T Ps^T  M = 128 head dims (D/128 MMAs), N = NQ, K = 64 tokens.
+//   O^T = V^T Ps^T  M = 128 head dims (D/128 MMAs), N = NQ, K = 48 tokens.
 //                   A: the V tile; B: the softmax weights in three terms.
 // Every product is exact in fp32 and summed in fp32: scores and outputs keep
 // fp32 accuracy.  K and V tiles arrive by TMA in the 128-byte-swizzle layout
-// of tma.cuh: features 64j .. 64j+63 in an 8 KB block at 8192j, token row t
+// of tma.cuh: features 64j .. 64j+63 in a 6 KB block at 6144j, token row t
 // at t*128 with its 16-byte chunks permuted by chunk ^= t % 8.  The S MMA
 // reads the K tile as K-major (a K step of 16 features: +32 bytes inside a
 // block), the O MMA the V tile as MN-major (next 64 features: the next block,
-// LBO 8192; next 8 tokens: SBO 1024).  A 3-stage ring; a token row of 128-byte
-// pieces per box keeps the copy engine's requests large.
+// LBO 6144; next 8 tokens: SBO 1024).  A 4-stage ring; 128-byte rows per box
+// keep the copy engine's requests large (16-byte rows ran at half the rate).
+// Measured at B = 16 over 32k tokens: 48-token tiles in 4 stages beat 64 in
+// 3 (381 vs 420 us) and 32 in 6 (523 us).
 //
 // Warp specialised.  Warp 8 issues, per tile j: S(j+1) once its tile has
-// landed, the load of tile j+2 into the stage O(j-1) has released, then O(j)
+// landed, the load of tile j+3 into the stage O(j-1) has released, then O(j)
 // once the weights of tile j are written.  Warps 0-7, per tile j: wait for
-// S(j); warps 0-3 (rows 16w .. 16w+15 of the M = 64 accumulator, lanes
+// S(j); warps 0-2 (rows 16w .. 16w+15 of the M = 64 accumulator, lanes
 // 0-15) turn it into scores and the tile maximum; after one barrier of the
 // eight warps every thread knows the running maximum; every thread folds
 // O(j-2) from TMEM into its registers (one head dim, all G heads; issued two
@@ -446,15 +450,16 @@ __global__ void __launch_bounds__(256) attn_combine_kernel(AttnP p) {
 // weights of tile j and all arrive on the weights-ready barrier.  S, O and
 // the weights are double-buffered.  Waits are bounded: a timeout sets the
 // library's error word and the CTA stops, frees its TMEM and exits.
-constexpr int TC_TT = 64;
+constexpr int TC_TT = 48;
 constexpr int TC_AT = 288;  // 8 softmax / fold warps + 1 issuing warp
 template <int D, int G> struct TcAttnGeo {
     static constexpr int NQ = (3 * G + 15) / 16 * 16;  // MMA N: three terms of G heads, padded
+    static constexpr int BOX = TC_TT * 128;             // bytes of one 64-feature box
     static constexpr int KT = TC_TT * D * 2;            // bytes of a K (or V) tile
     static constexpr int STAGE = 2 * KT;
-    static constexpr int NST = 3;
+    static constexpr int NST = 4;
     static constexpr int QOP = NQ * D * 2;              // Qs, K-major NQ x D
-    static constexpr int POP = NQ * TC_TT * 2;          // Ps, K-major NQ x 64
+    static constexpr int POP = NQ * TC_TT * 2;          // Ps, K-major NQ x TC_TT
     static constexpr int S_COL = 0, O_COL = 2 * NQ;     // TMEM: S buffers, then O buffers
     static constexpr int OCOLS = (D / 128) * NQ;        // one O buffer
     static constexpr int NCOL = O_COL + 2 * OCOLS;
@@ -551,9 +556,17 @@ __global__ void __launch_bounds__(TC_AT, 1)
                 mbar_init(&bar_o[s], 1);
                 mbar_init(&pready[s], 256);
             }
-            tma::prefetch_map(&kmap);
-            tma::prefetch_map(&vmap);
+            asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+            // the first tiles load while the other warps build the query operand
+            for (int s = 0; s < NST && s < ntile; ++s) {
+                mbar_arrive_expect_tx(&full[s], 2 * Gm::KT);
+                const int t0 = (int)(s0 + (long long)s * TT);
+                tma::load_chunk_sw128(ring + s * Gm::STAGE, &kmap, t0, (int)kh, (int)b, &full[s], D / 64, Gm::BOX);
+                tma::load_chunk_sw128(ring + s * Gm::STAGE + Gm::KT, &vmap, t0, (int)kh, (int)b, &full[s], D / 64,
+                                      Gm::BOX);
+            }
         }
+        __syncwarp();
         tmem_alloc(&tmem_slot, Gm::TMEM_COLS);
     }
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
@@ -572,8 +585,8 @@ __global__ void __launch_bounds__(TC_AT, 1)
             unsigned char *kt = ring + st * Gm::STAGE;
             mbar_arrive_expect_tx(&full[st], 2 * Gm::KT);
             const int t0 = (int)(s0 + (long long)tile * TT);
-            tma::load_chunk_sw128(kt, &kmap, t0, (int)kh, (int)b, &full[st], D / 64);
-            tma::load_chunk_sw128(kt + Gm::KT, &vmap, t0, (int)kh, (int)b, &full[st], D / 64);
+            tma::load_chunk_sw128(kt, &kmap, t0, (int)kh, (int)b, &full[st], D / 64, Gm::BOX);
+            tma::load_chunk_sw128(kt + Gm::KT, &vmap, t0, (int)kh, (int)b, &full[st], D / 64, Gm::BOX);
         };
         // Wait for tile `tile`, patch the new token in, issue its S MMAs.
         auto issue_s = [&](int tile) -> bool {
@@ -586,7 +599,7 @@ __global__ void __launch_bounds__(TC_AT, 1)
                 const int r = (int)(p.pos - tb);
                 for (int d = lane; d < D; d += 32) {
                     const uint32_t off =
-                        (uint32_t)((d >> 6) * 8192 + r * 128 + ((((d & 63) >> 3) ^ (r & 7)) << 4) + (d & 7) * 2);
+                        (uint32_t)((d >> 6) * Gm::BOX + r * 128 + ((((d & 63) >> 3) ^ (r & 7)) << 4) + (d & 7) * 2);
                     *reinterpret_cast<T *>(kt + off) = __float2bfloat16_rn(knew[d]);
                     *reinterpret_cast<T *>(kt + Gm::KT + off) = __float2bfloat16_rn(vnew[d]);
                 }
@@ -597,31 +610,28 @@ __global__ void __launch_bounds__(TC_AT, 1)
                 const uint32_t ka = smem_addr(kt);
 #pragma unroll
                 for (int ks = 0; ks < D / 16; ++ks)
-                    mma_f16(tmem + Gm::S_COL + (tile & 1) * NQ, smem_desc_sw128(ka + (ks / 4) * 8192 + (ks % 4) * 32, 16, 1024),
+                    mma_f16(tmem + Gm::S_COL + (tile & 1) * NQ, smem_desc_sw128(ka + (ks / 4) * Gm::BOX + (ks % 4) * 32, 16, 1024),
                             desc_kmaj16(qop, D, ks), id_s, ks > 0);
                 commit(&bar_s[tile & 1]);
             }
             __syncwarp();
             return true;
         };
-        if (elect_one())
-            for (int s = 0; s < NST && s < ntile; ++s) load(s);
-        __syncwarp();
-        nload = min(NST, ntile);
+        nload = min(NST, ntile);  // issued before the set-up barrier
         bad = !issue_s(0);
         for (int j = 0; j < ntile && !bad; ++j) {
             if (j + 1 < ntile && !issue_s(j + 1)) {
                 bad = true;
                 break;
             }
-            if (j >= 1 && j + 2 < ntile) {  // O(j-1) has released its stage: tile j+2 goes there
+            if (j >= 1 && j + NST - 1 < ntile) {  // O(j-1) has released its stage: tile j+NST-1 goes there
                 if (!__all_sync(0xffffffffu, mbar_wait(&bar_o[(j - 1) & 1], ((j - 1) >> 1) & 1, err))) {
                     bad = true;
                     break;
                 }
-                if (elect_one()) load(j + 2);
+                if (elect_one()) load(j + NST - 1);
                 __syncwarp();
-                nload = j + 3;
+                nload = j + NST;
             }
             if (!__all_sync(0xffffffffu, mbar_wait(&pready[j & 1], (j >> 1) & 1, err))) {
                 bad = true;
@@ -636,7 +646,8 @@ __global__ void __launch_bounds__(TC_AT, 1)
 #pragma unroll
                     for (int ks = 0; ks < TT / 16; ++ks)
                         mma_f16(tmem + Gm::O_COL + (j & 1) * Gm::OCOLS + h2 * NQ,
-                                smem_desc_sw128(va + h2 * 16384 + ks * 2048, 8192, 1024), desc_kmaj16(pb, TT, ks), id_o,
+                                smem_desc_sw128(va + h2 * 2 * Gm::BOX + ks * 2048, Gm::BOX, 1024), desc_kmaj16(pb, TT, ks),
+                                id_o,
                                 ks > 0);
                 commit(&bar_o[j & 1]);
             }
@@ -683,7 +694,7 @@ __global__ void __launch_bounds__(TC_AT, 1)
             if (!mbar_wait(&bar_s[j & 1], (j >> 1) & 1, err)) bad = true;
             fence_after_sync();
             bad = __any_sync(0xffffffffu, bad);  // TMEM loads are warp-wide
-            const bool valid = s_thread && tb + srow < s1;
+            const bool valid = s_thread && srow < TT && tb + srow < s1;  // S rows past TT: the next block's bytes
             float sc[G];
             if (w < 4 && !bad) {
                 float sv[NQ];
@@ -724,7 +735,7 @@ __global__ void __launch_bounds__(TC_AT, 1)
                 else
                     a_even[h] = a[h];
             }
-            if (s_thread && !bad) {
+            if (s_thread && srow < TT && !bad) {
                 unsigned char *pb = pop + (j & 1) * Gm::POP;
 #pragma unroll
                 for (int h = 0; h < G; ++h) {
@@ -855,8 +866,10 @@ int run_attn(AttnP p, long long B, cudaStream_t st) {
         int *err = nullptr;
         if ((rc = device_error_word(&err))) return rc;
         CUtensorMap kmap, vmap;
-        if (tma::make_chunk_map(&kmap, p.k_cache, true, (uint64_t)B, (uint64_t)p.max_ctx, (uint64_t)p.Hkv, D, true) ||
-            tma::make_chunk_map(&vmap, p.v_cache, true, (uint64_t)B, (uint64_t)p.max_ctx, (uint64_t)p.Hkv, D, true))
+        if (tma::make_chunk_map(&kmap, p.k_cache, true, (uint64_t)B, (uint64_t)p.max_ctx, (uint64_t)p.Hkv, D, true,
+                                TC_TT) ||
+            tma::make_chunk_map(&vmap, p.v_cache, true, (uint64_t)B, (uint64_t)p.max_ctx, (uint64_t)p.Hkv, D, true,
+                                TC_TT))
             return set_error(KAI_GDN_ERR_CUDA, "attention_decode: tensor map encoding failed");
         attn_tc_kernel<D, G><<<grid, TC_AT, smem, st>>>(p, kmap, vmap, err);
     } else {

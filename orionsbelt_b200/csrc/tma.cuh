@@ -52,7 +52,7 @@ inline EncodeTiled encoder() {
 // Host: map of a [B][T][H][D] tensor of 16-bit elements.  Returns 0 or the
 // failing CUresult (-1 when the driver entry point is unavailable).
 inline int make_chunk_map(CUtensorMap *map, const void *base, bool bf16, uint64_t B, uint64_t T, uint64_t H,
-                          uint64_t D, bool swizzle128) {
+                          uint64_t D, bool swizzle128, uint32_t rows = ROWS) {
     EncodeTiled enc = encoder();
     if (!enc) return -1;
     const CUtensorMapDataType dt = bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
@@ -67,7 +67,7 @@ inline int make_chunk_map(CUtensorMap *map, const void *base, bool bf16, uint64_
     } else {
         const cuuint64_t dims[4] = {D, H, T, B};
         const cuuint64_t strides[3] = {D * 2, H * D * 2, T * H * D * 2};
-        const cuuint32_t box[4] = {64, 1, ROWS, 1};
+        const cuuint32_t box[4] = {64, 1, rows, 1};
         const cuuint32_t es[4] = {1, 1, 1, 1};
         r = enc(map, dt, 4, const_cast<void *>(base), dims, strides, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE,
                 CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
@@ -91,16 +91,17 @@ __device__ __forceinline__ void load_chunk(void *dst, const CUtensorMap *map, in
         : "memory");
 }
 
-// 128-byte swizzle: features 64j .. 64j+63 (j < nbox = D/64) of tokens
-// t0 .. t0+63 into `dst` + 8192*j (1024-byte aligned).
+// 128-byte swizzle: features 64j .. 64j+63 (j < nbox = D/64) of the map's
+// rows (64 by default) from token t0 into `dst` + box_bytes*j (1024-byte
+// aligned; box_bytes = rows * 128).
 __device__ __forceinline__ void load_chunk_sw128(void *dst, const CUtensorMap *map, int t0, int h, int b,
-                                                 uint64_t *bar, int nbox = 2) {
+                                                 uint64_t *bar, int nbox = 2, uint32_t box_bytes = 8192) {
     const uint32_t d = static_cast<uint32_t>(__cvta_generic_to_shared(dst));
     const uint32_t m = static_cast<uint32_t>(__cvta_generic_to_shared(bar));
     for (int j = 0; j < nbox; ++j)
         asm volatile(
             "cp.async.bulk.tensor.4d.shared::cluster.global.tile.mbarrier::complete_tx::bytes "
-            "[%0], [%1, {%2, %3, %4, %5}], [%6];" ::"r"(d + 8192u * j),
+            "[%0], [%1, {%2, %3, %4, %5}], [%6];" ::"r"(d + box_bytes * j),
             "l"(reinterpret_cast<uint64_t>(map)), "r"(64 * j), "r"(h), "r"(t0), "r"(b), "r"(m)
             : "memory");
 }
