@@ -582,7 +582,7 @@ def run_rows(args, peaks) -> dict:
         ms = _time(lambda: ops.attention_decode(qa, kna, vna, kc, vc, oa, ctx - 1, 0.0625, ksc, vsc), reps, flush)
         bw_row(name, f"GQA decode, B={B}, 16 q / 4 kv heads x 256, {ctx}-token {cdt} KV cache",
                metrics.attn_decode_bytes(B, ctx, H, Hkv, D, kc.element_size()), ms,
-               "attn_chunk_kernel + attn_combine_kernel")
+               ("attn_tc_kernel" if cdt == torch.bfloat16 else "attn_split_kernel") + " + attn_combine_kernel")
         del kc, vc, qa, kna, vna, oa
     torch.cuda.empty_cache()
     # f1: the reference's end-to-end decode loop at its default (4B) geometry:
