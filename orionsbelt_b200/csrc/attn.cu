@@ -6,18 +6,21 @@
 // Cache layout as the reference's: [batch][max_ctx][kv_heads][head_dim].
 //
 // Split over the context (flash decoding): CTA (split, kv head, batch) takes a
-// run of tokens and the G query heads of its kv head, streaming K and V tiles
-// through a cp.async ring.  A warp takes TB tokens at a time: each lane dots
-// its D/32 elements of each key with the G query slices it holds, the G*TB
-// partial sums are reduced together by a butterfly (each shuffle round halves
-// the values a lane keeps), and the warp keeps its own running softmax and
-// output (lane: its D/32 dims of every head).  Products run as packed fp32
-// pairs (fma.rn.f32x2).  The warps merge once per CTA, and a second kernel
-// merges the splits in order (running max and rescaled sums), so the result
-// does not depend on timing.
-// The chunk that holds `pos` first writes the new token into the cache
-// (converted to the cache type, int8 as the reference quantizes it) and reads
-// it back after a barrier with ordinary loads.
+// run of tokens and the G query heads of its kv head; a second kernel merges
+// the splits.  bf16 caches run both products on the tensor cores
+// (attn_tc_kernel, described where it is defined).  fp32 and int8 caches use
+// attn_split_kernel, streaming K and V tiles through a cp.async ring.  A warp
+// takes TB tokens at a time: each lane dots its D/32 elements of each key
+// with the G query slices it holds, the G*TB partial sums are reduced
+// together by a butterfly (each shuffle round halves the values a lane
+// keeps), and the warp keeps its own running softmax and output (lane: its
+// D/32 dims of every head).  Products run as packed fp32 pairs
+// (fma.rn.f32x2).  The warps merge once per CTA, and the merge kernel
+// combines the splits in a fixed order (running max and rescaled sums), so
+// the result does not depend on timing.
+// The CTA whose split holds `pos` writes the new token into the cache
+// (converted to the cache type, int8 as the reference quantizes it) and
+// patches the converted value into its own shared-memory tile.
 #include <algorithm>
 #include <atomic>
 
