@@ -78,10 +78,11 @@ def test_attention_decode_vs_oracle(cuda, orc, kind, B, H, Hkv, D, pos, max_ctx)
     assert rel_l2(o, o_want) < TOL, rel_l2(o, o_want)
 
 
-@pytest.mark.parametrize("kind", ["f32", "i8"])
+@pytest.mark.parametrize("kind", ["f32", "bf16", "i8"])
 def test_attention_decode_steps(cuda, orc, kind):
     """Eight decode steps in a row on one cache (the reference's ctx-sweep use:
-    the cache grows by one token per call)."""
+    the cache grows by one token per call; for bf16 the new token moves through
+    one tensor-core tile)."""
     B, H, Hkv, D, max_ctx = 1, 16, 4, 256, 600
     _, _, _, kc, vc, ks, vs = _case(B, H, Hkv, D, max_ctx, kind, 5)
     kcd, vcd = _to_dev(cuda, kc, kind), _to_dev(cuda, vc, kind)
