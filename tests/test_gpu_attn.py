@@ -65,6 +65,9 @@ def _run(cuda, q, kn, vn, kc, vc, ks, vs, pos, scale, kind):
     (1, 16, 4, 256, 0, 8), (1, 16, 4, 256, 63, 64), (1, 16, 4, 256, 64, 100), (1, 16, 4, 256, 1000, 1024),
     (2, 16, 4, 256, 4095, 4096), (3, 8, 8, 128, 200, 300), (2, 4, 2, 128, 511, 600), (1, 32, 4, 128, 777, 800),
     (1, 16, 4, 256, 32767, 32768),
+    # 48-token tiles of the tensor-core kernel: one full tile, the first row of
+    # the second, the last row of the second
+    (1, 16, 4, 256, 47, 48), (1, 16, 4, 256, 48, 100), (2, 16, 4, 256, 95, 96),
 ])
 def test_attention_decode_vs_oracle(cuda, orc, kind, B, H, Hkv, D, pos, max_ctx):
     if pos >= 32767 and kind != "bf16":
