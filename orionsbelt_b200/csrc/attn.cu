@@ -124,6 +124,13 @@ struct AttnP {
     float scale;
 };
 
+// The merge kernel is launched as a programmatic dependent of the split
+// kernel: every split thread allows its launch at once, so at small batch
+// (one wave of split CTAs) the merge's CTAs are placed while the splits run;
+// the merge waits (griddepcontrol.wait) for the split grid to complete and
+// its writes to be visible before it reads a partial.
+__device__ __forceinline__ void allow_merge_launch() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
 constexpr int STAGE_BYTES = 32768;  // K and V of one tile
 constexpr int NSTAGE = 3;
 
@@ -151,6 +158,7 @@ template <int N> __device__ __forceinline__ void cp_wait() { asm volatile("cp.as
 // stage over, and the eight warps' states are merged once at the end.
 template <int D, int G, int CDT>
 __global__ void __launch_bounds__(AT, G == 8 ? 1 : 2) attn_split_kernel(AttnP p) {  // G = 8: 64 query regs
+    allow_merge_launch();
     using C = Cache<CDT>;
     using Geo = AttnGeo<D, CDT>;
     using T = typename C::T;
@@ -357,6 +365,7 @@ __global__ void __launch_bounds__(AT, G == 8 ? 1 : 2) attn_split_kernel(AttnP p)
 // so a merge of many chunks costs about one round of loads.
 template <int D, int G>
 __global__ void __launch_bounds__(256) attn_combine_kernel(AttnP p) {
+    asm volatile("griddepcontrol.wait;" ::: "memory");  // the split kernel has completed
     constexpr int NW = 8, J = D / 64, CU = 4;  // J float2 per lane and chunk
     __shared__ float s_m[NW], s_l[NW], s_acc[NW][D];
     const long long h = blockIdx.x, b = blockIdx.y, kh = h / G;
@@ -503,6 +512,7 @@ template <int D, int G>
 __global__ void __launch_bounds__(TC_AT, 1)
     attn_tc_kernel(AttnP p, const __grid_constant__ CUtensorMap kmap, const __grid_constant__ CUtensorMap vmap,
                    int *err) {
+    allow_merge_launch();
     using namespace umma;
     using Gm = TcAttnGeo<D, G>;
     using T = __nv_bfloat16;
@@ -880,7 +890,17 @@ int run_attn(AttnP p, long long B, cudaStream_t st) {
     }
     rc = check_launch("attention split kernel");
     if (rc || p.nch == 1) return rc;
-    attn_combine_kernel<D, G><<<dim3((unsigned)p.H, (unsigned)B), 256, 0, st>>>(p);
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)p.H, (unsigned)B);
+    cfg.blockDim = dim3(256);
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    const cudaError_t le = cudaLaunchKernelEx(&cfg, attn_combine_kernel<D, G>, p);
+    if (le != cudaSuccess) return check_cuda(le, "attn_combine_kernel launch");
     return check_launch("attn_combine_kernel");
 }
 
