@@ -28,6 +28,7 @@
 // for tiles that are already running; every wait is bounded and a timeout
 // sets an error word instead of hanging.  HBM traffic is the algorithmic one
 // (read once, write once) plus a 16-byte record per tile and channel.
+#include <algorithm>
 #include <mutex>
 
 #include "gdn_internal.cuh"
@@ -229,8 +230,19 @@ template <int ODT, int VEC> __device__ __forceinline__ void stv(void *base, size
 // not yet published); reduce the tile; if the carry is still unknown, publish
 // the tile's aggregate and look back again, waiting this time; publish the
 // inclusive prefix and write the outputs from registers.
+// Zeroes the ticket and records of a look-back launch.  The scan kernel is
+// launched as its programmatic dependent: it may be placed at once and waits
+// (griddepcontrol.wait) for this kernel to complete before it touches
+// memory, which spares the gap between two stream operations.
+__global__ void __launch_bounds__(256) zero_records_kernel(uint4 *p, size_t n16) {
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+    for (size_t i = (size_t)blockIdx.x * 256 + threadIdx.x; i < n16; i += (size_t)gridDim.x * 256)
+        p[i] = make_uint4(0u, 0u, 0u, 0u);
+}
+
 template <int OP, int ODT, int SDT, int VEC, int RPW, int W>
 __global__ void __launch_bounds__(32 * W, 16 / W) scan_lookback_kernel(ScanParams p, Lookback lb) {
+    asm volatile("griddepcontrol.wait;" ::: "memory");  // the records are zero
     static_assert(VEC == 1, "one channel per lane: the look-back record is one 16-byte word");
     constexpr int NIN = Nin<OP>::n, TROWS = W * RPW, TC = 32 * VEC;
     using Rec = TileRecord;
@@ -432,14 +444,25 @@ int launch_lookback(ScanParams p, size_t batch, cudaStream_t st, const char *nam
     lb.first_spin = first_spin(lb.nct * lb.batch);
     const long long tiles = lb.ntr * lb.nct * lb.batch;
     if (tiles > 0x7fffffffll) return set_error(KAI_GDN_ERR_UNSUPPORTED, "%s: shape too large", name);
-    const size_t bytes = lookback_bytes(batch, p.seq, p.ch, g);
-    int rc = check_cuda(cudaMemsetAsync(scratch, 0, bytes, st), name);
-    if (rc) return rc;
+    const size_t n16 = lookback_bytes(batch, p.seq, p.ch, g) / 16;  // 256 + 512 per tile: whole 16-byte words
     lb.counter = static_cast<unsigned int *>(scratch);
-    rc = device_error_word(&lb.err);
+    int rc = device_error_word(&lb.err);
     if (rc) return rc;
     lb.rec = static_cast<char *>(scratch) + 256;
-    scan_lookback_kernel<OP, ODT, SDT, VEC, RPW, W><<<(unsigned)tiles, 32 * W, 0, st>>>(p, lb);
+    const unsigned zg = (unsigned)std::min<size_t>((n16 + 255) / 256, 4 * (size_t)sm_count());
+    zero_records_kernel<<<zg, 256, 0, st>>>(static_cast<uint4 *>(scratch), n16);
+    if ((rc = check_launch(name))) return rc;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)tiles);
+    cfg.blockDim = dim3(32 * W);
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    const cudaError_t le = cudaLaunchKernelEx(&cfg, scan_lookback_kernel<OP, ODT, SDT, VEC, RPW, W>, p, lb);
+    if (le != cudaSuccess) return check_cuda(le, name);
     return check_launch(name);
 }
 
@@ -551,8 +574,9 @@ int launch_gdn2_scan(const float *g, const float *bg, const float *wg, const flo
 // address (on the host it is only a stand-in), so the address is looked up
 // once per device with cudaGetSymbolAddress, with that device current, on the
 // first call there; that first call should come before any stream capture.
-// Every call shares the array; each call clears (cudaMemsetAsync, which
-// allocates nothing) the part it uses before its kernel runs.  Calls that
+// Every call shares the array; each call clears (with a small zeroing
+// kernel, which allocates nothing) the part it uses before its scan kernel
+// runs.  Calls that
 // overlap on the GPU -- two streams, or two host threads -- race on it and
 // must be serialised by the caller.
 // ---------------------------------------------------------------------------
