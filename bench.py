@@ -33,6 +33,8 @@ import sys
 import time
 from pathlib import Path
 
+import numpy as np
+
 ROOT = Path(__file__).resolve().parent
 sys.path.insert(0, str(ROOT))
 
@@ -215,10 +217,19 @@ def run_ours(args):
     # ---- every other hot-path row on its own configuration (this GPU)
     rows = None if (args.no_rows or world > 1) else run_rows(args, peaks)
 
-    # ---- CPU baseline on a bounded sample (rank 0, N = 1 only)
+    # ---- CPU baselines on bounded samples (rank 0, N = 1 only): the headline
+    # decode step, and one per row beside its GPU figure
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu:
-        cpu = cpu_decode_sample(seconds=10.0)
+        nthreads = host_threads()
+        cpu = cpu_decode_sample(seconds=5.0, nthreads=nthreads)
+        crow = cpu_rows(nthreads)
+        if rows is not None:
+            for name, row in rows.items():
+                if name in crow:
+                    row["cpu_baseline"] = crow[name]
+        if chunk is not None and "chunk_cfg2" in crow:
+            chunk["cpu_baseline"] = crow["chunk_cfg2"]
 
     if rank == 0:
         line = {
@@ -653,79 +664,298 @@ def run_rows(args, peaks) -> dict:
     return out
 
 
-def cpu_decode_sample(seconds: float = 10.0, nthreads: int = 0) -> dict:
-    """Oracle port of ref_delta_rule (gpu/gdn_gpu_validate.c:100-118), OpenMP over
-    (batch, head), on one config-1 layer at B=64, repeated for ~`seconds`."""
-    import numpy as np
+def host_threads() -> int:
+    """Host threads this process may run on (its CPU affinity), set explicitly
+    for every CPU measurement: a launcher such as torchrun exports
+    OMP_NUM_THREADS=1, which must not decide the baseline's thread count."""
+    try:
+        return len(os.sched_getaffinity(0))
+    except AttributeError:
+        return os.cpu_count() or 1
 
+
+def host_info(nthreads: int) -> dict:
+    model = "unknown"
+    try:
+        for ln in Path("/proc/cpuinfo").read_text().splitlines():
+            if ln.startswith("model name"):
+                model = ln.split(":", 1)[1].strip()
+                break
+    except OSError:
+        pass
+    return {"cpu": model, "threads_used": nthreads, "nproc": os.cpu_count()}
+
+
+def _cpu_time(fn, min_s: float = 1.0, min_reps: int = 3, max_reps: int = 50) -> dict:
+    """p50 / p95 seconds per call after one discarded warm-up call (the
+    reference protocol, docs/METRICS.md:393-456, asks for >= 5 timed repeats
+    after warm-ups; small calls get more, large ones at least three)."""
+    fn()
+    ts = []
+    t_all = time.perf_counter()
+    while len(ts) < max_reps and (len(ts) < min_reps or time.perf_counter() - t_all < min_s):
+        t0 = time.perf_counter()
+        fn()
+        ts.append(time.perf_counter() - t0)
+    ts.sort()
+    return {"p50": ts[len(ts) // 2], "p95": ts[min(len(ts) - 1, int(0.95 * len(ts)))], "reps": len(ts)}
+
+
+def _decode_inputs(r, B, Hk, Hv, dk, dv, state_std=0.02):
+    """One config-1 layer's host inputs; q/k/v rounded to bf16 (the GPU arm's
+    input type), g and beta fp32."""
     import oracle
     from orionsbelt_b200 import synth
 
+    rb = lambda a: oracle.u16_to_f32(oracle.f32_to_u16(a, "bf16"), "bf16")  # noqa: E731
+    S = (r.standard_normal((B, Hv, dk, dv), dtype=np.float32) * state_std) if state_std else None
+    q = rb(synth.l2norm(r.standard_normal((B, Hk, dk))))
+    k = rb(synth.l2norm(r.standard_normal((B, Hk, dk))))
+    v = rb(r.standard_normal((B, Hv, dv)).astype(np.float32))
+    beta = (1 / (1 + np.exp(-r.standard_normal((B, Hv))))).astype(np.float32)
+    g = (-synth.softplus(r.standard_normal((B, Hv))) * 0.1).astype(np.float32)
+    return S, q, k, v, g, beta
+
+
+def cpu_decode_sample(seconds: float = 5.0, nthreads: int = 0) -> dict:
+    """Oracle port of ref_delta_rule (gpu/gdn_gpu_validate.c:100-118), OpenMP over
+    (batch, head) on `nthreads` host threads, on one config-1 layer at B=64
+    (bf16-rounded q/k/v, the state updated in place), repeated for ~`seconds`.
+    Bytes are counted as for the GPU arm."""
+    import oracle
+
     orc, _ = oracle.require()
+    nthreads = nthreads or host_threads()
+    orc.set_threads(nthreads)
     c = CFG1
     r = np.random.default_rng(5)
-    S = (r.standard_normal((c["B"], c["Hv"], c["dk"], c["dv"])) * 0.02).astype(np.float32)
-    q = synth.l2norm(r.standard_normal((c["B"], c["Hk"], c["dk"])))
-    k = synth.l2norm(r.standard_normal((c["B"], c["Hk"], c["dk"])))
-    v = r.standard_normal((c["B"], c["Hv"], c["dv"])).astype(np.float32)
-    beta = (1 / (1 + np.exp(-r.standard_normal((c["B"], c["Hv"]))))).astype(np.float32)
-    g = (-synth.softplus(r.standard_normal((c["B"], c["Hv"]))) * 0.1).astype(np.float32)
-    layer_bytes = metrics.decode_bytes(c["B"], c["Hk"], c["Hv"], c["dk"], c["dv"], e_state=4, e_in=4, e_out=4)
-    orc.delta_rule_decode(S, q, k, v, g, beta, nthreads=nthreads)
+    S, q, k, v, g, beta = _decode_inputs(r, c["B"], c["Hk"], c["Hv"], c["dk"], c["dv"])
+    layer_bytes = metrics.decode_bytes(c["B"], c["Hk"], c["Hv"], c["dk"], c["dv"], e_state=4, e_in=2, e_out=2)
+    orc.delta_rule_decode(S, q, k, v, g, beta, nthreads=nthreads, copy=False)
     n, t_start = 0, time.perf_counter()
     while True:
-        S, _ = orc.delta_rule_decode(S, q, k, v, g, beta, nthreads=nthreads)
+        orc.delta_rule_decode(S, q, k, v, g, beta, nthreads=nthreads, copy=False)
         n += 1
         el = time.perf_counter() - t_start
         if el >= seconds:
             break
-    cores = nthreads if nthreads > 0 else orc.num_threads()
-    return {"value": round(layer_bytes * n / el / 1e9, 3), "unit": "GB/s", "cores": cores, "kind": "port",
-            "sample": f"{n} x one config-1 layer (B=64, 32 heads, 128x128 fp32 state, fp32 q/k/v), "
-                      f"{el:.1f} s; oracle restatement of gpu/gdn_gpu_validate.c:100-118 (the reference's "
-                      f"C decode step is in an OpenCL host file that does not build here)"}
+    return {"value": round(layer_bytes * n / el / 1e9, 3), "unit": "GB/s", "cores": nthreads, "kind": "port",
+            "sample": f"{n} x one config-1 layer (B=64, 32 heads, 128x128 fp32 state updated in place, bf16-rounded "
+                      f"q/k/v), {el:.1f} s, OpenMP over (batch, head) on {nthreads} threads; oracle restatement of "
+                      f"gpu/gdn_gpu_validate.c:100-118 (the reference's C decode step is in an OpenCL host file "
+                      f"that does not build here)", "host": host_info(nthreads)}
+
+
+def cpu_rows(nthreads: int) -> dict:
+    """CPU baseline of every per-row measurement, on this host's cores: the
+    reference's own C (oracle/_ref, compiled from its sources; kind
+    "reference") where the reference has code for the row, else the oracle
+    restatement (kind "port").  kai_run_* kernels are single-threaded by
+    design; gdn_sve.c's gdn_* twins and the oracle's loops run OpenMP on
+    `nthreads` threads.  Chunk rows: the reference has no chunked
+    implementation, so the CPU figure is the token loop (the recurrence the
+    chunked form restates), timed on a sample of (batch, head) pairs and
+    tokens and extrapolated to the configuration's tokens/s."""
+    import oracle
+    from orionsbelt_b200 import synth
+
+    orc, ref = oracle.require()
+    orc.set_threads(nthreads)
+    r = np.random.default_rng(31)
+    f32 = lambda *sh: r.standard_normal(sh, dtype=np.float32)  # noqa: E731
+    out = {}
+
+    def bw(name, nbytes, fn, kind, cores, sample):
+        t = _cpu_time(fn)
+        out[name] = {"value": round(nbytes / t["p50"] / 1e9, 4), "unit": "GB/s", "cores": cores, "kind": kind,
+                     "ms_p50": round(t["p50"] * 1e3, 3), "ms_p95": round(t["p95"] * 1e3, 3), "reps": t["reps"],
+                     "sample": sample}
+
+    def have(lib):
+        return lib is not None
+
+    P = lambda a: a.ctypes.data_as(oracle.C.POINTER(oracle.C.c_float))  # noqa: E731
+    sz = oracle.C.c_size_t
+
+    # a1: log-decay cumsum (the reference has the prefix product only: port)
+    g = (-synth.softplus(f32(8, 32768, 32)) * 0.1).astype(np.float32)
+    bw("a1_cumsum_cfg2", 2 * g.size * 4, lambda: [orc.cumsum(g[b]) for b in range(8)], "port", 1,
+       "full size, 8 x 32768 x 32, oracle cumsum (single thread)")
+    a0 = np.exp(g[0, :2048]).astype(np.float32)
+    a4k = (r.uniform(0.9, 1.1, (4096, 4096))).astype(np.float32)
+    if have(ref):
+        o0 = np.empty_like(a0)
+        bw("a1_cumdecay_cfg0", 2 * a0.size * 4,
+           lambda: ref.lib.kai_run_gdn_cumdecay_f32_sve(P(a0), P(o0), sz(2048), sz(32)), "reference", 1,
+           "full size, 2048 x 32, kai_run_gdn_cumdecay_f32_sve (single-threaded by design)")
+        bw("a1_cumdecay_4096x4096", 2 * a4k.size * 4, lambda: ref.cumdecay(a4k), "reference", nthreads,
+           f"full size, gdn_cumdecay_f32 (gdn_sve.c, OpenMP, {nthreads} threads)")
+    # a2: conv, config 0 (reference, OpenMP) and the config-3 fp16 shard (port, sampled rows)
+    x0, w0, h0 = f32(2048, 8192), (f32(4, 8192) * 0.5).astype(np.float32), np.zeros((3, 8192), np.float32)
+    if have(ref):
+        bw("a2_conv_cfg0", metrics.conv_bytes(1, 2048, 8192, 4), lambda: ref.conv(x0, w0, h0), "reference",
+           nthreads, f"full size, 2048 x 8192 fp32, gdn_causal_dwconv1d_f32 (gdn_sve.c, OpenMP, {nthreads} threads)")
+    xh = oracle.f32_to_u16(f32(1024, 8192), "f16")
+    hh = np.zeros((3, 8192), np.uint16)
+    bw("a2_conv_cfg3_shard", metrics.conv_bytes(1, 1024, 8192, 2), lambda: orc.conv_narrow(xh, w0, hh, "f16"),
+       "port", 1, "1024 of 8 x 8192 rows x 8192 channels, fp16 I/O, oracle conv (the reference's conv is fp32 "
+       "only), GB/s of the sample")
+    # a3: gated scan (reference, OpenMP), 4096 of the 32768 rows
+    gs = r.uniform(0.5, 0.99, (4096, 4096)).astype(np.float32)
+    xs = f32(4096, 4096)
+    st = np.zeros(4096, np.float32)
+    if have(ref):
+        bw("a3_gated_scan", metrics.gated_scan_bytes(1, 4096, 4096), lambda: ref.gated_scan(gs, xs, st), "reference",
+           nthreads, f"4096 of the 32768 rows x 4096 channels, gdn_gated_scan_f32 (gdn_sve.c, OpenMP, {nthreads} "
+           f"threads), GB/s of the sample")
+        # a4: GEMV (kai, single-threaded) and the delta-rule matmul
+        av, B1 = f32(128), f32(128, 4096)
+        bw("a4_gemv", metrics.matmul_bytes(1, 128, 4096), lambda: ref.gemv(av, B1), "reference", 1,
+           "full size, K=128 N=4096, kai_run_gdn_gemv_f32_f32_f32_1x4_neon (scalar branch, single thread)")
+        Am, Bm = f32(64, 128), f32(128, 2048)
+        bw("a4_matmul", metrics.matmul_bytes(64, 128, 2048), lambda: ref.matmul(Am, Bm), "reference", 1,
+           "full size, M=64 K=128 N=2048, gdn_delta_rule_matmul (scalar path, single thread)")
+    # a5 / f4: one config-1 layer, port (OpenMP over (batch, head)), state in place
+    S, q, k, v, gd, beta = _decode_inputs(r, 64, 16, 32, 128, 128)
+    bw("a5_decode_cfg1_layer", metrics.decode_bytes(64, 16, 32, 128, 128),
+       lambda: orc.delta_rule_decode(S, q, k, v, gd, beta, nthreads=nthreads, copy=False), "port", nthreads,
+       f"full config-1 layer (B=64), oracle ref_delta_rule restatement, OpenMP over (batch, head) on {nthreads} "
+       f"threads, state updated in place")
+    g2 = (-synth.softplus(f32(64, 32, 128)) * 0.1).astype(np.float32)
+    bg2, wg2 = r.uniform(0, 1, (64, 32, 128)).astype(np.float32), r.uniform(0, 1, (64, 32, 128)).astype(np.float32)
+    bw("f4_gdn2_decode_cfg1", metrics.gdn2_decode_bytes(64, 16, 32, 128, 128),
+       lambda: orc.gdn2_decode(S, q, k, v, g2, bg2, wg2, nthreads=nthreads), "port", nthreads,
+       f"full config-1 layer (B=64), oracle restatement of gdn2_recurrent (bench/gdn2_reference.py:58-145), "
+       f"OpenMP on {nthreads} threads")
+    del S
+    # f2: int8 weights, the reference's own gemv_int8_neon / gemm_int8_neon (scalar branch)
+    if oracle.ref_int8 is not None:
+        for name, (M, K, N) in [("f2_int8_gemv_ffn_up", (1, 2560, 9216)), ("f2_int8_gemv_ffn_down", (1, 9216, 2560)),
+                                ("f2_int8_gemm_b16_ffn_up", (16, 2560, 9216))]:
+            W = (f32(K, N) * 0.05).astype(np.float32)
+            q8, s8 = oracle.ref_int8.quantize_int8(W)
+            A8 = f32(M, K)
+            bw(name, metrics.int8_matmul_bytes(M, K, N), lambda A8=A8, q8=q8, s8=s8: oracle.ref_int8.matmul_int8(
+                A8, q8, s8), "reference", 1,
+               f"full size, M={M} K={K} N={N}, the reference's {'gemv' if M == 1 else 'gemm'}_int8_neon "
+               f"(gdn_e2e_decode.c, scalar branch, single thread)")
+    # f3: attention decode over a 32768-token cache; bf16 cache: oracle (the
+    # reference's attention has fp32 / int8 caches only); int8: the reference's own
+    H, Hkv, D, ctx = 16, 4, 256, 32768
+    for name, Bs, Bfull in [("f3_attn_decode_bf16_b1", 1, 1), ("f3_attn_decode_bf16_b16", 2, 16)]:
+        qa, kn, vn = f32(Bs, H, D), f32(Bs, Hkv, D), f32(Bs, Hkv, D)
+        kc = oracle.f32_to_u16(f32(Bs, ctx, Hkv, D), "bf16")
+        vc = oracle.f32_to_u16(f32(Bs, ctx, Hkv, D), "bf16")
+        bw(name, metrics.attn_decode_bytes(Bs, ctx, H, Hkv, D, 2),
+           lambda qa=qa, kn=kn, vn=vn, kc=kc, vc=vc: orc.attn_decode(qa, kn, vn, kc, vc, ctx - 1, 0.0625,
+                                                                   nthreads=nthreads), "port", nthreads,
+           f"B={Bs} of {Bfull}, 32768-token bf16 cache, oracle attention decode (OpenMP on {nthreads} threads), "
+           f"GB/s of the sample")
+        del kc, vc
+    qa, kn, vn = f32(1, H, D), f32(1, Hkv, D), f32(1, Hkv, D)
+    kc8 = r.integers(-128, 128, (1, ctx, Hkv, D)).astype(np.int8)
+    vc8 = r.integers(-128, 128, (1, ctx, Hkv, D)).astype(np.int8)
+    sc = np.full((1, Hkv), 0.01, np.float32)
+    bw("f3_attn_decode_int8_b1", metrics.attn_decode_bytes(1, ctx, H, Hkv, D, 1),
+       lambda: orc.attn_decode(qa, kn, vn, kc8, vc8, ctx - 1, 0.0625, sc, sc, nthreads=nthreads), "port", nthreads,
+       f"full size, B=1, 32768-token int8 cache, oracle restatement of full_attn_real_forward_int8kv "
+       f"(gdn_e2e_decode.c:1652-1830, bit-identical to it), OpenMP on {nthreads} threads")
+    # chunk scans: the token loop on sampled (batch, head) pairs and tokens
+    def chunk_row(name, B, T, g_scale, T_sample, pairs, kind_in):
+        d = synth.host_gdn(1, T_sample, pairs, pairs, 128, 128, g_scale=g_scale, seed=3)
+        if kind_in != "f32":
+            for key in ("q", "k", "v"):
+                d[key] = oracle.u16_to_f32(oracle.f32_to_u16(d[key], kind_in), kind_in)
+        t = _cpu_time(lambda: orc.delta_rule_seq(d["S0"], d["q"], d["k"], d["v"], d["g"], d["beta"],
+                                                 nthreads=nthreads), min_s=1.0, min_reps=2)
+        pair_tok = pairs * T_sample / t["p50"]
+        out[name] = {"value": round(pair_tok / 32, 1), "unit": "tokens/s", "cores": nthreads, "kind": "port",
+                     "ms_p50": round(t["p50"] * 1e3, 2), "reps": t["reps"],
+                     "sample": f"token loop (oracle restatement of gpu/gdn_gpu_validate.c:100-118; the reference "
+                               f"has no chunked implementation) over {pairs} (batch, head) pairs x {T_sample} "
+                               f"tokens, OpenMP over pairs on {nthreads} threads; tokens/s of the B={B}, T={T}, "
+                               f"32-head configuration extrapolated as pair-tokens/s / 32"}
+
+    chunk_row("a6_chunk_cfg0", 1, 2048, 0.1, 512, 32, "f32")
+    chunk_row("chunk_cfg2", 8, 32768, 0.1, 1024, max(nthreads, 8), "bf16")
+    chunk_row("a6_chunk_cfg3", 32, 8192, 1.0, 1024, max(nthreads, 8), "f16")
+    # f1: the end-to-end loop, oracle restatement at the 4B geometry, one token
+    dims = (2560, 2048, 4096, 8192, 9216, 16, 4, 256, 32)
+    W = {n: (r.standard_normal(sh, dtype=np.float32) * 0.005) for n, sh in synth.e2e_weight_shapes(dims).items()}
+    W["g_beta"] = r.uniform(0, 1, W["g_beta"].shape).astype(np.float32)
+    pat = synth.e2e_layer_pattern(32)
+    h1 = (f32(1, 1, 2560) * 0.1).astype(np.float32)
+    h2 = (f32(2, 1, 2560) * 0.1).astype(np.float32)
+    t0 = time.perf_counter()
+    orc.e2e_decode(dims, pat, W, h1, nthreads=nthreads)
+    t1 = time.perf_counter()
+    orc.e2e_decode(dims, pat, W, h2, nthreads=nthreads)
+    t2 = time.perf_counter()
+    per_tok = max((t2 - t1) - (t1 - t0), 1e-9)
+    for name in ("f1_e2e_decode_b1", "f1_e2e_decode_b16"):
+        out[name] = {"value": round(1.0 / per_tok, 3), "unit": "tokens/s", "cores": nthreads, "kind": "port",
+                     "ms_per_token": round(per_tok * 1e3, 2),
+                     "sample": f"decode tokens of one sequence, 4B geometry, int8 weights, oracle restatement of the "
+                               f"reference's loop (gdn_e2e_decode.c:2775-2796; its int8 GEMVs split over {nthreads} "
+                               f"threads by columns); time per token = (2-token call - 1-token call), so the weight "
+                               f"quantization each call repeats is excluded; sequences run one after another, so "
+                               f"batch 16 has the same tokens/s"}
+    return out
 
 
 # ---------------------------------------------------------------- reference
 
 def run_reference(args):
+    """The reference path's CPU implementation of the headline step: the
+    oracle port of ref_delta_rule (the reference's C decode step lives in an
+    OpenCL host file that does not build here), on every host thread this
+    process may use (set explicitly, whatever OMP_NUM_THREADS a launcher
+    exported), over the same workload as the GPU arm: one step = the decode
+    step of all 24 config-1 layers at B = 64, bf16-rounded q/k/v, each layer's
+    fp32 state updated in place; bytes counted as for the GPU arm."""
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return
-    import numpy as np
-
     import oracle
-    from orionsbelt_b200 import synth
 
     orc, _ = oracle.require()
+    nthreads = host_threads()
+    orc.set_threads(nthreads)
     c = CFG1
     r = np.random.default_rng(5)
-    S = (r.standard_normal((c["B"], c["Hv"], c["dk"], c["dv"])) * 0.02).astype(np.float32)
-    q = synth.l2norm(r.standard_normal((c["B"], c["Hk"], c["dk"])))
-    k = synth.l2norm(r.standard_normal((c["B"], c["Hk"], c["dk"])))
-    v = r.standard_normal((c["B"], c["Hv"], c["dv"])).astype(np.float32)
-    beta = (1 / (1 + np.exp(-r.standard_normal((c["B"], c["Hv"]))))).astype(np.float32)
-    g = (-synth.softplus(r.standard_normal((c["B"], c["Hv"]))) * 0.1).astype(np.float32)
-    layer_bytes = metrics.decode_bytes(c["B"], c["Hk"], c["Hv"], c["dk"], c["dv"], e_state=4, e_in=4, e_out=4)
+    base = _decode_inputs(r, c["B"], c["Hk"], c["Hv"], c["dk"], c["dv"])
+    layers = []
+    for li in range(c["layers"]):
+        S = base[0] * np.float32(1.0 + 0.001 * li)  # each layer its own 268 MB state
+        layers.append((S,) + _decode_inputs(r, c["B"], c["Hk"], c["Hv"], c["dk"], c["dv"], state_std=0)[1:])
+    layer_bytes = metrics.decode_bytes(c["B"], c["Hk"], c["Hv"], c["dk"], c["dv"], e_state=4, e_in=2, e_out=2)
+    step_bytes = layer_bytes * c["layers"]
+
+    def step():
+        for S, q, k, v, g, beta in layers:
+            orc.delta_rule_decode(S, q, k, v, g, beta, nthreads=nthreads, copy=False)
+
     for _ in range(args.warmup):
-        S, _ = orc.delta_rule_decode(S, q, k, v, g, beta)
+        step()
     t0 = time.perf_counter()
     for _ in range(args.steps):
-        S, _ = orc.delta_rule_decode(S, q, k, v, g, beta)
+        step()
     el = time.perf_counter() - t0
-    value = layer_bytes * args.steps / el / 1e9
-    cores = orc.num_threads()
-    sample = ("each step = one config-1 layer (B=64, 32 value heads, 128x128 fp32 state, fp32 q/k/v) of the "
-              "24-layer decode step, on all host threads; oracle port of the reference's ref_delta_rule "
-              "(gpu/gdn_gpu_validate.c:100-118; that file needs OpenCL headers and does not build here)")
+    value = step_bytes * args.steps / el / 1e9
+    sample = (f"each step = the full config-1 decode step (24 layers, B=64, 32 value heads, 128x128 fp32 state "
+              f"updated in place, bf16-rounded q/k/v) on {nthreads} host threads (OpenMP over (batch, head)); "
+              f"oracle port of the reference's ref_delta_rule (gpu/gdn_gpu_validate.c:100-118; that file needs "
+              f"OpenCL headers and does not build here)")
     line = {"metric": METRIC, "value": round(value, 3), "unit": "GB/s", "n_gpus": args.gpus, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": round(el / args.steps * 1e3, 3), "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-            "config": {"workload": "config 1 decode step, one layer of 24 per step (CPU sample)", "global_batch": 64,
-                       "parallelism": f"OpenMP x{cores} over (batch, head)"},
+            "config": {"workload": "config 1: recurrent decode step over 24 GDN layers, batch 64, 32 value / 16 key "
+                                   "heads, 128x128 fp32 state, bf16 q/k/v (CPU)", "global_batch": c["B"],
+                       "layers": c["layers"], "parallelism": f"OpenMP x{nthreads} over (batch, head)",
+                       "bytes_per_step": step_bytes},
             "impl": "reference",
-            "cpu_baseline": {"value": round(value, 3), "unit": "GB/s", "cores": cores, "kind": "port",
-                             "sample": sample},
+            "cpu_baseline": {"value": round(value, 3), "unit": "GB/s", "cores": nthreads, "kind": "port",
+                             "sample": sample, "host": host_info(nthreads)},
             "e2e": {"value": round(value, 3), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
 

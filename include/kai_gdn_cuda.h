@@ -145,7 +145,9 @@ KAI_GDN_API int kai_run_gdn_gated_scan_sm100a(const float *g, const float *x, fl
  * KAI_GDN_ERR_INVALID with a message.  The first call on a device looks up
  * the array's address (cudaGetSymbolAddress) and should come before any
  * stream capture.  All calls share the array: calls that overlap on the GPU
- * (several streams or host threads) race and must be serialised. */
+ * (several streams or host threads) race and must be serialised.  The
+ * looked-up address is kept for the life of the process, so a process that
+ * calls cudaDeviceReset must not call this entry point afterwards. */
 #define KAI_GDN_NOALLOC_SCRATCH_BYTES (4u << 20)
 KAI_GDN_API int kai_run_gdn_gated_scan_noalloc_sm100a(const float *g, const float *x, float *s,
                                                       void *state, int state_dtype, size_t batch,
@@ -321,7 +323,10 @@ KAI_GDN_API int kai_run_gdn_chunk_delta_rule_sm100a(const kai_gdn_chunk_args *ar
  * ==================================================================== */
 
 /* Make `device` current for this host thread (one thread per GPU in the
- * multi-GPU driver).  Returns a status. */
+ * multi-GPU driver).  Returns a status.  The library keeps per-device state
+ * for the life of the process (device addresses of its file-scope words,
+ * per-stream scratch, tensor-map and attribute caches); a process that calls
+ * cudaDeviceReset must not use the library on that device afterwards. */
 KAI_GDN_API int kai_gdn_cuda_set_device(int device);
 /* Number of visible CUDA devices, or -1 on error. */
 KAI_GDN_API int kai_gdn_cuda_device_count(void);

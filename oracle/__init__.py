@@ -21,6 +21,7 @@ buffers so callers keep their inputs.
 from __future__ import annotations
 
 import ctypes as C
+import os
 import subprocess
 from pathlib import Path
 
@@ -39,10 +40,17 @@ _u16 = C.POINTER(C.c_uint16)
 _sz = C.c_size_t
 
 
+def reference_root():
+    """The reference source tree, from the ORIONSBELT_REF environment variable
+    (None when it is unset or not a directory)."""
+    r = os.environ.get("ORIONSBELT_REF")
+    return Path(r) if r and Path(r).is_dir() else None
+
+
 def build(ref: bool = True) -> None:
-    """Compile liboracle.so (and, when the reference tree exists, _ref/)."""
+    """Compile liboracle.so (and, when ORIONSBELT_REF names the reference tree, _ref/)."""
     subprocess.run(["make", "-s", "-C", str(HERE), "oracle"], check=True)
-    if ref and Path("/root/reference").is_dir():
+    if ref and reference_root() is not None:
         subprocess.run(["make", "-s", "-C", str(HERE), "ref", "ref-tests"], check=True)
 
 
@@ -199,9 +207,13 @@ class _Oracle(_Kernels):
                                      _p(out, np.float32), _sz(S.shape[0]), _sz(S.shape[1]))
         return S, out
 
-    def delta_rule_decode(self, S, q, k, v, g, beta, scale=1.0, nthreads=0):
-        """S [B][Hv][dk][dv], q,k [B][Hk][dk], v [B][Hv][dv], g,beta [B][Hv]."""
-        S = _f32(S).copy()
+    def delta_rule_decode(self, S, q, k, v, g, beta, scale=1.0, nthreads=0, copy=True):
+        """S [B][Hv][dk][dv], q,k [B][Hk][dk], v [B][Hv][dv], g,beta [B][Hv].
+        copy=False updates S (float32, C-contiguous) in place."""
+        if copy:
+            S = _f32(S).copy()
+        else:
+            assert S.dtype == np.float32 and S.flags["C_CONTIGUOUS"]
         q, k, v, g, beta = map(_f32, (q, k, v, g, beta))
         B, Hv, dk, dv = S.shape
         Hk = q.shape[1]
@@ -323,6 +335,10 @@ class _Oracle(_Kernels):
 
     def num_threads(self) -> int:
         return int(self.lib.orc_num_threads())
+
+    def set_threads(self, n: int) -> None:
+        """OpenMP threads for later calls (of this library and of the reference's)."""
+        self.lib.orc_set_threads(C.c_int(int(n)))
 
 
 def _f16_to_u16(a) -> np.ndarray:

@@ -538,6 +538,26 @@ void orc_matmul_int8(const float *A, const int8_t *q, const float *s, float *C, 
                      size_t N, int nthreads) {
 #ifdef _OPENMP
     int nt = nthreads > 0 ? nthreads : omp_get_max_threads();
+    if (M < (size_t)nt && nt > 1 && N >= 256) {
+        /* few rows: split the columns instead (each column's sum keeps its k
+         * order, so the result is the same bit for bit) */
+        const size_t nb = (N + 63) / 64;
+#pragma omp parallel for schedule(static) num_threads(nt)
+        for (size_t blk = 0; blk < nb; ++blk) {
+            const size_t n0 = blk * 64, n1 = n0 + 64 < N ? n0 + 64 : N;
+            for (size_t m = 0; m < M; ++m) {
+                float *c = C + m * N;
+                for (size_t n = n0; n < n1; ++n) c[n] = 0.0f;
+                for (size_t k = 0; k < K; ++k) {
+                    const float a = A[m * K + k];
+                    const int8_t *row = q + k * N;
+                    for (size_t n = n0; n < n1; ++n) c[n] += a * (float)row[n];
+                }
+                for (size_t n = n0; n < n1; ++n) c[n] *= s[n];
+            }
+        }
+        return;
+    }
 #pragma omp parallel for schedule(static) num_threads(nt)
 #endif
     for (size_t m = 0; m < M; ++m) {
@@ -739,5 +759,17 @@ int orc_num_threads(void) {
     return omp_get_max_threads();
 #else
     return 1;
+#endif
+}
+
+/* Set the OpenMP thread count of later parallel regions started by the
+ * calling thread (benchmark control: a launcher may have exported
+ * OMP_NUM_THREADS=1).  The reference's own library shares the OpenMP runtime,
+ * so this also sets the threads its gdn_* kernels use. */
+void orc_set_threads(int n) {
+#ifdef _OPENMP
+    if (n > 0) omp_set_num_threads(n);
+#else
+    (void)n;
 #endif
 }

@@ -251,15 +251,29 @@ __global__ void __launch_bounds__(TCT, 1)
     fence_before_sync();
     __syncthreads();
     if (warp == 0) tmem_dealloc(tmem, G::TMEM_COLS);
-    if (ksplit == 1 || bad) return;
-    // serial fix-up: the last CTA of the tile adds the K parts in order
+    if (ksplit == 1) return;
+    // serial fix-up: the last CTA of the tile adds the K parts in order.  A
+    // CTA whose wait ran out (bad) wrote no partials but still counts itself
+    // (adding a mark in the high half), so the counter always reaches ksplit
+    // and the last CTA resets it; when any part of the tile is missing the
+    // sum is skipped (the call has already recorded its timeout).
+    __shared__ bool s_skip;
     __threadfence();
     __syncthreads();
     const unsigned int tile = blockIdx.y * gridDim.x + blockIdx.x;
-    if (t == 0) s_last = atomicAdd(&ctr[tile], 1u) == (unsigned)ksplit - 1;
+    if (t == 0) {
+        const unsigned int mine = bad ? 0x10001u : 1u;
+        const unsigned int old = atomicAdd(&ctr[tile], mine);
+        s_last = (old & 0xFFFFu) == (unsigned)ksplit - 1;
+        s_skip = ((old + mine) >> 16) != 0u;
+    }
     __syncthreads();
     if (!s_last) return;
     __threadfence();
+    if (s_skip) {
+        if (t == 0) ctr[tile] = 0u;
+        return;
+    }
     if (n < N) {
         for (int i = wh; i < MT; i += TCT / 128) {
             const long long m = m0 + i;

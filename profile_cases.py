@@ -1,8 +1,8 @@
 """Small, self-terminating workloads for ncu captures of one kernel at a time.
 
-    python -m orionsbelt_b200.profile_cases decode [--launches 3]
-    python -m orionsbelt_b200.profile_cases chunk  [--launches 1]
-    python -m orionsbelt_b200.profile_cases conv | cumsum | scan | attn | int8
+    python profile_cases.py decode [--launches 3]
+    python profile_cases.py chunk  [--launches 1]
+    python profile_cases.py conv | cumsum | scan | attn | int8
 
 Each case holds a few hundred MB to a few GB on the device (inputs larger
 than the 126 MB L2, so DRAM counters mean something), runs a few launches of
@@ -21,10 +21,14 @@ its kernel through the C ABI, and exits.  Cases:
 from __future__ import annotations
 
 import argparse
+import sys
+from pathlib import Path
 
 import torch
 
-from . import _lib, ops, synth
+sys.path.insert(0, str(Path(__file__).resolve().parent))
+
+from orionsbelt_b200 import _lib, ops, synth  # noqa: E402
 
 
 def main() -> None:

@@ -27,6 +27,7 @@ from __future__ import annotations
 
 import importlib
 import importlib.util
+import os
 import sys
 from pathlib import Path
 
@@ -142,4 +143,8 @@ def main(ref_root: Path, only=None) -> None:
 
 if __name__ == "__main__":
     # python make_golden.py [reference root] [fixture names to (re)write only]
-    main(Path(sys.argv[1]) if len(sys.argv) > 1 else Path("/root/reference"), set(sys.argv[2:]) or None)
+    # (the root defaults to the ORIONSBELT_REF environment variable)
+    root = sys.argv[1] if len(sys.argv) > 1 else os.environ.get("ORIONSBELT_REF")
+    if not root:
+        sys.exit("usage: make_golden.py <reference root> [names]  (or set ORIONSBELT_REF)")
+    main(Path(root), set(sys.argv[2:]) or None)
