@@ -214,6 +214,9 @@ def run_ours(args):
     # ---- chunk scan (config-2 shard) on this GPU
     chunk = None if args.no_chunk else run_chunk_bench(args, world, barrier, peaks, seed)
 
+    # ---- strong scaling: the fixed global problems split over the ranks
+    strong = run_strong(args, world, rank, barrier, peaks)
+
     # ---- every other hot-path row on its own configuration (this GPU)
     rows = None if (args.no_rows or world > 1) else run_rows(args, peaks)
 
@@ -265,6 +268,7 @@ def run_ours(args):
             "gpu_launches": K * c["layers"],
             "clocks": clk.summary(),
             "chunk_scan": chunk,
+            "strong_scaling": strong,
             "rows": rows,
             "cpu_baseline": cpu,
         }
@@ -301,6 +305,16 @@ def run_e2e_decode(args, layers, launch_layers, world, barrier, step_bytes):
             off += n
         return out
 
+    # Pinned buffers are first touched on the CPUs of the GPU's NUMA node (the
+    # process affinity is narrowed for the allocation and restored after).
+    numa = gpu_numa_node(torch.cuda.current_device())
+    saved_aff = None
+    if numa["cpus"]:
+        try:
+            saved_aff = os.sched_getaffinity(0)
+            os.sched_setaffinity(0, numa["cpus"])
+        except (AttributeError, OSError):
+            saved_aff = None
     sets = []
     for b in range(2):
         host_in = torch.empty(h2d, dtype=torch.uint8, pin_memory=True)
@@ -324,6 +338,8 @@ def run_e2e_decode(args, layers, launch_layers, world, barrier, step_bytes):
             launch_layers(arg_list)
         sets.append(dict(host_in=host_in, dev_in=dev_in, host_out=host_out, dev_out=dev_out, graph=g,
                          args=arg_list))
+    if saved_aff is not None:
+        os.sched_setaffinity(0, saved_aff)
     compute = torch.cuda.current_stream()
     up, down = torch.cuda.Stream(), torch.cuda.Stream()
     done = [torch.cuda.Event(), torch.cuda.Event()]
@@ -371,8 +387,33 @@ def run_e2e_decode(args, layers, launch_layers, world, barrier, step_bytes):
         ms = t.item()
     for st in sets:
         del st["graph"]
+    # The host copies alone, each timed on its own stream (max over ranks):
+    # the per-rank and aggregate host-link rates that bound this leg.
+    copies = {}
+    for name, fn, nbytes, stream in (("h2d", lambda st: st["dev_in"].copy_(st["host_in"], non_blocking=True), h2d, up),
+                                     ("d2h", lambda st: st["host_out"].copy_(st["dev_out"], non_blocking=True), d2h,
+                                      down)):
+        barrier()
+        c0, c1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        reps = 5
+        with torch.cuda.stream(stream):
+            c0.record(stream)
+            for r in range(reps):
+                fn(sets[r % 2])
+            c1.record(stream)
+        torch.cuda.synchronize()
+        cms = c0.elapsed_time(c1) / reps
+        if world > 1:
+            import torch.distributed as dist
+            t = torch.tensor([cms], device="cuda")
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            cms = t.item()
+        copies[name] = {"bytes": nbytes, "ms": round(cms, 4), "gbs_per_rank": round(nbytes / (cms / 1e3) / 1e9, 2),
+                        "gbs_all_ranks": round(world * nbytes / (cms / 1e3) / 1e9, 1)}
+    barrier()
     return {"value": round(step_bytes * args.steps * world / (ms / 1e3) / 1e9, 1), "unit": "GB/s",
             "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "ms_per_step": round(ms / args.steps, 4),
+            "host_copies": copies, "numa_node": numa["node"],
             "path": "pinned host -> HBM copy, 24 C-ABI decode launches (CUDA graph), HBM -> pinned host copy; "
                     "uploads/downloads of neighbouring steps overlap compute on two copy streams"}
 
@@ -423,6 +464,100 @@ def run_chunk_bench(args, world, barrier, peaks, seed):
             "tensor_frac_of_bf16_peak": round(flops / world / (ms / 1e3) / 1e12 / peaks["bf16_tflops"], 4),
             "hbm_frac": round(nbytes / world / (ms / 1e3) / 1e9 / peaks["hbm_gbs"], 4),
             "l2": "256 MB buffer written, then a 256 MB buffer read, before each timed call"}
+
+
+def run_strong(args, world, rank, barrier, peaks):
+    """Strong scaling: the fixed global problem split over the ranks with
+    shard.batch_slice, no exchange (max over ranks of each rank's device time).
+      decode: config 1's B = 64 global sequences, 24 layers (64 / N per rank);
+      chunk:  config 2's B = 8 sequences x 32 value heads (8 / N per rank).
+    At N = 8 each rank holds one config-2 sequence (32 (b, h) units): the
+    sequential state pass per unit is what bounds that point."""
+    import torch
+    import torch.distributed as dist
+
+    from orionsbelt_b200 import _lib, ops, shard, synth
+
+    L = _lib.lib()
+    out = {}
+
+    def tmax(ms):
+        if world > 1:
+            t = torch.tensor([ms], device="cuda")
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            ms = t.item()
+        return ms
+
+    c = CFG1
+    b0, b1 = shard.batch_slice(c["B"], world, rank)
+    Bl = b1 - b0
+    layers = []
+    for layer in range(c["layers"]):
+        d = synth.device_gdn(Bl, 1, c["Hk"], c["Hv"], c["dk"], c["dv"], g_scale=0.1, seed=500 + layer,
+                             in_dtype=torch.bfloat16, state_std=0.02)
+        o = torch.empty((Bl, c["Hv"], c["dv"]), dtype=torch.bfloat16, device="cuda")
+        layers.append((d, o, ops.decode_args(d["S0"], d["q"][:, 0].contiguous(), d["k"][:, 0].contiguous(),
+                                             d["v"][:, 0].contiguous(), d["g"][:, 0].contiguous(),
+                                             d["beta"][:, 0].contiguous(), o, scale=1.0)))
+    launch = L.kai_run_gdn_delta_rule_decode_sm100a
+
+    def step():
+        sp = torch.cuda.current_stream().cuda_stream
+        for _, _, a in layers:
+            _lib.check(launch(a, sp))
+
+    step()
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        step()
+    for _ in range(args.warmup):
+        g.replay()
+    barrier()
+    K = args.steps
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(K):
+        g.replay()
+    e1.record()
+    torch.cuda.synchronize()
+    ms = tmax(e0.elapsed_time(e1) / K)
+    barrier()
+    del g
+    gbytes = metrics.decode_bytes(c["B"], c["Hk"], c["Hv"], c["dk"], c["dv"]) * c["layers"]
+    out["decode_cfg1"] = {"global_batch": c["B"], "batch_per_rank": Bl, "ms_per_step": round(ms, 4),
+                          "gbs": round(gbytes / (ms / 1e3) / 1e9, 1),
+                          "gbs_per_gpu": round(gbytes / world / (ms / 1e3) / 1e9, 1)}
+    del layers
+    torch.cuda.empty_cache()
+    if not args.no_chunk:
+        cc = CFG2_SHARD
+        b0, b1 = shard.batch_slice(cc["B"], world, rank)
+        Bl = b1 - b0
+        d = synth.device_gdn(Bl, cc["T"], cc["Hk"], cc["Hv"], cc["dk"], cc["dv"], g_scale=0.1, seed=600 + rank,
+                             in_dtype=torch.bfloat16)
+        o = torch.empty_like(d["v"])
+        S = d["S0"].clone()
+        a = ops.chunk_args(d["q"], d["k"], d["v"], d["g"], d["beta"], S, o, scale=1.0)
+        sp = torch.cuda.current_stream().cuda_stream
+        _lib.check(L.kai_run_gdn_chunk_delta_rule_sm100a(a, sp))
+        flush = L2Flush()
+        barrier()
+        flush()
+        e0.record()
+        _lib.check(L.kai_run_gdn_chunk_delta_rule_sm100a(a, sp))
+        e1.record()
+        torch.cuda.synchronize()
+        ms = tmax(e0.elapsed_time(e1))
+        barrier()
+        flops = metrics.chunk_flops(cc["B"], cc["T"], cc["Hv"], cc["dk"], 64)
+        out["chunk_cfg2"] = {"global_batch": cc["B"], "batch_per_rank": Bl, "units_per_rank": Bl * cc["Hv"],
+                             "ms": round(ms, 3), "tokens_per_s": round(cc["B"] * cc["T"] / (ms / 1e3), 1),
+                             "tflops": round(flops / (ms / 1e3) / 1e12, 2),
+                             "tensor_frac_per_gpu": round(flops / world / (ms / 1e3) / 1e12 / peaks["bf16_tflops"], 4)}
+        del d, o, S
+        torch.cuda.empty_cache()
+    return out
 
 
 class L2Flush:
@@ -662,6 +797,36 @@ def run_rows(args, peaks) -> dict:
         del d, oo, S0
     torch.cuda.empty_cache()
     return out
+
+
+def gpu_numa_node(device: int) -> dict:
+    """NUMA node of a GPU (from its PCI device in sysfs) and that node's CPUs
+    (empty when unknown)."""
+    import torch
+    try:
+        bus = torch.cuda.get_device_properties(device).pci_bus_id.lower()
+    except (AttributeError, RuntimeError):
+        return {"node": None, "cpus": set()}
+    parts = bus.split(":")
+    if len(parts[0]) == 8:  # 00000000:1b:00.0 -> 0000:1b:00.0
+        bus = parts[0][4:] + ":" + ":".join(parts[1:])
+    try:
+        node = int(Path(f"/sys/bus/pci/devices/{bus}/numa_node").read_text().strip())
+    except (OSError, ValueError):
+        return {"node": None, "cpus": set()}
+    cpus = set()
+    if node >= 0:
+        try:
+            for part in Path(f"/sys/devices/system/node/node{node}/cpulist").read_text().strip().split(","):
+                a, _, b = part.partition("-")
+                cpus.update(range(int(a), int(b or a) + 1))
+        except (OSError, ValueError):
+            cpus = set()
+    try:
+        cpus &= os.sched_getaffinity(0)
+    except AttributeError:
+        pass
+    return {"node": node, "cpus": cpus}
 
 
 def host_threads() -> int:
