@@ -297,6 +297,76 @@ KAI_GDN_API int kai_gdn_e2e_step(void *engine, const float *hidden_in, float *hi
 KAI_GDN_API int kai_gdn_e2e_state(void *engine, size_t layer, float *gdn_state, float *conv_hist);
 KAI_GDN_API int kai_gdn_e2e_destroy(void *engine);
 
+/* Decode engine of a Qwen3.5-style GDN hybrid, tensor
+ * parallel over NCCL.  No single reference counterpart: it runs the layer
+ * structure of the reference's model notes (docs/GDN_ARCHITECTURE_AUDIT.md
+ * sections 2-3) in the block order of its decode loop
+ * (gdn_e2e_decode.c:2775-2796), on this library's kernels:
+ *   - GDN layers: in-projection, Conv1D + SiLU, L2-normalised q / k, the
+ *     decode step, gated RMSNorm, out-projection;
+ *   - attention layers: q / gate / k / v, per-head RMSNorm, partial RoPE,
+ *     GQA decode over a bf16 KV cache, sigmoid gate, o-projection;
+ *   - each layer's SwiGLU FFN after RMSNorm;
+ *   - embedding, final RMSNorm, LM head and greedy argmax.
+ * All projections are int8 with per-column scales (quantize_weight,
+ * gdn_e2e_decode.c:175-199).  The weights are N(0, weight_std) from `seed`,
+ * generated on the device; norm weights are 1 + N(0, weight_std).  With
+ * tp_size > 1 each rank holds its heads, FFN columns and vocabulary shard,
+ * and the output projections meet in NCCL all-reduces (two per layer, over
+ * [batch][hidden]).  The engine loads libnccl.so.2 at run time. */
+#define KAI_GDN_NCCL_ID_BYTES 128
+typedef struct kai_gdn_model_config {
+    size_t hidden, layers, vocab, inter;           /* 2560, 32, 151936, 9216 for config 4 */
+    const unsigned char *is_gdn;                   /* [layers]: 1 GDN, 0 attention (host)  */
+    size_t gdn_heads_k, gdn_heads_v, gdn_head_dim; /* 16, 32, 128                          */
+    size_t attn_heads, attn_kv_heads, attn_head_dim, rope_dims; /* 16, 4, 256, 64          */
+    float rope_theta, rms_eps;
+    size_t batch, max_ctx;                         /* sequences; KV cache capacity (tokens) */
+    int tp_rank, tp_size;                          /* tensor-parallel position              */
+    const void *nccl_id;                           /* KAI_GDN_NCCL_ID_BYTES, same on every rank (tp_size > 1) */
+    unsigned long long seed;
+    float weight_std;                              /* 0: 0.02                               */
+} kai_gdn_model_config;
+/* A fresh NCCL unique id (rank 0 makes it and shares it with the others). */
+KAI_GDN_API int kai_gdn_model_nccl_id(void *id_out);
+KAI_GDN_API int kai_gdn_model_create(const kai_gdn_model_config *cfg, void **engine);
+/* One greedy decode step of every sequence at position `pos` (0-based): reads
+ * the engine's current tokens [batch], leaves the argmax tokens in their
+ * place.  Stream-ordered; the first step on a stream runs eagerly, the
+ * second captures the per-segment CUDA graphs, later ones replay them. */
+KAI_GDN_API int kai_gdn_model_step(void *engine, size_t pos, void *stream);
+/* Set (set = 1) or read (set = 0) the current tokens [batch] (int32, host or
+ * device memory); synchronises the device. */
+KAI_GDN_API int kai_gdn_model_tokens(void *engine, int32_t *tokens, int set);
+#define KAI_GDN_MODEL_HIDDEN 0 /* [batch][hidden] residual stream after the last step */
+#define KAI_GDN_MODEL_LOGITS 1 /* [batch][vocab / tp_size] this rank's logits         */
+KAI_GDN_API int kai_gdn_model_read(void *engine, int what, float *out);
+/* Copy out this rank's weight `which` of `layer` (for a checker): int8 codes
+ * [rows][cols] and fp32 scales [cols] of a projection (the embedding:
+ * [vocab][hidden] codes, one scale per row), or an fp32 vector (rows = 1).
+ * data / scales may be NULL to query the shape. */
+#define KAI_GDN_MODEL_W_IN 0        /* GDN [q|k|v|z|b|a|pad], attention [q,gate per head|k|v] */
+#define KAI_GDN_MODEL_W_OUT 1       /* GDN out / attention o projection (this rank's rows)    */
+#define KAI_GDN_MODEL_W_GATE_UP 2   /* FFN [gate | up]                                        */
+#define KAI_GDN_MODEL_W_DOWN 3      /* FFN down (this rank's rows)                            */
+#define KAI_GDN_MODEL_V_NORM_IN 4
+#define KAI_GDN_MODEL_V_NORM_POST 5
+#define KAI_GDN_MODEL_V_CONV 6      /* [4][channels]                                          */
+#define KAI_GDN_MODEL_V_A_LOG 7
+#define KAI_GDN_MODEL_V_DT_BIAS 8
+#define KAI_GDN_MODEL_V_NORM_GDN 9
+#define KAI_GDN_MODEL_V_NORM_Q 10
+#define KAI_GDN_MODEL_V_NORM_K 11
+#define KAI_GDN_MODEL_W_LM 12       /* [hidden][vocab / tp_size]                              */
+#define KAI_GDN_MODEL_V_NORM_FINAL 13
+#define KAI_GDN_MODEL_W_EMBED 14
+KAI_GDN_API int kai_gdn_model_weight(void *engine, size_t layer, int which, void *data, float *scales,
+                                     size_t *rows, size_t *cols);
+/* Synthetic state of `ctx` already-consumed tokens: KV cache rows [0, ctx)
+ * N(0, 1) in bf16, GDN states N(0, 0.02), conv histories N(0, 1). */
+KAI_GDN_API int kai_gdn_model_fill(void *engine, size_t ctx, unsigned long long seed);
+KAI_GDN_API int kai_gdn_model_destroy(void *engine);
+
 /* Chunkwise (WY / UT-transform) gated delta-rule scan over a whole sequence,
  * for every (batch, value head), chunk length `chunk` (64).  Equal, up to
  * rounding, to applying the decode step above for t = 0 .. seq-1 with

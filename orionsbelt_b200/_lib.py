@@ -54,6 +54,15 @@ class E2EWeights(C.Structure):
                                    "f_k_proj", "f_v_proj", "f_o_proj", "gate_proj", "up_proj", "down_proj")]
 
 
+class ModelConfig(C.Structure):
+    """struct kai_gdn_model_config."""
+    _fields_ = [("hidden", _sz), ("layers", _sz), ("vocab", _sz), ("inter", _sz), ("is_gdn", _vp),
+                ("gdn_heads_k", _sz), ("gdn_heads_v", _sz), ("gdn_head_dim", _sz), ("attn_heads", _sz),
+                ("attn_kv_heads", _sz), ("attn_head_dim", _sz), ("rope_dims", _sz), ("rope_theta", _f),
+                ("rms_eps", _f), ("batch", _sz), ("max_ctx", _sz), ("tp_rank", _i), ("tp_size", _i),
+                ("nccl_id", _vp), ("seed", C.c_ulonglong), ("weight_std", _f)]
+
+
 class ChunkArgs(C.Structure):
     """struct kai_gdn_chunk_args."""
     _fields_ = [("q", _vp), ("k", _vp), ("v", _vp), ("g", _vp), ("beta", _vp), ("state", _vp), ("o", _vp),
@@ -95,6 +104,14 @@ SIGNATURES = {
     "kai_gdn_e2e_destroy": (_i, [_vp]),
     "kai_run_gdn_matmul_int8_sm100a": (_i, [_vp, _vp, _vp, _vp, _sz, _sz, _sz, _vp]),
     "kai_run_gdn_chunk_delta_rule_sm100a": (_i, [C.POINTER(ChunkArgs), _vp]),
+    "kai_gdn_model_nccl_id": (_i, [_vp]),
+    "kai_gdn_model_create": (_i, [C.POINTER(ModelConfig), C.POINTER(_vp)]),
+    "kai_gdn_model_step": (_i, [_vp, _sz, _vp]),
+    "kai_gdn_model_tokens": (_i, [_vp, _vp, _i]),
+    "kai_gdn_model_read": (_i, [_vp, _i, _vp]),
+    "kai_gdn_model_weight": (_i, [_vp, _sz, _i, _vp, _vp, C.POINTER(_sz), C.POINTER(_sz)]),
+    "kai_gdn_model_fill": (_i, [_vp, _sz, C.c_ulonglong]),
+    "kai_gdn_model_destroy": (_i, [_vp]),
     # control
     "kai_gdn_cuda_set_device": (_i, [_i]),
     "kai_gdn_cuda_device_count": (_i, []),

@@ -59,6 +59,14 @@ int e2e_create(const kai_gdn_e2e_config *cfg, const kai_gdn_e2e_weights *w, void
 int e2e_step(void *engine, const float *hidden_in, float *hidden_out, cudaStream_t st);
 int e2e_state(void *engine, size_t layer, float *gdn_state, float *conv_hist);
 int e2e_destroy(void *engine);
+int model_nccl_id(void *out);
+int model_create(const kai_gdn_model_config *cfg, void **out);
+int model_step(void *engine, size_t pos, cudaStream_t st);
+int model_tokens(void *engine, int *tokens, int set);
+int model_read(void *engine, int what, float *out);
+int model_weight(void *engine, size_t layer, int which, void *data, float *scales, size_t *rows, size_t *cols);
+int model_fill(void *engine, size_t ctx, unsigned long long seed);
+int model_destroy(void *engine);
 int launch_quantize_int8(const float *B, int8_t *q, float *s, size_t K, size_t N, cudaStream_t st);
 int launch_matmul_int8(const float *A, const int8_t *q, const float *s, float *C, size_t M, size_t K, size_t N,
                        cudaStream_t st);

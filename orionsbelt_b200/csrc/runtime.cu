@@ -411,6 +411,20 @@ int kai_gdn_e2e_state(void *engine, size_t layer, float *gdn_state, float *conv_
 
 int kai_gdn_e2e_destroy(void *engine) { return e2e_destroy(engine); }
 
+int kai_gdn_model_nccl_id(void *id_out) { return model_nccl_id(id_out); }
+int kai_gdn_model_create(const kai_gdn_model_config *cfg, void **engine) { return model_create(cfg, engine); }
+int kai_gdn_model_step(void *engine, size_t pos, void *stream) {
+    return model_step(engine, pos, (cudaStream_t)stream);
+}
+int kai_gdn_model_tokens(void *engine, int32_t *tokens, int set) { return model_tokens(engine, tokens, set); }
+int kai_gdn_model_read(void *engine, int what, float *out) { return model_read(engine, what, out); }
+int kai_gdn_model_weight(void *engine, size_t layer, int which, void *data, float *scales, size_t *rows,
+                         size_t *cols) {
+    return model_weight(engine, layer, which, data, scales, rows, cols);
+}
+int kai_gdn_model_fill(void *engine, size_t ctx, unsigned long long seed) { return model_fill(engine, ctx, seed); }
+int kai_gdn_model_destroy(void *engine) { return model_destroy(engine); }
+
 int kai_run_gdn_quantize_int8_sm100a(const float *B, int8_t *q, float *s, size_t K, size_t N, void *stream) {
     return launch_quantize_int8(B, q, s, K, N, (cudaStream_t)stream);
 }

@@ -249,6 +249,91 @@ class E2EEngine:
             pass
 
 
+class ModelEngine:
+    """Decode engine of a Qwen3.5-style GDN hybrid (kai_gdn_model_*), optionally
+    tensor-parallel: `geom` is a dict of the kai_gdn_model_config fields
+    (hidden, layers, vocab, inter, is_gdn, gdn_heads_k, gdn_heads_v, gdn_head_dim,
+    attn_heads, attn_kv_heads, attn_head_dim, rope_dims, rope_theta, rms_eps,
+    max_ctx, weight_std); tp_rank / tp_size / nccl_id place it in a
+    tensor-parallel group (nccl_id: bytes from nccl_id())."""
+
+    W_IN, W_OUT, W_GATE_UP, W_DOWN = 0, 1, 2, 3
+    V_NORM_IN, V_NORM_POST, V_CONV, V_A_LOG, V_DT_BIAS, V_NORM_GDN, V_NORM_Q, V_NORM_K = 4, 5, 6, 7, 8, 9, 10, 11
+    W_LM, V_NORM_FINAL, W_EMBED = 12, 13, 14
+
+    @staticmethod
+    def nccl_id() -> bytes:
+        import ctypes as C
+        buf = C.create_string_buffer(128)
+        check(lib().kai_gdn_model_nccl_id(buf))
+        return buf.raw
+
+    def __init__(self, geom: dict, batch: int, seed: int = 1, tp_rank: int = 0, tp_size: int = 1,
+                 nccl_id: bytes | None = None):
+        import ctypes as C
+        g = dict(geom)
+        self._is_gdn = np.ascontiguousarray(g.pop("is_gdn"), dtype=np.uint8)
+        self._nid = C.create_string_buffer(nccl_id, 128) if nccl_id is not None else None
+        self.batch = int(batch)
+        self.geom = dict(geom)
+        cfg = _lib.ModelConfig(g["hidden"], len(self._is_gdn), g["vocab"], g["inter"], self._is_gdn.ctypes.data,
+                               g["gdn_heads_k"], g["gdn_heads_v"], g["gdn_head_dim"], g["attn_heads"],
+                               g["attn_kv_heads"], g["attn_head_dim"], g["rope_dims"], float(g["rope_theta"]),
+                               float(g["rms_eps"]), self.batch, g["max_ctx"], int(tp_rank), int(tp_size),
+                               C.cast(self._nid, C.c_void_p) if self._nid is not None else None, int(seed),
+                               float(g.get("weight_std", 0.0)))
+        h = C.c_void_p()
+        check(lib().kai_gdn_model_create(C.byref(cfg), C.byref(h)))
+        self._h = h
+
+    def set_tokens(self, tokens) -> None:
+        t = np.ascontiguousarray(tokens, dtype=np.int32)
+        check(lib().kai_gdn_model_tokens(self._h, t.ctypes.data, 1))
+
+    def tokens(self) -> np.ndarray:
+        t = np.empty(self.batch, np.int32)
+        check(lib().kai_gdn_model_tokens(self._h, t.ctypes.data, 0))
+        return t
+
+    def step(self, pos: int, stream=None) -> None:
+        check(lib().kai_gdn_model_step(self._h, int(pos), _stream(stream)))
+
+    def read(self, what: int, shape) -> np.ndarray:
+        out = np.empty(shape, np.float32)
+        check(lib().kai_gdn_model_read(self._h, what, out.ctypes.data))
+        return out
+
+    def weight(self, layer: int, which: int):
+        """(codes or vector, scales or None) of this rank's weight `which` of `layer`."""
+        import ctypes as C
+        rows, cols = C.c_size_t(), C.c_size_t()
+        check(lib().kai_gdn_model_weight(self._h, layer, which, None, None, C.byref(rows), C.byref(cols)))
+        r, c = rows.value, cols.value
+        if which in (self.W_IN, self.W_OUT, self.W_GATE_UP, self.W_DOWN, self.W_LM, self.W_EMBED):
+            q = np.empty((r, c), np.int8)
+            s = np.empty(r if which == self.W_EMBED else c, np.float32)
+            check(lib().kai_gdn_model_weight(self._h, layer, which, q.ctypes.data, s.ctypes.data, C.byref(rows),
+                                             C.byref(cols)))
+            return q, s
+        v = np.empty(c, np.float32)
+        check(lib().kai_gdn_model_weight(self._h, layer, which, v.ctypes.data, None, C.byref(rows), C.byref(cols)))
+        return v, None
+
+    def fill(self, ctx: int, seed: int = 7) -> None:
+        check(lib().kai_gdn_model_fill(self._h, int(ctx), int(seed)))
+
+    def close(self) -> None:
+        if self._h:
+            lib().kai_gdn_model_destroy(self._h)
+            self._h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
 def decode_args(state, q, k, v, g, beta, o, scale: float) -> _lib.DecodeArgs:
     """Pack struct kai_gdn_decode_args from tensors:
     state [B][Hv][dk][dv], q,k [B][Hk][dk], v [B][Hv][dv], g,beta [B][Hv], o [B][Hv][dv]."""
