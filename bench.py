@@ -54,6 +54,7 @@ def parse():
     ap.add_argument("--no-chunk", action="store_true", help="skip the chunk-scan measurement")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline sample")
     ap.add_argument("--no-rows", action="store_true", help="skip the per-row measurements")
+    ap.add_argument("--no-model", action="store_true", help="skip the config-4 model decode")
     return ap.parse_args()
 
 
@@ -217,6 +218,9 @@ def run_ours(args):
     # ---- strong scaling: the fixed global problems split over the ranks
     strong = run_strong(args, world, rank, barrier, peaks)
 
+    # ---- config 4: the hybrid model's decode, tensor-parallel over the ranks
+    model = None if args.no_model else run_model(args, world, rank, barrier, peaks)
+
     # ---- every other hot-path row on its own configuration (this GPU)
     rows = None if (args.no_rows or world > 1) else run_rows(args, peaks)
 
@@ -269,6 +273,7 @@ def run_ours(args):
             "clocks": clk.summary(),
             "chunk_scan": chunk,
             "strong_scaling": strong,
+            "model_config4": model,
             "rows": rows,
             "cpu_baseline": cpu,
         }
@@ -557,6 +562,82 @@ def run_strong(args, world, rank, barrier, peaks):
                              "tensor_frac_per_gpu": round(flops / world / (ms / 1e3) / 1e12 / peaks["bf16_tflops"], 4)}
         del d, o, S
         torch.cuda.empty_cache()
+    return out
+
+
+CFG4 = dict(hidden=2560, vocab=151936, inter=9216, is_gdn=[1, 1, 1, 0] * 8, gdn_heads_k=16, gdn_heads_v=32,
+            gdn_head_dim=128, attn_heads=16, attn_kv_heads=4, attn_head_dim=256, rope_dims=64, rope_theta=1e7,
+            rms_eps=1e-6, weight_std=0.02)
+
+
+def run_model(args, world, rank, barrier, peaks, ctx=32768, steps=256):
+    """BASELINE config 4 decode: the Qwen3.5-4B-style hybrid (kai_gdn_model_*),
+    tensor-parallel over all ranks (NCCL all-reduce after every output
+    projection, all-gather of the argmax), 256 greedy steps at batch 1 and 16
+    after a `ctx`-token context.  The context's KV cache and GDN states are
+    synthetic (kai_gdn_model_fill): the 32k prefill itself is not run.  Device
+    time of the 256 steps (CUDA events, max over ranks); the generated tokens
+    are read back to the host once, after the last step."""
+    import torch
+    import torch.distributed as dist
+
+    from orionsbelt_b200 import ops
+
+    out = {}
+    nid = None
+    if world > 1:
+        box = [ops.ModelEngine.nccl_id() if rank == 0 else None]
+        dist.broadcast_object_list(box, src=0)
+        nid = box[0]
+    geom = dict(CFG4, max_ctx=ctx + steps + 8)
+    H, L = geom["hidden"], len(geom["is_gdn"])
+    # int8 weight bytes one token streams on each GPU (all layers + LM head), for the roofline
+    d, hk, hv, D, hq, hkv_g, I, V = 128, 16, 32, 256, 16, 4, 9216, 151936
+    gdn_in = H * ((2 * hk + 2 * hv) * d + 2 * hv)
+    gdn_w = gdn_in + hv * d * H
+    att_w = H * (hq * 2 * D + 2 * hkv_g * D) + hq * D * H
+    ffn_w = 3 * H * I
+    tok_bytes = (24 * (gdn_w + ffn_w) + 8 * (att_w + ffn_w) + H * V) / world
+    stream = torch.cuda.Stream()
+    for B in (1, 16):
+        eng = ops.ModelEngine(geom, B, seed=42, tp_rank=rank, tp_size=world, nccl_id=nid)
+        eng.fill(ctx, seed=3)
+        eng.set_tokens(np.random.default_rng(9).integers(0, geom["vocab"], B).astype(np.int32))
+        barrier()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        with torch.cuda.stream(stream):
+            for w in range(3):  # eager step, graph capture, one replay
+                eng.step(ctx + w, stream)
+            stream.synchronize()
+            barrier()
+            e0.record(stream)
+            for i in range(steps):
+                eng.step(ctx + 3 + i, stream)
+            e1.record(stream)
+            stream.synchronize()
+        ms = e0.elapsed_time(e1)
+        if world > 1:
+            t = torch.tensor([ms], device="cuda")
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            ms = t.item()
+        toks = eng.tokens()
+        per = ms / steps
+        out[f"b{B}"] = {"batch": B, "steps": steps, "ms_per_step": round(per, 4),
+                        "tokens_per_s": round(B * steps / (ms / 1e3), 1),
+                        "weight_gbs_per_gpu": round(tok_bytes / (per / 1e3) / 1e9, 1),
+                        "weight_hbm_frac": round(tok_bytes / (per / 1e3) / 1e9 / peaks["hbm_gbs"], 4),
+                        "last_tokens": [int(x) for x in toks[:4]]}
+        eng.close()
+        del eng
+        torch.cuda.empty_cache()
+        barrier()
+    out.update({"workload": f"config 4: Qwen3.5-4B-style hybrid (hidden 2560, 24 GDN + 8 gated-GQA layers, FFN "
+                            f"9216, vocab 151936, int8 weights, bf16 KV cache), greedy decode of {steps} tokens "
+                            f"after a {ctx}-token context (KV cache and GDN states synthetic; the prefill is not "
+                            f"run), tensor-parallel x{world} over NCCL",
+                "kernels": "int8 matmul (stream / tensor-core), decode_step_kernel, attn_tc_kernel, model "
+                           "elementwise kernels; per-segment CUDA graphs",
+                "weight_bytes_per_token_per_gpu": int(tok_bytes)})
     return out
 
 
