@@ -70,6 +70,11 @@ int model_destroy(void *engine);
 int launch_quantize_int8(const float *B, int8_t *q, float *s, size_t K, size_t N, cudaStream_t st);
 int launch_matmul_int8(const float *A, const int8_t *q, const float *s, float *C, size_t M, size_t K, size_t N,
                        cudaStream_t st);
+// Weight-streaming GEMV for M <= 4 (gemv.cu), launched as a programmatic
+// dependent of the previous kernel on the stream.
+bool gemv_int8_supported(size_t M, size_t K, size_t N, const int8_t *q);
+int launch_gemv_int8(const float *A, const int8_t *q, const float *s, float *C, size_t M, size_t K, size_t N,
+                     cudaStream_t st);
 int launch_matmul_int8_tc(const float *A, const int8_t *q, const float *s, float *C, size_t M, size_t K, size_t N,
                           cudaStream_t st);
 // Per-stream split-K workspace of the int8 matmuls: slab counters (zero

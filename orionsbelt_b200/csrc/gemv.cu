@@ -1,0 +1,359 @@
+// gemv.cu -- int8-weight GEMV for the decode shapes (M <= 4 activation rows),
+// C = (A q) diag(s) with q [K][N] int8 and one fp32 scale per column (the
+// reference's gemv_int8_neon / gemm_int8_neon, gdn_e2e_decode.c:296-358,
+// 608-678), streamed from HBM at the copy rate.
+//
+// Layout of the work: a warp owns 512 columns (16 per lane, one 16-byte load
+// per weight row) and a K range; the 8 warps of a CTA take interleaved rows of
+// the CTA's K range and add their sums through shared memory; CTAs split K so
+// that the grid covers every SM twice, and the K parts meet in a fix-up by the
+// last CTA of a column tile, in K order (deterministic).  Each thread keeps 8
+// weight rows (128 bytes) in flight in registers, loaded with non-allocating
+// read-only loads, while it converts and accumulates the previous 8: int8 ->
+// fp32 exactly (the byte, biased by 128, in the mantissa of 2^23; packed pair
+// subtraction) and packed fp32 multiply-adds.
+//
+// Programmatic dependent launch: the kernel may start while the kernel before
+// it on the stream is still running.  Weights never depend on earlier work, so
+// every CTA issues its first weight loads, allows its own dependents to launch,
+// and only then waits (griddepcontrol.wait) for the preceding grid before it
+// reads the activations.  The K-part workspace alternates between two halves
+// from one launch to the next on a stream, so a dependent that overlaps this
+// kernel's fix-up never writes the partial sums being read.
+#include <algorithm>
+#include <mutex>
+#include <vector>
+
+#include "gdn_internal.cuh"
+#include "tma.cuh"
+#include "umma.cuh"
+
+namespace gdn {
+namespace {
+
+constexpr int GW = 8;            // consumer warps per CTA
+constexpr int GCOLS = 512;       // columns per CTA (32 lanes x 16)
+constexpr int KT = 32;           // weight rows per ring stage
+constexpr int NSTG = 6;          // ring depth: 6 x 16 KB in flight per CTA
+constexpr int GNT = GW * 32 + 32;  // + one producer warp
+constexpr int STAGE = KT * GCOLS;  // bytes
+
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
+// Four signed bytes of w as two float2 pairs, exact.
+__device__ __forceinline__ void deq4x2(uint32_t w, float2 &a, float2 &b) {
+    const uint32_t u = w ^ 0x80808080u;
+    const float2 nbias = make_float2(-8388736.0f, -8388736.0f);  // -(2^23 + 128), exact sums
+    a = __fadd2_rn(make_float2(__uint_as_float(__byte_perm(u, 0x4B000000u, 0x7650)),
+                               __uint_as_float(__byte_perm(u, 0x4B000000u, 0x7651))),
+                   nbias);
+    b = __fadd2_rn(make_float2(__uint_as_float(__byte_perm(u, 0x4B000000u, 0x7652)),
+                               __uint_as_float(__byte_perm(u, 0x4B000000u, 0x7653))),
+                   nbias);
+}
+
+// acc[m][0..7] (float2 pairs of 16 columns) += a[m] * row
+template <int MB>
+__device__ __forceinline__ void accumulate(float2 (&acc)[MB][8], const uint4 w, const float *a) {
+    const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+        float2 p0, p1;
+        deq4x2(ws[j], p0, p1);
+#pragma unroll
+        for (int m = 0; m < MB; ++m) {
+            const float2 am = make_float2(a[m], a[m]);
+            acc[m][2 * j] = __ffma2_rn(am, p0, acc[m][2 * j]);
+            acc[m][2 * j + 1] = __ffma2_rn(am, p1, acc[m][2 * j + 1]);
+        }
+    }
+}
+
+__device__ __forceinline__ void tma_rows(unsigned char *dst, const CUtensorMap *map, int x, int y, uint64_t *bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];"
+        ::"r"(umma::smem_addr(dst)), "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y),
+        "r"(umma::smem_addr(bar))
+        : "memory");
+}
+
+// Grid (ceil(N / 512), ksplit).  A [M][K], q [K][N] (through `map`: boxes of
+// 256 columns x 32 rows), s [N], C [M][N]; part [ksplit][M][N] and ctr
+// [tiles] (zero between calls) when ksplit > 1.  Warp 8 (one lane) fills a
+// six-deep ring of 32-row x 512-column stages by TMA; warps 0-7 take four
+// rows of each stage, each lane 16 columns.
+template <int MB>
+__global__ void __launch_bounds__(GNT) gemv_int8_kernel(const __grid_constant__ CUtensorMap map,
+                                                        const float *__restrict__ A, const float *__restrict__ s,
+                                                        float *__restrict__ C, int M, long long K, long long N,
+                                                        long long kper, float *__restrict__ part,
+                                                        unsigned int *__restrict__ ctr, int *err) {
+    extern __shared__ unsigned char dsm_raw[];
+    unsigned char *ring = dsm_raw + ((1024u - (umma::smem_addr(dsm_raw) & 1023u)) & 1023u);  // [NSTG][STAGE]
+    float *sm_a = reinterpret_cast<float *>(ring + NSTG * STAGE);                          // [MB][kper]
+    // after the ring has been drained: one row m at a time, [warp][column % 16][column / 16]
+    float(*red)[16][32] = reinterpret_cast<float(*)[16][32]>(ring);
+    __shared__ uint64_t full[NSTG], empty[NSTG];
+    __shared__ bool s_last;
+    const int t = threadIdx.x, w = t / 32, lane = t % 32;
+    const int ksplit = (int)gridDim.y, rank = (int)blockIdx.y;
+    const long long tile0 = (long long)blockIdx.x * GCOLS;
+    const long long k0 = (long long)rank * kper, k1 = min(K, k0 + kper);
+    const int nk = k1 > k0 ? (int)((k1 - k0 + KT - 1) / KT) : 0;
+
+    if (t == 0) {
+        for (int i = 0; i < NSTG; ++i) {
+            umma::mbar_init(&full[i], 1);
+            umma::mbar_init(&empty[i], GW);
+        }
+    }
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    __syncthreads();
+    int issued = 0;
+    bool bad = false;
+    if (w == GW) {
+        // ---- producer: weights never depend on earlier kernels, so the
+        // first stages are issued before the dependency wait
+        if (lane == 0) {
+            for (; issued < nk && issued < NSTG; ++issued) {
+                umma::mbar_arrive_expect_tx(&full[issued], STAGE);
+                tma_rows(ring + issued * STAGE, &map, (int)tile0, (int)(k0 + issued * KT), &full[issued]);
+                tma_rows(ring + issued * STAGE + STAGE / 2, &map, (int)tile0 + 256, (int)(k0 + issued * KT),
+                         &full[issued]);
+            }
+        }
+        pdl_trigger();
+        if (lane == 0) {
+            for (; issued < nk && !bad; ++issued) {
+                const int st = issued % NSTG;
+                if (!umma::mbar_wait(&empty[st], (uint32_t)(((issued / NSTG) - 1) & 1), err)) {
+                    bad = true;
+                    break;
+                }
+                umma::mbar_arrive_expect_tx(&full[st], STAGE);
+                tma_rows(ring + st * STAGE, &map, (int)tile0, (int)(k0 + issued * KT), &full[st]);
+                tma_rows(ring + st * STAGE + STAGE / 2, &map, (int)tile0 + 256, (int)(k0 + issued * KT), &full[st]);
+            }
+            // every issued load lands before the CTA may leave
+            for (int i = issued - NSTG > 0 ? issued - NSTG : 0; i < issued; ++i)
+                umma::mbar_wait(&full[i % NSTG], (uint32_t)((i / NSTG) & 1), err);
+        }
+        __syncwarp();
+    } else {
+        pdl_trigger();
+        pdl_wait();
+        // this CTA's activations
+        const long long kn = k1 > k0 ? k1 - k0 : 0;
+        for (long long e = t; e < (long long)MB * kn; e += GW * 32) {
+            const int m = (int)(e / kn);
+            const long long k = e % kn;
+            sm_a[(long long)m * kper + k] = m < M ? A[(long long)m * K + k0 + k] : 0.f;
+        }
+        asm volatile("bar.sync 1, %0;" ::"n"(GW * 32) : "memory");
+        float2 acc[MB][8];
+#pragma unroll
+        for (int m = 0; m < MB; ++m)
+#pragma unroll
+            for (int j = 0; j < 8; ++j) acc[m][j] = make_float2(0.f, 0.f);
+        const int box = lane / 16, cw = lane % 16;
+        for (int i = 0; i < nk; ++i) {
+            const int st = i % NSTG;
+            if (!umma::mbar_wait(&full[st], (uint32_t)((i / NSTG) & 1), err)) bad = true;
+            if (__any_sync(0xffffffffu, bad)) break;
+            const unsigned char *sb = ring + st * STAGE + box * (STAGE / 2) + cw * 16;
+            uint4 wv[KT / GW];
+#pragma unroll
+            for (int j = 0; j < KT / GW; ++j) wv[j] = *reinterpret_cast<const uint4 *>(sb + (w + GW * j) * 256);
+            __syncwarp();
+            if (lane == 0) asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(umma::smem_addr(&empty[st])) : "memory");
+#pragma unroll
+            for (int j = 0; j < KT / GW; ++j) {
+                const long long rr = k0 + (long long)i * KT + w + GW * j;
+                if (rr < k1) {
+                    float a[MB];
+#pragma unroll
+                    for (int m = 0; m < MB; ++m) a[m] = sm_a[(long long)m * kper + (rr - k0)];
+                    accumulate<MB>(acc, wv[j], a);
+                }
+            }
+        }
+        // add the 8 warps' sums one activation row at a time (in the drained
+        // ring); thread e takes column (e % 32) * 16 + e / 32 of the tile
+        asm volatile("bar.sync 1, %0;" ::"n"(GW * 32) : "memory");
+#pragma unroll
+        for (int m = 0; m < MB; ++m) {
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+                red[w][2 * j][lane] = acc[m][j].x;
+                red[w][2 * j + 1][lane] = acc[m][j].y;
+            }
+            asm volatile("bar.sync 1, %0;" ::"n"(GW * 32) : "memory");
+            for (int e = t; e < GCOLS; e += GW * 32) {
+                const int jj = e / 32, ln = e % 32;
+                const long long n = tile0 + ln * 16 + jj;
+                float v = 0.f;
+#pragma unroll
+                for (int ww = 0; ww < GW; ++ww) v += red[ww][jj][ln];
+                if (m < M && n < N) {
+                    if (ksplit == 1)
+                        C[(long long)m * N + n] = v * s[n];
+                    else
+                        part[((long long)rank * M + m) * N + n] = v;
+                }
+            }
+            asm volatile("bar.sync 1, %0;" ::"n"(GW * 32) : "memory");
+        }
+    }
+    if (ksplit == 1) return;
+    // K parts meet in the last CTA of the tile, in K order (a CTA whose wait
+    // ran out still counts itself, marked, so the counter always resets)
+    __threadfence();
+    __syncthreads();
+    bad = __syncthreads_or(bad);
+    if (t == 0) {
+        const unsigned int mine = bad ? 0x10001u : 1u;
+        const unsigned int old = atomicAdd(&ctr[blockIdx.x], mine);
+        s_last = (old & 0xFFFFu) == (unsigned)ksplit - 1;
+        if (s_last && ((old + mine) >> 16) != 0u) {
+            ctr[blockIdx.x] = 0u;
+            s_last = false;
+        }
+    }
+    __syncthreads();
+    if (!s_last) return;
+    __threadfence();
+    for (int e = t; e < MB * GCOLS; e += GNT) {
+        const int m = e / GCOLS, c = e % GCOLS;
+        const long long n = tile0 + c;
+        if (m >= M || n >= N) continue;
+        float v = 0.f;
+        for (int k = 0; k < ksplit; ++k) v += __ldcg(part + ((long long)k * M + m) * N + n);
+        C[(long long)m * N + n] = v * s[n];
+    }
+    if (t == 0) ctr[blockIdx.x] = 0u;
+}
+
+// Per-stream workspace: two halves, alternating per launch.
+struct GemvWs {
+    int device;
+    cudaStream_t stream;
+    unsigned int *ctr[2];
+    float *part[2];
+    size_t nctr, npart;
+    unsigned flip;
+};
+std::mutex g_gemv_mu;
+std::vector<GemvWs> g_gemv_ws;
+
+int gemv_workspace(cudaStream_t st, size_t nctr, size_t npart, unsigned int **ctr, float **part) {
+    int dev = 0;
+    int rc = check_cuda(cudaGetDevice(&dev), "gemv: cudaGetDevice");
+    if (rc) return rc;
+    std::lock_guard<std::mutex> lock(g_gemv_mu);
+    GemvWs *e = nullptr;
+    for (auto &x : g_gemv_ws)
+        if (x.device == dev && x.stream == st) e = &x;
+    if (!e) {
+        g_gemv_ws.push_back({dev, st, {nullptr, nullptr}, {nullptr, nullptr}, 0, 0, 0});
+        e = &g_gemv_ws.back();
+    }
+    if (e->nctr < nctr || e->npart < npart) {
+        for (int h = 0; h < 2; ++h) {  // cudaFree waits for the device
+            if (e->ctr[h]) cudaFree(e->ctr[h]);
+            if (e->part[h]) cudaFree(e->part[h]);
+            e->ctr[h] = nullptr;
+            e->part[h] = nullptr;
+        }
+        const size_t nc = std::max<size_t>(nctr, 4096), np = std::max<size_t>(npart, 1 << 18);
+        for (int h = 0; h < 2 && !rc; ++h) {
+            rc = check_cuda(cudaMalloc(&e->ctr[h], nc * sizeof(unsigned int)), "gemv: cudaMalloc");
+            if (!rc) rc = check_cuda(cudaMemsetAsync(e->ctr[h], 0, nc * sizeof(unsigned int), st), "gemv: memset");
+            if (!rc) rc = check_cuda(cudaMalloc(&e->part[h], np * sizeof(float)), "gemv: cudaMalloc");
+        }
+        if (rc) return rc;
+        e->nctr = nc;
+        e->npart = np;
+    }
+    const unsigned h = e->flip++ & 1u;
+    *ctr = e->ctr[h];
+    *part = e->part[h];
+    return KAI_GDN_OK;
+}
+
+template <int MB>
+int run_gemv(const float *A, const int8_t *q, const float *s, float *Cm, int M, long long K, long long N,
+             cudaStream_t st) {
+    const long long tiles = (N + GCOLS - 1) / GCOLS;
+    const long long want = 2ll * sm_count();
+    long long ksplit = std::max<long long>(1, std::min<long long>((want + tiles - 1) / tiles, (K + 2 * KT - 1) / (2 * KT)));
+    ksplit = std::min<long long>(ksplit, 0xFFFF);
+    long long kper = (K + ksplit - 1) / ksplit;
+    kper = (kper + KT - 1) / KT * KT;
+    ksplit = (K + kper - 1) / kper;
+    const size_t smem = 1024 + (size_t)NSTG * STAGE + (size_t)MB * (size_t)kper * sizeof(float);
+    if (smem > 220 * 1024) return set_error(KAI_GDN_ERR_UNSUPPORTED, "gemv: K part too long");
+    unsigned int *ctr = nullptr;
+    float *part = nullptr;
+    if (ksplit > 1) {
+        int rc = gemv_workspace(st, (size_t)tiles, (size_t)(ksplit * M * N), &ctr, &part);
+        if (rc) return rc;
+    }
+    int *err = nullptr;
+    int rc = device_error_word(&err);
+    if (rc) return rc;
+    tma::EncodeTiled enc = tma::encoder();
+    if (!enc) return set_error(KAI_GDN_ERR_CUDA, "gemv: cuTensorMapEncodeTiled unavailable");
+    CUtensorMap map;
+    const cuuint64_t dims[2] = {(cuuint64_t)N, (cuuint64_t)K};
+    const cuuint64_t strides[1] = {(cuuint64_t)N};
+    const cuuint32_t box[2] = {256, KT};
+    const cuuint32_t es[2] = {1, 1};
+    const CUresult cr = enc(&map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<int8_t *>(q), dims, strides, box, es,
+                            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+                            CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (cr != CUDA_SUCCESS) return set_error(KAI_GDN_ERR_CUDA, "gemv: tensor map encoding failed (%d)", (int)cr);
+    static int attr_done[64] = {0};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev >= 0 && dev < 64 && !attr_done[dev]) {
+        rc = check_cuda(cudaFuncSetAttribute(gemv_int8_kernel<MB>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             220 * 1024),
+                        "gemv: smem attribute");
+        if (rc) return rc;
+        attr_done[dev] = 1;
+    }
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = dim3((unsigned)tiles, (unsigned)ksplit);
+    cfg.blockDim = dim3(GNT);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    const cudaError_t le =
+        cudaLaunchKernelEx(&cfg, gemv_int8_kernel<MB>, map, A, s, Cm, M, K, N, kper, part, ctr, err);
+    if (le != cudaSuccess) return check_cuda(le, "gemv_int8_kernel launch");
+    return check_launch("gemv_int8_kernel");
+}
+
+}  // namespace
+
+bool gemv_int8_supported(size_t M, size_t K, size_t N, const int8_t *q) {
+    return M >= 1 && M <= 4 && K > 0 && N % 16 == 0 && (uintptr_t)q % 16 == 0 && K < (1ull << 31) &&
+           N < (1ull << 31);
+}
+
+int launch_gemv_int8(const float *A, const int8_t *q, const float *s, float *Cm, size_t M, size_t K, size_t N,
+                     cudaStream_t st) {
+    if (M == 0 || N == 0) return KAI_GDN_OK;
+    if (!A || !q || !s || !Cm) return set_error(KAI_GDN_ERR_INVALID, "gemv_int8: null pointer");
+    if (!gemv_int8_supported(M, K, N, q)) return set_error(KAI_GDN_ERR_UNSUPPORTED, "gemv_int8: shape");
+    if (M == 1) return run_gemv<1>(A, q, s, Cm, 1, (long long)K, (long long)N, st);
+    if (M == 2) return run_gemv<2>(A, q, s, Cm, 2, (long long)K, (long long)N, st);
+    return run_gemv<4>(A, q, s, Cm, (int)M, (long long)K, (long long)N, st);
+}
+
+}  // namespace gdn

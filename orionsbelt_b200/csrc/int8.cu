@@ -540,6 +540,7 @@ int launch_matmul_int8(const float *A, const int8_t *q, const float *s, float *C
     if (!A || !q || !s) return set_error(KAI_GDN_ERR_INVALID, "matmul_int8: null pointer");
     const long long m = (long long)M, k = (long long)K, n = (long long)N;
     const bool vec = N % 16 == 0 && (uintptr_t)q % 16 == 0;
+    if (gemv_int8_supported(M, K, N, q)) return launch_gemv_int8(A, q, s, C, M, K, N, st);
     if (M <= 16 && vec) {
         if (M == 1) return launch_stream<1>(A, q, s, C, m, k, n, st);
         if (M == 2) return launch_stream<2>(A, q, s, C, m, k, n, st);

@@ -91,6 +91,29 @@ int check_nccl(const NcclApi *n, ncclResult_t r, const char *what) {
     return set_error(KAI_GDN_ERR_CUDA, "%s: %s", what, n->errorString(r));
 }
 
+// Programmatic dependent launch: every per-token kernel waits for the
+// preceding grid before it touches memory and lets its own dependents launch
+// at once, so the weight streams of the matmuls that follow start early.
+__device__ __forceinline__ void pdl_enter() {
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+template <typename... KArgs, typename... Args>
+int launch_pdl(const char *name, void (*kernel)(KArgs...), dim3 grid, dim3 block, cudaStream_t st, Args... args) {
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    const cudaError_t e = cudaLaunchKernelEx(&cfg, kernel, static_cast<KArgs>(args)...);
+    if (e != cudaSuccess) return check_cuda(e, name);
+    return check_launch(name);
+}
+
 // ------------------------------------------------------------- weights
 __device__ __forceinline__ unsigned long long mix64(unsigned long long z) {
     z += 0x9E3779B97F4A7C15ull;
@@ -173,6 +196,7 @@ __global__ void set_pos_kernel(int *pos, int v) { *pos = v; }
 // h[b] = E_q[tok[b]] * E_s[tok[b]]
 __global__ void embed_kernel(const int *__restrict__ tok, const int8_t *__restrict__ eq, const float *__restrict__ es,
                              float *__restrict__ h, long long H, long long vocab) {
+    pdl_enter();
     const long long b = blockIdx.x;
     long long t = tok[b];
     t = t < 0 ? 0 : (t >= vocab ? vocab - 1 : t);
@@ -182,6 +206,7 @@ __global__ void embed_kernel(const int *__restrict__ tok, const int8_t *__restri
 // h += delta (when given); y = h / sqrt(mean(h^2) + eps) * w   (one CTA per row)
 __global__ void add_rmsnorm_kernel(float *__restrict__ h, const float *__restrict__ delta, const float *__restrict__ w,
                                    float *__restrict__ y, long long H, float eps) {
+    pdl_enter();
     __shared__ float red[32];
     const long long b = blockIdx.x;
     float *hr = h + b * H;
@@ -209,6 +234,7 @@ __global__ void gdn_prep_kernel(const float *__restrict__ y, long long ny, float
                                 const float *__restrict__ dt_bias, float *__restrict__ q, float *__restrict__ k,
                                 float *__restrict__ v, float *__restrict__ beta, float *__restrict__ g, int hk, int hv,
                                 int d) {
+    pdl_enter();
     __shared__ float red[32];
     const int b = blockIdx.y, head = blockIdx.x, i = threadIdx.x;  // i < d
     const long long C = (long long)(2 * hk + hv) * d;
@@ -247,6 +273,7 @@ __global__ void gdn_prep_kernel(const float *__restrict__ y, long long ny, float
 __global__ void gated_rmsnorm_kernel(const float *__restrict__ o, const float *__restrict__ y, long long ny,
                                      long long zoff, const float *__restrict__ w, float *__restrict__ out, int hv,
                                      int d, float eps) {
+    pdl_enter();
     __shared__ float red[32];
     const int b = blockIdx.y, hh = blockIdx.x, i = threadIdx.x;
     const long long idx = ((long long)b * hv + hh) * d + i;
@@ -263,6 +290,7 @@ __global__ void attn_prep_kernel(const float *__restrict__ y, long long ny, cons
                                  const float *__restrict__ wk, const int *__restrict__ pos_p, float *__restrict__ q,
                                  float *__restrict__ gate, float *__restrict__ kn, float *__restrict__ vn, int hq,
                                  int hkv, int D, int R, float theta, float eps) {
+    pdl_enter();
     __shared__ float red[32];
     __shared__ float row[512];
     const int b = blockIdx.y, r = blockIdx.x, i = threadIdx.x;  // r < hq + 2 hkv
@@ -295,11 +323,13 @@ __global__ void attn_prep_kernel(const float *__restrict__ y, long long ny, cons
 }
 __global__ void attn_gate_kernel(const float *__restrict__ o, const float *__restrict__ gate, float *__restrict__ out,
                                  long long n) {
+    pdl_enter();
     for (long long e = blockIdx.x * (long long)blockDim.x + threadIdx.x; e < n; e += (long long)gridDim.x * blockDim.x)
         out[e] = o[e] * sigm(gate[e]);
 }
 // act = SiLU(gate) * up over rows [gate (I) | up (I)]
 __global__ void swiglu_kernel(const float *__restrict__ gu, float *__restrict__ act, long long I, long long n) {
+    pdl_enter();
     for (long long e = blockIdx.x * (long long)blockDim.x + threadIdx.x; e < n; e += (long long)gridDim.x * blockDim.x) {
         const long long b = e / I, c = e % I;
         act[e] = silu(gu[b * 2 * I + c]) * gu[b * 2 * I + I + c];
@@ -310,13 +340,17 @@ struct ArgMax {
     float v;
     int i;
 };
+// Grid (AM_BLOCKS, B): block x of row b scans columns x, x + AM_BLOCKS * 256, ...
+// and writes its candidate to out[b * AM_BLOCKS + x].
+constexpr int AM_BLOCKS = 64;
 __global__ void argmax_kernel(const float *__restrict__ logits, long long V, long long v0, ArgMax *__restrict__ out) {
+    pdl_enter();
     __shared__ float sv[32];
     __shared__ int si[32];
-    const long long b = blockIdx.x;
+    const long long b = blockIdx.y;
     float best = -INFINITY;
     int bi = 0x7fffffff;
-    for (long long c = threadIdx.x; c < V; c += blockDim.x) {
+    for (long long c = (long long)blockIdx.x * blockDim.x + threadIdx.x; c < V; c += (long long)gridDim.x * blockDim.x) {
         const float x = logits[b * V + c];
         if (x > best || (x == best && (int)(v0 + c) < bi)) {
             best = x;
@@ -342,18 +376,20 @@ __global__ void argmax_kernel(const float *__restrict__ logits, long long V, lon
                 best = sv[w];
                 bi = si[w];
             }
-        out[b] = {best, bi};
+        out[b * gridDim.x + blockIdx.x] = {best, bi};
     }
 }
-// tok[b] = argmax over the ranks' candidates all[r][b]
-__global__ void select_kernel(const ArgMax *__restrict__ all, int world, int B, int *__restrict__ tok) {
+// tok[b] = argmax over the candidates all[r][b][0 .. per) of every rank r
+__global__ void select_kernel(const ArgMax *__restrict__ all, int world, int B, int per, int *__restrict__ tok) {
+    pdl_enter();
     const int b = blockIdx.x * blockDim.x + threadIdx.x;
     if (b >= B) return;
-    ArgMax best = all[b];
-    for (int r = 1; r < world; ++r) {
-        const ArgMax c = all[(long long)r * B + b];
-        if (c.v > best.v || (c.v == best.v && c.i < best.i)) best = c;
-    }
+    ArgMax best = all[(long long)b * per];
+    for (int r = 0; r < world; ++r)
+        for (int j = 0; j < per; ++j) {
+            const ArgMax c = all[((long long)r * B + b) * per + j];
+            if (c.v > best.v || (c.v == best.v && c.i < best.i)) best = c;
+        }
     tok[b] = best.i;
 }
 
@@ -497,23 +533,19 @@ int run_segment(ModelEngine *e, size_t s, cudaStream_t st) {
     } while (0)
     const float *pending = nullptr;  // residual update still to be added to h
     if (s == 0) {
-        embed_kernel<<<(unsigned)B, 256, 0, st>>>(e->tok, e->emb_q, e->emb_s, e->h, (long long)H,
-                                                  (long long)c.vocab);
-        M_TRY(check_launch("embed_kernel"));
+        M_TRY(launch_pdl("embed_kernel", embed_kernel, dim3((unsigned)B), dim3(1024), st, e->tok, e->emb_q, e->emb_s, e->h, (long long)H,
+                                                  (long long)c.vocab));
     } else {
         // the rest of attention layer l_begin: gate, o projection, FFN
         const ModelEngine::Layer &L = e->layers[l_begin];
-        attn_gate_kernel<<<grid_for((long long)(B * e->hq * e->D)), 256, 0, st>>>(e->o, e->gate, e->o2,
-                                                                                 (long long)(B * e->hq * e->D));
-        M_TRY(check_launch("attn_gate_kernel"));
+        M_TRY(launch_pdl("attn_gate_kernel", attn_gate_kernel, dim3(grid_for((long long)(B * e->hq * e->D))), dim3(256), st, e->o, e->gate, e->o2,
+                                                                                 (long long)(B * e->hq * e->D)));
         M_TRY(mm(e->o2, L.wout, e->part, B, st));
         M_TRY(allreduce(e, e->part, B * H, st));
-        add_rmsnorm_kernel<<<(unsigned)B, 256, 0, st>>>(e->h, e->part, L.w_post, e->x, (long long)H, c.rms_eps);
-        M_TRY(check_launch("add_rmsnorm_kernel"));
+        M_TRY(launch_pdl("add_rmsnorm_kernel", add_rmsnorm_kernel, dim3((unsigned)B), dim3(1024), st, e->h, e->part, L.w_post, e->x, (long long)H, c.rms_eps));
         M_TRY(mm(e->x, L.wgu, e->gu, B, st));
-        swiglu_kernel<<<grid_for((long long)(B * e->I)), 256, 0, st>>>(e->gu, e->act, (long long)e->I,
-                                                                     (long long)(B * e->I));
-        M_TRY(check_launch("swiglu_kernel"));
+        M_TRY(launch_pdl("swiglu_kernel", swiglu_kernel, dim3(grid_for((long long)(B * e->I))), dim3(256), st, e->gu, e->act, (long long)e->I,
+                                                                     (long long)(B * e->I)));
         M_TRY(mm(e->act, L.wdown, e->part, B, st));
         M_TRY(allreduce(e, e->part, B * H, st));
         pending = e->part;
@@ -521,25 +553,20 @@ int run_segment(ModelEngine *e, size_t s, cudaStream_t st) {
     const size_t first = s == 0 ? 0 : l_begin + 1;
     for (size_t l = first; l < l_end || (l == l_end && l < c.layers); ++l) {
         const ModelEngine::Layer &L = e->layers[l];
-        add_rmsnorm_kernel<<<(unsigned)B, 256, 0, st>>>(e->h, pending, L.w_in, e->x, (long long)H, c.rms_eps);
-        M_TRY(check_launch("add_rmsnorm_kernel"));
+        M_TRY(launch_pdl("add_rmsnorm_kernel", add_rmsnorm_kernel, dim3((unsigned)B), dim3(1024), st, e->h, pending, L.w_in, e->x, (long long)H, c.rms_eps));
         pending = nullptr;
         if (l == l_end) {
             // attention layer: projections and the prepared q / k / v; the
             // decode itself follows this segment
             M_TRY(mm(e->x, L.win, e->y, B, st));
-            attn_prep_kernel<<<dim3((unsigned)(e->hq + 2 * e->hkv), (unsigned)B), (unsigned)e->D, 0, st>>>(
-                e->y, (long long)e->ny_att, L.w_qn, L.w_kn, e->pos, e->q, e->gate, e->k, e->v, (int)e->hq,
-                (int)e->hkv, (int)e->D, (int)c.rope_dims, c.rope_theta, c.rms_eps);
-            M_TRY(check_launch("attn_prep_kernel"));
+            M_TRY(launch_pdl("attn_prep_kernel", attn_prep_kernel, dim3(dim3((unsigned)(e->hq + 2 * e->hkv), (unsigned)B)), dim3((unsigned)e->D), st, e->y, (long long)e->ny_att, L.w_qn, L.w_kn, e->pos, e->q, e->gate, e->k, e->v, (int)e->hq,
+                (int)e->hkv, (int)e->D, (int)c.rope_dims, c.rope_theta, c.rms_eps));
             return KAI_GDN_OK;
         }
         // GDN layer
         M_TRY(mm(e->x, L.win, e->y, B, st));
-        gdn_prep_kernel<<<dim3((unsigned)(2 * e->hk + e->hv), (unsigned)B), (unsigned)e->d, 0, st>>>(
-            e->y, (long long)e->ny_gdn, L.hist, L.conv_w, L.A_log, L.dt_bias, e->q, e->k, e->v, e->beta, e->g,
-            (int)e->hk, (int)e->hv, (int)e->d);
-        M_TRY(check_launch("gdn_prep_kernel"));
+        M_TRY(launch_pdl("gdn_prep_kernel", gdn_prep_kernel, dim3(dim3((unsigned)(2 * e->hk + e->hv), (unsigned)B)), dim3((unsigned)e->d), st, e->y, (long long)e->ny_gdn, L.hist, L.conv_w, L.A_log, L.dt_bias, e->q, e->k, e->v, e->beta, e->g,
+            (int)e->hk, (int)e->hv, (int)e->d));
         kai_gdn_decode_args da{};
         da.state = L.state;
         da.q = e->q;
@@ -558,33 +585,29 @@ int run_segment(ModelEngine *e, size_t s, cudaStream_t st) {
         da.state_dtype = KAI_GDN_F32;
         da.out_dtype = KAI_GDN_F32;
         M_TRY(launch_decode(&da, st));
-        gated_rmsnorm_kernel<<<dim3((unsigned)e->hv, (unsigned)B), (unsigned)e->d, 0, st>>>(
-            e->o, e->y, (long long)e->ny_gdn, (long long)e->C, L.w_gn, e->o2, (int)e->hv, (int)e->d, c.rms_eps);
-        M_TRY(check_launch("gated_rmsnorm_kernel"));
+        M_TRY(launch_pdl("gated_rmsnorm_kernel", gated_rmsnorm_kernel, dim3(dim3((unsigned)e->hv, (unsigned)B)), dim3((unsigned)e->d), st, e->o, e->y, (long long)e->ny_gdn, (long long)e->C, L.w_gn, e->o2, (int)e->hv, (int)e->d, c.rms_eps));
         M_TRY(mm(e->o2, L.wout, e->part, B, st));
         M_TRY(allreduce(e, e->part, B * H, st));
-        add_rmsnorm_kernel<<<(unsigned)B, 256, 0, st>>>(e->h, e->part, L.w_post, e->x, (long long)H, c.rms_eps);
-        M_TRY(check_launch("add_rmsnorm_kernel"));
+        M_TRY(launch_pdl("add_rmsnorm_kernel", add_rmsnorm_kernel, dim3((unsigned)B), dim3(1024), st, e->h, e->part, L.w_post, e->x, (long long)H, c.rms_eps));
         M_TRY(mm(e->x, L.wgu, e->gu, B, st));
-        swiglu_kernel<<<grid_for((long long)(B * e->I)), 256, 0, st>>>(e->gu, e->act, (long long)e->I,
-                                                                     (long long)(B * e->I));
-        M_TRY(check_launch("swiglu_kernel"));
+        M_TRY(launch_pdl("swiglu_kernel", swiglu_kernel, dim3(grid_for((long long)(B * e->I))), dim3(256), st, e->gu, e->act, (long long)e->I,
+                                                                     (long long)(B * e->I)));
         M_TRY(mm(e->act, L.wdown, e->part, B, st));
         M_TRY(allreduce(e, e->part, B * H, st));
         pending = e->part;
     }
     // end of the token: final norm, LM head over this rank's vocabulary, argmax
-    add_rmsnorm_kernel<<<(unsigned)B, 256, 0, st>>>(e->h, pending, e->w_final, e->x, (long long)H, c.rms_eps);
-    M_TRY(check_launch("add_rmsnorm_kernel"));
+    M_TRY(launch_pdl("add_rmsnorm_kernel", add_rmsnorm_kernel, dim3((unsigned)B), dim3(1024), st, e->h, pending, e->w_final, e->x, (long long)H, c.rms_eps));
     M_TRY(mm(e->x, e->lm, e->logits, B, st));
-    argmax_kernel<<<(unsigned)B, 256, 0, st>>>(e->logits, (long long)e->V, (long long)e->v0, e->cand);
-    M_TRY(check_launch("argmax_kernel"));
+    M_TRY(launch_pdl("argmax_kernel", argmax_kernel, dim3(dim3(AM_BLOCKS, (unsigned)B)), dim3(256), st, e->logits, (long long)e->V, (long long)e->v0,
+                                                                e->cand));
     if (c.tp_size > 1)
-        M_TRY(check_nccl(e->nccl, e->nccl->allGather(e->cand, e->cand_all, B * 2, ncclFloat32, e->comm, st),
+        M_TRY(check_nccl(e->nccl,
+                         e->nccl->allGather(e->cand, e->cand_all, B * AM_BLOCKS * 2, ncclFloat32, e->comm, st),
                          "model: all-gather"));
-    select_kernel<<<(unsigned)((B + 127) / 128), 128, 0, st>>>(c.tp_size > 1 ? e->cand_all : e->cand,
-                                                              c.tp_size > 1 ? c.tp_size : 1, (int)B, e->tok);
-    M_TRY(check_launch("select_kernel"));
+    M_TRY(launch_pdl("select_kernel", select_kernel, dim3((unsigned)((B + 127) / 128)), dim3(128), st, c.tp_size > 1 ? e->cand_all : e->cand,
+                                                              c.tp_size > 1 ? c.tp_size : 1, (int)B, AM_BLOCKS,
+                                                              e->tok));
 #undef M_TRY
     return KAI_GDN_OK;
 }
@@ -834,8 +857,8 @@ int model_create(const kai_gdn_model_config *cfg, void **out) {
         if (!rc) rc = malloc_keep(e, (void **)bf.p, bf.n * sizeof(float), true);
     if (!rc) rc = malloc_keep(e, (void **)&e->tok, B * sizeof(int), true);
     if (!rc) rc = malloc_keep(e, (void **)&e->pos, sizeof(int), true);
-    if (!rc) rc = malloc_keep(e, (void **)&e->cand, B * sizeof(ArgMax), true);
-    if (!rc) rc = malloc_keep(e, (void **)&e->cand_all, (size_t)W * B * sizeof(ArgMax), true);
+    if (!rc) rc = malloc_keep(e, (void **)&e->cand, B * AM_BLOCKS * sizeof(ArgMax), true);
+    if (!rc) rc = malloc_keep(e, (void **)&e->cand_all, (size_t)W * B * AM_BLOCKS * sizeof(ArgMax), true);
     if (rc) {
         model_destroy(e);
         return rc;
