@@ -584,11 +584,14 @@ def run_model(args, world, rank, barrier, peaks, ctx=32768, steps=256):
     from orionsbelt_b200 import ops
 
     out = {}
-    nid = None
-    if world > 1:
+
+    def fresh_id():  # an NCCL unique id serves one communicator: one per engine
+        if world == 1:
+            return None
         box = [ops.ModelEngine.nccl_id() if rank == 0 else None]
         dist.broadcast_object_list(box, src=0)
-        nid = box[0]
+        return box[0]
+
     geom = dict(CFG4, max_ctx=ctx + steps + 8)
     H, L = geom["hidden"], len(geom["is_gdn"])
     # int8 weight bytes one token streams on each GPU (all layers + LM head), for the roofline
@@ -600,7 +603,7 @@ def run_model(args, world, rank, barrier, peaks, ctx=32768, steps=256):
     tok_bytes = (24 * (gdn_w + ffn_w) + 8 * (att_w + ffn_w) + H * V) / world
     stream = torch.cuda.Stream()
     for B in (1, 16):
-        eng = ops.ModelEngine(geom, B, seed=42, tp_rank=rank, tp_size=world, nccl_id=nid)
+        eng = ops.ModelEngine(geom, B, seed=42, tp_rank=rank, tp_size=world, nccl_id=fresh_id())
         eng.fill(ctx, seed=3)
         eng.set_tokens(np.random.default_rng(9).integers(0, geom["vocab"], B).astype(np.int32))
         barrier()

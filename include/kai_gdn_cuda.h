@@ -327,7 +327,8 @@ typedef struct kai_gdn_model_config {
     unsigned long long seed;
     float weight_std;                              /* 0: 0.02                               */
 } kai_gdn_model_config;
-/* A fresh NCCL unique id (rank 0 makes it and shares it with the others). */
+/* A fresh NCCL unique id (rank 0 makes it and shares it with the others);
+ * an id serves the creation of one engine's communicator. */
 KAI_GDN_API int kai_gdn_model_nccl_id(void *id_out);
 KAI_GDN_API int kai_gdn_model_create(const kai_gdn_model_config *cfg, void **engine);
 /* One greedy decode step of every sequence at position `pos` (0-based): reads

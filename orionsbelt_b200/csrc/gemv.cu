@@ -21,6 +21,7 @@
 // from one launch to the next on a stream, so a dependent that overlaps this
 // kernel's fix-up never writes the partial sums being read.
 #include <algorithm>
+#include <cstring>
 #include <mutex>
 #include <vector>
 
@@ -83,8 +84,9 @@ __device__ __forceinline__ void tma_rows(unsigned char *dst, const CUtensorMap *
 // [tiles] (zero between calls) when ksplit > 1.  Warp 8 (one lane) fills a
 // six-deep ring of 32-row x 512-column stages by TMA; warps 0-7 take four
 // rows of each stage, each lane 16 columns.
-template <int MB>
+template <int MB, bool BLK>
 __global__ void __launch_bounds__(GNT) gemv_int8_kernel(const __grid_constant__ CUtensorMap map,
+                                                        const int8_t *__restrict__ qb,
                                                         const float *__restrict__ A, const float *__restrict__ s,
                                                         float *__restrict__ C, int M, long long K, long long N,
                                                         long long kper, float *__restrict__ part,
@@ -112,16 +114,25 @@ __global__ void __launch_bounds__(GNT) gemv_int8_kernel(const __grid_constant__ 
     __syncthreads();
     int issued = 0;
     bool bad = false;
+    // blocked layout: this tile's rows are contiguous, 512 bytes each
+    const int8_t *tile_rows = BLK ? qb + (size_t)blockIdx.x * (size_t)K * GCOLS : nullptr;
+    auto load_stage = [&](int i, int st) {
+        const long long r0 = k0 + (long long)i * KT;
+        if (BLK) {
+            const uint32_t bytes = (uint32_t)(min((long long)KT, k1 - r0) * GCOLS);
+            umma::mbar_arrive_expect_tx(&full[st], bytes);
+            umma::bulk_load(ring + st * STAGE, tile_rows + r0 * GCOLS, bytes, &full[st]);
+        } else {
+            umma::mbar_arrive_expect_tx(&full[st], STAGE);
+            tma_rows(ring + st * STAGE, &map, (int)tile0, (int)r0, &full[st]);
+            tma_rows(ring + st * STAGE + STAGE / 2, &map, (int)tile0 + 256, (int)r0, &full[st]);
+        }
+    };
     if (w == GW) {
         // ---- producer: weights never depend on earlier kernels, so the
         // first stages are issued before the dependency wait
         if (lane == 0) {
-            for (; issued < nk && issued < NSTG; ++issued) {
-                umma::mbar_arrive_expect_tx(&full[issued], STAGE);
-                tma_rows(ring + issued * STAGE, &map, (int)tile0, (int)(k0 + issued * KT), &full[issued]);
-                tma_rows(ring + issued * STAGE + STAGE / 2, &map, (int)tile0 + 256, (int)(k0 + issued * KT),
-                         &full[issued]);
-            }
+            for (; issued < nk && issued < NSTG; ++issued) load_stage(issued, issued);
         }
         pdl_trigger();
         if (lane == 0) {
@@ -131,9 +142,7 @@ __global__ void __launch_bounds__(GNT) gemv_int8_kernel(const __grid_constant__ 
                     bad = true;
                     break;
                 }
-                umma::mbar_arrive_expect_tx(&full[st], STAGE);
-                tma_rows(ring + st * STAGE, &map, (int)tile0, (int)(k0 + issued * KT), &full[st]);
-                tma_rows(ring + st * STAGE + STAGE / 2, &map, (int)tile0 + 256, (int)(k0 + issued * KT), &full[st]);
+                load_stage(issued, st);
             }
             // every issued load lands before the CTA may leave
             for (int i = issued - NSTG > 0 ? issued - NSTG : 0; i < issued; ++i)
@@ -157,14 +166,16 @@ __global__ void __launch_bounds__(GNT) gemv_int8_kernel(const __grid_constant__ 
 #pragma unroll
             for (int j = 0; j < 8; ++j) acc[m][j] = make_float2(0.f, 0.f);
         const int box = lane / 16, cw = lane % 16;
+        const int lane_off = BLK ? lane * 16 : box * (STAGE / 2) + cw * 16;
+        const int row_bytes = BLK ? GCOLS : 256;
         for (int i = 0; i < nk; ++i) {
             const int st = i % NSTG;
             if (!umma::mbar_wait(&full[st], (uint32_t)((i / NSTG) & 1), err)) bad = true;
             if (__any_sync(0xffffffffu, bad)) break;
-            const unsigned char *sb = ring + st * STAGE + box * (STAGE / 2) + cw * 16;
+            const unsigned char *sb = ring + st * STAGE + lane_off;
             uint4 wv[KT / GW];
 #pragma unroll
-            for (int j = 0; j < KT / GW; ++j) wv[j] = *reinterpret_cast<const uint4 *>(sb + (w + GW * j) * 256);
+            for (int j = 0; j < KT / GW; ++j) wv[j] = *reinterpret_cast<const uint4 *>(sb + (w + GW * j) * row_bytes);
             __syncwarp();
             if (lane == 0) asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(umma::smem_addr(&empty[st])) : "memory");
 #pragma unroll
@@ -281,7 +292,7 @@ int gemv_workspace(cudaStream_t st, size_t nctr, size_t npart, unsigned int **ct
     return KAI_GDN_OK;
 }
 
-template <int MB>
+template <int MB, bool BLK>
 int run_gemv(const float *A, const int8_t *q, const float *s, float *Cm, int M, long long K, long long N,
              cudaStream_t st) {
     const long long tiles = (N + GCOLS - 1) / GCOLS;
@@ -302,22 +313,25 @@ int run_gemv(const float *A, const int8_t *q, const float *s, float *Cm, int M, 
     int *err = nullptr;
     int rc = device_error_word(&err);
     if (rc) return rc;
-    tma::EncodeTiled enc = tma::encoder();
-    if (!enc) return set_error(KAI_GDN_ERR_CUDA, "gemv: cuTensorMapEncodeTiled unavailable");
     CUtensorMap map;
-    const cuuint64_t dims[2] = {(cuuint64_t)N, (cuuint64_t)K};
-    const cuuint64_t strides[1] = {(cuuint64_t)N};
-    const cuuint32_t box[2] = {256, KT};
-    const cuuint32_t es[2] = {1, 1};
-    const CUresult cr = enc(&map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<int8_t *>(q), dims, strides, box, es,
-                            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
-                            CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-    if (cr != CUDA_SUCCESS) return set_error(KAI_GDN_ERR_CUDA, "gemv: tensor map encoding failed (%d)", (int)cr);
+    memset(&map, 0, sizeof(map));
+    if (!BLK) {
+        tma::EncodeTiled enc = tma::encoder();
+        if (!enc) return set_error(KAI_GDN_ERR_CUDA, "gemv: cuTensorMapEncodeTiled unavailable");
+        const cuuint64_t dims[2] = {(cuuint64_t)N, (cuuint64_t)K};
+        const cuuint64_t strides[1] = {(cuuint64_t)N};
+        const cuuint32_t box[2] = {256, KT};
+        const cuuint32_t es[2] = {1, 1};
+        const CUresult cr = enc(&map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<int8_t *>(q), dims, strides, box,
+                                es, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+                                CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+        if (cr != CUDA_SUCCESS) return set_error(KAI_GDN_ERR_CUDA, "gemv: tensor map encoding failed (%d)", (int)cr);
+    }
     static int attr_done[64] = {0};
     int dev = 0;
     cudaGetDevice(&dev);
     if (dev >= 0 && dev < 64 && !attr_done[dev]) {
-        rc = check_cuda(cudaFuncSetAttribute(gemv_int8_kernel<MB>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+        rc = check_cuda(cudaFuncSetAttribute(gemv_int8_kernel<MB, BLK>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                              220 * 1024),
                         "gemv: smem attribute");
         if (rc) return rc;
@@ -334,7 +348,7 @@ int run_gemv(const float *A, const int8_t *q, const float *s, float *Cm, int M, 
     cfg.attrs = attr;
     cfg.numAttrs = 1;
     const cudaError_t le =
-        cudaLaunchKernelEx(&cfg, gemv_int8_kernel<MB>, map, A, s, Cm, M, K, N, kper, part, ctr, err);
+        cudaLaunchKernelEx(&cfg, gemv_int8_kernel<MB, BLK>, map, q, A, s, Cm, M, K, N, kper, part, ctr, err);
     if (le != cudaSuccess) return check_cuda(le, "gemv_int8_kernel launch");
     return check_launch("gemv_int8_kernel");
 }
@@ -351,9 +365,45 @@ int launch_gemv_int8(const float *A, const int8_t *q, const float *s, float *Cm,
     if (M == 0 || N == 0) return KAI_GDN_OK;
     if (!A || !q || !s || !Cm) return set_error(KAI_GDN_ERR_INVALID, "gemv_int8: null pointer");
     if (!gemv_int8_supported(M, K, N, q)) return set_error(KAI_GDN_ERR_UNSUPPORTED, "gemv_int8: shape");
-    if (M == 1) return run_gemv<1>(A, q, s, Cm, 1, (long long)K, (long long)N, st);
-    if (M == 2) return run_gemv<2>(A, q, s, Cm, 2, (long long)K, (long long)N, st);
-    return run_gemv<4>(A, q, s, Cm, (int)M, (long long)K, (long long)N, st);
+    if (M == 1) return run_gemv<1, false>(A, q, s, Cm, 1, (long long)K, (long long)N, st);
+    if (M == 2) return run_gemv<2, false>(A, q, s, Cm, 2, (long long)K, (long long)N, st);
+    return run_gemv<4, false>(A, q, s, Cm, (int)M, (long long)K, (long long)N, st);
+}
+
+// Blocked weight layout: [ceil(N / 512)][K][512] bytes (the columns of a
+// 512-wide tile contiguous row after row, the last tile zero-padded), so one
+// tile's rows stream as contiguous 16 KB bulk copies.
+__global__ void block_weights_kernel(const int8_t *__restrict__ q, int8_t *__restrict__ qb, long long K, long long N) {
+    const long long tiles = (N + GCOLS - 1) / GCOLS, n16 = tiles * K * (GCOLS / 16);
+    for (long long e = blockIdx.x * (long long)blockDim.x + threadIdx.x; e < n16; e += (long long)gridDim.x * blockDim.x) {
+        const long long t = e / (K * (GCOLS / 16)), rem = e % (K * (GCOLS / 16));
+        const long long k = rem / (GCOLS / 16), c16 = rem % (GCOLS / 16);
+        const long long n = t * GCOLS + c16 * 16;
+        uint4 v = make_uint4(0, 0, 0, 0);
+        if (n < N) v = *reinterpret_cast<const uint4 *>(q + k * N + n);
+        *reinterpret_cast<uint4 *>(qb + (t * K + k) * GCOLS + c16 * 16) = v;
+    }
+}
+
+size_t gemv_blocked_bytes(size_t K, size_t N) { return (N + GCOLS - 1) / GCOLS * K * GCOLS; }
+
+int gemv_block_weights(const int8_t *q, int8_t *qb, size_t K, size_t N, cudaStream_t st) {
+    if (N % 16 || (uintptr_t)q % 16 || (uintptr_t)qb % 16)
+        return set_error(KAI_GDN_ERR_UNSUPPORTED, "gemv_block_weights: N % 16 and 16-byte alignment");
+    const long long n16 = (long long)gemv_blocked_bytes(K, N) / 16;
+    block_weights_kernel<<<(unsigned)std::min<long long>((n16 + 255) / 256, 65535), 256, 0, st>>>(q, qb, (long long)K,
+                                                                                                 (long long)N);
+    return check_launch("block_weights_kernel");
+}
+
+int launch_gemv_int8_blocked(const float *A, const int8_t *qb, const float *s, float *Cm, size_t M, size_t K,
+                             size_t N, cudaStream_t st) {
+    if (M == 0 || N == 0) return KAI_GDN_OK;
+    if (!A || !qb || !s || !Cm) return set_error(KAI_GDN_ERR_INVALID, "gemv_int8: null pointer");
+    if (!gemv_int8_supported(M, K, N, qb)) return set_error(KAI_GDN_ERR_UNSUPPORTED, "gemv_int8: shape");
+    if (M == 1) return run_gemv<1, true>(A, qb, s, Cm, 1, (long long)K, (long long)N, st);
+    if (M == 2) return run_gemv<2, true>(A, qb, s, Cm, 2, (long long)K, (long long)N, st);
+    return run_gemv<4, true>(A, qb, s, Cm, (int)M, (long long)K, (long long)N, st);
 }
 
 }  // namespace gdn

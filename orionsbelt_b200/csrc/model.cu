@@ -396,7 +396,8 @@ __global__ void select_kernel(const ArgMax *__restrict__ all, int world, int B, 
 unsigned grid_for(long long n) { return (unsigned)std::min<long long>((n + 255) / 256, 8ll * sm_count()); }
 
 struct QW {
-    int8_t *q = nullptr;
+    int8_t *q = nullptr;   // [K][N]
+    int8_t *qb = nullptr;  // the same codes in the GEMV's blocked layout (batch <= 4)
     float *s = nullptr;
     size_t K = 0, N = 0;
 };
@@ -475,6 +476,10 @@ int build_qw(ModelEngine *e, QW *w, size_t K, size_t k0, size_t k1, const std::v
     if (!rc) rc = launch_quantize_int8(tmp, qt, w->s, K, N, 0);
     if (!rc) rc = malloc_keep(e, (void **)&w->q, (k1 - k0) * N, false);
     if (!rc) rc = check_cuda(cudaMemcpy(w->q, qt + k0 * N, (k1 - k0) * N, cudaMemcpyDeviceToDevice), "model: codes");
+    if (!rc && e->cfg.batch <= 4 && gemv_int8_supported(e->cfg.batch, k1 - k0, N, w->q)) {
+        if (!(rc = malloc_keep(e, (void **)&w->qb, gemv_blocked_bytes(k1 - k0, N), false)))
+            rc = gemv_block_weights(w->q, w->qb, k1 - k0, N, 0);
+    }
     if (!rc) rc = check_cuda(cudaDeviceSynchronize(), "model: weights");
     if (tmp) cudaFree(tmp);
     if (qt) cudaFree(qt);
@@ -513,6 +518,7 @@ enum : unsigned {
 unsigned tidl(size_t layer, unsigned kind) { return (unsigned)(layer * 64 + kind); }
 
 int mm(const float *A, const QW &w, float *Cm, size_t M, cudaStream_t st) {
+    if (w.qb) return launch_gemv_int8_blocked(A, w.qb, w.s, Cm, M, w.K, w.N, st);
     return launch_matmul_int8(A, w.q, w.s, Cm, M, w.K, w.N, st);
 }
 int allreduce(ModelEngine *e, float *buf, size_t n, cudaStream_t st) {

@@ -255,7 +255,8 @@ class ModelEngine:
     (hidden, layers, vocab, inter, is_gdn, gdn_heads_k, gdn_heads_v, gdn_head_dim,
     attn_heads, attn_kv_heads, attn_head_dim, rope_dims, rope_theta, rms_eps,
     max_ctx, weight_std); tp_rank / tp_size / nccl_id place it in a
-    tensor-parallel group (nccl_id: bytes from nccl_id())."""
+    tensor-parallel group (nccl_id: bytes from nccl_id(), made by one rank and
+    shared with the others; an id serves one engine's communicator)."""
 
     W_IN, W_OUT, W_GATE_UP, W_DOWN = 0, 1, 2, 3
     V_NORM_IN, V_NORM_POST, V_CONV, V_A_LOG, V_DT_BIAS, V_NORM_GDN, V_NORM_Q, V_NORM_K = 4, 5, 6, 7, 8, 9, 10, 11
