@@ -70,15 +70,15 @@ int model_destroy(void *engine);
 int launch_quantize_int8(const float *B, int8_t *q, float *s, size_t K, size_t N, cudaStream_t st);
 int launch_matmul_int8(const float *A, const int8_t *q, const float *s, float *C, size_t M, size_t K, size_t N,
                        cudaStream_t st);
-// Weight-streaming GEMV for M <= 4 (gemv.cu), launched as a programmatic
+// Weight-streaming GEMV for M <= 8 (gemv.cu), launched as a programmatic
 // dependent of the previous kernel on the stream.
 bool gemv_int8_supported(size_t M, size_t K, size_t N, const int8_t *q);
 int launch_gemv_int8(const float *A, const int8_t *q, const float *s, float *C, size_t M, size_t K, size_t N,
                      cudaStream_t st);
-// The same over weights in the blocked layout [ceil(N/512)][K][512] (made by
+// The same over weights in the blocked layout for M rows (made by
 // gemv_block_weights from [K][N]; gemv_blocked_bytes bytes).
-size_t gemv_blocked_bytes(size_t K, size_t N);
-int gemv_block_weights(const int8_t *q, int8_t *qb, size_t K, size_t N, cudaStream_t st);
+size_t gemv_blocked_bytes(size_t M, size_t K, size_t N);
+int gemv_block_weights(size_t M, const int8_t *q, int8_t *qb, size_t K, size_t N, cudaStream_t st);
 int launch_gemv_int8_blocked(const float *A, const int8_t *qb, const float *s, float *C, size_t M, size_t K,
                              size_t N, cudaStream_t st);
 int launch_matmul_int8_tc(const float *A, const int8_t *q, const float *s, float *C, size_t M, size_t K, size_t N,

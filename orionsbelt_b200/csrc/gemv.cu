@@ -1,4 +1,4 @@
-// gemv.cu -- int8-weight GEMV for the decode shapes (M <= 4 activation rows),
+// gemv.cu -- int8-weight GEMV for the decode shapes (M <= 8 activation rows),
 // C = (A q) diag(s) with q [K][N] int8 and one fp32 scale per column (the
 // reference's gemv_int8_neon / gemm_int8_neon, gdn_e2e_decode.c:296-358,
 // 608-678), streamed from HBM at the copy rate.
@@ -32,12 +32,24 @@
 namespace gdn {
 namespace {
 
-constexpr int GW = 8;            // consumer warps per CTA
-constexpr int GCOLS = 512;       // columns per CTA (32 lanes x 16)
-constexpr int KT = 32;           // weight rows per ring stage
-constexpr int NSTG = 6;          // ring depth: 6 x 16 KB in flight per CTA
+constexpr int GW = 8;             // consumer warps per CTA
+constexpr int KT = 32;            // weight rows per ring stage
 constexpr int GNT = GW * 32 + 32;  // + one producer warp
-constexpr int STAGE = KT * GCOLS;  // bytes
+constexpr int KMAX_OCC = 1024;     // longest K part (rows) a CTA takes
+
+// Tile geometry: CPL columns per lane (16: one 16-byte load per row, for up
+// to 4 activation rows; 8: an 8-byte load, for 5..8 rows, which keeps the
+// accumulators in registers), 32 lanes per tile, NSTG stages of KT rows.
+// (At 16 rows the CUDA cores' multiply-adds, not HBM, bound this kernel:
+// measured 48 us at 16 x 2560 x 9216 against 39 us on the tensor-core path.)
+template <int CPL> struct GemvGeo {
+    static constexpr int TC = 32 * CPL;         // columns per CTA tile
+    static constexpr int STAGE = KT * TC;       // bytes per ring stage
+    static constexpr int NSTG = CPL == 16 ? 6 : 8;
+};
+template <int MB> struct GemvCpl {
+    static constexpr int CPL = MB <= 4 ? 16 : 8;
+};
 
 __device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 __device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
@@ -54,12 +66,12 @@ __device__ __forceinline__ void deq4x2(uint32_t w, float2 &a, float2 &b) {
                    nbias);
 }
 
-// acc[m][0..7] (float2 pairs of 16 columns) += a[m] * row
-template <int MB>
-__device__ __forceinline__ void accumulate(float2 (&acc)[MB][8], const uint4 w, const float *a) {
-    const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
+// acc[m][0 .. CPL/2) (float2 pairs of the lane's columns) += a[m] * row
+template <int MB, int CPL>
+__device__ __forceinline__ void accumulate(float2 (&acc)[MB][CPL / 2], const uint32_t (&ws)[CPL / 4],
+                                           const float *a) {
 #pragma unroll
-    for (int j = 0; j < 4; ++j) {
+    for (int j = 0; j < CPL / 4; ++j) {
         float2 p0, p1;
         deq4x2(ws[j], p0, p1);
 #pragma unroll
@@ -70,6 +82,15 @@ __device__ __forceinline__ void accumulate(float2 (&acc)[MB][8], const uint4 w, 
         }
     }
 }
+template <int CPL> __device__ __forceinline__ void ld_row(const unsigned char *p, uint32_t (&ws)[CPL / 4]);
+template <> __device__ __forceinline__ void ld_row<16>(const unsigned char *p, uint32_t (&ws)[4]) {
+    const uint4 v = *reinterpret_cast<const uint4 *>(p);
+    ws[0] = v.x, ws[1] = v.y, ws[2] = v.z, ws[3] = v.w;
+}
+template <> __device__ __forceinline__ void ld_row<8>(const unsigned char *p, uint32_t (&ws)[2]) {
+    const uint2 v = *reinterpret_cast<const uint2 *>(p);
+    ws[0] = v.x, ws[1] = v.y;
+}
 
 __device__ __forceinline__ void tma_rows(unsigned char *dst, const CUtensorMap *map, int x, int y, uint64_t *bar) {
     asm volatile(
@@ -79,28 +100,31 @@ __device__ __forceinline__ void tma_rows(unsigned char *dst, const CUtensorMap *
         : "memory");
 }
 
-// Grid (ceil(N / 512), ksplit).  A [M][K], q [K][N] (through `map`: boxes of
-// 256 columns x 32 rows), s [N], C [M][N]; part [ksplit][M][N] and ctr
-// [tiles] (zero between calls) when ksplit > 1.  Warp 8 (one lane) fills a
-// six-deep ring of 32-row x 512-column stages by TMA; warps 0-7 take four
-// rows of each stage, each lane 16 columns.
-template <int MB, bool BLK>
+// Grid (ceil(N / TC), ksplit).  A [M][K], s [N], C [M][N]; the weights come
+// either through `map` (q [K][N], boxes of 256 columns x KT rows) or, BLK,
+// from qb in the blocked layout [ceil(N / TC)][K][TC] (one contiguous bulk
+// copy per stage).  part [ksplit][M][N] and ctr [tiles] (zero between calls)
+// when ksplit > 1.  Warp 8 (one lane) fills the ring; warps 0-7 take KT / 8
+// rows of each stage, each lane CPL columns.
+template <int MB, int CPL, bool BLK>
 __global__ void __launch_bounds__(GNT) gemv_int8_kernel(const __grid_constant__ CUtensorMap map,
                                                         const int8_t *__restrict__ qb,
                                                         const float *__restrict__ A, const float *__restrict__ s,
                                                         float *__restrict__ C, int M, long long K, long long N,
                                                         long long kper, float *__restrict__ part,
                                                         unsigned int *__restrict__ ctr, int *err) {
+    using G = GemvGeo<CPL>;
+    constexpr int TC = G::TC, STAGE = G::STAGE, NSTG = G::NSTG;
     extern __shared__ unsigned char dsm_raw[];
     unsigned char *ring = dsm_raw + ((1024u - (umma::smem_addr(dsm_raw) & 1023u)) & 1023u);  // [NSTG][STAGE]
     float *sm_a = reinterpret_cast<float *>(ring + NSTG * STAGE);                          // [MB][kper]
-    // after the ring has been drained: one row m at a time, [warp][column % 16][column / 16]
-    float(*red)[16][32] = reinterpret_cast<float(*)[16][32]>(ring);
+    // after the ring has been drained: one row m at a time, [warp][column % CPL][column / CPL]
+    float(*red)[CPL][32] = reinterpret_cast<float(*)[CPL][32]>(ring);
     __shared__ uint64_t full[NSTG], empty[NSTG];
     __shared__ bool s_last;
     const int t = threadIdx.x, w = t / 32, lane = t % 32;
     const int ksplit = (int)gridDim.y, rank = (int)blockIdx.y;
-    const long long tile0 = (long long)blockIdx.x * GCOLS;
+    const long long tile0 = (long long)blockIdx.x * TC;
     const long long k0 = (long long)rank * kper, k1 = min(K, k0 + kper);
     const int nk = k1 > k0 ? (int)((k1 - k0 + KT - 1) / KT) : 0;
 
@@ -114,26 +138,25 @@ __global__ void __launch_bounds__(GNT) gemv_int8_kernel(const __grid_constant__ 
     __syncthreads();
     int issued = 0;
     bool bad = false;
-    // blocked layout: this tile's rows are contiguous, 512 bytes each
-    const int8_t *tile_rows = BLK ? qb + (size_t)blockIdx.x * (size_t)K * GCOLS : nullptr;
+    const int8_t *tile_rows = BLK ? qb + (size_t)blockIdx.x * (size_t)K * TC : nullptr;
     auto load_stage = [&](int i, int st) {
         const long long r0 = k0 + (long long)i * KT;
         if (BLK) {
-            const uint32_t bytes = (uint32_t)(min((long long)KT, k1 - r0) * GCOLS);
+            const uint32_t bytes = (uint32_t)(min((long long)KT, k1 - r0) * TC);
             umma::mbar_arrive_expect_tx(&full[st], bytes);
-            umma::bulk_load(ring + st * STAGE, tile_rows + r0 * GCOLS, bytes, &full[st]);
+            umma::bulk_load(ring + st * STAGE, tile_rows + r0 * TC, bytes, &full[st]);
         } else {
             umma::mbar_arrive_expect_tx(&full[st], STAGE);
-            tma_rows(ring + st * STAGE, &map, (int)tile0, (int)r0, &full[st]);
-            tma_rows(ring + st * STAGE + STAGE / 2, &map, (int)tile0 + 256, (int)r0, &full[st]);
+#pragma unroll
+            for (int b = 0; b < TC / 256; ++b)
+                tma_rows(ring + st * STAGE + b * (KT * 256), &map, (int)tile0 + 256 * b, (int)r0, &full[st]);
         }
     };
     if (w == GW) {
         // ---- producer: weights never depend on earlier kernels, so the
         // first stages are issued before the dependency wait
-        if (lane == 0) {
+        if (lane == 0)
             for (; issued < nk && issued < NSTG; ++issued) load_stage(issued, issued);
-        }
         pdl_trigger();
         if (lane == 0) {
             for (; issued < nk && !bad; ++issued) {
@@ -160,24 +183,25 @@ __global__ void __launch_bounds__(GNT) gemv_int8_kernel(const __grid_constant__ 
             sm_a[(long long)m * kper + k] = m < M ? A[(long long)m * K + k0 + k] : 0.f;
         }
         asm volatile("bar.sync 1, %0;" ::"n"(GW * 32) : "memory");
-        float2 acc[MB][8];
+        float2 acc[MB][CPL / 2];
 #pragma unroll
         for (int m = 0; m < MB; ++m)
 #pragma unroll
-            for (int j = 0; j < 8; ++j) acc[m][j] = make_float2(0.f, 0.f);
-        const int box = lane / 16, cw = lane % 16;
-        const int lane_off = BLK ? lane * 16 : box * (STAGE / 2) + cw * 16;
-        const int row_bytes = BLK ? GCOLS : 256;
+            for (int j = 0; j < CPL / 2; ++j) acc[m][j] = make_float2(0.f, 0.f);
+        // blocked rows are TC contiguous bytes; TMA stages hold 256-column boxes one after another
+        const int lane_off = BLK ? lane * CPL : (lane * CPL / 256) * (KT * 256) + (lane * CPL) % 256;
+        const int row_bytes = BLK ? TC : 256;
         for (int i = 0; i < nk; ++i) {
             const int st = i % NSTG;
             if (!umma::mbar_wait(&full[st], (uint32_t)((i / NSTG) & 1), err)) bad = true;
             if (__any_sync(0xffffffffu, bad)) break;
             const unsigned char *sb = ring + st * STAGE + lane_off;
-            uint4 wv[KT / GW];
+            uint32_t wv[KT / GW][CPL / 4];
 #pragma unroll
-            for (int j = 0; j < KT / GW; ++j) wv[j] = *reinterpret_cast<const uint4 *>(sb + (w + GW * j) * row_bytes);
+            for (int j = 0; j < KT / GW; ++j) ld_row<CPL>(sb + (w + GW * j) * row_bytes, wv[j]);
             __syncwarp();
-            if (lane == 0) asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(umma::smem_addr(&empty[st])) : "memory");
+            if (lane == 0)
+                asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(umma::smem_addr(&empty[st])) : "memory");
 #pragma unroll
             for (int j = 0; j < KT / GW; ++j) {
                 const long long rr = k0 + (long long)i * KT + w + GW * j;
@@ -185,24 +209,24 @@ __global__ void __launch_bounds__(GNT) gemv_int8_kernel(const __grid_constant__ 
                     float a[MB];
 #pragma unroll
                     for (int m = 0; m < MB; ++m) a[m] = sm_a[(long long)m * kper + (rr - k0)];
-                    accumulate<MB>(acc, wv[j], a);
+                    accumulate<MB, CPL>(acc, wv[j], a);
                 }
             }
         }
         // add the 8 warps' sums one activation row at a time (in the drained
-        // ring); thread e takes column (e % 32) * 16 + e / 32 of the tile
+        // ring); thread e takes column (e % 32) * CPL + e / 32 of the tile
         asm volatile("bar.sync 1, %0;" ::"n"(GW * 32) : "memory");
 #pragma unroll
         for (int m = 0; m < MB; ++m) {
 #pragma unroll
-            for (int j = 0; j < 8; ++j) {
+            for (int j = 0; j < CPL / 2; ++j) {
                 red[w][2 * j][lane] = acc[m][j].x;
                 red[w][2 * j + 1][lane] = acc[m][j].y;
             }
             asm volatile("bar.sync 1, %0;" ::"n"(GW * 32) : "memory");
-            for (int e = t; e < GCOLS; e += GW * 32) {
+            for (int e = t; e < TC; e += GW * 32) {
                 const int jj = e / 32, ln = e % 32;
-                const long long n = tile0 + ln * 16 + jj;
+                const long long n = tile0 + ln * CPL + jj;
                 float v = 0.f;
 #pragma unroll
                 for (int ww = 0; ww < GW; ++ww) v += red[ww][jj][ln];
@@ -220,7 +244,6 @@ __global__ void __launch_bounds__(GNT) gemv_int8_kernel(const __grid_constant__ 
     // K parts meet in the last CTA of the tile, in K order (a CTA whose wait
     // ran out still counts itself, marked, so the counter always resets)
     __threadfence();
-    __syncthreads();
     bad = __syncthreads_or(bad);
     if (t == 0) {
         const unsigned int mine = bad ? 0x10001u : 1u;
@@ -234,8 +257,8 @@ __global__ void __launch_bounds__(GNT) gemv_int8_kernel(const __grid_constant__ 
     __syncthreads();
     if (!s_last) return;
     __threadfence();
-    for (int e = t; e < MB * GCOLS; e += GNT) {
-        const int m = e / GCOLS, c = e % GCOLS;
+    for (int e = t; e < MB * TC; e += GNT) {
+        const int m = e / TC, c = e % TC;
         const long long n = tile0 + c;
         if (m >= M || n >= N) continue;
         float v = 0.f;
@@ -295,24 +318,44 @@ int gemv_workspace(cudaStream_t st, size_t nctr, size_t npart, unsigned int **ct
 template <int MB, bool BLK>
 int run_gemv(const float *A, const int8_t *q, const float *s, float *Cm, int M, long long K, long long N,
              cudaStream_t st) {
-    const long long tiles = (N + GCOLS - 1) / GCOLS;
-    const long long want = 2ll * sm_count();
-    long long ksplit = std::max<long long>(1, std::min<long long>((want + tiles - 1) / tiles, (K + 2 * KT - 1) / (2 * KT)));
+    constexpr int CPL = GemvCpl<MB>::CPL;
+    using G = GemvGeo<CPL>;
+    auto kern = gemv_int8_kernel<MB, CPL, BLK>;
+    static int occ[64] = {0};  // resident CTAs per SM, per device
+    int dev = 0;
+    int rc = check_cuda(cudaGetDevice(&dev), "gemv: cudaGetDevice");
+    if (rc) return rc;
+    if (dev < 0 || dev >= 64) return set_error(KAI_GDN_ERR_UNSUPPORTED, "gemv: device %d", dev);
+    const size_t ring = 1024 + (size_t)G::NSTG * G::STAGE;
+    if (!occ[dev]) {
+        if ((rc = check_cuda(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 220 * 1024),
+                             "gemv: smem attribute")))
+            return rc;
+        // residency with a K part of up to KMAX_OCC rows of activations
+        int n = 0;
+        if ((rc = check_cuda(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, kern, GNT,
+                                                                            ring + (size_t)MB * KMAX_OCC * 4),
+                             "gemv: occupancy")))
+            return rc;
+        occ[dev] = std::max(1, n);
+    }
+    // one wave: tiles x ksplit <= resident CTAs on the device, each K part at
+    // most KMAX_OCC rows (the residency assumed above)
+    const long long tiles = (N + G::TC - 1) / G::TC;
+    const long long slots = (long long)occ[dev] * sm_count();
+    long long ksplit = std::max<long long>(1, std::min<long long>(slots / tiles, (K + 2 * KT - 1) / (2 * KT)));
+    ksplit = std::max<long long>(ksplit, (K + KMAX_OCC - 1) / KMAX_OCC);
     ksplit = std::min<long long>(ksplit, 0xFFFF);
     long long kper = (K + ksplit - 1) / ksplit;
     kper = (kper + KT - 1) / KT * KT;
     ksplit = (K + kper - 1) / kper;
-    const size_t smem = 1024 + (size_t)NSTG * STAGE + (size_t)MB * (size_t)kper * sizeof(float);
+    const size_t smem = ring + (size_t)MB * (size_t)kper * sizeof(float);
     if (smem > 220 * 1024) return set_error(KAI_GDN_ERR_UNSUPPORTED, "gemv: K part too long");
     unsigned int *ctr = nullptr;
     float *part = nullptr;
-    if (ksplit > 1) {
-        int rc = gemv_workspace(st, (size_t)tiles, (size_t)(ksplit * M * N), &ctr, &part);
-        if (rc) return rc;
-    }
+    if (ksplit > 1 && (rc = gemv_workspace(st, (size_t)tiles, (size_t)(ksplit * M * N), &ctr, &part))) return rc;
     int *err = nullptr;
-    int rc = device_error_word(&err);
-    if (rc) return rc;
+    if ((rc = device_error_word(&err))) return rc;
     CUtensorMap map;
     memset(&map, 0, sizeof(map));
     if (!BLK) {
@@ -327,16 +370,6 @@ int run_gemv(const float *A, const int8_t *q, const float *s, float *Cm, int M, 
                                 CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
         if (cr != CUDA_SUCCESS) return set_error(KAI_GDN_ERR_CUDA, "gemv: tensor map encoding failed (%d)", (int)cr);
     }
-    static int attr_done[64] = {0};
-    int dev = 0;
-    cudaGetDevice(&dev);
-    if (dev >= 0 && dev < 64 && !attr_done[dev]) {
-        rc = check_cuda(cudaFuncSetAttribute(gemv_int8_kernel<MB, BLK>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                             220 * 1024),
-                        "gemv: smem attribute");
-        if (rc) return rc;
-        attr_done[dev] = 1;
-    }
     cudaLaunchConfig_t cfg{};
     cfg.gridDim = dim3((unsigned)tiles, (unsigned)ksplit);
     cfg.blockDim = dim3(GNT);
@@ -347,16 +380,25 @@ int run_gemv(const float *A, const int8_t *q, const float *s, float *Cm, int M, 
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    const cudaError_t le =
-        cudaLaunchKernelEx(&cfg, gemv_int8_kernel<MB, BLK>, map, q, A, s, Cm, M, K, N, kper, part, ctr, err);
+    const cudaError_t le = cudaLaunchKernelEx(&cfg, kern, map, q, A, s, Cm, M, K, N, kper, part, ctr, err);
     if (le != cudaSuccess) return check_cuda(le, "gemv_int8_kernel launch");
     return check_launch("gemv_int8_kernel");
+}
+
+template <bool BLK>
+int dispatch_gemv(const float *A, const int8_t *q, const float *s, float *Cm, size_t M, size_t K, size_t N,
+                  cudaStream_t st) {
+    const long long k = (long long)K, n = (long long)N;
+    if (M == 1) return run_gemv<1, BLK>(A, q, s, Cm, 1, k, n, st);
+    if (M == 2) return run_gemv<2, BLK>(A, q, s, Cm, 2, k, n, st);
+    if (M <= 4) return run_gemv<4, BLK>(A, q, s, Cm, (int)M, k, n, st);
+    return run_gemv<8, BLK>(A, q, s, Cm, (int)M, k, n, st);
 }
 
 }  // namespace
 
 bool gemv_int8_supported(size_t M, size_t K, size_t N, const int8_t *q) {
-    return M >= 1 && M <= 4 && K > 0 && N % 16 == 0 && (uintptr_t)q % 16 == 0 && K < (1ull << 31) &&
+    return M >= 1 && M <= 8 && K > 0 && N % 16 == 0 && (uintptr_t)q % 16 == 0 && K < (1ull << 31) &&
            N < (1ull << 31);
 }
 
@@ -365,34 +407,39 @@ int launch_gemv_int8(const float *A, const int8_t *q, const float *s, float *Cm,
     if (M == 0 || N == 0) return KAI_GDN_OK;
     if (!A || !q || !s || !Cm) return set_error(KAI_GDN_ERR_INVALID, "gemv_int8: null pointer");
     if (!gemv_int8_supported(M, K, N, q)) return set_error(KAI_GDN_ERR_UNSUPPORTED, "gemv_int8: shape");
-    if (M == 1) return run_gemv<1, false>(A, q, s, Cm, 1, (long long)K, (long long)N, st);
-    if (M == 2) return run_gemv<2, false>(A, q, s, Cm, 2, (long long)K, (long long)N, st);
-    return run_gemv<4, false>(A, q, s, Cm, (int)M, (long long)K, (long long)N, st);
+    return dispatch_gemv<false>(A, q, s, Cm, M, K, N, st);
 }
 
-// Blocked weight layout: [ceil(N / 512)][K][512] bytes (the columns of a
-// 512-wide tile contiguous row after row, the last tile zero-padded), so one
-// tile's rows stream as contiguous 16 KB bulk copies.
-__global__ void block_weights_kernel(const int8_t *__restrict__ q, int8_t *__restrict__ qb, long long K, long long N) {
-    const long long tiles = (N + GCOLS - 1) / GCOLS, n16 = tiles * K * (GCOLS / 16);
+// Blocked weight layout for M activation rows: [ceil(N / TC)][K][TC] bytes
+// (TC = 512 for M <= 4, 256 for M <= 8; the columns of a tile contiguous row
+// after row, the last tile zero-padded), so one tile's rows stream as
+// contiguous bulk copies.
+size_t gemv_tile_cols(size_t M) { return M <= 4 ? 512 : 256; }
+
+__global__ void block_weights_kernel(const int8_t *__restrict__ q, int8_t *__restrict__ qb, long long K, long long N,
+                                     long long TC) {
+    const long long tiles = (N + TC - 1) / TC, per = TC / 16, n16 = tiles * K * per;
     for (long long e = blockIdx.x * (long long)blockDim.x + threadIdx.x; e < n16; e += (long long)gridDim.x * blockDim.x) {
-        const long long t = e / (K * (GCOLS / 16)), rem = e % (K * (GCOLS / 16));
-        const long long k = rem / (GCOLS / 16), c16 = rem % (GCOLS / 16);
-        const long long n = t * GCOLS + c16 * 16;
+        const long long t = e / (K * per), rem = e % (K * per);
+        const long long k = rem / per, c16 = rem % per;
+        const long long n = t * TC + c16 * 16;
         uint4 v = make_uint4(0, 0, 0, 0);
         if (n < N) v = *reinterpret_cast<const uint4 *>(q + k * N + n);
-        *reinterpret_cast<uint4 *>(qb + (t * K + k) * GCOLS + c16 * 16) = v;
+        *reinterpret_cast<uint4 *>(qb + (t * K + k) * TC + c16 * 16) = v;
     }
 }
 
-size_t gemv_blocked_bytes(size_t K, size_t N) { return (N + GCOLS - 1) / GCOLS * K * GCOLS; }
+size_t gemv_blocked_bytes(size_t M, size_t K, size_t N) {
+    const size_t tc = gemv_tile_cols(M);
+    return (N + tc - 1) / tc * K * tc;
+}
 
-int gemv_block_weights(const int8_t *q, int8_t *qb, size_t K, size_t N, cudaStream_t st) {
+int gemv_block_weights(size_t M, const int8_t *q, int8_t *qb, size_t K, size_t N, cudaStream_t st) {
     if (N % 16 || (uintptr_t)q % 16 || (uintptr_t)qb % 16)
         return set_error(KAI_GDN_ERR_UNSUPPORTED, "gemv_block_weights: N % 16 and 16-byte alignment");
-    const long long n16 = (long long)gemv_blocked_bytes(K, N) / 16;
-    block_weights_kernel<<<(unsigned)std::min<long long>((n16 + 255) / 256, 65535), 256, 0, st>>>(q, qb, (long long)K,
-                                                                                                 (long long)N);
+    const long long n16 = (long long)gemv_blocked_bytes(M, K, N) / 16;
+    block_weights_kernel<<<(unsigned)std::min<long long>((n16 + 255) / 256, 65535), 256, 0, st>>>(
+        q, qb, (long long)K, (long long)N, (long long)gemv_tile_cols(M));
     return check_launch("block_weights_kernel");
 }
 
@@ -401,9 +448,7 @@ int launch_gemv_int8_blocked(const float *A, const int8_t *qb, const float *s, f
     if (M == 0 || N == 0) return KAI_GDN_OK;
     if (!A || !qb || !s || !Cm) return set_error(KAI_GDN_ERR_INVALID, "gemv_int8: null pointer");
     if (!gemv_int8_supported(M, K, N, qb)) return set_error(KAI_GDN_ERR_UNSUPPORTED, "gemv_int8: shape");
-    if (M == 1) return run_gemv<1, true>(A, qb, s, Cm, 1, (long long)K, (long long)N, st);
-    if (M == 2) return run_gemv<2, true>(A, qb, s, Cm, 2, (long long)K, (long long)N, st);
-    return run_gemv<4, true>(A, qb, s, Cm, (int)M, (long long)K, (long long)N, st);
+    return dispatch_gemv<true>(A, qb, s, Cm, M, K, N, st);
 }
 
 }  // namespace gdn

@@ -476,9 +476,10 @@ int build_qw(ModelEngine *e, QW *w, size_t K, size_t k0, size_t k1, const std::v
     if (!rc) rc = launch_quantize_int8(tmp, qt, w->s, K, N, 0);
     if (!rc) rc = malloc_keep(e, (void **)&w->q, (k1 - k0) * N, false);
     if (!rc) rc = check_cuda(cudaMemcpy(w->q, qt + k0 * N, (k1 - k0) * N, cudaMemcpyDeviceToDevice), "model: codes");
-    if (!rc && e->cfg.batch <= 4 && gemv_int8_supported(e->cfg.batch, k1 - k0, N, w->q)) {
-        if (!(rc = malloc_keep(e, (void **)&w->qb, gemv_blocked_bytes(k1 - k0, N), false)))
-            rc = gemv_block_weights(w->q, w->qb, k1 - k0, N, 0);
+    if (!rc && gemv_int8_supported(e->cfg.batch, k1 - k0, N, w->q)) {
+        const size_t B = e->cfg.batch;
+        if (!(rc = malloc_keep(e, (void **)&w->qb, gemv_blocked_bytes(B, k1 - k0, N), false)))
+            rc = gemv_block_weights(B, w->q, w->qb, k1 - k0, N, 0);
     }
     if (!rc) rc = check_cuda(cudaDeviceSynchronize(), "model: weights");
     if (tmp) cudaFree(tmp);
