@@ -978,43 +978,61 @@ int model_weight(void *engine, size_t layer, int which, void *data, float *scale
 }
 
 // Synthetic state of an already-consumed context of `ctx` tokens (a
-// stand-in for the prefill): every attention layer's K/V cache rows [0, ctx)
-// N(0, 1) in bf16, every GDN state N(0, 0.02), conv histories N(0, 1).
+// stand-in for the prefill), drawn by global index so that every
+// tensor-parallel split holds the same state: every attention layer's K/V
+// cache rows [0, ctx) N(0, 1) in bf16, every GDN state N(0, 0.02), conv
+// histories N(0, 1).
 __global__ void fill_cache_kernel(__nv_bfloat16 *__restrict__ c, long long B, long long max_ctx, long long row,
-                                  long long ctx, unsigned long long seed, unsigned tid) {
+                                  long long grow, long long g0, long long ctx, unsigned long long seed,
+                                  unsigned tid) {
     const long long n = B * ctx * row;
     for (long long e = blockIdx.x * (long long)blockDim.x + threadIdx.x; e < n; e += (long long)gridDim.x * blockDim.x) {
-        const long long b = e / (ctx * row), rem = e % (ctx * row);
-        const unsigned long long u = mix64(seed ^ mix64(((unsigned long long)tid << 40) ^ (unsigned long long)e));
+        const long long bt = e / row, col = e % row, b = bt / ctx, tt = bt % ctx;
+        const unsigned long long idx = (unsigned long long)((b * max_ctx + tt) * grow + g0 + col);
+        const unsigned long long u = mix64(seed ^ mix64(((unsigned long long)tid << 40) ^ idx));
         const float u1 = ((float)(u >> 40) + 0.5f) * 5.9604644775390625e-8f;
         const float u2 = ((float)(u & 0xFFFFFFull) + 0.5f) * 5.9604644775390625e-8f;
-        c[b * max_ctx * row + rem] = __float2bfloat16_rn(sqrtf(-2.0f * logf(u1)) * cospif(2.0f * u2));
+        c[(b * max_ctx + tt) * row + col] = __float2bfloat16_rn(sqrtf(-2.0f * logf(u1)) * cospif(2.0f * u2));
     }
 }
 int model_fill(void *engine, size_t ctx, unsigned long long seed) {
     ModelEngine *e = static_cast<ModelEngine *>(engine);
     if (!e) return set_error(KAI_GDN_ERR_INVALID, "model_fill: null engine");
     if (ctx > e->cfg.max_ctx) return set_error(KAI_GDN_ERR_INVALID, "model_fill: ctx %zu > max_ctx", ctx);
-    const size_t B = e->cfg.batch;
+    const kai_gdn_model_config &c = e->cfg;
+    const size_t B = c.batch, d = e->d, R = (size_t)c.tp_rank;
+    const size_t hv0 = R * e->hv, hk0 = R * e->hk, GK = c.gdn_heads_k * d, GV = c.gdn_heads_v * d;
     int rc = 0;
     for (size_t l = 0; l < e->layers.size() && !rc; ++l) {
         ModelEngine::Layer &L = e->layers[l];
-        const unsigned t = (unsigned)(l * 64 + 40) + (unsigned)e->cfg.tp_rank * 7919u;
+        const unsigned t = (unsigned)(l * 64 + 40);
         if (e->is_gdn[l]) {
-            const long long ns = (long long)(B * e->hv * e->d * e->d);
-            rng_normal_kernel<<<grid_for(ns), 256>>>(L.state, 1, ns, ns, 0, 0, ns, seed, t, 0.02f);
+            // state [B][hv][d][d]: global heads hv0 .. of Hv
+            const long long per = (long long)(e->hv * d * d), gper = (long long)(c.gdn_heads_v * d * d);
+            rng_normal_kernel<<<grid_for((long long)B * per), 256>>>(L.state, (long long)B, per, per, 0,
+                                                                    (long long)(hv0 * d * d), gper, seed, t, 0.02f);
             rc = check_launch("rng_normal_kernel");
-            const long long nh = (long long)(B * 3 * e->C);
-            if (!rc) rng_normal_kernel<<<grid_for(nh), 256>>>(L.hist, 1, nh, nh, 0, 0, nh, seed, t + 1, 1.0f);
-            if (!rc) rc = check_launch("rng_normal_kernel");
+            // history [B][3][C]: this rank's q, k and v channels of the global [3][2 GK + GV]
+            const size_t gc = 2 * GK + GV;
+            const size_t segs[3][2] = {{hk0 * d, e->hk * d}, {GK + hk0 * d, e->hk * d}, {2 * GK + hv0 * d, e->hv * d}};
+            size_t col = 0;
+            for (int sg = 0; sg < 3 && !rc; ++sg) {
+                rng_normal_kernel<<<grid_for((long long)(B * 3 * segs[sg][1])), 256>>>(
+                    L.hist + col, (long long)(B * 3), (long long)segs[sg][1], (long long)e->C, 0,
+                    (long long)segs[sg][0], (long long)gc, seed, t + 1, 1.0f);
+                rc = check_launch("rng_normal_kernel");
+                col += segs[sg][1];
+            }
         } else if (ctx > 0) {
-            const long long row = (long long)(e->hkv * e->D), n = (long long)B * (long long)ctx * row;
+            const long long row = (long long)(e->hkv * e->D), grow = (long long)(c.attn_kv_heads * e->D);
+            const long long g0 = (long long)(e->kv_first * e->D), n = (long long)B * (long long)ctx * row;
             fill_cache_kernel<<<grid_for(n), 256>>>(static_cast<__nv_bfloat16 *>(L.kc), (long long)B,
-                                                   (long long)e->cfg.max_ctx, row, (long long)ctx, seed, t + 2);
+                                                   (long long)c.max_ctx, row, grow, g0, (long long)ctx, seed, t + 2);
             rc = check_launch("fill_cache_kernel");
             if (!rc)
                 fill_cache_kernel<<<grid_for(n), 256>>>(static_cast<__nv_bfloat16 *>(L.vc), (long long)B,
-                                                       (long long)e->cfg.max_ctx, row, (long long)ctx, seed, t + 3);
+                                                       (long long)c.max_ctx, row, grow, g0, (long long)ctx, seed,
+                                                       t + 3);
             if (!rc) rc = check_launch("fill_cache_kernel");
         }
     }
