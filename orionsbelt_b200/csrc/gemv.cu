@@ -39,9 +39,11 @@ constexpr int KMAX_OCC = 1024;     // longest K part (rows) a CTA takes
 
 // Tile geometry: CPL columns per lane (16: one 16-byte load per row, for up
 // to 4 activation rows; 8: an 8-byte load, for 5..8 rows, which keeps the
-// accumulators in registers), 32 lanes per tile, NSTG stages of KT rows.
-// (At 16 rows the CUDA cores' multiply-adds, not HBM, bound this kernel:
-// measured 48 us at 16 x 2560 x 9216 against 39 us on the tensor-core path.)
+// accumulators in registers), 32 lanes per tile, NSTG stages of KT rows.  The
+// activation tile is [k][m], so a weight row's activations are broadcast
+// vector loads.  (At 16 rows this kernel measured 46 us at 16 x 2560 x 9216,
+// one CTA per SM by registers, against 39 us on the tensor-core path, which
+// keeps M > 8.)
 template <int CPL> struct GemvGeo {
     static constexpr int TC = 32 * CPL;         // columns per CTA tile
     static constexpr int STAGE = KT * TC;       // bytes per ring stage
@@ -117,7 +119,7 @@ __global__ void __launch_bounds__(GNT) gemv_int8_kernel(const __grid_constant__ 
     constexpr int TC = G::TC, STAGE = G::STAGE, NSTG = G::NSTG;
     extern __shared__ unsigned char dsm_raw[];
     unsigned char *ring = dsm_raw + ((1024u - (umma::smem_addr(dsm_raw) & 1023u)) & 1023u);  // [NSTG][STAGE]
-    float *sm_a = reinterpret_cast<float *>(ring + NSTG * STAGE);                          // [MB][kper]
+    float *sm_a = reinterpret_cast<float *>(ring + NSTG * STAGE);                          // [kper][MB]
     // after the ring has been drained: one row m at a time, [warp][column % CPL][column / CPL]
     float(*red)[CPL][32] = reinterpret_cast<float(*)[CPL][32]>(ring);
     __shared__ uint64_t full[NSTG], empty[NSTG];
@@ -180,7 +182,7 @@ __global__ void __launch_bounds__(GNT) gemv_int8_kernel(const __grid_constant__ 
         for (long long e = t; e < (long long)MB * kn; e += GW * 32) {
             const int m = (int)(e / kn);
             const long long k = e % kn;
-            sm_a[(long long)m * kper + k] = m < M ? A[(long long)m * K + k0 + k] : 0.f;
+            sm_a[k * MB + m] = m < M ? A[(long long)m * K + k0 + k] : 0.f;
         }
         asm volatile("bar.sync 1, %0;" ::"n"(GW * 32) : "memory");
         float2 acc[MB][CPL / 2];
@@ -207,8 +209,17 @@ __global__ void __launch_bounds__(GNT) gemv_int8_kernel(const __grid_constant__ 
                 const long long rr = k0 + (long long)i * KT + w + GW * j;
                 if (rr < k1) {
                     float a[MB];
+                    const float *ar = sm_a + (rr - k0) * MB;  // broadcast vector loads
+                    if constexpr (MB % 4 == 0) {
 #pragma unroll
-                    for (int m = 0; m < MB; ++m) a[m] = sm_a[(long long)m * kper + (rr - k0)];
+                        for (int m = 0; m < MB; m += 4) {
+                            const float4 v = *reinterpret_cast<const float4 *>(ar + m);
+                            a[m] = v.x, a[m + 1] = v.y, a[m + 2] = v.z, a[m + 3] = v.w;
+                        }
+                    } else {
+#pragma unroll
+                        for (int m = 0; m < MB; ++m) a[m] = ar[m];
+                    }
                     accumulate<MB, CPL>(acc, wv[j], a);
                 }
             }
