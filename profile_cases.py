@@ -2,7 +2,7 @@
 
     python profile_cases.py decode [--launches 3]
     python profile_cases.py chunk  [--launches 1]
-    python profile_cases.py conv | cumsum | scan | attn | int8
+    python profile_cases.py conv | cumsum | scan | attn | int8 | int8m16 | lmhead | model
 
 Each case holds a few hundred MB to a few GB on the device (inputs larger
 than the 126 MB L2, so DRAM counters mean something), runs a few launches of
@@ -17,6 +17,10 @@ its kernel through the C ABI, and exits.  Cases:
           32768-token bf16 KV cache (537 MB)
   int8    int8-weight GEMV, M=1, K=2560, N=9216 (23.6 MB of weights)
   int8m16 the same weights, M=16 (the tensor-core path)
+  lmhead  int8-weight GEMV over the config-4 LM head, M=1, K=2560, N=151936
+          (389 MB of weights)
+  model   the config-4 engine (4B geometry, batch 1, synthetic 32k context):
+          one greedy decode step per launch
 """
 from __future__ import annotations
 
@@ -33,7 +37,8 @@ from orionsbelt_b200 import _lib, ops, synth  # noqa: E402
 
 def main() -> None:
     ap = argparse.ArgumentParser()
-    ap.add_argument("case", choices=["decode", "chunk", "conv", "cumsum", "scan", "attn", "int8", "int8m16"])
+    ap.add_argument("case", choices=["decode", "chunk", "conv", "cumsum", "scan", "attn", "int8", "int8m16", "lmhead",
+                                     "model"])
     ap.add_argument("--launches", type=int, default=3)
     a = ap.parse_args()
     torch.cuda.set_device(0)
@@ -76,6 +81,30 @@ def main() -> None:
         A = synth.device_normal((M, 2560), 7, 2)
         Cm = torch.empty((M, 9216), device="cuda")
         fn = lambda: ops.matmul_int8(A, q8, s8, Cm)  # noqa: E731
+    elif a.case == "lmhead":
+        K, N = 2560, 151936
+        W = synth.device_normal((K, N), 8, 1, std=0.02)
+        q8 = torch.empty((K, N), dtype=torch.int8, device="cuda")
+        s8 = torch.empty(N, device="cuda")
+        ops.quantize_int8(W, q8, s8)
+        del W
+        A = synth.device_normal((1, K), 8, 2)
+        Cm = torch.empty((1, N), device="cuda")
+        fn = lambda: ops.matmul_int8(A, q8, s8, Cm)  # noqa: E731
+    elif a.case == "model":
+        import numpy as np
+
+        import bench
+        eng = ops.ModelEngine(dict(bench.CFG4, max_ctx=32768 + 64), 1, seed=42)
+        eng.fill(32768, seed=3)
+        eng.set_tokens(np.zeros(1, np.int32))
+        side = torch.cuda.Stream()
+        step = [0]
+
+        def fn():
+            with torch.cuda.stream(side):
+                eng.step(32768 + step[0], side)
+            step[0] += 1
     else:
         g = torch.sigmoid(synth.device_normal((4096, 8192), 5, 1))
         x = synth.device_normal((4096, 8192), 5, 2)
