@@ -233,6 +233,23 @@ KAI_GDN_API int kai_run_gdn_quantize_int8_sm100a(const float *B, int8_t *q, floa
  * holds.  Deterministic. */
 KAI_GDN_API int kai_run_gdn_matmul_int8_sm100a(const float *A, const int8_t *q, const float *s, float *C, size_t M,
                                                size_t K, size_t N, void *stream);
+/* The same product over weights packed once for streaming (the analogue of
+ * the reference preparing its QW weights once at load, quantize_weight,
+ * gdn_e2e_decode.c:175-199).  kai_gdn_int8_packed_bytes gives the size of
+ * the packed form of q [K][N] (0 when N % 16 is non-zero or K > 131072);
+ * kai_run_gdn_int8_pack_sm100a writes it (qp 16-byte aligned, device
+ * memory, not aliasing q); kai_run_gdn_matmul_int8_packed_sm100a computes C
+ * from it on the int8 tensor cores, 16 activation rows per pass over the
+ * weights.  Each activation row is carried as three 8-bit fixed-point terms
+ * of its largest magnitude (representation error at most 2^-24 of it, one
+ * fp32 rounding) and the products are summed exactly in integers, so the
+ * result is deterministic whatever the work split, and agrees with
+ * kai_run_gdn_matmul_int8_sm100a to fp32 accuracy.  Activations must be
+ * finite. */
+KAI_GDN_API size_t kai_gdn_int8_packed_bytes(size_t K, size_t N);
+KAI_GDN_API int kai_run_gdn_int8_pack_sm100a(const int8_t *q, int8_t *qp, size_t K, size_t N, void *stream);
+KAI_GDN_API int kai_run_gdn_matmul_int8_packed_sm100a(const float *A, const int8_t *qp, const float *s, float *C,
+                                                      size_t M, size_t K, size_t N, void *stream);
 
 /* Grouped-query attention decode with a growing KV cache, the full-attention
  * layer of the reference's hybrid decode: full_attn_real_forward

@@ -103,6 +103,9 @@ SIGNATURES = {
     "kai_gdn_e2e_state": (_i, [_vp, _sz, _vp, _vp]),
     "kai_gdn_e2e_destroy": (_i, [_vp]),
     "kai_run_gdn_matmul_int8_sm100a": (_i, [_vp, _vp, _vp, _vp, _sz, _sz, _sz, _vp]),
+    "kai_gdn_int8_packed_bytes": (_sz, [_sz, _sz]),
+    "kai_run_gdn_int8_pack_sm100a": (_i, [_vp, _vp, _sz, _sz, _vp]),
+    "kai_run_gdn_matmul_int8_packed_sm100a": (_i, [_vp, _vp, _vp, _vp, _sz, _sz, _sz, _vp]),
     "kai_run_gdn_chunk_delta_rule_sm100a": (_i, [C.POINTER(ChunkArgs), _vp]),
     "kai_gdn_model_nccl_id": (_i, [_vp]),
     "kai_gdn_model_create": (_i, [C.POINTER(ModelConfig), C.POINTER(_vp)]),

@@ -83,6 +83,14 @@ int launch_gemv_int8_blocked(const float *A, const int8_t *qb, const float *s, f
                              size_t N, cudaStream_t st);
 int launch_matmul_int8_tc(const float *A, const int8_t *q, const float *s, float *C, size_t M, size_t K, size_t N,
                           cudaStream_t st);
+// Weight-streaming tensor-core matmul over weights packed once into its
+// streaming layout (int8_packed.cu): 16 activation rows per launch, launched
+// as a programmatic dependent of the previous kernel on the stream.
+bool int8_packed_supported(size_t K, size_t N);
+size_t int8_packed_bytes(size_t K, size_t N);
+int int8_pack_weights(const int8_t *q, int8_t *qp, size_t K, size_t N, cudaStream_t st);
+int launch_matmul_int8_packed(const float *A, const int8_t *qp, const float *s, float *C, size_t M, size_t K,
+                              size_t N, cudaStream_t st);
 // Per-stream split-K workspace of the int8 matmuls: slab counters (zero
 // between calls: each kernel's last CTA resets its counter) and partial sums.
 int split_workspace(cudaStream_t st, size_t nctr, size_t npart, unsigned int **ctr, float **part);

@@ -397,7 +397,8 @@ unsigned grid_for(long long n) { return (unsigned)std::min<long long>((n + 255) 
 
 struct QW {
     int8_t *q = nullptr;   // [K][N]
-    int8_t *qb = nullptr;  // the same codes in the GEMV's blocked layout (batch <= 4)
+    int8_t *qb = nullptr;  // the same codes in the GEMV's blocked layout (small batches)
+    int8_t *qp = nullptr;  // the same codes packed for the tensor-core stream (larger batches, LM head)
     float *s = nullptr;
     size_t K = 0, N = 0;
 };
@@ -456,7 +457,13 @@ int malloc_keep(ModelEngine *e, void **p, size_t bytes, bool zero) {
 // A [K][N] int8 projection of this rank: the column parts (each a column range
 // of a global tensor) side by side, rows [k0, k1) of the global K rows; the
 // per-column scales come from all K rows, as in the unsharded model.
-int build_qw(ModelEngine *e, QW *w, size_t K, size_t k0, size_t k1, const std::vector<Part> &parts, float stdv) {
+// Which kernel streams a projection: the CUDA-core GEMV for batch <= 4 (one
+// launch, no activation preparation), the int8 tensor-core stream above that
+// and for the LM head at every batch (measured faster there from batch 1).
+constexpr size_t GEMV_MAX_BATCH = 4;
+
+int build_qw(ModelEngine *e, QW *w, size_t K, size_t k0, size_t k1, const std::vector<Part> &parts, float stdv,
+             bool lm_head = false) {
     size_t N = 0;
     for (const Part &p : parts) N += p.ncols;
     float *tmp = nullptr;
@@ -476,8 +483,11 @@ int build_qw(ModelEngine *e, QW *w, size_t K, size_t k0, size_t k1, const std::v
     if (!rc) rc = launch_quantize_int8(tmp, qt, w->s, K, N, 0);
     if (!rc) rc = malloc_keep(e, (void **)&w->q, (k1 - k0) * N, false);
     if (!rc) rc = check_cuda(cudaMemcpy(w->q, qt + k0 * N, (k1 - k0) * N, cudaMemcpyDeviceToDevice), "model: codes");
-    if (!rc && gemv_int8_supported(e->cfg.batch, k1 - k0, N, w->q)) {
-        const size_t B = e->cfg.batch;
+    const size_t B = e->cfg.batch;
+    if (!rc && (lm_head || B > GEMV_MAX_BATCH) && int8_packed_supported(k1 - k0, N)) {
+        if (!(rc = malloc_keep(e, (void **)&w->qp, int8_packed_bytes(k1 - k0, N), false)))
+            rc = int8_pack_weights(w->q, w->qp, k1 - k0, N, 0);
+    } else if (!rc && gemv_int8_supported(B, k1 - k0, N, w->q)) {
         if (!(rc = malloc_keep(e, (void **)&w->qb, gemv_blocked_bytes(B, k1 - k0, N), false)))
             rc = gemv_block_weights(B, w->q, w->qb, k1 - k0, N, 0);
     }
@@ -519,6 +529,7 @@ enum : unsigned {
 unsigned tidl(size_t layer, unsigned kind) { return (unsigned)(layer * 64 + kind); }
 
 int mm(const float *A, const QW &w, float *Cm, size_t M, cudaStream_t st) {
+    if (w.qp) return launch_matmul_int8_packed(A, w.qp, w.s, Cm, M, w.K, w.N, st);
     if (w.qb) return launch_gemv_int8_blocked(A, w.qb, w.s, Cm, M, w.K, w.N, st);
     return launch_matmul_int8(A, w.q, w.s, Cm, M, w.K, w.N, st);
 }
@@ -820,7 +831,7 @@ int model_create(const kai_gdn_model_config *cfg, void **out) {
                           {{tidl(l, T_GATE), c.inter, I0, e->I}, {tidl(l, T_UP), c.inter, I0, e->I}}, sd);
         if (!rc) rc = build_qw(e, &L.wdown, c.inter, I0, I0 + e->I, {{tidl(l, T_DOWN), H, 0, H}}, sd);
     }
-    if (!rc) rc = build_qw(e, &e->lm, H, 0, H, {{T_LM, c.vocab, e->v0, e->V}}, sd);
+    if (!rc) rc = build_qw(e, &e->lm, H, 0, H, {{T_LM, c.vocab, e->v0, e->V}}, sd, true);
     if (!rc) rc = vec_normal(e, &e->w_final, H, 0, T_FINAL, sd, 1.0f);
     if (!rc) {  // embedding table [vocab][hidden], int8 per token row (replicated)
         const size_t rows_per = 8192;

@@ -434,6 +434,17 @@ int kai_run_gdn_matmul_int8_sm100a(const float *A, const int8_t *q, const float 
     return launch_matmul_int8(A, q, s, C, M, K, N, (cudaStream_t)stream);
 }
 
+size_t kai_gdn_int8_packed_bytes(size_t K, size_t N) { return int8_packed_supported(K, N) ? int8_packed_bytes(K, N) : 0; }
+
+int kai_run_gdn_int8_pack_sm100a(const int8_t *q, int8_t *qp, size_t K, size_t N, void *stream) {
+    return int8_pack_weights(q, qp, K, N, (cudaStream_t)stream);
+}
+
+int kai_run_gdn_matmul_int8_packed_sm100a(const float *A, const int8_t *qp, const float *s, float *C, size_t M,
+                                          size_t K, size_t N, void *stream) {
+    return launch_matmul_int8_packed(A, qp, s, C, M, K, N, (cudaStream_t)stream);
+}
+
 int kai_run_gdn_chunk_delta_rule_sm100a(const kai_gdn_chunk_args *args, void *stream) {
     return launch_chunk(args, (cudaStream_t)stream);
 }

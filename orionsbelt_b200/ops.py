@@ -10,7 +10,7 @@ Two layers, both calling the C ABI (include/kai_gdn_cuda.h) through ctypes:
 * The device layer takes CUDA tensors (torch is used only to own device memory
   and streams) and launches on the current torch stream: ``cumdecay``,
   ``cumsum``, ``gated_scan``, ``gdn2_gated_scan``, ``causal_dwconv1d``,
-  ``matmul``, ``quantize_int8``, ``matmul_int8``, ``attention_decode``, ``E2EEngine``, ``delta_rule_decode``,
+  ``matmul``, ``quantize_int8``, ``matmul_int8``, ``pack_int8``, ``matmul_int8_packed``, ``attention_decode``, ``E2EEngine``, ``delta_rule_decode``,
   ``gdn2_delta_rule_decode`` and ``chunk_delta_rule``.
 
 There is no CPU fallback anywhere: a missing library raises at import of the
@@ -178,6 +178,31 @@ def matmul_int8(A, q, s, Cm, stream=None) -> None:
     N = q.shape[1]
     check(lib().kai_run_gdn_matmul_int8_sm100a(_dev(A, dtype=f), _dev(q, dtype=torch.int8), _dev(s, dtype=f),
                                                _dev(Cm, dtype=f), M, K, N, _stream(stream)))
+
+
+def pack_int8(q, stream=None):
+    """The streaming layout of q [K][N] int8 for matmul_int8_packed (a new
+    uint8 device tensor; the reference prepares its QW weights once at load
+    the same way, quantize_weight, gdn_e2e_decode.c:175-199)."""
+    torch = _torch()
+    K, N = q.shape
+    nbytes = lib().kai_gdn_int8_packed_bytes(K, N)
+    if nbytes == 0:
+        raise ValueError(f"pack_int8: N % 16 must be zero and K <= 131072 (K={K}, N={N})")
+    qp = torch.empty(nbytes, dtype=torch.uint8, device=q.device)
+    check(lib().kai_run_gdn_int8_pack_sm100a(_dev(q, dtype=torch.int8), qp.data_ptr(), K, N, _stream(stream)))
+    return qp
+
+
+def matmul_int8_packed(A, qp, s, Cm, stream=None) -> None:
+    """Cm [M][N] = (A [M][K] . q) * s[n] over qp = pack_int8(q), on the tensor
+    cores (16 rows of A per pass over the weights)."""
+    torch = _torch()
+    f = torch.float32
+    M, K = A.shape
+    N = Cm.shape[1]
+    check(lib().kai_run_gdn_matmul_int8_packed_sm100a(_dev(A, dtype=f), qp.data_ptr(), _dev(s, dtype=f),
+                                                      _dev(Cm, dtype=f), M, K, N, _stream(stream)))
 
 
 def attn_decode_args(q, k_new, v_new, k_cache, v_cache, o, pos: int, scale: float, k_scale=None,

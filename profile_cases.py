@@ -2,7 +2,7 @@
 
     python profile_cases.py decode [--launches 3]
     python profile_cases.py chunk  [--launches 1]
-    python profile_cases.py conv | cumsum | scan | attn | int8 | int8m16 | lmhead | model
+    python profile_cases.py conv | cumsum | scan | attn | int8 | int8m16 | lmhead | lmhead16 | ffn16 | model
 
 Each case holds a few hundred MB to a few GB on the device (inputs larger
 than the 126 MB L2, so DRAM counters mean something), runs a few launches of
@@ -19,6 +19,9 @@ its kernel through the C ABI, and exits.  Cases:
   int8m16 the same weights, M=16 (the tensor-core path)
   lmhead  int8-weight GEMV over the config-4 LM head, M=1, K=2560, N=151936
           (389 MB of weights)
+  lmhead16 the LM head weights packed for streaming, M=16 (the tensor-core
+          weight-streaming kernel)
+  ffn16   the packed path on the FFN up weights, M=16
   model   the config-4 engine (4B geometry, batch 1, synthetic 32k context):
           one greedy decode step per launch
 """
@@ -38,7 +41,7 @@ from orionsbelt_b200 import _lib, ops, synth  # noqa: E402
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("case", choices=["decode", "chunk", "conv", "cumsum", "scan", "attn", "int8", "int8m16", "lmhead",
-                                     "model"])
+                                     "lmhead16", "ffn16", "model"])
     ap.add_argument("--launches", type=int, default=3)
     a = ap.parse_args()
     torch.cuda.set_device(0)
@@ -91,6 +94,18 @@ def main() -> None:
         A = synth.device_normal((1, K), 8, 2)
         Cm = torch.empty((1, N), device="cuda")
         fn = lambda: ops.matmul_int8(A, q8, s8, Cm)  # noqa: E731
+    elif a.case in ("lmhead16", "ffn16"):
+        K, N = (2560, 151936) if a.case == "lmhead16" else (2560, 9216)
+        W = synth.device_normal((K, N), 8, 1, std=0.02)
+        q8 = torch.empty((K, N), dtype=torch.int8, device="cuda")
+        s8 = torch.empty(N, device="cuda")
+        ops.quantize_int8(W, q8, s8)
+        del W
+        qp = ops.pack_int8(q8)
+        del q8
+        A = synth.device_normal((16, K), 8, 2)
+        Cm = torch.empty((16, N), device="cuda")
+        fn = lambda: ops.matmul_int8_packed(A, qp, s8, Cm)  # noqa: E731
     elif a.case == "model":
         import numpy as np
 

@@ -4,8 +4,9 @@ matmul, decode step and attention decode with the elementwise steps of the
 reference's layer notes (docs/GDN_ARCHITECTURE_AUDIT.md sections 2-3).
 
 A reduced geometry (two blocks of 3 GDN + 1 attention layer, hidden 256,
-vocab 4096) runs six greedy steps of three sequences, teacher-forced with the
-oracle's own tokens so both sides see the same inputs at every step.
+vocab 4096) runs six greedy steps of three and of six sequences,
+teacher-forced with the oracle's own tokens so both sides see the same inputs
+at every step.
 Bars: hidden state and logits within 1e-3 relative L2 at every step (fp32
 arithmetic in other orders through eight layers: int8 matmul sums, norms);
 the engine's argmax equals the oracle's wherever the oracle's top two logits
@@ -31,7 +32,11 @@ GEOM = dict(hidden=256, vocab=4096, inter=512, is_gdn=[1, 1, 1, 0, 1, 1, 1, 0], 
 B, STEPS = 3, 6
 
 
-def test_model_matches_oracle(cuda, orc):
+@pytest.mark.parametrize("B", [3, 6])
+def test_model_matches_oracle(cuda, orc, B):
+    """Batch 3 streams the layer projections with the CUDA-core GEMV, batch 6
+    with the int8 tensor-core kernel; the LM head takes the tensor cores at
+    every batch."""
     from oracle.model import ModelOracle, read_weights
 
     torch = cuda
@@ -40,7 +45,7 @@ def test_model_matches_oracle(cuda, orc):
     W = read_weights(eng, GEOM)
     mo = ModelOracle(orc, GEOM, B, W)
     H, V = GEOM["hidden"], GEOM["vocab"]
-    tok = np.array([5, 1000, 4095], np.int32)
+    tok = np.array([5, 1000, 4095, 7, 2048, 1][:B], np.int32)
     with torch.cuda.stream(stream):
         for pos in range(STEPS):
             eng.set_tokens(tok)
