@@ -776,20 +776,37 @@ def run_rows(args, peaks) -> dict:
            "bf16 q/k/v/o, fp32 per-channel gates)", metrics.gdn2_decode_bytes(64, 16, 32, 128, 128), ms,
            "decode_step_kernel<128, f32, GDN-2>")
     del d, g2, bg2, wg2, o2, q2, k2, v2, S2
-    # f2: int8-weight GEMV / small GEMM at the config-4 FFN shapes (hidden
-    # 2560, FFN 9216): up / gate projection, down projection, batch 16
-    for name, (M, K, N) in [("f2_int8_gemv_ffn_up", (1, 2560, 9216)), ("f2_int8_gemv_ffn_down", (1, 9216, 2560)),
-                            ("f2_int8_gemm_b16_ffn_up", (16, 2560, 9216))]:
+    # f2: int8-weight GEMV / small GEMM at the config-4 shapes (hidden 2560,
+    # FFN 9216, vocab 151936): the row-major drop-in (kai_run_gdn_matmul_int8)
+    # and the packed-weight tensor-core stream (kai_run_gdn_matmul_int8_packed)
+    kern_rm = {1: "gemv_int8_kernel (row-major weights, TMA ring)", 16: "matmul_int8_tc_kernel (row-major weights)"}
+    for name, (M, K, N), packed in [("f2_int8_gemv_ffn_up", (1, 2560, 9216), False),
+                                    ("f2_int8_gemv_ffn_down", (1, 9216, 2560), False),
+                                    ("f2_int8_gemm_b16_ffn_up", (16, 2560, 9216), False),
+                                    ("f2_int8_packed_b16_ffn_up", (16, 2560, 9216), True),
+                                    ("f2_int8_packed_b16_ffn_down", (16, 9216, 2560), True),
+                                    ("f2_int8_packed_b16_gate_up", (16, 2560, 18432), True),
+                                    ("f2_int8_packed_lm_head_b1", (1, 2560, 151936), True),
+                                    ("f2_int8_packed_lm_head_b16", (16, 2560, 151936), True)]:
         W = synth.device_normal((K, N), 16, 1, std=0.05)
         q8 = torch.empty((K, N), dtype=torch.int8, device="cuda")
         s8 = torch.empty(N, device="cuda")
         ops.quantize_int8(W, q8, s8)
+        del W
         A8 = synth.device_normal((M, K), 16, 2)
         C8 = torch.empty((M, N), device="cuda")
-        ms = _time(lambda A8=A8, q8=q8, s8=s8, C8=C8: ops.matmul_int8(A8, q8, s8, C8), reps, flush)
-        bw_row(name, f"int8 weights x fp32 activations, M={M} K={K} N={N} (per-column scales)",
-               metrics.int8_matmul_bytes(M, K, N), ms, "matmul_int8_stream_kernel (cluster split-K)")
-        del W, q8, s8, A8, C8
+        if packed:
+            qp = ops.pack_int8(q8)
+            ms = _time(lambda A8=A8, qp=qp, s8=s8, C8=C8: ops.matmul_int8_packed(A8, qp, s8, C8), reps, flush)
+            kern = "act_terms_kernel + int8_packed_kernel (kind::i8 tcgen05, stream-K)"
+            del qp
+        else:
+            ms = _time(lambda A8=A8, q8=q8, s8=s8, C8=C8: ops.matmul_int8(A8, q8, s8, C8), reps, flush)
+            kern = kern_rm[M]
+        bw_row(name, f"int8 weights x fp32 activations, M={M} K={K} N={N} (per-column scales"
+               f"{', weights packed once' if packed else ''}), one call after the L2 flush",
+               metrics.int8_matmul_bytes(M, K, N), ms, kern)
+        del q8, s8, A8, C8
     # f3: GQA attention decode at the config-4 geometry (16 query / 4 kv
     # heads, head_dim 256) over a 32768-token cache: bf16 at batch 1 and 16,
     # int8 (per-head scales) at batch 1
@@ -1079,15 +1096,23 @@ def cpu_rows(nthreads: int) -> dict:
     del S
     # f2: int8 weights, the reference's own gemv_int8_neon / gemm_int8_neon (scalar branch)
     if oracle.ref_int8 is not None:
-        for name, (M, K, N) in [("f2_int8_gemv_ffn_up", (1, 2560, 9216)), ("f2_int8_gemv_ffn_down", (1, 9216, 2560)),
-                                ("f2_int8_gemm_b16_ffn_up", (16, 2560, 9216))]:
-            W = (f32(K, N) * 0.05).astype(np.float32)
+        # (the packed rows compute the same product; the reference has one weight layout)
+        for names, (M, K, N), Ns in [(("f2_int8_gemv_ffn_up",), (1, 2560, 9216), 9216),
+                                     (("f2_int8_gemv_ffn_down",), (1, 9216, 2560), 2560),
+                                     (("f2_int8_gemm_b16_ffn_up", "f2_int8_packed_b16_ffn_up"), (16, 2560, 9216), 9216),
+                                     (("f2_int8_packed_b16_ffn_down",), (16, 9216, 2560), 2560),
+                                     (("f2_int8_packed_b16_gate_up",), (16, 2560, 18432), 18432),
+                                     (("f2_int8_packed_lm_head_b1",), (1, 2560, 151936), 151936),
+                                     (("f2_int8_packed_lm_head_b16",), (16, 2560, 151936), 151936)]:
+            W = (f32(K, Ns) * 0.05).astype(np.float32)
             q8, s8 = oracle.ref_int8.quantize_int8(W)
             A8 = f32(M, K)
-            bw(name, metrics.int8_matmul_bytes(M, K, N), lambda A8=A8, q8=q8, s8=s8: oracle.ref_int8.matmul_int8(
-                A8, q8, s8), "reference", 1,
-               f"full size, M={M} K={K} N={N}, the reference's {'gemv' if M == 1 else 'gemm'}_int8_neon "
-               f"(gdn_e2e_decode.c, scalar branch, single thread)")
+            what = "full size" if Ns == N else f"{Ns} of the {N} columns, GB/s of the sample"
+            for name in names:
+                bw(name, metrics.int8_matmul_bytes(M, K, Ns), lambda A8=A8, q8=q8, s8=s8: oracle.ref_int8.matmul_int8(
+                    A8, q8, s8), "reference", 1,
+                   f"{what}, M={M} K={K} N={N}, the reference's {'gemv' if M == 1 else 'gemm'}_int8_neon "
+                   f"(gdn_e2e_decode.c, scalar branch, single thread)")
     # f3: attention decode over a 32768-token cache; bf16 cache: oracle (the
     # reference's attention has fp32 / int8 caches only); int8: the reference's own
     H, Hkv, D, ctx = 16, 4, 256, 32768

@@ -278,6 +278,27 @@ typedef struct kai_gdn_attn_decode_args {
 } kai_gdn_attn_decode_args;
 KAI_GDN_API int kai_run_gdn_attention_decode_sm100a(const kai_gdn_attn_decode_args *args, void *stream);
 
+/* The same attention for a whole prompt (not in the reference, which feeds
+ * its prompt one token at a time through full_attn_real_forward): the keys
+ * and values of positions 0 .. pos0 + T - 1 are already in the bf16 caches,
+ * and query t of sequence b (position pos0 + t) attends over positions
+ * 0 .. pos0 + t (causal):
+ *   o[b][t][h] = sum_{s <= pos0 + t} softmax_s((q[b][t][h] . k_s) * scale) v_s.
+ * Equal to T calls of kai_run_gdn_attention_decode_sm100a (positions pos0 ..)
+ * to fp32 accuracy (queries and softmax weights carried as two bf16 terms,
+ * 16 significant bits; products summed in fp32).  bf16 caches only;
+ * head_dim 128 or 256; 1, 2, 4 or 8 query heads per kv head; caches 16-byte
+ * aligned. */
+typedef struct kai_gdn_attn_prefill_args {
+    const float *q;        /* [batch][T][heads][head_dim]                     */
+    const void *k_cache;   /* [batch][max_ctx][kv_heads][head_dim] bf16       */
+    const void *v_cache;   /* same                                            */
+    float *o;              /* [batch][T][heads][head_dim]                     */
+    size_t batch, T, heads, kv_heads, head_dim, pos0, max_ctx;
+    float scale;
+} kai_gdn_attn_prefill_args;
+KAI_GDN_API int kai_run_gdn_attention_prefill_sm100a(const kai_gdn_attn_prefill_args *args, void *stream);
+
 /* End-to-end hybrid decode: the reference's decode loop
  * (src/orionsbelt/engines/cpu/kernels/gdn_e2e_decode.c:2775-2796) on the
  * GPU, one token through every layer for `batch` independent sequences:

@@ -41,6 +41,12 @@ class AttnDecodeArgs(C.Structure):
                 ("pos", _sz), ("max_ctx", _sz), ("scale", _f), ("cache_dtype", _i)]
 
 
+class AttnPrefillArgs(C.Structure):
+    """struct kai_gdn_attn_prefill_args."""
+    _fields_ = [("q", _vp), ("k_cache", _vp), ("v_cache", _vp), ("o", _vp), ("batch", _sz), ("T", _sz),
+                ("heads", _sz), ("kv_heads", _sz), ("head_dim", _sz), ("pos0", _sz), ("max_ctx", _sz), ("scale", _f)]
+
+
 class E2EConfig(C.Structure):
     """struct kai_gdn_e2e_config."""
     _fields_ = [("hidden", _sz), ("key_dim", _sz), ("value_dim", _sz), ("conv_dim", _sz), ("inter", _sz),
@@ -98,6 +104,7 @@ SIGNATURES = {
     "kai_run_gdn2_delta_rule_decode_sm100a": (_i, [C.POINTER(Gdn2DecodeArgs), _vp]),
     "kai_run_gdn_quantize_int8_sm100a": (_i, [_vp, _vp, _vp, _sz, _sz, _vp]),
     "kai_run_gdn_attention_decode_sm100a": (_i, [C.POINTER(AttnDecodeArgs), _vp]),
+    "kai_run_gdn_attention_prefill_sm100a": (_i, [C.POINTER(AttnPrefillArgs), _vp]),
     "kai_gdn_e2e_create": (_i, [C.POINTER(E2EConfig), C.POINTER(E2EWeights), C.POINTER(_vp)]),
     "kai_gdn_e2e_step": (_i, [_vp, _vp, _vp, _vp]),
     "kai_gdn_e2e_state": (_i, [_vp, _sz, _vp, _vp]),

@@ -55,6 +55,7 @@ int launch_matmul(const float *A, const float *B, float *C, size_t M, size_t K,
 int launch_decode(const kai_gdn_decode_args *a, cudaStream_t st);
 int launch_gdn2_decode(const kai_gdn2_decode_args *a, cudaStream_t st);
 int launch_attn_decode(const kai_gdn_attn_decode_args *a, cudaStream_t st);
+int launch_attn_prefill(const kai_gdn_attn_prefill_args *a, cudaStream_t st);
 int e2e_create(const kai_gdn_e2e_config *cfg, const kai_gdn_e2e_weights *w, void **out);
 int e2e_step(void *engine, const float *hidden_in, float *hidden_out, cudaStream_t st);
 int e2e_state(void *engine, size_t layer, float *gdn_state, float *conv_hist);

@@ -397,6 +397,10 @@ int kai_run_gdn_attention_decode_sm100a(const kai_gdn_attn_decode_args *args, vo
     return launch_attn_decode(args, (cudaStream_t)stream);
 }
 
+int kai_run_gdn_attention_prefill_sm100a(const kai_gdn_attn_prefill_args *args, void *stream) {
+    return launch_attn_prefill(args, (cudaStream_t)stream);
+}
+
 int kai_gdn_e2e_create(const kai_gdn_e2e_config *cfg, const kai_gdn_e2e_weights *weights, void **engine) {
     return e2e_create(cfg, weights, engine);
 }

@@ -10,7 +10,7 @@ Two layers, both calling the C ABI (include/kai_gdn_cuda.h) through ctypes:
 * The device layer takes CUDA tensors (torch is used only to own device memory
   and streams) and launches on the current torch stream: ``cumdecay``,
   ``cumsum``, ``gated_scan``, ``gdn2_gated_scan``, ``causal_dwconv1d``,
-  ``matmul``, ``quantize_int8``, ``matmul_int8``, ``pack_int8``, ``matmul_int8_packed``, ``attention_decode``, ``E2EEngine``, ``delta_rule_decode``,
+  ``matmul``, ``quantize_int8``, ``matmul_int8``, ``pack_int8``, ``matmul_int8_packed``, ``attention_prefill``, ``attention_decode``, ``E2EEngine``, ``delta_rule_decode``,
   ``gdn2_delta_rule_decode`` and ``chunk_delta_rule``.
 
 There is no CPU fallback anywhere: a missing library raises at import of the
@@ -228,6 +228,20 @@ def attention_decode(q, k_new, v_new, k_cache, v_cache, o, pos: int, scale: floa
     """GQA attention decode with KV-cache append (gdn_e2e_decode.c:1532-1634, int8 cache :1652-1830)."""
     args = attn_decode_args(q, k_new, v_new, k_cache, v_cache, o, pos, scale, k_scale, v_scale)
     check(lib().kai_run_gdn_attention_decode_sm100a(args, _stream(stream)))
+
+
+def attention_prefill(q, k_cache, v_cache, o, pos0: int, scale: float, stream=None) -> None:
+    """Causal GQA attention of a prompt over bf16 caches that already hold its
+    keys and values: q, o [B][T][H][D] fp32, caches [B][max_ctx][Hkv][D]; query
+    t attends to positions 0 .. pos0 + t."""
+    torch = _torch()
+    f = torch.float32
+    B, T, H, D = q.shape
+    Hkv, max_ctx = k_cache.shape[2], k_cache.shape[1]
+    args = _lib.AttnPrefillArgs(_dev(q, dtype=f), _dev(k_cache, dtype=torch.bfloat16),
+                                _dev(v_cache, dtype=torch.bfloat16), _dev(o, dtype=f), B, T, H, Hkv, D, int(pos0),
+                                max_ctx, float(scale))
+    check(lib().kai_run_gdn_attention_prefill_sm100a(args, _stream(stream)))
 
 
 class E2EEngine:
