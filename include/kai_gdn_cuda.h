@@ -374,6 +374,14 @@ KAI_GDN_API int kai_gdn_model_create(const kai_gdn_model_config *cfg, void **eng
  * place.  Stream-ordered; the first step on a stream runs eagerly, the
  * second captures the per-segment CUDA graphs, later ones replay them. */
 KAI_GDN_API int kai_gdn_model_step(void *engine, size_t pos, void *stream);
+/* Consume a prompt of T tokens per sequence (tokens [batch][T], int32, host
+ * or device memory) at positions pos0 .. pos0 + T - 1, as T decode steps
+ * would but in whole-prompt launches: projections over all T rows, the GDN
+ * layers' chunked delta-rule scan from their current state, the attention
+ * layers' keys and values written into the cache and the causal prompt
+ * attention.  Leaves the state for a decode step at position pos0 + T and
+ * the greedy next tokens as the current tokens.  Synchronises `stream`. */
+KAI_GDN_API int kai_gdn_model_prefill(void *engine, const int32_t *tokens, size_t T, size_t pos0, void *stream);
 /* Set (set = 1) or read (set = 0) the current tokens [batch] (int32, host or
  * device memory); synchronises the device. */
 KAI_GDN_API int kai_gdn_model_tokens(void *engine, int32_t *tokens, int set);

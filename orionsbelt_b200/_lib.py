@@ -117,6 +117,7 @@ SIGNATURES = {
     "kai_gdn_model_nccl_id": (_i, [_vp]),
     "kai_gdn_model_create": (_i, [C.POINTER(ModelConfig), C.POINTER(_vp)]),
     "kai_gdn_model_step": (_i, [_vp, _sz, _vp]),
+    "kai_gdn_model_prefill": (_i, [_vp, _vp, _sz, _sz, _vp]),
     "kai_gdn_model_tokens": (_i, [_vp, _vp, _i]),
     "kai_gdn_model_read": (_i, [_vp, _i, _vp]),
     "kai_gdn_model_weight": (_i, [_vp, _sz, _i, _vp, _vp, C.POINTER(_sz), C.POINTER(_sz)]),

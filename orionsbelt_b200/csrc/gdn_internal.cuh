@@ -63,6 +63,7 @@ int e2e_destroy(void *engine);
 int model_nccl_id(void *out);
 int model_create(const kai_gdn_model_config *cfg, void **out);
 int model_step(void *engine, size_t pos, cudaStream_t st);
+int model_prefill(void *engine, const int *tokens, size_t T, size_t pos0, cudaStream_t st);
 int model_tokens(void *engine, int *tokens, int set);
 int model_read(void *engine, int what, float *out);
 int model_weight(void *engine, size_t layer, int which, void *data, float *scales, size_t *rows, size_t *cols);

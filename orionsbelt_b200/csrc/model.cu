@@ -434,6 +434,13 @@ struct ModelEngine {
     int *tok = nullptr, *pos = nullptr;
     ArgMax *cand = nullptr, *cand_all = nullptr;
     std::vector<void *> allocs;
+    // prompt workspace (grown on demand by model_prefill): per-token rows
+    struct Prompt {
+        void *base = nullptr;
+        size_t T = 0;
+        float *h, *x, *part, *y, *q, *k, *v, *beta, *g, *o, *o2, *gate, *gu, *act;
+        int *tok;
+    } pf;
     const NcclApi *nccl = nullptr;
     ncclComm_t comm = nullptr;
     // graphs: segment s runs from attention layer s-1 (after its decode) to
@@ -538,6 +545,25 @@ int allreduce(ModelEngine *e, float *buf, size_t n, cudaStream_t st) {
     return check_nccl(e->nccl, e->nccl->allReduce(buf, buf, n, ncclFloat32, ncclSum, e->comm, st), "model: all-reduce");
 }
 
+// LM head over this rank's vocabulary and the greedy token of every
+// sequence from the final-normed rows x [B][H].
+int lm_head(ModelEngine *e, cudaStream_t st) {
+    const kai_gdn_model_config &c = e->cfg;
+    const size_t B = c.batch;
+    int rc = mm(e->x, e->lm, e->logits, B, st);
+    if (!rc)
+        rc = launch_pdl("argmax_kernel", argmax_kernel, dim3(dim3(AM_BLOCKS, (unsigned)B)), dim3(256), st, e->logits,
+                        (long long)e->V, (long long)e->v0, e->cand);
+    if (!rc && c.tp_size > 1)
+        rc = check_nccl(e->nccl, e->nccl->allGather(e->cand, e->cand_all, B * AM_BLOCKS * 2, ncclFloat32, e->comm, st),
+                        "model: all-gather");
+    if (!rc)
+        rc = launch_pdl("select_kernel", select_kernel, dim3((unsigned)((B + 127) / 128)), dim3(128), st,
+                        c.tp_size > 1 ? e->cand_all : e->cand, c.tp_size > 1 ? c.tp_size : 1, (int)B, AM_BLOCKS,
+                        e->tok);
+    return rc;
+}
+
 // Segment s of a token (see ModelEngine::seg).
 int run_segment(ModelEngine *e, size_t s, cudaStream_t st) {
     const kai_gdn_model_config &c = e->cfg;
@@ -616,16 +642,7 @@ int run_segment(ModelEngine *e, size_t s, cudaStream_t st) {
     }
     // end of the token: final norm, LM head over this rank's vocabulary, argmax
     M_TRY(launch_pdl("add_rmsnorm_kernel", add_rmsnorm_kernel, dim3((unsigned)B), dim3(1024), st, e->h, pending, e->w_final, e->x, (long long)H, c.rms_eps));
-    M_TRY(mm(e->x, e->lm, e->logits, B, st));
-    M_TRY(launch_pdl("argmax_kernel", argmax_kernel, dim3(dim3(AM_BLOCKS, (unsigned)B)), dim3(256), st, e->logits, (long long)e->V, (long long)e->v0,
-                                                                e->cand));
-    if (c.tp_size > 1)
-        M_TRY(check_nccl(e->nccl,
-                         e->nccl->allGather(e->cand, e->cand_all, B * AM_BLOCKS * 2, ncclFloat32, e->comm, st),
-                         "model: all-gather"));
-    M_TRY(launch_pdl("select_kernel", select_kernel, dim3((unsigned)((B + 127) / 128)), dim3(128), st, c.tp_size > 1 ? e->cand_all : e->cand,
-                                                              c.tp_size > 1 ? c.tp_size : 1, (int)B, AM_BLOCKS,
-                                                              e->tok));
+    M_TRY(lm_head(e, st));
 #undef M_TRY
     return KAI_GDN_OK;
 }
@@ -663,6 +680,260 @@ int run_token(ModelEngine *e, size_t pos, cudaStream_t st, bool use_graphs) {
         if (rc) return rc;
         if (s < e->attn_layers.size() && (rc = run_attention(e, e->attn_layers[s], pos, st))) return rc;
     }
+    return KAI_GDN_OK;
+}
+
+
+// ---------------------------------------------------------------- prompt
+// The prompt of one sequence runs as whole-prompt launches, layer by layer:
+// projections with M = T rows, the GDN layers' conv and gates per token and
+// the chunked delta-rule scan from the sequence's state, the attention
+// layers' keys and values written into the cache and the causal prompt
+// attention.  The state a decode step needs afterwards -- conv histories,
+// GDN states, KV caches, the last token's hidden state -- is what T decode
+// steps would leave.
+
+// GDN input side for every prompt token, one CTA (d threads) per (head,
+// token): the Conv1D over the three inputs before the token (the history for
+// the first three) in the decode step's order of operations, SiLU, L2
+// normalisation of q and k, beta and g of the value heads.
+//   y [T][ny] rows as gdn_prep_kernel's; hist [3][C] (read only here)
+//   q, k [T][hk][d], v [T][hv][d], beta, g [T][hv]
+__global__ void gdn_prompt_prep_kernel(const float *__restrict__ y, long long ny, const float *__restrict__ hist,
+                                       const float *__restrict__ w, const float *__restrict__ A_log,
+                                       const float *__restrict__ dt_bias, float *__restrict__ q, float *__restrict__ k,
+                                       float *__restrict__ v, float *__restrict__ beta, float *__restrict__ g, int hk,
+                                       int hv, int d) {
+    pdl_enter();
+    __shared__ float red[32];
+    const long long t = blockIdx.y;
+    const int head = blockIdx.x, i = threadIdx.x;
+    const long long C = (long long)(2 * hk + hv) * d;
+    const long long ch = (long long)head * d + i;
+    auto in = [&](long long u) { return u >= 0 ? y[u * ny + ch] : hist[(3 + u) * C + ch]; };
+    const float x = y[t * ny + ch], h0 = in(t - 3), h1 = in(t - 2), h2 = in(t - 1);
+    float c = __fmul_rn(w[ch], h0);
+    c = __fadd_rn(c, __fmul_rn(w[C + ch], h1));
+    c = __fadd_rn(c, __fmul_rn(w[2 * C + ch], h2));
+    c = __fadd_rn(c, __fmul_rn(w[3 * C + ch], x));
+    const float s = silu(c);
+    if (head < 2 * hk) {
+        const float inv = rsqrtf(block_sum(s * s, red) + 1e-6f);
+        if (head < hk)
+            q[(t * hk + head) * d + i] = s * inv;
+        else
+            k[(t * hk + head - hk) * d + i] = s * inv;
+    } else {
+        const int vh = head - 2 * hk;
+        v[(t * hv + vh) * d + i] = s;
+        if (i == 0) {
+            const long long zoff = C + (long long)hv * d;
+            const float bb = y[t * ny + zoff + vh], aa = y[t * ny + zoff + hv + vh];
+            const float xa = aa + dt_bias[vh];
+            const float sp = xa > 20.f ? xa : log1pf(expf(xa));
+            beta[t * hv + vh] = sigm(bb);
+            g[t * hv + vh] = -expf(A_log[vh]) * sp;
+        }
+    }
+}
+// The conv history after the prompt: its last three inputs (older history
+// where the prompt is shorter than three).
+__global__ void gdn_prompt_hist_kernel(const float *__restrict__ y, long long ny, float *__restrict__ hist,
+                                       long long C, long long T) {
+    pdl_enter();
+    for (long long ch = blockIdx.x * (long long)blockDim.x + threadIdx.x; ch < C; ch += (long long)gridDim.x * blockDim.x) {
+        float nh[3];
+#pragma unroll
+        for (int j = 0; j < 3; ++j) {
+            const long long u = T - 3 + j;
+            nh[j] = u >= 0 ? y[u * ny + ch] : hist[(3 + u) * C + ch];
+        }
+#pragma unroll
+        for (int j = 0; j < 3; ++j) hist[j * C + ch] = nh[j];
+    }
+}
+// Attention input side for every prompt token (attn_prep_kernel's
+// arithmetic at position pos0 + t): query and gate rows to q / gate
+// [T][hq][D], RMSNormed and rotated keys and the values straight into the
+// bf16 caches at their positions.  One CTA of D threads per (head row, token).
+__global__ void attn_prompt_prep_kernel(const float *__restrict__ y, long long ny, const float *__restrict__ wq,
+                                        const float *__restrict__ wk, long long pos0, float *__restrict__ q,
+                                        float *__restrict__ gate, __nv_bfloat16 *__restrict__ kc,
+                                        __nv_bfloat16 *__restrict__ vc, int hq, int hkv, int D, int R, float theta,
+                                        float eps) {
+    pdl_enter();
+    __shared__ float red[32];
+    __shared__ float row[512];
+    const long long t = blockIdx.y;
+    const int r = blockIdx.x, i = threadIdx.x;
+    const long long pos = pos0 + t;
+    const float *yr = y + t * ny;
+    if (r >= hq + hkv) {  // v
+        const int kv = r - hq - hkv;
+        vc[(pos * hkv + kv) * D + i] = __float2bfloat16_rn(yr[(long long)hq * 2 * D + (long long)(hkv + kv) * D + i]);
+        return;
+    }
+    const bool isq = r < hq;
+    const float x = isq ? yr[(long long)r * 2 * D + i] : yr[(long long)hq * 2 * D + (long long)(r - hq) * D + i];
+    if (isq) gate[(t * hq + r) * D + i] = yr[(long long)r * 2 * D + D + i];
+    const float inv = rsqrtf(block_sum(x * x, red) / (float)D + eps);
+    const float nx = x * inv * (isq ? wq[i] : wk[i]);
+    row[i] = nx;
+    __syncthreads();
+    float outv = nx;
+    if (i < R) {
+        const int half = R / 2, j = i < half ? i : i - half;
+        const float inv_freq = powf(theta, -2.0f * (float)j / (float)R);
+        float sn, cs;
+        sincosf((float)pos * inv_freq, &sn, &cs);
+        outv = i < half ? nx * cs - row[i + half] * sn : row[i - half] * sn + nx * cs;
+    }
+    if (isq)
+        q[(t * hq + r) * D + i] = outv;
+    else
+        kc[(pos * hkv + (r - hq)) * D + i] = __float2bfloat16_rn(outv);
+}
+
+// Row-major int8 projection of M prompt rows (the tensor-core GEMM).
+int mm_rows(const float *A, const QW &w, float *Cm, size_t M, cudaStream_t st) {
+    return launch_matmul_int8(A, w.q, w.s, Cm, M, w.K, w.N, st);
+}
+
+int prompt_workspace(ModelEngine *e, size_t T) {
+    ModelEngine::Prompt &P = e->pf;
+    if (P.T >= T) return KAI_GDN_OK;
+    if (P.base) {
+        cudaFree(P.base);  // waits for the device
+        P.base = nullptr;
+        P.T = 0;
+    }
+    const size_t H = e->cfg.hidden, d = e->d;
+    const size_t widths[] = {H,
+                             H,
+                             H,
+                             std::max(e->ny_gdn, e->ny_att),
+                             std::max(e->hk * d, e->hq * e->D),
+                             std::max(e->hk * d, (size_t)1),
+                             std::max(e->hv * d, (size_t)1),
+                             e->hv,
+                             e->hv,
+                             std::max(e->hv * d, e->hq * e->D),
+                             std::max(e->hv * d, e->hq * e->D),
+                             e->hq * e->D,
+                             2 * e->I,
+                             e->I};
+    float **ptrs[] = {&P.h, &P.x, &P.part, &P.y, &P.q, &P.k, &P.v, &P.beta, &P.g, &P.o, &P.o2, &P.gate, &P.gu, &P.act};
+    size_t total = 0;
+    for (size_t wdt : widths) total += (T * wdt * sizeof(float) + 255) / 256 * 256;
+    total += (T * sizeof(int) + 255) / 256 * 256;
+    int rc = check_cuda(cudaMalloc(&P.base, total), "model_prefill: workspace");
+    if (rc) return rc;
+    unsigned char *cur = static_cast<unsigned char *>(P.base);
+    for (size_t i = 0; i < sizeof(widths) / sizeof(widths[0]); ++i) {
+        *ptrs[i] = reinterpret_cast<float *>(cur);
+        cur += (T * widths[i] * sizeof(float) + 255) / 256 * 256;
+    }
+    P.tok = reinterpret_cast<int *>(cur);
+    P.T = T;
+    return KAI_GDN_OK;
+}
+
+// The prompt of sequence b (tokens already in pf.tok) from position pos0:
+// leaves the last token's hidden state in h[b] and its final RMSNorm in x[b].
+int run_prompt(ModelEngine *e, size_t b, size_t T, size_t pos0, cudaStream_t st) {
+    const kai_gdn_model_config &c = e->cfg;
+    const size_t H = c.hidden, d = e->d;
+    ModelEngine::Prompt &P = e->pf;
+    int rc = 0;
+#define M_TRY(x)                   \
+    do {                           \
+        if ((rc = (x))) return rc; \
+    } while (0)
+    M_TRY(launch_pdl("embed_kernel", embed_kernel, dim3((unsigned)T), dim3(1024), st, P.tok, e->emb_q, e->emb_s, P.h,
+                     (long long)H, (long long)c.vocab));
+    const float *pending = nullptr;
+    for (size_t l = 0; l < c.layers; ++l) {
+        ModelEngine::Layer &L = e->layers[l];
+        M_TRY(launch_pdl("add_rmsnorm_kernel", add_rmsnorm_kernel, dim3((unsigned)T), dim3(1024), st, P.h, pending,
+                         L.w_in, P.x, (long long)H, c.rms_eps));
+        if (e->is_gdn[l]) {
+            float *hist = L.hist + b * 3 * e->C;
+            M_TRY(mm_rows(P.x, L.win, P.y, T, st));
+            M_TRY(launch_pdl("gdn_prompt_prep_kernel", gdn_prompt_prep_kernel,
+                             dim3((unsigned)(2 * e->hk + e->hv), (unsigned)T), dim3((unsigned)d), st, P.y,
+                             (long long)e->ny_gdn, hist, L.conv_w, L.A_log, L.dt_bias, P.q, P.k, P.v, P.beta, P.g,
+                             (int)e->hk, (int)e->hv, (int)d));
+            M_TRY(launch_pdl("gdn_prompt_hist_kernel", gdn_prompt_hist_kernel, dim3(grid_for((long long)e->C)),
+                             dim3(256), st, P.y, (long long)e->ny_gdn, hist, (long long)e->C, (long long)T));
+            kai_gdn_chunk_args ca{};
+            ca.q = P.q;
+            ca.k = P.k;
+            ca.v = P.v;
+            ca.g = P.g;
+            ca.beta = P.beta;
+            ca.state = L.state + b * e->hv * d * d;
+            ca.o = P.o;
+            ca.batch = 1;
+            ca.seq = T;
+            ca.heads_k = e->hk;
+            ca.heads_v = e->hv;
+            ca.dk = d;
+            ca.dv = d;
+            ca.chunk = 64;
+            ca.scale = 1.0f / sqrtf((float)d);
+            ca.in_dtype = KAI_GDN_F32;
+            ca.state_dtype = KAI_GDN_F32;
+            ca.out_dtype = KAI_GDN_F32;
+            M_TRY(launch_chunk(&ca, st));
+            M_TRY(launch_pdl("gated_rmsnorm_kernel", gated_rmsnorm_kernel, dim3((unsigned)e->hv, (unsigned)T),
+                             dim3((unsigned)d), st, P.o, P.y, (long long)e->ny_gdn, (long long)e->C, L.w_gn, P.o2,
+                             (int)e->hv, (int)d, c.rms_eps));
+        } else {
+            const size_t kvrow = e->hkv * e->D;
+            __nv_bfloat16 *kc = static_cast<__nv_bfloat16 *>(L.kc) + b * c.max_ctx * kvrow;
+            __nv_bfloat16 *vc = static_cast<__nv_bfloat16 *>(L.vc) + b * c.max_ctx * kvrow;
+            M_TRY(mm_rows(P.x, L.win, P.y, T, st));
+            M_TRY(launch_pdl("attn_prompt_prep_kernel", attn_prompt_prep_kernel,
+                             dim3((unsigned)(e->hq + 2 * e->hkv), (unsigned)T), dim3((unsigned)e->D), st, P.y,
+                             (long long)e->ny_att, L.w_qn, L.w_kn, (long long)pos0, P.q, P.gate, kc, vc, (int)e->hq,
+                             (int)e->hkv, (int)e->D, (int)c.rope_dims, c.rope_theta, c.rms_eps));
+            kai_gdn_attn_prefill_args aa{};
+            aa.q = P.q;
+            aa.k_cache = kc;
+            aa.v_cache = vc;
+            aa.o = P.o;
+            aa.batch = 1;
+            aa.T = T;
+            aa.heads = e->hq;
+            aa.kv_heads = e->hkv;
+            aa.head_dim = e->D;
+            aa.pos0 = pos0;
+            aa.max_ctx = c.max_ctx;
+            aa.scale = 1.0f / sqrtf((float)e->D);
+            M_TRY(launch_attn_prefill(&aa, st));
+            M_TRY(launch_pdl("attn_gate_kernel", attn_gate_kernel, dim3(grid_for((long long)(T * e->hq * e->D))),
+                             dim3(256), st, P.o, P.gate, P.o2, (long long)(T * e->hq * e->D)));
+        }
+        M_TRY(mm_rows(P.o2, L.wout, P.part, T, st));
+        M_TRY(allreduce(e, P.part, T * H, st));
+        M_TRY(launch_pdl("add_rmsnorm_kernel", add_rmsnorm_kernel, dim3((unsigned)T), dim3(1024), st, P.h, P.part,
+                         L.w_post, P.x, (long long)H, c.rms_eps));
+        M_TRY(mm_rows(P.x, L.wgu, P.gu, T, st));
+        M_TRY(launch_pdl("swiglu_kernel", swiglu_kernel, dim3(grid_for((long long)(T * e->I))), dim3(256), st, P.gu,
+                         P.act, (long long)e->I, (long long)(T * e->I)));
+        M_TRY(mm_rows(P.act, L.wdown, P.part, T, st));
+        M_TRY(allreduce(e, P.part, T * H, st));
+        pending = P.part;
+    }
+    // the last token: residual, final norm into the decode buffers
+    const size_t lr = (T - 1) * H;
+    M_TRY(launch_pdl("add_rmsnorm_kernel", add_rmsnorm_kernel, dim3(1), dim3(1024), st, P.h + lr, pending + lr,
+                     e->w_final, P.x + lr, (long long)H, c.rms_eps));
+    M_TRY(check_cuda(cudaMemcpyAsync(e->h + b * H, P.h + lr, H * sizeof(float), cudaMemcpyDeviceToDevice, st),
+                     "model_prefill: copy"));
+    M_TRY(check_cuda(cudaMemcpyAsync(e->x + b * H, P.x + lr, H * sizeof(float), cudaMemcpyDeviceToDevice, st),
+                     "model_prefill: copy"));
+#undef M_TRY
     return KAI_GDN_OK;
 }
 
@@ -885,6 +1156,24 @@ int model_create(const kai_gdn_model_config *cfg, void **out) {
     return KAI_GDN_OK;
 }
 
+int model_prefill(void *engine, const int *tokens, size_t T, size_t pos0, cudaStream_t st) {
+    ModelEngine *e = static_cast<ModelEngine *>(engine);
+    if (!e || !tokens) return set_error(KAI_GDN_ERR_INVALID, "model_prefill: null argument");
+    if (T == 0) return KAI_GDN_OK;
+    if (pos0 + T > e->cfg.max_ctx)
+        return set_error(KAI_GDN_ERR_INVALID, "model_prefill: positions %zu .. %zu outside the cache (%zu)", pos0,
+                         pos0 + T - 1, e->cfg.max_ctx);
+    int rc = prompt_workspace(e, T);
+    for (size_t b = 0; b < e->cfg.batch && !rc; ++b) {
+        rc = check_cuda(cudaMemcpyAsync(e->pf.tok, tokens + b * T, T * sizeof(int), cudaMemcpyDefault, st),
+                        "model_prefill: tokens");
+        if (!rc) rc = run_prompt(e, b, T, pos0, st);
+    }
+    if (!rc) rc = lm_head(e, st);
+    if (!rc) rc = check_cuda(cudaStreamSynchronize(st), "model_prefill: sync");
+    return rc;
+}
+
 int model_step(void *engine, size_t pos, cudaStream_t st) {
     ModelEngine *e = static_cast<ModelEngine *>(engine);
     if (!e) return set_error(KAI_GDN_ERR_INVALID, "model_step: null engine");
@@ -1058,6 +1347,7 @@ int model_destroy(void *engine) {
     for (cudaGraphExec_t x : e->seg)
         if (x) cudaGraphExecDestroy(x);
     if (e->comm && e->nccl) e->nccl->commDestroy(e->comm);
+    if (e->pf.base) cudaFree(e->pf.base);
     for (void *p : e->allocs) cudaFree(p);
     delete e;
     return KAI_GDN_OK;

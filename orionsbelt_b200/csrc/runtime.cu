@@ -420,6 +420,10 @@ int kai_gdn_model_create(const kai_gdn_model_config *cfg, void **engine) { retur
 int kai_gdn_model_step(void *engine, size_t pos, void *stream) {
     return model_step(engine, pos, (cudaStream_t)stream);
 }
+
+int kai_gdn_model_prefill(void *engine, const int32_t *tokens, size_t T, size_t pos0, void *stream) {
+    return model_prefill(engine, tokens, T, pos0, (cudaStream_t)stream);
+}
 int kai_gdn_model_tokens(void *engine, int32_t *tokens, int set) { return model_tokens(engine, tokens, set); }
 int kai_gdn_model_read(void *engine, int what, float *out) { return model_read(engine, what, out); }
 int kai_gdn_model_weight(void *engine, size_t layer, int which, void *data, float *scales, size_t *rows,

@@ -338,6 +338,14 @@ class ModelEngine:
     def step(self, pos: int, stream=None) -> None:
         check(lib().kai_gdn_model_step(self._h, int(pos), _stream(stream)))
 
+    def prefill(self, tokens, pos0: int = 0, stream=None) -> None:
+        """Consume prompts tokens [batch][T] at positions pos0 .. pos0 + T - 1;
+        the greedy next tokens become the current tokens."""
+        t = np.ascontiguousarray(tokens, dtype=np.int32)
+        if t.ndim != 2 or t.shape[0] != self.batch:
+            raise ValueError(f"prefill: tokens must be [batch={self.batch}][T], got {t.shape}")
+        check(lib().kai_gdn_model_prefill(self._h, t.ctypes.data, t.shape[1], int(pos0), _stream(stream)))
+
     def read(self, what: int, shape) -> np.ndarray:
         out = np.empty(shape, np.float32)
         check(lib().kai_gdn_model_read(self._h, what, out.ctypes.data))

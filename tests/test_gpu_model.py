@@ -64,6 +64,51 @@ def test_model_matches_oracle(cuda, orc, B):
     eng.close()
 
 
+@pytest.mark.parametrize("B,split", [(2, None), (6, 40)])
+def test_model_prefill_matches_oracle(cuda, orc, B, split):
+    """A 70-token prompt (two 64-token chunks of the GDN scan, a partial last
+    one) through kai_gdn_model_prefill -- in one call, or as 40 tokens and a
+    continuation of 30 from position 40 -- equals the oracle stepping through
+    the prompt token by token; then three decode steps from position 70."""
+    from oracle.model import ModelOracle, read_weights
+
+    torch = cuda
+    geom = dict(GEOM, max_ctx=96)
+    T, steps = 70, 3
+    eng = ops.ModelEngine(geom, B, seed=13)
+    W = read_weights(eng, geom)
+    mo = ModelOracle(orc, geom, B, W)
+    H, V = geom["hidden"], geom["vocab"]
+    prompt = np.random.default_rng(B).integers(0, V, (B, T)).astype(np.int32)
+    stream = torch.cuda.Stream()
+    with torch.cuda.stream(stream):
+        if split is None:
+            eng.prefill(prompt, 0, stream)
+        else:
+            eng.prefill(prompt[:, :split], 0, stream)
+            eng.prefill(prompt[:, split:], split, stream)
+    for t in range(T):
+        h, logits, want_tok = mo.step(prompt[:, t], t)
+    got_h, got_l = eng.read(0, (B, H)), eng.read(1, (B, V))
+    assert rel_l2(got_h, h) < 1e-3, rel_l2(got_h, h)
+    assert rel_l2(got_l, logits) < 1e-3, rel_l2(got_l, logits)
+    top2 = np.sort(logits, -1)[:, -2:]
+    clear = (top2[:, 1] - top2[:, 0]) > 1e-4 * np.abs(logits).max()
+    assert np.array_equal(eng.tokens()[clear], want_tok[clear])
+    tok = want_tok
+    with torch.cuda.stream(stream):
+        for pos in range(T, T + steps):
+            eng.set_tokens(tok)
+            eng.step(pos, stream)
+            stream.synchronize()
+            h, logits, want_tok = mo.step(tok, pos)
+            got_h, got_l = eng.read(0, (B, H)), eng.read(1, (B, V))
+            assert rel_l2(got_h, h) < 1e-3, (pos, rel_l2(got_h, h))
+            assert rel_l2(got_l, logits) < 1e-3, (pos, rel_l2(got_l, logits))
+            tok = want_tok
+    eng.close()
+
+
 def _tp_rank(rank, nid, tokens, q):
     try:
         import torch
