@@ -239,8 +239,9 @@ KAI_GDN_API int kai_run_gdn_matmul_int8_sm100a(const float *A, const int8_t *q, 
  * the packed form of q [K][N] (0 when N % 16 is non-zero or K > 131072);
  * kai_run_gdn_int8_pack_sm100a writes it (qp 16-byte aligned, device
  * memory, not aliasing q); kai_run_gdn_matmul_int8_packed_sm100a computes C
- * from it on the int8 tensor cores, 16 activation rows per pass over the
- * weights.  Each activation row is carried as three 8-bit fixed-point terms
+ * from it on the int8 tensor cores: up to 16 activation rows as one stream
+ * over the weights, more rows (a prompt) as a GEMM of 64-row x 128-column
+ * tiles.  Each activation row is carried as three 8-bit fixed-point terms
  * of its largest magnitude (representation error at most 2^-24 of it, one
  * fp32 rounding) and the products are summed exactly in integers, so the
  * result is deterministic whatever the work split, and agrees with
@@ -412,6 +413,9 @@ KAI_GDN_API int kai_gdn_model_weight(void *engine, size_t layer, int which, void
 /* Synthetic state of `ctx` already-consumed tokens: KV cache rows [0, ctx)
  * N(0, 1) in bf16, GDN states N(0, 0.02), conv histories N(0, 1). */
 KAI_GDN_API int kai_gdn_model_fill(void *engine, size_t ctx, unsigned long long seed);
+/* Every sequence back to position 0 (a new prompt follows): GDN states and
+ * conv histories zero.  Synchronises the device. */
+KAI_GDN_API int kai_gdn_model_reset(void *engine);
 KAI_GDN_API int kai_gdn_model_destroy(void *engine);
 
 /* Chunkwise (WY / UT-transform) gated delta-rule scan over a whole sequence,

@@ -122,6 +122,7 @@ SIGNATURES = {
     "kai_gdn_model_read": (_i, [_vp, _i, _vp]),
     "kai_gdn_model_weight": (_i, [_vp, _sz, _i, _vp, _vp, C.POINTER(_sz), C.POINTER(_sz)]),
     "kai_gdn_model_fill": (_i, [_vp, _sz, C.c_ulonglong]),
+    "kai_gdn_model_reset": (_i, [_vp]),
     "kai_gdn_model_destroy": (_i, [_vp]),
     # control
     "kai_gdn_cuda_set_device": (_i, [_i]),

@@ -68,6 +68,7 @@ int model_tokens(void *engine, int *tokens, int set);
 int model_read(void *engine, int what, float *out);
 int model_weight(void *engine, size_t layer, int which, void *data, float *scales, size_t *rows, size_t *cols);
 int model_fill(void *engine, size_t ctx, unsigned long long seed);
+int model_reset(void *engine);
 int model_destroy(void *engine);
 int launch_quantize_int8(const float *B, int8_t *q, float *s, size_t K, size_t N, cudaStream_t st);
 int launch_matmul_int8(const float *A, const int8_t *q, const float *s, float *C, size_t M, size_t K, size_t N,

@@ -119,9 +119,11 @@ struct Split {
 };
 
 // One CTA per activation row: S_m and the three terms of every k (zeros for
-// k >= K up to the last stage).  terms [M/16 blocks][S][4][48][16].
+// k >= K up to the last stage).  terms [M/RB blocks][S][4][3 RB][16]: per
+// stage and k-group, the RB rows of t0, then of t1, then of t2 (RB = 16 for
+// the stream kernel, 64 for the row-tiled GEMM).
 __global__ void __launch_bounds__(256) act_terms_kernel(const float *__restrict__ A, int8_t *__restrict__ terms,
-                                                        float *__restrict__ scale, long long K, long long S) {
+                                                        float *__restrict__ scale, long long K, long long S, int RB) {
     pdl_trigger();  // the matmul may start streaming its weights meanwhile
     const int m = blockIdx.x, t = threadIdx.x;
     const float *a = A + (long long)m * K;
@@ -137,18 +139,19 @@ __global__ void __launch_bounds__(256) act_terms_kernel(const float *__restrict_
     for (int i = 1; i < 8; ++i) mx = fmaxf(mx, red[i]);
     if (t == 0) scale[m] = mx;
     const float inv = mx > 0.f ? 127.0f / mx : 0.f;
-    int8_t *blk = terms + (long long)(m / PMT) * S * T_BYTES;
-    const int r = m % PMT;
+    const long long sb = 3ll * RB * PK;  // bytes of one stage of a row block
+    int8_t *blk = terms + (long long)(m / RB) * S * sb;
+    const int r = m % RB;
     for (long long k = t; k < S * PK; k += 256) {
         float x = k < K ? a[k] * inv : 0.f;
         const float t0 = rintf(x);
         x = (x - t0) * 254.0f;
         const float t1 = rintf(x);
         const float t2 = rintf((x - t1) * 254.0f);
-        int8_t *p = blk + (k / PK) * T_BYTES + ((k % PK) / 16) * (PNM * 16) + (k % 16);
+        int8_t *p = blk + (k / PK) * sb + ((k % PK) / 16) * (3 * RB * 16) + (k % 16);
         p[r * 16] = (int8_t)(int)t0;
-        p[(PMT + r) * 16] = (int8_t)(int)t1;
-        p[(2 * PMT + r) * 16] = (int8_t)(int)t2;
+        p[(RB + r) * 16] = (int8_t)(int)t1;
+        p[(2 * RB + r) * 16] = (int8_t)(int)t2;
     }
 }
 
@@ -358,6 +361,143 @@ __global__ void __launch_bounds__(PNT, 1)
     }
 }
 
+// Row-tiled GEMM for many activation rows (a prompt): CTA = (64 rows, 128
+// weight columns = half of a packed tile), the whole K, no split.  D^T
+// [128 columns][64 rows] per term in TMEM (three int32 accumulators, 192
+// columns); per 64-k stage two bulk-copy groups (the weight half's four
+// 2 KB k-groups, the 12 KB of activation terms) and six MMAs (3 terms x 2 K
+// steps of 32).  Two CTAs per SM, so one CTA's epilogue overlaps the other's
+// main loop.  Warp 0 loads, warp 1 issues, warps 2-5 write C (lane = weight
+// column, so stores are coalesced).
+constexpr int GR = 64, GC = 128;
+constexpr int GW_BYTES = PK * GC, GT_BYTES = 3 * GR * PK, GSTAGE = GW_BYTES + GT_BYTES;
+constexpr int GNSTG = 5;
+constexpr int GNT = 6 * 32;
+constexpr size_t GSMEM = 1024 + (size_t)GNSTG * GSTAGE;
+
+__global__ void __launch_bounds__(GNT, 2)
+    int8_gemm_kernel(const int8_t *__restrict__ qp, const int8_t *__restrict__ terms, const float *__restrict__ scale,
+                     const float *__restrict__ s, float *__restrict__ C, long long M, long long N, long long S,
+                     long long ncol_tiles, int *err) {
+    extern __shared__ unsigned char dsm_raw[];
+    unsigned char *ring = dsm_raw + ((1024u - (smem_addr(dsm_raw) & 1023u)) & 1023u);  // [GNSTG][GSTAGE]
+    __shared__ uint64_t full[GNSTG], empty[GNSTG], accf;
+    __shared__ uint32_t tmem_slot;
+    __shared__ volatile int s_bad;
+    const int t = threadIdx.x, warp = t / 32, lane = t % 32;
+    const long long ct = (long long)blockIdx.x % ncol_tiles, rt = (long long)blockIdx.x / ncol_tiles;
+    const long long ptile = ct / 2, half = ct % 2, n0 = ct * GC, m0 = rt * GR;
+    const int pre = (int)min((long long)GNSTG, S);
+    auto load_w = [&](int st, int slot) {
+        unsigned char *dst = ring + slot * GSTAGE;
+#pragma unroll
+        for (int kg = 0; kg < 4; ++kg)
+            bulk_load(dst + kg * 2048, qp + ((ptile * S + st) * 4 + kg) * 4096 + half * 2048, 2048, &full[slot]);
+    };
+    if (t == 0) {
+        for (int i = 0; i < GNSTG; ++i) {
+            mbar_init(&full[i], 1);
+            mbar_init(&empty[i], 1);
+        }
+        mbar_init(&accf, 1);
+        s_bad = 0;
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+        for (int i = 0; i < pre; ++i) {  // weights never depend on earlier kernels
+            mbar_arrive_expect_tx(&full[i], GSTAGE);
+            load_w(i, i);
+        }
+    }
+    if (warp == W_MMA) tmem_alloc(&tmem_slot, 256);
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    fence_before_sync();
+    __syncthreads();
+    fence_after_sync();
+    const uint32_t tmem = tmem_slot;
+    pdl_trigger();
+    if (warp == W_PROD) {
+        if (lane == 0) {
+            pdl_wait();
+            for (int i = 0; i < pre; ++i)
+                bulk_load(ring + i * GSTAGE + GW_BYTES, terms + (rt * S + i) * GT_BYTES, GT_BYTES, &full[i]);
+            int issued = pre;
+            for (; issued < S; ++issued) {
+                const int slot = issued % GNSTG;
+                if (s_bad || !mbar_wait(&empty[slot], (uint32_t)(((issued / GNSTG) - 1) & 1), err)) {
+                    s_bad = 1;
+                    break;
+                }
+                mbar_arrive_expect_tx(&full[slot], GSTAGE);
+                load_w(issued, slot);
+                bulk_load(ring + slot * GSTAGE + GW_BYTES, terms + (rt * S + issued) * GT_BYTES, GT_BYTES,
+                          &full[slot]);
+            }
+            for (int i = max(0, issued - GNSTG); i < issued; ++i)
+                mbar_wait(&full[i % GNSTG], (uint32_t)((i / GNSTG) & 1), err);
+        }
+        __syncwarp();
+    } else if (warp == W_MMA) {
+        constexpr uint32_t id = idesc_s8(128, GR);
+        int done = 0;
+        for (int st = 0; st < S; ++st) {
+            const int slot = st % GNSTG;
+            if (s_bad || !mbar_wait(&full[slot], (uint32_t)((st / GNSTG) & 1), err)) {
+                s_bad = 1;
+                break;
+            }
+            fence_after_sync();
+            if (elect_one()) {
+                const uint32_t a = smem_addr(ring + slot * GSTAGE), b = a + GW_BYTES;
+#pragma unroll
+                for (int tm = 0; tm < 3; ++tm)
+#pragma unroll
+                    for (int ks = 0; ks < PK / 32; ++ks)
+                        mma_i8(tmem + tm * GR, smem_desc(a + ks * 2 * 2048, 2048, 128),
+                               smem_desc(b + tm * GR * 16 + ks * 2 * (3 * GR * 16), 3 * GR * 16, 128), id,
+                               st > 0 || ks > 0);
+                commit(&empty[slot]);
+                if (st + 1 == S) commit(&accf);
+            }
+            __syncwarp();
+            done = st + 1;
+        }
+        if (s_bad && done > 0) mbar_wait(&empty[(done - 1) % GNSTG], (uint32_t)(((done - 1) / GNSTG) & 1), err);
+    } else {
+        const int q4 = warp & 3;
+        const long long n = n0 + 32 * q4 + lane;
+        pdl_wait();
+        bool ok = !s_bad && mbar_wait(&accf, 0, err);
+        if (!ok) s_bad = 1;
+        fence_after_sync();
+        ok = __all_sync(0xffffffffu, ok);
+        if (ok) {
+            const float sc = n < N ? s[n] : 0.f;
+#pragma unroll
+            for (int rc = 0; rc < GR; rc += 16) {
+                int d0[16], d1[16], d2[16];
+                tmem_ld16i(taddr(tmem, 32 * q4, rc), d0);
+                tmem_ld16i(taddr(tmem, 32 * q4, GR + rc), d1);
+                tmem_ld16i(taddr(tmem, 32 * q4, 2 * GR + rc), d2);
+                tmem_wait_ld();
+                reg_fence16i(d0);
+                reg_fence16i(d1);
+                reg_fence16i(d2);
+#pragma unroll
+                for (int i = 0; i < 16; ++i) {
+                    const long long r = m0 + rc + i;
+                    if (r < M && n < N)
+                        C[r * N + n] = (float)term_sum(d0[i], d1[i], d2[i]) * (scale[r] * TERM_INV * sc);
+                }
+            }
+        }
+    }
+    fence_before_sync();
+    __syncthreads();
+    if (warp == W_MMA) {
+        fence_after_sync();
+        tmem_dealloc(tmem, 256);
+    }
+}
+
 __global__ void pack_kernel(const int8_t *__restrict__ q, int8_t *__restrict__ qp, long long K, long long N,
                             long long S, long long chunks) {
     for (long long e = blockIdx.x * (long long)blockDim.x + threadIdx.x; e < chunks;
@@ -437,6 +577,36 @@ int packed_workspace(cudaStream_t st, size_t nterms, size_t nscale, size_t ntile
     return KAI_GDN_OK;
 }
 
+// Many rows: activation terms in blocks of 64 rows, then the row-tiled GEMM
+// (a programmatic dependent of the terms kernel).
+int run_gemm(const float *A, const int8_t *qp, const float *s, float *C, size_t M, size_t K, size_t N,
+             cudaStream_t st) {
+    const long long S = (long long)((K + PK - 1) / PK), ncol = (long long)((N + GC - 1) / GC);
+    const long long rows = (long long)((M + GR - 1) / GR), grid = ncol * rows;
+    if (grid > 0x7fffffffll || M > 0x7fffffffull) return set_error(KAI_GDN_ERR_UNSUPPORTED, "matmul_int8_packed: shape");
+    PackedWs ws{};
+    int rc = packed_workspace(st, (size_t)rows * (size_t)S * GT_BYTES, (size_t)rows * GR, 0, &ws);
+    if (rc) return rc;
+    int *err = nullptr;
+    if ((rc = device_error_word(&err))) return rc;
+    act_terms_kernel<<<(unsigned)M, 256, 0, st>>>(A, ws.terms, ws.scale, (long long)K, S, GR);
+    if ((rc = check_launch("act_terms_kernel"))) return rc;
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = dim3((unsigned)grid);
+    cfg.blockDim = dim3(GNT);
+    cfg.dynamicSmemBytes = GSMEM;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    const cudaError_t le = cudaLaunchKernelEx(&cfg, int8_gemm_kernel, qp, (const int8_t *)ws.terms,
+                                              (const float *)ws.scale, s, C, (long long)M, (long long)N, S, ncol, err);
+    if (le != cudaSuccess) return check_cuda(le, "int8_gemm_kernel launch");
+    return check_launch("int8_gemm_kernel");
+}
+
 }  // namespace
 
 bool int8_packed_supported(size_t K, size_t N) {
@@ -475,8 +645,13 @@ int launch_matmul_int8_packed(const float *A, const int8_t *qp, const float *s, 
                                                   (int)PSMEM),
                              "matmul_int8_packed: smem attribute")))
             return rc;
+        if ((rc = check_cuda(cudaFuncSetAttribute(int8_gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                  (int)GSMEM),
+                             "matmul_int8_packed: smem attribute")))
+            return rc;
         attr_set.fetch_or(bit);
     }
+    if (M > (size_t)PMT) return run_gemm(A, qp, s, C, M, K, N, st);
     const long long S = (long long)((K + PK - 1) / PK), tiles = (long long)((N + PT - 1) / PT), U = tiles * S;
     const long long G = std::min<long long>(U, sm_count());
     const size_t blocks = (M + PMT - 1) / PMT;
@@ -484,7 +659,7 @@ int launch_matmul_int8_packed(const float *A, const int8_t *qp, const float *s, 
     if ((rc = packed_workspace(st, blocks * (size_t)S * T_BYTES, blocks * PMT, (size_t)tiles, &ws))) return rc;
     int *err = nullptr;
     if ((rc = device_error_word(&err))) return rc;
-    act_terms_kernel<<<(unsigned)M, 256, 0, st>>>(A, ws.terms, ws.scale, (long long)K, S);
+    act_terms_kernel<<<(unsigned)M, 256, 0, st>>>(A, ws.terms, ws.scale, (long long)K, S, PMT);
     if ((rc = check_launch("act_terms_kernel"))) return rc;
     // one pass over the weights per 16 activation rows
     for (size_t b = 0; b < blocks; ++b) {

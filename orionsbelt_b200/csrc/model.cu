@@ -491,10 +491,13 @@ int build_qw(ModelEngine *e, QW *w, size_t K, size_t k0, size_t k1, const std::v
     if (!rc) rc = malloc_keep(e, (void **)&w->q, (k1 - k0) * N, false);
     if (!rc) rc = check_cuda(cudaMemcpy(w->q, qt + k0 * N, (k1 - k0) * N, cudaMemcpyDeviceToDevice), "model: codes");
     const size_t B = e->cfg.batch;
-    if (!rc && (lm_head || B > GEMV_MAX_BATCH) && int8_packed_supported(k1 - k0, N)) {
+    // packed for the tensor-core stream (decode above batch 4, the LM head,
+    // every prompt), and blocked for the GEMV where small batches decode
+    if (!rc && int8_packed_supported(k1 - k0, N)) {
         if (!(rc = malloc_keep(e, (void **)&w->qp, int8_packed_bytes(k1 - k0, N), false)))
             rc = int8_pack_weights(w->q, w->qp, k1 - k0, N, 0);
-    } else if (!rc && gemv_int8_supported(B, k1 - k0, N, w->q)) {
+    }
+    if (!rc && !lm_head && B <= GEMV_MAX_BATCH && gemv_int8_supported(B, k1 - k0, N, w->q)) {
         if (!(rc = malloc_keep(e, (void **)&w->qb, gemv_blocked_bytes(B, k1 - k0, N), false)))
             rc = gemv_block_weights(B, w->q, w->qb, k1 - k0, N, 0);
     }
@@ -536,8 +539,8 @@ enum : unsigned {
 unsigned tidl(size_t layer, unsigned kind) { return (unsigned)(layer * 64 + kind); }
 
 int mm(const float *A, const QW &w, float *Cm, size_t M, cudaStream_t st) {
+    if (w.qb && M <= GEMV_MAX_BATCH) return launch_gemv_int8_blocked(A, w.qb, w.s, Cm, M, w.K, w.N, st);
     if (w.qp) return launch_matmul_int8_packed(A, w.qp, w.s, Cm, M, w.K, w.N, st);
-    if (w.qb) return launch_gemv_int8_blocked(A, w.qb, w.s, Cm, M, w.K, w.N, st);
     return launch_matmul_int8(A, w.q, w.s, Cm, M, w.K, w.N, st);
 }
 int allreduce(ModelEngine *e, float *buf, size_t n, cudaStream_t st) {
@@ -794,8 +797,10 @@ __global__ void attn_prompt_prep_kernel(const float *__restrict__ y, long long n
         kc[(pos * hkv + (r - hq)) * D + i] = __float2bfloat16_rn(outv);
 }
 
-// Row-major int8 projection of M prompt rows (the tensor-core GEMM).
+// int8 projection of M prompt rows: the row-tiled int8 GEMM over the packed
+// weights (the row-major tensor-core GEMM where they could not be packed).
 int mm_rows(const float *A, const QW &w, float *Cm, size_t M, cudaStream_t st) {
+    if (w.qp) return launch_matmul_int8_packed(A, w.qp, w.s, Cm, M, w.K, w.N, st);
     return launch_matmul_int8(A, w.q, w.s, Cm, M, w.K, w.N, st);
 }
 
@@ -1337,6 +1342,22 @@ int model_fill(void *engine, size_t ctx, unsigned long long seed) {
         }
     }
     if (!rc) rc = check_cuda(cudaDeviceSynchronize(), "model_fill: sync");
+    return rc;
+}
+
+// Every sequence back to position 0: GDN states and conv histories zero (the
+// KV cache rows are written before they are read).
+int model_reset(void *engine) {
+    ModelEngine *e = static_cast<ModelEngine *>(engine);
+    if (!e) return set_error(KAI_GDN_ERR_INVALID, "model_reset: null engine");
+    const size_t B = e->cfg.batch, d = e->d;
+    int rc = check_cuda(cudaDeviceSynchronize(), "model_reset: sync");
+    for (size_t l = 0; l < e->layers.size() && !rc; ++l) {
+        ModelEngine::Layer &L = e->layers[l];
+        if (!e->is_gdn[l]) continue;
+        rc = check_cuda(cudaMemset(L.state, 0, B * e->hv * d * d * sizeof(float)), "model_reset: state");
+        if (!rc) rc = check_cuda(cudaMemset(L.hist, 0, B * 3 * e->C * sizeof(float)), "model_reset: history");
+    }
     return rc;
 }
 

@@ -431,6 +431,8 @@ int kai_gdn_model_weight(void *engine, size_t layer, int which, void *data, floa
     return model_weight(engine, layer, which, data, scales, rows, cols);
 }
 int kai_gdn_model_fill(void *engine, size_t ctx, unsigned long long seed) { return model_fill(engine, ctx, seed); }
+
+int kai_gdn_model_reset(void *engine) { return model_reset(engine); }
 int kai_gdn_model_destroy(void *engine) { return model_destroy(engine); }
 
 int kai_run_gdn_quantize_int8_sm100a(const float *B, int8_t *q, float *s, size_t K, size_t N, void *stream) {

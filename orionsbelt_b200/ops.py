@@ -338,6 +338,10 @@ class ModelEngine:
     def step(self, pos: int, stream=None) -> None:
         check(lib().kai_gdn_model_step(self._h, int(pos), _stream(stream)))
 
+    def reset(self) -> None:
+        """Every sequence back to position 0 (GDN states and conv histories zero)."""
+        check(lib().kai_gdn_model_reset(self._h))
+
     def prefill(self, tokens, pos0: int = 0, stream=None) -> None:
         """Consume prompts tokens [batch][T] at positions pos0 .. pos0 + T - 1;
         the greedy next tokens become the current tokens."""

@@ -3,6 +3,7 @@
     python profile_cases.py decode [--launches 3]
     python profile_cases.py chunk  [--launches 1]
     python profile_cases.py conv | cumsum | scan | attn | int8 | int8m16 | lmhead | lmhead16 | ffn16 | model
+    python profile_cases.py prefill [--launches 1]
 
 Each case holds a few hundred MB to a few GB on the device (inputs larger
 than the 126 MB L2, so DRAM counters mean something), runs a few launches of
@@ -22,6 +23,8 @@ its kernel through the C ABI, and exits.  Cases:
   lmhead16 the LM head weights packed for streaming, M=16 (the tensor-core
           weight-streaming kernel)
   ffn16   the packed path on the FFN up weights, M=16
+  prefill the config-4 engine's prefill of a 32768-token prompt at batch 1
+          (one prompt per launch, after a 256-token warm-up prefill)
   model   the config-4 engine (4B geometry, batch 1, synthetic 32k context):
           one greedy decode step per launch
 """
@@ -41,7 +44,7 @@ from orionsbelt_b200 import _lib, ops, synth  # noqa: E402
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("case", choices=["decode", "chunk", "conv", "cumsum", "scan", "attn", "int8", "int8m16", "lmhead",
-                                     "lmhead16", "ffn16", "model"])
+                                     "lmhead16", "ffn16", "model", "prefill"])
     ap.add_argument("--launches", type=int, default=3)
     a = ap.parse_args()
     torch.cuda.set_device(0)
@@ -106,6 +109,21 @@ def main() -> None:
         A = synth.device_normal((16, K), 8, 2)
         Cm = torch.empty((16, N), device="cuda")
         fn = lambda: ops.matmul_int8_packed(A, qp, s8, Cm)  # noqa: E731
+    elif a.case == "prefill":
+        import numpy as np
+
+        import bench
+        T = 32768
+        eng = ops.ModelEngine(dict(bench.CFG4, max_ctx=T + 64), 1, seed=42)
+        prompt = np.random.default_rng(0).integers(0, bench.CFG4["vocab"], (1, T)).astype(np.int32)
+        side = torch.cuda.Stream()
+        with torch.cuda.stream(side):
+            eng.prefill(prompt[:, :256], 0, side)
+
+        def fn():
+            eng.reset()
+            with torch.cuda.stream(side):
+                eng.prefill(prompt, 0, side)
     elif a.case == "model":
         import numpy as np
 

@@ -1,6 +1,7 @@
 """GPU parity of the packed int8 matmul (kai_run_gdn_int8_pack_sm100a,
 kai_run_gdn_matmul_int8_packed_sm100a): the reference's matmul_int8
-(gdn_e2e_decode.c:608-681) over weights packed once for streaming.
+(gdn_e2e_decode.c:608-681) over weights packed once for streaming -- the
+weight stream for up to 16 activation rows, the row-tiled GEMM above.
 
 Bars (written here):
   packing            bit-identical to a numpy restatement of the layout
@@ -52,7 +53,7 @@ def test_pack_layout_bit_identical(cuda, orc, K, N):
 SHAPES = [(64, 256), (66, 272), (300, 48), (2560, 9216), (9216, 2560), (4096, 2560), (2560, 2064)]
 
 
-@pytest.mark.parametrize("M", [1, 2, 5, 15, 16, 17, 40])
+@pytest.mark.parametrize("M", [1, 2, 5, 15, 16, 17, 40, 64, 300])
 @pytest.mark.parametrize("K,N", SHAPES)
 def test_matmul_int8_packed_vs_oracle(cuda, orc, M, K, N):
     if M > 17 and K * N > 6_000_000:

@@ -13,8 +13,8 @@ the engine's argmax equals the oracle's wherever the oracle's top two logits
 differ by more than 1e-4 of the logit scale.
 
 Tensor parallelism: the same model on two GPUs (tp_size 2, NCCL all-reduce
-and all-gather) equals the single-GPU engine (skipped with fewer than two
-GPUs).
+and all-gather), prompt prefill then decode steps, equals the single-GPU
+engine (skipped with fewer than two GPUs).
 """
 from __future__ import annotations
 
@@ -30,6 +30,7 @@ GEOM = dict(hidden=256, vocab=4096, inter=512, is_gdn=[1, 1, 1, 0, 1, 1, 1, 0], 
             gdn_head_dim=128, attn_heads=4, attn_kv_heads=2, attn_head_dim=128, rope_dims=32, rope_theta=1e6,
             rms_eps=1e-6, max_ctx=64, weight_std=0.05)
 B, STEPS = 3, 6
+GEOM_TP = dict(GEOM, max_ctx=64 + STEPS)  # a 40-token prompt, then the steps
 
 
 @pytest.mark.parametrize("B", [3, 6])
@@ -109,16 +110,18 @@ def test_model_prefill_matches_oracle(cuda, orc, B, split):
     eng.close()
 
 
-def _tp_rank(rank, nid, tokens, q):
+def _tp_rank(rank, nid, prompt, tokens, q):
     try:
         import torch
 
         torch.cuda.set_device(rank)
-        eng = ops.ModelEngine(GEOM, B, seed=11, tp_rank=rank, tp_size=2, nccl_id=nid)
+        eng = ops.ModelEngine(GEOM_TP, B, seed=11, tp_rank=rank, tp_size=2, nccl_id=nid)
         stream = torch.cuda.Stream()
         out = []
         with torch.cuda.stream(stream):
-            for pos, tok in enumerate(tokens):
+            eng.prefill(prompt, 0, stream)
+            out.append((eng.tokens(), eng.read(0, (B, GEOM["hidden"])), eng.read(1, (B, GEOM["vocab"] // 2))))
+            for pos, tok in enumerate(tokens, start=prompt.shape[1]):
                 eng.set_tokens(tok)
                 eng.step(pos, stream)
                 stream.synchronize()
@@ -137,11 +140,12 @@ def test_model_tensor_parallel_two_gpus(cuda):
     import torch.multiprocessing as mp
 
     rng = np.random.default_rng(4)
+    prompt = rng.integers(0, GEOM["vocab"], (B, 40)).astype(np.int32)
     tokens = [rng.integers(0, GEOM["vocab"], B).astype(np.int32) for _ in range(STEPS)]
     nid = ops.ModelEngine.nccl_id()
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
-    procs = [ctx.Process(target=_tp_rank, args=(r, nid, tokens, q)) for r in (0, 1)]
+    procs = [ctx.Process(target=_tp_rank, args=(r, nid, prompt, tokens, q)) for r in (0, 1)]
     for p in procs:
         p.start()
     try:
@@ -153,19 +157,21 @@ def test_model_tensor_parallel_two_gpus(cuda):
                 p.kill()
     for r in (0, 1):
         assert not isinstance(res[r], str), res[r]
-    eng = ops.ModelEngine(GEOM, B, seed=11)
+    eng = ops.ModelEngine(GEOM_TP, B, seed=11)
     stream = torch.cuda.Stream()
     with torch.cuda.stream(stream):
-        for pos, tok in enumerate(tokens):
-            eng.set_tokens(tok)
-            eng.step(pos, stream)
-            stream.synchronize()
+        eng.prefill(prompt, 0, stream)
+        for i, tok in enumerate([None] + tokens):
+            if tok is not None:
+                eng.set_tokens(tok)
+                eng.step(prompt.shape[1] + i - 1, stream)
+                stream.synchronize()
             h = eng.read(0, (B, GEOM["hidden"]))
             lg = eng.read(1, (B, GEOM["vocab"]))
             t1 = eng.tokens()
             for r in (0, 1):
-                tt, hh, ll = res[r][pos]
-                assert rel_l2(hh, h) < 1e-4, (pos, r, rel_l2(hh, h))
+                tt, hh, ll = res[r][i]
+                assert rel_l2(hh, h) < 1e-4, (i, r, rel_l2(hh, h))
                 half = GEOM["vocab"] // 2
                 assert rel_l2(ll, lg[:, r * half:(r + 1) * half]) < 1e-4
                 assert np.array_equal(tt, t1)
