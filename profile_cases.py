@@ -4,6 +4,7 @@
     python profile_cases.py chunk  [--launches 1]
     python profile_cases.py conv | cumsum | scan | attn | int8 | int8m16 | lmhead | lmhead16 | ffn16 | model
     python profile_cases.py prefill [--launches 1]
+    python profile_cases.py gemm4k
 
 Each case holds a few hundred MB to a few GB on the device (inputs larger
 than the 126 MB L2, so DRAM counters mean something), runs a few launches of
@@ -23,6 +24,8 @@ its kernel through the C ABI, and exits.  Cases:
   lmhead16 the LM head weights packed for streaming, M=16 (the tensor-core
           weight-streaming kernel)
   ffn16   the packed path on the FFN up weights, M=16
+  gemm4k  the packed-weight GEMM of a 4096-row prompt block through the
+          config-4 GDN input projection (K=2560, N=12352)
   prefill the config-4 engine's prefill of a 32768-token prompt at batch 1
           (one prompt per launch, after a 256-token warm-up prefill)
   model   the config-4 engine (4B geometry, batch 1, synthetic 32k context):
@@ -44,7 +47,7 @@ from orionsbelt_b200 import _lib, ops, synth  # noqa: E402
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("case", choices=["decode", "chunk", "conv", "cumsum", "scan", "attn", "int8", "int8m16", "lmhead",
-                                     "lmhead16", "ffn16", "model", "prefill"])
+                                     "lmhead16", "ffn16", "model", "prefill", "gemm4k"])
     ap.add_argument("--launches", type=int, default=3)
     a = ap.parse_args()
     torch.cuda.set_device(0)
@@ -108,6 +111,18 @@ def main() -> None:
         del q8
         A = synth.device_normal((16, K), 8, 2)
         Cm = torch.empty((16, N), device="cuda")
+        fn = lambda: ops.matmul_int8_packed(A, qp, s8, Cm)  # noqa: E731
+    elif a.case == "gemm4k":
+        K, N, M = 2560, 12352, 4096
+        W = synth.device_normal((K, N), 8, 1, std=0.02)
+        q8 = torch.empty((K, N), dtype=torch.int8, device="cuda")
+        s8 = torch.empty(N, device="cuda")
+        ops.quantize_int8(W, q8, s8)
+        del W
+        qp = ops.pack_int8(q8)
+        del q8
+        A = synth.device_normal((M, K), 8, 2)
+        Cm = torch.empty((M, N), device="cuda")
         fn = lambda: ops.matmul_int8_packed(A, qp, s8, Cm)  # noqa: E731
     elif a.case == "prefill":
         import numpy as np
