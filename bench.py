@@ -573,11 +573,10 @@ CFG4 = dict(hidden=2560, vocab=151936, inter=9216, is_gdn=[1, 1, 1, 0] * 8, gdn_
 def run_model(args, world, rank, barrier, peaks, ctx=32768, steps=256):
     """the Qwen3.5-4B-style hybrid (kai_gdn_model_*),
     tensor-parallel over all ranks (NCCL all-reduce after every output
-    projection, all-gather of the argmax).  Batch 1: a `ctx`-token prompt
-    through kai_gdn_model_prefill (timed), then 256 greedy decode steps from
-    the state it left.  Batch 16: the same 256 steps after a synthetic
-    `ctx`-token context (kai_gdn_model_fill; sixteen 32k prefills would take
-    over a minute).  Device time with CUDA events, max over ranks; the
+    projection, all-gather of the argmax).  At batch 1 and at batch 16: a
+    `ctx`-token prompt of uniform random token ids per sequence through
+    kai_gdn_model_prefill (timed), then 256 greedy decode steps from the
+    state it left (timed).  Device time with CUDA events, max over ranks; the
     generated tokens are read back to the host once, after the last step."""
     import torch
     import torch.distributed as dist
@@ -605,28 +604,24 @@ def run_model(args, world, rank, barrier, peaks, ctx=32768, steps=256):
     stream = torch.cuda.Stream()
     for B in (1, 16):
         eng = ops.ModelEngine(geom, B, seed=42, tp_rank=rank, tp_size=world, nccl_id=fresh_id())
-        if B == 1:
-            prompt = np.random.default_rng(9).integers(0, geom["vocab"], (1, ctx)).astype(np.int32)
-            with torch.cuda.stream(stream):
-                eng.prefill(prompt[:, :512], 0, stream)  # the prompt workspace and the kernels' first launches
-                eng.reset()
-                barrier()
-                p0, p1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-                p0.record(stream)
-                eng.prefill(prompt, 0, stream)
-                p1.record(stream)
-                stream.synchronize()
-            pms = p0.elapsed_time(p1)
-            if world > 1:
-                t = torch.tensor([pms], device="cuda")
-                dist.all_reduce(t, op=dist.ReduceOp.MAX)
-                pms = t.item()
-            out["prefill_b1"] = {"tokens": ctx, "s": round(pms / 1e3, 4),
-                                 "tokens_per_s": round(ctx / (pms / 1e3), 1),
-                                 "first_token": int(eng.tokens()[0])}
-        else:
-            eng.fill(ctx, seed=3)
-            eng.set_tokens(np.random.default_rng(9).integers(0, geom["vocab"], B).astype(np.int32))
+        prompt = np.random.default_rng(9 + B).integers(0, geom["vocab"], (B, ctx)).astype(np.int32)
+        with torch.cuda.stream(stream):
+            eng.prefill(prompt[:, :512], 0, stream)  # the prompt workspace and the kernels' first launches
+            eng.reset()
+            barrier()
+            p0, p1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            p0.record(stream)
+            eng.prefill(prompt, 0, stream)
+            p1.record(stream)
+            stream.synchronize()
+        pms = p0.elapsed_time(p1)
+        if world > 1:
+            t = torch.tensor([pms], device="cuda")
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            pms = t.item()
+        out[f"prefill_b{B}"] = {"tokens": B * ctx, "s": round(pms / 1e3, 4),
+                                "tokens_per_s": round(B * ctx / (pms / 1e3), 1),
+                                "first_tokens": [int(x) for x in eng.tokens()[:4]]}
         barrier()
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         with torch.cuda.stream(stream):
@@ -656,9 +651,9 @@ def run_model(args, world, rank, barrier, peaks, ctx=32768, steps=256):
         torch.cuda.empty_cache()
         barrier()
     out.update({"workload": f"config 4: Qwen3.5-4B-style hybrid (hidden 2560, 24 GDN + 8 gated-GQA layers, FFN "
-                            f"9216, vocab 151936, int8 weights, bf16 KV cache): batch 1 a {ctx}-token prompt "
-                            f"(prefill) then {steps} greedy decode steps; batch 16 {steps} steps after a synthetic "
-                            f"{ctx}-token context; tensor-parallel x{world} over NCCL",
+                            f"9216, vocab 151936, int8 weights, bf16 KV cache): per sequence a {ctx}-token prompt "
+                            f"of uniform random ids (prefill), then {steps} greedy decode steps, at batch 1 and 16; "
+                            f"tensor-parallel x{world} over NCCL",
                 "kernels": "decode: gemv_int8_kernel / int8_packed_kernel, decode_step_kernel, attn_tc_kernel, model "
                            "elementwise kernels, per-segment CUDA graphs; prefill: int8_gemm_kernel (row-tiled int8 "
                            "tcgen05 GEMM over the packed weights), chunk_scan_fp32_kernel, attn_prefill_kernel",
