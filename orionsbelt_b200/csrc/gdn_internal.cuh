@@ -94,6 +94,11 @@ size_t int8_packed_bytes(size_t K, size_t N);
 int int8_pack_weights(const int8_t *q, int8_t *qp, size_t K, size_t N, cudaStream_t st);
 int launch_matmul_int8_packed(const float *A, const int8_t *qp, const float *s, float *C, size_t M, size_t K,
                               size_t N, cudaStream_t st);
+// The same over activation terms a producer kernel already wrote
+// (int8_terms.cuh, 16-row blocks: int8_terms_bytes(M, K) bytes; scales [M]).
+size_t int8_terms_bytes(size_t M, size_t K);
+int launch_matmul_int8_packed_terms(const int8_t *terms, const float *scale, const int8_t *qp, const float *s,
+                                    float *C, size_t M, size_t K, size_t N, cudaStream_t st);
 // Per-stream split-K workspace of the int8 matmuls: slab counters (zero
 // between calls: each kernel's last CTA resets its counter) and partial sums.
 int split_workspace(cudaStream_t st, size_t nctr, size_t npart, unsigned int **ctr, float **part);

@@ -57,6 +57,7 @@
 #include <vector>
 
 #include "gdn_internal.cuh"
+#include "int8_terms.cuh"
 #include "umma.cuh"
 
 namespace gdn {
@@ -137,6 +138,10 @@ __global__ void __launch_bounds__(256) act_terms_kernel(const float *__restrict_
     mx = red[0];
 #pragma unroll
     for (int i = 1; i < 8; ++i) mx = fmaxf(mx, red[i]);
+    if (K % 16 == 0) {  // 16-byte stores of whole k-groups
+        terms::write_row(a, K, S, mx, terms, scale, RB, m);
+        return;
+    }
     if (t == 0) scale[m] = mx;
     const float inv = mx > 0.f ? 127.0f / mx : 0.f;
     const long long sb = 3ll * RB * PK;  // bytes of one stage of a row block
@@ -627,14 +632,8 @@ int int8_pack_weights(const int8_t *q, int8_t *qp, size_t K, size_t N, cudaStrea
     return check_launch("int8_pack_kernel");
 }
 
-int launch_matmul_int8_packed(const float *A, const int8_t *qp, const float *s, float *C, size_t M, size_t K,
-                              size_t N, cudaStream_t st) {
-    if (M == 0 || N == 0) return KAI_GDN_OK;
-    if (!A || !qp || !s || !C) return set_error(KAI_GDN_ERR_INVALID, "matmul_int8_packed: null pointer");
-    if (!int8_packed_supported(K, N) || (uintptr_t)qp % 16)
-        return set_error(KAI_GDN_ERR_UNSUPPORTED,
-                         "matmul_int8_packed: N %% 16, K <= 131072 and 16-byte aligned packed weights");
-    if (M > 0x7fffffffull) return set_error(KAI_GDN_ERR_UNSUPPORTED, "matmul_int8_packed: M too large");
+namespace {
+int packed_attrs() {
     static std::atomic<unsigned long long> attr_set{0};  // per device
     int dev = 0;
     int rc = check_cuda(cudaGetDevice(&dev), "matmul_int8_packed: cudaGetDevice");
@@ -651,17 +650,51 @@ int launch_matmul_int8_packed(const float *A, const int8_t *qp, const float *s, 
             return rc;
         attr_set.fetch_or(bit);
     }
+    return KAI_GDN_OK;
+}
+}  // namespace
+
+int launch_matmul_int8_packed(const float *A, const int8_t *qp, const float *s, float *C, size_t M, size_t K,
+                              size_t N, cudaStream_t st) {
+    if (M == 0 || N == 0) return KAI_GDN_OK;
+    if (!A || !qp || !s || !C) return set_error(KAI_GDN_ERR_INVALID, "matmul_int8_packed: null pointer");
+    if (!int8_packed_supported(K, N) || (uintptr_t)qp % 16)
+        return set_error(KAI_GDN_ERR_UNSUPPORTED,
+                         "matmul_int8_packed: N %% 16, K <= 131072 and 16-byte aligned packed weights");
+    if (M > 0x7fffffffull) return set_error(KAI_GDN_ERR_UNSUPPORTED, "matmul_int8_packed: M too large");
+    int rc = packed_attrs();
+    if (rc) return rc;
     if (M > (size_t)PMT) return run_gemm(A, qp, s, C, M, K, N, st);
+    const long long S = (long long)((K + PK - 1) / PK);
+    PackedWs ws{};
+    if ((rc = packed_workspace(st, (size_t)S * T_BYTES, PMT, 0, &ws))) return rc;
+    act_terms_kernel<<<(unsigned)M, 256, 0, st>>>(A, ws.terms, ws.scale, (long long)K, S, PMT);
+    if ((rc = check_launch("act_terms_kernel"))) return rc;
+    return launch_matmul_int8_packed_terms(ws.terms, ws.scale, qp, s, C, M, K, N, st);
+}
+
+size_t int8_terms_bytes(size_t M, size_t K) {
+    return (M + PMT - 1) / PMT * ((K + PK - 1) / PK) * (size_t)T_BYTES;
+}
+
+// The weight stream over activation terms already in place (the 16-row
+// layout of int8_terms.cuh, scales [M]): one pass over the weights per 16
+// rows, each a programmatic dependent of the kernel before it.
+int launch_matmul_int8_packed_terms(const int8_t *terms, const float *scale, const int8_t *qp, const float *s,
+                                    float *C, size_t M, size_t K, size_t N, cudaStream_t st) {
+    if (M == 0 || N == 0) return KAI_GDN_OK;
+    if (!terms || !scale || !qp || !s || !C) return set_error(KAI_GDN_ERR_INVALID, "matmul_int8_packed: null pointer");
+    if (!int8_packed_supported(K, N) || (uintptr_t)qp % 16 || (uintptr_t)terms % 16)
+        return set_error(KAI_GDN_ERR_UNSUPPORTED, "matmul_int8_packed: shape or alignment");
+    int rc = packed_attrs();
+    if (rc) return rc;
     const long long S = (long long)((K + PK - 1) / PK), tiles = (long long)((N + PT - 1) / PT), U = tiles * S;
     const long long G = std::min<long long>(U, sm_count());
     const size_t blocks = (M + PMT - 1) / PMT;
     PackedWs ws{};
-    if ((rc = packed_workspace(st, blocks * (size_t)S * T_BYTES, blocks * PMT, (size_t)tiles, &ws))) return rc;
+    if ((rc = packed_workspace(st, 0, 0, (size_t)tiles, &ws))) return rc;
     int *err = nullptr;
     if ((rc = device_error_word(&err))) return rc;
-    act_terms_kernel<<<(unsigned)M, 256, 0, st>>>(A, ws.terms, ws.scale, (long long)K, S, PMT);
-    if ((rc = check_launch("act_terms_kernel"))) return rc;
-    // one pass over the weights per 16 activation rows
     for (size_t b = 0; b < blocks; ++b) {
         const size_t r0 = b * PMT, rows = std::min<size_t>(PMT, M - r0);
         cudaLaunchConfig_t cfg{};
@@ -675,9 +708,8 @@ int launch_matmul_int8_packed(const float *A, const int8_t *qp, const float *s, 
         cfg.attrs = attr;
         cfg.numAttrs = 1;
         const cudaError_t le =
-            cudaLaunchKernelEx(&cfg, int8_packed_kernel, qp, (const int8_t *)(ws.terms + b * (size_t)S * T_BYTES),
-                               (const float *)(ws.scale + r0), s, C + r0 * N, (int)rows, (long long)N, S, U, ws.acc,
-                               ws.ctr, err);
+            cudaLaunchKernelEx(&cfg, int8_packed_kernel, qp, terms + b * (size_t)S * T_BYTES, scale + r0, s,
+                               C + r0 * N, (int)rows, (long long)N, S, U, ws.acc, ws.ctr, err);
         if (le != cudaSuccess) return check_cuda(le, "int8_packed_kernel launch");
         if ((rc = check_launch("int8_packed_kernel"))) return rc;
     }

@@ -47,6 +47,7 @@
 #include <vector>
 
 #include "gdn_internal.cuh"
+#include "int8_terms.cuh"
 
 namespace gdn {
 namespace {
@@ -99,10 +100,12 @@ __device__ __forceinline__ void pdl_enter() {
     asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 }
 template <typename... KArgs, typename... Args>
-int launch_pdl(const char *name, void (*kernel)(KArgs...), dim3 grid, dim3 block, cudaStream_t st, Args... args) {
+int launch_pdl_smem(const char *name, void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st,
+                    Args... args) {
     cudaLaunchConfig_t cfg{};
     cfg.gridDim = grid;
     cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
     cfg.stream = st;
     cudaLaunchAttribute attr[1];
     attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
@@ -112,6 +115,10 @@ int launch_pdl(const char *name, void (*kernel)(KArgs...), dim3 grid, dim3 block
     const cudaError_t e = cudaLaunchKernelEx(&cfg, kernel, static_cast<KArgs>(args)...);
     if (e != cudaSuccess) return check_cuda(e, name);
     return check_launch(name);
+}
+template <typename... KArgs, typename... Args>
+int launch_pdl(const char *name, void (*kernel)(KArgs...), dim3 grid, dim3 block, cudaStream_t st, Args... args) {
+    return launch_pdl_smem(name, kernel, grid, block, 0, st, args...);
 }
 
 // ------------------------------------------------------------- weights
@@ -335,6 +342,114 @@ __global__ void swiglu_kernel(const float *__restrict__ gu, float *__restrict__ 
         act[e] = silu(gu[b * 2 * I + c]) * gu[b * 2 * I + I + c];
     }
 }
+// ------------------------------------------------------------------
+// Producers that write a projection's input straight as the packed int8
+// matmul's activation terms (int8_terms.cuh), for batches the tensor-core
+// stream serves: each is the elementwise kernel above with the row kept in
+// shared memory, its largest magnitude reduced and its terms written, so the
+// fp32 row never goes through memory and one launch per projection is saved.
+// One CTA (1024 threads) per row; dynamic shared memory holds the row.
+__device__ __forceinline__ float block_max(float v, float *red) {
+    for (int o = 16; o; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+    const int w = threadIdx.x >> 5, nw = blockDim.x >> 5;
+    __syncthreads();
+    if ((threadIdx.x & 31) == 0) red[w] = v;
+    __syncthreads();
+    float t = threadIdx.x < nw ? red[threadIdx.x] : 0.f;
+    if (w == 0)
+        for (int o = 16; o; o >>= 1) t = fmaxf(t, __shfl_xor_sync(0xffffffffu, t, o));
+    if (threadIdx.x == 0) red[0] = t;
+    __syncthreads();
+    return red[0];
+}
+// h += delta (when given); terms of h / sqrt(mean(h^2) + eps) * w   (add_rmsnorm_kernel)
+__global__ void addnorm_terms_kernel(float *__restrict__ h, const float *__restrict__ delta,
+                                     const float *__restrict__ w, long long H, float eps, long long S,
+                                     int8_t *__restrict__ terms, float *__restrict__ scale) {
+    pdl_enter();
+    extern __shared__ float xs[];
+    __shared__ float red[32];
+    const long long b = blockIdx.x;
+    float *hr = h + b * H;
+    float ss = 0.f;
+    for (long long i = threadIdx.x; i < H; i += blockDim.x) {
+        float v = hr[i];
+        if (delta) {
+            v += delta[b * H + i];
+            hr[i] = v;
+        }
+        xs[i] = v;
+        ss += v * v;
+    }
+    const float inv = rsqrtf(block_sum(ss, red) / (float)H + eps);
+    float mx = 0.f;
+    for (long long i = threadIdx.x; i < H; i += blockDim.x) {
+        const float x = xs[i] * inv * w[i];
+        xs[i] = x;
+        mx = fmaxf(mx, fabsf(x));
+    }
+    mx = block_max(mx, red);
+    terms::write_row(xs, H, S, mx, terms, scale, 16, b);
+}
+// terms of SiLU(gate) * up over rows [gate (I) | up (I)]   (swiglu_kernel)
+__global__ void swiglu_terms_kernel(const float *__restrict__ gu, long long I, long long S, int8_t *__restrict__ terms,
+                                    float *__restrict__ scale) {
+    pdl_enter();
+    extern __shared__ float xs[];
+    __shared__ float red[32];
+    const long long b = blockIdx.x;
+    float mx = 0.f;
+    for (long long c = threadIdx.x; c < I; c += blockDim.x) {
+        const float x = silu(gu[b * 2 * I + c]) * gu[b * 2 * I + I + c];
+        xs[c] = x;
+        mx = fmaxf(mx, fabsf(x));
+    }
+    mx = block_max(mx, red);
+    terms::write_row(xs, I, S, mx, terms, scale, 16, b);
+}
+// terms of o_head / sqrt(mean(o_head^2) + eps) * w * SiLU(z)   (gated_rmsnorm_kernel);
+// a warp per head
+__global__ void gatednorm_terms_kernel(const float *__restrict__ o, const float *__restrict__ y, long long ny,
+                                       long long zoff, const float *__restrict__ w, int hv, int d, float eps,
+                                       long long S, int8_t *__restrict__ terms, float *__restrict__ scale) {
+    pdl_enter();
+    extern __shared__ float xs[];
+    __shared__ float red[32];
+    const long long b = blockIdx.x;
+    const int lane = threadIdx.x & 31, wp = threadIdx.x >> 5, nw = blockDim.x >> 5;
+    float mx = 0.f;
+    for (int hh = wp; hh < hv; hh += nw) {
+        const float *orow = o + ((long long)b * hv + hh) * d;
+        float ss = 0.f;
+        for (int i = lane; i < d; i += 32) ss += orow[i] * orow[i];
+        for (int m = 16; m; m >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, m);
+        const float inv = rsqrtf(ss / (float)d + eps);
+        for (int i = lane; i < d; i += 32) {
+            const float x = orow[i] * inv * w[i] * silu(y[b * ny + zoff + (long long)hh * d + i]);
+            xs[hh * d + i] = x;
+            mx = fmaxf(mx, fabsf(x));
+        }
+    }
+    mx = block_max(mx, red);
+    terms::write_row(xs, (long long)hv * d, S, mx, terms, scale, 16, b);
+}
+// terms of o * sigmoid(gate)   (attn_gate_kernel)
+__global__ void attngate_terms_kernel(const float *__restrict__ o, const float *__restrict__ gate, long long n,
+                                      long long S, int8_t *__restrict__ terms, float *__restrict__ scale) {
+    pdl_enter();
+    extern __shared__ float xs[];
+    __shared__ float red[32];
+    const long long b = blockIdx.x;
+    float mx = 0.f;
+    for (long long i = threadIdx.x; i < n; i += blockDim.x) {
+        const float x = o[b * n + i] * sigm(gate[b * n + i]);
+        xs[i] = x;
+        mx = fmaxf(mx, fabsf(x));
+    }
+    mx = block_max(mx, red);
+    terms::write_row(xs, n, S, mx, terms, scale, 16, b);
+}
+
 // Per row: the largest logit and its global index (smallest index on ties).
 struct ArgMax {
     float v;
@@ -434,6 +549,11 @@ struct ModelEngine {
     int *tok = nullptr, *pos = nullptr;
     ArgMax *cand = nullptr, *cand_all = nullptr;
     std::vector<void *> allocs;
+    // batches the tensor-core stream serves: projection inputs go straight
+    // to activation terms (fused producers)
+    bool fused = false;
+    int8_t *terms = nullptr;
+    float *tscale = nullptr;
     // prompt workspace (grown on demand by model_prefill): per-token rows
     struct Prompt {
         void *base = nullptr;
@@ -543,19 +663,78 @@ int mm(const float *A, const QW &w, float *Cm, size_t M, cudaStream_t st) {
     if (w.qp) return launch_matmul_int8_packed(A, w.qp, w.s, Cm, M, w.K, w.N, st);
     return launch_matmul_int8(A, w.q, w.s, Cm, M, w.K, w.N, st);
 }
+// A projection of this step's rows together with the producer of its input:
+// the fp32 elementwise kernel then mm(), or (fused batches) the producer
+// writing the activation terms then the packed weight stream over them.
+long long kstages(size_t K) { return (long long)((K + 63) / 64); }
+int terms_mm(ModelEngine *e, const QW &w, float *Cm, cudaStream_t st) {
+    return launch_matmul_int8_packed_terms(e->terms, e->tscale, w.qp, w.s, Cm, e->cfg.batch, w.K, w.N, st);
+}
+// h += delta; Cm = RMSNorm(h) w
+int norm_mm(ModelEngine *e, const float *delta, const float *wn, const QW &w, float *Cm, cudaStream_t st) {
+    const size_t B = e->cfg.batch, H = e->cfg.hidden;
+    int rc;
+    if (e->fused) {
+        rc = launch_pdl_smem("addnorm_terms_kernel", addnorm_terms_kernel, dim3((unsigned)B), dim3(1024),
+                             H * sizeof(float), st, e->h, delta, wn, (long long)H, e->cfg.rms_eps, kstages(H), e->terms,
+                             e->tscale);
+        return rc ? rc : terms_mm(e, w, Cm, st);
+    }
+    rc = launch_pdl("add_rmsnorm_kernel", add_rmsnorm_kernel, dim3((unsigned)B), dim3(1024), st, e->h, delta, wn, e->x,
+                    (long long)H, e->cfg.rms_eps);
+    return rc ? rc : mm(e->x, w, Cm, B, st);
+}
+// Cm = SwiGLU(gu) w
+int swiglu_mm(ModelEngine *e, const QW &w, float *Cm, cudaStream_t st) {
+    const size_t B = e->cfg.batch, I = e->I;
+    int rc;
+    if (e->fused) {
+        rc = launch_pdl_smem("swiglu_terms_kernel", swiglu_terms_kernel, dim3((unsigned)B), dim3(1024),
+                             I * sizeof(float), st, e->gu, (long long)I, kstages(I), e->terms, e->tscale);
+        return rc ? rc : terms_mm(e, w, Cm, st);
+    }
+    rc = launch_pdl("swiglu_kernel", swiglu_kernel, dim3(grid_for((long long)(B * I))), dim3(256), st, e->gu, e->act,
+                    (long long)I, (long long)(B * I));
+    return rc ? rc : mm(e->act, w, Cm, B, st);
+}
+// Cm = RMSNormGated(o, z) w   (GDN output side)
+int gatednorm_mm(ModelEngine *e, const float *wn, const QW &w, float *Cm, cudaStream_t st) {
+    const size_t B = e->cfg.batch, d = e->d;
+    int rc;
+    if (e->fused) {
+        rc = launch_pdl_smem("gatednorm_terms_kernel", gatednorm_terms_kernel, dim3((unsigned)B), dim3(1024),
+                             e->hv * d * sizeof(float), st, e->o, e->y, (long long)e->ny_gdn, (long long)e->C, wn,
+                             (int)e->hv, (int)d, e->cfg.rms_eps, kstages(e->hv * d), e->terms, e->tscale);
+        return rc ? rc : terms_mm(e, w, Cm, st);
+    }
+    rc = launch_pdl("gated_rmsnorm_kernel", gated_rmsnorm_kernel, dim3((unsigned)e->hv, (unsigned)B), dim3((unsigned)d), st,
+                    e->o, e->y, (long long)e->ny_gdn, (long long)e->C, wn, e->o2, (int)e->hv, (int)d, e->cfg.rms_eps);
+    return rc ? rc : mm(e->o2, w, Cm, B, st);
+}
+// Cm = (o * sigmoid(gate)) w   (attention output side)
+int attngate_mm(ModelEngine *e, const QW &w, float *Cm, cudaStream_t st) {
+    const size_t B = e->cfg.batch, n = e->hq * e->D;
+    int rc;
+    if (e->fused) {
+        rc = launch_pdl_smem("attngate_terms_kernel", attngate_terms_kernel, dim3((unsigned)B), dim3(1024),
+                             n * sizeof(float), st, e->o, e->gate, (long long)n, kstages(n), e->terms, e->tscale);
+        return rc ? rc : terms_mm(e, w, Cm, st);
+    }
+    rc = launch_pdl("attn_gate_kernel", attn_gate_kernel, dim3(grid_for((long long)(B * n))), dim3(256), st, e->o,
+                    e->gate, e->o2, (long long)(B * n));
+    return rc ? rc : mm(e->o2, w, Cm, B, st);
+}
 int allreduce(ModelEngine *e, float *buf, size_t n, cudaStream_t st) {
     if (e->cfg.tp_size <= 1) return KAI_GDN_OK;
     return check_nccl(e->nccl, e->nccl->allReduce(buf, buf, n, ncclFloat32, ncclSum, e->comm, st), "model: all-reduce");
 }
 
-// LM head over this rank's vocabulary and the greedy token of every
-// sequence from the final-normed rows x [B][H].
-int lm_head(ModelEngine *e, cudaStream_t st) {
+// The greedy token of every sequence from this rank's logits [B][V] (an
+// all-gather of the candidates across ranks).
+int select_tokens(ModelEngine *e, cudaStream_t st) {
     const kai_gdn_model_config &c = e->cfg;
     const size_t B = c.batch;
-    int rc = mm(e->x, e->lm, e->logits, B, st);
-    if (!rc)
-        rc = launch_pdl("argmax_kernel", argmax_kernel, dim3(dim3(AM_BLOCKS, (unsigned)B)), dim3(256), st, e->logits,
+    int rc = launch_pdl("argmax_kernel", argmax_kernel, dim3(dim3(AM_BLOCKS, (unsigned)B)), dim3(256), st, e->logits,
                         (long long)e->V, (long long)e->v0, e->cand);
     if (!rc && c.tp_size > 1)
         rc = check_nccl(e->nccl, e->nccl->allGather(e->cand, e->cand_all, B * AM_BLOCKS * 2, ncclFloat32, e->comm, st),
@@ -565,6 +744,12 @@ int lm_head(ModelEngine *e, cudaStream_t st) {
                         c.tp_size > 1 ? e->cand_all : e->cand, c.tp_size > 1 ? c.tp_size : 1, (int)B, AM_BLOCKS,
                         e->tok);
     return rc;
+}
+// LM head over this rank's vocabulary and the greedy tokens, from the
+// final-normed rows x [B][H].
+int lm_head(ModelEngine *e, cudaStream_t st) {
+    int rc = mm(e->x, e->lm, e->logits, e->cfg.batch, st);
+    return rc ? rc : select_tokens(e, st);
 }
 
 // Segment s of a token (see ModelEngine::seg).
@@ -585,33 +770,26 @@ int run_segment(ModelEngine *e, size_t s, cudaStream_t st) {
     } else {
         // the rest of attention layer l_begin: gate, o projection, FFN
         const ModelEngine::Layer &L = e->layers[l_begin];
-        M_TRY(launch_pdl("attn_gate_kernel", attn_gate_kernel, dim3(grid_for((long long)(B * e->hq * e->D))), dim3(256), st, e->o, e->gate, e->o2,
-                                                                                 (long long)(B * e->hq * e->D)));
-        M_TRY(mm(e->o2, L.wout, e->part, B, st));
+        M_TRY(attngate_mm(e, L.wout, e->part, st));
         M_TRY(allreduce(e, e->part, B * H, st));
-        M_TRY(launch_pdl("add_rmsnorm_kernel", add_rmsnorm_kernel, dim3((unsigned)B), dim3(1024), st, e->h, e->part, L.w_post, e->x, (long long)H, c.rms_eps));
-        M_TRY(mm(e->x, L.wgu, e->gu, B, st));
-        M_TRY(launch_pdl("swiglu_kernel", swiglu_kernel, dim3(grid_for((long long)(B * e->I))), dim3(256), st, e->gu, e->act, (long long)e->I,
-                                                                     (long long)(B * e->I)));
-        M_TRY(mm(e->act, L.wdown, e->part, B, st));
+        M_TRY(norm_mm(e, e->part, L.w_post, L.wgu, e->gu, st));
+        M_TRY(swiglu_mm(e, L.wdown, e->part, st));
         M_TRY(allreduce(e, e->part, B * H, st));
         pending = e->part;
     }
     const size_t first = s == 0 ? 0 : l_begin + 1;
     for (size_t l = first; l < l_end || (l == l_end && l < c.layers); ++l) {
         const ModelEngine::Layer &L = e->layers[l];
-        M_TRY(launch_pdl("add_rmsnorm_kernel", add_rmsnorm_kernel, dim3((unsigned)B), dim3(1024), st, e->h, pending, L.w_in, e->x, (long long)H, c.rms_eps));
+        M_TRY(norm_mm(e, pending, L.w_in, L.win, e->y, st));
         pending = nullptr;
         if (l == l_end) {
             // attention layer: projections and the prepared q / k / v; the
             // decode itself follows this segment
-            M_TRY(mm(e->x, L.win, e->y, B, st));
             M_TRY(launch_pdl("attn_prep_kernel", attn_prep_kernel, dim3(dim3((unsigned)(e->hq + 2 * e->hkv), (unsigned)B)), dim3((unsigned)e->D), st, e->y, (long long)e->ny_att, L.w_qn, L.w_kn, e->pos, e->q, e->gate, e->k, e->v, (int)e->hq,
                 (int)e->hkv, (int)e->D, (int)c.rope_dims, c.rope_theta, c.rms_eps));
             return KAI_GDN_OK;
         }
         // GDN layer
-        M_TRY(mm(e->x, L.win, e->y, B, st));
         M_TRY(launch_pdl("gdn_prep_kernel", gdn_prep_kernel, dim3(dim3((unsigned)(2 * e->hk + e->hv), (unsigned)B)), dim3((unsigned)e->d), st, e->y, (long long)e->ny_gdn, L.hist, L.conv_w, L.A_log, L.dt_bias, e->q, e->k, e->v, e->beta, e->g,
             (int)e->hk, (int)e->hv, (int)e->d));
         kai_gdn_decode_args da{};
@@ -632,20 +810,16 @@ int run_segment(ModelEngine *e, size_t s, cudaStream_t st) {
         da.state_dtype = KAI_GDN_F32;
         da.out_dtype = KAI_GDN_F32;
         M_TRY(launch_decode(&da, st));
-        M_TRY(launch_pdl("gated_rmsnorm_kernel", gated_rmsnorm_kernel, dim3(dim3((unsigned)e->hv, (unsigned)B)), dim3((unsigned)e->d), st, e->o, e->y, (long long)e->ny_gdn, (long long)e->C, L.w_gn, e->o2, (int)e->hv, (int)e->d, c.rms_eps));
-        M_TRY(mm(e->o2, L.wout, e->part, B, st));
+        M_TRY(gatednorm_mm(e, L.w_gn, L.wout, e->part, st));
         M_TRY(allreduce(e, e->part, B * H, st));
-        M_TRY(launch_pdl("add_rmsnorm_kernel", add_rmsnorm_kernel, dim3((unsigned)B), dim3(1024), st, e->h, e->part, L.w_post, e->x, (long long)H, c.rms_eps));
-        M_TRY(mm(e->x, L.wgu, e->gu, B, st));
-        M_TRY(launch_pdl("swiglu_kernel", swiglu_kernel, dim3(grid_for((long long)(B * e->I))), dim3(256), st, e->gu, e->act, (long long)e->I,
-                                                                     (long long)(B * e->I)));
-        M_TRY(mm(e->act, L.wdown, e->part, B, st));
+        M_TRY(norm_mm(e, e->part, L.w_post, L.wgu, e->gu, st));
+        M_TRY(swiglu_mm(e, L.wdown, e->part, st));
         M_TRY(allreduce(e, e->part, B * H, st));
         pending = e->part;
     }
     // end of the token: final norm, LM head over this rank's vocabulary, argmax
-    M_TRY(launch_pdl("add_rmsnorm_kernel", add_rmsnorm_kernel, dim3((unsigned)B), dim3(1024), st, e->h, pending, e->w_final, e->x, (long long)H, c.rms_eps));
-    M_TRY(lm_head(e, st));
+    M_TRY(norm_mm(e, pending, e->w_final, e->lm, e->logits, st));
+    M_TRY(select_tokens(e, st));
 #undef M_TRY
     return KAI_GDN_OK;
 }
@@ -1149,6 +1323,22 @@ int model_create(const kai_gdn_model_config *cfg, void **out) {
                 {&e->logits, B * e->V}};
     for (auto &bf : bufs)
         if (!rc) rc = malloc_keep(e, (void **)bf.p, bf.n * sizeof(float), true);
+    if (!rc && B > GEMV_MAX_BATCH) {
+        // fused producers need every projection packed and 16-multiple inputs
+        bool all = e->lm.qp != nullptr;
+        size_t kmax = H;
+        for (const ModelEngine::Layer &L : e->layers) {
+            for (const QW *w : {&L.win, &L.wout, &L.wgu, &L.wdown}) {
+                all = all && w->qp != nullptr && w->K % 16 == 0;
+                kmax = std::max(kmax, w->K);
+            }
+        }
+        if (all) {
+            rc = malloc_keep(e, (void **)&e->terms, int8_terms_bytes(B, kmax), true);
+            if (!rc) rc = malloc_keep(e, (void **)&e->tscale, B * sizeof(float), true);
+            e->fused = !rc;
+        }
+    }
     if (!rc) rc = malloc_keep(e, (void **)&e->tok, B * sizeof(int), true);
     if (!rc) rc = malloc_keep(e, (void **)&e->pos, sizeof(int), true);
     if (!rc) rc = malloc_keep(e, (void **)&e->cand, B * AM_BLOCKS * sizeof(ArgMax), true);

@@ -5,6 +5,7 @@
     python profile_cases.py conv | cumsum | scan | attn | int8 | int8m16 | lmhead | lmhead16 | ffn16 | model
     python profile_cases.py prefill [--launches 1]
     python profile_cases.py gemm4k
+    python profile_cases.py model16
 
 Each case holds a few hundred MB to a few GB on the device (inputs larger
 than the 126 MB L2, so DRAM counters mean something), runs a few launches of
@@ -30,6 +31,7 @@ its kernel through the C ABI, and exits.  Cases:
           (one prompt per launch, after a 256-token warm-up prefill)
   model   the config-4 engine (4B geometry, batch 1, synthetic 32k context):
           one greedy decode step per launch
+  model16 the same at batch 16
 """
 from __future__ import annotations
 
@@ -47,7 +49,7 @@ from orionsbelt_b200 import _lib, ops, synth  # noqa: E402
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("case", choices=["decode", "chunk", "conv", "cumsum", "scan", "attn", "int8", "int8m16", "lmhead",
-                                     "lmhead16", "ffn16", "model", "prefill", "gemm4k"])
+                                     "lmhead16", "ffn16", "model", "prefill", "gemm4k", "model16"])
     ap.add_argument("--launches", type=int, default=3)
     a = ap.parse_args()
     torch.cuda.set_device(0)
@@ -139,13 +141,14 @@ def main() -> None:
             eng.reset()
             with torch.cuda.stream(side):
                 eng.prefill(prompt, 0, side)
-    elif a.case == "model":
+    elif a.case in ("model", "model16"):
         import numpy as np
 
         import bench
-        eng = ops.ModelEngine(dict(bench.CFG4, max_ctx=32768 + 64), 1, seed=42)
+        nb = 16 if a.case == "model16" else 1
+        eng = ops.ModelEngine(dict(bench.CFG4, max_ctx=32768 + 64), nb, seed=42)
         eng.fill(32768, seed=3)
-        eng.set_tokens(np.zeros(1, np.int32))
+        eng.set_tokens(np.zeros(nb, np.int32))
         side = torch.cuda.Stream()
         step = [0]
 
