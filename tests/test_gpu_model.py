@@ -110,12 +110,12 @@ def test_model_prefill_matches_oracle(cuda, orc, B, split):
     eng.close()
 
 
-def _tp_rank(rank, nid, prompt, tokens, q):
+def _tp_rank(rank, nid, geom, prompt, tokens, q):
     try:
         import torch
 
         torch.cuda.set_device(rank)
-        eng = ops.ModelEngine(GEOM_TP, B, seed=11, tp_rank=rank, tp_size=2, nccl_id=nid)
+        eng = ops.ModelEngine(geom, B, seed=11, tp_rank=rank, tp_size=2, nccl_id=nid)
         stream = torch.cuda.Stream()
         out = []
         with torch.cuda.stream(stream):
@@ -133,8 +133,12 @@ def _tp_rank(rank, nid, prompt, tokens, q):
         q.put((rank, f"error: {exc!r}"))
 
 
-def test_model_tensor_parallel_two_gpus(cuda):
+@pytest.mark.parametrize("kv_heads", [2, 1])
+def test_model_tensor_parallel_two_gpus(cuda, kv_heads):
+    """kv_heads 1 < tp_size: every rank keeps a copy of the one kv head (the
+    path eight GPUs take with the config-4 model's four kv heads)."""
     torch = cuda
+    geom = dict(GEOM_TP, attn_kv_heads=kv_heads)
     if torch.cuda.device_count() < 2:
         pytest.skip("needs two GPUs")
     import torch.multiprocessing as mp
@@ -145,7 +149,7 @@ def test_model_tensor_parallel_two_gpus(cuda):
     nid = ops.ModelEngine.nccl_id()
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
-    procs = [ctx.Process(target=_tp_rank, args=(r, nid, prompt, tokens, q)) for r in (0, 1)]
+    procs = [ctx.Process(target=_tp_rank, args=(r, nid, geom, prompt, tokens, q)) for r in (0, 1)]
     for p in procs:
         p.start()
     try:
@@ -157,7 +161,7 @@ def test_model_tensor_parallel_two_gpus(cuda):
                 p.kill()
     for r in (0, 1):
         assert not isinstance(res[r], str), res[r]
-    eng = ops.ModelEngine(GEOM_TP, B, seed=11)
+    eng = ops.ModelEngine(geom, B, seed=11)
     stream = torch.cuda.Stream()
     with torch.cuda.stream(stream):
         eng.prefill(prompt, 0, stream)
