@@ -15,10 +15,11 @@
 //   O^T += V^T Ps^T   M = 128 head dims (D / 128 MMAs), N = 128 (two bf16
 //                     terms of each softmax weight), K = 64 tokens.
 // O^T accumulates in TMEM across the tiles.  The softmax keeps, per query
-// row, a reference maximum m: weights are e^(s - m) and only when a tile's
-// maximum exceeds m by more than e^8 (weights stay below 2981, exact enough
-// in two bf16 terms) is m raised and O^T and the row sums rescaled in place
-// -- a handful of times per row, at the first tiles.
+// row, a reference maximum m: weights are e^(s - m) and only when a score
+// exceeds m by more than e^8 (weights stay below 2981, exact enough in two
+// bf16 terms) are the tile's maxima reduced, m raised and O^T and the row
+// sums rescaled in place -- a handful of times per row, at the first tiles;
+// other tiles check their scores against m and need no reduction at all.
 //
 // Warp 8 issues the loads (TMA, 128-byte swizzle, two stages) and the MMAs;
 // warps 0-7 run the softmax (warp w: the tokens of TMEM lanes 32 (w % 4) ..
@@ -102,7 +103,7 @@ __global__ void __launch_bounds__(PF_AT, 1)
     __shared__ uint64_t full[NST], bar_s[2], bar_o[2], pready[2];
     __shared__ uint32_t tmem_slot;
     __shared__ float s_red[4][PF_QR];   // tile maxima / row sums per lane quarter
-    __shared__ float s_m[2][PF_QR];     // reference maxima (double-buffered by tile parity)
+    __shared__ float s_m[PF_QR];        // reference maxima of the rows
     __shared__ float s_a[PF_QR];        // rescale factors of the current tile
 
     const int t = threadIdx.x, lane = t % 32, w = t / 32;
@@ -128,7 +129,7 @@ __global__ void __launch_bounds__(PF_AT, 1)
             }
             *reinterpret_cast<uint32_t *>(qop + kmaj16(n, k, D)) = pf_bf16x2(v0, v1);
         }
-        if (t < PF_QR) s_m[0][t] = -INFINITY;
+        if (t < PF_QR) s_m[t] = -INFINITY;
         fence_smem_to_async();
     } else {
         if (lane == 0) {
@@ -225,14 +226,19 @@ __global__ void __launch_bounds__(PF_AT, 1)
         const bool key_lane = lane < 16;
         const float sl2 = p.scale * 1.4426950408889634f;  // scores in log2 units
         const float margin = PF_RESCALE * 1.4426950408889634f;
-        float l_part[32];
+        float l_part[32], mref[32];  // row sums of this thread's token, reference maxima of its rows
 #pragma unroll
-        for (int i = 0; i < 32; ++i) l_part[i] = 0.f;
+        for (int i = 0; i < 32; ++i) {
+            l_part[i] = 0.f;
+            mref[i] = -INFINITY;
+        }
         for (int j = 0; j < ntile; ++j) {
             if (!mbar_wait(&bar_s[j & 1], (j >> 1) & 1, err)) bad = true;
             fence_after_sync();
             bad = __any_sync(0xffffffffu, bad);
             float sc[32];
+#pragma unroll
+            for (int i = 0; i < 32; ++i) sc[i] = -INFINITY;
             if (!bad) {
                 float hv[32], lv[32];
                 const uint32_t c0 = Gm::S_COL + (j & 1) * NQ + 32 * qh;
@@ -253,7 +259,20 @@ __global__ void __launch_bounds__(PF_AT, 1)
                     const bool valid = key_lane && key <= qpos && p0 + r / G < p.T;
                     sc[i] = valid ? (hv[i] + lv[i]) * sl2 : -INFINITY;
                 }
-                // tile maximum of each row over this warp's 16 tokens
+            }
+            // Fast path: no score above its row's reference maximum plus the
+            // margin (weights stay below e^8) -- nothing to reduce.  Otherwise
+            // (and on the first tile) the tile maxima are reduced and the rows
+            // that need it raised, with O^T and the row sums rescaled.
+            bool over = false;
+#pragma unroll
+            for (int i = 0; i < 32; ++i) over = over || sc[i] > mref[i] + margin;
+            bool resc = false;
+            if (pf_sync_or(bad || over)) {
+                if (pf_sync_or(bad)) {
+                    bad = true;
+                    break;
+                }
 #pragma unroll
                 for (int i = 0; i < 32; ++i) {
                     float mx = sc[i];
@@ -261,27 +280,23 @@ __global__ void __launch_bounds__(PF_AT, 1)
                     for (int mask = 8; mask >= 1; mask >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, mask));
                     if (lane == 0) s_red[q4][32 * qh + i] = mx;
                 }
-            }
-            if (pf_sync_or(bad)) {
-                bad = true;
-                break;
-            }
-            // reference maxima: raised past the margin (first tile: set)
-            bool resc = false;
-            if (t < PF_QR) {
-                float mt = fmaxf(fmaxf(s_red[0][t], s_red[1][t]), fmaxf(s_red[2][t], s_red[3][t]));
-                if (mt == -INFINITY) mt = 0.f;  // a row past the prompt's end: no token, weights 0
-                const float mo = s_m[j & 1][t];
-                float mn = mo, a = 1.f;
-                if (mt > mo + margin || mo == -INFINITY) {
-                    mn = mt;
-                    a = exp2f(mo - mt);
-                    resc = j > 0;
+                pf_sync_or(false);
+                if (t < PF_QR) {
+                    float mt = fmaxf(fmaxf(s_red[0][t], s_red[1][t]), fmaxf(s_red[2][t], s_red[3][t]));
+                    if (mt == -INFINITY) mt = 0.f;  // a row past the prompt's end: no token, weights 0
+                    const float mo = s_m[t];
+                    float a = 1.f;
+                    if (mt > mo + margin || mo == -INFINITY) {
+                        s_m[t] = mt;
+                        a = exp2f(mo - mt);
+                        resc = j > 0;
+                    }
+                    s_a[t] = a;
                 }
-                s_m[(j + 1) & 1][t] = mn;
-                s_a[t] = a;
+                resc = pf_sync_or(resc);
+#pragma unroll
+                for (int i = 0; i < 32; ++i) mref[i] = s_m[32 * qh + i];
             }
-            resc = pf_sync_or(resc);
             if (resc) {
                 // O(j-1) must be complete before O^T is rescaled in TMEM
                 if (!mbar_wait(&bar_o[(j - 1) & 1], ((j - 1) >> 1) & 1, err)) bad = true;
@@ -311,7 +326,7 @@ __global__ void __launch_bounds__(PF_AT, 1)
 #pragma unroll
                 for (int i = 0; i < 32; ++i) {
                     const int r = 32 * qh + i;
-                    const float e = exp2f(sc[i] - s_m[(j + 1) & 1][r]);  // 0 for masked tokens
+                    const float e = exp2f(sc[i] - mref[i]);  // 0 for masked tokens
                     l_part[i] += e;
                     const __nv_bfloat16 hi = __float2bfloat16_rn(e);
                     *reinterpret_cast<T *>(pb + kmaj16(r, key_in_tile, TT)) = hi;
