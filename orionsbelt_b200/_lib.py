@@ -164,13 +164,18 @@ def last_error() -> str:
 
 
 def check(status: int) -> None:
-    """Raise GdnError for a non-zero status from a device entry point."""
+    """Raise GdnError for a non-zero status from a device entry point (and
+    clear the thread's recorded failure, which the error now carries)."""
     if status != OK:
-        raise GdnError(status, last_error())
+        msg = last_error()
+        lib().kai_gdn_cuda_clear_error()
+        raise GdnError(status, msg)
 
 
 def check_dropin() -> None:
-    """Raise if the last drop-in (void) call on this thread recorded a failure."""
+    """Raise if the drop-in (void) call just made on this thread recorded a
+    failure (callers clear the record before the call: it keeps the last
+    failure, not the last call's outcome)."""
     L = lib()
     st = L.kai_gdn_cuda_last_status()
     if st != OK:

@@ -34,24 +34,28 @@ def _host(a: np.ndarray, dtype=np.float32) -> int:
 
 def kai_run_gdn_cumdecay_f32_sve(a: np.ndarray, decay: np.ndarray) -> None:
     seq, ch = a.shape
+    lib().kai_gdn_cuda_clear_error()  # a failure recorded earlier is not this call's
     lib().kai_run_gdn_cumdecay_f32_sve(_host(a), _host(decay), seq, ch)
     check_dropin()
 
 
 def kai_run_gdn_gated_scan_f32_sve(g, x, s, state) -> None:
     seq, ch = x.shape
+    lib().kai_gdn_cuda_clear_error()  # a failure recorded earlier is not this call's
     lib().kai_run_gdn_gated_scan_f32_sve(_host(g), _host(x), _host(s), _host(state), seq, ch)
     check_dropin()
 
 
 def kai_run_gdn_causal_dwconv1d_f32_k4_sve(x, w, out, hist) -> None:
     seq, ch = x.shape
+    lib().kai_gdn_cuda_clear_error()  # a failure recorded earlier is not this call's
     lib().kai_run_gdn_causal_dwconv1d_f32_k4_sve(_host(x), _host(w), _host(out), _host(hist), seq, ch)
     check_dropin()
 
 
 def kai_run_gdn_gemv_f32_f32_f32_1x4_neon(a, b, c) -> None:
     k, n = b.shape
+    lib().kai_gdn_cuda_clear_error()  # a failure recorded earlier is not this call's
     lib().kai_run_gdn_gemv_f32_f32_f32_1x4_neon(_host(a), _host(b), _host(c), k, n)
     check_dropin()
 
@@ -59,24 +63,28 @@ def kai_run_gdn_gemv_f32_f32_f32_1x4_neon(a, b, c) -> None:
 def gdn_delta_rule_matmul(A, B, Cm) -> None:
     M, K = A.shape
     N = B.shape[1]
+    lib().kai_gdn_cuda_clear_error()  # a failure recorded earlier is not this call's
     lib().gdn_delta_rule_matmul(_host(A), _host(B), _host(Cm), M, K, N)
     check_dropin()
 
 
 def gdn_cumdecay_narrow(a, decay_u16, kind: str) -> None:
     seq, ch = a.shape
+    lib().kai_gdn_cuda_clear_error()  # a failure recorded earlier is not this call's
     getattr(lib(), "gdn_cumdecay_" + kind)(_host(a), _host(decay_u16, np.uint16), seq, ch)
     check_dropin()
 
 
 def gdn_gated_scan_narrow(g, x, s, state_u16, kind: str) -> None:
     seq, ch = x.shape
+    lib().kai_gdn_cuda_clear_error()  # a failure recorded earlier is not this call's
     getattr(lib(), "gdn_gated_scan_" + kind)(_host(g), _host(x), _host(s), _host(state_u16, np.uint16), seq, ch)
     check_dropin()
 
 
 def gdn2_gated_scan_f32(g, b_gate, w_gate, x, s, state) -> None:
     seq, ch = x.shape
+    lib().kai_gdn_cuda_clear_error()  # a failure recorded earlier is not this call's
     lib().gdn2_gated_scan_f32(_host(g), _host(b_gate), _host(w_gate), _host(x), _host(s), _host(state), seq, ch)
     check_dropin()
 
