@@ -67,27 +67,91 @@ def load_peaks() -> dict:
 
 
 class ClockSampler:
-    """nvidia-smi clocks and throttle reasons sampled during the timed region."""
+    """SM clocks and throttle reasons sampled during the timed region.
+
+    A thread polls NVML (read-only queries) every 2 ms, so a timed region of a
+    few milliseconds still holds several samples; it is started, and has taken
+    its first sample, before the region begins.  Without NVML the recipe's
+    `nvidia-smi -lms 200` line is used instead (which a region this short may
+    fall between)."""
 
     Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
          "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
          "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    NAMES = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
 
     def __init__(self, index: int):
         self.index = index
         self.proc = None
+        self.thread = None
+        self.samples = []  # (sm MHz, max MHz, set of reason names)
+        self.source = None
+
+    def _nvml_handle(self, nv):
+        import torch
+
+        props = torch.cuda.get_device_properties(self.index)
+        try:
+            return nv.nvmlDeviceGetHandleByUUID("GPU-" + str(props.uuid))
+        except Exception:
+            pass
+        try:
+            bus = f"{props.pci_domain_id:08x}:{props.pci_bus_id:02x}:{props.pci_device_id:02x}.0"
+            return nv.nvmlDeviceGetHandleByPciBusId(bus)
+        except Exception:
+            return nv.nvmlDeviceGetHandleByIndex(self.index)
+
+    def _start_nvml(self) -> bool:
+        import threading
+
+        try:
+            import pynvml as nv
+
+            nv.nvmlInit()
+            h = self._nvml_handle(nv)
+            mx = float(nv.nvmlDeviceGetMaxClockInfo(h, nv.NVML_CLOCK_SM))
+        except Exception:
+            return False
+        bits = [nv.nvmlClocksEventReasonHwSlowdown, nv.nvmlClocksEventReasonHwThermalSlowdown,
+                nv.nvmlClocksEventReasonSwThermalSlowdown, nv.nvmlClocksEventReasonSwPowerCap]
+        self.stop = threading.Event()
+        first = threading.Event()
+
+        def poll():
+            while True:
+                try:
+                    sm = float(nv.nvmlDeviceGetClockInfo(h, nv.NVML_CLOCK_SM))
+                    r = nv.nvmlDeviceGetCurrentClocksEventReasons(h)
+                    self.samples.append((sm, mx, {n for n, b in zip(self.NAMES, bits) if r & b}))
+                except Exception:
+                    pass
+                first.set()
+                if self.stop.wait(0.002):
+                    break
+
+        self.thread = threading.Thread(target=poll, daemon=True)
+        self.thread.start()
+        first.wait(2.0)
+        self.source = "nvml, 2 ms"
+        return True
 
     def __enter__(self):
+        if self._start_nvml():
+            return self
         try:
             self.proc = subprocess.Popen(["nvidia-smi", "-i", str(self.index), f"--query-gpu={self.Q}",
                                           "--format=csv,noheader,nounits", "-lms", "200"],
                                          stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.source = "nvidia-smi, 200 ms"
         except OSError:
             self.proc = None
         return self
 
     def __exit__(self, *a):
-        self.lines = []
+        if self.thread is not None:
+            self.stop.set()
+            self.thread.join(timeout=5)
+            return
         if self.proc is not None:
             time.sleep(0.25)
             self.proc.terminate()
@@ -96,25 +160,22 @@ class ClockSampler:
             except subprocess.TimeoutExpired:
                 self.proc.kill()
                 out, _ = self.proc.communicate()
-            self.lines = [ln for ln in out.splitlines() if ln.strip()]
+            for ln in out.splitlines():
+                f = [x.strip() for x in ln.split(",")]
+                if len(f) < 9:
+                    continue
+                try:
+                    sm, mx = float(f[1]), float(f[2])
+                except ValueError:
+                    continue
+                self.samples.append((sm, mx, {n for n, v in zip(self.NAMES, f[5:9]) if v.lower() == "active"}))
 
     def summary(self) -> dict:
-        sm, mx, reasons = [], None, set()
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for ln in getattr(self, "lines", []):
-            f = [x.strip() for x in ln.split(",")]
-            if len(f) < 9:
-                continue
-            try:
-                sm.append(float(f[1]))
-                mx = float(f[2])
-            except ValueError:
-                continue
-            for n, v in zip(names, f[5:9]):
-                if v.lower() == "active":
-                    reasons.add(n)
-        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx, "reasons": sorted(reasons),
-                "samples": len(sm)}
+        sm = [x[0] for x in self.samples]
+        reasons = set().union(*[x[2] for x in self.samples]) if self.samples else set()
+        return {"sm_mhz": statistics.median(sm) if sm else None,
+                "sm_max_mhz": self.samples[-1][1] if self.samples else None, "reasons": sorted(reasons),
+                "samples": len(sm), "source": self.source}
 
 
 def dist_setup(n_gpus: int):
