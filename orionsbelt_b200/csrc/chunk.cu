@@ -529,9 +529,12 @@ int launch_chunk(const kai_gdn_chunk_args *a, cudaStream_t st) {
         return set_error(KAI_GDN_ERR_INVALID, "chunk: bad dtype");
     if (a->chunk != (size_t)CH)
         return set_error(KAI_GDN_ERR_UNSUPPORTED, "chunk: chunk length %zu (supported: 64)", a->chunk);
-    // bf16 / fp16 inputs at the model's head size run on the tensor cores;
-    // fp32 inputs (and other head sizes) take the fp32 CUDA-core kernel.
+    // At the model's head size both input precisions run on the tensor
+    // cores (bf16 / fp16 inputs in one warp-specialised kernel, fp32 inputs
+    // fp32-accurate in two launches); other head sizes take the fp32
+    // CUDA-core kernel.
     if (chunk_ws_supported(a)) return launch_chunk_ws(a, st);
+    if (chunk_tc32_supported(a)) return launch_chunk_tc32(a, st);
     return launch_chunk_fp32(a, st);
 }
 

@@ -1,0 +1,688 @@
+// chunk_tc32.cu -- the chunkwise gated delta-rule scan for fp32 inputs on the
+// tensor cores (sm_100a), fp32-accurate.
+//
+// Same algorithm and conventions as chunk.cu (the chunked form of
+// docs/GDN_ARCHITECTURE_AUDIT.md:142-153).  Per (b, value head) and chunk of
+// 64 tokens, G the in-chunk cumulative log decay:
+//   A  = beta_r (k_r . k_s) e^{G_r - G_s}          s <  r
+//   P  = scale (q_r . k_s) e^{G_r - G_s}           s <= r
+//   Tb = (I + A)^-1 diag(beta),   R = P Tb
+//   V'' = V - e^G (K S),   V' = Tb V'',   O = scale e^G (Q S) + R V''  (= P V')
+//   S  <- e^{G_63} S + K^T (e^{G_63 - G} V')
+//
+// Precision: every product runs as three bf16 MMAs, hi*hi + hi*lo + lo*hi,
+// with each operand split x = hi + lo (hi = bf16(x), lo = bf16(x - hi)), so
+// a product carries about 16 significant bits and lo*lo (2^-18 relative) is
+// the dropped term; sums accumulate in fp32 in TMEM, the state stays fp32 in
+// TMEM for the whole sequence.
+//
+// Two launches per segment of chunks:
+//  * chunk_prep_kernel -- one CTA per (b, key head, chunk), all chunks at
+//    once (nothing here depends on the state): K K^T and Q K^T, then for each
+//    value head of the group A and P, the inverse by substitution, Tb and
+//    R = P Tb, all in fp32 on the CUDA cores.  It writes the MMA operand
+//    images into a workspace, exactly as the recurrence's shared memory holds
+//    them (no-swizzle K-major core-matrix layout, bf16 hi then lo):
+//      [K;Q]   128 rows (64 of k, 64 of q) x 128 features      65536 bytes
+//      [Tb;R]  128 rows (64 of Tb, 64 of R) x 64 tokens + G    33024 bytes
+//  * chunk_rec_kernel -- one CTA per (b, value head, 32 value columns).  The
+//    value columns of the state evolve independently (V' = Tb V'' and the
+//    update are column-wise), so the 32-column blocks are exact splits; the
+//    state block S (128 keys x 32 values, fp32) lives in TMEM.  Per chunk,
+//    three MMA batches (M = 128, N = 32) on one warp:
+//      D_a  = [K;Q] S      K = 128   rows 0-63: K S, rows 64-127: Q S
+//      D_b  = [Tb;R] V''   K = 64    rows 0-63: V',  rows 64-127: R V''
+//      S   += K^T V'_s     K = 64    A = the K half of [K;Q] read MN-major
+//    and between them element-wise passes on four warps (TMEM lane quarters):
+//    V'' and its split (rows 0-63), V'_s = e^{G_63-G} V' and its split, the
+//    output rows (64-127), and the state pass (all 128 lanes: the split
+//    copy of S for the next D_a, then S *= e^{G_63} of the next chunk, back
+//    into TMEM).  One warp issues the bulk copies of the next chunks' images
+//    into a two-deep ring.
+//
+// Long sequences run in segments of chunks whose images fit a bounded
+// workspace; the state goes through the state buffer between segments.
+#include "gdn_internal.cuh"
+#include "umma.cuh"
+
+namespace gdn {
+namespace {
+
+using namespace umma;
+
+constexpr int CH = 64;                       // chunk length
+constexpr int DK = 128;                      // key features
+constexpr int NV = 32;                       // value columns per recurrence CTA
+constexpr int KQ_HALF = 128 * DK * 2;        // one bf16 [K;Q] image
+constexpr int KQ_BYTES = 2 * KQ_HALF;        // hi + lo
+constexpr int TR_HALF = 128 * CH * 2;        // one bf16 [Tb;R] image
+constexpr int TR_BYTES = 2 * TR_HALF + CH * 4;  // hi + lo + G
+constexpr size_t SEG_BUDGET = 256ull << 20;  // workspace bound per launch
+
+// ---------------------------------------------------------------- helpers
+__device__ __forceinline__ uint32_t bf2_bits(__nv_bfloat162 v) { return *reinterpret_cast<uint32_t *>(&v); }
+
+// Eight floats to their bf16 hi and lo parts, packed (lower index in the low half).
+__device__ __forceinline__ void split8(const float *x, uint4 &hi, uint4 &lo) {
+    uint32_t h[4], l[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        const __nv_bfloat162 hh = __floats2bfloat162_rn(x[2 * i], x[2 * i + 1]);
+        const float2 hf = __bfloat1622float2(hh);
+        h[i] = bf2_bits(hh);
+        l[i] = bf2_bits(__floats2bfloat162_rn(x[2 * i] - hf.x, x[2 * i + 1] - hf.y));
+    }
+    hi = make_uint4(h[0], h[1], h[2], h[3]);
+    lo = make_uint4(l[0], l[1], l[2], l[3]);
+}
+
+// Row `k` (32 values along N) of an MN-major 16-bit operand with NV columns,
+// hi image at `hi`, lo image at `lo`.
+__device__ __forceinline__ void put_row_mn(unsigned char *hi, unsigned char *lo, int k, const float (&x)[NV]) {
+#pragma unroll
+    for (int j = 0; j < NV / 8; ++j) {
+        uint4 h, l;
+        split8(&x[8 * j], h, l);
+        const uint32_t off = mnmaj16(k, 8 * j, NV);
+        *reinterpret_cast<uint4 *>(hi + off) = h;
+        *reinterpret_cast<uint4 *>(lo + off) = l;
+    }
+}
+
+__device__ __forceinline__ void mbar_arrive1(uint64_t *bar) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_addr(bar)) : "memory");
+}
+
+// A bounded wait whose outcome is the same for the whole warp (the
+// tcgen05.ld / st that follow are warp-collective).
+__device__ __forceinline__ bool wait_w(uint64_t *bar, uint32_t phase, int *err) {
+    return __all_sync(0xffffffffu, mbar_wait(bar, phase, err));
+}
+
+__device__ __forceinline__ void ld32(uint32_t taddr, float (&v)[NV]) {
+    tmem_ld16(taddr, *reinterpret_cast<float(*)[16]>(&v[0]));
+    tmem_ld16(taddr + 16, *reinterpret_cast<float(*)[16]>(&v[16]));
+    tmem_wait_ld();
+    reg_fence16(&v[0]);
+    reg_fence16(&v[16]);
+}
+__device__ __forceinline__ void st32(uint32_t taddr, const float (&v)[NV]) {
+    tmem_st16(taddr, *reinterpret_cast<const float(*)[16]>(&v[0]));
+    tmem_st16(taddr + 16, *reinterpret_cast<const float(*)[16]>(&v[16]));
+    tmem_wait_st();
+}
+
+// 32 consecutive values of a row in dtype `dt` (16-byte aligned).
+__device__ __forceinline__ void store32(void *base, size_t idx, int dt, const float (&x)[NV]) {
+    if (dt == KAI_GDN_F32) {
+        float4 *p = reinterpret_cast<float4 *>(static_cast<float *>(base) + idx);
+#pragma unroll
+        for (int j = 0; j < NV / 4; ++j) p[j] = make_float4(x[4 * j], x[4 * j + 1], x[4 * j + 2], x[4 * j + 3]);
+        return;
+    }
+    uint4 *p = reinterpret_cast<uint4 *>(static_cast<uint16_t *>(base) + idx);
+#pragma unroll
+    for (int j = 0; j < NV / 8; ++j) {
+        uint32_t w[4];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            const float a = x[8 * j + 2 * i], b = x[8 * j + 2 * i + 1];
+            if (dt == KAI_GDN_BF16) {
+                w[i] = bf2_bits(__floats2bfloat162_rn(a, b));
+            } else {
+                const __half2 hv = __floats2half2_rn(a, b);
+                w[i] = *reinterpret_cast<const uint32_t *>(&hv);
+            }
+        }
+        p[j] = make_uint4(w[0], w[1], w[2], w[3]);
+    }
+}
+
+// ================================================================ prep
+constexpr int PT = 256;   // threads
+constexpr int LDT = 132;  // K / Q tile row stride (floats)
+constexpr int LDP = 65;   // 64 x 64 work matrices
+
+struct PrepSmem {
+    union {
+        struct {
+            float K[CH * LDT];
+            float Q[CH * LDT];
+        } in;
+        struct {
+            float A[CH * LDP];
+            float P[CH * LDP];
+            float T[CH * LDP];  // Tb once the substitution is done
+            float R[CH * LDP];
+        } w;
+    } u;
+    float KK[CH * LDP];
+    float QK[CH * LDP];
+    float G[CH];
+    float beta[CH];
+};
+
+__global__ void __launch_bounds__(PT, 2)
+    chunk_prep_kernel(const kai_gdn_chunk_args p, unsigned char *ws_kq, unsigned char *ws_tr, long long c_begin,
+                      int nc) {
+    extern __shared__ __align__(16) unsigned char smem_raw[];
+    PrepSmem &sm = *reinterpret_cast<PrepSmem *>(smem_raw);
+    const int t = threadIdx.x, tx = t % 16, ty = t / 16;
+    const long long Hk = (long long)p.heads_k, Hv = (long long)p.heads_v, T = (long long)p.seq;
+    const int grp = (int)(Hv / Hk);
+    const long long cl = blockIdx.x % nc, bh = blockIdx.x / nc;  // bh = b * Hk + hk
+    const long long b = bh / Hk, hk = bh % Hk;
+    const long long c0 = (c_begin + cl) * CH;
+
+    // ---- k, q tiles (rows past T are zeros)
+    {
+        const float *kg = static_cast<const float *>(p.k), *qg = static_cast<const float *>(p.q);
+        float4 kv[8], qv[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+            const int e = t + PT * i, r = e / 32, c4 = e % 32;
+            const long long tok = c0 + r;
+            kv[i] = qv[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+            if (tok < T) {
+                const size_t off = ((size_t)(b * T + tok) * Hk + hk) * DK + 4 * c4;
+                kv[i] = __ldg(reinterpret_cast<const float4 *>(kg + off));
+                qv[i] = __ldg(reinterpret_cast<const float4 *>(qg + off));
+            }
+        }
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+            const int e = t + PT * i, r = e / 32, c4 = e % 32;
+            *reinterpret_cast<float4 *>(&sm.u.in.K[r * LDT + 4 * c4]) = kv[i];
+            *reinterpret_cast<float4 *>(&sm.u.in.Q[r * LDT + 4 * c4]) = qv[i];
+        }
+    }
+    __syncthreads();
+
+    // ---- the [K;Q] image: unit u covers 8 features of one row; with
+    // u = ((row / 8) * 16 + feature group) * 8 + row % 8 its K-major offset
+    // is u * 16, so the warp's stores are contiguous.
+    {
+        unsigned char *kq = ws_kq + (size_t)(bh * nc + cl) * KQ_BYTES;
+        for (int u = t; u < 128 * (DK / 8); u += PT) {
+            const int r8 = u % 8, g = (u / 8) % (DK / 8), row = (u / 128) * 8 + r8;
+            const float *src = row < CH ? &sm.u.in.K[row * LDT + 8 * g] : &sm.u.in.Q[(row - CH) * LDT + 8 * g];
+            float x[8];
+            *reinterpret_cast<float4 *>(&x[0]) = *reinterpret_cast<const float4 *>(src);
+            *reinterpret_cast<float4 *>(&x[4]) = *reinterpret_cast<const float4 *>(src + 4);
+            uint4 h, l;
+            split8(x, h, l);
+            *reinterpret_cast<uint4 *>(kq + (size_t)u * 16) = h;
+            *reinterpret_cast<uint4 *>(kq + KQ_HALF + (size_t)u * 16) = l;
+        }
+    }
+
+    // ---- K K^T and Q K^T (fp32; rows ty + 16 i, columns tx + 16 j)
+    {
+        float kk[4][4], qk[4][4];
+#pragma unroll
+        for (int i = 0; i < 4; ++i)
+#pragma unroll
+            for (int j = 0; j < 4; ++j) kk[i][j] = qk[i][j] = 0.f;
+#pragma unroll 2
+        for (int d = 0; d < DK; d += 4) {
+            float4 kr[4], qr[4], ks[4];
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                kr[i] = *reinterpret_cast<const float4 *>(&sm.u.in.K[(ty + 16 * i) * LDT + d]);
+                qr[i] = *reinterpret_cast<const float4 *>(&sm.u.in.Q[(ty + 16 * i) * LDT + d]);
+                ks[i] = *reinterpret_cast<const float4 *>(&sm.u.in.K[(tx + 16 * i) * LDT + d]);
+            }
+#pragma unroll
+            for (int i = 0; i < 4; ++i)
+#pragma unroll
+                for (int j = 0; j < 4; ++j) {
+                    kk[i][j] = fmaf(kr[i].x, ks[j].x, kk[i][j]);
+                    kk[i][j] = fmaf(kr[i].y, ks[j].y, kk[i][j]);
+                    kk[i][j] = fmaf(kr[i].z, ks[j].z, kk[i][j]);
+                    kk[i][j] = fmaf(kr[i].w, ks[j].w, kk[i][j]);
+                    qk[i][j] = fmaf(qr[i].x, ks[j].x, qk[i][j]);
+                    qk[i][j] = fmaf(qr[i].y, ks[j].y, qk[i][j]);
+                    qk[i][j] = fmaf(qr[i].z, ks[j].z, qk[i][j]);
+                    qk[i][j] = fmaf(qr[i].w, ks[j].w, qk[i][j]);
+                }
+        }
+#pragma unroll
+        for (int i = 0; i < 4; ++i)
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                sm.KK[(ty + 16 * i) * LDP + tx + 16 * j] = kk[i][j];
+                sm.QK[(ty + 16 * i) * LDP + tx + 16 * j] = qk[i][j];
+            }
+    }
+    __syncthreads();  // the k, q tiles are dead from here (union)
+
+    float *const A = sm.u.w.A, *const Pm = sm.u.w.P, *const Tm = sm.u.w.T, *const R = sm.u.w.R;
+    for (int gi = 0; gi < grp; ++gi) {
+        const long long h = hk * grp + gi;
+        if (t < 32) {
+            // in-chunk inclusive cumsum of g, two rows per lane; beta
+            const long long r0 = c0 + 2 * t, r1 = r0 + 1;
+            const float g0 = r0 < T ? p.g[(size_t)(b * T + r0) * Hv + h] : 0.f;
+            const float g1 = r1 < T ? p.g[(size_t)(b * T + r1) * Hv + h] : 0.f;
+            const float b0 = r0 < T ? p.beta[(size_t)(b * T + r0) * Hv + h] : 0.f;
+            const float b1 = r1 < T ? p.beta[(size_t)(b * T + r1) * Hv + h] : 0.f;
+            const float pair = g0 + g1;
+            float incl = pair;
+#pragma unroll
+            for (int o = 1; o < 32; o <<= 1) {
+                const float u = __shfl_up_sync(0xffffffffu, incl, o);
+                if (t >= o) incl += u;
+            }
+            sm.G[2 * t] = incl - pair + g0;
+            sm.G[2 * t + 1] = incl;
+            sm.beta[2 * t] = b0;
+            sm.beta[2 * t + 1] = b1;
+        }
+        __syncthreads();
+        // ---- A (s < r) and P (s <= r)
+        for (int e = t; e < CH * CH; e += PT) {
+            const int r = e / CH, s = e % CH;
+            const float dec = r >= s ? expf(sm.G[r] - sm.G[s]) : 0.f;
+            A[r * LDP + s] = r > s ? sm.beta[r] * sm.KK[r * LDP + s] * dec : 0.f;
+            Pm[r * LDP + s] = p.scale * sm.QK[r * LDP + s] * dec;
+        }
+        __syncthreads();
+        // ---- T = (I + A)^-1 by right-looking substitution on the identity,
+        // four lanes per column n (rows j + 4 m on lane j); x_r is final when
+        // step r starts and reaches the group by a shuffle.  Tb = T diag(beta).
+        {
+            const int n = t / 4, j = t % 4, lane = t % 32;
+            float x[16];
+#pragma unroll
+            for (int m = 0; m < 16; ++m) x[m] = (j + 4 * m == n) ? 1.f : 0.f;
+#pragma unroll 1
+            for (int r = 0; r < CH - 1; ++r) {
+                const int owner = r % 4, mr = r / 4;
+                float xr = 0.f;
+#pragma unroll
+                for (int m = 0; m < 16; ++m)
+                    if (m == mr) xr = x[m];
+                xr = __shfl_sync(0xffffffffu, xr, lane - j + owner);
+#pragma unroll
+                for (int m = 0; m < 16; ++m) {
+                    const int i = j + 4 * m;
+                    if (i > r) x[m] = fmaf(-A[i * LDP + r], xr, x[m]);
+                }
+            }
+            const float bn = sm.beta[n];
+#pragma unroll
+            for (int m = 0; m < 16; ++m) Tm[(j + 4 * m) * LDP + n] = x[m] * bn;
+        }
+        __syncthreads();
+        // ---- R = P Tb
+        {
+            float acc[4][4];
+#pragma unroll
+            for (int i = 0; i < 4; ++i)
+#pragma unroll
+                for (int q = 0; q < 4; ++q) acc[i][q] = 0.f;
+#pragma unroll 4
+            for (int jj = 0; jj < CH; ++jj) {
+                float pr[4], tb[4];
+#pragma unroll
+                for (int i = 0; i < 4; ++i) pr[i] = Pm[(ty + 16 * i) * LDP + jj];
+#pragma unroll
+                for (int q = 0; q < 4; ++q) tb[q] = Tm[jj * LDP + tx + 16 * q];
+#pragma unroll
+                for (int i = 0; i < 4; ++i)
+#pragma unroll
+                    for (int q = 0; q < 4; ++q) acc[i][q] = fmaf(pr[i], tb[q], acc[i][q]);
+            }
+#pragma unroll
+            for (int i = 0; i < 4; ++i)
+#pragma unroll
+                for (int q = 0; q < 4; ++q) R[(ty + 16 * i) * LDP + tx + 16 * q] = acc[i][q];
+        }
+        __syncthreads();
+        // ---- the [Tb;R] image (unit u -> K-major offset u * 16) and G
+        {
+            unsigned char *tr = ws_tr + (size_t)((b * Hv + h) * nc + cl) * TR_BYTES;
+            for (int u = t; u < 128 * (CH / 8); u += PT) {
+                const int r8 = u % 8, g = (u / 8) % (CH / 8), row = (u / 64) * 8 + r8;
+                const float *src = row < CH ? &Tm[row * LDP + 8 * g] : &R[(row - CH) * LDP + 8 * g];
+                float x[8];
+#pragma unroll
+                for (int e = 0; e < 8; ++e) x[e] = src[e];
+                uint4 hh, ll;
+                split8(x, hh, ll);
+                *reinterpret_cast<uint4 *>(tr + (size_t)u * 16) = hh;
+                *reinterpret_cast<uint4 *>(tr + TR_HALF + (size_t)u * 16) = ll;
+            }
+            if (t < CH) reinterpret_cast<float *>(tr + 2 * TR_HALF)[t] = sm.G[t];
+        }
+        __syncthreads();  // A, P, T, R, G are rewritten by the next value head
+    }
+}
+
+// ============================================================ recurrence
+constexpr int RT = 256;  // warp 0 copies, warp 1 MMAs, warps 4-7 passes
+constexpr uint32_t COL_A = 0, COL_B = 32, COL_S = 64, TM_COLS = 128;
+
+struct RecSmem {
+    unsigned char kq[2][KQ_BYTES];
+    unsigned char tr[2][TR_BYTES];
+    unsigned char s_op[2][128 * NV * 2];  // state, MN-major B operand (hi, lo)
+    unsigned char vpp[2][CH * NV * 2];    // V''
+    unsigned char vp[2][CH * NV * 2];     // V'_s
+    uint64_t kq_full[2], kq_empty[2], tr_full[2], tr_empty[2];
+    uint64_t bar_a, bar_b, bar_c, bar_s, bar_vpp, bar_vp;
+    uint32_t tmem;
+};
+static_assert(sizeof(RecSmem) <= 232448, "recurrence shared memory");
+
+template <int SDT>
+__global__ void __launch_bounds__(RT, 1)
+    chunk_rec_kernel(const kai_gdn_chunk_args p, const unsigned char *ws_kq, const unsigned char *ws_tr,
+                     long long c_begin, int nc, int *err) {
+    extern __shared__ __align__(16) unsigned char smem_raw[];
+    RecSmem &sm = *reinterpret_cast<RecSmem *>(smem_raw);
+    const int t = threadIdx.x, warp = t / 32, lane = t % 32;
+    const long long Hk = (long long)p.heads_k, Hv = (long long)p.heads_v, T = (long long)p.seq;
+    const long long DV = (long long)p.dv;
+    const int nvb = (int)(DV / NV);
+    const long long unit = blockIdx.x / nvb;  // b * Hv + h
+    const int vb = blockIdx.x % nvb;
+    const long long b = unit / Hv, h = unit % Hv, hk = h / (Hv / Hk);
+    const long long v0 = (long long)vb * NV;
+    const unsigned char *kq_src = ws_kq + (size_t)((b * Hk + hk) * nc) * KQ_BYTES;
+    const unsigned char *tr_src = ws_tr + (size_t)(unit * nc) * TR_BYTES;
+
+    if (t == 0) {
+        for (int s = 0; s < 2; ++s) {
+            mbar_init(&sm.kq_full[s], 1);
+            mbar_init(&sm.kq_empty[s], 1);
+            mbar_init(&sm.tr_full[s], 1);
+            mbar_init(&sm.tr_empty[s], 1 + 128);  // the D_b commit and the 128 readers of G
+        }
+        mbar_init(&sm.bar_a, 1);
+        mbar_init(&sm.bar_b, 1);
+        mbar_init(&sm.bar_c, 1);
+        mbar_init(&sm.bar_s, 128);
+        mbar_init(&sm.bar_vpp, 64);
+        mbar_init(&sm.bar_vp, 64);
+    }
+    if (warp == 1) tmem_alloc(&sm.tmem, TM_COLS);
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    fence_before_sync();
+    __syncthreads();
+    fence_after_sync();
+    const uint32_t tm = sm.tmem;
+
+    if (warp == 0) {
+        // ---------------------------------------------------- copy warp
+        if (lane == 0) {
+            int issued = 0;
+            for (int c = 0; c < nc; ++c) {
+                const int s = c & 1;
+                const uint32_t use = (uint32_t)(c >> 1);
+                if (use > 0 && !mbar_wait(&sm.kq_empty[s], (use - 1) & 1, err)) break;
+                mbar_arrive_expect_tx(&sm.kq_full[s], KQ_BYTES);
+                bulk_load(sm.kq[s], kq_src + (size_t)c * KQ_BYTES, KQ_BYTES, &sm.kq_full[s]);
+                if (use > 0 && !mbar_wait(&sm.tr_empty[s], (use - 1) & 1, err)) {
+                    mbar_wait(&sm.kq_full[s], use & 1, err);  // the copy just issued lands first
+                    break;
+                }
+                mbar_arrive_expect_tx(&sm.tr_full[s], TR_BYTES);
+                bulk_load(sm.tr[s], tr_src + (size_t)c * TR_BYTES, TR_BYTES, &sm.tr_full[s]);
+                issued = c + 1;
+            }
+            // no copy may still be landing when the CTA leaves
+            for (int c = issued - 2 < 0 ? 0 : issued - 2; c < issued; ++c) {
+                mbar_wait(&sm.kq_full[c & 1], (c >> 1) & 1, err);
+                mbar_wait(&sm.tr_full[c & 1], (c >> 1) & 1, err);
+            }
+        }
+    } else if (warp == 1) {
+        // ----------------------------------------------------- MMA warp
+        const uint32_t id_n = idesc(128, NV, BF16, false, true);  // A K-major, B MN-major
+        const uint32_t id_t = idesc(128, NV, BF16, true, true);   // A = K^T, MN-major
+        uint64_t *last = nullptr;
+        uint32_t last_ph = 0;
+        for (int c = 0; c < nc; ++c) {
+            const int s = c & 1;
+            const uint32_t ph = (uint32_t)(c >> 1) & 1, pc = (uint32_t)c & 1;
+            if (!wait_w(&sm.kq_full[s], ph, err) || !wait_w(&sm.bar_s, pc, err)) break;
+            fence_after_sync();
+            if (elect_one()) {
+#pragma unroll
+                for (int ks = 0; ks < DK / 16; ++ks) {
+                    const uint64_t ah = desc_kmaj16(sm.kq[s], DK, ks), al = desc_kmaj16(sm.kq[s] + KQ_HALF, DK, ks);
+                    const uint64_t bh = desc_mnmaj16(sm.s_op[0], NV, ks), bl = desc_mnmaj16(sm.s_op[1], NV, ks);
+                    mma_f16(tm + COL_A, ah, bh, id_n, ks > 0);
+                    mma_f16(tm + COL_A, ah, bl, id_n, true);
+                    mma_f16(tm + COL_A, al, bh, id_n, true);
+                }
+                commit(&sm.bar_a);
+            }
+            __syncwarp();
+            last = &sm.bar_a;
+            last_ph = pc;
+            if (!wait_w(&sm.tr_full[s], ph, err) || !wait_w(&sm.bar_vpp, pc, err)) break;
+            fence_after_sync();
+            if (elect_one()) {
+#pragma unroll
+                for (int ks = 0; ks < CH / 16; ++ks) {
+                    const uint64_t ah = desc_kmaj16(sm.tr[s], CH, ks), al = desc_kmaj16(sm.tr[s] + TR_HALF, CH, ks);
+                    const uint64_t bh = desc_mnmaj16(sm.vpp[0], NV, ks), bl = desc_mnmaj16(sm.vpp[1], NV, ks);
+                    mma_f16(tm + COL_B, ah, bh, id_n, ks > 0);
+                    mma_f16(tm + COL_B, ah, bl, id_n, true);
+                    mma_f16(tm + COL_B, al, bh, id_n, true);
+                }
+                commit(&sm.bar_b);
+                commit(&sm.tr_empty[s]);
+            }
+            __syncwarp();
+            last = &sm.bar_b;
+            if (!wait_w(&sm.bar_vp, pc, err)) break;
+            fence_after_sync();
+            if (elect_one()) {
+#pragma unroll
+                for (int ks = 0; ks < CH / 16; ++ks) {
+                    // the K rows of [K;Q] are the first 64; read MN-major they
+                    // are K^T (M = features, K = tokens)
+                    const uint64_t ah = desc_mnmaj16(sm.kq[s], DK, ks), al = desc_mnmaj16(sm.kq[s] + KQ_HALF, DK, ks);
+                    const uint64_t bh = desc_mnmaj16(sm.vp[0], NV, ks), bl = desc_mnmaj16(sm.vp[1], NV, ks);
+                    mma_f16(tm + COL_S, ah, bh, id_t, true);
+                    mma_f16(tm + COL_S, ah, bl, id_t, true);
+                    mma_f16(tm + COL_S, al, bh, id_t, true);
+                }
+                commit(&sm.bar_c);
+                commit(&sm.kq_empty[s]);
+            }
+            __syncwarp();
+            last = &sm.bar_c;
+        }
+        // every MMA has completed before the TMEM goes
+        if (last) wait_w(last, last_ph, err);
+    } else if (warp >= 4) {
+        // -------------------------------------------------- pass warps
+        using ST = Store<SDT>;
+        const int wq = warp - 4, row = 32 * wq + lane, r = row % CH;
+        const bool vrow = row < CH;  // warps 4, 5: V'' and V'; warps 6, 7: output rows
+        const uint32_t loff = (uint32_t)(32 * wq) << 16;
+        const uint32_t ta = tm + loff + COL_A, tb = tm + loff + COL_B, ts = tm + loff + COL_S;
+        typename ST::T *st = static_cast<typename ST::T *>(p.state) + ((size_t)unit * DK + row) * DV + v0;
+        float sv[NV];
+        // initial state row `row` (key feature), split for the first D_a and
+        // decayed by e^{G_63} of the first chunk into TMEM
+#pragma unroll
+        for (int n = 0; n < NV; ++n) sv[n] = ST::load(st + n);
+        bool ok = wait_w(&sm.tr_full[0], 0, err);
+        if (ok) {
+            const float e = expf(reinterpret_cast<const float *>(sm.tr[0] + 2 * TR_HALF)[CH - 1]);
+            put_row_mn(sm.s_op[0], sm.s_op[1], row, sv);
+#pragma unroll
+            for (int n = 0; n < NV; ++n) sv[n] *= e;
+            st32(ts, sv);
+            fence_smem_to_async();
+            fence_before_sync();
+            mbar_arrive1(&sm.bar_s);
+        }
+        for (int c = 0; ok && c < nc; ++c) {
+            const int s = c & 1;
+            const uint32_t ph = (uint32_t)(c >> 1) & 1, pc = (uint32_t)c & 1;
+            const long long tok = (c_begin + c) * CH + r;
+            if (!(ok = wait_w(&sm.tr_full[s], ph, err))) break;
+            const float *Gs = reinterpret_cast<const float *>(sm.tr[s] + 2 * TR_HALF);
+            const float gr = Gs[r], gl = Gs[CH - 1];
+            mbar_arrive1(&sm.tr_empty[s]);
+            if (vrow) {
+                float v[NV];
+                if (tok < T) {
+                    const float4 *vs = reinterpret_cast<const float4 *>(static_cast<const float *>(p.v) +
+                                                                        ((size_t)(b * T + tok) * Hv + h) * DV + v0);
+#pragma unroll
+                    for (int j = 0; j < NV / 4; ++j) *reinterpret_cast<float4 *>(&v[4 * j]) = __ldg(vs + j);
+                } else {
+#pragma unroll
+                    for (int n = 0; n < NV; ++n) v[n] = 0.f;
+                }
+                if (!(ok = wait_w(&sm.bar_a, pc, err))) break;
+                fence_after_sync();
+                float ks[NV];
+                ld32(ta, ks);
+                const float eg = expf(gr);
+#pragma unroll
+                for (int n = 0; n < NV; ++n) v[n] = fmaf(-eg, ks[n], v[n]);  // V''
+                put_row_mn(sm.vpp[0], sm.vpp[1], r, v);
+                fence_smem_to_async();
+                fence_before_sync();
+                mbar_arrive1(&sm.bar_vpp);
+                if (!(ok = wait_w(&sm.bar_b, pc, err))) break;
+                fence_after_sync();
+                ld32(tb, v);  // V'
+                const float el = expf(gl - gr);
+#pragma unroll
+                for (int n = 0; n < NV; ++n) v[n] *= el;
+                put_row_mn(sm.vp[0], sm.vp[1], r, v);
+                fence_smem_to_async();
+                fence_before_sync();
+                mbar_arrive1(&sm.bar_vp);
+            } else {
+                float x[NV], y[NV];
+                if (!(ok = wait_w(&sm.bar_a, pc, err))) break;
+                fence_after_sync();
+                ld32(ta, x);  // Q S
+                if (!(ok = wait_w(&sm.bar_b, pc, err))) break;
+                fence_after_sync();
+                ld32(tb, y);  // R V''
+                const float f = p.scale * expf(gr);
+#pragma unroll
+                for (int n = 0; n < NV; ++n) x[n] = fmaf(f, x[n], y[n]);
+                if (tok < T) store32(p.o, ((size_t)(b * T + tok) * Hv + h) * DV + v0, p.out_dtype, x);
+            }
+            // ---- the state after this chunk
+            const bool fin = c + 1 == nc;
+            float gn = 0.f;
+            if (!fin) {
+                if (!(ok = wait_w(&sm.tr_full[s ^ 1], (uint32_t)((c + 1) >> 1) & 1, err))) break;
+                gn = reinterpret_cast<const float *>(sm.tr[s ^ 1] + 2 * TR_HALF)[CH - 1];
+            }
+            if (!(ok = wait_w(&sm.bar_c, pc, err))) break;
+            fence_after_sync();
+            ld32(ts, sv);
+            if (fin) {
+#pragma unroll
+                for (int n = 0; n < NV; ++n) ST::store(st + n, sv[n]);
+            } else {
+                put_row_mn(sm.s_op[0], sm.s_op[1], row, sv);
+                const float e = expf(gn);
+#pragma unroll
+                for (int n = 0; n < NV; ++n) sv[n] *= e;
+                st32(ts, sv);
+                fence_smem_to_async();
+                fence_before_sync();
+                mbar_arrive1(&sm.bar_s);
+            }
+        }
+    }
+    fence_before_sync();
+    __syncthreads();
+    fence_after_sync();
+    if (warp == 1) tmem_dealloc(tm, TM_COLS);
+}
+
+template <int SDT>
+int launch_rec(const kai_gdn_chunk_args *a, const unsigned char *kq, const unsigned char *tr, long long c_begin,
+               int nc, int *err, cudaStream_t st) {
+    static thread_local int done_dev = -1;
+    int dev = 0;
+    int rc = check_cuda(cudaGetDevice(&dev), "chunk_tc32: cudaGetDevice");
+    if (rc) return rc;
+    if (done_dev != dev) {
+        rc = check_cuda(cudaFuncSetAttribute(chunk_rec_kernel<SDT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             (int)sizeof(RecSmem)),
+                        "chunk_tc32: smem attribute");
+        if (rc) return rc;
+        done_dev = dev;
+    }
+    const unsigned blocks = (unsigned)(a->batch * a->heads_v * (a->dv / NV));
+    chunk_rec_kernel<SDT><<<blocks, RT, sizeof(RecSmem), st>>>(*a, kq, tr, c_begin, nc, err);
+    return check_launch("chunk_tc32_rec");
+}
+
+}  // namespace
+
+bool chunk_tc32_supported(const kai_gdn_chunk_args *a) {
+    if (a->in_dtype != KAI_GDN_F32 || a->dk != (size_t)DK || a->chunk != (size_t)CH) return false;
+    if (a->dv == 0 || a->dv % NV) return false;
+    if (((uintptr_t)a->q | (uintptr_t)a->k | (uintptr_t)a->v | (uintptr_t)a->o) % 16) return false;
+    if (a->seq > 0x7fffffffull || a->batch * a->heads_v * (a->dv / NV) > 0x7fffffffull) return false;
+    return true;
+}
+
+size_t chunk_tc32_workspace_bytes(const kai_gdn_chunk_args *a) {
+    const size_t per_chunk = a->batch * (a->heads_k * (size_t)KQ_BYTES + a->heads_v * (size_t)TR_BYTES);
+    const size_t nch = (a->seq + CH - 1) / CH;
+    size_t seg = SEG_BUDGET / per_chunk;
+    if (seg < 1) seg = 1;
+    if (seg > nch) seg = nch;
+    return seg * per_chunk;
+}
+
+int launch_chunk_tc32(const kai_gdn_chunk_args *a, cudaStream_t st) {
+    const size_t per_chunk = a->batch * (a->heads_k * (size_t)KQ_BYTES + a->heads_v * (size_t)TR_BYTES);
+    const long long nch = (long long)((a->seq + CH - 1) / CH);
+    long long seg = (long long)(SEG_BUDGET / per_chunk);
+    if (seg < 1) seg = 1;
+    if (seg > nch) seg = nch;
+    const long long prep_blocks = (long long)(a->batch * a->heads_k) * seg;
+    if (prep_blocks > 0x7fffffffll) return set_error(KAI_GDN_ERR_UNSUPPORTED, "chunk_tc32: too many heads");
+    void *scr = nullptr;
+    int rc = scratch_for_stream(st, (size_t)seg * per_chunk, &scr);
+    if (rc) return rc;
+    unsigned char *kq = static_cast<unsigned char *>(scr);
+    unsigned char *tr = kq + (size_t)seg * a->batch * a->heads_k * KQ_BYTES;
+    int *err = nullptr;
+    if ((rc = device_error_word(&err))) return rc;
+    static thread_local int prep_dev = -1;
+    int dev = 0;
+    if ((rc = check_cuda(cudaGetDevice(&dev), "chunk_tc32: cudaGetDevice"))) return rc;
+    if (prep_dev != dev) {
+        rc = check_cuda(cudaFuncSetAttribute(chunk_prep_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             (int)sizeof(PrepSmem)),
+                        "chunk_tc32: smem attribute");
+        if (rc) return rc;
+        prep_dev = dev;
+    }
+    for (long long c_begin = 0; c_begin < nch; c_begin += seg) {
+        const int nc = (int)(nch - c_begin < seg ? nch - c_begin : seg);
+        chunk_prep_kernel<<<(unsigned)(a->batch * a->heads_k * nc), PT, sizeof(PrepSmem), st>>>(*a, kq, tr, c_begin,
+                                                                                                 nc);
+        if ((rc = check_launch("chunk_tc32_prep"))) return rc;
+        switch (a->state_dtype) {
+            case KAI_GDN_BF16: rc = launch_rec<KAI_GDN_BF16>(a, kq, tr, c_begin, nc, err, st); break;
+            case KAI_GDN_F16: rc = launch_rec<KAI_GDN_F16>(a, kq, tr, c_begin, nc, err, st); break;
+            default: rc = launch_rec<KAI_GDN_F32>(a, kq, tr, c_begin, nc, err, st);
+        }
+        if (rc) return rc;
+    }
+    return KAI_GDN_OK;
+}
+
+}  // namespace gdn

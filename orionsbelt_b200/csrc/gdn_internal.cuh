@@ -107,6 +107,11 @@ int launch_chunk(const kai_gdn_chunk_args *a, cudaStream_t st);
 // dk = dv = 128, chunk 64; TMA-fed, tcgen05 MMAs, fp32 state in TMEM.
 bool chunk_ws_supported(const kai_gdn_chunk_args *a);
 int launch_chunk_ws(const kai_gdn_chunk_args *a, cudaStream_t st);
+// Tensor-core chunk scan for fp32 inputs (chunk_tc32.cu): dk = 128, dv a
+// multiple of 32, 16-byte aligned q, k, v, o; fp32-accurate (three bf16 MMAs
+// per product); a parallel per-chunk launch, then the recurrence.
+bool chunk_tc32_supported(const kai_gdn_chunk_args *a);
+int launch_chunk_tc32(const kai_gdn_chunk_args *a, cudaStream_t st);
 
 // --------------------------------------------------- storage conversions
 // Loads widen to fp32 exactly; stores round to nearest even.
