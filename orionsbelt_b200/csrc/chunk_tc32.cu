@@ -99,6 +99,28 @@ __device__ __forceinline__ bool wait_w(uint64_t *bar, uint32_t phase, int *err) 
     return __all_sync(0xffffffffu, mbar_wait(bar, phase, err));
 }
 
+// The same by polling (mbarrier.test_wait never suspends): for the waits on
+// the recurrence's critical path, where a suspended thread measured ~200
+// cycles to resume after the phase completed.  At most 2^24 polls (well
+// under a second), then *err is set.
+__device__ __forceinline__ bool test_wait(uint64_t *bar, uint32_t phase) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}\n"
+        : "=r"(ok)
+        : "r"(smem_addr(bar)), "r"(phase)
+        : "memory");
+    return ok != 0;
+}
+__device__ __forceinline__ bool spin_w(uint64_t *bar, uint32_t phase, int *err) {
+    bool ok = false;
+    for (uint32_t i = 0; i < (1u << 24) && !ok; ++i) ok = test_wait(bar, phase);
+    if (!ok && err) atomicExch(err, 1);
+    return __all_sync(0xffffffffu, ok);
+}
+
 __device__ __forceinline__ void ld32(uint32_t taddr, float (&v)[NV]) {
     tmem_ld16(taddr, *reinterpret_cast<float(*)[16]>(&v[0]));
     tmem_ld16(taddr + 16, *reinterpret_cast<float(*)[16]>(&v[16]));
@@ -167,7 +189,7 @@ __global__ void __launch_bounds__(PT, 2)
                       int nc) {
     extern __shared__ __align__(16) unsigned char smem_raw[];
     PrepSmem &sm = *reinterpret_cast<PrepSmem *>(smem_raw);
-    const int t = threadIdx.x, tx = t % 16, ty = t / 16;
+    const int t = threadIdx.x;
     const long long Hk = (long long)p.heads_k, Hv = (long long)p.heads_v, T = (long long)p.seq;
     const int grp = (int)(Hv / Hk);
     const long long cl = blockIdx.x % nc, bh = blockIdx.x / nc;  // bh = b * Hk + hk
@@ -216,8 +238,13 @@ __global__ void __launch_bounds__(PT, 2)
         }
     }
 
-    // ---- K K^T and Q K^T (fp32; rows ty + 16 i, columns tx + 16 j)
-    {
+    // ---- K K^T and Q K^T, lower triangle (s <= r) only: the 136 4x4 tiles
+    // on or below the diagonal, one per thread of the first 136 (rows
+    // 4 ty .. 4 ty + 3, columns 4 tx .. 4 tx + 3, tx <= ty)
+    if (t < 136) {
+        int ty4 = 0;
+        while ((ty4 + 1) * (ty4 + 2) / 2 <= t) ++ty4;
+        const int tx4 = t - ty4 * (ty4 + 1) / 2, r0 = 4 * ty4, s0 = 4 * tx4;
         float kk[4][4], qk[4][4];
 #pragma unroll
         for (int i = 0; i < 4; ++i)
@@ -228,9 +255,9 @@ __global__ void __launch_bounds__(PT, 2)
             float4 kr[4], qr[4], ks[4];
 #pragma unroll
             for (int i = 0; i < 4; ++i) {
-                kr[i] = *reinterpret_cast<const float4 *>(&sm.u.in.K[(ty + 16 * i) * LDT + d]);
-                qr[i] = *reinterpret_cast<const float4 *>(&sm.u.in.Q[(ty + 16 * i) * LDT + d]);
-                ks[i] = *reinterpret_cast<const float4 *>(&sm.u.in.K[(tx + 16 * i) * LDT + d]);
+                kr[i] = *reinterpret_cast<const float4 *>(&sm.u.in.K[(r0 + i) * LDT + d]);
+                qr[i] = *reinterpret_cast<const float4 *>(&sm.u.in.Q[(r0 + i) * LDT + d]);
+                ks[i] = *reinterpret_cast<const float4 *>(&sm.u.in.K[(s0 + i) * LDT + d]);
             }
 #pragma unroll
             for (int i = 0; i < 4; ++i)
@@ -250,13 +277,16 @@ __global__ void __launch_bounds__(PT, 2)
         for (int i = 0; i < 4; ++i)
 #pragma unroll
             for (int j = 0; j < 4; ++j) {
-                sm.KK[(ty + 16 * i) * LDP + tx + 16 * j] = kk[i][j];
-                sm.QK[(ty + 16 * i) * LDP + tx + 16 * j] = qk[i][j];
+                sm.KK[(r0 + i) * LDP + s0 + j] = kk[i][j];
+                sm.QK[(r0 + i) * LDP + s0 + j] = qk[i][j];
             }
     }
     __syncthreads();  // the k, q tiles are dead from here (union)
 
+    // 16 x 16 block (bi, bj) of a 64 x 64 work matrix
+    auto blk = [](float *m, int bi, int bj, int rr, int cc) -> float & { return m[(16 * bi + rr) * LDP + 16 * bj + cc]; };
     float *const A = sm.u.w.A, *const Pm = sm.u.w.P, *const Tm = sm.u.w.T, *const R = sm.u.w.R;
+    const int rr = t / 16, cc = t % 16;  // this thread's element of a 16 x 16 block
     for (int gi = 0; gi < grp; ++gi) {
         const long long h = hk * grp + gi;
         if (t < 32) {
@@ -279,75 +309,97 @@ __global__ void __launch_bounds__(PT, 2)
             sm.beta[2 * t + 1] = b1;
         }
         __syncthreads();
-        // ---- A (s < r) and P (s <= r)
+        // ---- A (s < r) and P (s <= r); zeros above; T cleared
         for (int e = t; e < CH * CH; e += PT) {
             const int r = e / CH, s = e % CH;
-            const float dec = r >= s ? expf(sm.G[r] - sm.G[s]) : 0.f;
-            A[r * LDP + s] = r > s ? sm.beta[r] * sm.KK[r * LDP + s] * dec : 0.f;
-            Pm[r * LDP + s] = p.scale * sm.QK[r * LDP + s] * dec;
+            float a = 0.f, pv = 0.f;
+            if (r >= s) {
+                const float dec = expf(sm.G[r] - sm.G[s]);
+                if (r > s) a = sm.beta[r] * sm.KK[r * LDP + s] * dec;
+                pv = p.scale * sm.QK[r * LDP + s] * dec;
+            }
+            A[r * LDP + s] = a;
+            Pm[r * LDP + s] = pv;
+            Tm[r * LDP + s] = 0.f;
         }
         __syncthreads();
-        // ---- T = (I + A)^-1 by right-looking substitution on the identity,
-        // four lanes per column n (rows j + 4 m on lane j); x_r is final when
-        // step r starts and reaches the group by a shuffle.  Tb = T diag(beta).
+        // ---- T = (I + A)^-1, blocked.  Diagonal 16 x 16 blocks by
+        // right-looking substitution on the identity: four lanes per column
+        // (rows j + 4 m on lane j), x_r reaches the group by a shuffle.
         {
-            const int n = t / 4, j = t % 4, lane = t % 32;
-            float x[16];
+            const int bi = t / 64, col = (t / 4) % 16, j = t % 4, lane = t % 32;
+            float x[4];
 #pragma unroll
-            for (int m = 0; m < 16; ++m) x[m] = (j + 4 * m == n) ? 1.f : 0.f;
-#pragma unroll 1
-            for (int r = 0; r < CH - 1; ++r) {
-                const int owner = r % 4, mr = r / 4;
-                float xr = 0.f;
+            for (int m = 0; m < 4; ++m) x[m] = (j + 4 * m == col) ? 1.f : 0.f;
 #pragma unroll
-                for (int m = 0; m < 16; ++m)
-                    if (m == mr) xr = x[m];
-                xr = __shfl_sync(0xffffffffu, xr, lane - j + owner);
+            for (int r = 0; r < 15; ++r) {
+                float xr = x[r / 4];
+                xr = __shfl_sync(0xffffffffu, xr, lane - j + (r % 4));
 #pragma unroll
-                for (int m = 0; m < 16; ++m) {
-                    const int i = j + 4 * m;
-                    if (i > r) x[m] = fmaf(-A[i * LDP + r], xr, x[m]);
+                for (int m = 0; m < 4; ++m)
+                    if (j + 4 * m > r) x[m] = fmaf(-blk(A, bi, bi, j + 4 * m, r), xr, x[m]);
+            }
+#pragma unroll
+            for (int m = 0; m < 4; ++m) blk(Tm, bi, bi, j + 4 * m, col) = x[m];
+        }
+        __syncthreads();
+        // Off-diagonal blocks by block forward substitution, one distance
+        // d = bi - bj at a time: X = sum_{k=bj}^{bi-1} A_{bi,k} T_{k,bj}, then
+        // T_{bi,bj} = -T_{bi,bi} X.  X goes through R (free until R = P Tb).
+        for (int d = 1; d < 4; ++d) {
+            for (int bj = 0; bj + d < 4; ++bj) {
+                const int bi = bj + d;
+                float acc = 0.f;
+                for (int k = 16 * bj; k < 16 * bi; ++k)
+                    acc = fmaf(A[(16 * bi + rr) * LDP + k], Tm[k * LDP + 16 * bj + cc], acc);
+                blk(R, bi, bj, rr, cc) = acc;
+            }
+            __syncthreads();
+            for (int bj = 0; bj + d < 4; ++bj) {
+                const int bi = bj + d;
+                float acc = 0.f;
+#pragma unroll
+                for (int k = 0; k < 16; ++k) acc = fmaf(blk(Tm, bi, bi, rr, k), blk(R, bi, bj, k, cc), acc);
+                blk(Tm, bi, bj, rr, cc) = -acc;
+            }
+            __syncthreads();
+        }
+        // ---- R = P Tb over the blocks on or below the diagonal:
+        // R_{bi,bj} = (sum_{k=bj}^{bi} P_{bi,k} T_{k,bj}) diag(beta)
+        {
+            const float bcol[4] = {sm.beta[cc], sm.beta[16 + cc], sm.beta[32 + cc], sm.beta[48 + cc]};
+            float out[10];
+            int n = 0;
+#pragma unroll
+            for (int bi = 0; bi < 4; ++bi)
+#pragma unroll
+                for (int bj = 0; bj <= bi; ++bj) {
+                    float acc = 0.f;
+                    for (int k = 16 * bj; k < 16 * (bi + 1); ++k)
+                        acc = fmaf(Pm[(16 * bi + rr) * LDP + k], Tm[k * LDP + 16 * bj + cc], acc);
+                    out[n++] = acc * bcol[bj];
                 }
-            }
-            const float bn = sm.beta[n];
+            n = 0;
 #pragma unroll
-            for (int m = 0; m < 16; ++m) Tm[(j + 4 * m) * LDP + n] = x[m] * bn;
+            for (int bi = 0; bi < 4; ++bi)
+#pragma unroll
+                for (int bj = 0; bj < 4; ++bj) blk(R, bi, bj, rr, cc) = bj <= bi ? out[n++] : 0.f;
         }
         __syncthreads();
-        // ---- R = P Tb
-        {
-            float acc[4][4];
-#pragma unroll
-            for (int i = 0; i < 4; ++i)
-#pragma unroll
-                for (int q = 0; q < 4; ++q) acc[i][q] = 0.f;
-#pragma unroll 4
-            for (int jj = 0; jj < CH; ++jj) {
-                float pr[4], tb[4];
-#pragma unroll
-                for (int i = 0; i < 4; ++i) pr[i] = Pm[(ty + 16 * i) * LDP + jj];
-#pragma unroll
-                for (int q = 0; q < 4; ++q) tb[q] = Tm[jj * LDP + tx + 16 * q];
-#pragma unroll
-                for (int i = 0; i < 4; ++i)
-#pragma unroll
-                    for (int q = 0; q < 4; ++q) acc[i][q] = fmaf(pr[i], tb[q], acc[i][q]);
-            }
-#pragma unroll
-            for (int i = 0; i < 4; ++i)
-#pragma unroll
-                for (int q = 0; q < 4; ++q) R[(ty + 16 * i) * LDP + tx + 16 * q] = acc[i][q];
-        }
-        __syncthreads();
-        // ---- the [Tb;R] image (unit u -> K-major offset u * 16) and G
+        // ---- the [Tb;R] image (unit u -> K-major offset u * 16) and G;
+        // Tb = T diag(beta) is applied here
         {
             unsigned char *tr = ws_tr + (size_t)((b * Hv + h) * nc + cl) * TR_BYTES;
             for (int u = t; u < 128 * (CH / 8); u += PT) {
                 const int r8 = u % 8, g = (u / 8) % (CH / 8), row = (u / 64) * 8 + r8;
-                const float *src = row < CH ? &Tm[row * LDP + 8 * g] : &R[(row - CH) * LDP + 8 * g];
                 float x[8];
+                if (row < CH) {
 #pragma unroll
-                for (int e = 0; e < 8; ++e) x[e] = src[e];
+                    for (int e = 0; e < 8; ++e) x[e] = Tm[row * LDP + 8 * g + e] * sm.beta[8 * g + e];
+                } else {
+#pragma unroll
+                    for (int e = 0; e < 8; ++e) x[e] = R[(row - CH) * LDP + 8 * g + e];
+                }
                 uint4 hh, ll;
                 split8(x, hh, ll);
                 *reinterpret_cast<uint4 *>(tr + (size_t)u * 16) = hh;
@@ -446,7 +498,7 @@ __global__ void __launch_bounds__(RT, 1)
         for (int c = 0; c < nc; ++c) {
             const int s = c & 1;
             const uint32_t ph = (uint32_t)(c >> 1) & 1, pc = (uint32_t)c & 1;
-            if (!wait_w(&sm.kq_full[s], ph, err) || !wait_w(&sm.bar_s, pc, err)) break;
+            if (!wait_w(&sm.kq_full[s], ph, err) || !spin_w(&sm.bar_s, pc, err)) break;
             fence_after_sync();
             if (elect_one()) {
 #pragma unroll
@@ -462,7 +514,7 @@ __global__ void __launch_bounds__(RT, 1)
             __syncwarp();
             last = &sm.bar_a;
             last_ph = pc;
-            if (!wait_w(&sm.tr_full[s], ph, err) || !wait_w(&sm.bar_vpp, pc, err)) break;
+            if (!wait_w(&sm.tr_full[s], ph, err) || !spin_w(&sm.bar_vpp, pc, err)) break;
             fence_after_sync();
             if (elect_one()) {
 #pragma unroll
@@ -478,7 +530,7 @@ __global__ void __launch_bounds__(RT, 1)
             }
             __syncwarp();
             last = &sm.bar_b;
-            if (!wait_w(&sm.bar_vp, pc, err)) break;
+            if (!spin_w(&sm.bar_vp, pc, err)) break;
             fence_after_sync();
             if (elect_one()) {
 #pragma unroll
@@ -542,7 +594,7 @@ __global__ void __launch_bounds__(RT, 1)
 #pragma unroll
                     for (int n = 0; n < NV; ++n) v[n] = 0.f;
                 }
-                if (!(ok = wait_w(&sm.bar_a, pc, err))) break;
+                if (!(ok = spin_w(&sm.bar_a, pc, err))) break;
                 fence_after_sync();
                 float ks[NV];
                 ld32(ta, ks);
@@ -553,7 +605,7 @@ __global__ void __launch_bounds__(RT, 1)
                 fence_smem_to_async();
                 fence_before_sync();
                 mbar_arrive1(&sm.bar_vpp);
-                if (!(ok = wait_w(&sm.bar_b, pc, err))) break;
+                if (!(ok = spin_w(&sm.bar_b, pc, err))) break;
                 fence_after_sync();
                 ld32(tb, v);  // V'
                 const float el = expf(gl - gr);
@@ -565,10 +617,10 @@ __global__ void __launch_bounds__(RT, 1)
                 mbar_arrive1(&sm.bar_vp);
             } else {
                 float x[NV], y[NV];
-                if (!(ok = wait_w(&sm.bar_a, pc, err))) break;
+                if (!(ok = spin_w(&sm.bar_a, pc, err))) break;
                 fence_after_sync();
                 ld32(ta, x);  // Q S
-                if (!(ok = wait_w(&sm.bar_b, pc, err))) break;
+                if (!(ok = spin_w(&sm.bar_b, pc, err))) break;
                 fence_after_sync();
                 ld32(tb, y);  // R V''
                 const float f = p.scale * expf(gr);
@@ -583,7 +635,7 @@ __global__ void __launch_bounds__(RT, 1)
                 if (!(ok = wait_w(&sm.tr_full[s ^ 1], (uint32_t)((c + 1) >> 1) & 1, err))) break;
                 gn = reinterpret_cast<const float *>(sm.tr[s ^ 1] + 2 * TR_HALF)[CH - 1];
             }
-            if (!(ok = wait_w(&sm.bar_c, pc, err))) break;
+            if (!(ok = spin_w(&sm.bar_c, pc, err))) break;
             fence_after_sync();
             ld32(ts, sv);
             if (fin) {

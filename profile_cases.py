@@ -2,6 +2,7 @@
 
     python profile_cases.py decode [--launches 3]
     python profile_cases.py chunk  [--launches 1]
+    python profile_cases.py chunk32
     python profile_cases.py conv | cumsum | scan | attn | int8 | int8m16 | lmhead | lmhead16 | ffn16 | model
     python profile_cases.py prefill [--launches 1]
     python profile_cases.py gemm4k
@@ -13,6 +14,8 @@ its kernel through the C ABI, and exits.  Cases:
   decode  one config-1 layer: B=64, 32 value / 16 key heads, 128x128 fp32
           state (268 MB), bf16 q/k/v/o
   chunk   config-2 numerics on a reduced shard: B=1, T=8192, bf16 in / fp32 state
+  chunk32 config 0: B=1, T=2048, 16 key / 32 value heads, fp32 throughout (the
+          tensor-core prep and recurrence launches; 67 MB of operand images)
   conv    config-0 Conv1D: T=2048, 8192 channels, fp32 (134 MB)
   cumsum  config-2 decay cumsum: 8 x 32768 x 32 log-decays, fp32
   scan    gated scan, 4096 tokens x 8192 channels, fp32
@@ -48,7 +51,7 @@ from orionsbelt_b200 import _lib, ops, synth  # noqa: E402
 
 def main() -> None:
     ap = argparse.ArgumentParser()
-    ap.add_argument("case", choices=["decode", "chunk", "conv", "cumsum", "scan", "attn", "int8", "int8m16", "lmhead",
+    ap.add_argument("case", choices=["decode", "chunk", "chunk32", "conv", "cumsum", "scan", "attn", "int8", "int8m16", "lmhead",
                                      "lmhead16", "ffn16", "model", "prefill", "gemm4k", "model16"])
     ap.add_argument("--launches", type=int, default=3)
     a = ap.parse_args()
@@ -64,6 +67,10 @@ def main() -> None:
             args, torch.cuda.current_stream().cuda_stream))
     elif a.case == "chunk":
         d = synth.device_gdn(1, 8192, 16, 32, 128, 128, seed=2, in_dtype=torch.bfloat16)
+        o = torch.empty_like(d["v"])
+        fn = lambda: ops.chunk_delta_rule(d["q"], d["k"], d["v"], d["g"], d["beta"], d["S0"], o)  # noqa: E731
+    elif a.case == "chunk32":
+        d = synth.device_gdn(1, 2048, 16, 32, 128, 128, seed=2)
         o = torch.empty_like(d["v"])
         fn = lambda: ops.chunk_delta_rule(d["q"], d["k"], d["v"], d["g"], d["beta"], d["S0"], o)  # noqa: E731
     elif a.case == "conv":
