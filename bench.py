@@ -717,7 +717,8 @@ def run_model(args, world, rank, barrier, peaks, ctx=32768, steps=256):
                             f"tensor-parallel x{world} over NCCL",
                 "kernels": "decode: gemv_int8_kernel / int8_packed_kernel, decode_step_kernel, attn_tc_kernel, model "
                            "elementwise kernels, per-segment CUDA graphs; prefill: int8_gemm_kernel (row-tiled int8 "
-                           "tcgen05 GEMM over the packed weights), chunk_scan_fp32_kernel, attn_prefill_kernel",
+                           "tcgen05 GEMM over the packed weights), chunk_prep_kernel + chunk_rec_kernel (fp32 chunk "
+                           "scan on tcgen05), attn_prefill_kernel",
                 "weight_bytes_per_token_per_gpu": int(tok_bytes)})
     return out
 
@@ -954,7 +955,7 @@ def run_rows(args, peaks) -> dict:
     # a6: chunk scan at config 0 (fp32 throughout) and config 3 (fp16 in, fp16 state, strong decay)
     for name, c, dt, sdt, kern in [
             ("a6_chunk_cfg0", dict(B=1, T=2048, g=0.1), torch.float32, torch.float32,
-             "chunk_scan_fp32_kernel (fp32 CUDA cores)"),
+             "chunk_prep_kernel + chunk_rec_kernel (tcgen05, fp32-accurate: three bf16 MMAs per product)"),
             ("a6_chunk_cfg3", dict(B=32, T=8192, g=1.0), torch.float16, torch.float16,
              "chunk_ws_kernel<f16> (warp-specialised, tcgen05)")]:
         d = synth.device_gdn(c["B"], c["T"], 16, 32, 128, 128, g_scale=c["g"], seed=14, in_dtype=dt,

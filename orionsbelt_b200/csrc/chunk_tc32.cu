@@ -422,7 +422,7 @@ struct RecSmem {
     unsigned char vpp[2][CH * NV * 2];    // V''
     unsigned char vp[2][CH * NV * 2];     // V'_s
     uint64_t kq_full[2], kq_empty[2], tr_full[2], tr_empty[2];
-    uint64_t bar_a, bar_b, bar_c, bar_s, bar_vpp, bar_vp;
+    uint64_t bar_a, bar_b, bar_c, bar_s, bar_vpp, bar_vp, bar_fin;
     uint32_t tmem;
 };
 static_assert(sizeof(RecSmem) <= 232448, "recurrence shared memory");
@@ -454,6 +454,7 @@ __global__ void __launch_bounds__(RT, 1)
         mbar_init(&sm.bar_a, 1);
         mbar_init(&sm.bar_b, 1);
         mbar_init(&sm.bar_c, 1);
+        mbar_init(&sm.bar_fin, 1);
         mbar_init(&sm.bar_s, 128);
         mbar_init(&sm.bar_vpp, 64);
         mbar_init(&sm.bar_vp, 64);
@@ -493,8 +494,6 @@ __global__ void __launch_bounds__(RT, 1)
         // ----------------------------------------------------- MMA warp
         const uint32_t id_n = idesc(128, NV, BF16, false, true);  // A K-major, B MN-major
         const uint32_t id_t = idesc(128, NV, BF16, true, true);   // A = K^T, MN-major
-        uint64_t *last = nullptr;
-        uint32_t last_ph = 0;
         for (int c = 0; c < nc; ++c) {
             const int s = c & 1;
             const uint32_t ph = (uint32_t)(c >> 1) & 1, pc = (uint32_t)c & 1;
@@ -512,8 +511,6 @@ __global__ void __launch_bounds__(RT, 1)
                 commit(&sm.bar_a);
             }
             __syncwarp();
-            last = &sm.bar_a;
-            last_ph = pc;
             if (!wait_w(&sm.tr_full[s], ph, err) || !spin_w(&sm.bar_vpp, pc, err)) break;
             fence_after_sync();
             if (elect_one()) {
@@ -529,7 +526,6 @@ __global__ void __launch_bounds__(RT, 1)
                 commit(&sm.tr_empty[s]);
             }
             __syncwarp();
-            last = &sm.bar_b;
             if (!spin_w(&sm.bar_vp, pc, err)) break;
             fence_after_sync();
             if (elect_one()) {
@@ -547,10 +543,12 @@ __global__ void __launch_bounds__(RT, 1)
                 commit(&sm.kq_empty[s]);
             }
             __syncwarp();
-            last = &sm.bar_c;
         }
-        // every MMA has completed before the TMEM goes
-        if (last) wait_w(last, last_ph, err);
+        // every MMA has completed before the TMEM goes (the commit tracks all
+        // MMAs this lane issued)
+        if (elect_one()) commit(&sm.bar_fin);
+        __syncwarp();
+        wait_w(&sm.bar_fin, 0, err);
     } else if (warp >= 4) {
         // -------------------------------------------------- pass warps
         using ST = Store<SDT>;
