@@ -161,132 +161,109 @@ __device__ __forceinline__ void store32(void *base, size_t idx, int dt, const fl
 }
 
 // ================================================================ prep
-constexpr int PT = 256;   // threads
-constexpr int LDT = 132;  // K / Q tile row stride (floats)
-constexpr int LDP = 65;   // 64 x 64 work matrices
+constexpr int PT = 256;  // threads
+constexpr int LDP = 65;  // 64 x 64 fp32 work matrices
+constexpr uint32_t PCOL_KK = 0, PCOL_R = 64, PTM_COLS = 128;
 
 struct PrepSmem {
     union {
-        struct {
-            float K[CH * LDT];
-            float Q[CH * LDT];
-        } in;
+        unsigned char img[KQ_BYTES];  // the [K;Q] image, operands of K K^T and Q K^T, ...
         struct {
             float A[CH * LDP];
-            float P[CH * LDP];
-            float T[CH * LDP];  // Tb once the substitution is done
-            float R[CH * LDP];
-        } w;
+            float T[CH * LDP];
+            float X[CH * LDP];  // scratch of the blocked inverse
+        } w;                     // ... then, with those products in TMEM, the inverse's work
     } u;
-    float KK[CH * LDP];
-    float QK[CH * LDP];
+    unsigned char pimg[2][CH * CH * 2];   // P (hi, lo): K-major A operand of R = P Tb
+    unsigned char tbimg[2][CH * CH * 2];  // Tb (hi, lo): read MN-major as its B operand
     float G[CH];
     float beta[CH];
+    uint64_t bar_kk, bar_r, bar_fin;
+    uint32_t tmem;
 };
 
 __global__ void __launch_bounds__(PT, 2)
     chunk_prep_kernel(const kai_gdn_chunk_args p, unsigned char *ws_kq, unsigned char *ws_tr, long long c_begin,
-                      int nc) {
+                      int nc, int *err) {
     extern __shared__ __align__(16) unsigned char smem_raw[];
     PrepSmem &sm = *reinterpret_cast<PrepSmem *>(smem_raw);
-    const int t = threadIdx.x;
+    const int t = threadIdx.x, warp = t / 32, lane = t % 32;
     const long long Hk = (long long)p.heads_k, Hv = (long long)p.heads_v, T = (long long)p.seq;
     const int grp = (int)(Hv / Hk);
     const long long cl = blockIdx.x % nc, bh = blockIdx.x / nc;  // bh = b * Hk + hk
     const long long b = bh / Hk, hk = bh % Hk;
     const long long c0 = (c_begin + cl) * CH;
 
-    // ---- k, q tiles (rows past T are zeros)
+    if (t == 0) {
+        mbar_init(&sm.bar_kk, 1);
+        mbar_init(&sm.bar_r, 1);
+        mbar_init(&sm.bar_fin, 1);
+    }
+    if (warp == 0) tmem_alloc(&sm.tmem, PTM_COLS);
+
+    // ---- k, q rows (zeros past T) into the [K;Q] image, in shared memory for
+    // the MMAs below and in the workspace for the recurrence.  Unit u holds 8
+    // features of one row; with u = ((row / 8) * 16 + feature group) * 8 +
+    // row % 8 its K-major offset is u * 16 (contiguous stores).
     {
         const float *kg = static_cast<const float *>(p.k), *qg = static_cast<const float *>(p.q);
-        float4 kv[8], qv[8];
-#pragma unroll
-        for (int i = 0; i < 8; ++i) {
-            const int e = t + PT * i, r = e / 32, c4 = e % 32;
-            const long long tok = c0 + r;
-            kv[i] = qv[i] = make_float4(0.f, 0.f, 0.f, 0.f);
-            if (tok < T) {
-                const size_t off = ((size_t)(b * T + tok) * Hk + hk) * DK + 4 * c4;
-                kv[i] = __ldg(reinterpret_cast<const float4 *>(kg + off));
-                qv[i] = __ldg(reinterpret_cast<const float4 *>(qg + off));
-            }
-        }
-#pragma unroll
-        for (int i = 0; i < 8; ++i) {
-            const int e = t + PT * i, r = e / 32, c4 = e % 32;
-            *reinterpret_cast<float4 *>(&sm.u.in.K[r * LDT + 4 * c4]) = kv[i];
-            *reinterpret_cast<float4 *>(&sm.u.in.Q[r * LDT + 4 * c4]) = qv[i];
-        }
-    }
-    __syncthreads();
-
-    // ---- the [K;Q] image: unit u covers 8 features of one row; with
-    // u = ((row / 8) * 16 + feature group) * 8 + row % 8 its K-major offset
-    // is u * 16, so the warp's stores are contiguous.
-    {
         unsigned char *kq = ws_kq + (size_t)(bh * nc + cl) * KQ_BYTES;
-        for (int u = t; u < 128 * (DK / 8); u += PT) {
-            const int r8 = u % 8, g = (u / 8) % (DK / 8), row = (u / 128) * 8 + r8;
-            const float *src = row < CH ? &sm.u.in.K[row * LDT + 8 * g] : &sm.u.in.Q[(row - CH) * LDT + 8 * g];
-            float x[8];
-            *reinterpret_cast<float4 *>(&x[0]) = *reinterpret_cast<const float4 *>(src);
-            *reinterpret_cast<float4 *>(&x[4]) = *reinterpret_cast<const float4 *>(src + 4);
-            uint4 h, l;
-            split8(x, h, l);
-            *reinterpret_cast<uint4 *>(kq + (size_t)u * 16) = h;
-            *reinterpret_cast<uint4 *>(kq + KQ_HALF + (size_t)u * 16) = l;
+        float4 x[16];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+            const int u = t + PT * i, row = (u / 128) * 8 + u % 8, g = (u / 8) % (DK / 8);
+            const long long tok = c0 + row % CH;
+            x[2 * i] = x[2 * i + 1] = make_float4(0.f, 0.f, 0.f, 0.f);
+            if (tok < T) {
+                const float4 *src = reinterpret_cast<const float4 *>((row < CH ? kg : qg) +
+                                                                     ((size_t)(b * T + tok) * Hk + hk) * DK + 8 * g);
+                x[2 * i] = __ldg(src);
+                x[2 * i + 1] = __ldg(src + 1);
+            }
+        }
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+            const int u = t + PT * i;
+            uint4 hv, lv;
+            split8(reinterpret_cast<const float *>(&x[2 * i]), hv, lv);
+            *reinterpret_cast<uint4 *>(sm.u.img + u * 16) = hv;
+            *reinterpret_cast<uint4 *>(sm.u.img + KQ_HALF + u * 16) = lv;
+            *reinterpret_cast<uint4 *>(kq + (size_t)u * 16) = hv;
+            *reinterpret_cast<uint4 *>(kq + KQ_HALF + (size_t)u * 16) = lv;
         }
     }
+    fence_smem_to_async();
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    fence_before_sync();
+    __syncthreads();
+    fence_after_sync();
+    const uint32_t tm = sm.tmem;
 
-    // ---- K K^T and Q K^T, lower triangle (s <= r) only: the 136 4x4 tiles
-    // on or below the diagonal, one per thread of the first 136 (rows
-    // 4 ty .. 4 ty + 3, columns 4 tx .. 4 tx + 3, tx <= ty)
-    if (t < 136) {
-        int ty4 = 0;
-        while ((ty4 + 1) * (ty4 + 2) / 2 <= t) ++ty4;
-        const int tx4 = t - ty4 * (ty4 + 1) / 2, r0 = 4 * ty4, s0 = 4 * tx4;
-        float kk[4][4], qk[4][4];
+    // ---- D[128 x 64] = [K;Q] K^T: rows 0-63 K K^T, rows 64-127 Q K^T.  The
+    // B operand (64 tokens x 128 features, K-major) is the first 64 rows of
+    // the same image, so A and B share descriptors.
+    if (warp == 0) {
+        if (elect_one()) {
+            const uint32_t id = idesc(128, CH, BF16, false, false);
 #pragma unroll
-        for (int i = 0; i < 4; ++i)
-#pragma unroll
-            for (int j = 0; j < 4; ++j) kk[i][j] = qk[i][j] = 0.f;
-#pragma unroll 2
-        for (int d = 0; d < DK; d += 4) {
-            float4 kr[4], qr[4], ks[4];
-#pragma unroll
-            for (int i = 0; i < 4; ++i) {
-                kr[i] = *reinterpret_cast<const float4 *>(&sm.u.in.K[(r0 + i) * LDT + d]);
-                qr[i] = *reinterpret_cast<const float4 *>(&sm.u.in.Q[(r0 + i) * LDT + d]);
-                ks[i] = *reinterpret_cast<const float4 *>(&sm.u.in.K[(s0 + i) * LDT + d]);
+            for (int ks = 0; ks < DK / 16; ++ks) {
+                const uint64_t hi = desc_kmaj16(sm.u.img, DK, ks), lo = desc_kmaj16(sm.u.img + KQ_HALF, DK, ks);
+                mma_f16(tm + PCOL_KK, hi, hi, id, ks > 0);
+                mma_f16(tm + PCOL_KK, hi, lo, id, true);
+                mma_f16(tm + PCOL_KK, lo, hi, id, true);
             }
-#pragma unroll
-            for (int i = 0; i < 4; ++i)
-#pragma unroll
-                for (int j = 0; j < 4; ++j) {
-                    kk[i][j] = fmaf(kr[i].x, ks[j].x, kk[i][j]);
-                    kk[i][j] = fmaf(kr[i].y, ks[j].y, kk[i][j]);
-                    kk[i][j] = fmaf(kr[i].z, ks[j].z, kk[i][j]);
-                    kk[i][j] = fmaf(kr[i].w, ks[j].w, kk[i][j]);
-                    qk[i][j] = fmaf(qr[i].x, ks[j].x, qk[i][j]);
-                    qk[i][j] = fmaf(qr[i].y, ks[j].y, qk[i][j]);
-                    qk[i][j] = fmaf(qr[i].z, ks[j].z, qk[i][j]);
-                    qk[i][j] = fmaf(qr[i].w, ks[j].w, qk[i][j]);
-                }
+            commit(&sm.bar_kk);
         }
-#pragma unroll
-        for (int i = 0; i < 4; ++i)
-#pragma unroll
-            for (int j = 0; j < 4; ++j) {
-                sm.KK[(r0 + i) * LDP + s0 + j] = kk[i][j];
-                sm.QK[(r0 + i) * LDP + s0 + j] = qk[i][j];
-            }
+        __syncwarp();
     }
-    __syncthreads();  // the k, q tiles are dead from here (union)
 
     // 16 x 16 block (bi, bj) of a 64 x 64 work matrix
     auto blk = [](float *m, int bi, int bj, int rr, int cc) -> float & { return m[(16 * bi + rr) * LDP + 16 * bj + cc]; };
-    float *const A = sm.u.w.A, *const Pm = sm.u.w.P, *const Tm = sm.u.w.T, *const R = sm.u.w.R;
+    float *const A = sm.u.w.A, *const Tm = sm.u.w.T, *const X = sm.u.w.X;
     const int rr = t / 16, cc = t % 16;  // this thread's element of a 16 x 16 block
+    const int q4 = warp % 4, hh = warp / 4;  // TMEM lane quarter, half of the 64 columns
+    const int L = 32 * q4 + lane;            // this thread's TMEM lane
+    const uint32_t lq = (uint32_t)(32 * q4) << 16;
     for (int gi = 0; gi < grp; ++gi) {
         const long long h = hk * grp + gi;
         if (t < 32) {
@@ -308,26 +285,46 @@ __global__ void __launch_bounds__(PT, 2)
             sm.beta[2 * t] = b0;
             sm.beta[2 * t + 1] = b1;
         }
-        __syncthreads();
-        // ---- A (s < r) and P (s <= r); zeros above; T cleared
-        for (int e = t; e < CH * CH; e += PT) {
-            const int r = e / CH, s = e % CH;
-            float a = 0.f, pv = 0.f;
-            if (r >= s) {
-                const float dec = expf(sm.G[r] - sm.G[s]);
-                if (r > s) a = sm.beta[r] * sm.KK[r * LDP + s] * dec;
-                pv = p.scale * sm.QK[r * LDP + s] * dec;
+        const bool ok_kk = wait_w(&sm.bar_kk, 0, err);
+        if (__syncthreads_or(!ok_kk)) break;
+        fence_after_sync();
+        // ---- A (s < r) into shared memory and T cleared, from the K K^T rows;
+        // P (s <= r) into its operand image, from the Q K^T rows
+        {
+            float v[32];
+            ld32(tm + lq + PCOL_KK + 32 * hh, v);
+            const int r = L % CH;
+            const float gr = sm.G[r];
+            if (L < CH) {
+                const float br = sm.beta[r];
+#pragma unroll
+                for (int n = 0; n < 32; ++n) {
+                    const int s = 32 * hh + n;
+                    A[r * LDP + s] = s < r ? br * v[n] * expf(gr - sm.G[s]) : 0.f;
+                    Tm[r * LDP + s] = 0.f;
+                }
+            } else {
+#pragma unroll
+                for (int n = 0; n < 32; ++n) {
+                    const int s = 32 * hh + n;
+                    v[n] = s <= r ? p.scale * v[n] * expf(gr - sm.G[s]) : 0.f;
+                }
+#pragma unroll
+                for (int j = 0; j < 4; ++j) {
+                    uint4 hv, lv;
+                    split8(&v[8 * j], hv, lv);
+                    const uint32_t off = kmaj16(r, 32 * hh + 8 * j, CH);
+                    *reinterpret_cast<uint4 *>(sm.pimg[0] + off) = hv;
+                    *reinterpret_cast<uint4 *>(sm.pimg[1] + off) = lv;
+                }
             }
-            A[r * LDP + s] = a;
-            Pm[r * LDP + s] = pv;
-            Tm[r * LDP + s] = 0.f;
         }
         __syncthreads();
         // ---- T = (I + A)^-1, blocked.  Diagonal 16 x 16 blocks by
         // right-looking substitution on the identity: four lanes per column
         // (rows j + 4 m on lane j), x_r reaches the group by a shuffle.
         {
-            const int bi = t / 64, col = (t / 4) % 16, j = t % 4, lane = t % 32;
+            const int bi = t / 64, col = (t / 4) % 16, j = t % 4;
             float x[4];
 #pragma unroll
             for (int m = 0; m < 4; ++m) x[m] = (j + 4 * m == col) ? 1.f : 0.f;
@@ -345,70 +342,92 @@ __global__ void __launch_bounds__(PT, 2)
         __syncthreads();
         // Off-diagonal blocks by block forward substitution, one distance
         // d = bi - bj at a time: X = sum_{k=bj}^{bi-1} A_{bi,k} T_{k,bj}, then
-        // T_{bi,bj} = -T_{bi,bi} X.  X goes through R (free until R = P Tb).
+        // T_{bi,bj} = -T_{bi,bi} X.
         for (int d = 1; d < 4; ++d) {
             for (int bj = 0; bj + d < 4; ++bj) {
                 const int bi = bj + d;
                 float acc = 0.f;
                 for (int k = 16 * bj; k < 16 * bi; ++k)
                     acc = fmaf(A[(16 * bi + rr) * LDP + k], Tm[k * LDP + 16 * bj + cc], acc);
-                blk(R, bi, bj, rr, cc) = acc;
+                blk(X, bi, bj, rr, cc) = acc;
             }
             __syncthreads();
             for (int bj = 0; bj + d < 4; ++bj) {
                 const int bi = bj + d;
                 float acc = 0.f;
 #pragma unroll
-                for (int k = 0; k < 16; ++k) acc = fmaf(blk(Tm, bi, bi, rr, k), blk(R, bi, bj, k, cc), acc);
+                for (int k = 0; k < 16; ++k) acc = fmaf(blk(Tm, bi, bi, rr, k), blk(X, bi, bj, k, cc), acc);
                 blk(Tm, bi, bj, rr, cc) = -acc;
             }
             __syncthreads();
         }
-        // ---- R = P Tb over the blocks on or below the diagonal:
-        // R_{bi,bj} = (sum_{k=bj}^{bi} P_{bi,k} T_{k,bj}) diag(beta)
-        {
-            const float bcol[4] = {sm.beta[cc], sm.beta[16 + cc], sm.beta[32 + cc], sm.beta[48 + cc]};
-            float out[10];
-            int n = 0;
+        // ---- Tb = T diag(beta): the top half of the [Tb;R] image in the
+        // workspace, and in shared memory the B operand of R = P Tb
+        unsigned char *tr = ws_tr + (size_t)((b * Hv + h) * nc + cl) * TR_BYTES;
+        for (int u = t; u < CH * (CH / 8); u += PT) {
+            const int row = (u / 64) * 8 + u % 8, g = (u / 8) % (CH / 8);  // K-major offset u * 16
+            float x[8];
 #pragma unroll
-            for (int bi = 0; bi < 4; ++bi)
-#pragma unroll
-                for (int bj = 0; bj <= bi; ++bj) {
-                    float acc = 0.f;
-                    for (int k = 16 * bj; k < 16 * (bi + 1); ++k)
-                        acc = fmaf(Pm[(16 * bi + rr) * LDP + k], Tm[k * LDP + 16 * bj + cc], acc);
-                    out[n++] = acc * bcol[bj];
-                }
-            n = 0;
-#pragma unroll
-            for (int bi = 0; bi < 4; ++bi)
-#pragma unroll
-                for (int bj = 0; bj < 4; ++bj) blk(R, bi, bj, rr, cc) = bj <= bi ? out[n++] : 0.f;
+            for (int e = 0; e < 8; ++e) x[e] = Tm[row * LDP + 8 * g + e] * sm.beta[8 * g + e];
+            uint4 hv, lv;
+            split8(x, hv, lv);
+            *reinterpret_cast<uint4 *>(sm.tbimg[0] + u * 16) = hv;
+            *reinterpret_cast<uint4 *>(sm.tbimg[1] + u * 16) = lv;
+            *reinterpret_cast<uint4 *>(tr + (size_t)u * 16) = hv;
+            *reinterpret_cast<uint4 *>(tr + TR_HALF + (size_t)u * 16) = lv;
         }
+        if (t < CH) reinterpret_cast<float *>(tr + 2 * TR_HALF)[t] = sm.G[t];
+        fence_smem_to_async();
         __syncthreads();
-        // ---- the [Tb;R] image (unit u -> K-major offset u * 16) and G;
-        // Tb = T diag(beta) is applied here
-        {
-            unsigned char *tr = ws_tr + (size_t)((b * Hv + h) * nc + cl) * TR_BYTES;
-            for (int u = t; u < 128 * (CH / 8); u += PT) {
-                const int r8 = u % 8, g = (u / 8) % (CH / 8), row = (u / 64) * 8 + r8;
-                float x[8];
-                if (row < CH) {
+        // ---- R = P Tb (M = 64: rows 16 q .. 16 q + 15 in lanes 32 q .. 32 q + 15);
+        // Tb's K-major image read MN-major is Tb as the B operand (K = j, N = s)
+        if (warp == 0) {
+            if (elect_one()) {
+                const uint32_t id = idesc(64, CH, BF16, false, true);
 #pragma unroll
-                    for (int e = 0; e < 8; ++e) x[e] = Tm[row * LDP + 8 * g + e] * sm.beta[8 * g + e];
-                } else {
-#pragma unroll
-                    for (int e = 0; e < 8; ++e) x[e] = R[(row - CH) * LDP + 8 * g + e];
+                for (int ks = 0; ks < CH / 16; ++ks) {
+                    const uint64_t ah = desc_kmaj16(sm.pimg[0], CH, ks), al = desc_kmaj16(sm.pimg[1], CH, ks);
+                    const uint64_t bh = desc_mnmaj16(sm.tbimg[0], CH, ks), bl = desc_mnmaj16(sm.tbimg[1], CH, ks);
+                    mma_f16(tm + PCOL_R, ah, bh, id, ks > 0);
+                    mma_f16(tm + PCOL_R, ah, bl, id, true);
+                    mma_f16(tm + PCOL_R, al, bh, id, true);
                 }
-                uint4 hh, ll;
-                split8(x, hh, ll);
-                *reinterpret_cast<uint4 *>(tr + (size_t)u * 16) = hh;
-                *reinterpret_cast<uint4 *>(tr + TR_HALF + (size_t)u * 16) = ll;
+                commit(&sm.bar_r);
             }
-            if (t < CH) reinterpret_cast<float *>(tr + 2 * TR_HALF)[t] = sm.G[t];
+            __syncwarp();
         }
-        __syncthreads();  // A, P, T, R, G are rewritten by the next value head
+        const bool ok_r = wait_w(&sm.bar_r, (uint32_t)gi & 1, err);
+        if (__syncthreads_or(!ok_r)) break;
+        fence_after_sync();
+        // ---- R: the bottom half of the [Tb;R] image
+        {
+            float v[32];
+            ld32(tm + lq + PCOL_R + 32 * hh, v);
+            if (lane < 16) {
+                const int r = 16 * q4 + lane;
+#pragma unroll
+                for (int j = 0; j < 4; ++j) {
+                    uint4 hv, lv;
+                    split8(&v[8 * j], hv, lv);
+                    const uint32_t off = kmaj16(CH + r, 32 * hh + 8 * j, CH);
+                    *reinterpret_cast<uint4 *>(tr + off) = hv;
+                    *reinterpret_cast<uint4 *>(tr + TR_HALF + off) = lv;
+                }
+            }
+        }
+        fence_before_sync();
+        __syncthreads();  // the next value head rewrites A, T, X, the images and the R accumulator
     }
+    // every MMA has completed before the TMEM goes
+    if (warp == 0) {
+        if (elect_one()) commit(&sm.bar_fin);
+        __syncwarp();
+        wait_w(&sm.bar_fin, 0, err);
+    }
+    fence_before_sync();
+    __syncthreads();
+    fence_after_sync();
+    if (warp == 0) tmem_dealloc(tm, PTM_COLS);
 }
 
 // ============================================================ recurrence
@@ -723,7 +742,7 @@ int launch_chunk_tc32(const kai_gdn_chunk_args *a, cudaStream_t st) {
     for (long long c_begin = 0; c_begin < nch; c_begin += seg) {
         const int nc = (int)(nch - c_begin < seg ? nch - c_begin : seg);
         chunk_prep_kernel<<<(unsigned)(a->batch * a->heads_k * nc), PT, sizeof(PrepSmem), st>>>(*a, kq, tr, c_begin,
-                                                                                                 nc);
+                                                                                                 nc, err);
         if ((rc = check_launch("chunk_tc32_prep"))) return rc;
         switch (a->state_dtype) {
             case KAI_GDN_BF16: rc = launch_rec<KAI_GDN_BF16>(a, kq, tr, c_begin, nc, err, st); break;
