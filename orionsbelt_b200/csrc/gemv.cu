@@ -272,8 +272,7 @@ __global__ void __launch_bounds__(GNT) gemv_int8_kernel(const __grid_constant__ 
         const int m = e / TC, c = e % TC;
         const long long n = tile0 + c;
         if (m >= M || n >= N) continue;
-        float v = 0.f;
-        for (int k = 0; k < ksplit; ++k) v += __ldcg(part + ((long long)k * M + m) * N + n);
+        const float v = sum_parts_ordered(part + (long long)m * N + n, (long long)M * N, ksplit);
         C[(long long)m * N + n] = v * s[n];
     }
     if (t == 0) ctr[blockIdx.x] = 0u;

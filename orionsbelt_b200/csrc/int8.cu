@@ -229,8 +229,7 @@ __global__ void __launch_bounds__(NT)
     for (long long i = t; i < M * SW; i += NT) {
         const long long m = i / SW, col = slab * SW + i % SW;
         if (col >= N) continue;
-        float v = 0.0f;
-        for (int r = 0; r < ksplit; ++r) v += __ldcg(part + ((long long)r * M + m) * N + col);
+        const float v = sum_parts_ordered(part + (long long)m * N + col, (long long)M * N, ksplit);
         C[m * N + col] = v * s[col];
     }
     if (t == 0) ctr[slab] = 0u;  // ready for the next call on this stream
@@ -354,8 +353,7 @@ __global__ void __launch_bounds__(NT, 1)
     for (long long i = t; i < M * SW16; i += NT) {
         const long long m = i / SW16, col = slab * SW16 + i % SW16;
         if (col >= N) continue;
-        float v = 0.0f;
-        for (int r = 0; r < ksplit; ++r) v += __ldcg(part + ((long long)r * M + m) * N + col);
+        const float v = sum_parts_ordered(part + (long long)m * N + col, (long long)M * N, ksplit);
         C[m * N + col] = v * s[col];
     }
     if (t == 0) ctr[slab] = 0u;

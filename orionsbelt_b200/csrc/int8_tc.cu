@@ -278,8 +278,7 @@ __global__ void __launch_bounds__(TCT, 1)
         for (int i = wh; i < MT; i += TCT / 128) {
             const long long m = m0 + i;
             if (m >= M) break;
-            float v = 0.0f;
-            for (int r = 0; r < ksplit; ++r) v += __ldcg(part + ((long long)r * M + m) * N + n);
+            const float v = sum_parts_ordered(part + (long long)m * N + n, (long long)M * N, ksplit);
             C[m * N + n] = v * s[n];
         }
     }
