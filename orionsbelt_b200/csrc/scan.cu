@@ -241,7 +241,7 @@ __global__ void __launch_bounds__(256) zero_records_kernel(uint4 *p, size_t n16)
 }
 
 template <int OP, int ODT, int SDT, int VEC, int RPW, int W>
-__global__ void __launch_bounds__(32 * W, 16 / W) scan_lookback_kernel(ScanParams p, Lookback lb) {
+__global__ void __launch_bounds__(32 * W, W < 16 ? 16 / W : 1) scan_lookback_kernel(ScanParams p, Lookback lb) {
     asm volatile("griddepcontrol.wait;" ::: "memory");  // the records are zero
     static_assert(VEC == 1, "one channel per lane: the look-back record is one 16-byte word");
     constexpr int NIN = Nin<OP>::n, TROWS = W * RPW, TC = 32 * VEC;
@@ -427,6 +427,15 @@ struct Geo {
 // independent chains in flight per SM.  The allocation-free entry point uses
 // it too, so its scratch bound is fixed.
 template <int OP> constexpr Geo narrow_geo() { return {1, OP == GDN2 ? 16 : 32, 8}; }
+// With few independent chains (batch x 32-channel groups) the chains' tiles
+// mostly wait on one another: each round of a look-back reads one record per
+// warp, so a tile far down a chain of 256-row tiles walks many dependent
+// rounds (cumsum at 8 x 32768 x 32: 128 tiles per chain).  One-input scans
+// then take 1024-row tiles (32 warps x 32 rows): a quarter of the tiles per
+// chain, and 32 records per round.  Fewer tiles also means fewer records, so
+// the scratch bound of the narrow geometry still holds.
+constexpr long long TALL_CHAINS = 32;
+template <int OP> constexpr Geo tall_geo() { return {1, 32, 32}; }
 
 // Scratch bytes of a look-back launch: the ticket, then the records.
 size_t lookback_bytes(size_t batch, long long seq, long long ch, Geo g) {
@@ -474,6 +483,12 @@ int run_scan_with(ScanParams p, size_t batch, cudaStream_t st, const char *name,
         if (gx > 0x7fffffffll) return set_error(KAI_GDN_ERR_UNSUPPORTED, "%s: too many channels", name);
         scan_walk_kernel<OP, ODT, SDT><<<dim3((unsigned)gx, 1, (unsigned)batch), dim3(32, 8), 0, st>>>(p);
         return check_launch(name);
+    }
+    if constexpr (Nin<OP>::n == 1) {
+        if ((long long)batch * ((p.ch + 31) / 32) < TALL_CHAINS) {
+            constexpr Geo t = tall_geo<OP>();
+            return launch_lookback<OP, ODT, SDT, t.vec, t.rpw, t.w>(p, batch, st, name, scratch);
+        }
     }
     constexpr Geo g = narrow_geo<OP>();
     return launch_lookback<OP, ODT, SDT, g.vec, g.rpw, g.w>(p, batch, st, name, scratch);
