@@ -423,7 +423,12 @@ KAI_GDN_API int kai_gdn_model_destroy(void *engine);
  * rounding, to applying the decode step above for t = 0 .. seq-1 with
  * g, beta taken per token.  The reference names this form
  * (docs/GDN_ARCHITECTURE_AUDIT.md:142-153) and reaches it only through HF
- * transformers' torch_chunk_gated_delta_rule. */
+ * transformers' torch_chunk_gated_delta_rule.
+ * fp32 q/k/v at dk = 128 (16-byte aligned q, k, v, o; dv a multiple of 32)
+ * run on the tensor cores in two launches whose per-chunk operands go through
+ * library scratch of the stream (at most 256 MiB, allocated on the first call
+ * that needs it on that stream and kept; a longer sequence runs in segments);
+ * bf16 / fp16 inputs and other head sizes use no scratch. */
 typedef struct kai_gdn_chunk_args {
     const void *q;     /* [batch][seq][heads_k][dk], in_dtype             */
     const void *k;     /* [batch][seq][heads_k][dk], in_dtype             */
