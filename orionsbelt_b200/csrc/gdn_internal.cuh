@@ -82,8 +82,11 @@ int launch_gemv_int8(const float *A, const int8_t *q, const float *s, float *C, 
 // gemv_block_weights from [K][N]; gemv_blocked_bytes bytes).
 size_t gemv_blocked_bytes(size_t M, size_t K, size_t N);
 int gemv_block_weights(size_t M, const int8_t *q, int8_t *qb, size_t K, size_t N, cudaStream_t st);
+// swiglu: A is [M][2K], rows [gate | up], and the GEMV's activations are
+// SiLU(gate) * up (the FFN down projection takes its input straight from the
+// gate+up output, one launch fewer).
 int launch_gemv_int8_blocked(const float *A, const int8_t *qb, const float *s, float *C, size_t M, size_t K,
-                             size_t N, cudaStream_t st);
+                             size_t N, cudaStream_t st, bool swiglu = false);
 int launch_matmul_int8_tc(const float *A, const int8_t *q, const float *s, float *C, size_t M, size_t K, size_t N,
                           cudaStream_t st);
 // Weight-streaming tensor-core matmul over weights packed once into its

@@ -117,7 +117,7 @@ __global__ void __launch_bounds__(GNT) gemv_int8_kernel(const __grid_constant__ 
                                                         const float *__restrict__ A, const float *__restrict__ s,
                                                         float *__restrict__ C, int M, long long K, long long N,
                                                         long long kper, float *__restrict__ part,
-                                                        unsigned int *__restrict__ ctr, int *err) {
+                                                        unsigned int *__restrict__ ctr, int *err, int swiglu) {
     using G = GemvGeo<CPL>;
     constexpr int TC = G::TC, STAGE = G::STAGE, NSTG = G::NSTG;
     extern __shared__ unsigned char dsm_raw[];
@@ -186,7 +186,16 @@ __global__ void __launch_bounds__(GNT) gemv_int8_kernel(const __grid_constant__ 
         for (long long e = t; e < (long long)MB * kn; e += GW * 32) {
             const int m = (int)(e / kn);
             const long long k = e % kn;
-            sm_a[k * MB + m] = m < M ? A[(long long)m * K + k0 + k] : 0.f;
+            float a = 0.f;
+            if (m < M) {
+                if (swiglu) {  // rows [gate (K) | up (K)]: SiLU(gate) * up, the FFN activation
+                    const float gv = A[(long long)m * 2 * K + k0 + k];
+                    a = gv / (1.0f + expf(-gv)) * A[(long long)m * 2 * K + K + k0 + k];
+                } else {
+                    a = A[(long long)m * K + k0 + k];
+                }
+            }
+            sm_a[k * MB + m] = a;
         }
         asm volatile("bar.sync 1, %0;" ::"n"(GW * 32) : "memory");
         float2 acc[MB][CPL / 2];
@@ -331,7 +340,7 @@ int gemv_workspace(cudaStream_t st, size_t nctr, size_t npart, unsigned int **ct
 
 template <int MB, bool BLK>
 int run_gemv(const float *A, const int8_t *q, const float *s, float *Cm, int M, long long K, long long N,
-             cudaStream_t st) {
+             cudaStream_t st, bool swiglu) {
     constexpr int CPL = GemvCpl<MB>::CPL;
     using G = GemvGeo<CPL>;
     auto kern = gemv_int8_kernel<MB, CPL, BLK>;
@@ -394,19 +403,19 @@ int run_gemv(const float *A, const int8_t *q, const float *s, float *Cm, int M, 
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    const cudaError_t le = cudaLaunchKernelEx(&cfg, kern, map, q, A, s, Cm, M, K, N, kper, part, ctr, err);
+    const cudaError_t le = cudaLaunchKernelEx(&cfg, kern, map, q, A, s, Cm, M, K, N, kper, part, ctr, err, swiglu ? 1 : 0);
     if (le != cudaSuccess) return check_cuda(le, "gemv_int8_kernel launch");
     return check_launch("gemv_int8_kernel");
 }
 
 template <bool BLK>
 int dispatch_gemv(const float *A, const int8_t *q, const float *s, float *Cm, size_t M, size_t K, size_t N,
-                  cudaStream_t st) {
+                  cudaStream_t st, bool swiglu = false) {
     const long long k = (long long)K, n = (long long)N;
-    if (M == 1) return run_gemv<1, BLK>(A, q, s, Cm, 1, k, n, st);
-    if (M == 2) return run_gemv<2, BLK>(A, q, s, Cm, 2, k, n, st);
-    if (M <= 4) return run_gemv<4, BLK>(A, q, s, Cm, (int)M, k, n, st);
-    return run_gemv<8, BLK>(A, q, s, Cm, (int)M, k, n, st);
+    if (M == 1) return run_gemv<1, BLK>(A, q, s, Cm, 1, k, n, st, swiglu);
+    if (M == 2) return run_gemv<2, BLK>(A, q, s, Cm, 2, k, n, st, swiglu);
+    if (M <= 4) return run_gemv<4, BLK>(A, q, s, Cm, (int)M, k, n, st, swiglu);
+    return run_gemv<8, BLK>(A, q, s, Cm, (int)M, k, n, st, swiglu);
 }
 
 }  // namespace
@@ -458,11 +467,11 @@ int gemv_block_weights(size_t M, const int8_t *q, int8_t *qb, size_t K, size_t N
 }
 
 int launch_gemv_int8_blocked(const float *A, const int8_t *qb, const float *s, float *Cm, size_t M, size_t K,
-                             size_t N, cudaStream_t st) {
+                             size_t N, cudaStream_t st, bool swiglu) {
     if (M == 0 || N == 0) return KAI_GDN_OK;
     if (!A || !qb || !s || !Cm) return set_error(KAI_GDN_ERR_INVALID, "gemv_int8: null pointer");
     if (!gemv_int8_supported(M, K, N, qb)) return set_error(KAI_GDN_ERR_UNSUPPORTED, "gemv_int8: shape");
-    return dispatch_gemv<true>(A, qb, s, Cm, M, K, N, st);
+    return dispatch_gemv<true>(A, qb, s, Cm, M, K, N, st, swiglu);
 }
 
 }  // namespace gdn

@@ -696,6 +696,8 @@ int swiglu_mm(ModelEngine *e, const QW &w, float *Cm, cudaStream_t st) {
                              I * sizeof(float), st, e->gu, (long long)I, kstages(I), e->terms, e->tscale);
         return rc ? rc : terms_mm(e, w, Cm, st);
     }
+    if (w.qb && B <= GEMV_MAX_BATCH)  // the GEMV applies SiLU(gate) * up as it loads its activations
+        return launch_gemv_int8_blocked(e->gu, w.qb, w.s, Cm, B, w.K, w.N, st, true);
     rc = launch_pdl("swiglu_kernel", swiglu_kernel, dim3(grid_for((long long)(B * I))), dim3(256), st, e->gu, e->act,
                     (long long)I, (long long)(B * I));
     return rc ? rc : mm(e->act, w, Cm, B, st);
