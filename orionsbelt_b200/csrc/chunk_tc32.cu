@@ -193,6 +193,9 @@ __global__ void __launch_bounds__(PT, 2)
     const long long cl = blockIdx.x % nc, bh = blockIdx.x / nc;  // bh = b * Hk + hk
     const long long b = bh / Hk, hk = bh % Hk;
     const long long c0 = (c_begin + cl) * CH;
+    // the recurrence launch may be scheduled once every CTA of this grid has
+    // started; it reads the images only after this grid has completed
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 
     if (t == 0) {
         mbar_init(&sm.bar_kk, 1);
@@ -488,6 +491,11 @@ __global__ void __launch_bounds__(RT, 1)
     if (warp == 0) {
         // ---------------------------------------------------- copy warp
         if (lane == 0) {
+            // launched as a programmatic dependent of the prep launch: its
+            // images are complete and visible after this wait (only this
+            // thread reads them from global memory; everything else here
+            // runs ahead of it)
+            asm volatile("griddepcontrol.wait;" ::: "memory");
             int issued = 0;
             for (int c = 0; c < nc; ++c) {
                 const int s = c & 1;
@@ -690,8 +698,20 @@ int launch_rec(const kai_gdn_chunk_args *a, const unsigned char *kq, const unsig
         if (rc) return rc;
         done_dev = dev;
     }
-    const unsigned blocks = (unsigned)(a->batch * a->heads_v * (a->dv / NV));
-    chunk_rec_kernel<SDT><<<blocks, RT, sizeof(RecSmem), st>>>(*a, kq, tr, c_begin, nc, err);
+    // a programmatic dependent of the prep launch before it: set-up, the
+    // state load and TMEM allocation overlap the prep's last CTAs
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = dim3((unsigned)(a->batch * a->heads_v * (a->dv / NV)));
+    cfg.blockDim = dim3(RT);
+    cfg.dynamicSmemBytes = sizeof(RecSmem);
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    const cudaError_t le = cudaLaunchKernelEx(&cfg, chunk_rec_kernel<SDT>, *a, kq, tr, c_begin, nc, err);
+    if (le != cudaSuccess) return check_cuda(le, "chunk_tc32_rec launch");
     return check_launch("chunk_tc32_rec");
 }
 
