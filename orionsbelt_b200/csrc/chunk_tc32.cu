@@ -7,8 +7,9 @@
 //   A  = beta_r (k_r . k_s) e^{G_r - G_s}          s <  r
 //   P  = scale (q_r . k_s) e^{G_r - G_s}           s <= r
 //   Tb = (I + A)^-1 diag(beta),   R = P Tb
-//   V'' = V - e^G (K S),   V' = Tb V'',   O = scale e^G (Q S) + R V''  (= P V')
-//   S  <- e^{G_63} S + K^T (e^{G_63 - G} V')
+//   V'' = V - e^G (K S),   O = scale e^G (Q S) + R V''  (= P V', V' = Tb V'')
+//   S  <- e^{G_63} S + K^T (e^{G_63 - G} Tb V'') = e^{G_63} S + W^T V'',
+//         W = Tb'^T K with Tb' = diag(e^{G_63 - G}) Tb
 //
 // Precision: every product runs as three bf16 MMAs, hi*hi + hi*lo + lo*hi,
 // with each operand split x = hi + lo (hi = bf16(x), lo = bf16(x - hi)), so
@@ -18,27 +19,26 @@
 //
 // Two launches per segment of chunks:
 //  * chunk_prep_kernel -- one CTA per (b, key head, chunk), all chunks at
-//    once (nothing here depends on the state): K K^T and Q K^T, then for each
-//    value head of the group A and P, the inverse by substitution, Tb and
-//    R = P Tb, all in fp32 on the CUDA cores.  It writes the MMA operand
-//    images into a workspace, exactly as the recurrence's shared memory holds
-//    them (no-swizzle K-major core-matrix layout, bf16 hi then lo):
-//      [K;Q]   128 rows (64 of k, 64 of q) x 128 features      65536 bytes
-//      [Tb;R]  128 rows (64 of Tb, 64 of R) x 64 tokens + G    33024 bytes
+//    once (nothing here depends on the state): K K^T and Q K^T on tcgen05,
+//    then for each value head of the group A and P, the blocked inverse on the
+//    CUDA cores, Tb, R = P Tb and W = Tb'^T K on tcgen05.  It writes the MMA
+//    operand images into a workspace, exactly as the recurrence's shared
+//    memory holds them (no-swizzle K-major core-matrix layout, bf16 hi then lo):
+//      [K;Q]          128 rows (64 of k, 64 of q) x 128 features      65536 bytes
+//      [Tb;R], G, W   128 rows x 64 tokens, G, 64 rows x 128 features 65792 bytes
 //  * chunk_rec_kernel -- one CTA per (b, value head, 32 value columns).  The
-//    value columns of the state evolve independently (V' = Tb V'' and the
-//    update are column-wise), so the 32-column blocks are exact splits; the
-//    state block S (128 keys x 32 values, fp32) lives in TMEM.  Per chunk,
-//    three MMA batches (M = 128, N = 32) on one warp:
+//    value columns of the state evolve independently, so the 32-column
+//    blocks are exact splits; the state block S (128 keys x 32 values, fp32)
+//    lives in TMEM.  Per chunk, on one MMA warp (M = 128, N = 32):
 //      D_a  = [K;Q] S      K = 128   rows 0-63: K S, rows 64-127: Q S
-//      D_b  = [Tb;R] V''   K = 64    rows 0-63: V',  rows 64-127: R V''
-//      S   += K^T V'_s     K = 64    A = the K half of [K;Q] read MN-major
-//    and between them element-wise passes on four warps (TMEM lane quarters):
-//    V'' and its split (rows 0-63), V'_s = e^{G_63-G} V' and its split, the
-//    output rows (64-127), and the state pass (all 128 lanes: the split
-//    copy of S for the next D_a, then S *= e^{G_63} of the next chunk, back
-//    into TMEM).  One warp issues the bulk copies of the next chunks' images
-//    into a two-deep ring.
+//      S   += W^T V''      K = 64    A = W's image read MN-major
+//      D_b  = [Tb;R] V''   K = 64    rows 64-127: R V'' (for the output only)
+//    so the state's chain is two MMA batches and two element-wise passes:
+//    V'' and its split (warps 4, 5: rows 0-63), and the state pass (all four
+//    warps: the split copy of S for the next D_a, then S *= e^{G_63} of the
+//    next chunk, back into TMEM); the output rows (warps 6, 7: Q S and R V'')
+//    are written after it.  One warp issues the bulk copies: [K;Q] into a
+//    single slot as soon as D_a is done with it, [Tb;R], G, W two chunks deep.
 //
 // Long sequences run in segments of chunks whose images fit a bounded
 // workspace; the state goes through the state buffer between segments.
@@ -56,7 +56,9 @@ constexpr int NV = 32;                       // value columns per recurrence CTA
 constexpr int KQ_HALF = 128 * DK * 2;        // one bf16 [K;Q] image
 constexpr int KQ_BYTES = 2 * KQ_HALF;        // hi + lo
 constexpr int TR_HALF = 128 * CH * 2;        // one bf16 [Tb;R] image
-constexpr int TR_BYTES = 2 * TR_HALF + CH * 4;  // hi + lo + G
+constexpr int WK_OFF = 2 * TR_HALF + CH * 4;   // after [Tb;R] hi, lo and G: the W image
+constexpr int WK_HALF = CH * DK * 2;           // one bf16 W image (64 tokens x 128 features)
+constexpr int TR_BYTES = WK_OFF + 2 * WK_HALF;  // [Tb;R] hi + lo, G, W hi + lo
 constexpr size_t SEG_BUDGET = 256ull << 20;  // workspace bound per launch
 
 // ---------------------------------------------------------------- helpers
@@ -163,7 +165,7 @@ __device__ __forceinline__ void store32(void *base, size_t idx, int dt, const fl
 // ================================================================ prep
 constexpr int PT = 256;  // threads
 constexpr int LDP = 65;  // 64 x 64 fp32 work matrices
-constexpr uint32_t PCOL_KK = 0, PCOL_R = 64, PTM_COLS = 128;
+constexpr uint32_t PCOL_KK = 0, PCOL_R = 64, PCOL_W = 128, PTM_COLS = 256;
 
 struct PrepSmem {
     union {
@@ -178,7 +180,7 @@ struct PrepSmem {
     unsigned char tbimg[2][CH * CH * 2];  // Tb (hi, lo): read MN-major as its B operand
     float G[CH];
     float beta[CH];
-    uint64_t bar_kk, bar_r, bar_fin;
+    uint64_t bar_kk, bar_r, bar_k, bar_w, bar_fin;
     uint32_t tmem;
 };
 
@@ -200,6 +202,8 @@ __global__ void __launch_bounds__(PT, 2)
     if (t == 0) {
         mbar_init(&sm.bar_kk, 1);
         mbar_init(&sm.bar_r, 1);
+        mbar_init(&sm.bar_k, 1);
+        mbar_init(&sm.bar_w, 1);
         mbar_init(&sm.bar_fin, 1);
     }
     if (warp == 0) tmem_alloc(&sm.tmem, PTM_COLS);
@@ -234,6 +238,8 @@ __global__ void __launch_bounds__(PT, 2)
             *reinterpret_cast<uint4 *>(kq + (size_t)u * 16) = hv;
             *reinterpret_cast<uint4 *>(kq + KQ_HALF + (size_t)u * 16) = lv;
         }
+        // the K half is copied back in by a bulk copy later (async proxy)
+        asm volatile("fence.proxy.async.global;" ::: "memory");
     }
     fence_smem_to_async();
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
@@ -365,19 +371,29 @@ __global__ void __launch_bounds__(PT, 2)
             __syncthreads();
         }
         // ---- Tb = T diag(beta): the top half of the [Tb;R] image in the
-        // workspace, and in shared memory the B operand of R = P Tb
+        // workspace, and in shared memory the B operand of R = P Tb; beside
+        // it (in the inverse's scratch, dead now) Tb' = diag(e^{G_63 - G}) Tb,
+        // the A operand of W = Tb'^T K
         unsigned char *tr = ws_tr + (size_t)((b * Hv + h) * nc + cl) * TR_BYTES;
+        unsigned char *tbp = reinterpret_cast<unsigned char *>(X);
         for (int u = t; u < CH * (CH / 8); u += PT) {
             const int row = (u / 64) * 8 + u % 8, g = (u / 8) % (CH / 8);  // K-major offset u * 16
-            float x[8];
+            const float el = expf(sm.G[CH - 1] - sm.G[row]);
+            float x[8], y[8];
 #pragma unroll
-            for (int e = 0; e < 8; ++e) x[e] = Tm[row * LDP + 8 * g + e] * sm.beta[8 * g + e];
+            for (int e = 0; e < 8; ++e) {
+                x[e] = Tm[row * LDP + 8 * g + e] * sm.beta[8 * g + e];
+                y[e] = x[e] * el;
+            }
             uint4 hv, lv;
             split8(x, hv, lv);
             *reinterpret_cast<uint4 *>(sm.tbimg[0] + u * 16) = hv;
             *reinterpret_cast<uint4 *>(sm.tbimg[1] + u * 16) = lv;
             *reinterpret_cast<uint4 *>(tr + (size_t)u * 16) = hv;
             *reinterpret_cast<uint4 *>(tr + TR_HALF + (size_t)u * 16) = lv;
+            split8(y, hv, lv);
+            *reinterpret_cast<uint4 *>(tbp + u * 16) = hv;
+            *reinterpret_cast<uint4 *>(tbp + CH * CH * 2 + u * 16) = lv;
         }
         if (t < CH) reinterpret_cast<float *>(tr + 2 * TR_HALF)[t] = sm.G[t];
         fence_smem_to_async();
@@ -402,6 +418,14 @@ __global__ void __launch_bounds__(PT, 2)
         const bool ok_r = wait_w(&sm.bar_r, (uint32_t)gi & 1, err);
         if (__syncthreads_or(!ok_r)) break;
         fence_after_sync();
+        // K's image back into the P / Tb images' space (P Tb is done with
+        // them) for W below; the copy overlaps R's readout
+        if (t == 0) {
+            const unsigned char *kq = ws_kq + (size_t)(bh * nc + cl) * KQ_BYTES;
+            mbar_arrive_expect_tx(&sm.bar_k, 2 * CH * DK * 2);
+            bulk_load(sm.pimg[0], kq, CH * DK * 2, &sm.bar_k);
+            bulk_load(sm.tbimg[0], kq + KQ_HALF, CH * DK * 2, &sm.bar_k);
+        }
         // ---- R: the bottom half of the [Tb;R] image
         {
             float v[32];
@@ -419,7 +443,53 @@ __global__ void __launch_bounds__(PT, 2)
             }
         }
         fence_before_sync();
-        __syncthreads();  // the next value head rewrites A, T, X, the images and the R accumulator
+        __syncthreads();
+        // ---- W = Tb'^T K (M = 64 tokens j, N = 128 features, K = 64 tokens r),
+        // so that the recurrence's state update is S += W^T V'' straight from
+        // V''.  K's image (hi, lo: the first 16 KB of each half of this chunk's
+        // [K;Q] image, written above, copied back before R's readout): read
+        // MN-major it is K as the B operand, and Tb''s K-major image read
+        // MN-major is Tb'^T as the A operand.
+        const bool ok_k = wait_w(&sm.bar_k, (uint32_t)gi & 1, err);
+        if (__syncthreads_or(!ok_k)) break;
+        if (warp == 0) {
+            if (elect_one()) {
+                const uint32_t id = idesc(64, DK, BF16, true, true);
+#pragma unroll
+                for (int ks = 0; ks < CH / 16; ++ks) {
+                    const uint64_t ah = desc_mnmaj16(tbp, CH, ks), al = desc_mnmaj16(tbp + CH * CH * 2, CH, ks);
+                    const uint64_t bh = desc_mnmaj16(sm.pimg[0], DK, ks), bl = desc_mnmaj16(sm.tbimg[0], DK, ks);
+                    mma_f16(tm + PCOL_W, ah, bh, id, ks > 0);
+                    mma_f16(tm + PCOL_W, ah, bl, id, true);
+                    mma_f16(tm + PCOL_W, al, bh, id, true);
+                }
+                commit(&sm.bar_w);
+            }
+            __syncwarp();
+        }
+        const bool ok_w = wait_w(&sm.bar_w, (uint32_t)gi & 1, err);
+        if (__syncthreads_or(!ok_w)) break;
+        fence_after_sync();
+        // ---- W's image (K-major, rows j, 128 features) after [Tb;R] and G;
+        // M = 64: row 16 q + lane in lane 32 q + lane (lane < 16)
+#pragma unroll
+        for (int half = 0; half < 2; ++half) {
+            float v[32];
+            ld32(tm + lq + PCOL_W + 64 * hh + 32 * half, v);
+            if (lane < 16) {
+                const int r = 16 * q4 + lane;
+#pragma unroll
+                for (int j = 0; j < 4; ++j) {
+                    uint4 hv, lv;
+                    split8(&v[8 * j], hv, lv);
+                    const uint32_t off = kmaj16(r, 64 * hh + 32 * half + 8 * j, DK);
+                    *reinterpret_cast<uint4 *>(tr + WK_OFF + off) = hv;
+                    *reinterpret_cast<uint4 *>(tr + WK_OFF + WK_HALF + off) = lv;
+                }
+            }
+        }
+        fence_before_sync();
+        __syncthreads();  // the next value head rewrites A, T, X, the images and the accumulators
     }
     // every MMA has completed before the TMEM goes
     if (warp == 0) {
@@ -438,13 +508,12 @@ constexpr int RT = 256;  // warp 0 copies, warp 1 MMAs, warps 4-7 passes
 constexpr uint32_t COL_A = 0, COL_B = 32, COL_S = 64, TM_COLS = 128;
 
 struct RecSmem {
-    unsigned char kq[2][KQ_BYTES];
-    unsigned char tr[2][TR_BYTES];
+    unsigned char kq[KQ_BYTES];           // [K;Q]: D_a(c) is done with it before chunk c+1's arrives
+    unsigned char tr[2][TR_BYTES];        // [Tb;R], G, W: two-deep ring
     unsigned char s_op[2][128 * NV * 2];  // state, MN-major B operand (hi, lo)
-    unsigned char vpp[2][CH * NV * 2];    // V''
-    unsigned char vp[2][CH * NV * 2];     // V'_s
-    uint64_t kq_full[2], kq_empty[2], tr_full[2], tr_empty[2];
-    uint64_t bar_a, bar_b, bar_c, bar_s, bar_vpp, bar_vp, bar_fin;
+    unsigned char vpp[2][CH * NV * 2];    // V'', MN-major B operand of the update and of D_b
+    uint64_t kq_full, kq_empty, tr_full[2], tr_empty[2];
+    uint64_t bar_a, bar_b, bar_c, bar_s, bar_vpp, bar_o, bar_fin;
     uint32_t tmem;
 };
 static_assert(sizeof(RecSmem) <= 232448, "recurrence shared memory");
@@ -467,9 +536,9 @@ __global__ void __launch_bounds__(RT, 1)
     const unsigned char *tr_src = ws_tr + (size_t)(unit * nc) * TR_BYTES;
 
     if (t == 0) {
+        mbar_init(&sm.kq_full, 1);
+        mbar_init(&sm.kq_empty, 1);
         for (int s = 0; s < 2; ++s) {
-            mbar_init(&sm.kq_full[s], 1);
-            mbar_init(&sm.kq_empty[s], 1);
             mbar_init(&sm.tr_full[s], 1);
             mbar_init(&sm.tr_empty[s], 1 + 128);  // the D_b commit and the 128 readers of G
         }
@@ -479,7 +548,7 @@ __global__ void __launch_bounds__(RT, 1)
         mbar_init(&sm.bar_fin, 1);
         mbar_init(&sm.bar_s, 128);
         mbar_init(&sm.bar_vpp, 64);
-        mbar_init(&sm.bar_vp, 64);
+        mbar_init(&sm.bar_o, 64);
     }
     if (warp == 1) tmem_alloc(&sm.tmem, TM_COLS);
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
@@ -496,49 +565,75 @@ __global__ void __launch_bounds__(RT, 1)
             // thread reads them from global memory; everything else here
             // runs ahead of it)
             asm volatile("griddepcontrol.wait;" ::: "memory");
-            int issued = 0;
-            for (int c = 0; c < nc; ++c) {
-                const int s = c & 1;
-                const uint32_t use = (uint32_t)(c >> 1);
-                if (use > 0 && !mbar_wait(&sm.kq_empty[s], (use - 1) & 1, err)) break;
-                mbar_arrive_expect_tx(&sm.kq_full[s], KQ_BYTES);
-                bulk_load(sm.kq[s], kq_src + (size_t)c * KQ_BYTES, KQ_BYTES, &sm.kq_full[s]);
-                if (use > 0 && !mbar_wait(&sm.tr_empty[s], (use - 1) & 1, err)) {
-                    mbar_wait(&sm.kq_full[s], use & 1, err);  // the copy just issued lands first
-                    break;
+            // [K;Q](c) as soon as D_a(c-1) is done with the single slot;
+            // [Tb;R, G, W](c+1) as soon as its slot's chunk c-1 is released
+            int kq_n = 0, tr_n = 0;
+            bool ok = true;
+            mbar_arrive_expect_tx(&sm.tr_full[0], TR_BYTES);
+            bulk_load(sm.tr[0], tr_src, TR_BYTES, &sm.tr_full[0]);
+            tr_n = 1;
+            for (int c = 0; c < nc && ok; ++c) {
+                if (c > 0 && !(ok = mbar_wait(&sm.kq_empty, (uint32_t)(c - 1) & 1, err))) break;
+                mbar_arrive_expect_tx(&sm.kq_full, KQ_BYTES);
+                bulk_load(sm.kq, kq_src + (size_t)c * KQ_BYTES, KQ_BYTES, &sm.kq_full);
+                kq_n = c + 1;
+                const int cn = c + 1;
+                if (cn < nc) {
+                    const int sn = cn & 1;
+                    if (cn >= 2 && !(ok = mbar_wait(&sm.tr_empty[sn], (uint32_t)((cn >> 1) - 1) & 1, err))) break;
+                    mbar_arrive_expect_tx(&sm.tr_full[sn], TR_BYTES);
+                    bulk_load(sm.tr[sn], tr_src + (size_t)cn * TR_BYTES, TR_BYTES, &sm.tr_full[sn]);
+                    tr_n = cn + 1;
                 }
-                mbar_arrive_expect_tx(&sm.tr_full[s], TR_BYTES);
-                bulk_load(sm.tr[s], tr_src + (size_t)c * TR_BYTES, TR_BYTES, &sm.tr_full[s]);
-                issued = c + 1;
             }
             // no copy may still be landing when the CTA leaves
-            for (int c = issued - 2 < 0 ? 0 : issued - 2; c < issued; ++c) {
-                mbar_wait(&sm.kq_full[c & 1], (c >> 1) & 1, err);
-                mbar_wait(&sm.tr_full[c & 1], (c >> 1) & 1, err);
-            }
+            if (kq_n > 0) mbar_wait(&sm.kq_full, (uint32_t)(kq_n - 1) & 1, err);
+            for (int c = tr_n - 2 < 0 ? 0 : tr_n - 2; c < tr_n; ++c)
+                mbar_wait(&sm.tr_full[c & 1], (uint32_t)(c >> 1) & 1, err);
         }
     } else if (warp == 1) {
         // ----------------------------------------------------- MMA warp
         const uint32_t id_n = idesc(128, NV, BF16, false, true);  // A K-major, B MN-major
-        const uint32_t id_t = idesc(128, NV, BF16, true, true);   // A = K^T, MN-major
+        const uint32_t id_t = idesc(128, NV, BF16, true, true);   // A = W^T, MN-major
         for (int c = 0; c < nc; ++c) {
             const int s = c & 1;
             const uint32_t ph = (uint32_t)(c >> 1) & 1, pc = (uint32_t)c & 1;
-            if (!wait_w(&sm.kq_full[s], ph, err) || !spin_w(&sm.bar_s, pc, err)) break;
+            if (!wait_w(&sm.kq_full, pc, err) || !spin_w(&sm.bar_s, pc, err)) break;
             fence_after_sync();
+            // D_a = [K;Q] S
             if (elect_one()) {
 #pragma unroll
                 for (int ks = 0; ks < DK / 16; ++ks) {
-                    const uint64_t ah = desc_kmaj16(sm.kq[s], DK, ks), al = desc_kmaj16(sm.kq[s] + KQ_HALF, DK, ks);
+                    const uint64_t ah = desc_kmaj16(sm.kq, DK, ks), al = desc_kmaj16(sm.kq + KQ_HALF, DK, ks);
                     const uint64_t bh = desc_mnmaj16(sm.s_op[0], NV, ks), bl = desc_mnmaj16(sm.s_op[1], NV, ks);
                     mma_f16(tm + COL_A, ah, bh, id_n, ks > 0);
                     mma_f16(tm + COL_A, ah, bl, id_n, true);
                     mma_f16(tm + COL_A, al, bh, id_n, true);
                 }
                 commit(&sm.bar_a);
+                commit(&sm.kq_empty);
             }
             __syncwarp();
             if (!wait_w(&sm.tr_full[s], ph, err) || !spin_w(&sm.bar_vpp, pc, err)) break;
+            fence_after_sync();
+            // the state update S += W^T V'' (W's K-major image read MN-major
+            // is W^T: M = features, K = tokens)
+            if (elect_one()) {
+                const unsigned char *wk = sm.tr[s] + WK_OFF;
+#pragma unroll
+                for (int ks = 0; ks < CH / 16; ++ks) {
+                    const uint64_t ah = desc_mnmaj16(wk, DK, ks), al = desc_mnmaj16(wk + WK_HALF, DK, ks);
+                    const uint64_t bh = desc_mnmaj16(sm.vpp[0], NV, ks), bl = desc_mnmaj16(sm.vpp[1], NV, ks);
+                    mma_f16(tm + COL_S, ah, bh, id_t, true);
+                    mma_f16(tm + COL_S, ah, bl, id_t, true);
+                    mma_f16(tm + COL_S, al, bh, id_t, true);
+                }
+                commit(&sm.bar_c);
+            }
+            __syncwarp();
+            // D_b = [Tb;R] V'' for the output (off the state's chain), once the
+            // output warps have read the previous chunk's
+            if (c > 0 && !spin_w(&sm.bar_o, pc ^ 1, err)) break;
             fence_after_sync();
             if (elect_one()) {
 #pragma unroll
@@ -553,23 +648,6 @@ __global__ void __launch_bounds__(RT, 1)
                 commit(&sm.tr_empty[s]);
             }
             __syncwarp();
-            if (!spin_w(&sm.bar_vp, pc, err)) break;
-            fence_after_sync();
-            if (elect_one()) {
-#pragma unroll
-                for (int ks = 0; ks < CH / 16; ++ks) {
-                    // the K rows of [K;Q] are the first 64; read MN-major they
-                    // are K^T (M = features, K = tokens)
-                    const uint64_t ah = desc_mnmaj16(sm.kq[s], DK, ks), al = desc_mnmaj16(sm.kq[s] + KQ_HALF, DK, ks);
-                    const uint64_t bh = desc_mnmaj16(sm.vp[0], NV, ks), bl = desc_mnmaj16(sm.vp[1], NV, ks);
-                    mma_f16(tm + COL_S, ah, bh, id_t, true);
-                    mma_f16(tm + COL_S, ah, bl, id_t, true);
-                    mma_f16(tm + COL_S, al, bh, id_t, true);
-                }
-                commit(&sm.bar_c);
-                commit(&sm.kq_empty[s]);
-            }
-            __syncwarp();
         }
         // every MMA has completed before the TMEM goes (the commit tracks all
         // MMAs this lane issued)
@@ -580,7 +658,7 @@ __global__ void __launch_bounds__(RT, 1)
         // -------------------------------------------------- pass warps
         using ST = Store<SDT>;
         const int wq = warp - 4, row = 32 * wq + lane, r = row % CH;
-        const bool vrow = row < CH;  // warps 4, 5: V'' and V'; warps 6, 7: output rows
+        const bool vrow = row < CH;  // warps 4, 5: V''; warps 6, 7: output rows
         const uint32_t loff = (uint32_t)(32 * wq) << 16;
         const uint32_t ta = tm + loff + COL_A, tb = tm + loff + COL_B, ts = tm + loff + COL_S;
         typename ST::T *st = static_cast<typename ST::T *>(p.state) + ((size_t)unit * DK + row) * DV + v0;
@@ -605,19 +683,18 @@ __global__ void __launch_bounds__(RT, 1)
             const uint32_t ph = (uint32_t)(c >> 1) & 1, pc = (uint32_t)c & 1;
             const long long tok = (c_begin + c) * CH + r;
             if (!(ok = wait_w(&sm.tr_full[s], ph, err))) break;
-            const float *Gs = reinterpret_cast<const float *>(sm.tr[s] + 2 * TR_HALF);
-            const float gr = Gs[r], gl = Gs[CH - 1];
+            const float gr = reinterpret_cast<const float *>(sm.tr[s] + 2 * TR_HALF)[r];
             mbar_arrive1(&sm.tr_empty[s]);
+            float x[NV];
             if (vrow) {
-                float v[NV];
                 if (tok < T) {
                     const float4 *vs = reinterpret_cast<const float4 *>(static_cast<const float *>(p.v) +
                                                                         ((size_t)(b * T + tok) * Hv + h) * DV + v0);
 #pragma unroll
-                    for (int j = 0; j < NV / 4; ++j) *reinterpret_cast<float4 *>(&v[4 * j]) = __ldg(vs + j);
+                    for (int j = 0; j < NV / 4; ++j) *reinterpret_cast<float4 *>(&x[4 * j]) = __ldg(vs + j);
                 } else {
 #pragma unroll
-                    for (int n = 0; n < NV; ++n) v[n] = 0.f;
+                    for (int n = 0; n < NV; ++n) x[n] = 0.f;
                 }
                 if (!(ok = spin_w(&sm.bar_a, pc, err))) break;
                 fence_after_sync();
@@ -625,33 +702,17 @@ __global__ void __launch_bounds__(RT, 1)
                 ld32(ta, ks);
                 const float eg = expf(gr);
 #pragma unroll
-                for (int n = 0; n < NV; ++n) v[n] = fmaf(-eg, ks[n], v[n]);  // V''
-                put_row_mn(sm.vpp[0], sm.vpp[1], r, v);
+                for (int n = 0; n < NV; ++n) x[n] = fmaf(-eg, ks[n], x[n]);  // V''
+                // the previous chunk's D_b has read V''
+                if (c > 0 && !(ok = spin_w(&sm.bar_b, pc ^ 1, err))) break;
+                put_row_mn(sm.vpp[0], sm.vpp[1], r, x);
                 fence_smem_to_async();
                 fence_before_sync();
                 mbar_arrive1(&sm.bar_vpp);
-                if (!(ok = spin_w(&sm.bar_b, pc, err))) break;
-                fence_after_sync();
-                ld32(tb, v);  // V'
-                const float el = expf(gl - gr);
-#pragma unroll
-                for (int n = 0; n < NV; ++n) v[n] *= el;
-                put_row_mn(sm.vp[0], sm.vp[1], r, v);
-                fence_smem_to_async();
-                fence_before_sync();
-                mbar_arrive1(&sm.bar_vp);
             } else {
-                float x[NV], y[NV];
                 if (!(ok = spin_w(&sm.bar_a, pc, err))) break;
                 fence_after_sync();
-                ld32(ta, x);  // Q S
-                if (!(ok = spin_w(&sm.bar_b, pc, err))) break;
-                fence_after_sync();
-                ld32(tb, y);  // R V''
-                const float f = p.scale * expf(gr);
-#pragma unroll
-                for (int n = 0; n < NV; ++n) x[n] = fmaf(f, x[n], y[n]);
-                if (tok < T) store32(p.o, ((size_t)(b * T + tok) * Hv + h) * DV + v0, p.out_dtype, x);
+                ld32(ta, x);  // Q S, kept until the output below
             }
             // ---- the state after this chunk
             const bool fin = c + 1 == nc;
@@ -675,6 +736,19 @@ __global__ void __launch_bounds__(RT, 1)
                 fence_smem_to_async();
                 fence_before_sync();
                 mbar_arrive1(&sm.bar_s);
+            }
+            // ---- the output rows, off the state's chain
+            if (!vrow) {
+                float y[NV];
+                if (!(ok = spin_w(&sm.bar_b, pc, err))) break;
+                fence_after_sync();
+                ld32(tb, y);  // R V''
+                fence_before_sync();
+                mbar_arrive1(&sm.bar_o);
+                const float f = p.scale * expf(gr);
+#pragma unroll
+                for (int n = 0; n < NV; ++n) x[n] = fmaf(f, x[n], y[n]);
+                if (tok < T) store32(p.o, ((size_t)(b * T + tok) * Hv + h) * DV + v0, p.out_dtype, x);
             }
         }
     }
