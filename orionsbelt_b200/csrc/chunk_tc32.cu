@@ -678,6 +678,23 @@ __global__ void __launch_bounds__(RT, 1)
             fence_before_sync();
             mbar_arrive1(&sm.bar_s);
         }
+        // V rows (warps 4, 5) are loaded a chunk ahead: with the image copies
+        // streaming, a load issued at the chunk's start was still in flight
+        // when D_a completed (~1.5K cycles on the chain)
+        float vn[NV];
+        auto load_v = [&](int cc) {
+            const long long tk = (c_begin + cc) * CH + r;
+            if (cc < nc && tk < T) {
+                const float4 *vs = reinterpret_cast<const float4 *>(static_cast<const float *>(p.v) +
+                                                                    ((size_t)(b * T + tk) * Hv + h) * DV + v0);
+#pragma unroll
+                for (int j = 0; j < NV / 4; ++j) *reinterpret_cast<float4 *>(&vn[4 * j]) = __ldg(vs + j);
+            } else {
+#pragma unroll
+                for (int n = 0; n < NV; ++n) vn[n] = 0.f;
+            }
+        };
+        if (vrow) load_v(0);
         for (int c = 0; ok && c < nc; ++c) {
             const int s = c & 1;
             const uint32_t ph = (uint32_t)(c >> 1) & 1, pc = (uint32_t)c & 1;
@@ -687,15 +704,9 @@ __global__ void __launch_bounds__(RT, 1)
             mbar_arrive1(&sm.tr_empty[s]);
             float x[NV];
             if (vrow) {
-                if (tok < T) {
-                    const float4 *vs = reinterpret_cast<const float4 *>(static_cast<const float *>(p.v) +
-                                                                        ((size_t)(b * T + tok) * Hv + h) * DV + v0);
 #pragma unroll
-                    for (int j = 0; j < NV / 4; ++j) *reinterpret_cast<float4 *>(&x[4 * j]) = __ldg(vs + j);
-                } else {
-#pragma unroll
-                    for (int n = 0; n < NV; ++n) x[n] = 0.f;
-                }
+                for (int n = 0; n < NV; ++n) x[n] = vn[n];
+                load_v(c + 1);
                 if (!(ok = spin_w(&sm.bar_a, pc, err))) break;
                 fence_after_sync();
                 float ks[NV];
