@@ -714,8 +714,9 @@ __global__ void __launch_bounds__(RT, 1)
                 const float eg = expf(gr);
 #pragma unroll
                 for (int n = 0; n < NV; ++n) x[n] = fmaf(-eg, ks[n], x[n]);  // V''
-                // the previous chunk's D_b has read V''
-                if (c > 0 && !(ok = spin_w(&sm.bar_b, pc ^ 1, err))) break;
+                // the previous chunk's D_b has read V'': it was issued before
+                // D_a by the same thread, and a commit (bar_a) completes only
+                // once every earlier MMA of its thread has
                 put_row_mn(sm.vpp[0], sm.vpp[1], r, x);
                 fence_smem_to_async();
                 fence_before_sync();
