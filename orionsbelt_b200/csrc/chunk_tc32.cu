@@ -309,14 +309,14 @@ __global__ void __launch_bounds__(PT, 2)
 #pragma unroll
                 for (int n = 0; n < 32; ++n) {
                     const int s = 32 * hh + n;
-                    A[r * LDP + s] = s < r ? br * v[n] * expf(gr - sm.G[s]) : 0.f;
+                    A[r * LDP + s] = s < r ? br * v[n] * __expf(gr - sm.G[s]) : 0.f;
                     Tm[r * LDP + s] = 0.f;
                 }
             } else {
 #pragma unroll
                 for (int n = 0; n < 32; ++n) {
                     const int s = 32 * hh + n;
-                    v[n] = s <= r ? p.scale * v[n] * expf(gr - sm.G[s]) : 0.f;
+                    v[n] = s <= r ? p.scale * v[n] * __expf(gr - sm.G[s]) : 0.f;
                 }
 #pragma unroll
                 for (int j = 0; j < 4; ++j) {
@@ -352,21 +352,30 @@ __global__ void __launch_bounds__(PT, 2)
         // Off-diagonal blocks by block forward substitution, one distance
         // d = bi - bj at a time: X = sum_{k=bj}^{bi-1} A_{bi,k} T_{k,bj}, then
         // T_{bi,bj} = -T_{bi,bi} X.
+        // (every bound is a constant, so the loops unroll and the loads run
+        // ahead of four independent sums; with run-time bounds each step
+        // waited for its own load, ~1K cycles per distance)
+#pragma unroll
         for (int d = 1; d < 4; ++d) {
+#pragma unroll
             for (int bj = 0; bj + d < 4; ++bj) {
                 const int bi = bj + d;
-                float acc = 0.f;
-                for (int k = 16 * bj; k < 16 * bi; ++k)
-                    acc = fmaf(A[(16 * bi + rr) * LDP + k], Tm[k * LDP + 16 * bj + cc], acc);
-                blk(X, bi, bj, rr, cc) = acc;
+                float acc[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+                for (int k = 0; k < 16 * d; ++k)
+                    acc[k & 3] = fmaf(A[(16 * bi + rr) * LDP + 16 * bj + k], Tm[(16 * bj + k) * LDP + 16 * bj + cc],
+                                      acc[k & 3]);
+                blk(X, bi, bj, rr, cc) = (acc[0] + acc[1]) + (acc[2] + acc[3]);
             }
             __syncthreads();
+#pragma unroll
             for (int bj = 0; bj + d < 4; ++bj) {
                 const int bi = bj + d;
-                float acc = 0.f;
+                float acc[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-                for (int k = 0; k < 16; ++k) acc = fmaf(blk(Tm, bi, bi, rr, k), blk(X, bi, bj, k, cc), acc);
-                blk(Tm, bi, bj, rr, cc) = -acc;
+                for (int k = 0; k < 16; ++k)
+                    acc[k & 3] = fmaf(blk(Tm, bi, bi, rr, k), blk(X, bi, bj, k, cc), acc[k & 3]);
+                blk(Tm, bi, bj, rr, cc) = -((acc[0] + acc[1]) + (acc[2] + acc[3]));
             }
             __syncthreads();
         }
