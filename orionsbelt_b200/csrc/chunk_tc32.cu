@@ -820,15 +820,6 @@ bool chunk_tc32_supported(const kai_gdn_chunk_args *a) {
     return true;
 }
 
-size_t chunk_tc32_workspace_bytes(const kai_gdn_chunk_args *a) {
-    const size_t per_chunk = a->batch * (a->heads_k * (size_t)KQ_BYTES + a->heads_v * (size_t)TR_BYTES);
-    const size_t nch = (a->seq + CH - 1) / CH;
-    size_t seg = SEG_BUDGET / per_chunk;
-    if (seg < 1) seg = 1;
-    if (seg > nch) seg = nch;
-    return seg * per_chunk;
-}
-
 int launch_chunk_tc32(const kai_gdn_chunk_args *a, cudaStream_t st) {
     const size_t per_chunk = a->batch * (a->heads_k * (size_t)KQ_BYTES + a->heads_v * (size_t)TR_BYTES);
     const long long nch = (long long)((a->seq + CH - 1) / CH);
